@@ -1,0 +1,76 @@
+// kernels.h -- host-side launchers for the hoard_b200 CUDA kernels (no CUDA types beyond streams).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hoard {
+
+// Bytes of one GGUF block of 256 weights (Q4_K 144, Q6_K 210), host side.
+inline int fmt_block_bytes(int type) { return type == 12 ? 144 : (type == 14 ? 210 : 0); }
+inline int64_t fmt_mat_bytes(int type, int64_t n, int64_t k) { return n * (k / 256) * fmt_block_bytes(type); }
+
+// Where one layer's experts live: pool slot s of a layer holds gate | up | down in plane layout at
+// base + s*slot_stride + {0, off_up, off_down}. The shared expert (if any) has its own base.
+struct LayerWeights {
+    const uint8_t* pool;
+    int64_t slot_stride;
+    int64_t off_up, off_down;
+    int n_slots;
+    int gate_type, up_type, down_type;
+    const uint8_t* shared;        // gate | up | down of the shared expert, or nullptr
+    int64_t sh_off_up, sh_off_down;
+    int sh_gate_type, sh_up_type, sh_down_type;
+    const float* sh_gate_inp;     // [H]
+    const float* w_router;        // [E][H]
+    const float* w_norm;          // [H]
+};
+
+struct Dims {
+    int H, E, k, I;
+    int renorm;
+    float eps;
+    int resid_bf16;
+};
+
+// Scratch owned by a context (device pointers), sized for max_tokens.
+struct Scratch {
+    float* fx;        // [T][H]
+    int8_t* fx_q;     // [T][H]
+    float* fx_d;      // [T][H/256]
+    int* fx_bs;       // [T][H/16]
+    float* sh_gate;   // [T]
+    int32_t* sel;     // [T][k]      (internal routing output when the caller passes none)
+    float* w;         // [T][k]
+    int* counts;      // [n_slots+1]
+    int* offsets;     // [n_slots+2]
+    int* perm;        // [T*(k+1)] entry ids (t*KK + j) grouped by slot
+    float* h;         // [T*(k+1)][I]
+    int8_t* h_q;      // [T*(k+1)][I]
+    float* h_d;       // [T*(k+1)][I/256]
+    int* h_bs;        // [T*(k+1)][I/16]
+    float* y;         // [T*(k+1)][H]
+    unsigned* amax;   // [T*(k+1)][I/256] bit patterns of max|h| (persistent decode path)
+    float* partials;  // persistent decode: per-CTA partial router sums
+    unsigned* sync;   // persistent decode: grid barrier words + error flag
+};
+
+// Re-lays nrows x nb GGUF blocks of `type` from src (raw) into dst (plane layout).
+cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int64_t nblk_total, cudaStream_t s);
+
+// Router: fx, sel, w (and sh_gate when the layer has a shared expert) for T tokens.
+cudaError_t launch_route(const Dims& d, const LayerWeights& lw, const void* x, int T, float* fx, int32_t* sel,
+                         float* w, float* sh_gate, cudaStream_t s);
+
+// The grouped expert path for any T (fx given), adding into x_inout.
+cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const Scratch& sc, const float* fx,
+                                   const int32_t* slot_of_sel, const float* w, void* x_inout, int T,
+                                   bool need_sh_gate, cudaStream_t s, int* launches);
+
+// Persistent fused decode kernel over n_layers layers (T <= decode_max_tokens()).
+int decode_max_tokens();
+bool decode_supported(const Dims& d, const LayerWeights* lws, int n_layers);
+cudaError_t launch_decode_persistent(const Dims& d, const LayerWeights* lws_dev, int n_layers, const Scratch& sc,
+                                     void* x_inout, int T, int32_t* sel_out, float* w_out, cudaStream_t s,
+                                     int* status_host_flag);
+
+}  // namespace hoard

@@ -1,0 +1,408 @@
+// moe_api.cpp -- the C ABI of include/hoard_moe.h: context, HBM expert pool, router weights,
+// scratch, uploads and the per-call dispatch between the persistent decode kernel and the grouped
+// path. Host C++ only; kernels are launched through kernels.h.
+#include "../../include/hoard_moe.h"
+#include "kernels.h"
+
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+using namespace hoard;
+
+namespace {
+
+constexpr int64_t kAlign = 256;
+inline int64_t align_up(int64_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+inline bool is_quant(int t) { return t == HOARD_TYPE_Q4_K || t == HOARD_TYPE_Q6_K; }
+
+struct LayerStore {
+    int gt = HOARD_TYPE_Q4_K, ut = HOARD_TYPE_Q4_K, dt = HOARD_TYPE_Q6_K;
+    int64_t gate_bytes = 0, up_bytes = 0, down_bytes = 0;   // raw GGUF bytes per expert
+    int64_t off_up = 0, off_down = 0, slot_stride = 0;
+    uint8_t* pool = nullptr;           // n_slots * slot_stride
+    float* w_router = nullptr;         // [E][H]
+    float* w_norm = nullptr;           // [H]
+    bool router_set = false;
+    uint8_t* shared = nullptr;         // gate | up | down, plane layout
+    int64_t sh_off_up = 0, sh_off_down = 0;
+    float* sh_gate_inp = nullptr;      // [H]
+    bool shared_set = false;
+};
+
+}  // namespace
+
+struct hoard_moe_ctx {
+    hoard_moe_desc desc{};
+    Dims dims{};
+    std::vector<LayerStore> layers;
+    Scratch sc{};
+    std::vector<void*> allocations;
+    uint8_t* staging = nullptr;
+    int64_t staging_bytes = 0;
+    cudaEvent_t staging_free = nullptr;
+    int64_t launches = 0;
+    int decode_impl = 1;
+    int routed_layer = -1;
+    int routed_T = 0;
+    LayerWeights* lw_dev = nullptr;    // device copy of LayerWeights for the persistent kernel
+    int lw_dev_cap = 0;
+    std::string err;
+};
+
+namespace {
+
+int fail(hoard_moe_ctx* c, int code, const std::string& msg) {
+    if (c) c->err = msg;
+    return code;
+}
+
+int cuda_fail(hoard_moe_ctx* c, cudaError_t e, const char* what) {
+    std::string m = std::string(what) + ": " + cudaGetErrorString(e);
+    return fail(c, HOARD_ECUDA, m);
+}
+
+#define HCHECK(ctx, call)                                                    \
+    do {                                                                     \
+        cudaError_t _e = (call);                                             \
+        if (_e != cudaSuccess) return cuda_fail((ctx), _e, #call);           \
+    } while (0)
+
+template <typename T>
+int dalloc(hoard_moe_ctx* c, T** p, int64_t bytes) {
+    void* v = nullptr;
+    if (bytes <= 0) bytes = kAlign;
+    cudaError_t e = cudaMalloc(&v, (size_t)bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(c, HOARD_ENOMEM, std::string("cudaMalloc failed: ") + cudaGetErrorString(e));
+    }
+    c->allocations.push_back(v);
+    *p = reinterpret_cast<T*>(v);
+    return HOARD_OK;
+}
+
+LayerWeights layer_weights(const hoard_moe_ctx* c, int layer) {
+    const LayerStore& L = c->layers[layer];
+    LayerWeights lw{};
+    lw.pool = L.pool;
+    lw.slot_stride = L.slot_stride;
+    lw.off_up = L.off_up;
+    lw.off_down = L.off_down;
+    lw.n_slots = c->desc.n_slots;
+    lw.gate_type = L.gt;
+    lw.up_type = L.ut;
+    lw.down_type = L.dt;
+    if (c->desc.n_ff_shexp > 0 && L.shared_set) {
+        lw.shared = L.shared;
+        lw.sh_off_up = L.sh_off_up;
+        lw.sh_off_down = L.sh_off_down;
+        lw.sh_gate_type = c->desc.shexp_gate_type;
+        lw.sh_up_type = c->desc.shexp_up_type;
+        lw.sh_down_type = c->desc.shexp_down_type;
+        lw.sh_gate_inp = L.sh_gate_inp;
+    }
+    lw.w_router = L.w_router;
+    lw.w_norm = L.w_norm;
+    return lw;
+}
+
+int check_layer(hoard_moe_ctx* c, int layer) {
+    if (!c) return HOARD_EINVAL;
+    if (layer < 0 || layer >= c->desc.n_layer) return fail(c, HOARD_EINVAL, "layer out of range");
+    return HOARD_OK;
+}
+
+int check_ready(hoard_moe_ctx* c, int layer) {
+    const LayerStore& L = c->layers[layer];
+    if (!L.router_set) return fail(c, HOARD_ESTATE, "router weights of this layer were never set");
+    if (c->desc.n_ff_shexp > 0 && !L.shared_set) return fail(c, HOARD_ESTATE, "shared expert of this layer was never set");
+    return HOARD_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* hoard_strerror(int status) {
+    switch (status) {
+        case HOARD_OK: return "ok";
+        case HOARD_EINVAL: return "invalid argument";
+        case HOARD_ENOMEM: return "out of memory";
+        case HOARD_ECUDA: return "CUDA error";
+        case HOARD_ETIMEOUT: return "device wait timed out";
+        case HOARD_ENCCL: return "collective failed";
+        case HOARD_ESTATE: return "call out of order";
+        default: return "unknown status";
+    }
+}
+
+const char* hoard_moe_last_error(const hoard_moe_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+int64_t hoard_moe_launch_count(const hoard_moe_ctx* ctx) { return ctx ? ctx->launches : -1; }
+
+int hoard_moe_create(const hoard_moe_desc* d, hoard_moe_ctx** out) {
+    if (!d || !out) return HOARD_EINVAL;
+    *out = nullptr;
+    const int H = d->n_embd, E = d->n_expert, k = d->n_expert_used, I = d->n_ff;
+    if (H <= 0 || H % 256 || I <= 0 || I % 256 || E <= 0 || E > 1024 || k <= 0 || k > 16 || k > E ||
+        d->n_layer <= 0 || d->n_slots <= 0 || d->n_slots > 4096 || d->max_tokens <= 0 ||
+        (d->resid_type != HOARD_TYPE_F32 && d->resid_type != HOARD_TYPE_BF16))
+        return HOARD_EINVAL;
+    if (d->n_ff_shexp != 0 && (d->n_ff_shexp != I || !is_quant(d->shexp_gate_type) || !is_quant(d->shexp_up_type) ||
+                               !is_quant(d->shexp_down_type)))
+        return HOARD_EINVAL;
+    for (int l = 0; l < d->n_layer; ++l) {
+        if ((d->gate_types && !is_quant(d->gate_types[l])) || (d->up_types && !is_quant(d->up_types[l])) ||
+            (d->down_types && !is_quant(d->down_types[l])))
+            return HOARD_EINVAL;
+    }
+    auto* c = new hoard_moe_ctx();
+    c->desc = *d;
+    c->desc.gate_types = c->desc.up_types = c->desc.down_types = nullptr;  // caller's arrays are not retained
+    c->dims = Dims{H, E, k, I, d->norm_topk ? 1 : 0, d->eps, d->resid_type == HOARD_TYPE_BF16 ? 1 : 0};
+    int rc = HOARD_OK;
+    cudaError_t e = cudaSetDevice(d->device);
+    if (e != cudaSuccess) {
+        rc = cuda_fail(c, e, "cudaSetDevice");
+        delete c;
+        return rc;
+    }
+    c->layers.resize(d->n_layer);
+    int64_t max_raw = 0;
+    for (int l = 0; l < d->n_layer && rc == HOARD_OK; ++l) {
+        LayerStore& L = c->layers[l];
+        L.gt = d->gate_types ? d->gate_types[l] : HOARD_TYPE_Q4_K;
+        L.ut = d->up_types ? d->up_types[l] : HOARD_TYPE_Q4_K;
+        L.dt = d->down_types ? d->down_types[l] : HOARD_TYPE_Q6_K;
+        L.gate_bytes = fmt_mat_bytes(L.gt, I, H);
+        L.up_bytes = fmt_mat_bytes(L.ut, I, H);
+        L.down_bytes = fmt_mat_bytes(L.dt, H, I);
+        L.off_up = align_up(L.gate_bytes);
+        L.off_down = L.off_up + align_up(L.up_bytes);
+        L.slot_stride = L.off_down + align_up(L.down_bytes);
+        max_raw = std::max(max_raw, L.gate_bytes + L.up_bytes + L.down_bytes);
+        rc = dalloc(c, &L.pool, (int64_t)d->n_slots * L.slot_stride);
+        if (rc == HOARD_OK) rc = dalloc(c, &L.w_router, (int64_t)E * H * 4);
+        if (rc == HOARD_OK) rc = dalloc(c, &L.w_norm, (int64_t)H * 4);
+        if (rc == HOARD_OK && d->n_ff_shexp > 0) {
+            const int64_t g = fmt_mat_bytes(d->shexp_gate_type, I, H), u = fmt_mat_bytes(d->shexp_up_type, I, H),
+                          dn = fmt_mat_bytes(d->shexp_down_type, H, I);
+            L.sh_off_up = align_up(g);
+            L.sh_off_down = L.sh_off_up + align_up(u);
+            rc = dalloc(c, &L.shared, L.sh_off_down + align_up(dn));
+            if (rc == HOARD_OK) rc = dalloc(c, &L.sh_gate_inp, (int64_t)H * 4);
+            max_raw = std::max(max_raw, g + u + dn);
+        }
+    }
+    // scratch
+    const int64_t T = d->max_tokens, KK = k + 1;
+    Scratch& s = c->sc;
+    if (rc == HOARD_OK) rc = dalloc(c, &s.fx, T * H * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.fx_q, T * H);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.fx_d, T * (H / 256) * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.fx_bs, T * (H / 16) * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.sh_gate, T * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.sel, T * k * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.w, T * k * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.counts, (int64_t)(d->n_slots + 2) * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.offsets, (int64_t)(d->n_slots + 2) * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.perm, T * KK * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.h, T * KK * I * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.h_q, T * KK * I);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.h_d, T * KK * (I / 256) * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.h_bs, T * KK * (I / 16) * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.y, T * KK * H * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.amax, T * KK * (I / 256) * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.partials, (int64_t)4096 * 1024 * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.sync, 1024 * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &c->staging, max_raw);
+    c->staging_bytes = max_raw;
+    if (rc == HOARD_OK) {
+        e = cudaMemset(s.sync, 0, 1024 * 4);
+        if (e == cudaSuccess) e = cudaMemset(s.amax, 0, T * KK * (I / 256) * 4);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->staging_free, cudaEventDisableTiming);
+        if (e != cudaSuccess) rc = cuda_fail(c, e, "context init");
+    }
+    if (rc != HOARD_OK) {
+        hoard_moe_destroy(c);
+        return rc;
+    }
+    *out = c;
+    return HOARD_OK;
+}
+
+int hoard_moe_destroy(hoard_moe_ctx* c) {
+    if (!c) return HOARD_EINVAL;
+    cudaSetDevice(c->desc.device);
+    cudaDeviceSynchronize();
+    for (void* p : c->allocations) cudaFree(p);
+    if (c->lw_dev) cudaFree(c->lw_dev);
+    if (c->staging_free) cudaEventDestroy(c->staging_free);
+    delete c;
+    return HOARD_OK;
+}
+
+int64_t hoard_moe_expert_bytes(const hoard_moe_ctx* c, int layer) {
+    if (!c || layer < 0 || layer >= c->desc.n_layer) return -1;
+    const LayerStore& L = c->layers[layer];
+    return L.gate_bytes + L.up_bytes + L.down_bytes;
+}
+
+int hoard_moe_set_router(hoard_moe_ctx* c, int layer, const float* w_router, const float* w_norm) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (!w_router || !w_norm) return fail(c, HOARD_EINVAL, "null router pointer");
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    LayerStore& L = c->layers[layer];
+    HCHECK(c, cudaMemcpy(L.w_router, w_router, (size_t)c->dims.E * c->dims.H * 4, cudaMemcpyDefault));
+    HCHECK(c, cudaMemcpy(L.w_norm, w_norm, (size_t)c->dims.H * 4, cudaMemcpyDefault));
+    L.router_set = true;
+    return HOARD_OK;
+}
+
+static int upload3(hoard_moe_ctx* c, uint8_t* dst_base, const int types[3], const int64_t offs[3],
+                   const int64_t bytes[3], const int64_t rows[3], const void* const src[3], cudaStream_t s) {
+    HCHECK(c, cudaStreamWaitEvent(s, c->staging_free, 0));
+    int64_t so = 0;
+    for (int m = 0; m < 3; ++m) {
+        HCHECK(c, cudaMemcpyAsync(c->staging + so, src[m], (size_t)bytes[m], cudaMemcpyDefault, s));
+        const int64_t nblk = bytes[m] / fmt_block_bytes(types[m]);
+        (void)rows;
+        HCHECK(c, launch_repack(types[m], c->staging + so, dst_base + offs[m], nblk, s));
+        ++c->launches;
+        so += bytes[m];
+    }
+    HCHECK(c, cudaEventRecord(c->staging_free, s));
+    return HOARD_OK;
+}
+
+int hoard_moe_upload_expert(hoard_moe_ctx* c, int layer, int slot, const void* gate, const void* up,
+                            const void* down, hoard_stream stream) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (slot < 0 || slot >= c->desc.n_slots) return fail(c, HOARD_EINVAL, "slot out of range");
+    if (!gate || !up || !down) return fail(c, HOARD_EINVAL, "null expert pointer");
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    LayerStore& L = c->layers[layer];
+    const int types[3] = {L.gt, L.ut, L.dt};
+    const int64_t offs[3] = {0, L.off_up, L.off_down};
+    const int64_t bytes[3] = {L.gate_bytes, L.up_bytes, L.down_bytes};
+    const int64_t rows[3] = {c->dims.I, c->dims.I, c->dims.H};
+    const void* const src[3] = {gate, up, down};
+    return upload3(c, L.pool + (int64_t)slot * L.slot_stride, types, offs, bytes, rows, src, (cudaStream_t)stream);
+}
+
+int hoard_moe_set_shared(hoard_moe_ctx* c, int layer, const void* gate, const void* up, const void* down,
+                         const float* gate_inp) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (c->desc.n_ff_shexp <= 0) return fail(c, HOARD_EINVAL, "context has no shared expert");
+    if (!gate || !up || !down || !gate_inp) return fail(c, HOARD_EINVAL, "null shared-expert pointer");
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    LayerStore& L = c->layers[layer];
+    const int H = c->dims.H, I = c->dims.I;
+    const int types[3] = {c->desc.shexp_gate_type, c->desc.shexp_up_type, c->desc.shexp_down_type};
+    const int64_t offs[3] = {0, L.sh_off_up, L.sh_off_down};
+    const int64_t bytes[3] = {fmt_mat_bytes(types[0], I, H), fmt_mat_bytes(types[1], I, H), fmt_mat_bytes(types[2], H, I)};
+    const int64_t rows[3] = {I, I, H};
+    const void* const src[3] = {gate, up, down};
+    rc = upload3(c, L.shared, types, offs, bytes, rows, src, (cudaStream_t)0);
+    if (rc) return rc;
+    HCHECK(c, cudaMemcpy(L.sh_gate_inp, gate_inp, (size_t)H * 4, cudaMemcpyDefault));
+    HCHECK(c, cudaDeviceSynchronize());
+    L.shared_set = true;
+    return HOARD_OK;
+}
+
+int hoard_moe_route(hoard_moe_ctx* c, int layer, const void* x, int T, int32_t* sel, float* w,
+                    hoard_stream stream) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (T <= 0 || T > c->desc.max_tokens) return fail(c, HOARD_EINVAL, "T out of range (1..max_tokens)");
+    if (!x || !sel || !w) return fail(c, HOARD_EINVAL, "null pointer");
+    if ((rc = check_ready(c, layer))) return rc;
+    const LayerWeights lw = layer_weights(c, layer);
+    HCHECK(c, launch_route(c->dims, lw, x, T, c->sc.fx, sel, w, nullptr, (cudaStream_t)stream));
+    ++c->launches;
+    c->routed_layer = layer;
+    c->routed_T = T;
+    return HOARD_OK;
+}
+
+int hoard_moe_experts(hoard_moe_ctx* c, int layer, const float* fx, const int32_t* sel, const int32_t* slot_of_sel,
+                      const float* w, void* x_inout, int T, hoard_stream stream) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (T <= 0 || T > c->desc.max_tokens) return fail(c, HOARD_EINVAL, "T out of range (1..max_tokens)");
+    if (!sel || !w || !x_inout) return fail(c, HOARD_EINVAL, "null pointer");
+    if ((rc = check_ready(c, layer))) return rc;
+    if (!fx) {
+        if (c->routed_T < T || c->routed_layer < 0) return fail(c, HOARD_ESTATE, "no routed activations for this T");
+        fx = c->sc.fx;
+    }
+    if (!slot_of_sel && c->desc.n_slots < c->dims.E)
+        return fail(c, HOARD_EINVAL, "slot_of_sel is required when n_slots < n_expert");
+    const LayerWeights lw = layer_weights(c, layer);
+    int nl = 0;
+    HCHECK(c, launch_experts_grouped(c->dims, lw, c->sc, fx, slot_of_sel ? slot_of_sel : sel, w, x_inout, T, true,
+                                     (cudaStream_t)stream, &nl));
+    c->launches += nl;
+    return HOARD_OK;
+}
+
+int hoard_moe_layers(hoard_moe_ctx* c, int layer0, int n_layers, void* x_inout, int T, int32_t* sel_out,
+                     float* w_out, hoard_stream stream) {
+    if (!c) return HOARD_EINVAL;
+    if (n_layers <= 0 || layer0 < 0 || layer0 + n_layers > c->desc.n_layer)
+        return fail(c, HOARD_EINVAL, "layer range out of bounds");
+    if (T <= 0 || T > c->desc.max_tokens) return fail(c, HOARD_EINVAL, "T out of range (1..max_tokens)");
+    if (!x_inout) return fail(c, HOARD_EINVAL, "null x");
+    if (c->desc.n_slots < c->dims.E) return fail(c, HOARD_EINVAL, "fused layer needs every expert resident");
+    for (int l = layer0; l < layer0 + n_layers; ++l) {
+        int rc = check_ready(c, l);
+        if (rc) return rc;
+    }
+    const int k = c->dims.k;
+    for (int l = layer0; l < layer0 + n_layers; ++l) {
+        const int64_t o = (int64_t)(l - layer0) * T * k;
+        int32_t* sel = sel_out ? sel_out + o : c->sc.sel;
+        float* w = w_out ? w_out + o : c->sc.w;
+        int rc = hoard_moe_route(c, l, x_inout, T, sel, w, stream);
+        if (rc) return rc;
+        rc = hoard_moe_experts(c, l, nullptr, sel, nullptr, w, x_inout, T, stream);
+        if (rc) return rc;
+    }
+    return HOARD_OK;
+}
+
+int hoard_moe_layer(hoard_moe_ctx* c, int layer, void* x_inout, int T, int32_t* sel_out, float* w_out,
+                    hoard_stream stream) {
+    return hoard_moe_layers(c, layer, 1, x_inout, T, sel_out, w_out, stream);
+}
+
+int hoard_moe_set_decode_impl(hoard_moe_ctx* c, int impl) {
+    if (!c || impl < 0 || impl > 1) return HOARD_EINVAL;
+    c->decode_impl = impl;
+    return HOARD_OK;
+}
+
+int hoard_moe_sync_status(hoard_moe_ctx* c, hoard_stream stream) {
+    if (!c) return HOARD_EINVAL;
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    HCHECK(c, cudaStreamSynchronize((cudaStream_t)stream));
+    unsigned flags = 0;
+    HCHECK(c, cudaMemcpy(&flags, c->sc.sync, 4, cudaMemcpyDeviceToHost));
+    if (flags) {
+        const unsigned zero = 0;
+        HCHECK(c, cudaMemcpy(c->sc.sync, &zero, 4, cudaMemcpyHostToDevice));
+        if (flags & 2u) return fail(c, HOARD_ETIMEOUT, "a device-side wait gave up");
+        return fail(c, HOARD_EINVAL, "an expert or slot id was out of range (entries skipped)");
+    }
+    return HOARD_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,149 @@
+/* hoard_moe.h -- C ABI of the B200-native MoE layer (router -> expert dispatch -> SwiGLU expert
+ * FFN on Q4_K/Q6_K -> weighted combine into the residual).
+ *
+ * This is the boundary that hoard's C++ layer schedule calls in place of its inline ggml graph
+ * code for one MoE layer. Each entry point names the hoard code it replaces (paths inside the
+ * hoard project). Conventions, for every function:
+ *   - returns HOARD_OK (0) or a negative HOARD_E* status; never exits, never throws;
+ *   - device buffers passed in are owned by the caller; the context owns its expert pool,
+ *     router weights and scratch;
+ *   - one context is driven by one host thread at a time;
+ *   - a stream argument of NULL means the legacy default stream.
+ */
+#ifndef HOARD_MOE_H
+#define HOARD_MOE_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define HOARD_OK 0
+#define HOARD_EINVAL (-1)   /* bad argument: size, type, index, null pointer */
+#define HOARD_ENOMEM (-2)   /* device or pinned-host allocation failed */
+#define HOARD_ECUDA (-3)    /* a CUDA runtime call failed; see hoard_moe_last_error */
+#define HOARD_ETIMEOUT (-4) /* a bounded device-side wait gave up */
+#define HOARD_ENCCL (-5)    /* a collective failed */
+#define HOARD_ESTATE (-6)   /* call out of order, e.g. experts before any route on this context */
+
+/* weight / activation types: GGUF (ggml) type ids */
+#define HOARD_TYPE_F32 0
+#define HOARD_TYPE_Q4_K 12
+#define HOARD_TYPE_Q6_K 14
+#define HOARD_TYPE_BF16 30
+
+typedef struct hoard_moe_ctx hoard_moe_ctx;
+typedef void* hoard_stream; /* a cudaStream_t */
+
+/* Layer hyper-parameters. hoard reads these from GGUF metadata in load_model
+ * (src/run_moe_stream.cpp:125-151; src/run_qwen35.cpp:160-200). */
+typedef struct hoard_moe_desc {
+    int n_embd;          /* H: hidden size (multiple of 256) */
+    int n_expert;        /* E: experts per layer (<= 1024) */
+    int n_expert_used;   /* k: experts per token (<= 16); the TOPK override of
+                            src/run_qwen35.cpp:169 is expressed by passing a smaller k */
+    int n_ff;            /* I: expert intermediate size (multiple of 256) */
+    int n_layer;         /* layers held by this context */
+    int n_slots;         /* expert slots per layer; n_expert = all experts HBM-resident */
+    int norm_topk;       /* 1: renormalise the top-k weights to sum 1 (clamped at
+                            6.103515625e-5), src/run_moe_stream.cpp:150, :371-373 */
+    float eps;           /* RMSNorm epsilon */
+    int resid_type;      /* HOARD_TYPE_F32 or HOARD_TYPE_BF16: dtype of x / x_inout */
+    const int* gate_types; /* [n_layer] HOARD_TYPE_Q4_K / _Q6_K, or NULL = all Q4_K */
+    const int* up_types;   /* [n_layer] or NULL = all Q4_K */
+    const int* down_types; /* [n_layer] or NULL = all Q6_K (per-layer mix: H.dtype[il],
+                              src/run_moe_stream.cpp:179) */
+    int n_ff_shexp;      /* shared-expert intermediate size; 0 = none. Must equal n_ff when set
+                            (src/run_qwen35.cpp:195, :659-666) */
+    int shexp_gate_type; /* types of the shared expert's gate/up/down */
+    int shexp_up_type;
+    int shexp_down_type;
+    int max_tokens;      /* largest T of any call (sizes the scratch) */
+    int device;          /* CUDA device ordinal */
+} hoard_moe_desc;
+
+/* Creates a context: allocates the HBM expert pool [n_layer][n_slots] and the scratch.
+ * Replaces the slot-pool allocation of src/run_moe_stream.cpp:242-254. */
+int hoard_moe_create(const hoard_moe_desc* desc, hoard_moe_ctx** out);
+
+/* Frees everything the context owns. */
+int hoard_moe_destroy(hoard_moe_ctx* ctx);
+
+/* Sets one layer's router weight ffn_gate_inp (f32 [E][H]: GGUF ne=[H,E]) and its ffn_norm
+ * (f32 [H]). Host or device pointers. Replaces the resident tensors read by
+ * src/run_moe_stream.cpp:352-353. */
+int hoard_moe_set_router(hoard_moe_ctx* ctx, int layer, const float* w_router, const float* w_norm);
+
+/* Copies one expert's raw GGUF block bytes (gate [I][H], up [I][H], down [H][I], each in the
+ * layer's type, per-expert stride as stored in the GGUF file) into pool slot `slot` of
+ * `layer`, asynchronously on `stream`. Host (pinned for true asynchrony) or device pointers.
+ * The bytes are re-laid into the pool's plane layout on the device.
+ * Replaces to_vram (src/run_moe_stream.cpp:279-284) and the pool upload in ensure
+ * (src/run_specloop.cpp:63-65). */
+int hoard_moe_upload_expert(hoard_moe_ctx* ctx, int layer, int slot, const void* gate,
+                            const void* up, const void* down, hoard_stream stream);
+
+/* Sets one layer's shared expert (raw GGUF bytes of ffn_{gate,up,down}_shexp) and its gate
+ * vector ffn_gate_inp_shexp (f32 [H]). Replaces src/run_qwen35.cpp:659-666's resident tensors. */
+int hoard_moe_set_shared(hoard_moe_ctx* ctx, int layer, const void* gate, const void* up,
+                         const void* down, const float* gate_inp);
+
+/* Router for T tokens: fx = rms_norm(x) * ffn_norm; probs = softmax(W_r . fx) over all E;
+ * sel = top-k (descending, ties to the lower id); w = probs[sel], renormalised if norm_topk.
+ * x: device [T][H] of resid_type. sel [T][k] int32 and w [T][k] f32: device or pinned host.
+ * fx is kept in the context for the next hoard_moe_experts call.
+ * Replaces graph A's router tail + readback + renorm, src/run_moe_stream.cpp:352-373. */
+int hoard_moe_route(hoard_moe_ctx* ctx, int layer, const void* x, int T, int32_t* sel, float* w,
+                    hoard_stream stream);
+
+/* Expert FFN + weighted combine: x_inout[t] += sum_j w[t][j] * FFN_{slot(t,j)}(fx[t])
+ * (+ the gated shared expert). fx: device f32 [T][H], or NULL to use the fx of the last
+ * hoard_moe_route on this context. sel [T][k]: expert ids; slot_of_sel [T][k]: pool slots, or
+ * NULL when slot == expert id (all experts resident). Device pointers.
+ * Replaces graph B + the host weighted sum, src/run_moe_stream.cpp:425-447, and the batched
+ * mul_mat_id form src/run_specloop.cpp:125-140. */
+int hoard_moe_experts(hoard_moe_ctx* ctx, int layer, const float* fx, const int32_t* sel,
+                      const int32_t* slot_of_sel, const float* w, void* x_inout, int T,
+                      hoard_stream stream);
+
+/* Fused layer with every expert resident (slot == expert id): route + experts + combine, with
+ * no host round trip. sel_out / w_out may be NULL. Replaces src/run_moe_stream.cpp:352-447 for
+ * the all-resident case (K = n_expert) and the fused chain of src/run_m1.cpp:92-108. */
+int hoard_moe_layer(hoard_moe_ctx* ctx, int layer, void* x_inout, int T, int32_t* sel_out,
+                    float* w_out, hoard_stream stream);
+
+/* n_layers consecutive fused layers [layer0, layer0 + n_layers) on the same x_inout (an MoE
+ * stack with nothing between the layers). sel_out / w_out, if given, are [n_layers][T][k]. */
+int hoard_moe_layers(hoard_moe_ctx* ctx, int layer0, int n_layers, void* x_inout, int T,
+                     int32_t* sel_out, float* w_out, hoard_stream stream);
+
+/* Waits for `stream`, then reports and clears the errors kernels recorded on the device:
+ * HOARD_EINVAL for expert or slot ids out of range (those entries were skipped), HOARD_ETIMEOUT
+ * for a bounded device-side wait that gave up. hoard aborts on such input instead
+ * (src/run_moe_stream.cpp:56); this library reports it. */
+int hoard_moe_sync_status(hoard_moe_ctx* ctx, hoard_stream stream);
+
+/* Bytes of one expert's raw GGUF gate+up+down at `layer` (what upload_expert reads). */
+int64_t hoard_moe_expert_bytes(const hoard_moe_ctx* ctx, int layer);
+
+/* Kernel launches issued by this context since creation (instrumentation). */
+int64_t hoard_moe_launch_count(const hoard_moe_ctx* ctx);
+
+/* Selects the decode implementation for small T: 0 = grouped kernels (any T),
+ * 1 = persistent fused decode kernel (default where supported). */
+int hoard_moe_set_decode_impl(hoard_moe_ctx* ctx, int impl);
+
+/* Last error message of this context (CUDA error string or argument check). */
+const char* hoard_moe_last_error(const hoard_moe_ctx* ctx);
+
+/* Static description of a status code. */
+const char* hoard_strerror(int status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HOARD_MOE_H */

@@ -1,0 +1,227 @@
+"""GPU parity: the CUDA path through the C ABI against the CPU oracle on the same seeded bytes.
+
+Tolerances (the MoE delta out - x is compared, since the residual would hide errors):
+  * vs the oracle in ggml mode (Q8_K activations, the arithmetic of hoard's ggml CPU backend):
+    rel-L2 <= 1e-4; expert ids identical wherever the k-th/(k+1)-th logit gap exceeds 1e-3;
+    weights within 1e-5 relative.
+  * vs the oracle in exact mode (f32 activations): rel-L2 <= 3e-2 on the delta; the Q8_K
+    activation noise alone accounts for ~1.8e-2 at these shapes.
+  * structural invariants are bit-exact: LRU slot permutation == all-resident, split
+    route+experts == fused layer, repeated calls are deterministic.
+"""
+import numpy as np
+import pytest
+import torch
+
+from hoard_b200 import moe
+from oracle import oracle as orc
+from tests.moe_fixtures import (LayerSpec, load_context, make_layer, make_x, near_tie_mask, oracle_layer,
+                                rel_l2, Q4_K, Q6_K)
+
+pytestmark = pytest.mark.gpu
+
+DEV = 0
+
+
+def make_ctx(spec: LayerSpec, n_layer=1, max_tokens=64, resid=torch.float32, n_slots=None, down_types=None):
+    return moe.MoEContext(n_embd=spec.H, n_expert=spec.E, n_expert_used=spec.k, n_ff=spec.I, n_layer=n_layer,
+                          n_slots=n_slots, norm_topk=spec.renorm, eps=spec.eps, resid_dtype=resid,
+                          gate_types=[spec.types[0]] * n_layer, up_types=[spec.types[1]] * n_layer,
+                          down_types=down_types or [spec.types[2]] * n_layer,
+                          n_ff_shexp=spec.I if spec.shared else 0, shexp_types=spec.sh_types,
+                          max_tokens=max_tokens, device=DEV)
+
+
+def check_against_oracle(spec, L, x, out, sel, w):
+    ref_out, ref_sel, ref_w, _, ref_probs = oracle_layer(L, x, orc.MODE_GGML)
+    tie = near_tie_mask(ref_probs, ref_sel, spec.k)
+    ok = ~tie
+    assert np.array_equal(np.sort(sel[ok], 1), np.sort(ref_sel[ok], 1))
+    # the descending order itself where every adjacent gap inside the top-k is clear
+    srt = -np.sort(-ref_probs, 1)[:, :spec.k + 1]
+    lp = np.log(np.maximum(srt, 1e-30))
+    clear = (np.diff(-lp, axis=1) > 1e-3).all(1)
+    assert np.array_equal(sel[clear], ref_sel[clear])
+    assert np.allclose(w[clear], ref_w[clear], rtol=1e-5, atol=1e-7)
+    if ok.all():
+        assert rel_l2(out - x, ref_out - x) < 1e-4
+    exact_out = oracle_layer(L, x, orc.MODE_EXACT)[0]
+    assert rel_l2(out - x, exact_out - x) < 3e-2
+    return ref_out
+
+
+def run_layer(ctx, x_np, resid=torch.float32):
+    T = x_np.shape[0]
+    x = torch.from_numpy(x_np).to(f"cuda:{DEV}").to(resid)
+    sel = torch.empty(T, ctx.k, dtype=torch.int32, device=x.device)
+    w = torch.empty(T, ctx.k, dtype=torch.float32, device=x.device)
+    ctx.layer(0, x, sel, w)
+    ctx.sync_status()
+    return x.float().cpu().numpy(), sel.cpu().numpy(), w.cpu().numpy()
+
+
+@pytest.fixture(scope="module")
+def small():
+    spec = LayerSpec(H=512, E=16, k=4, I=256)
+    L = make_layer(spec, seed=101)
+    ctx = make_ctx(spec)
+    load_context(ctx, 0, L)
+    yield spec, L, ctx
+    ctx.close()
+
+
+@pytest.mark.parametrize("T", [1, 2, 5, 16, 64])
+def test_small_layer_parity(small, T):
+    spec, L, ctx = small
+    x = make_x(T, spec.H, seed=T)
+    out, sel, w = run_layer(ctx, x)
+    check_against_oracle(spec, L, x, out, sel, w)
+
+
+def test_deterministic_and_split_equals_fused(small):
+    spec, L, ctx = small
+    x_np = make_x(7, spec.H, seed=77)
+    a, sa, wa = run_layer(ctx, x_np)
+    b, sb, wb = run_layer(ctx, x_np)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32)) and np.array_equal(sa, sb)
+    x = torch.from_numpy(x_np).cuda(DEV)
+    sel, w = ctx.route(0, x)
+    ctx.experts(0, sel, w, x)
+    ctx.sync_status()
+    assert np.array_equal(x.cpu().numpy().view(np.uint32), a.view(np.uint32))
+
+
+@pytest.fixture(scope="module")
+def qwen_c2():
+    """Config 2: isolated MoE layer at Qwen3-30B-A3B shape (E=128, k=8, I=768, renorm, down Q6_K)."""
+    spec = LayerSpec(H=2048, E=128, k=8, I=768)
+    L = make_layer(spec, seed=2)
+    ctx = make_ctx(spec, max_tokens=64)
+    load_context(ctx, 0, L)
+    yield spec, L, ctx
+    ctx.close()
+
+
+@pytest.mark.parametrize("T", [1, 16])
+def test_c2_layer_parity(qwen_c2, T):
+    spec, L, ctx = qwen_c2
+    x = make_x(T, spec.H, seed=1000 + T)
+    out, sel, w = run_layer(ctx, x)
+    check_against_oracle(spec, L, x, out, sel, w)
+
+
+def test_c2_bf16_residual(qwen_c2):
+    spec, L, _ = qwen_c2
+    ctx = make_ctx(spec, resid=torch.bfloat16, max_tokens=4)
+    load_context(ctx, 0, L)
+    x = make_x(4, spec.H, seed=9)
+    xb = torch.from_numpy(x).to(torch.bfloat16).float().numpy()   # the input the layer actually sees
+    out, sel, w = run_layer(ctx, xb, resid=torch.bfloat16)
+    ref = oracle_layer(L, xb, orc.MODE_GGML)[0]
+    # one bf16 rounding of the output on top of the f32 result
+    assert np.abs(out - ref).max() <= np.abs(ref).max() * 2 ** -8 + 1e-6
+    assert rel_l2(out - xb, ref - xb) < 5e-3
+    ctx.close()
+
+
+def test_olmoe_shape_q4k_down_no_renorm():
+    """Config 1 layer shape: E=64, k=8, I=1024, no renorm, Q4_K down (the odd-layer type)."""
+    spec = LayerSpec(H=2048, E=64, k=8, I=1024, types=(Q4_K, Q4_K, Q4_K), renorm=False, eps=1e-5)
+    L = make_layer(spec, seed=3)
+    ctx = make_ctx(spec, max_tokens=8)
+    load_context(ctx, 0, L)
+    x = make_x(3, spec.H, seed=3)
+    out, sel, w = run_layer(ctx, x)
+    check_against_oracle(spec, L, x, out, sel, w)
+    assert (w.sum(1) < 1.0).all()        # not renormalised
+    ctx.close()
+
+
+def test_shared_expert_top10():
+    """Config 5 structure: top-10 routing plus a gated shared expert (scaled-down E)."""
+    spec = LayerSpec(H=2048, E=64, k=10, I=512, shared=True)
+    L = make_layer(spec, seed=5)
+    ctx = make_ctx(spec, max_tokens=8)
+    load_context(ctx, 0, L)
+    x = make_x(5, spec.H, seed=5)
+    out, sel, w = run_layer(ctx, x)
+    check_against_oracle(spec, L, x, out, sel, w)
+    ctx.close()
+
+
+def test_lru_slots_equal_all_resident(small):
+    """hoard's invariant (LRU cache == naive == all-resident, bit-identical): the same kernels over a
+    permuted slot pool smaller than E give identical output."""
+    spec, L, full = small
+    x_np = make_x(6, spec.H, seed=6)
+    ref, ref_sel, _ = run_layer(full, x_np)
+    used = sorted(set(ref_sel.reshape(-1).tolist()))
+    rng = np.random.default_rng(0)
+    n_slots = len(used) + 1
+    slots = rng.permutation(n_slots)[:len(used)]
+    slot_of_expert = {e: int(s) for e, s in zip(used, slots)}
+    ctx = make_ctx(spec, n_slots=n_slots)
+    load_context(ctx, 0, L, slot_of_expert=slot_of_expert)
+    x = torch.from_numpy(x_np).cuda(DEV)
+    sel, w = ctx.route(0, x)
+    sel_h = sel.cpu().numpy()                                   # the host readback hoard does
+    slot_of_sel = torch.from_numpy(np.vectorize(slot_of_expert.get)(sel_h).astype(np.int32)).cuda(DEV)
+    ctx.experts(0, sel, w, x, slot_of_sel=slot_of_sel)
+    ctx.sync_status()
+    assert np.array_equal(x.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    ctx.close()
+
+
+def test_out_of_range_slot_is_reported(small):
+    spec, L, ctx = small
+    x = torch.from_numpy(make_x(2, spec.H, seed=8)).cuda(DEV)
+    sel, w = ctx.route(0, x)
+    bad = sel.clone()
+    bad[1, 0] = spec.E + 3
+    ctx.experts(0, sel, w, x, slot_of_sel=bad)
+    with pytest.raises(moe.HoardError) as ei:
+        ctx.sync_status()
+    assert ei.value.status == moe.HOARD_EINVAL
+    ctx.sync_status()            # cleared, context still usable
+    out, _, _ = run_layer(ctx, make_x(1, spec.H, seed=1))
+    assert np.isfinite(out).all()
+
+
+def test_argument_errors(small):
+    spec, L, ctx = small
+    x = torch.zeros(ctx.max_tokens + 1, spec.H, device=f"cuda:{DEV}")
+    with pytest.raises(moe.HoardError) as ei:
+        ctx.layer(0, x)
+    assert ei.value.status == moe.HOARD_EINVAL
+    with pytest.raises(moe.HoardError):
+        ctx.layer(3, x[:1])
+    fresh = make_ctx(spec)
+    with pytest.raises(moe.HoardError) as ei:
+        fresh.layer(0, x[:1])
+    assert ei.value.status == moe.HOARD_ESTATE
+    fresh.close()
+
+
+def test_layer_stack_equals_sequential_layers():
+    spec = LayerSpec(H=512, E=16, k=4, I=256)
+    Ls = [make_layer(spec, seed=300 + i) for i in range(3)]
+    ctx = make_ctx(spec, n_layer=3, down_types=[Q6_K, Q4_K, Q6_K])
+    # layer 1 has Q4_K down: rebuild its bytes in that type
+    Ls[1] = make_layer(LayerSpec(H=512, E=16, k=4, I=256, types=(Q4_K, Q4_K, Q4_K)), seed=301)
+    for i, L in enumerate(Ls):
+        load_context(ctx, i, L)
+    x_np = make_x(3, spec.H, seed=4)
+    x = torch.from_numpy(x_np).cuda(DEV)
+    sel = torch.empty(3, 3, ctx.k, dtype=torch.int32, device=x.device)
+    w = torch.empty(3, 3, ctx.k, device=x.device)
+    ctx.layers(0, 3, x, sel, w)
+    ctx.sync_status()
+    y = torch.from_numpy(x_np).cuda(DEV)
+    for i in range(3):
+        ctx.layer(i, y)
+    assert torch.equal(x, y)
+    ref = x_np
+    for i, L in enumerate(Ls):
+        ref = oracle_layer(L, ref, orc.MODE_GGML)[0]
+    assert rel_l2(x.cpu().numpy() - x_np, ref - x_np) < 1e-3
+    ctx.close()
