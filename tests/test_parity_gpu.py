@@ -2,8 +2,9 @@
 
 Tolerances (the MoE delta out - x is compared, since the residual would hide errors):
   * vs the oracle in ggml mode (Q8_K activations, the arithmetic of hoard's ggml CPU backend):
-    rel-L2 <= 1e-4; expert ids identical wherever the k-th/(k+1)-th logit gap exceeds 1e-3;
-    weights within 1e-5 relative.
+    >= 90 % of tokens within 1e-5 rel-L2 and the whole batch within 1e-3 (a Q8_K rounding flip
+    on a .5 boundary moves one token by ~2e-3); expert ids identical wherever the
+    k-th/(k+1)-th logit gap exceeds 1e-3; weights within 1e-5 relative.
   * vs the oracle in exact mode (f32 activations): rel-L2 <= 3e-2 on the delta; the Q8_K
     activation noise alone accounts for ~1.8e-2 at these shapes.
   * structural invariants are bit-exact: LRU slot permutation == all-resident, split
@@ -44,7 +45,12 @@ def check_against_oracle(spec, L, x, out, sel, w):
     assert np.array_equal(sel[clear], ref_sel[clear])
     assert np.allclose(w[clear], ref_w[clear], rtol=1e-5, atol=1e-7)
     if ok.all():
-        assert rel_l2(out - x, ref_out - x) < 1e-4
+        # Per token the GPU and the oracle differ only by f32 summation order, which can flip the
+        # Q8_K rounding of an h element that sits on a .5 boundary (p ~ 2e-5 per element). Most
+        # tokens therefore agree to ~1e-6; a flipped token moves by ~2e-3.
+        per_tok = np.array([rel_l2(out[t] - x[t], ref_out[t] - x[t]) for t in range(x.shape[0])])
+        assert (per_tok < 1e-5).mean() >= 0.9, per_tok
+        assert rel_l2(out - x, ref_out - x) < 1e-3
     exact_out = oracle_layer(L, x, orc.MODE_EXACT)[0]
     assert rel_l2(out - x, exact_out - x) < 3e-2
     return ref_out
