@@ -22,6 +22,7 @@ struct LayerWeights {
     int sh_gate_type, sh_up_type, sh_down_type;
     const float* sh_gate_inp;     // [H]
     const float* w_router;        // [E][H]
+    const float* w_router_t;      // [H][E] (the persistent decode kernel's per-row router slices)
     const float* w_norm;          // [H]
 };
 
@@ -56,6 +57,9 @@ struct Scratch {
 
 // Re-lays nrows x nb GGUF blocks of `type` from src (raw) into dst (plane layout).
 cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int64_t nblk_total, cudaStream_t s);
+
+// dst[c][r] = src[r][c] for an R x C f32 matrix.
+cudaError_t launch_transpose(const float* src, float* dst, int R, int C, cudaStream_t s);
 
 // Router: fx, sel, w (and sh_gate when the layer has a shared expert) for T tokens.
 cudaError_t launch_route(const Dims& d, const LayerWeights& lw, const void* x, int T, float* fx, int32_t* sel,

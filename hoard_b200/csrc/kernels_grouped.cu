@@ -12,6 +12,7 @@
 // :425-447) and the batched mul_mat_id form (src/run_specloop.cpp:115-140).
 #include "common.cuh"
 #include "kernels.h"
+#include "block_ops.cuh"
 
 namespace hoard {
 
@@ -46,68 +47,23 @@ cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int64_t nb
     return cudaGetLastError();
 }
 
-// ---------------------------------------------------------------------------------------------
-// block reductions (256 threads)
-// ---------------------------------------------------------------------------------------------
-__device__ double block_sum_d(double v, double* red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    v = warp_sum(v);
+__global__ void k_transpose(const float* __restrict__ src, float* __restrict__ dst, int R, int C) {
+    __shared__ float tile[32][33];
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int r = r0 + i, c = c0 + threadIdx.x;
+        if (r < R && c < C) tile[i][threadIdx.x] = src[(int64_t)r * C + c];
+    }
     __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    double r = 0.0;
-    for (int i = 0; i < nw; ++i) r += red[i];
-    return r;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int c = c0 + i, r = r0 + threadIdx.x;
+        if (r < R && c < C) dst[(int64_t)c * R + r] = tile[threadIdx.x][i];
+    }
 }
 
-__device__ float block_max_f(float v, float* red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    v = warp_max(v);
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float r = red[0];
-    for (int i = 1; i < nw; ++i) r = fmaxf(r, red[i]);
-    return r;
-}
-
-// softmax over E logits held in shared memory (in place -> probabilities), then top-k by rank:
-// rank(e) = #{j : p_j > p_e} + #{j < e : p_j == p_e}, i.e. descending with ties to the lower id.
-__device__ void softmax_topk(float* lg, int E, int k, int renorm, int32_t* sel, float* w, double* redd,
-                             float* redf, int* s_sel, float* s_w) {
-    float m = -INFINITY;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) m = fmaxf(m, lg[e]);
-    m = block_max_f(m, redf);
-    double s = 0.0;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        const float v = expf(lg[e] - m);
-        lg[e] = v;
-        s += (double)v;
-    }
-    s = block_sum_d(s, redd);
-    const float inv = (float)(1.0 / s);
-    for (int e = threadIdx.x; e < E; e += blockDim.x) lg[e] *= inv;
-    __syncthreads();
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        const float p = lg[e];
-        int rank = 0;
-        for (int j = 0; j < E; ++j) {
-            const float q = lg[j];
-            rank += (q > p) || (q == p && j < e);
-        }
-        if (rank < k) { s_sel[rank] = e; s_w[rank] = p; }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        if (renorm) {
-            float sum = 0.f;
-            for (int j = 0; j < k; ++j) sum += s_w[j];
-            if (sum < 6.103515625e-5f) sum = 6.103515625e-5f;
-            for (int j = 0; j < k; ++j) s_w[j] /= sum;
-        }
-        for (int j = 0; j < k; ++j) { sel[j] = s_sel[j]; w[j] = s_w[j]; }
-    }
-    __syncthreads();
+cudaError_t launch_transpose(const float* src, float* dst, int R, int C, cudaStream_t s) {
+    k_transpose<<<dim3((C + 31) / 32, (R + 31) / 32), dim3(32, 8), 0, s>>>(src, dst, R, C);
+    return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -25,6 +25,7 @@ struct LayerStore {
     int64_t off_up = 0, off_down = 0, slot_stride = 0;
     uint8_t* pool = nullptr;           // n_slots * slot_stride
     float* w_router = nullptr;         // [E][H]
+    float* w_router_t = nullptr;       // [H][E]
     float* w_norm = nullptr;           // [H]
     bool router_set = false;
     uint8_t* shared = nullptr;         // gate | up | down, plane layout
@@ -48,8 +49,8 @@ struct hoard_moe_ctx {
     int decode_impl = 1;
     int routed_layer = -1;
     int routed_T = 0;
-    LayerWeights* lw_dev = nullptr;    // device copy of LayerWeights for the persistent kernel
-    int lw_dev_cap = 0;
+    LayerWeights* lw_dev = nullptr;    // device copy of every layer's LayerWeights (persistent kernel)
+    bool decode_ok = false;            // the persistent decode kernel supports these shapes / types
     std::string err;
 };
 
@@ -106,6 +107,7 @@ LayerWeights layer_weights(const hoard_moe_ctx* c, int layer) {
         lw.sh_gate_inp = L.sh_gate_inp;
     }
     lw.w_router = L.w_router;
+    lw.w_router_t = L.w_router_t;
     lw.w_norm = L.w_norm;
     return lw;
 }
@@ -187,6 +189,7 @@ int hoard_moe_create(const hoard_moe_desc* d, hoard_moe_ctx** out) {
         max_raw = std::max(max_raw, L.gate_bytes + L.up_bytes + L.down_bytes);
         rc = dalloc(c, &L.pool, (int64_t)d->n_slots * L.slot_stride);
         if (rc == HOARD_OK) rc = dalloc(c, &L.w_router, (int64_t)E * H * 4);
+        if (rc == HOARD_OK) rc = dalloc(c, &L.w_router_t, (int64_t)E * H * 4);
         if (rc == HOARD_OK) rc = dalloc(c, &L.w_norm, (int64_t)H * 4);
         if (rc == HOARD_OK && d->n_ff_shexp > 0) {
             const int64_t g = fmt_mat_bytes(d->shexp_gate_type, I, H), u = fmt_mat_bytes(d->shexp_up_type, I, H),
@@ -216,16 +219,29 @@ int hoard_moe_create(const hoard_moe_desc* d, hoard_moe_ctx** out) {
     if (rc == HOARD_OK) rc = dalloc(c, &s.h_d, T * KK * (I / 256) * 4);
     if (rc == HOARD_OK) rc = dalloc(c, &s.h_bs, T * KK * (I / 16) * 4);
     if (rc == HOARD_OK) rc = dalloc(c, &s.y, T * KK * H * 4);
-    if (rc == HOARD_OK) rc = dalloc(c, &s.amax, T * KK * (I / 256) * 4);
+    const int64_t amax_rows = std::max<int64_t>(T, 2) * KK;   // >= 2 layer buffers of k rows
+    if (rc == HOARD_OK) rc = dalloc(c, &s.amax, amax_rows * (I / 256) * 4);
     if (rc == HOARD_OK) rc = dalloc(c, &s.partials, (int64_t)4096 * 1024 * 4);
     if (rc == HOARD_OK) rc = dalloc(c, &s.sync, 1024 * 4);
     if (rc == HOARD_OK) rc = dalloc(c, &c->staging, max_raw);
     c->staging_bytes = max_raw;
     if (rc == HOARD_OK) {
         e = cudaMemset(s.sync, 0, 1024 * 4);
-        if (e == cudaSuccess) e = cudaMemset(s.amax, 0, T * KK * (I / 256) * 4);
+        if (e == cudaSuccess) e = cudaMemset(s.amax, 0, amax_rows * (I / 256) * 4);
+        if (e == cudaSuccess) e = cudaMemset(s.partials, 0, (size_t)4096 * 1024 * 4);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->staging_free, cudaEventDisableTiming);
         if (e != cudaSuccess) rc = cuda_fail(c, e, "context init");
+    }
+    if (rc == HOARD_OK) {
+        std::vector<LayerWeights> tab(d->n_layer);
+        for (int l = 0; l < d->n_layer; ++l) tab[l] = layer_weights(c, l);
+        rc = dalloc(c, &c->lw_dev, (int64_t)d->n_layer * (int64_t)sizeof(LayerWeights));
+        if (rc == HOARD_OK) {
+            e = cudaMemcpy(c->lw_dev, tab.data(), tab.size() * sizeof(LayerWeights), cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) rc = cuda_fail(c, e, "layer table upload");
+        }
+        if (rc == HOARD_OK)
+            c->decode_ok = decode_supported(c->dims, tab.data(), d->n_layer);
     }
     if (rc != HOARD_OK) {
         hoard_moe_destroy(c);
@@ -240,7 +256,6 @@ int hoard_moe_destroy(hoard_moe_ctx* c) {
     cudaSetDevice(c->desc.device);
     cudaDeviceSynchronize();
     for (void* p : c->allocations) cudaFree(p);
-    if (c->lw_dev) cudaFree(c->lw_dev);
     if (c->staging_free) cudaEventDestroy(c->staging_free);
     delete c;
     return HOARD_OK;
@@ -260,6 +275,8 @@ int hoard_moe_set_router(hoard_moe_ctx* c, int layer, const float* w_router, con
     LayerStore& L = c->layers[layer];
     HCHECK(c, cudaMemcpy(L.w_router, w_router, (size_t)c->dims.E * c->dims.H * 4, cudaMemcpyDefault));
     HCHECK(c, cudaMemcpy(L.w_norm, w_norm, (size_t)c->dims.H * 4, cudaMemcpyDefault));
+    HCHECK(c, launch_transpose(L.w_router, L.w_router_t, c->dims.E, c->dims.H, 0));
+    HCHECK(c, cudaDeviceSynchronize());
     L.router_set = true;
     return HOARD_OK;
 }
@@ -367,6 +384,13 @@ int hoard_moe_layers(hoard_moe_ctx* c, int layer0, int n_layers, void* x_inout, 
         if (rc) return rc;
     }
     const int k = c->dims.k;
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    if (T == 1 && c->decode_impl == 1 && c->decode_ok) {
+        HCHECK(c, launch_decode_persistent(c->dims, c->lw_dev + layer0, n_layers, c->sc, x_inout, T, sel_out, w_out,
+                                           (cudaStream_t)stream, nullptr));
+        ++c->launches;
+        return HOARD_OK;
+    }
     for (int l = layer0; l < layer0 + n_layers; ++l) {
         const int64_t o = (int64_t)(l - layer0) * T * k;
         int32_t* sel = sel_out ? sel_out + o : c->sc.sel;

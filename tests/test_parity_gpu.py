@@ -231,3 +231,54 @@ def test_layer_stack_equals_sequential_layers():
         ref = oracle_layer(L, ref, orc.MODE_GGML)[0]
     assert rel_l2(x.cpu().numpy() - x_np, ref - x_np) < 1e-3
     ctx.close()
+
+
+@pytest.mark.parametrize("resid", [torch.float32, torch.bfloat16])
+def test_decode_persistent_matches_grouped_and_oracle(resid):
+    """T = 1 through the persistent fused kernel (the default for decode) vs the grouped kernels
+    and vs the oracle, over a 4-layer stack with both down types (Q6_K even, Q4_K odd)."""
+    spec = LayerSpec(H=2048, E=64, k=8, I=768)
+    types = [Q6_K, Q4_K, Q6_K, Q4_K]
+    Ls = [make_layer(LayerSpec(H=2048, E=64, k=8, I=768, types=(Q4_K, Q4_K, t)), seed=500 + i)
+          for i, t in enumerate(types)]
+    ctx = make_ctx(spec, n_layer=4, down_types=types, resid=resid, max_tokens=2)
+    for i, L in enumerate(Ls):
+        load_context(ctx, i, L)
+    x_np = make_x(1, spec.H, seed=55)
+    if resid == torch.bfloat16:
+        x_np = torch.from_numpy(x_np).to(torch.bfloat16).float().numpy()
+    outs = {}
+    for impl in (1, 0):
+        ctx.set_decode_impl(impl)
+        x = torch.from_numpy(x_np).cuda(DEV).to(resid)
+        sel = torch.empty(4, 1, ctx.k, dtype=torch.int32, device=x.device)
+        w = torch.empty(4, 1, ctx.k, device=x.device)
+        ctx.layers(0, 4, x, sel, w)
+        ctx.sync_status()
+        outs[impl] = (x.float().cpu().numpy(), sel.cpu().numpy(), w.cpu().numpy())
+    assert np.array_equal(outs[0][1], outs[1][1])
+    assert np.allclose(outs[0][2], outs[1][2], rtol=1e-5, atol=1e-7)
+    assert rel_l2(outs[1][0] - x_np, outs[0][0] - x_np) < 1e-3
+    ref = x_np
+    for i, L in enumerate(Ls):
+        ref_l, ref_sel = oracle_layer(L, ref, orc.MODE_GGML)[:2]
+        assert np.array_equal(np.sort(ref_sel, 1), np.sort(outs[1][1][i], 1))
+        ref = ref_l if resid == torch.float32 else torch.from_numpy(ref_l).to(torch.bfloat16).float().numpy()
+    assert rel_l2(outs[1][0] - x_np, ref - x_np) < (1e-3 if resid == torch.float32 else 1e-2)
+    ctx.close()
+
+
+def test_decode_persistent_repeatable_and_counters_reset(qwen_c2):
+    """Back-to-back persistent launches (the barrier/exit counters must return to zero) give
+    identical results, and single-layer calls chain like one multi-layer call."""
+    spec, L, ctx = qwen_c2
+    x_np = make_x(1, spec.H, seed=4242)
+    res = []
+    for _ in range(3):
+        x = torch.from_numpy(x_np).cuda(DEV)
+        ctx.layer(0, x)
+        res.append(x.cpu().numpy())
+    ctx.sync_status()
+    assert all(np.array_equal(r.view(np.uint32), res[0].view(np.uint32)) for r in res)
+    ref = oracle_layer(L, x_np, orc.MODE_GGML)[0]
+    assert rel_l2(res[0] - x_np, ref - x_np) < 1e-3
