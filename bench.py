@@ -185,6 +185,49 @@ def cpu_sample(max_seconds: float, nthreads: int):
                    f"tok/s = 1/(48 x mean layer time)")
 
 
+PHASE_NAMES = ["router_sums_read", "softmax+fx_q8", "topk", "issue", "renorm", "gu_first_wait", "gate_up", "barrier_h",
+               "h_q8", "down_wait", "down", "combine+router_partials", "barrier_x_in_layer"]
+
+
+def trace_breakdown(ctx, x_row, device):
+    """One extra (untimed) decode step with the persistent kernel's phase stamps on; returns the
+    mean over layers of the median and max over CTAs of each phase's duration (us)."""
+    import torch
+    ctas, nph = ctx.trace_layout()
+    buf = torch.zeros(ctas * N_LAYER * nph, dtype=torch.int64, device=device)
+    ctx.set_trace(buf)
+    x = x_row.clone()
+    ctx.layers(0, N_LAYER, x)
+    torch.cuda.synchronize(device)
+    ctx.set_trace(None)
+    t = buf.view(ctas, N_LAYER, nph).cpu().numpy().astype(np.float64)
+    if not t.any():
+        return None
+    main = t[:, :, :14]
+    d = np.diff(main, axis=2) / 1e3                # [cta, layer, 13] us between consecutive stamps
+    out = {}
+    for i, name in enumerate(PHASE_NAMES[:13]):
+        di = d[:, :-1, i] if i >= 10 else d[:, :, i]     # the last layer has no router partials
+        out[name] = {"median": round(float(np.median(di, axis=0).mean()), 3),
+                     "max": round(float(di.max(axis=0).mean()), 3)}
+    if nph >= 20:
+        def span(a_, b_, layers=slice(None)):
+            v = (t[:, layers, b_] - t[:, layers, a_]) / 1e3
+            return {"median": round(float(np.median(v, axis=0).mean()), 3), "max": round(float(v.max(axis=0).mean()), 3)}
+        out["barrier_h.fence"] = span(7, 14)
+        out["barrier_h.poll"] = span(14, 15)
+        out["barrier_x.fence"] = span(12, 16, slice(0, -1))
+        out["barrier_x.poll"] = span(16, 17, slice(0, -1))
+        out["route.sums_read"] = span(0, 19)
+        out["route.softmax"] = span(19, 1)
+        out["route.sort"] = span(1, 2)
+        out["route.topk"] = span(2, 3)
+        out["issue.expect_tx"] = span(3, 18)
+        out["issue.copies"] = span(18, 4)
+    out["layer_total"] = round(float(np.median(t[:, 1:, 0] - t[:, :-1, 0]) / 1e3), 3)
+    return out
+
+
 # --------------------------------------------------------------------------------------------
 def run_reference(args, rank, world):
     """The reference arm: the CPU restatement of hoard's ggml-CPU path, all host threads."""
@@ -285,6 +328,10 @@ def run_gpu(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_e2e = float(t.item())
 
+    phases = None
+    if args.trace:
+        phases = trace_breakdown(ctx, xs[0], device)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle as orc
@@ -327,6 +374,8 @@ def run_gpu(args, rank, world, local_rank):
         }
         if cpu:
             line["cpu_baseline"] = cpu
+        if phases:
+            line["phase_us"] = phases
         print(json.dumps(line), flush=True)
     ctx.close()
     if dist:
@@ -335,6 +384,7 @@ def run_gpu(args, rank, world, local_rank):
 
 
 def main():
+    global N_LAYER
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
@@ -343,8 +393,12 @@ def main():
     ap.add_argument("--decode-impl", type=int, default=None, help="0 grouped kernels, 1 persistent kernel")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--trace", action="store_true", help="add the persistent kernel's per-phase breakdown")
+    ap.add_argument("--layers", type=int, default=N_LAYER, help="MoE layers per step (48 = the full stack; "
+                    "fewer only for small profiling captures)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    N_LAYER = args.layers
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -72,9 +72,11 @@ cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const 
 
 // Persistent fused decode kernel over n_layers layers (T <= decode_max_tokens()).
 int decode_max_tokens();
+int decode_grid();           // CTAs of a persistent launch (one per SM)
+int decode_trace_phases();   // stamps per CTA and layer written when tracing
 bool decode_supported(const Dims& d, const LayerWeights* lws, int n_layers);
 cudaError_t launch_decode_persistent(const Dims& d, const LayerWeights* lws_dev, int n_layers, const Scratch& sc,
                                      void* x_inout, int T, int32_t* sel_out, float* w_out, cudaStream_t s,
-                                     int* status_host_flag);
+                                     unsigned long long* trace);
 
 }  // namespace hoard

@@ -2,19 +2,22 @@
 // consecutive layers in one cooperative launch (one CTA per SM).
 //
 // Per layer l (hoard's graph A router tail + graph B + host combine, src/run_moe_stream.cpp:352-447):
-//   A  every CTA reduces the router sums of layer l (accumulated by all CTAs at the end of layer
-//      l-1), runs softmax + top-k itself (identical arithmetic in every CTA), and builds the Q8_K
-//      activation of fx = rms_norm(x) * ffn_norm in shared memory;
-//   B  one thread issues cp.async.bulk copies of this CTA's share of the selected experts' bytes
-//      (gate/up row pairs AND down rows) plus the next layer's router slice, all at once, so the
-//      whole layer's weight bytes are in flight while the CTA computes;
-//   C  gate/up row pairs from shared memory: h = silu(gate . fx) * (up . fx) -> global, plus a
-//      per-256-block max|h| (the Q8_K scale of h) by atomicMax;
+//   A  every CTA reads the router sums of layer l (accumulated by all CTAs at the end of layer l-1),
+//      runs softmax + top-k itself (identical arithmetic in every CTA) while its other warps build
+//      the Q8_K activation of fx = rms_norm(x) * ffn_norm in shared memory;
+//   B  warp 0 issues cp.async.bulk copies of this CTA's share of the selected experts' bytes
+//      (gate/up row pairs in four chunks, and the down rows) plus the next layer's router slice, all
+//      at once, so the whole layer's weight bytes are in flight while the CTA computes;
+//   C  gate/up row pairs from shared memory as each chunk lands: h = silu(gate . fx) * (up . fx) to
+//      global, plus a per-256-block max|h| (the Q8_K scale of h) by atomicMax;
 //      ---- grid barrier ----
 //   D  Q8_K of h in shared memory; this CTA's output rows for every selected expert; the combine
 //      x[d] = sum_j w_j*y_j[d] + x[d] (j ascending); then the next layer's router partial sums over
 //      these rows (sum x^2 and W_r^T[d,:] . (ffn_norm[d]*x[d])) added into double accumulators;
 //      ---- grid barrier ----
+// Matmul mapping: one lane owns one 256-weight block of a row (its scales are decoded once), lanes
+// read the block's 16-byte chunks in a lane-rotated order so that a warp's shared-memory reads hit
+// distinct banks, and the integer dot of each chunk is exact (dp4a).
 // Every wait (grid barrier, mbarrier) is bounded by %globaltimer; on expiry the kernel sets
 // bit 2 of the error word, stops computing, drains its own copies (bounded) and exits.
 #include "common.cuh"
@@ -23,9 +26,14 @@
 
 namespace hoard {
 
+static int g_num_sms = 0;
+
 namespace {
 
 constexpr int DEC_THREADS = 512;
+constexpr int DEC_TRACE_PHASES = 20;
+constexpr int NCH = 4;                                   // gate/up arrival chunks
+constexpr int RACC_COPIES = 8;                           // router accumulators spread over copies
 constexpr unsigned long long WAIT_NS = 2000000000ull;   // 2 s bound on any wait
 
 __device__ __forceinline__ unsigned long long gtimer() {
@@ -41,11 +49,13 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
+// try_wait with a suspend-time hint: a waiting warp sleeps in hardware until the phase completes
+// (or the hint elapses) instead of spinning, so it takes no issue slots from the working warps.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
     unsigned ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u) : "memory");
     return ok != 0;
 }
 // Bounded wait for phase `parity` of an mbarrier; false if the bound expired.
@@ -62,60 +72,48 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 __device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
     unsigned v;
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void red_add_release(unsigned* p, unsigned v) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ float ld_f32(const float* p) {   // coherent load of data written in this launch
-    float v;
-    asm volatile("ld.relaxed.gpu.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ double ld_f64(const double* p) {
-    double v;
-    asm volatile("ld.relaxed.gpu.global.f64 %0, [%1];" : "=d"(v) : "l"(p) : "memory");
-    return v;
+// Loads of data produced earlier in this launch by other CTAs go through L2 only (ld.global.cg):
+// L2 is the point of coherence, and the grid barrier's acquire fence orders them after the
+// producers' writes. They are ordinary loads, so the compiler can issue them back to back.
+__device__ __forceinline__ float4 ld_resid4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float4 ld_resid4(const __nv_bfloat16* p) {
+    const unsigned short* q = reinterpret_cast<const unsigned short*>(p);
+    return make_float4(__bfloat162float(__ushort_as_bfloat16(__ldcg(q))),
+                       __bfloat162float(__ushort_as_bfloat16(__ldcg(q + 1))),
+                       __bfloat162float(__ushort_as_bfloat16(__ldcg(q + 2))),
+                       __bfloat162float(__ushort_as_bfloat16(__ldcg(q + 3))));
 }
 
-__device__ __forceinline__ float ld_resid(const float* p) { return ld_f32(p); }
-__device__ __forceinline__ float ld_resid(const __nv_bfloat16* p) {
-    unsigned short v;
-    asm volatile("ld.relaxed.gpu.global.u16 %0, [%1];" : "=h"(v) : "l"(p) : "memory");
-    return __bfloat162float(__ushort_as_bfloat16(v));
-}
-__device__ __forceinline__ float4 ld_f32x4(const float* p) {
-    float4 v;
-    asm volatile("ld.relaxed.gpu.global.v4.f32 {%0,%1,%2,%3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p) : "memory");
-    return v;
-}
-
-// Grid barrier number `n` (0, 1, 2, ... within this launch). Returns false on timeout / error.
-__device__ bool grid_barrier(unsigned* sync, unsigned n, int* s_ok) {
+// Grid barrier number `n` (0, 1, 2, ... within this launch): release by fence + relaxed add,
+// poll with relaxed loads, acquire by fence. Returns false on timeout / error.
+// It is driven by the last warp, which issues no bulk copies, so that its fence does not wait on
+// weight copies still in flight.
+__device__ bool grid_barrier(unsigned* sync, unsigned n, int* s_ok, unsigned long long* st = nullptr) {
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == blockDim.x - 32) {
         int ok = 1;
-        __threadfence();
-        red_add_release(&sync[1], 1u);
         const unsigned target = (n + 1) * gridDim.x;
-        if (ld_acquire(&sync[1]) < target) {
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        if (st) st[0] = gtimer();
+        asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(&sync[1]) : "memory");
+        if (ld_relaxed(&sync[1]) < target) {
             const unsigned long long t0 = gtimer();
-            while (ld_acquire(&sync[1]) < target) {
-                if (ld_relaxed(&sync[0]) & 2u) { ok = 0; break; }
-                if (gtimer() - t0 > WAIT_NS) { atomicOr(&sync[0], 2u); ok = 0; break; }
+            for (unsigned it = 1;; ++it) {
+                if (ld_relaxed(&sync[1]) >= target) break;
+                if ((it & 15) == 0) {
+                    if (ld_relaxed(&sync[0]) & 2u) { ok = 0; break; }
+                    if (gtimer() - t0 > WAIT_NS) { atomicOr(&sync[0], 2u); ok = 0; break; }
+                }
             }
         }
+        if (st) st[1] = gtimer();
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
         *s_ok = ok;
     }
     __syncthreads();
@@ -123,6 +121,146 @@ __device__ bool grid_barrier(unsigned* sync, unsigned n, int* s_ok) {
 }
 
 inline __host__ __device__ int64_t a16(int64_t v) { return (v + 15) & ~(int64_t)15; }
+
+// Q8_K activations in shared memory are padded so that lanes reading the same offset of different
+// 256-value blocks (stride 272 B) or of different experts (stride = odd multiple of 16 B mod 128)
+// land in different banks.
+constexpr int ACT_BLK = 272;
+inline __host__ __device__ int hq_stride(int nbI) {
+    const int s = nbI * ACT_BLK;
+    return ((s / 16) & 1) ? s : s + 16;
+}
+
+__device__ __forceinline__ void named_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int count) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// unsigned bytes of a . signed bytes of b, accumulated into c
+__device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int sext8(unsigned x) { return (int)(signed char)(x & 0xFFu); }
+__device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ int4 lds128i(const void* p) { return *reinterpret_cast<const int4*>(p); }
+
+// The 6-bit scales and mins of a Q4_K block header, unpacked four per register (one byte each):
+// sc[0..3], sc[4..7], m[0..3], m[4..7] (GGUF packing: bytes 0..3 low 6 bits = sc[0..3], bytes 4..7
+// = m[0..3]; bytes 8..11 low/high nibbles = low 4 bits of sc[4..7]/m[4..7], whose top 2 bits are
+// the top 2 bits of bytes 0..3 / 4..7).
+struct Q4Scales {
+    uint32_t sc_lo, sc_hi, m_lo, m_hi;
+};
+__device__ __forceinline__ Q4Scales q4_scales(const uint4& h) {
+    Q4Scales s;
+    s.sc_lo = h.y & 0x3F3F3F3Fu;
+    s.m_lo = h.z & 0x3F3F3F3Fu;
+    s.sc_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+    s.m_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+    return s;
+}
+__device__ __forceinline__ int byte_of(uint32_t lo, uint32_t hi, int j) {   // byte j (0..7) of (lo, hi)
+    return (int)(((j < 4 ? lo : hi) >> (8 * (j & 3))) & 0xFFu);
+}
+
+// Exact integer parts of one 16-byte Q4_K chunk c (0..7) of a block against the activation block:
+// low nibbles belong to sub-block 2g, high nibbles to 2g+1 (g = c/2); returns sc0*dot_lo + sc1*dot_hi.
+__device__ __forceinline__ int q4_chunk(const uint4& w, const int4& alo, const int4& ahi, int sc0, int sc1) {
+    int lo = __dp4a((int)(w.x & 0x0F0F0F0Fu), alo.x, 0);
+    lo = __dp4a((int)(w.y & 0x0F0F0F0Fu), alo.y, lo);
+    lo = __dp4a((int)(w.z & 0x0F0F0F0Fu), alo.z, lo);
+    lo = __dp4a((int)(w.w & 0x0F0F0F0Fu), alo.w, lo);
+    int hi = dp4a_us(w.x & 0xF0F0F0F0u, ahi.x, 0);
+    hi = dp4a_us(w.y & 0xF0F0F0F0u, ahi.y, hi);
+    hi = dp4a_us(w.z & 0xF0F0F0F0u, ahi.z, hi);
+    hi = dp4a_us(w.w & 0xF0F0F0F0u, ahi.w, hi);
+    return sc0 * lo + sc1 * (hi >> 4);
+}
+
+// sum_j m_j * bs32_j over the 8 sub-blocks (the dmin part of a Q4_K block dot)
+__device__ __forceinline__ int q4_min_dot(const Q4Scales& s, const int* bs32) {
+    const int4 b0 = lds128i(bs32), b1 = lds128i(bs32 + 4);
+    return (int)(s.m_lo & 0xFF) * b0.x + (int)((s.m_lo >> 8) & 0xFF) * b0.y + (int)((s.m_lo >> 16) & 0xFF) * b0.z +
+           (int)(s.m_lo >> 24) * b0.w + (int)(s.m_hi & 0xFF) * b1.x + (int)((s.m_hi >> 8) & 0xFF) * b1.y +
+           (int)((s.m_hi >> 16) & 0xFF) * b1.z + (int)(s.m_hi >> 24) * b1.w;
+}
+
+// Warp 0's router tail for E <= 32*NV: router sums (RACC_COPIES partial copies) -> logits ->
+// softmax over all E (double sum, as ggml's soft_max) -> top-k -> optional renormalisation with
+// clamp. Each lane sorts its NV probabilities once; every round takes the warp-wide maximum of the
+// lanes' heads (non-negative floats order as unsigned integers) and, among equal values, the
+// lowest expert id. Lanes < k leave expert id and weight of rank `lane` in s_sel / s_w.
+template <int NV>
+__device__ __forceinline__ void route_warp(const double* s_lgd, int E, int k, int renorm, float scale, int lane,
+                                           int* s_sel, float* s_w, int32_t* sel_out, float* w_out,
+                                           unsigned long long* st) {
+    float p[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) p[i] = lane + 32 * i < E ? (float)((double)scale * s_lgd[lane + 32 * i]) : -INFINITY;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) mx = fmaxf(mx, p[i]);
+    mx = warp_max(mx);
+    double sum = 0.0;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        if (lane + 32 * i < E) {
+            p[i] = expf(p[i] - mx);
+            sum += (double)p[i];
+        }
+    }
+    sum = warp_sum(sum);
+    const float inv = (float)(1.0 / sum);
+    if (st && lane == 0) st[0] = gtimer();
+    unsigned key[NV], idx[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const bool valid = lane + 32 * i < E;
+        key[i] = valid ? __float_as_uint(p[i] * inv) + 1u : 0u;
+        idx[i] = (unsigned)(lane + 32 * i);
+    }
+#pragma unroll
+    for (int i = 1; i < NV; ++i) {
+#pragma unroll
+        for (int j = i; j > 0; --j) {
+            const bool sw = key[j] > key[j - 1] || (key[j] == key[j - 1] && idx[j] < idx[j - 1]);
+            const unsigned k0 = key[j - 1], i0 = idx[j - 1];
+            key[j - 1] = sw ? key[j] : k0;
+            idx[j - 1] = sw ? idx[j] : i0;
+            key[j] = sw ? k0 : key[j];
+            idx[j] = sw ? i0 : idx[j];
+        }
+    }
+    if (st && lane == 0) st[1] = gtimer();
+    float my_w = 0.f, wsum = 0.f;
+    int my_sel = 0;
+    for (int r = 0; r < k; ++r) {
+        const unsigned M = __reduce_max_sync(0xFFFFFFFFu, key[0]);
+        const unsigned W = __reduce_min_sync(0xFFFFFFFFu, key[0] == M ? idx[0] : 0xFFFFFFFFu);
+        if (key[0] == M && idx[0] == W) {
+#pragma unroll
+            for (int i = 0; i + 1 < NV; ++i) { key[i] = key[i + 1]; idx[i] = idx[i + 1]; }
+            key[NV - 1] = 0u;
+        }
+        const float wv = __uint_as_float(M - 1u);
+        wsum += wv;                               // sequential in rank order, as hoard's host loop
+        if (lane == r) { my_w = wv; my_sel = (int)W; }
+    }
+    if (st && lane == 0) st[2] = gtimer();
+    if (renorm) {
+        if (wsum < 6.103515625e-5f) wsum = 6.103515625e-5f;
+        my_w /= wsum;
+    }
+    if (lane < k) {
+        s_sel[lane] = my_sel;
+        s_w[lane] = my_w;
+        if (sel_out) { sel_out[lane] = my_sel; w_out[lane] = my_w; }
+    }
+}
 
 }  // namespace
 
@@ -135,8 +273,8 @@ struct DecodePlan {
     int64_t off_gate_qs, off_gate_hdr, off_up_qs, off_up_hdr;
     int64_t dn_stride;                      // bytes of one expert's down rows (all planes)
     int64_t dn_p0, dn_p1, dn_p2, dn_p3;     // plane offsets inside an expert's down region
-    int64_t off_dn, off_wt, off_wn, off_fxq, off_fxd, off_fxbs, off_hq, off_hd, off_hbs, off_y, off_xs,
-        off_lg, off_misc, total;
+    int64_t off_dn, off_wt, off_wn, off_fxq, off_fxd, off_fxbs32, off_hq, off_hd, off_hbs, off_y, off_xs,
+        off_misc, total;
 
     __host__ __device__ void init(int H_, int E_, int k_, int I_, int dt_, int G) {
         H = H_; E = E_; k = k_; I = I_; dt = dt_;
@@ -167,16 +305,16 @@ struct DecodePlan {
         off_dn = o; o += (int64_t)k * dn_stride;
         off_wt = o; o += a16((int64_t)nr_max * E * 4) + 16;
         off_wn = o; o += a16((int64_t)nr_max * 4) + 32;
-        off_fxq = o; o += a16(H);
+        off_fxq = o; o += (int64_t)nbH * ACT_BLK + 16;
+
         off_fxd = o; o += a16((int64_t)nbH * 4);
-        off_fxbs = o; o += a16((int64_t)(H / 16) * 4);
-        off_hq = o; o += a16((int64_t)k * I);
+        off_fxbs32 = o; o += a16((int64_t)(H / 32) * 4);
+        off_hq = o; o += (int64_t)k * hq_stride(nbI) + 16;
         off_hd = o; o += a16((int64_t)k * nbI * 4);
-        off_hbs = o; o += a16((int64_t)k * (I / 16) * 4);
+        off_hbs = o; o += a16((int64_t)k * (I / 16) * 4);   // Q6_K: 16-sums in unit order; Q4_K: 32-sums
         off_y = o; o += a16((int64_t)nr_max * k * 4);
         off_xs = o; o += a16((int64_t)nr_max * 4);
-        off_lg = o; o += a16((int64_t)E * 4);
-        off_misc = o; o += 256;                  // mbarriers, sel/w, flags
+        off_misc = o; o += 128;                  // mbarriers
         total = o;
     }
 };
@@ -192,72 +330,25 @@ struct DecodeArgs {
     float* w_out;
     float* h;                   // [k][I]
     unsigned* amax;             // [2][k][I/256]
-    double* racc;               // [2][E+1]
+    double* racc;               // [2][RACC_COPIES][E+1]
     unsigned* sync;             // [0] error bits, [1] barrier counter, [2] exit counter
+    unsigned long long* trace;  // optional [G][n_layers][DEC_TRACE_PHASES] %globaltimer stamps
 };
-
-template <int DT>
-__device__ __forceinline__ float down_unit(const uint8_t* reg, const DecodePlan& P, int r, int u, const int8_t* aq,
-                                           const float* ad, const int* abs_, int d0_sub) {
-    // reg: this expert's down region; r: row within the CTA's rows; u: unit within the row
-    if (DT == T_Q4K) {
-        const int b = u >> 3, c8 = u & 7;
-        const int64_t blk = (int64_t)r * P.nbI + b;
-        const uint4 w = *reinterpret_cast<const uint4*>(reg + P.dn_p0 + blk * 128 + 16 * c8);
-        const uint4 hh = *reinterpret_cast<const uint4*>(reg + P.dn_p1 + blk * 16);
-        return q4k_unit_dot(w, hh, c8, aq + QK * b, abs_ + 16 * b, ad[b]);
-    } else {
-        const int b = u >> 2, v = u & 3, h2 = v >> 1, rr = v & 1;
-        const int64_t blk = (int64_t)r * P.nbI + b;
-        const uint4 A = *reinterpret_cast<const uint4*>(reg + P.dn_p0 + blk * 128 + 64 * h2 + 16 * rr);
-        const uint4 B = *reinterpret_cast<const uint4*>(reg + P.dn_p0 + blk * 128 + 64 * h2 + 32 + 16 * rr);
-        const uint4 C = *reinterpret_cast<const uint4*>(reg + P.dn_p1 + blk * 64 + 32 * h2 + 16 * rr);
-        const uint4 S = *reinterpret_cast<const uint4*>(reg + P.dn_p2 + blk * 16);
-        const unsigned short dbits = *reinterpret_cast<const unsigned short*>(reg + P.dn_p3 + d0_sub + blk * 2);
-        const float d6 = __half2float(__ushort_as_half(dbits));
-        return ad[b] * d6 * (float)q6k_unit_isum(A, B, C, S, v, aq + QK * b, abs_ + 16 * b);
-    }
-}
-
-template <int DT>
-__device__ void down_phase(const DecodePlan& P, uint8_t* smem, int nr, int KKk, int dsub) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const int sub = lane & 15, hw = warp * 2 + (lane >> 4);
-    const int nunits = P.nbI * (DT == T_Q4K ? 8 : 4);
-    const int8_t* hq = reinterpret_cast<const int8_t*>(smem + P.off_hq);
-    const float* hd = reinterpret_cast<const float*>(smem + P.off_hd);
-    const int* hbs = reinterpret_cast<const int*>(smem + P.off_hbs);
-    float* y = reinterpret_cast<float*>(smem + P.off_y);
-    const int items = nr * KKk;
-    for (int it0 = 0; it0 < items; it0 += 2 * nw) {
-        const int it = it0 + hw;
-        float acc = 0.f;
-        int r = 0, j = 0;
-        if (it < items) {
-            r = it / KKk;
-            j = it - r * KKk;
-            const uint8_t* reg = smem + P.off_dn + (int64_t)j * P.dn_stride;
-            for (int u = sub; u < nunits; u += 16)
-                acc += down_unit<DT>(reg, P, r, u, hq + (int64_t)j * P.I, hd + j * P.nbI, hbs + j * (P.I / 16),
-                                     dsub);
-        }
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (it < items && sub == 0) y[r * KKk + j] = acc;
-    }
-}
 
 template <typename R>
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ double redd[32];
-    __shared__ float redf[32];
     __shared__ int s_sel[16];
     __shared__ float s_w[16];
     __shared__ int s_ok;
-    __shared__ float s_scale;
+    __shared__ int4 s_cd_gu[32];           // gate/up copy descriptors: [NCH chunks][2 segments][4 planes]
+    __shared__ int4 s_cd_dn[2][64];        // down copy descriptors per type (Q4_K, Q6_K): [k][planes]
+    __shared__ unsigned s_gu_bytes[NCH];
+    __shared__ unsigned s_amax[16 * 4];
+    __shared__ double s_lgd[513];            // router sums of this layer: [E] logits/scale, [E] = sum x^2      // per (expert position, 256 block) max|h| of this CTA
 
     const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     const int H = a.H, E = a.E, k = a.k, I = a.I;
     const int nbH = H / QK, nbI = I / QK;
     const int P_pairs = k * I;
@@ -265,50 +356,123 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
     const int np = q1 - q0;
     const int d0 = (int)((int64_t)c * H / G), d1 = (int)((int64_t)(c + 1) * H / G);
     const int nr = d1 - d0;
+    const int racc_stride = RACC_COPIES * (E + 1);
     R* x = reinterpret_cast<R*>(a.x);
-
-    float* xs = nullptr;
     bool alive = true;
     unsigned nbar = 0;
+#define DEC_TR(layer, ph)                                                                                  \
+    do {                                                                                                   \
+        if (a.trace && tid == 0)                                                                           \
+            a.trace[((int64_t)c * a.n_layers + (layer)) * DEC_TRACE_PHASES + (ph)] = gtimer();            \
+    } while (0)
 
-    // plan for layer 0's down type (re-initialised per layer: only the down planes depend on it)
+#define DEC_TRP(layer, ph) \
+    (a.trace ? a.trace + ((int64_t)c * a.n_layers + (layer)) * DEC_TRACE_PHASES + (ph) : nullptr)
+    // gate/up row pairs are processed in groups of RPW pairs per warp (LPR lanes per row)
+    const int LPR = nbH;                    // lanes per gate/up row: one per 256-weight block
+    const int RPW = 32 / LPR;
+    const int ngroups = (np + RPW - 1) / RPW;
+
     DecodePlan P;
     P.init(H, E, k, I, a.lw[0].down_type, G);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.off_misc);
-    uint64_t* bar_gu = bars + 0;
-    uint64_t* bar_dn = bars + 1;
-    uint64_t* bar_wt = bars + 2;
+    uint64_t* bar_gu = bars;                // [NCH]
+    uint64_t* bar_dn = bars + NCH;
+    uint64_t* bar_wt = bars + NCH + 1;
     if (tid == 0) {
-        mbar_init(bar_gu, 1);
-        mbar_init(bar_dn, 1);
-        mbar_init(bar_wt, 1);
+        for (int i = 0; i < NCH + 2; ++i) mbar_init(bars + i, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    xs = reinterpret_cast<float*>(smem + P.off_xs);
+    float* xs = reinterpret_cast<float*>(smem + P.off_xs);
     float* wt = reinterpret_cast<float*>(smem + P.off_wt);
     unsigned ph_gu = 0, ph_dn = 0, ph_wt = 0;
+    const int wn_sub = (int)(((int64_t)d0 * 4) & 15) / 4;
+    const int64_t wn_lo = ((int64_t)d0 * 4) & ~(int64_t)15, wn_hi = a16((int64_t)d1 * 4);
+    const unsigned wt_bytes = (unsigned)((int64_t)nr * E * 4);
+    // bytes of one layer's down rows [d0, d1) of all k experts, per down type (16-byte supersets)
+    unsigned dn_bytes_q4 = 0, dn_bytes_q6 = 0;
+    {
+        const int64_t nblk_dn = (int64_t)H * nbI;
+        const int64_t q4_off[2] = {0, nblk_dn * 128}, q4_row[2] = {(int64_t)nbI * 128, (int64_t)nbI * 16};
+        const int64_t q6_off[4] = {0, nblk_dn * 128, nblk_dn * 192, nblk_dn * 208};
+        const int64_t q6_row[4] = {(int64_t)nbI * 128, (int64_t)nbI * 64, (int64_t)nbI * 16, (int64_t)nbI * 2};
+        for (int pl = 0; pl < 2; ++pl)
+            dn_bytes_q4 += (unsigned)(k * (a16(q4_off[pl] + (int64_t)d1 * q4_row[pl]) -
+                                           ((q4_off[pl] + (int64_t)d0 * q4_row[pl]) & ~(int64_t)15)));
+        for (int pl = 0; pl < 4; ++pl)
+            dn_bytes_q6 += (unsigned)(k * (a16(q6_off[pl] + (int64_t)d1 * q6_row[pl]) -
+                                           ((q6_off[pl] + (int64_t)d0 * q6_row[pl]) & ~(int64_t)15)));
+    }
+
+    // Copy descriptors of this CTA's share, fixed for the whole launch: {src offset lo, hi, smem
+    // offset, meta = bytes | j << 20 | chunk << 25 | up << 28 | valid << 29}; gate/up sources are
+    // relative to the slot base, down sources to the down matrix.
+    if (warp == 0) {
+        {
+            const int ci = lane, ch = ci >> 3, sg = (ci >> 2) & 1, m = ci & 3;
+            const int pa = min(np, (ch * ngroups / NCH) * RPW);
+            const int pb = min(np, ((ch + 1) * ngroups / NCH) * RPW);
+            int4 d = make_int4(0, 0, 0, 0);
+            if (pa < pb) {
+                const int j = (q0 + pa) / I + sg;
+                const int qa = max(q0 + pa, j * I), qe = min(q0 + pb, (j + 1) * I);
+                if (qa < qe && j < k) {
+                    const int i = qa - j * I, n = qe - qa;
+                    const int64_t pp = qa - q0;
+                    const int64_t nblk_gu = (int64_t)I * nbH;
+                    const bool hdr = m & 1, up = m >> 1;
+                    const int64_t src = hdr ? nblk_gu * 128 + (int64_t)i * P.gu_row_hdr : (int64_t)i * P.gu_row_qs;
+                    const int64_t dst = (hdr ? (up ? P.off_up_hdr : P.off_gate_hdr) : (up ? P.off_up_qs : P.off_gate_qs)) +
+                                        pp * (hdr ? P.gu_row_hdr : P.gu_row_qs);
+                    const unsigned bytes = (unsigned)(n * (hdr ? P.gu_row_hdr : P.gu_row_qs));
+                    d = make_int4((int)(unsigned)(src & 0xFFFFFFFF), (int)(unsigned)(src >> 32), (int)dst,
+                                  (int)(bytes | ((unsigned)j << 20) | ((unsigned)ch << 25) | ((unsigned)up << 28) | (1u << 29)));
+                }
+            }
+            s_cd_gu[ci] = d;
+            if (lane < NCH) {
+                const int qa = min(np, (lane * ngroups / NCH) * RPW), qb = min(np, ((lane + 1) * ngroups / NCH) * RPW);
+                s_gu_bytes[lane] = (unsigned)(2 * (int64_t)(qb - qa) * (P.gu_row_qs + P.gu_row_hdr));
+            }
+        }
+        const int64_t nblk_dn = (int64_t)H * nbI;
+        for (int tsel = 0; tsel < 2; ++tsel) {
+            DecodePlan Pt;
+            Pt.init(H, E, k, I, tsel == 0 ? T_Q4K : T_Q6K, G);
+            const int nplanes = tsel == 0 ? 2 : 4;
+            for (int ci = lane; ci < k * nplanes; ci += 32) {
+                const int j = ci / nplanes, pl = ci - j * nplanes;
+                int64_t off, row, dst;
+                if (pl == 0) { off = 0; row = (int64_t)nbI * 128; dst = Pt.dn_p0; }
+                else if (tsel == 0) { off = nblk_dn * 128; row = (int64_t)nbI * 16; dst = Pt.dn_p1; }
+                else if (pl == 1) { off = nblk_dn * 128; row = (int64_t)nbI * 64; dst = Pt.dn_p1; }
+                else if (pl == 2) { off = nblk_dn * 192; row = (int64_t)nbI * 16; dst = Pt.dn_p2; }
+                else { off = nblk_dn * 208; row = (int64_t)nbI * 2; dst = Pt.dn_p3; }
+                const int64_t alo = (off + (int64_t)d0 * row) & ~(int64_t)15, ahi = a16(off + (int64_t)d1 * row);
+                const int64_t so = Pt.off_dn + (int64_t)j * Pt.dn_stride + dst;
+                s_cd_dn[tsel][ci] = make_int4((int)(unsigned)(alo & 0xFFFFFFFF), (int)(unsigned)(alo >> 32), (int)so,
+                                              (int)((unsigned)(ahi - alo) | ((unsigned)j << 20) | (1u << 29)));
+            }
+        }
+    }
+
+    for (int i = tid; i < 16 * 4; i += blockDim.x) s_amax[i] = 0u;
 
     // ---- prologue: residual rows, router slice of layer 0, partial router sums ------------------
     for (int r = tid; r < nr; r += blockDim.x) xs[r] = to_f32<R>(x[d0 + r]);
-    int wn_sub = 0;
+    if (tid == 0) {
+        mbar_expect_tx(bar_wt, wt_bytes + (unsigned)(wn_hi - wn_lo));
+        bulk_g2s(wt, a.lw[0].w_router_t + (int64_t)d0 * E, wt_bytes, bar_wt);
+        bulk_g2s(smem + P.off_wn, reinterpret_cast<const uint8_t*>(a.lw[0].w_norm) + wn_lo, (unsigned)(wn_hi - wn_lo),
+                 bar_wt);
+    }
+    if (!mbar_wait(bar_wt, ph_wt)) { atomicOr(&a.sync[0], 2u); alive = false; }
+    ph_wt ^= 1;
+    __syncthreads();
     {
-        const LayerWeights& L0 = a.lw[0];
-        if (tid == 0) {
-            const unsigned wt_bytes = (unsigned)((int64_t)nr * E * 4);
-            const int64_t wn_lo = ((int64_t)d0 * 4) & ~(int64_t)15;
-            const int64_t wn_hi = a16((int64_t)d1 * 4);
-            mbar_expect_tx(bar_wt, wt_bytes + (unsigned)(wn_hi - wn_lo));
-            bulk_g2s(wt, L0.w_router_t + (int64_t)d0 * E, wt_bytes, bar_wt);
-            bulk_g2s(smem + P.off_wn, reinterpret_cast<const uint8_t*>(L0.w_norm) + wn_lo, (unsigned)(wn_hi - wn_lo),
-                     bar_wt);
-        }
-        wn_sub = (int)(((int64_t)d0 * 4) & 15) / 4;
-        if (!mbar_wait(bar_wt, ph_wt)) { atomicOr(&a.sync[0], 2u); alive = false; }
-        ph_wt ^= 1;
-        __syncthreads();
         const float* wn = reinterpret_cast<const float*>(smem + P.off_wn) + wn_sub;
-        double* acc = a.racc;                       // buffer 0
+        double* acc = a.racc + (int64_t)(c % RACC_COPIES) * (E + 1);
         for (int e = tid; e <= E; e += blockDim.x) {
             double s = 0.0;
             if (e < E) {
@@ -322,239 +486,341 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
     if (!grid_barrier(a.sync, nbar++, &s_ok)) alive = false;
 
     for (int l = 0; l < a.n_layers; ++l) {
-        const LayerWeights& L = a.lw[l];
         const int buf = l & 1;
-        P.init(H, E, k, I, L.down_type, G);
-        // ---- A. routing ------------------------------------------------------------------------
-        float* lg = reinterpret_cast<float*>(smem + P.off_lg);
-        const double* racc = a.racc + (int64_t)buf * (E + 1);
-        if (tid == 0) {
-            const double ss = ld_f64(&racc[E]);
-            const float mean = (float)(ss / H);
-            s_scale = 1.0f / sqrtf(mean + a.eps);
-        }
-        __syncthreads();
-        const float scale = s_scale;
-        for (int e = tid; e < E; e += blockDim.x) lg[e] = (float)((double)scale * ld_f64(&racc[e]));
-        __syncthreads();
-        int32_t* sel_o = a.sel_out ? a.sel_out + (int64_t)l * k : nullptr;
-        float* w_o = a.w_out ? a.w_out + (int64_t)l * k : nullptr;
-        {
-            // softmax + top-k into shared s_sel/s_w (thread 0 also writes the caller's outputs)
-            __shared__ int32_t t_sel[16];
-            __shared__ float t_w[16];
-            softmax_topk(lg, E, k, a.renorm, t_sel, t_w, redd, redf, s_sel, s_w);
-            if (tid < k) {
-                s_sel[tid] = t_sel[tid];
-                s_w[tid] = t_w[tid];
-                if (c == 0 && sel_o) { sel_o[tid] = t_sel[tid]; w_o[tid] = t_w[tid]; }
-            }
-            __syncthreads();
-        }
-        // ---- B. issue this CTA's weight copies for the whole layer ---------------------------------
-        // (every CTA issues or skips as a whole: `alive` is uniform inside a CTA)
+        // this layer's and the next layer's descriptors (global loads overlap the router read)
+        const uint8_t* L_pool = a.lw[l].pool;
+        const int64_t L_stride = a.lw[l].slot_stride, L_off_up = a.lw[l].off_up, L_off_down = a.lw[l].off_down;
+        const int L_dt = a.lw[l].down_type;
+        const float* L_wnorm = a.lw[l].w_norm;
+        const bool has_next = l + 1 < a.n_layers;
+        const float* Ln_wrt = has_next ? a.lw[l + 1].w_router_t : nullptr;
+        const float* Ln_wnorm = has_next ? a.lw[l + 1].w_norm : nullptr;
+        P.init(H, E, k, I, L_dt, G);
+        DEC_TR(l, 0);
+        // ---- A/B. warp 0: router sums -> softmax -> top-k -> copies -> renorm, all in registers;
+        //      warps 1..: fx = rms_norm(x) * ffn_norm -> Q8_K (named barriers, no CTA-wide sync) ------
         const bool issued = alive;
-        const bool issued_wt = alive && (l + 1 < a.n_layers);
-        if (tid == 0 && alive) {
-            fence_proxy_async();
-            // gate/up row pairs [q0, q1), split at expert boundaries
-            unsigned gu_bytes = (unsigned)(2 * (int64_t)np * (P.gu_row_qs + P.gu_row_hdr));
-            mbar_expect_tx(bar_gu, gu_bytes);
-            const int64_t nblk_gu = (int64_t)I * nbH;
-            for (int q = q0; q < q1;) {
-                const int j = q / I, i = q - j * I;
-                const int qe = min(q1, (j + 1) * I);
-                const int n = qe - q;
-                const uint8_t* base = L.pool + (int64_t)s_sel[j] * L.slot_stride;
-                const int64_t p = q - q0;
-                bulk_g2s(smem + P.off_gate_qs + p * P.gu_row_qs, base + (int64_t)i * P.gu_row_qs,
-                         (unsigned)(n * P.gu_row_qs), bar_gu);
-                bulk_g2s(smem + P.off_gate_hdr + p * P.gu_row_hdr, base + nblk_gu * 128 + (int64_t)i * P.gu_row_hdr,
-                         (unsigned)(n * P.gu_row_hdr), bar_gu);
-                const uint8_t* ub = base + L.off_up;
-                bulk_g2s(smem + P.off_up_qs + p * P.gu_row_qs, ub + (int64_t)i * P.gu_row_qs,
-                         (unsigned)(n * P.gu_row_qs), bar_gu);
-                bulk_g2s(smem + P.off_up_hdr + p * P.gu_row_hdr, ub + nblk_gu * 128 + (int64_t)i * P.gu_row_hdr,
-                         (unsigned)(n * P.gu_row_hdr), bar_gu);
-                q = qe;
-            }
-            // down rows [d0, d1) of every selected expert
-            const int64_t nblk_dn = (int64_t)H * nbI;
-            unsigned dn_bytes = 0;
-            int64_t plane_off[4], plane_row[4];
-            int nplanes;
-            if (P.dt == T_Q4K) {
-                nplanes = 2;
-                plane_off[0] = 0; plane_row[0] = (int64_t)nbI * 128;
-                plane_off[1] = nblk_dn * 128; plane_row[1] = (int64_t)nbI * 16;
-            } else {
-                nplanes = 4;
-                plane_off[0] = 0; plane_row[0] = (int64_t)nbI * 128;
-                plane_off[1] = nblk_dn * 128; plane_row[1] = (int64_t)nbI * 64;
-                plane_off[2] = nblk_dn * 192; plane_row[2] = (int64_t)nbI * 16;
-                plane_off[3] = nblk_dn * 208; plane_row[3] = (int64_t)nbI * 2;
-            }
-            const int64_t dst_off[4] = {P.dn_p0, P.dn_p1, P.dn_p2, P.dn_p3};
-            for (int pl = 0; pl < nplanes; ++pl) {
-                const int64_t lo = plane_off[pl] + (int64_t)d0 * plane_row[pl];
-                const int64_t hi = plane_off[pl] + (int64_t)d1 * plane_row[pl];
-                const int64_t alo = lo & ~(int64_t)15, ahi = a16(hi);
-                dn_bytes += (unsigned)(k * (ahi - alo));
-            }
-            mbar_expect_tx(bar_dn, dn_bytes);
-            for (int j = 0; j < k; ++j) {
-                const uint8_t* base = L.pool + (int64_t)s_sel[j] * L.slot_stride + L.off_down;
-                uint8_t* reg = smem + P.off_dn + (int64_t)j * P.dn_stride;
-                for (int pl = 0; pl < nplanes; ++pl) {
-                    const int64_t lo = plane_off[pl] + (int64_t)d0 * plane_row[pl];
-                    const int64_t hi = plane_off[pl] + (int64_t)d1 * plane_row[pl];
-                    const int64_t alo = lo & ~(int64_t)15, ahi = a16(hi);
-                    bulk_g2s(reg + dst_off[pl], base + alo, (unsigned)(ahi - alo), bar_dn);
-                }
-            }
-            // router slice of the next layer
-            if (l + 1 < a.n_layers) {
-                const LayerWeights& Ln = a.lw[l + 1];
-                const unsigned wt_bytes = (unsigned)((int64_t)nr * E * 4);
-                const int64_t wn_lo = ((int64_t)d0 * 4) & ~(int64_t)15;
-                const int64_t wn_hi = a16((int64_t)d1 * 4);
-                mbar_expect_tx(bar_wt, wt_bytes + (unsigned)(wn_hi - wn_lo));
-                bulk_g2s(wt, Ln.w_router_t + (int64_t)d0 * E, wt_bytes, bar_wt);
-                bulk_g2s(smem + P.off_wn, reinterpret_cast<const uint8_t*>(Ln.w_norm) + wn_lo,
-                         (unsigned)(wn_hi - wn_lo), bar_wt);
+        const bool issued_wt = alive && has_next;
+        int8_t* fxq = reinterpret_cast<int8_t*>(smem + P.off_fxq);
+        float* fxd = reinterpret_cast<float*>(smem + P.off_fxd);
+        int* fxbs32 = reinterpret_cast<int*>(smem + P.off_fxbs32);
+        // router sums: every thread t <= E adds the RACC_COPIES partial copies of entry t (one L2 round trip)
+        {
+            const double* racc = a.racc + (int64_t)buf * racc_stride;
+            for (int e = tid; e <= E; e += blockDim.x) {
+                double v = 0.0;
+#pragma unroll
+                for (int cp = 0; cp < RACC_COPIES; ++cp) v += __ldcg(racc + cp * (E + 1) + e);
+                s_lgd[e] = v;
             }
         }
-        // ---- A'. fx = rms_norm(x) * ffn_norm -> Q8_K in shared memory ------------------------------
-        {
-            int8_t* fxq = reinterpret_cast<int8_t*>(smem + P.off_fxq);
-            float* fxd = reinterpret_cast<float*>(smem + P.off_fxd);
-            int* fxbs = reinterpret_cast<int*>(smem + P.off_fxbs);
+        __syncthreads();
+        DEC_TR(l, 19);
+        const float scale = 1.0f / sqrtf((float)(s_lgd[E] / H) + a.eps);
+        if (warp == 0) {
+            int32_t* so = (c == 0 && a.sel_out) ? a.sel_out + (int64_t)l * k : nullptr;
+            float* wo = (c == 0 && a.sel_out) ? a.w_out + (int64_t)l * k : nullptr;
+            if (E <= 64) route_warp<2>(s_lgd, E, k, a.renorm, scale, lane, s_sel, s_w, so, wo, DEC_TRP(l, 1));
+            else if (E <= 128) route_warp<4>(s_lgd, E, k, a.renorm, scale, lane, s_sel, s_w, so, wo, DEC_TRP(l, 1));
+            else if (E <= 256) route_warp<8>(s_lgd, E, k, a.renorm, scale, lane, s_sel, s_w, so, wo, DEC_TRP(l, 1));
+            else route_warp<16>(s_lgd, E, k, a.renorm, scale, lane, s_sel, s_w, so, wo, DEC_TRP(l, 1));
+            __syncwarp();
+            // ---- B. this CTA's copies for the whole layer (descriptors precomputed at launch) ----
+            if (alive) {
+                if (lane < NCH) {
+                    mbar_expect_tx(bar_gu + lane, s_gu_bytes[lane]);
+                } else if (lane == NCH) {
+                    mbar_expect_tx(bar_dn, L_dt == T_Q4K ? dn_bytes_q4 : dn_bytes_q6);
+                } else if (lane == NCH + 1 && has_next) {
+                    mbar_expect_tx(bar_wt, wt_bytes + (unsigned)(wn_hi - wn_lo));
+                }
+                __syncwarp();
+                DEC_TR(l, 18);
+                {
+                    const int4 d = s_cd_gu[lane];
+                    const unsigned meta = (unsigned)d.w;
+                    if (meta >> 29) {
+                        const int j = (meta >> 20) & 31, ch = (meta >> 25) & 7;
+                        const int64_t src = ((int64_t)(unsigned)d.y << 32) | (unsigned)d.x;
+                        const uint8_t* base = L_pool + (int64_t)s_sel[j] * L_stride + (((meta >> 28) & 1) ? L_off_up : 0);
+                        bulk_g2s(smem + d.z, base + src, meta & 0xFFFFFu, bar_gu + ch);
+                    }
+                }
+                const int tsel = L_dt == T_Q4K ? 0 : 1;
+                const int n_dn = k * (L_dt == T_Q4K ? 2 : 4);
+                for (int ci = lane; ci < n_dn; ci += 32) {
+                    const int4 d = s_cd_dn[tsel][ci];
+                    const unsigned meta = (unsigned)d.w;
+                    const int j = (meta >> 20) & 31;
+                    const int64_t src = ((int64_t)(unsigned)d.y << 32) | (unsigned)d.x;
+                    bulk_g2s(smem + d.z, L_pool + (int64_t)s_sel[j] * L_stride + L_off_down + src, meta & 0xFFFFFu,
+                             bar_dn);
+                }
+                if (has_next && lane == 0) bulk_g2s(wt, Ln_wrt + (int64_t)d0 * E, wt_bytes, bar_wt);
+                if (has_next && lane == 1)
+                    bulk_g2s(smem + P.off_wn, reinterpret_cast<const uint8_t*>(Ln_wnorm) + wn_lo,
+                             (unsigned)(wn_hi - wn_lo), bar_wt);
+            }
+            DEC_TR(l, 4);
+            DEC_TR(l, 5);
+            named_sync(2, blockDim.x);              // fx (written by warps 1..) is complete
+        } else {
             const int ng = H / 16;
-            for (int g0 = 0; g0 < ng; g0 += blockDim.x) {   // groups of 16; a 256-block = 16 groups
-                const int g = g0 + tid;
+            for (int g0 = 0; g0 < ng; g0 += blockDim.x - 32) {
+                const int g = g0 + tid - 32;
                 float v[16];
                 float am = 0.f;
                 if (g < ng) {
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const int dd = 16 * g + i;
-                        const float xr = ld_resid(x + dd);
-                        v[i] = (xr * scale) * __ldg(L.w_norm + dd);
-                        am = fmaxf(am, fabsf(v[i]));
+                    for (int i = 0; i < 4; ++i) {
+                        const float4 xr = ld_resid4(x + 16 * g + 4 * i);
+                        const float4 wv = __ldg(reinterpret_cast<const float4*>(L_wnorm + 16 * g + 4 * i));
+                        v[4 * i] = (xr.x * scale) * wv.x;
+                        v[4 * i + 1] = (xr.y * scale) * wv.y;
+                        v[4 * i + 2] = (xr.z * scale) * wv.z;
+                        v[4 * i + 3] = (xr.w * scale) * wv.w;
                     }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) am = fmaxf(am, fabsf(v[i]));
                 }
+                // the 16 groups of a 256 block are 16 consecutive lanes (warps 1.. start at group 0)
 #pragma unroll
                 for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+                int bsum = 0;
                 if (g < ng) {
-                    int bs = 0;
-                    float iscale = am != 0.f ? 127.f / am : 0.f;
+                    const float iscale = am != 0.f ? 127.f / am : 0.f;
                     uint32_t packed[4] = {0, 0, 0, 0};
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const int q = am != 0.f ? min(127, __float2int_rn(iscale * v[i])) : 0;
-                        bs += q;
+                        bsum += q;
                         packed[i >> 2] |= ((uint32_t)(q & 0xFF)) << (8 * (i & 3));
                     }
-                    *reinterpret_cast<uint4*>(fxq + 16 * g) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                    fxbs[g] = bs;
+                    *reinterpret_cast<uint4*>(fxq + (g >> 4) * ACT_BLK + 16 * (g & 15)) =
+                        make_uint4(packed[0], packed[1], packed[2], packed[3]);
                     if ((g & 15) == 0) fxd[g >> 4] = am != 0.f ? 1.f / iscale : 0.f;
                 }
+                const int nb_sum = bsum + __shfl_xor_sync(0xffffffffu, bsum, 1);   // 32-value sub-block sum
+                if (g < ng && (g & 1) == 0) fxbs32[g >> 1] = nb_sum;
             }
+            named_arrive(2, blockDim.x);            // for warp 0
+            named_sync(1, blockDim.x - 32);         // among warps 1..
         }
-        __syncthreads();
-        // ---- C. gate/up + SwiGLU -------------------------------------------------------------------
-        if (issued && !mbar_wait(bar_gu, ph_gu)) { atomicOr(&a.sync[0], 2u); alive = false; }
-        ph_gu ^= 1;
-        const int lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+        // ---- C. gate/up + SwiGLU: lane = (row slot, 256-weight block) -----------------------------
         unsigned* amax = a.amax + (int64_t)buf * k * nbI;
-        if (alive) {
-            const int8_t* fxq = reinterpret_cast<const int8_t*>(smem + P.off_fxq);
-            const float* fxd = reinterpret_cast<const float*>(smem + P.off_fxd);
-            const int* fxbs = reinterpret_cast<const int*>(smem + P.off_fxbs);
-            const int nunits = nbH * 8;
-            for (int p = warp; p < np; p += nw) {
-                const int q = q0 + p, j = q / I, i = q - j * I;
-                float g = 0.f, u = 0.f;
-                for (int un = lane; un < nunits; un += 32) {
-                    const int b = un >> 3, c8 = un & 7;
-                    const uint4 wg = *reinterpret_cast<const uint4*>(smem + P.off_gate_qs + p * P.gu_row_qs + 16 * un);
-                    const uint4 hg = *reinterpret_cast<const uint4*>(smem + P.off_gate_hdr + p * P.gu_row_hdr + 16 * b);
-                    const uint4 wu = *reinterpret_cast<const uint4*>(smem + P.off_up_qs + p * P.gu_row_qs + 16 * un);
-                    const uint4 hu = *reinterpret_cast<const uint4*>(smem + P.off_up_hdr + p * P.gu_row_hdr + 16 * b);
-                    g += q4k_unit_dot(wg, hg, c8, fxq + QK * b, fxbs + 16 * b, fxd[b]);
-                    u += q4k_unit_dot(wu, hu, c8, fxq + QK * b, fxbs + 16 * b, fxd[b]);
+        {
+            const int rs = lane / LPR, b = lane % LPR;
+            const int8_t* act = fxq + ACT_BLK * b;
+            const int* bs32 = fxbs32 + 8 * b;
+            const float d8 = fxd[b];
+            int waited = -1;
+            for (int gi = warp - 1; warp > 0 && gi < ngroups; gi += nw - 1) {   // warp 0 routes and issues
+                int ch = 0;
+                while (ch + 1 < NCH && gi >= ((ch + 1) * ngroups) / NCH) ++ch;
+                for (int cw = waited + 1; cw <= ch; ++cw) {
+                    if (issued && alive && !mbar_wait(bar_gu + cw, ph_gu)) { atomicOr(&a.sync[0], 2u); alive = false; }
                 }
-                g = warp_sum(g);
-                u = warp_sum(u);
-                if (lane == 0) {
-                    const float hv = silu_f(g) * u;
+                waited = max(waited, ch);
+                if (gi == 0 && tid == 32 && a.trace)
+                    a.trace[((int64_t)c * a.n_layers + l) * DEC_TRACE_PHASES + 6] = gtimer();
+                const int p = gi * RPW + rs;
+                const bool valid = alive && p < np;
+                float gsum = 0.f, usum = 0.f;
+                if (valid) {
+                    const uint8_t* gq = smem + P.off_gate_qs + p * P.gu_row_qs + 128 * b;
+                    const uint8_t* uq = smem + P.off_up_qs + p * P.gu_row_qs + 128 * b;
+                    const uint4 hg = lds128(smem + P.off_gate_hdr + p * P.gu_row_hdr + 16 * b);
+                    const uint4 hu = lds128(smem + P.off_up_hdr + p * P.gu_row_hdr + 16 * b);
+                    const Q4Scales sg = q4_scales(hg), su = q4_scales(hu);
+                    int ig = 0, iu = 0;
+#pragma unroll
+                    for (int cc = 0; cc < 8; ++cc) {
+                        const int cr = (cc + b) & 7, g = cr >> 1, hh = cr & 1;
+                        const uint4 wg = lds128(gq + 16 * cr);
+                        const uint4 wu = lds128(uq + 16 * cr);
+                        const int4 alo = lds128i(act + 64 * g + 16 * hh);
+                        const int4 ahi = lds128i(act + 64 * g + 32 + 16 * hh);
+                        ig += q4_chunk(wg, alo, ahi, byte_of(sg.sc_lo, sg.sc_hi, 2 * g), byte_of(sg.sc_lo, sg.sc_hi, 2 * g + 1));
+                        iu += q4_chunk(wu, alo, ahi, byte_of(su.sc_lo, su.sc_hi, 2 * g), byte_of(su.sc_lo, su.sc_hi, 2 * g + 1));
+                    }
+                    const int mg = q4_min_dot(sg, bs32), mu = q4_min_dot(su, bs32);
+                    const float2 dg = __half22float2(*reinterpret_cast<const __half2*>(&hg.x));
+                    const float2 du = __half22float2(*reinterpret_cast<const __half2*>(&hu.x));
+                    gsum = d8 * (dg.x * (float)ig - dg.y * (float)mg);
+                    usum = d8 * (du.x * (float)iu - du.y * (float)mu);
+                }
+                for (int o = 1; o < LPR; o <<= 1) {
+                    gsum += __shfl_xor_sync(0xffffffffu, gsum, o);
+                    usum += __shfl_xor_sync(0xffffffffu, usum, o);
+                }
+                if (valid && b == 0) {
+                    const int q = q0 + p, j = q / I, i = q - j * I;
+                    const float hv = silu_f(gsum) * usum;
                     a.h[(int64_t)j * I + i] = hv;
-                    atomicMax(&amax[j * nbI + (i >> 8)], __float_as_uint(fabsf(hv)));
+                    atomicMax(&s_amax[j * nbI + (i >> 8)], __float_as_uint(fabsf(hv)));
                 }
             }
+            // drain the chunks this warp did not need (every chunk's phase must complete)
+            for (int cw = waited + 1; cw < NCH; ++cw)
+                if (issued && !mbar_wait(bar_gu + cw, ph_gu)) { atomicOr(&a.sync[0], 2u); alive = false; }
         }
-        if (!grid_barrier(a.sync, nbar++, &s_ok)) alive = false;
-        // ---- D. down + combine -------------------------------------------------------------------
+        ph_gu ^= 1;
+        // publish this CTA's block maxima of h (a few atomics per CTA instead of one per row)
+        __syncthreads();
+        if (tid < k * nbI) {
+            const unsigned v = s_amax[tid];
+            if (v) atomicMax(&amax[tid], v);
+            s_amax[tid] = 0u;
+        }
+        DEC_TR(l, 7);
+        if (!grid_barrier(a.sync, nbar++, &s_ok, DEC_TRP(l, 14))) alive = false;
+        DEC_TR(l, 8);
+        // ---- D. Q8_K of h, down rows of every selected expert, combine, next router sums ---------
         if (c == 0 && alive) {
-            double* rz = a.racc + (int64_t)buf * (E + 1);
-            for (int e = tid; e <= E; e += blockDim.x) rz[e] = 0.0;
+            double* rz = a.racc + (int64_t)buf * racc_stride;
+            for (int e = tid; e < racc_stride; e += blockDim.x) rz[e] = 0.0;
             unsigned* az = a.amax + (int64_t)(buf ^ 1) * k * nbI;
             for (int e = tid; e < k * nbI; e += blockDim.x) az[e] = 0u;
         }
-        {
-            int8_t* hq = reinterpret_cast<int8_t*>(smem + P.off_hq);
-            float* hd = reinterpret_cast<float*>(smem + P.off_hd);
-            int* hbs = reinterpret_cast<int*>(smem + P.off_hbs);
-            const int ng = k * I / 16;
-            for (int g = tid; g < ng; g += blockDim.x) {
-                const int e0 = 16 * g;
-                const int j = e0 / I, blk = (e0 - j * I) >> 8;
-                const float am = __uint_as_float(ld_relaxed(&amax[j * nbI + blk]));
+        int8_t* hq = reinterpret_cast<int8_t*>(smem + P.off_hq);
+        float* hd = reinterpret_cast<float*>(smem + P.off_hd);
+        int* hbs = reinterpret_cast<int*>(smem + P.off_hbs);
+        for (int g0 = 0; g0 < k * I / 16; g0 += blockDim.x) {
+            const int g = g0 + tid;
+            const bool ok = g < k * I / 16;
+            const int e0 = 16 * (ok ? g : 0);
+            const int j = e0 / I, eb = e0 - j * I, blk = eb >> 8, gl = (eb & 255) >> 4;
+            int bsum = 0;
+            if (ok) {
+                const float am = __uint_as_float(__ldcg(amax + j * nbI + blk));
                 const float iscale = am != 0.f ? 127.f / am : 0.f;
-                int bs = 0;
-                uint32_t packed[4] = {0, 0, 0, 0};
                 float hv16[16];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const float4 t4 = ld_f32x4(a.h + e0 + 4 * i);
+                    const float4 t4 = __ldcg(reinterpret_cast<const float4*>(a.h + e0 + 4 * i));
                     hv16[4 * i] = t4.x; hv16[4 * i + 1] = t4.y; hv16[4 * i + 2] = t4.z; hv16[4 * i + 3] = t4.w;
                 }
+                uint32_t packed[4] = {0, 0, 0, 0};
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float hv = hv16[i];
-                    const int q = am != 0.f ? min(127, __float2int_rn(iscale * hv)) : 0;
-                    bs += q;
+                    const int q = am != 0.f ? min(127, __float2int_rn(iscale * hv16[i])) : 0;
+                    bsum += q;
                     packed[i >> 2] |= ((uint32_t)(q & 0xFF)) << (8 * (i & 3));
                 }
-                *reinterpret_cast<uint4*>(hq + e0) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                hbs[g] = bs;
-                if (((e0 - j * I) & 255) == 0) hd[j * nbI + blk] = am != 0.f ? 1.f / iscale : 0.f;
+                *reinterpret_cast<uint4*>(hq + j * hq_stride(nbI) + blk * ACT_BLK + (eb & 255)) =
+                    make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                if (gl == 0) hd[j * nbI + blk] = am != 0.f ? 1.f / iscale : 0.f;
+            }
+            const int pair = bsum + __shfl_xor_sync(0xffffffffu, bsum, 1);
+            if (ok) {
+                if (L_dt == T_Q6K) {
+                    // 16-sums in unit order [unit v = 2*h2 + r][a]: group gl = 8*h2 + 2*a + r
+                    const int h2 = gl >> 3, aa = (gl >> 1) & 3, rr = gl & 1;
+                    hbs[(j * nbI + blk) * 16 + 4 * (2 * h2 + rr) + aa] = bsum;
+                } else if ((gl & 1) == 0) {
+                    hbs[(j * nbI + blk) * 8 + (gl >> 1)] = pair;     // 32-sums per sub-block
+                }
             }
         }
         __syncthreads();
-        // offset of row d0 inside the 16-byte-aligned copy of the fp16 d plane (Q6_K only)
-        const int dsub = P.dt == T_Q6K ? (int)(((int64_t)d0 * nbI * 2) & 15) : 0;
-        if (issued && !mbar_wait(bar_dn, ph_dn)) { atomicOr(&a.sync[0], 2u); alive = false; }
+        DEC_TR(l, 9);
+        {
+            // four lanes per (row, expert) item, one per 256-weight block of the row (nbI <= 4)
+            float* y = reinterpret_cast<float*>(smem + P.off_y);
+            const int dsub = L_dt == T_Q6K ? (int)(((int64_t)d0 * nbI * 2) & 15) : 0;
+            const int bl = lane & 3;
+            const int items = nr * k, ngi = (items + 7) / 8;
+            if (issued && !mbar_wait(bar_dn, ph_dn)) { atomicOr(&a.sync[0], 2u); alive = false; }
+            DEC_TR(l, 10);
+            for (int gi = warp; gi < ngi; gi += nw) {
+                const int it = gi * 8 + (lane >> 2);
+                const bool valid = alive && it < items && bl < nbI;
+                const int r = valid ? it / k : 0, j = valid ? it - r * k : 0;
+                float acc = 0.f;
+                if (valid) {
+                    const uint8_t* reg = smem + P.off_dn + (int64_t)j * P.dn_stride;
+                    const int64_t blk = (int64_t)r * nbI + bl;
+                    const int8_t* act = hq + j * hq_stride(nbI) + ACT_BLK * bl;
+                    const float d8 = hd[j * nbI + bl];
+                    const int rot = (it + bl) & 7;
+                    if (L_dt == T_Q6K) {
+                        const uint4 S = lds128(reg + P.dn_p2 + blk * 16);
+                        const float d6 = __half2float(__ushort_as_half(
+                            *reinterpret_cast<const unsigned short*>(reg + P.dn_p3 + dsub + blk * 2)));
+                        const int* bsu = hbs + (j * nbI + bl) * 16;
+                        int isum = 0;
+#pragma unroll
+                        for (int vv = 0; vv < 4; ++vv) {
+                            const int v = (vv + rot) & 3, h2 = v >> 1, rr = v & 1;
+                            const uint4 A = lds128(reg + P.dn_p0 + blk * 128 + 64 * h2 + 16 * rr);
+                            const uint4 B = lds128(reg + P.dn_p0 + blk * 128 + 64 * h2 + 32 + 16 * rr);
+                            const uint4 C = lds128(reg + P.dn_p1 + blk * 64 + 32 * h2 + 16 * rr);
+                            const int8_t* a0 = act + 128 * h2 + 16 * rr;
+                            const int4 x0 = lds128i(a0), x1 = lds128i(a0 + 32), x2 = lds128i(a0 + 64), x3 = lds128i(a0 + 96);
+                            const int4 bs4 = lds128i(bsu + 4 * v);
+                            const uint32_t Aw[4] = {A.x, A.y, A.z, A.w}, Bw[4] = {B.x, B.y, B.z, B.w};
+                            const uint32_t Cw[4] = {C.x, C.y, C.z, C.w};
+                            const int xa0[4] = {x0.x, x0.y, x0.z, x0.w}, xa1[4] = {x1.x, x1.y, x1.z, x1.w};
+                            const int xa2[4] = {x2.x, x2.y, x2.z, x2.w}, xa3[4] = {x3.x, x3.y, x3.z, x3.w};
+                            int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const uint32_t cw = Cw[i];
+                                s0 = __dp4a((int)((Aw[i] & 0x0F0F0F0Fu) | ((cw << 4) & 0x30303030u)), xa0[i], s0);
+                                s1 = __dp4a((int)((Bw[i] & 0x0F0F0F0Fu) | ((cw << 2) & 0x30303030u)), xa1[i], s1);
+                                s2 = __dp4a((int)(((Aw[i] >> 4) & 0x0F0F0F0Fu) | (cw & 0x30303030u)), xa2[i], s2);
+                                s3 = __dp4a((int)(((Bw[i] >> 4) & 0x0F0F0F0Fu) | ((cw >> 2) & 0x30303030u)), xa3[i], s3);
+                            }
+                            // int8 scales sc[8h2 + rr + 2a]: bytes of word 2h2 (a = 0, 1) and 2h2+1 (a = 2, 3)
+                            const uint32_t wa = h2 ? S.z : S.x, wb = h2 ? S.w : S.y;
+                            const int sh = 8 * rr;
+                            isum += sext8(wa >> sh) * (s0 - 32 * bs4.x) + sext8(wa >> (sh + 16)) * (s1 - 32 * bs4.y) +
+                                    sext8(wb >> sh) * (s2 - 32 * bs4.z) + sext8(wb >> (sh + 16)) * (s3 - 32 * bs4.w);
+                        }
+                        acc = d8 * d6 * (float)isum;
+                    } else {
+                        const uint8_t* wq = reg + P.dn_p0 + blk * 128;
+                        const uint4 hh4 = lds128(reg + P.dn_p1 + blk * 16);
+                        const Q4Scales s4 = q4_scales(hh4);
+                        int isc = 0;
+#pragma unroll
+                        for (int cc = 0; cc < 8; ++cc) {
+                            const int cr = (cc + rot) & 7, g = cr >> 1, hh = cr & 1;
+                            const uint4 w = lds128(wq + 16 * cr);
+                            const int4 alo = lds128i(act + 64 * g + 16 * hh);
+                            const int4 ahi = lds128i(act + 64 * g + 32 + 16 * hh);
+                            isc += q4_chunk(w, alo, ahi, byte_of(s4.sc_lo, s4.sc_hi, 2 * g),
+                                            byte_of(s4.sc_lo, s4.sc_hi, 2 * g + 1));
+                        }
+                        const int mn = q4_min_dot(s4, hbs + (j * nbI + bl) * 8);
+                        const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hh4.x));
+                        acc = d8 * (dm.x * (float)isc - dm.y * (float)mn);
+                    }
+                }
+                acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+                if (valid && bl == 0) y[r * k + j] = acc;
+            }
+        }
         ph_dn ^= 1;
-        if (alive) {
-            if (P.dt == T_Q4K) down_phase<T_Q4K>(P, smem, nr, k, dsub);
-            else down_phase<T_Q6K>(P, smem, nr, k, dsub);
-        }
         __syncthreads();
-        const float* y = reinterpret_cast<const float*>(smem + P.off_y);
-        for (int r = tid; r < nr; r += blockDim.x) {
-            float acc = 0.f;
-            for (int j = 0; j < k; ++j) acc += s_w[j] * y[r * k + j];
-            const R xn = from_f32<R>(acc + xs[r]);
-            if (alive) x[d0 + r] = xn;
-            xs[r] = to_f32<R>(xn);
+        DEC_TR(l, 11);
+        {
+            const float* y = reinterpret_cast<const float*>(smem + P.off_y);
+            for (int r = tid; r < nr; r += blockDim.x) {
+                float acc = 0.f;
+                for (int j = 0; j < k; ++j) acc += s_w[j] * y[r * k + j];
+                const R xn = from_f32<R>(acc + xs[r]);
+                if (alive) x[d0 + r] = xn;
+                xs[r] = to_f32<R>(xn);
+            }
         }
-        if (l + 1 < a.n_layers) {
+        if (has_next) {
             if (issued_wt && !mbar_wait(bar_wt, ph_wt)) { atomicOr(&a.sync[0], 2u); alive = false; }
             ph_wt ^= 1;
             __syncthreads();
             const float* wn = reinterpret_cast<const float*>(smem + P.off_wn) + wn_sub;
-            double* acc = a.racc + (int64_t)(buf ^ 1) * (E + 1);
+            double* acc = a.racc + (int64_t)(buf ^ 1) * racc_stride + (int64_t)(c % RACC_COPIES) * (E + 1);
             for (int e = tid; e <= E; e += blockDim.x) {
                 double s = 0.0;
                 if (e < E) {
@@ -564,9 +830,13 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
                 }
                 if (alive) atomicAdd(&acc[e], s);
             }
-            if (!grid_barrier(a.sync, nbar++, &s_ok)) alive = false;
+            DEC_TR(l, 12);
+            if (!grid_barrier(a.sync, nbar++, &s_ok, DEC_TRP(l, 16))) alive = false;
         }
+        DEC_TR(l, 13);
     }
+#undef DEC_TR
+#undef DEC_TRP
     // ---- exit: the last CTA out restores the zero state of the counters and max buffers --------
     __syncthreads();
     if (tid == 0) {
@@ -576,8 +846,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
             __threadfence();
             unsigned* az = a.amax + (int64_t)((a.n_layers - 1) & 1) * k * nbI;
             for (int e = 0; e < k * nbI; ++e) az[e] = 0u;
-            double* rz = a.racc + (int64_t)(a.n_layers & 1) * (E + 1);
-            for (int e = 0; e <= E; ++e) rz[e] = 0.0;
             a.sync[1] = 0u;
             a.sync[2] = 0u;
             __threadfence();
@@ -586,18 +854,25 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
 }
 
 int decode_max_tokens() { return 1; }
-
-static int g_num_sms = 0;
-
-bool decode_supported(const Dims& d, const LayerWeights* lws, int n_layers) {
-    if (d.k > 16 || d.E % 4 != 0 || d.E > 1024) return false;
+int decode_grid() {
     int dev = 0;
     cudaGetDevice(&dev);
     if (g_num_sms == 0) cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    int max_smem = 0;
+    return g_num_sms;
+}
+int decode_trace_phases() { return DEC_TRACE_PHASES; }
+
+bool decode_supported(const Dims& d, const LayerWeights* lws, int n_layers) {
+    if (d.k > 16 || d.E % 4 != 0 || d.E > 512) return false;
+    const int nbH = d.H / QK, nbI = d.I / QK;
+    if (nbH > 32 || (nbH & (nbH - 1)) != 0) return false;    // lanes per gate/up row: a power of two <= 32
+    if (nbI > 4) return false;                                // down rows: one lane per block, 4 lanes per item
+    const int G = decode_grid();
+    int dev = 0, max_smem = 0;
+    cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    const int G = g_num_sms;
-    if ((int64_t)d.k * d.I < G || d.H < G) return false;   // every CTA must own rows
+    if ((int64_t)d.k * d.I < G || d.H < G) return false;     // every CTA must own rows
+    if ((d.k * d.I + G - 1) / G > d.I) return false;          // a CTA's pairs span at most 2 experts
     for (int l = 0; l < n_layers; ++l) {
         const LayerWeights& L = lws[l];
         if (L.gate_type != T_Q4K || L.up_type != T_Q4K) return false;
@@ -605,19 +880,16 @@ bool decode_supported(const Dims& d, const LayerWeights* lws, int n_layers) {
         if (L.shared) return false;
         DecodePlan P;
         P.init(d.H, d.E, d.k, d.I, L.down_type, G);
-        if (P.total + 2048 > max_smem) return false;
+        if (P.total + 1024 > max_smem) return false;   // + static shared memory
     }
     return true;
 }
 
 cudaError_t launch_decode_persistent(const Dims& d, const LayerWeights* lws_dev, int n_layers, const Scratch& sc,
                                      void* x_inout, int T, int32_t* sel_out, float* w_out, cudaStream_t s,
-                                     int* /*unused*/) {
+                                     unsigned long long* trace) {
     if (T != 1) return cudaErrorInvalidValue;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (g_num_sms == 0) cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    const int G = g_num_sms;
+    const int G = decode_grid();
     int64_t smem = 0;
     for (int dt : {(int)T_Q4K, (int)T_Q6K}) {
         DecodePlan P;
@@ -635,6 +907,7 @@ cudaError_t launch_decode_persistent(const Dims& d, const LayerWeights* lws_dev,
     a.amax = sc.amax;
     a.racc = reinterpret_cast<double*>(sc.partials);
     a.sync = sc.sync;
+    a.trace = trace;
     void* args[] = {&a};
     cudaError_t e;
     if (d.resid_bf16) {

@@ -51,6 +51,8 @@ struct hoard_moe_ctx {
     int routed_T = 0;
     LayerWeights* lw_dev = nullptr;    // device copy of every layer's LayerWeights (persistent kernel)
     bool decode_ok = false;            // the persistent decode kernel supports these shapes / types
+    unsigned long long* trace = nullptr;
+    int64_t trace_cap = 0;
     std::string err;
 };
 
@@ -386,8 +388,10 @@ int hoard_moe_layers(hoard_moe_ctx* c, int layer0, int n_layers, void* x_inout, 
     const int k = c->dims.k;
     HCHECK(c, cudaSetDevice(c->desc.device));
     if (T == 1 && c->decode_impl == 1 && c->decode_ok) {
+        unsigned long long* tr = nullptr;
+        if (c->trace && (int64_t)decode_grid() * n_layers * decode_trace_phases() <= c->trace_cap) tr = c->trace;
         HCHECK(c, launch_decode_persistent(c->dims, c->lw_dev + layer0, n_layers, c->sc, x_inout, T, sel_out, w_out,
-                                           (cudaStream_t)stream, nullptr));
+                                           (cudaStream_t)stream, tr));
         ++c->launches;
         return HOARD_OK;
     }
@@ -411,6 +415,20 @@ int hoard_moe_layer(hoard_moe_ctx* c, int layer, void* x_inout, int T, int32_t* 
 int hoard_moe_set_decode_impl(hoard_moe_ctx* c, int impl) {
     if (!c || impl < 0 || impl > 1) return HOARD_EINVAL;
     c->decode_impl = impl;
+    return HOARD_OK;
+}
+
+int hoard_moe_set_trace(hoard_moe_ctx* c, uint64_t* dev_buf, int64_t capacity) {
+    if (!c || capacity < 0 || (capacity > 0 && !dev_buf)) return HOARD_EINVAL;
+    c->trace = capacity > 0 ? reinterpret_cast<unsigned long long*>(dev_buf) : nullptr;
+    c->trace_cap = capacity;
+    return HOARD_OK;
+}
+
+int hoard_moe_trace_layout(const hoard_moe_ctx* c, int* ctas, int* phases) {
+    if (!c || !ctas || !phases) return HOARD_EINVAL;
+    *ctas = decode_grid();
+    *phases = decode_trace_phases();
     return HOARD_OK;
 }
 

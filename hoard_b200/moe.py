@@ -33,6 +33,7 @@ EXPORTED = [
     "hoard_moe_create", "hoard_moe_destroy", "hoard_moe_set_router", "hoard_moe_upload_expert",
     "hoard_moe_set_shared", "hoard_moe_route", "hoard_moe_experts", "hoard_moe_layer", "hoard_moe_layers",
     "hoard_moe_sync_status", "hoard_moe_expert_bytes", "hoard_moe_launch_count", "hoard_moe_set_decode_impl",
+    "hoard_moe_set_trace", "hoard_moe_trace_layout",
     "hoard_moe_last_error", "hoard_strerror",
 ]
 
@@ -81,6 +82,8 @@ def lib() -> ctypes.CDLL:
         L.hoard_moe_launch_count.argtypes = [vp]
         L.hoard_moe_launch_count.restype = i64
         L.hoard_moe_set_decode_impl.argtypes = [vp, i32]
+        L.hoard_moe_set_trace.argtypes = [vp, vp, i64]
+        L.hoard_moe_trace_layout.argtypes = [vp, ctypes.POINTER(i32), ctypes.POINTER(i32)]
         L.hoard_moe_last_error.argtypes = [vp]
         L.hoard_moe_last_error.restype = ctypes.c_char_p
         L.hoard_strerror.argtypes = [i32]
@@ -158,6 +161,18 @@ class MoEContext:
 
     def set_decode_impl(self, impl: int):
         self._check(lib().hoard_moe_set_decode_impl(self._h, impl), "set_decode_impl")
+
+    def set_trace(self, buf: torch.Tensor | None):
+        """Enables phase stamps of the persistent decode kernel into an int64 CUDA tensor."""
+        if buf is None:
+            self._check(lib().hoard_moe_set_trace(self._h, None, 0), "set_trace")
+        else:
+            self._check(lib().hoard_moe_set_trace(self._h, _ptr(buf), buf.numel()), "set_trace")
+
+    def trace_layout(self):
+        ctas, phases = ctypes.c_int(), ctypes.c_int()
+        self._check(lib().hoard_moe_trace_layout(self._h, ctypes.byref(ctas), ctypes.byref(phases)), "trace_layout")
+        return ctas.value, phases.value
 
     def sync_status(self, stream=None):
         self._check(lib().hoard_moe_sync_status(self._h, _stream(stream)), "sync_status")

@@ -126,6 +126,17 @@ int hoard_moe_layers(hoard_moe_ctx* ctx, int layer0, int n_layers, void* x_inout
  * (src/run_moe_stream.cpp:56); this library reports it. */
 int hoard_moe_sync_status(hoard_moe_ctx* ctx, hoard_stream stream);
 
+/* Phase tracing of the persistent decode kernel (the counterpart of hoard's per-phase timers
+ * tA/tFetch/tB, src/run_qwen35.cpp:434-435, :846-853). With capacity > 0, every later T = 1 fused
+ * launch whose stamps fit writes %globaltimer values (ns) into dev_buf laid out
+ * [cta][layer][phase]; capacity 0 turns tracing off. Phases: 0 layer start, 1 routed,
+ * 2 copies issued, 3 fx quantised, 4 gate/up bytes landed, 5 h written, 6 past barrier,
+ * 7 h quantised, 8 down bytes landed, 9 down done, 10 combined + router sums, 11 past barrier. */
+int hoard_moe_set_trace(hoard_moe_ctx* ctx, uint64_t* dev_buf, int64_t capacity);
+
+/* CTAs per persistent launch and stamps per (CTA, layer) of the trace layout. */
+int hoard_moe_trace_layout(const hoard_moe_ctx* ctx, int* ctas, int* phases);
+
 /* Bytes of one expert's raw GGUF gate+up+down at `layer` (what upload_expert reads). */
 int64_t hoard_moe_expert_bytes(const hoard_moe_ctx* ctx, int layer);
 

@@ -124,9 +124,11 @@ def test_c2_bf16_residual(qwen_c2):
     xb = torch.from_numpy(x).to(torch.bfloat16).float().numpy()   # the input the layer actually sees
     out, sel, w = run_layer(ctx, xb, resid=torch.bfloat16)
     ref = oracle_layer(L, xb, orc.MODE_GGML)[0]
-    # one bf16 rounding of the output on top of the f32 result
-    assert np.abs(out - ref).max() <= np.abs(ref).max() * 2 ** -8 + 1e-6
-    assert rel_l2(out - xb, ref - xb) < 5e-3
+    refb = torch.from_numpy(ref).to(torch.bfloat16).float().numpy()
+    # the output is the f32 result rounded once to bf16: equal to the rounded oracle, or one bf16
+    # step away where the f32 values straddle a rounding boundary
+    assert (np.abs(out - refb) <= np.abs(refb) * 2 ** -7 + 1e-30).all()
+    assert (out == refb).mean() > 0.98
     ctx.close()
 
 
@@ -266,6 +268,21 @@ def test_decode_persistent_matches_grouped_and_oracle(resid):
         ref = ref_l if resid == torch.float32 else torch.from_numpy(ref_l).to(torch.bfloat16).float().numpy()
     assert rel_l2(outs[1][0] - x_np, ref - x_np) < (1e-3 if resid == torch.float32 else 1e-2)
     ctx.close()
+
+
+def test_decode_takes_the_persistent_kernel(qwen_c2):
+    """A T = 1 fused call at the benchmark shape is one cooperative launch (no silent fallback)."""
+    spec, L, ctx = qwen_c2
+    x = torch.from_numpy(make_x(1, spec.H, seed=7)).cuda(DEV)
+    n0 = ctx.launch_count
+    ctx.layer(0, x)
+    ctx.sync_status()
+    assert ctx.launch_count - n0 == 1
+    ctx.set_decode_impl(0)
+    n0 = ctx.launch_count
+    ctx.layer(0, x)
+    ctx.set_decode_impl(1)
+    assert ctx.launch_count - n0 > 1
 
 
 def test_decode_persistent_repeatable_and_counters_reset(qwen_c2):
