@@ -79,4 +79,9 @@ cudaError_t launch_decode_persistent(const Dims& d, const LayerWeights* lws_dev,
                                      void* x_inout, int T, int32_t* sel_out, float* w_out, cudaStream_t s,
                                      unsigned long long* trace);
 
+// The same persistent decode kernel with its scratch in a static device array (no allocation).
+bool decode_static_fits(const Dims& d);
+cudaError_t launch_decode_static(const Dims& d, const LayerWeights* lws_dev, int n_layers, void* x_inout,
+                                 int32_t* sel_out, float* w_out, cudaStream_t s);
+
 }  // namespace hoard

@@ -24,6 +24,8 @@
 #include "kernels.h"
 #include "block_ops.cuh"
 
+#include <mutex>
+
 namespace hoard {
 
 static int g_num_sms = 0;
@@ -922,6 +924,68 @@ cudaError_t launch_decode_persistent(const Dims& d, const LayerWeights* lws_dev,
                                         s);
     }
     return e;
+}
+
+// ---- decode without any device allocation ---------------------------------------------------------
+// Some callers cannot allocate device memory when they run a decode step: code inside a CUDA stream
+// capture that forbids cudaMalloc, or an engine whose device memory is entirely handed out by its own
+// arena after start-up (hoard itself sizes its expert slot pool to the VRAM budget). For them the
+// persistent decode kernel can take its scratch (h, the block maxima of h, the router accumulators and
+// the grid-barrier words) from this fixed file-scope device array instead of a context's scratch.
+// Every GPU that loads this library holds the array until the process exits.
+constexpr int NOALLOC_MAX_K = 16;       // experts per token
+constexpr int NOALLOC_MAX_I = 1024;     // expert intermediate size
+constexpr int NOALLOC_MAX_E = 512;      // experts per layer
+constexpr size_t NOALLOC_H_BYTES = (size_t)NOALLOC_MAX_K * NOALLOC_MAX_I * 4;                  // 64 KiB
+constexpr size_t NOALLOC_AMAX_BYTES = 2 * NOALLOC_MAX_K * (NOALLOC_MAX_I / QK) * 4;           // 512 B
+constexpr size_t NOALLOC_RACC_BYTES = (size_t)2 * RACC_COPIES * (NOALLOC_MAX_E + 1) * 8;       // 65,664 B
+constexpr size_t NOALLOC_SYNC_BYTES = 256;
+constexpr size_t NOALLOC_ZERO_BYTES = NOALLOC_AMAX_BYTES + NOALLOC_RACC_BYTES + NOALLOC_SYNC_BYTES;
+constexpr size_t NOALLOC_BYTES = NOALLOC_H_BYTES + NOALLOC_ZERO_BYTES;                         // ~130 KiB
+static __device__ __align__(256) unsigned char g_decode_scratch[NOALLOC_BYTES];
+
+static std::mutex g_scratch_mu;
+static void* g_scratch_addr[64];          // per device ordinal, resolved on the first call there
+
+// Device address of g_decode_scratch on the current device. In host code the array's name is only a
+// host-side stand-in, so the address is looked up once per device with that device current.
+static cudaError_t decode_scratch_address(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_decode_scratch);
+        if (e != cudaSuccess) return e;
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
+    return cudaSuccess;
+}
+
+bool decode_static_fits(const Dims& d) {
+    return d.k <= NOALLOC_MAX_K && d.I <= NOALLOC_MAX_I && d.E <= NOALLOC_MAX_E;
+}
+
+cudaError_t launch_decode_static(const Dims& d, const LayerWeights* lws_dev, int n_layers, void* x_inout,
+                                 int32_t* sel_out, float* w_out, cudaStream_t s) {
+    if (!decode_static_fits(d)) return cudaErrorInvalidValue;
+    void* base = nullptr;
+    cudaError_t e = decode_scratch_address(&base);
+    if (e != cudaSuccess) return e;
+    uint8_t* b = static_cast<uint8_t*>(base);
+    Scratch sc{};
+    sc.h = reinterpret_cast<float*>(b);
+    sc.amax = reinterpret_cast<unsigned*>(b + NOALLOC_H_BYTES);
+    sc.partials = reinterpret_cast<float*>(b + NOALLOC_H_BYTES + NOALLOC_AMAX_BYTES);
+    sc.sync = reinterpret_cast<unsigned*>(b + NOALLOC_H_BYTES + NOALLOC_AMAX_BYTES + NOALLOC_RACC_BYTES);
+    // the array keeps whatever the last call left: clear everything the kernel expects at zero
+    // (block maxima, router accumulators, barrier counters, error word); h needs no clearing
+    e = cudaMemsetAsync(b + NOALLOC_H_BYTES, 0, NOALLOC_ZERO_BYTES, s);
+    if (e != cudaSuccess) return e;
+    return launch_decode_persistent(d, lws_dev, n_layers, sc, x_inout, 1, sel_out, w_out, s, nullptr);
 }
 
 }  // namespace hoard

@@ -412,6 +412,29 @@ int hoard_moe_layer(hoard_moe_ctx* c, int layer, void* x_inout, int T, int32_t* 
     return hoard_moe_layers(c, layer, 1, x_inout, T, sel_out, w_out, stream);
 }
 
+int hoard_moe_decode_noalloc(hoard_moe_ctx* c, int layer0, int n_layers, void* x_inout, int32_t* sel_out,
+                             float* w_out, hoard_stream stream) {
+    if (!c) return HOARD_EINVAL;
+    if (n_layers <= 0 || layer0 < 0 || layer0 + n_layers > c->desc.n_layer)
+        return fail(c, HOARD_EINVAL, "layer range out of bounds");
+    if (!x_inout) return fail(c, HOARD_EINVAL, "null x");
+    if ((sel_out == nullptr) != (w_out == nullptr)) return fail(c, HOARD_EINVAL, "sel_out and w_out go together");
+    if (!decode_static_fits(c->dims))
+        return fail(c, HOARD_EINVAL, "shape exceeds the static decode scratch (needs n_expert_used <= 16, "
+                                     "n_ff <= 1024, n_expert <= 512)");
+    if (!c->decode_ok || c->desc.n_slots < c->dims.E)
+        return fail(c, HOARD_ESTATE, "the persistent decode kernel does not support this context");
+    for (int l = layer0; l < layer0 + n_layers; ++l) {
+        int rc = check_ready(c, l);
+        if (rc) return rc;
+    }
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    HCHECK(c, launch_decode_static(c->dims, c->lw_dev + layer0, n_layers, x_inout, sel_out, w_out,
+                                   (cudaStream_t)stream));
+    ++c->launches;
+    return HOARD_OK;
+}
+
 int hoard_moe_set_decode_impl(hoard_moe_ctx* c, int impl) {
     if (!c || impl < 0 || impl > 1) return HOARD_EINVAL;
     c->decode_impl = impl;

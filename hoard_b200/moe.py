@@ -33,7 +33,7 @@ EXPORTED = [
     "hoard_moe_create", "hoard_moe_destroy", "hoard_moe_set_router", "hoard_moe_upload_expert",
     "hoard_moe_set_shared", "hoard_moe_route", "hoard_moe_experts", "hoard_moe_layer", "hoard_moe_layers",
     "hoard_moe_sync_status", "hoard_moe_expert_bytes", "hoard_moe_launch_count", "hoard_moe_set_decode_impl",
-    "hoard_moe_set_trace", "hoard_moe_trace_layout",
+    "hoard_moe_set_trace", "hoard_moe_trace_layout", "hoard_moe_decode_noalloc",
     "hoard_moe_last_error", "hoard_strerror",
 ]
 
@@ -83,6 +83,7 @@ def lib() -> ctypes.CDLL:
         L.hoard_moe_launch_count.restype = i64
         L.hoard_moe_set_decode_impl.argtypes = [vp, i32]
         L.hoard_moe_set_trace.argtypes = [vp, vp, i64]
+        L.hoard_moe_decode_noalloc.argtypes = [vp, i32, i32, vp, vp, vp, vp]
         L.hoard_moe_trace_layout.argtypes = [vp, ctypes.POINTER(i32), ctypes.POINTER(i32)]
         L.hoard_moe_last_error.argtypes = [vp]
         L.hoard_moe_last_error.restype = ctypes.c_char_p
@@ -222,6 +223,13 @@ class MoEContext:
         T = x_inout.shape[0]
         self._check(lib().hoard_moe_layer(self._h, layer, _ptr(x_inout), T, _ptr(sel_out), _ptr(w_out),
                                           _stream(stream)), "layer")
+        return x_inout
+
+    def decode_noalloc(self, layer0: int, n_layers: int, x_inout: torch.Tensor, sel_out=None, w_out=None,
+                       stream=None):
+        """T = 1 decode over n_layers layers with the library's static scratch (no device allocation)."""
+        self._check(lib().hoard_moe_decode_noalloc(self._h, layer0, n_layers, _ptr(x_inout), _ptr(sel_out),
+                                                   _ptr(w_out), _stream(stream)), "decode_noalloc")
         return x_inout
 
     def layers(self, layer0: int, n_layers: int, x_inout: torch.Tensor, sel_out=None, w_out=None, stream=None):

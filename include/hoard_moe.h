@@ -120,6 +120,23 @@ int hoard_moe_layer(hoard_moe_ctx* ctx, int layer, void* x_inout, int T, int32_t
 int hoard_moe_layers(hoard_moe_ctx* ctx, int layer0, int n_layers, void* x_inout, int T,
                      int32_t* sel_out, float* w_out, hoard_stream stream);
 
+/* Decode (T = 1) through n_layers consecutive fused layers, like hoard_moe_layers, but without any
+ * device allocation and without the context's scratch: the kernel's scratch (about 130 KiB) is a
+ * fixed device array inside this library. It exists for callers that cannot allocate device memory
+ * when they run a step -- code inside a CUDA stream capture that forbids cudaMalloc, or an engine
+ * whose device memory is fully handed out by its own arena after start-up -- while the weights stay
+ * in a context created at start-up. No counterpart in the hoard project.
+ *   - Limits: n_expert_used <= 16, n_ff <= 1024, n_expert <= 512; larger shapes return HOARD_EINVAL.
+ *     Contexts the persistent decode kernel cannot serve return HOARD_ESTATE.
+ *   - The first call on each device looks up the array's device address (cudaGetSymbolAddress);
+ *     make that first call before any stream capture.
+ *   - Every call on a device shares the one array; each call clears the parts that must start at
+ *     zero. Calls whose kernels overlap on the GPU (other streams, other threads) race: serialise them.
+ *   - A device-side wait that gives up is not reported back; use hoard_moe_layers where that matters.
+ * x_inout: device [H] of resid_type; sel_out / w_out: NULL or [n_layers][k]. */
+int hoard_moe_decode_noalloc(hoard_moe_ctx* ctx, int layer0, int n_layers, void* x_inout, int32_t* sel_out,
+                             float* w_out, hoard_stream stream);
+
 /* Waits for `stream`, then reports and clears the errors kernels recorded on the device:
  * HOARD_EINVAL for expert or slot ids out of range (those entries were skipped), HOARD_ETIMEOUT
  * for a bounded device-side wait that gave up. hoard aborts on such input instead
