@@ -348,7 +348,9 @@ def run_gpu(args, rank, world, local_rank):
     achieved = bytes_step / (ms_step * 1e-3) / 1e9
     traffic = None
     try:
+        # DRAM bytes of one 48-layer step from an ncu capture (profiles/), scaled to the layers run
         traffic = json.load(open(os.path.join(ROOT, "profiles", "traffic.json"))).get("decode_step_bytes")
+        traffic = int(traffic * N_LAYER / 48) if traffic else None
     except Exception:
         pass
     if rank == 0:
