@@ -52,7 +52,11 @@ struct Scratch {
     float* y;         // [T*(k+1)][H]
     unsigned* amax;   // [T*(k+1)][I/256] bit patterns of max|h| (persistent decode path)
     float* partials;  // persistent decode: per-CTA partial router sums
-    unsigned* sync;   // persistent decode: grid barrier words + error flag
+    unsigned* sync;   // [0] error bits (1 bad slot id, 2 device wait gave up); persistent decode barrier words
+    uint16_t* xq16;   // [T][H] f16 bits: Q8_K-dequantised fx (tensor-core path)
+    uint16_t* hq16;   // [T*(k+1)][I] f16 bits: Q8_K-dequantised h in slot-sorted order (tensor-core path)
+    int2* items;      // tensor-core work list: (slot, M tile)
+    int* n_items;     // [1]
 };
 
 // Re-lays nrows x nb GGUF blocks of `type` from src (raw) into dst (plane layout).
@@ -69,6 +73,20 @@ cudaError_t launch_route(const Dims& d, const LayerWeights& lw, const void* x, i
 cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const Scratch& sc, const float* fx,
                                    const int32_t* slot_of_sel, const float* w, void* x_inout, int T,
                                    bool need_sh_gate, cudaStream_t s, int* launches);
+
+// Pieces shared by the grouped and tensor-core expert paths.
+cudaError_t launch_shared_gate(const float* fx, const float* gate_inp, int H, int T, float* out, cudaStream_t s);
+cudaError_t launch_dispatch(const int32_t* slot_of_sel, int T, int k, int KK, int n_slots, const Scratch& sc,
+                            cudaStream_t s);
+cudaError_t launch_combine(const Dims& d, const Scratch& sc, const float* w, void* x_inout, int T, int KK,
+                           cudaStream_t s);
+
+// The tensor-core grouped GEMM expert path (prefill / batched tokens), adding into x_inout.
+bool tc_supported(const Dims& d, const LayerWeights& lw);
+int64_t tc_max_items(int T, int KK, int n_slots);
+cudaError_t launch_experts_tc(const Dims& d, const LayerWeights& lw, const Scratch& sc, const float* fx,
+                              const int32_t* slot_of_sel, const float* w, void* x_inout, int T, cudaStream_t s,
+                              int* launches);
 
 // Persistent fused decode kernel over n_layers layers (T <= decode_max_tokens()).
 int decode_max_tokens();

@@ -321,6 +321,30 @@ __global__ void __launch_bounds__(256) k_combine(const float* __restrict__ y, co
     }
 }
 
+cudaError_t launch_shared_gate(const float* fx, const float* gate_inp, int H, int T, float* out, cudaStream_t s) {
+    k_shared_gate<<<T, 256, 0, s>>>(fx, gate_inp, H, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dispatch(const int32_t* slot_of_sel, int T, int k, int KK, int n_slots, const Scratch& sc,
+                            cudaStream_t s) {
+    const int NS = n_slots + (KK > k ? 1 : 0);
+    const size_t dsm = (size_t)2 * (NS + 1) * sizeof(int);
+    k_dispatch<<<1, 1024, dsm, s>>>(slot_of_sel, T, k, KK, n_slots, sc.counts, sc.offsets, sc.perm, sc.sync);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const Dims& d, const Scratch& sc, const float* w, void* x_inout, int T, int KK,
+                           cudaStream_t s) {
+    const int64_t n = (int64_t)T * d.H;
+    const int cb = (int)((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
+    if (d.resid_bf16)
+        k_combine<__nv_bfloat16><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, (__nv_bfloat16*)x_inout);
+    else
+        k_combine<float><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, (float*)x_inout);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const Scratch& sc, const float* fx,
                                    const int32_t* slot_of_sel, const float* w, void* x_inout, int T,
                                    bool /*need_sh_gate*/, cudaStream_t s, int* launches) {
@@ -328,16 +352,16 @@ cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const 
     const int KK = d.k + (shared ? 1 : 0);
     const int NS = lw.n_slots + (shared ? 1 : 0);
     int nl = 0;
+    cudaError_t e;
     // 1. quantise fx
     k_quant_q8<<<(unsigned)((d.H / QK) * T), 256, 0, s>>>(fx, d.H, sc.fx_q, sc.fx_d, sc.fx_bs);
     ++nl;
     if (shared) {
-        k_shared_gate<<<T, 256, 0, s>>>(fx, lw.sh_gate_inp, d.H, sc.sh_gate);
+        if ((e = launch_shared_gate(fx, lw.sh_gate_inp, d.H, T, sc.sh_gate, s)) != cudaSuccess) return e;
         ++nl;
     }
     // 2. group entries by slot
-    const size_t dsm = (size_t)2 * (NS + 1) * sizeof(int);
-    k_dispatch<<<1, 1024, dsm, s>>>(slot_of_sel, T, d.k, KK, lw.n_slots, sc.counts, sc.offsets, sc.perm, sc.sync);
+    if ((e = launch_dispatch(slot_of_sel, T, d.k, KK, lw.n_slots, sc, s)) != cudaSuccess) return e;
     ++nl;
     // 3. gate/up + SwiGLU
     k_gateup<<<dim3(NS, (d.I + GU_ROWS - 1) / GU_ROWS), 256, 0, s>>>(lw, d.H, d.I, KK, sc.offsets, sc.perm, sc.fx_q,
@@ -351,12 +375,7 @@ cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const 
                                                                     sc.h_bs, sc.y);
     ++nl;
     // 6. weighted combine into the residual
-    const int64_t n = (int64_t)T * d.H;
-    const int cb = (int)((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
-    if (d.resid_bf16)
-        k_combine<__nv_bfloat16><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, (__nv_bfloat16*)x_inout);
-    else
-        k_combine<float><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, (float*)x_inout);
+    if ((e = launch_combine(d, sc, w, x_inout, T, KK, s)) != cudaSuccess) return e;
     ++nl;
     if (launches) *launches += nl;
     return cudaGetLastError();

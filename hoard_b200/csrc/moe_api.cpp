@@ -47,6 +47,7 @@ struct hoard_moe_ctx {
     cudaEvent_t staging_free = nullptr;
     int64_t launches = 0;
     int decode_impl = 1;
+    int gemm_min_tokens = 64;          // T at or above which the tensor-core expert path runs (0 = never)
     int routed_layer = -1;
     int routed_T = 0;
     LayerWeights* lw_dev = nullptr;    // device copy of every layer's LayerWeights (persistent kernel)
@@ -225,6 +226,10 @@ int hoard_moe_create(const hoard_moe_desc* d, hoard_moe_ctx** out) {
     if (rc == HOARD_OK) rc = dalloc(c, &s.amax, amax_rows * (I / 256) * 4);
     if (rc == HOARD_OK) rc = dalloc(c, &s.partials, (int64_t)4096 * 1024 * 4);
     if (rc == HOARD_OK) rc = dalloc(c, &s.sync, 1024 * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.xq16, T * H * 2);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.hq16, T * KK * I * 2);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.items, tc_max_items((int)T, (int)KK, d->n_slots) * (int64_t)sizeof(int2));
+    if (rc == HOARD_OK) rc = dalloc(c, &s.n_items, 4);
     if (rc == HOARD_OK) rc = dalloc(c, &c->staging, max_raw);
     c->staging_bytes = max_raw;
     if (rc == HOARD_OK) {
@@ -367,8 +372,12 @@ int hoard_moe_experts(hoard_moe_ctx* c, int layer, const float* fx, const int32_
         return fail(c, HOARD_EINVAL, "slot_of_sel is required when n_slots < n_expert");
     const LayerWeights lw = layer_weights(c, layer);
     int nl = 0;
-    HCHECK(c, launch_experts_grouped(c->dims, lw, c->sc, fx, slot_of_sel ? slot_of_sel : sel, w, x_inout, T, true,
-                                     (cudaStream_t)stream, &nl));
+    const int32_t* slots = slot_of_sel ? slot_of_sel : sel;
+    if (c->gemm_min_tokens > 0 && T >= c->gemm_min_tokens && tc_supported(c->dims, lw))
+        HCHECK(c, launch_experts_tc(c->dims, lw, c->sc, fx, slots, w, x_inout, T, (cudaStream_t)stream, &nl));
+    else
+        HCHECK(c, launch_experts_grouped(c->dims, lw, c->sc, fx, slots, w, x_inout, T, true, (cudaStream_t)stream,
+                                         &nl));
     c->launches += nl;
     return HOARD_OK;
 }
@@ -438,6 +447,12 @@ int hoard_moe_decode_noalloc(hoard_moe_ctx* c, int layer0, int n_layers, void* x
 int hoard_moe_set_decode_impl(hoard_moe_ctx* c, int impl) {
     if (!c || impl < 0 || impl > 1) return HOARD_EINVAL;
     c->decode_impl = impl;
+    return HOARD_OK;
+}
+
+int hoard_moe_set_gemm_min_tokens(hoard_moe_ctx* c, int min_tokens) {
+    if (!c || min_tokens < 0) return HOARD_EINVAL;
+    c->gemm_min_tokens = min_tokens;
     return HOARD_OK;
 }
 

@@ -34,7 +34,7 @@ EXPORTED = [
     "hoard_moe_set_shared", "hoard_moe_route", "hoard_moe_experts", "hoard_moe_layer", "hoard_moe_layers",
     "hoard_moe_sync_status", "hoard_moe_expert_bytes", "hoard_moe_launch_count", "hoard_moe_set_decode_impl",
     "hoard_moe_set_trace", "hoard_moe_trace_layout", "hoard_moe_decode_noalloc",
-    "hoard_moe_last_error", "hoard_strerror",
+    "hoard_moe_set_gemm_min_tokens", "hoard_moe_last_error", "hoard_strerror",
 ]
 
 
@@ -82,6 +82,7 @@ def lib() -> ctypes.CDLL:
         L.hoard_moe_launch_count.argtypes = [vp]
         L.hoard_moe_launch_count.restype = i64
         L.hoard_moe_set_decode_impl.argtypes = [vp, i32]
+        L.hoard_moe_set_gemm_min_tokens.argtypes = [vp, i32]
         L.hoard_moe_set_trace.argtypes = [vp, vp, i64]
         L.hoard_moe_decode_noalloc.argtypes = [vp, i32, i32, vp, vp, vp, vp]
         L.hoard_moe_trace_layout.argtypes = [vp, ctypes.POINTER(i32), ctypes.POINTER(i32)]
@@ -162,6 +163,10 @@ class MoEContext:
 
     def set_decode_impl(self, impl: int):
         self._check(lib().hoard_moe_set_decode_impl(self._h, impl), "set_decode_impl")
+
+    def set_gemm_min_tokens(self, min_tokens: int):
+        """T at or above which the expert FFN runs as the tensor-core grouped GEMM (0 = never)."""
+        self._check(lib().hoard_moe_set_gemm_min_tokens(self._h, min_tokens), "set_gemm_min_tokens")
 
     def set_trace(self, buf: torch.Tensor | None):
         """Enables phase stamps of the persistent decode kernel into an int64 CUDA tensor."""

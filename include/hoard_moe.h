@@ -164,6 +164,13 @@ int64_t hoard_moe_launch_count(const hoard_moe_ctx* ctx);
  * 1 = persistent fused decode kernel (default where supported). */
 int hoard_moe_set_decode_impl(hoard_moe_ctx* ctx, int impl);
 
+/* Token count at or above which hoard_moe_experts / hoard_moe_layer(s) run the expert FFN as the
+ * token-sorted grouped GEMM on the tensor cores (weights dequantised to f16 in shared memory, f32
+ * accumulation) instead of the exact-integer grouped kernels; 0 = never. Default 64. The batched
+ * counterpart of hoard's mul_mat_id path (src/run_specloop.cpp:125-140); hoard has no such switch,
+ * its graph picks the backend's matmul kernel by batch size. */
+int hoard_moe_set_gemm_min_tokens(hoard_moe_ctx* ctx, int min_tokens);
+
 /* Last error message of this context (CUDA error string or argument check). */
 const char* hoard_moe_last_error(const hoard_moe_ctx* ctx);
 

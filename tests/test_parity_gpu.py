@@ -25,12 +25,15 @@ DEV = 0
 
 
 def make_ctx(spec: LayerSpec, n_layer=1, max_tokens=64, resid=torch.float32, n_slots=None, down_types=None):
-    return moe.MoEContext(n_embd=spec.H, n_expert=spec.E, n_expert_used=spec.k, n_ff=spec.I, n_layer=n_layer,
-                          n_slots=n_slots, norm_topk=spec.renorm, eps=spec.eps, resid_dtype=resid,
-                          gate_types=[spec.types[0]] * n_layer, up_types=[spec.types[1]] * n_layer,
-                          down_types=down_types or [spec.types[2]] * n_layer,
-                          n_ff_shexp=spec.I if spec.shared else 0, shexp_types=spec.sh_types,
-                          max_tokens=max_tokens, device=DEV)
+    """A context pinned to the exact-integer kernels (the tensor-core path has its own tests)."""
+    ctx = moe.MoEContext(n_embd=spec.H, n_expert=spec.E, n_expert_used=spec.k, n_ff=spec.I, n_layer=n_layer,
+                         n_slots=n_slots, norm_topk=spec.renorm, eps=spec.eps, resid_dtype=resid,
+                         gate_types=[spec.types[0]] * n_layer, up_types=[spec.types[1]] * n_layer,
+                         down_types=down_types or [spec.types[2]] * n_layer,
+                         n_ff_shexp=spec.I if spec.shared else 0, shexp_types=spec.sh_types,
+                         max_tokens=max_tokens, device=DEV)
+    ctx.set_gemm_min_tokens(0)
+    return ctx
 
 
 def check_against_oracle(spec, L, x, out, sel, w):

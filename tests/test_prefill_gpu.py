@@ -1,0 +1,205 @@
+"""GPU parity of the tensor-core expert path (token-sorted grouped GEMM on tcgen05, the prefill /
+batched form of hoard's mul_mat_id, src/run_specloop.cpp:125-140) through the C ABI.
+
+Tolerance. The tensor-core path rounds both GEMM operands to f16 -- the Q8_K activation q*d and the
+dequantised weight d*sc*q - dmin*m -- and accumulates in f32, where ggml's CPU backend sums exact
+integer products per sub-block. That difference (~5e-4 relative per product), and the Q8_K rounding
+flips of h it causes, put the MoE delta (out - x) a few 1e-3 rel-L2 from the ggml-mode oracle.
+The tests require, on tokens whose routing is not a near tie:
+  * batch rel-L2 <= 1e-2 against ggml mode (half the north star's 2e-2 layer tolerance) and every
+    token <= 3e-2;
+  * batch rel-L2 <= 3e-2 against exact mode (f32 activations, dequantised weights);
+  * expert ids and weights exactly as the grouped path's (routing is the same kernel).
+Structural invariants are bit-exact: LRU slot permutation == all-resident, repeat calls identical.
+"""
+import numpy as np
+import pytest
+import torch
+
+from hoard_b200 import moe
+from oracle import oracle as orc
+from tests.moe_fixtures import (LayerSpec, load_context, make_layer, make_x, near_tie_mask, oracle_layer,
+                                rel_l2, Q4_K, Q6_K)
+
+pytestmark = pytest.mark.gpu
+
+DEV = 0
+TOL_GGML = 1e-2
+TOL_TOKEN = 3e-2
+TOL_EXACT = 3e-2
+
+
+def make_ctx(spec: LayerSpec, max_tokens, n_slots=None, resid=torch.float32, gemm_min_tokens=1):
+    ctx = moe.MoEContext(n_embd=spec.H, n_expert=spec.E, n_expert_used=spec.k, n_ff=spec.I, n_layer=1,
+                         n_slots=n_slots, norm_topk=spec.renorm, eps=spec.eps, resid_dtype=resid,
+                         gate_types=[spec.types[0]], up_types=[spec.types[1]], down_types=[spec.types[2]],
+                         n_ff_shexp=spec.I if spec.shared else 0, shexp_types=spec.sh_types,
+                         max_tokens=max_tokens, device=DEV)
+    ctx.set_gemm_min_tokens(gemm_min_tokens)
+    ctx.set_decode_impl(0)      # T = 1 also runs route + experts, not the persistent decode kernel
+    return ctx
+
+
+def run_layer(ctx, x_np, resid=torch.float32):
+    T = x_np.shape[0]
+    x = torch.from_numpy(x_np).to(f"cuda:{DEV}").to(resid)
+    sel = torch.empty(T, ctx.k, dtype=torch.int32, device=x.device)
+    w = torch.empty(T, ctx.k, dtype=torch.float32, device=x.device)
+    n0 = ctx.launch_count
+    ctx.layer(0, x, sel, w)
+    ctx.sync_status()
+    return x.float().cpu().numpy(), sel.cpu().numpy(), w.cpu().numpy(), ctx.launch_count - n0
+
+
+def check_tc(L, x, out, sel):
+    spec = L.spec
+    ref_out, ref_sel, _, _, ref_probs = oracle_layer(L, x, orc.MODE_GGML)
+    ok = ~near_tie_mask(ref_probs, ref_sel, spec.k)
+    assert ok.mean() > 0.8
+    assert np.array_equal(np.sort(sel[ok], 1), np.sort(ref_sel[ok], 1))
+    d, r = out[ok] - x[ok], ref_out[ok] - x[ok]
+    per_tok = np.array([rel_l2(d[i], r[i]) for i in range(d.shape[0])])
+    err = rel_l2(d, r)
+    assert err < TOL_GGML, (err, per_tok.max())
+    assert per_tok.max() < TOL_TOKEN, per_tok.max()
+    exact = oracle_layer(L, x, orc.MODE_EXACT)[0]
+    err_exact = rel_l2(d, exact[ok] - x[ok])
+    print(f"T={x.shape[0]} rel-L2 vs ggml {err:.2e} (max token {per_tok.max():.2e}), vs exact {err_exact:.2e}")
+    assert err_exact < TOL_EXACT
+    return err
+
+
+@pytest.fixture(scope="module")
+def qwen32():
+    """Qwen3-30B-A3B expert shapes (H 2048, I 768, top-8, renorm, down Q6_K) over 32 experts."""
+    spec = LayerSpec(H=2048, E=32, k=8, I=768)
+    L = make_layer(spec, seed=3101)
+    ctx = make_ctx(spec, max_tokens=1024)
+    load_context(ctx, 0, L)
+    yield spec, L, ctx
+    ctx.close()
+
+
+@pytest.mark.parametrize("T", [1, 37, 128, 300, 1024])
+def test_tc_layer_parity(qwen32, T):
+    spec, L, ctx = qwen32
+    x = make_x(T, spec.H, seed=500 + T)
+    out, sel, w, nl = run_layer(ctx, x)
+    # route + Q8 + dispatch + work list + gate/up GEMM + down GEMM + combine
+    assert nl == 7
+    check_tc(L, x, out, sel)
+
+
+def test_tc_matches_grouped_routing_and_is_close(qwen32):
+    """Same context, both expert paths: identical routing, outputs within the tensor-core tolerance."""
+    spec, L, ctx = qwen32
+    x = make_x(200, spec.H, seed=77)
+    out_tc, sel_tc, w_tc, _ = run_layer(ctx, x)
+    ctx.set_gemm_min_tokens(0)
+    try:
+        out_gr, sel_gr, w_gr, _ = run_layer(ctx, x)
+    finally:
+        ctx.set_gemm_min_tokens(1)
+    assert np.array_equal(sel_tc, sel_gr)
+    assert np.array_equal(w_tc.view(np.uint32), w_gr.view(np.uint32))
+    assert rel_l2(out_tc - x, out_gr - x) < TOL_GGML
+
+
+def test_tc_repeatable(qwen32):
+    spec, L, ctx = qwen32
+    x = make_x(257, spec.H, seed=78)
+    a = run_layer(ctx, x)[0]
+    b = run_layer(ctx, x)[0]
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_tc_ragged_tiles_and_empty_experts():
+    """Routing skewed onto a few experts: slots with several M tiles (the last one ragged), and
+    slots with no entries at all."""
+    spec = LayerSpec(H=2048, E=16, k=2, I=512, types=(Q4_K, Q4_K, Q4_K))
+    L = make_layer(spec, seed=3301)
+    g = np.random.default_rng(5)
+    u = g.standard_normal(spec.H).astype(np.float32)
+    u /= np.linalg.norm(u)
+    L.w_router[:2] += 0.5 * u / L.w_norm          # experts 0 and 1 align with the shared direction of x
+    T = 300
+    x = make_x(T, spec.H, seed=91) + 3.0 * np.sqrt(spec.H) * u[None, :]
+    x = (x / np.sqrt((x * x).mean(-1, keepdims=True) + 1e-6)).astype(np.float32)
+    ctx = make_ctx(spec, max_tokens=T)
+    load_context(ctx, 0, L)
+    out, sel, _, _ = run_layer(ctx, x)
+    counts = np.bincount(sel.reshape(-1), minlength=spec.E)
+    assert counts.max() > 2 * 128 and (counts == 0).any(), counts
+    check_tc(L, x, out, sel)
+    ctx.close()
+
+
+def test_tc_q4k_down_no_renorm_and_bf16_residual():
+    """OLMoE-style layer (64 experts, I 1024, Q4_K down, softmax weights without renorm) with a bf16
+    residual: the bf16 output equals the f32 result rounded once."""
+    spec = LayerSpec(H=2048, E=64, k=8, I=1024, types=(Q4_K, Q4_K, Q4_K), renorm=False, eps=1e-5)
+    L = make_layer(spec, seed=3401)
+    T = 160
+    x = make_x(T, spec.H, seed=92)
+    xb = torch.from_numpy(x).bfloat16().float().numpy()
+    c32 = make_ctx(spec, max_tokens=T)
+    load_context(c32, 0, L)
+    out32, sel, _, _ = run_layer(c32, xb)
+    check_tc(L, xb, out32, sel)
+    c32.close()
+    cbf = make_ctx(spec, max_tokens=T, resid=torch.bfloat16)
+    load_context(cbf, 0, L)
+    outbf, _, _, _ = run_layer(cbf, xb, resid=torch.bfloat16)
+    cbf.close()
+    rounded = torch.from_numpy(out32).bfloat16().float().numpy()
+    assert (outbf == rounded).mean() > 0.98
+    assert (np.abs(outbf - rounded) <= np.abs(rounded) * 2.0 ** -7).all()   # within one bf16 step
+
+
+def test_tc_shared_expert():
+    """Qwen2-MoE-style gated shared expert (slot n_slots of the same GEMM launches)."""
+    spec = LayerSpec(H=2048, E=16, k=4, I=512, shared=True, sh_types=(Q4_K, Q4_K, Q6_K))
+    L = make_layer(spec, seed=3501)
+    T = 100
+    x = make_x(T, spec.H, seed=93)
+    ctx = make_ctx(spec, max_tokens=T)
+    load_context(ctx, 0, L)
+    out, sel, _, _ = run_layer(ctx, x)
+    check_tc(L, x, out, sel)
+    ctx.close()
+
+
+def test_tc_lru_slots_equal_all_resident(qwen32):
+    """hoard's cache invariant on the tensor-core path: a permuted slot pool (slot ids unrelated to
+    expert ids), addressed through slot_of_sel, gives bit-identical output."""
+    spec, L, full = qwen32
+    T = 96
+    x_np = make_x(T, spec.H, seed=94)
+    ref, ref_sel, _, _ = run_layer(full, x_np)
+    used = sorted(set(ref_sel.reshape(-1).tolist()))
+    n_slots = len(used) + 2
+    slots = np.random.default_rng(1).permutation(n_slots)[:len(used)]
+    slot_of_expert = {e: int(s) for e, s in zip(used, slots)}
+    ctx = make_ctx(spec, max_tokens=T, n_slots=n_slots)
+    load_context(ctx, 0, L, slot_of_expert=slot_of_expert)
+    x = torch.from_numpy(x_np).cuda(DEV)
+    sel, w = ctx.route(0, x)
+    slot_of_sel = torch.from_numpy(np.vectorize(slot_of_expert.get)(sel.cpu().numpy()).astype(np.int32)).cuda(DEV)
+    ctx.experts(0, sel, w, x, slot_of_sel=slot_of_sel)
+    ctx.sync_status()
+    assert np.array_equal(x.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    ctx.close()
+
+
+def test_tc_out_of_range_slot_is_reported(qwen32):
+    spec, L, ctx = qwen32
+    x = torch.from_numpy(make_x(70, spec.H, seed=95)).cuda(DEV)
+    sel, w = ctx.route(0, x)
+    bad = sel.clone()
+    bad[5, 1] = spec.E + 7
+    ctx.experts(0, sel, w, x, slot_of_sel=bad)
+    with pytest.raises(moe.HoardError) as ei:
+        ctx.sync_status()
+    assert ei.value.status == moe.HOARD_EINVAL
+    out, _, _, _ = run_layer(ctx, make_x(70, spec.H, seed=96))
+    assert np.isfinite(out).all()
