@@ -57,6 +57,9 @@ struct Scratch {
     uint16_t* hq16;   // [T*(k+1)][I] f16 bits: Q8_K-dequantised h in slot-sorted order (tensor-core path)
     int2* items;      // tensor-core work list: (slot, M tile)
     int* n_items;     // [1]
+    double* rpart;    // router partial logits per K split
+    int* dcount;      // [n_slots+1] dispatch histogram of large batches (zero between calls)
+    int* dcursor;     // [n_slots+1] dispatch scatter cursors
 };
 
 // Re-lays nrows x nb GGUF blocks of `type` from src (raw) into dst (plane layout).
@@ -65,9 +68,10 @@ cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int64_t nb
 // dst[c][r] = src[r][c] for an R x C f32 matrix.
 cudaError_t launch_transpose(const float* src, float* dst, int R, int C, cudaStream_t s);
 
-// Router: fx, sel, w (and sh_gate when the layer has a shared expert) for T tokens.
+// Router: fx, sel, w for T tokens (three launches). `part` holds router_partial_elems() doubles.
+int64_t router_partial_elems(int max_tokens, int E);
 cudaError_t launch_route(const Dims& d, const LayerWeights& lw, const void* x, int T, float* fx, int32_t* sel,
-                         float* w, float* sh_gate, cudaStream_t s);
+                         float* w, double* part, cudaStream_t s, int* launches);
 
 // The grouped expert path for any T (fx given), adding into x_inout.
 cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const Scratch& sc, const float* fx,
@@ -76,17 +80,19 @@ cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const 
 
 // Pieces shared by the grouped and tensor-core expert paths.
 cudaError_t launch_shared_gate(const float* fx, const float* gate_inp, int H, int T, float* out, cudaStream_t s);
+// Counting sort of the entries by slot; with tile_m > 0 also the (slot, M tile) work list.
 cudaError_t launch_dispatch(const int32_t* slot_of_sel, int T, int k, int KK, int n_slots, const Scratch& sc,
-                            cudaStream_t s);
+                            int tile_m, cudaStream_t s, int* launches);
 cudaError_t launch_combine(const Dims& d, const Scratch& sc, const float* w, void* x_inout, int T, int KK,
                            cudaStream_t s);
 
 // The tensor-core grouped GEMM expert path (prefill / batched tokens), adding into x_inout.
 bool tc_supported(const Dims& d, const LayerWeights& lw);
 int64_t tc_max_items(int T, int KK, int n_slots);
+int64_t tc_trace_elems();   // stamps written by one call when tracing: [gate/up, down][cta][item][stage][slot]
 cudaError_t launch_experts_tc(const Dims& d, const LayerWeights& lw, const Scratch& sc, const float* fx,
                               const int32_t* slot_of_sel, const float* w, void* x_inout, int T, cudaStream_t s,
-                              int* launches);
+                              int* launches, unsigned long long* trace);
 
 // Persistent fused decode kernel over n_layers layers (T <= decode_max_tokens()).
 int decode_max_tokens();

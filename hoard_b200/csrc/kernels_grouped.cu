@@ -67,85 +67,220 @@ cudaError_t launch_transpose(const float* src, float* dst, int R, int C, cudaStr
 }
 
 // ---------------------------------------------------------------------------------------------
-// router: TT tokens per CTA; fx in shared memory; warp per expert row with double accumulation
+// router (graph A's tail, src/run_moe_stream.cpp:352-373): three kernels
+//   k_rmsnorm        fx = (x * 1/sqrt(mean(x^2) + eps)) * ffn_norm, one CTA per token
+//   k_router_logits  logits = W_r . fx as a tiled GEMM (32 tokens x 128 experts per CTA, K staged
+//                    in shared memory, split over K when there are few tiles); f32 products summed
+//                    over 32-wide K chunks, chunks summed in double; partial sums per K split
+//   k_route_topk     one warp per token: sum the K splits in order, softmax over all E, top-k by
+//                    (probability desc, id asc), optional renorm with the 6.103515625e-5 clamp
 // ---------------------------------------------------------------------------------------------
-constexpr int ROUTE_TT = 4;
 constexpr int MAX_K = 16;
+constexpr int RL_TT = 32;      // tokens per tile: 8 warps x 4
+constexpr int RL_EB = 128;     // experts per tile: 32 lanes x 4
+constexpr int RL_KC = 32;      // K chunk staged in shared memory
+constexpr int RL_MIN_KLEN = 128;
+constexpr int RL_TARGET_CTAS = 296;
+
+constexpr int RMS_MAXV = 32;   // H <= 8192: values per thread held in registers
 
 template <typename R>
-__global__ void __launch_bounds__(256) k_route(const R* __restrict__ x, int T, int H, int E, int k, int renorm,
-                                               float eps, const float* __restrict__ w_norm,
-                                               const float* __restrict__ w_router, float* __restrict__ fx_out,
-                                               int32_t* sel_out, float* w_out) {
-    extern __shared__ __align__(16) float smem[];
-    float* fxs = smem;                    // [TT][H]
-    float* lg = smem + ROUTE_TT * H;      // [TT][E]
+__global__ void __launch_bounds__(256) k_rmsnorm(const R* __restrict__ x, int H, float eps,
+                                                 const float* __restrict__ w_norm, float* __restrict__ fx) {
     __shared__ double redd[32];
-    __shared__ float redf[32];
-    __shared__ int s_sel[MAX_K];
-    __shared__ float s_w[MAX_K];
-    const int t0 = blockIdx.x * ROUTE_TT;
-    const int nt = min(ROUTE_TT, T - t0);
-    for (int tt = 0; tt < nt; ++tt) {
-        const R* xr = x + (size_t)(t0 + tt) * H;
-        double ss = 0.0;
-        for (int i = threadIdx.x; i < H; i += blockDim.x) {
-            const float v = to_f32<R>(xr[i]);
-            fxs[tt * H + i] = v;
-            ss += (double)(v * v);
+    const int64_t t = blockIdx.x;
+    const R* xr = x + t * H;
+    float v[RMS_MAXV];
+    double ss = 0.0;
+#pragma unroll
+    for (int j = 0; j < RMS_MAXV; ++j) {
+        const int i = threadIdx.x + 256 * j;
+        v[j] = i < H ? to_f32<R>(xr[i]) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < RMS_MAXV; ++j) ss += (double)(v[j] * v[j]);
+    ss = block_sum_d(ss, redd);
+    const float mean = (float)(ss / H);
+    const float scale = 1.0f / sqrtf(mean + eps);
+#pragma unroll
+    for (int j = 0; j < RMS_MAXV; ++j) {
+        const int i = threadIdx.x + 256 * j;
+        if (i < H) fx[t * H + i] = (v[j] * scale) * w_norm[i];
+    }
+}
+
+// grid (ceil(T/32), ceil(E/128), ksplit); CTA z covers K range [z*klen, (z+1)*klen)
+__global__ void __launch_bounds__(256) k_router_logits(const float* __restrict__ fx, const float* __restrict__ w_router,
+                                                       int T, int H, int E, int klen, double* __restrict__ part) {
+    __shared__ __align__(16) float sf[RL_KC][RL_TT];          // fx chunk, k-major
+    __shared__ __align__(16) float sw[RL_KC][RL_EB + 4];      // router chunk, k-major (padded rows)
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int t0 = blockIdx.x * RL_TT, e0 = blockIdx.y * RL_EB;
+    const int k0 = blockIdx.z * klen;
+    double acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
+    // global -> registers for chunk kb (fx: one float4 per thread, router: four)
+    const int st = tid >> 3, skq = (tid & 7) * 4;
+    float4 pf, pw[4];
+    auto fetch = [&](int kb) {
+        pf = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t0 + st < T) pf = *reinterpret_cast<const float4*>(fx + (int64_t)(t0 + st) * H + kb + skq);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int e = (tid + 256 * r) >> 3;
+            pw[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e0 + e < E) pw[r] = __ldg(reinterpret_cast<const float4*>(w_router + (int64_t)(e0 + e) * H + kb + skq));
         }
-        ss = block_sum_d(ss, redd);
-        const float mean = (float)(ss / H);
-        const float scale = 1.0f / sqrtf(mean + eps);
-        for (int i = threadIdx.x; i < H; i += blockDim.x) {
-            const float v = (fxs[tt * H + i] * scale) * w_norm[i];
-            fxs[tt * H + i] = v;
-            fx_out[(size_t)(t0 + tt) * H + i] = v;
+    };
+    fetch(k0);
+    for (int kb = k0; kb < k0 + klen; kb += RL_KC) {
+        sf[skq][st] = pf.x; sf[skq + 1][st] = pf.y; sf[skq + 2][st] = pf.z; sf[skq + 3][st] = pf.w;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int e = (tid + 256 * r) >> 3;
+            sw[skq][e] = pw[r].x; sw[skq + 1][e] = pw[r].y; sw[skq + 2][e] = pw[r].z; sw[skq + 3][e] = pw[r].w;
+        }
+        __syncthreads();
+        if (kb + RL_KC < k0 + klen) fetch(kb + RL_KC);     // next chunk in flight during this one
+        float a[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) a[i][j] = 0.f;
+#pragma unroll 8
+        for (int kk = 0; kk < RL_KC; ++kk) {
+            const float4 f = *reinterpret_cast<const float4*>(&sf[kk][warp * 4]);
+            const float4 w = *reinterpret_cast<const float4*>(&sw[kk][lane * 4]);
+            const float fv[4] = {f.x, f.y, f.z, f.w}, wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) a[i][j] = fmaf(fv[i], wv[j], a[i][j]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] += (double)a[i][j];
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + warp * 4 + i;
+        if (t >= T) continue;
+        double* dst = part + ((int64_t)blockIdx.z * T + t) * E;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int e = e0 + lane * 4 + j;
+            if (e < E) dst[e] = acc[i][j];
         }
     }
-    __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int e = warp; e < E; e += nw) {
-        double acc[ROUTE_TT];
-#pragma unroll
-        for (int tt = 0; tt < ROUTE_TT; ++tt) acc[tt] = 0.0;
-        const float* wr = w_router + (size_t)e * H;
-        for (int i = lane * 4; i < H; i += 128) {
-            const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + i));
-#pragma unroll
-            for (int tt = 0; tt < ROUTE_TT; ++tt) {
-                if (tt < nt) {
-                    const float4 f = *reinterpret_cast<const float4*>(fxs + tt * H + i);
-                    acc[tt] += (double)wv.x * (double)f.x + (double)wv.y * (double)f.y +
-                               (double)wv.z * (double)f.z + (double)wv.w * (double)f.w;
-                }
-            }
-        }
-#pragma unroll
-        for (int tt = 0; tt < ROUTE_TT; ++tt) {
-            const double v = warp_sum(acc[tt]);
-            if (lane == 0 && tt < nt) lg[tt * E + e] = (float)v;
-        }
+}
+
+// 8 tokens per CTA: all 256 threads sum the K splits into shared memory (independent loads), then
+// one warp per token does softmax + top-k (E <= 1024)
+constexpr int TOPK_TT = 8;
+constexpr int TOPK_MAXE = 1024;
+
+__global__ void __launch_bounds__(256) k_route_topk(const double* __restrict__ part, int ksplit, int T, int E, int k,
+                                                    int renorm, int32_t* __restrict__ sel, float* __restrict__ w) {
+    __shared__ float lg[TOPK_TT][TOPK_MAXE];
+    const int t0 = blockIdx.x * TOPK_TT;
+    const int nt = min(TOPK_TT, T - t0);
+    for (int i = threadIdx.x; i < nt * E; i += blockDim.x) {
+        const int tt = i / E, e = i - tt * E;
+        const double* src = part + (int64_t)(t0 + tt) * E + e;
+        double s = 0.0;
+        for (int z = 0; z < ksplit; ++z) s += src[(int64_t)z * T * E];
+        lg[tt][e] = (float)s;
     }
     __syncthreads();
-    for (int tt = 0; tt < nt; ++tt)
-        softmax_topk(lg + tt * E, E, k, renorm, sel_out + (size_t)(t0 + tt) * k, w_out + (size_t)(t0 + tt) * k,
-                     redd, redf, s_sel, s_w);
+    const int lane = threadIdx.x & 31, tt = threadIdx.x >> 5;
+    if (tt >= nt) return;
+    const int t = t0 + tt;
+    constexpr int NV = TOPK_MAXE / 32;
+    float p[NV];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int e = lane + 32 * i;
+        p[i] = e < E ? lg[tt][e] : -INFINITY;
+        m = fmaxf(m, p[i]);
+    }
+    m = warp_max(m);
+    double ssum = 0.0;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        if (lane + 32 * i < E) {
+            p[i] = expf(p[i] - m);
+            ssum += (double)p[i];
+        }
+    }
+    ssum = warp_sum(ssum);
+    const float inv = (float)(1.0 / ssum);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) p[i] = lane + 32 * i < E ? p[i] * inv : -1.f;
+    // k rounds of arg-max over (p desc, id asc); the winner's entry is retired with p = -1
+    float my_w = 0.f, wsum = 0.f;
+    int my_e = 0;
+    for (int r = 0; r < k; ++r) {
+        float bp = -1.f;
+        int be = 0x7FFFFFFF;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int e = lane + 32 * i;
+            if (p[i] > bp || (p[i] == bp && e < be)) { bp = p[i]; be = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float op = __shfl_xor_sync(0xFFFFFFFFu, bp, o);
+            const int oe = __shfl_xor_sync(0xFFFFFFFFu, be, o);
+            if (op > bp || (op == bp && oe < be)) { bp = op; be = oe; }
+        }
+#pragma unroll
+        for (int i = 0; i < NV; ++i)
+            if (lane + 32 * i == be) p[i] = -1.f;
+        wsum += bp;                                   // sequential f32 sum in rank order
+        if (lane == r) { my_w = bp; my_e = be; }
+    }
+    if (renorm) {
+        if (wsum < 6.103515625e-5f) wsum = 6.103515625e-5f;
+        my_w /= wsum;
+    }
+    if (lane < k) {
+        sel[(int64_t)t * k + lane] = my_e;
+        w[(int64_t)t * k + lane] = my_w;
+    }
+}
+
+int router_ksplit(int T, int E, int H) {
+    const int tiles = ((T + RL_TT - 1) / RL_TT) * ((E + RL_EB - 1) / RL_EB);
+    int ks = RL_TARGET_CTAS / tiles;
+    const int max_ks = H / RL_MIN_KLEN;
+    if (ks > max_ks) ks = max_ks;
+    while (ks > 1 && (H % (ks * RL_KC) != 0)) --ks;    // equal K ranges, whole chunks
+    return ks < 1 ? 1 : ks;
+}
+
+int64_t router_partial_elems(int max_tokens, int E) {
+    // ksplit * T <= (RL_TARGET_CTAS / tiles) * 32 * tiles
+    const int64_t rows = max_tokens > RL_TARGET_CTAS * RL_TT ? max_tokens : RL_TARGET_CTAS * RL_TT;
+    return rows * E;
 }
 
 cudaError_t launch_route(const Dims& d, const LayerWeights& lw, const void* x, int T, float* fx, int32_t* sel,
-                         float* w, float* /*sh_gate*/, cudaStream_t s) {
-    const size_t smem = (size_t)ROUTE_TT * (d.H + d.E) * sizeof(float);
-    const int blocks = (T + ROUTE_TT - 1) / ROUTE_TT;
-    if (d.resid_bf16) {
-        cudaFuncSetAttribute(k_route<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        k_route<__nv_bfloat16><<<blocks, 256, smem, s>>>((const __nv_bfloat16*)x, T, d.H, d.E, d.k, d.renorm, d.eps,
-                                                         lw.w_norm, lw.w_router, fx, sel, w);
-    } else {
-        cudaFuncSetAttribute(k_route<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        k_route<float><<<blocks, 256, smem, s>>>((const float*)x, T, d.H, d.E, d.k, d.renorm, d.eps, lw.w_norm,
-                                                 lw.w_router, fx, sel, w);
-    }
+                         float* w, double* part, cudaStream_t s, int* launches) {
+    if (d.resid_bf16)
+        k_rmsnorm<__nv_bfloat16><<<T, 256, 0, s>>>((const __nv_bfloat16*)x, d.H, d.eps, lw.w_norm, fx);
+    else
+        k_rmsnorm<float><<<T, 256, 0, s>>>((const float*)x, d.H, d.eps, lw.w_norm, fx);
+    const int ks = router_ksplit(T, d.E, d.H);
+    const dim3 grid((T + RL_TT - 1) / RL_TT, (d.E + RL_EB - 1) / RL_EB, ks);
+    k_router_logits<<<grid, 256, 0, s>>>(fx, lw.w_router, T, d.H, d.E, d.H / ks, part);
+    k_route_topk<<<(T + TOPK_TT - 1) / TOPK_TT, 256, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
+    if (launches) *launches += 3;
     return cudaGetLastError();
 }
 
@@ -176,44 +311,115 @@ __global__ void __launch_bounds__(256) k_quant_q8(const float* __restrict__ x, i
 }
 
 // ---------------------------------------------------------------------------------------------
-// dispatch: counting sort of entry ids e = t*KK + j by pool slot (one CTA)
+// dispatch: counting sort of entry ids e = t*KK + j by pool slot (one CTA of 1024 threads), and
+// optionally the tensor-core work list: one (slot, M tile) item per `tile_m` entries of a slot.
+// Entries are read 8 per thread at a time so their loads overlap; the offsets come from a
+// CTA-wide scan. The order of entries within a slot is arbitrary (every consumer is per entry).
 // ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) k_dispatch(const int32_t* __restrict__ slot_of, int T, int k, int KK,
-                                                   int n_slots, int* __restrict__ counts, int* __restrict__ offsets,
-                                                   int* __restrict__ perm, unsigned* err) {
+constexpr int DISP_THREADS = 1024;
+constexpr int DISP_UNROLL = 8;
+
+__device__ __forceinline__ int2 scan_excl_1024(int2 v, int2* wtot, int2& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int2 inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xFFFFFFFFu, inc.x, o), b = __shfl_up_sync(0xFFFFFFFFu, inc.y, o);
+        if (lane >= o) { inc.x += a; inc.y += b; }
+    }
+    if (lane == 31) wtot[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        int2 t = wtot[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int a = __shfl_up_sync(0xFFFFFFFFu, t.x, o), b = __shfl_up_sync(0xFFFFFFFFu, t.y, o);
+            if (lane >= o) { t.x += a; t.y += b; }
+        }
+        wtot[lane] = t;
+    }
+    __syncthreads();
+    const int2 pre = warp > 0 ? wtot[warp - 1] : make_int2(0, 0);
+    total = wtot[31];
+    return make_int2(pre.x + inc.x - v.x, pre.y + inc.y - v.y);
+}
+
+__global__ void __launch_bounds__(DISP_THREADS) k_dispatch(const int32_t* __restrict__ slot_of, int T, int k, int KK,
+                                                           int n_slots, int* __restrict__ counts,
+                                                           int* __restrict__ offsets, int* __restrict__ perm,
+                                                           unsigned* err, int tile_m, int2* __restrict__ items,
+                                                           int* __restrict__ n_items) {
     extern __shared__ int sm[];
+    __shared__ int2 wtot[32];
     const int NS = n_slots + (KK > k ? 1 : 0);
     int* cnt = sm;
     int* cur = sm + NS + 1;
     for (int i = threadIdx.x; i <= NS; i += blockDim.x) cnt[i] = 0;
     __syncthreads();
     const int n = T * KK;
-    for (int e = threadIdx.x; e < n; e += blockDim.x) {
+    auto slot_at = [&](int e) {
         const int t = e / KK, j = e - t * KK;
-        int s = (j < k) ? slot_of[(size_t)t * k + j] : n_slots;
-        if (s < 0 || s >= NS || (j < k && s >= n_slots)) {
-            atomicOr(err, 1u);
-            continue;
+        return (j < k) ? (int)slot_of[(size_t)t * k + j] : n_slots;
+    };
+    auto valid = [&](int e, int sl) {
+        const int j = e % KK;
+        return !(sl < 0 || sl >= NS || (j < k && sl >= n_slots));
+    };
+    for (int e0 = threadIdx.x; e0 < n; e0 += DISP_THREADS * DISP_UNROLL) {
+        int sv[DISP_UNROLL];
+#pragma unroll
+        for (int u = 0; u < DISP_UNROLL; ++u) {
+            const int e = e0 + u * DISP_THREADS;
+            sv[u] = e < n ? slot_at(e) : -1;
         }
-        atomicAdd(&cnt[s], 1);
+#pragma unroll
+        for (int u = 0; u < DISP_UNROLL; ++u) {
+            const int e = e0 + u * DISP_THREADS;
+            if (e >= n) continue;
+            if (!valid(e, sv[u])) { atomicOr(err, 1u); continue; }
+            atomicAdd(&cnt[sv[u]], 1);
+        }
     }
     __syncthreads();
+    // exclusive scan of (entries, M tiles) over the slots; thread i owns slots [i*c, (i+1)*c)
+    const int c = (NS + DISP_THREADS - 1) / DISP_THREADS;
+    const int s0 = threadIdx.x * c, s1 = min(NS, s0 + c);
+    int2 mine = make_int2(0, 0);
+    for (int sl = s0; sl < s1; ++sl) {
+        mine.x += cnt[sl];
+        if (tile_m > 0) mine.y += (cnt[sl] + tile_m - 1) / tile_m;
+    }
+    int2 total;
+    int2 off = scan_excl_1024(mine, wtot, total);
+    for (int sl = s0; sl < s1; ++sl) {
+        const int cn = cnt[sl];
+        offsets[sl] = off.x;
+        counts[sl] = cn;
+        cur[sl] = off.x;
+        off.x += cn;
+        if (tile_m > 0) {
+            for (int mt = 0; mt * tile_m < cn; ++mt) items[off.y + mt] = make_int2(sl, mt);
+            off.y += (cn + tile_m - 1) / tile_m;
+        }
+    }
     if (threadIdx.x == 0) {
-        int acc = 0;
-        for (int i = 0; i < NS; ++i) {
-            cur[i] = acc;
-            offsets[i] = acc;
-            counts[i] = cnt[i];
-            acc += cnt[i];
-        }
-        offsets[NS] = acc;
+        offsets[NS] = total.x;
+        if (tile_m > 0) *n_items = total.y;
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < n; e += blockDim.x) {
-        const int t = e / KK, j = e - t * KK;
-        const int s = (j < k) ? slot_of[(size_t)t * k + j] : n_slots;
-        if (s < 0 || s >= NS || (j < k && s >= n_slots)) continue;
-        perm[atomicAdd(&cur[s], 1)] = e;
+    for (int e0 = threadIdx.x; e0 < n; e0 += DISP_THREADS * DISP_UNROLL) {
+        int sv[DISP_UNROLL];
+#pragma unroll
+        for (int u = 0; u < DISP_UNROLL; ++u) {
+            const int e = e0 + u * DISP_THREADS;
+            sv[u] = e < n ? slot_at(e) : -1;
+        }
+#pragma unroll
+        for (int u = 0; u < DISP_UNROLL; ++u) {
+            const int e = e0 + u * DISP_THREADS;
+            if (e >= n || !valid(e, sv[u])) continue;
+            perm[atomicAdd(&cur[sv[u]], 1)] = e;
+        }
     }
 }
 
@@ -306,18 +512,45 @@ __global__ void __launch_bounds__(256) k_shared_gate(const float* __restrict__ f
     if (threadIdx.x == 0) out[t] = sigmoid_f((float)acc);
 }
 
+// x[t] += sum_j w[t][j] * y[t*KK + j] (+ sh_gate[t] * y[t*KK + k]), j ascending; four columns per
+// thread, the k rows' loads issued together
 template <typename R>
 __global__ void __launch_bounds__(256) k_combine(const float* __restrict__ y, const float* __restrict__ w,
                                                  const float* __restrict__ sh_gate, int k, int KK, int H, int T,
                                                  R* x) {
-    const int64_t n = (int64_t)T * H;
-    for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < n; idx += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t t = idx / H;
-        const int64_t dcol = idx - t * H;
-        float acc = 0.f;
-        for (int j = 0; j < k; ++j) acc += w[t * k + j] * y[(t * KK + j) * H + dcol];
-        if (KK > k) acc = acc + y[(t * KK + k) * H + dcol] * sh_gate[t];
-        x[idx] = from_f32<R>(acc + to_f32<R>(x[idx]));
+    const int64_t nq = (int64_t)T * H / 4;
+    for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < nq; q += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = (q * 4) / H;
+        const int64_t dcol = q * 4 - t * H;
+        const float* yb = y + t * KK * H + dcol;
+        float4 yv[MAX_K];
+#pragma unroll
+        for (int j = 0; j < MAX_K; ++j)
+            if (j < k) yv[j] = *reinterpret_cast<const float4*>(yb + (int64_t)j * H);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < MAX_K; ++j) {
+            if (j < k) {
+                const float wj = w[t * k + j];
+                acc.x += wj * yv[j].x;
+                acc.y += wj * yv[j].y;
+                acc.z += wj * yv[j].z;
+                acc.w += wj * yv[j].w;
+            }
+        }
+        if (KK > k) {
+            const float4 ys = *reinterpret_cast<const float4*>(yb + (int64_t)k * H);
+            const float g = sh_gate[t];
+            acc.x = acc.x + ys.x * g;
+            acc.y = acc.y + ys.y * g;
+            acc.z = acc.z + ys.z * g;
+            acc.w = acc.w + ys.w * g;
+        }
+        R* xp = x + q * 4;
+        xp[0] = from_f32<R>(acc.x + to_f32<R>(xp[0]));
+        xp[1] = from_f32<R>(acc.y + to_f32<R>(xp[1]));
+        xp[2] = from_f32<R>(acc.z + to_f32<R>(xp[2]));
+        xp[3] = from_f32<R>(acc.w + to_f32<R>(xp[3]));
     }
 }
 
@@ -326,17 +559,108 @@ cudaError_t launch_shared_gate(const float* fx, const float* gate_inp, int H, in
     return cudaGetLastError();
 }
 
-cudaError_t launch_dispatch(const int32_t* slot_of_sel, int T, int k, int KK, int n_slots, const Scratch& sc,
-                            cudaStream_t s) {
+// Large batches: per-CTA shared-memory histograms added into global counts, a one-CTA scan, and a
+// scatter through global cursors (warp-aggregated atomics).
+constexpr int DISP_SMALL = 4096;     // entries handled by the single-CTA kernel
+constexpr int DISP_CHUNK = 4096;     // entries per CTA in the multi-CTA kernels
+
+__global__ void __launch_bounds__(512) k_disp_count(const int32_t* __restrict__ slot_of, int T, int k, int KK,
+                                                    int n_slots, int* __restrict__ gcount, unsigned* err) {
+    extern __shared__ int hist[];
     const int NS = n_slots + (KK > k ? 1 : 0);
-    const size_t dsm = (size_t)2 * (NS + 1) * sizeof(int);
-    k_dispatch<<<1, 1024, dsm, s>>>(slot_of_sel, T, k, KK, n_slots, sc.counts, sc.offsets, sc.perm, sc.sync);
+    for (int i = threadIdx.x; i < NS; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    const int n = T * KK;
+    const int e0 = blockIdx.x * DISP_CHUNK, e1 = min(n, e0 + DISP_CHUNK);
+    for (int e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
+        const int t = e / KK, j = e - t * KK;
+        const int sl = (j < k) ? (int)slot_of[(size_t)t * k + j] : n_slots;
+        if (sl < 0 || sl >= NS || (j < k && sl >= n_slots)) { atomicOr(err, 1u); continue; }
+        atomicAdd(&hist[sl], 1);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < NS; i += blockDim.x)
+        if (hist[i]) atomicAdd(&gcount[i], hist[i]);
+}
+
+__global__ void __launch_bounds__(DISP_THREADS) k_disp_scan(int NS, int* __restrict__ gcount, int* __restrict__ counts,
+                                                            int* __restrict__ offsets, int* __restrict__ cursor,
+                                                            int tile_m, int2* __restrict__ items,
+                                                            int* __restrict__ n_items) {
+    __shared__ int2 wtot[32];
+    const int c = (NS + DISP_THREADS - 1) / DISP_THREADS;
+    const int s0 = threadIdx.x * c, s1 = min(NS, s0 + c);
+    int2 mine = make_int2(0, 0);
+    for (int sl = s0; sl < s1; ++sl) {
+        mine.x += gcount[sl];
+        if (tile_m > 0) mine.y += (gcount[sl] + tile_m - 1) / tile_m;
+    }
+    int2 total;
+    int2 off = scan_excl_1024(mine, wtot, total);
+    for (int sl = s0; sl < s1; ++sl) {
+        const int cn = gcount[sl];
+        offsets[sl] = off.x;
+        counts[sl] = cn;
+        cursor[sl] = off.x;
+        off.x += cn;
+        if (tile_m > 0) {
+            for (int mt = 0; mt * tile_m < cn; ++mt) items[off.y + mt] = make_int2(sl, mt);
+            off.y += (cn + tile_m - 1) / tile_m;
+        }
+        gcount[sl] = 0;                       // ready for the next call
+    }
+    if (threadIdx.x == 0) {
+        offsets[NS] = total.x;
+        if (tile_m > 0) *n_items = total.y;
+    }
+}
+
+__global__ void __launch_bounds__(512) k_disp_scatter(const int32_t* __restrict__ slot_of, int T, int k, int KK,
+                                                      int n_slots, int* __restrict__ cursor, int* __restrict__ perm) {
+    const int NS = n_slots + (KK > k ? 1 : 0);
+    const int n = T * KK;
+    const int lane = threadIdx.x & 31;
+    const int e0 = blockIdx.x * DISP_CHUNK, e1 = min(n, e0 + DISP_CHUNK);
+    for (int base = e0; base < e1; base += blockDim.x) {
+        const int e = base + threadIdx.x;
+        int sl = -1;
+        if (e < e1) {
+            const int t = e / KK, j = e - t * KK;
+            sl = (j < k) ? (int)slot_of[(size_t)t * k + j] : n_slots;
+            if (sl < 0 || sl >= NS || (j < k && sl >= n_slots)) sl = -1;
+        }
+        const unsigned peers = __match_any_sync(0xFFFFFFFFu, sl);
+        const int leader = __ffs(peers) - 1;
+        int pos = 0;
+        if (lane == leader && sl >= 0) pos = atomicAdd(&cursor[sl], __popc(peers));
+        pos = __shfl_sync(0xFFFFFFFFu, pos, leader);
+        if (sl >= 0) perm[pos + __popc(peers & ((1u << lane) - 1u))] = e;
+    }
+}
+
+cudaError_t launch_dispatch(const int32_t* slot_of_sel, int T, int k, int KK, int n_slots, const Scratch& sc,
+                            int tile_m, cudaStream_t s, int* launches) {
+    const int NS = n_slots + (KK > k ? 1 : 0);
+    const int n = T * KK;
+    if (n <= DISP_SMALL) {
+        const size_t dsm = (size_t)2 * (NS + 1) * sizeof(int);
+        k_dispatch<<<1, DISP_THREADS, dsm, s>>>(slot_of_sel, T, k, KK, n_slots, sc.counts, sc.offsets, sc.perm,
+                                                sc.sync, tile_m, sc.items, sc.n_items);
+        if (launches) *launches += 1;
+        return cudaGetLastError();
+    }
+    const int grid = (n + DISP_CHUNK - 1) / DISP_CHUNK;
+    k_disp_count<<<grid, 512, (size_t)NS * sizeof(int), s>>>(slot_of_sel, T, k, KK, n_slots, sc.dcount, sc.sync);
+    k_disp_scan<<<1, DISP_THREADS, 0, s>>>(NS, sc.dcount, sc.counts, sc.offsets, sc.dcursor, tile_m, sc.items,
+                                           sc.n_items);
+    k_disp_scatter<<<grid, 512, 0, s>>>(slot_of_sel, T, k, KK, n_slots, sc.dcursor, sc.perm);
+    if (launches) *launches += 3;
     return cudaGetLastError();
 }
 
 cudaError_t launch_combine(const Dims& d, const Scratch& sc, const float* w, void* x_inout, int T, int KK,
                            cudaStream_t s) {
-    const int64_t n = (int64_t)T * d.H;
+    const int64_t n = (int64_t)T * d.H / 4;
     const int cb = (int)((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
     if (d.resid_bf16)
         k_combine<__nv_bfloat16><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, (__nv_bfloat16*)x_inout);
@@ -361,8 +685,7 @@ cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const 
         ++nl;
     }
     // 2. group entries by slot
-    if ((e = launch_dispatch(slot_of_sel, T, d.k, KK, lw.n_slots, sc, s)) != cudaSuccess) return e;
-    ++nl;
+    if ((e = launch_dispatch(slot_of_sel, T, d.k, KK, lw.n_slots, sc, 0, s, &nl)) != cudaSuccess) return e;
     // 3. gate/up + SwiGLU
     k_gateup<<<dim3(NS, (d.I + GU_ROWS - 1) / GU_ROWS), 256, 0, s>>>(lw, d.H, d.I, KK, sc.offsets, sc.perm, sc.fx_q,
                                                                       sc.fx_d, sc.fx_bs, sc.h);

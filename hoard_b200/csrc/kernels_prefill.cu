@@ -37,6 +37,11 @@ constexpr int A_THREADS = 128;            // warps 1-4
 constexpr int B_THREADS = 256;            // warps 5-12
 constexpr int A_TID0 = 32, B_TID0 = 160;
 constexpr unsigned long long TC_WAIT_NS = 2000000000ull;
+// phase stamps (%globaltimer) of the first CTAs' first two items: 0 MMA saw the stage full, 1 MMA
+// committed it, 2 B-row 0 starts dequantising, 3 B-row 0 saw the stage empty, 4 B-row 0 arrived,
+// 5 A-thread 0 saw the stage empty, 6 A-thread 0 issued its copies; stage 0 / 1 of slot 7 =
+// epilogue start / end.
+constexpr int TC_TRACE_CTAS = 4, TC_TRACE_ITEMS = 2, TC_TRACE_STAGES = 32, TC_TRACE_SLOTS = 8;
 
 __device__ __forceinline__ unsigned long long gtime() {
     unsigned long long t;
@@ -133,19 +138,34 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 __device__ __forceinline__ __half2 h2bits(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
 __device__ __forceinline__ uint32_t bits_h2(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
 
+// A B thread owns one weight row. Per 64-weight segment (one pipeline stage) the row's quantised
+// bytes are copied with cp.async into a shared-memory ring several stages ahead of use (chunk-major:
+// 16-byte chunk c of row r at c * 4096 + r * 16, so a warp's reads are conflict-free); the per-block
+// scale words are read into registers one block (four stages) ahead.
 template <int TYPE> struct Seg;
 
 // Q4_K segment g (0..3) of a block = qs bytes [32g, 32g+32): low nibbles are weights [64g, 64g+32)
 // (sub-block 2g), high nibbles weights [64g+32, 64g+64) (sub-block 2g+1). w = d*sc*q - dmin*m.
 template <> struct Seg<T_Q4K> {
-    uint4 q0, q1, hdr;
-    __device__ __forceinline__ void load(const uint8_t* base, int64_t nblk_total, int64_t blk, int g) {
-        const uint8_t* qs = base + blk * 128 + 32 * g;
-        q0 = ld16(qs);
-        q1 = ld16(qs + 16);
-        hdr = ld16(base + nblk_total * 128 + blk * 16);
+    static constexpr int RAW_CH = 2;                       // 16-byte chunks per row and stage
+    struct Hdr { uint4 h; };
+    uint4 q0, q1;
+    static __device__ __forceinline__ Hdr load_hdr(const uint8_t* base, int64_t nblk_total, int64_t blk) {
+        return Hdr{ld16(base + nblk_total * 128 + blk * 16)};
     }
-    __device__ __forceinline__ void dequant(int g, uint4 out[8]) const {
+    static __device__ __forceinline__ void issue(uint8_t* ring, int r, const uint8_t* base, int64_t nblk_total,
+                                                 int64_t blk, int g) {
+        (void)nblk_total;
+        const uint8_t* qs = base + blk * 128 + 32 * g;
+        cp_async16(ring + r * 16, qs, 16u);
+        cp_async16(ring + 4096 + r * 16, qs + 16, 16u);
+    }
+    __device__ __forceinline__ void read(const uint8_t* ring, int r) {
+        q0 = *reinterpret_cast<const uint4*>(ring + r * 16);
+        q1 = *reinterpret_cast<const uint4*>(ring + 4096 + r * 16);
+    }
+    __device__ __forceinline__ void dequant(int g, const Hdr& hd, uint4 out[8]) const {
+        const uint4& hdr = hd.h;
         const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFF)));
         const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
         int sc0, m0, sc1, m1;
@@ -174,24 +194,36 @@ template <> struct Seg<T_Q4K> {
 // high for a >= 2), high bits = bits 2a..2a+1 of qh[32h2 + l], scale sc[8h2 + 2a + l/16];
 // w = d * sc * (q - 32).
 template <> struct Seg<T_Q6K> {
-    uint4 la0, la1, lb0, lb1, h0, h1, sc;
-    unsigned short d;
-    __device__ __forceinline__ void load(const uint8_t* base, int64_t nblk_total, int64_t blk, int s) {
+    static constexpr int RAW_CH = 6;                       // ql 64 bytes + qh 32 bytes
+    struct Hdr { uint4 sc; unsigned short d; };
+    uint4 la0, la1, lb0, lb1, h0, h1;
+    static __device__ __forceinline__ Hdr load_hdr(const uint8_t* base, int64_t nblk_total, int64_t blk) {
+        Hdr h;
+        h.sc = ld16(base + nblk_total * 192 + blk * 16);
+        h.d = *reinterpret_cast<const unsigned short*>(base + nblk_total * 208 + blk * 2);
+        return h;
+    }
+    static __device__ __forceinline__ void issue(uint8_t* ring, int r, const uint8_t* base, int64_t nblk_total,
+                                                 int64_t blk, int s) {
         const int h2 = s >> 1;
         const uint8_t* ql = base + blk * 128 + 64 * h2;
-        la0 = ld16(ql);
-        la1 = ld16(ql + 16);
-        lb0 = ld16(ql + 32);
-        lb1 = ld16(ql + 48);
         const uint8_t* qh = base + nblk_total * 128 + blk * 64 + 32 * h2;
-        h0 = ld16(qh);
-        h1 = ld16(qh + 16);
-        sc = ld16(base + nblk_total * 192 + blk * 16);
-        d = *reinterpret_cast<const unsigned short*>(base + nblk_total * 208 + blk * 2);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) cp_async16(ring + c * 4096 + r * 16, ql + 16 * c, 16u);
+        cp_async16(ring + 4 * 4096 + r * 16, qh, 16u);
+        cp_async16(ring + 5 * 4096 + r * 16, qh + 16, 16u);
     }
-    __device__ __forceinline__ void dequant(int s, uint4 out[8]) const {
+    __device__ __forceinline__ void read(const uint8_t* ring, int r) {
+        la0 = *reinterpret_cast<const uint4*>(ring + r * 16);
+        la1 = *reinterpret_cast<const uint4*>(ring + 4096 + r * 16);
+        lb0 = *reinterpret_cast<const uint4*>(ring + 2 * 4096 + r * 16);
+        lb1 = *reinterpret_cast<const uint4*>(ring + 3 * 4096 + r * 16);
+        h0 = *reinterpret_cast<const uint4*>(ring + 4 * 4096 + r * 16);
+        h1 = *reinterpret_cast<const uint4*>(ring + 5 * 4096 + r * 16);
+    }
+    __device__ __forceinline__ void dequant(int s, const Hdr& hd, uint4 out[8]) const {
         const int h2 = s >> 1, a0 = 2 * (s & 1);
-        const float df = __half2float(__ushort_as_half(d));
+        const float df = __half2float(__ushort_as_half(hd.d));
         const __half2 k1056 = __float2half2_rn(1056.f);   // 1024 + 32
         const uint32_t qhw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
 #pragma unroll
@@ -201,8 +233,8 @@ template <> struct Seg<T_Q6K> {
             const uint4& p1 = (a & 1) ? lb1 : la1;
             const uint32_t qlw[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
             const int nib = a >= 2 ? 4 : 0;
-            const __half2 s0 = __float2half2_rn(df * (float)sbyte(sc, 8 * h2 + 2 * a));
-            const __half2 s1 = __float2half2_rn(df * (float)sbyte(sc, 8 * h2 + 2 * a + 1));
+            const __half2 s0 = __float2half2_rn(df * (float)sbyte(hd.sc, 8 * h2 + 2 * a));
+            const __half2 s1 = __float2half2_rn(df * (float)sbyte(hd.sc, 8 * h2 + 2 * a + 1));
 #pragma unroll
             for (int i = 0; i < 8; ++i) {   // elements l = 4i..4i+3 -> chunk 4r + i/2
                 const uint32_t q = ((qlw[i] >> nib) & 0x0F0F0F0Fu) | (((qhw[i] >> (2 * a)) & 0x03030303u) << 4);
@@ -214,6 +246,37 @@ template <> struct Seg<T_Q6K> {
         }
     }
 };
+
+// Shared-memory plan of one CTA: an A ring (f16 activation tiles, 16 KiB per stage), a B ring
+// (dequantised f16 weight tiles, 32 KiB per matrix and stage) and the raw-byte ring of the B rows.
+// A has its own, deeper ring because its tiles come from L2 with ~1.3 us of latency under load,
+// while a stage of MMAs takes ~0.3-0.6 us.
+struct TcCfg {
+    int a, b, raw;   // stages of the A ring, the B ring, the raw-byte ring
+};
+constexpr int TC_A_BYTES = TC_M * 128;
+constexpr int tc_b_bytes(int mode) { return (mode == 0 ? 2 : 1) * TC_N * 128; }
+constexpr int tc_raw_bytes(int mode, int type) { return (mode == 0 ? 2 : 1) * (type == T_Q4K ? 2 : 6) * 4096; }
+constexpr int TC_SMEM_BUDGET = 225 * 1024 - 1024;          // dynamic shared memory per CTA, less alignment slack
+constexpr int tc_raw_fit(int mode, int type, int a, int b) {
+    return (TC_SMEM_BUDGET - a * TC_A_BYTES - b * tc_b_bytes(mode)) / tc_raw_bytes(mode, type) > 4
+               ? 4
+               : (TC_SMEM_BUDGET - a * TC_A_BYTES - b * tc_b_bytes(mode)) / tc_raw_bytes(mode, type);
+}
+// deepest A ring first, then three B stages if the raw ring still gets three, else two
+constexpr TcCfg tc_cfg(int mode, int type) {
+    for (int a = 4; a >= 2; --a) {
+        if (tc_raw_fit(mode, type, a, 3) >= 3) return TcCfg{a, 3, tc_raw_fit(mode, type, a, 3)};
+        if (tc_raw_fit(mode, type, a, 2) >= 1) return TcCfg{a, 2, tc_raw_fit(mode, type, a, 2)};
+    }
+    return TcCfg{0, 0, 0};
+}
+constexpr size_t tc_smem(int mode, int type) {
+    return (size_t)tc_cfg(mode, type).a * TC_A_BYTES + (size_t)tc_cfg(mode, type).b * tc_b_bytes(mode) +
+           (size_t)tc_cfg(mode, type).raw * tc_raw_bytes(mode, type) + 1024;   // + alignment slack
+}
+static_assert(tc_cfg(0, T_Q4K).a >= 2 && tc_cfg(0, T_Q6K).a >= 2 && tc_cfg(1, T_Q4K).a >= 2 &&
+                  tc_cfg(1, T_Q6K).a >= 2, "shared-memory plan");
 
 // 64 f16 of row r into a 128B-swizzled tile: 16-byte chunk c of the row lands at chunk c ^ (r % 8)
 __device__ __forceinline__ void store_row_sw128(uint8_t* tile, int r, const uint4 v[8]) {
@@ -235,22 +298,30 @@ struct TcArgs {
     __half* hq;             // MODE 0 output [P][I] (sorted order)
     float* y;               // MODE 1 output [entries][H] by entry id
     unsigned* err;
+    unsigned long long* trace;   // optional stamps [cta < TC_TRACE_CTAS][item < 2][stage < 32][TC_TRACE_SLOTS]
 };
 
 template <int MODE, int TYPE>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
     constexpr int NMAT = MODE == 0 ? 2 : 1;
-    constexpr int STAGES = MODE == 0 ? 2 : 3;
+    constexpr TcCfg CFG = tc_cfg(MODE, TYPE);
+    constexpr int AST = CFG.a, BST = CFG.b;
     constexpr int A_BYTES = TC_M * 128;                    // 16 KiB
     constexpr int B_BYTES = TC_N * 128;                    // 32 KiB per matrix
-    constexpr int STAGE_BYTES = A_BYTES + NMAT * B_BYTES;
+    constexpr int BSTAGE_BYTES = NMAT * B_BYTES;
+    constexpr int RAW_MAT = Seg<TYPE>::RAW_CH * 4096;      // raw bytes of one matrix per stage
+    constexpr int RAW_BYTES = NMAT * RAW_MAT;
+    constexpr int RAWD = CFG.raw;                          // stages of raw bytes in flight
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t full_bar[STAGES], empty_bar[STAGES], acc_full, acc_empty, done_bar;
+    __shared__ uint64_t full_a[AST], empty_a[AST], full_b[BST], empty_b[BST], acc_full, acc_empty, done_bar;
     __shared__ uint32_t s_tmem;
     __shared__ volatile int s_abort;
     __shared__ float s_amax[2][TC_M];
 
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* ring_a = smem;                                // [AST][A_BYTES]
+    uint8_t* ring_b = smem + AST * A_BYTES;                // [BST][NMAT][B_BYTES]
+    uint8_t* ring = ring_b + BST * BSTAGE_BYTES;           // [RAWD][RAW_BYTES]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = MODE == 0 ? a.H : a.I;                   // reduction length
     const int NOUT = MODE == 0 ? a.I : a.H;                // output rows of the weight matrix
@@ -260,9 +331,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
     const int64_t nblk_total = (int64_t)NOUT * nbK;
 
     if (tid == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            bar_init(&full_bar[s], A_THREADS + B_THREADS);
-            bar_init(&empty_bar[s], 1);
+        for (int s = 0; s < AST; ++s) {
+            bar_init(&full_a[s], A_THREADS);
+            bar_init(&empty_a[s], 1);
+        }
+        for (int s = 0; s < BST; ++s) {
+            bar_init(&full_b[s], B_THREADS);
+            bar_init(&empty_b[s], 1);
         }
         bar_init(&acc_full, 1);
         bar_init(&acc_empty, B_THREADS);
@@ -280,6 +355,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
     tc_fence_after();
     const uint32_t tmem = s_tmem;
     const int n_items = *a.n_items * NBLK;
+    unsigned long long* trc = a.trace && blockIdx.x < TC_TRACE_CTAS
+                                  ? a.trace + (int64_t)blockIdx.x * TC_TRACE_ITEMS * TC_TRACE_STAGES * TC_TRACE_SLOTS
+                                  : nullptr;
+#define TC_STAMP(item_no_, kc_, slot_)                                                                     \
+    do {                                                                                                   \
+        if (trc && (item_no_) < TC_TRACE_ITEMS && (kc_) < TC_TRACE_STAGES)                                 \
+            trc[((item_no_) * TC_TRACE_STAGES + (kc_)) * TC_TRACE_SLOTS + (slot_)] = gtime();              \
+    } while (0)
 
     int item_no = 0;   // items this CTA has run; stage counter = item_no * KC + kc in every role
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++item_no) {
@@ -297,21 +380,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
                 tc_fence_after();
                 for (int kc = 0; kc < KC && ok; ++kc) {
                     const uint32_t st_it = it0 + kc;
-                    const int s = st_it % STAGES;
-                    if (!bar_wait(&full_bar[s], (st_it / STAGES) & 1, &s_abort)) { ok = false; break; }
+                    const int sa = st_it % AST, sb = st_it % BST;
+                    if (!bar_wait(&full_a[sa], (st_it / AST) & 1, &s_abort) ||
+                        !bar_wait(&full_b[sb], (st_it / BST) & 1, &s_abort)) { ok = false; break; }
+                    TC_STAMP(item_no, kc, 0);
                     fence_async_smem();
                     tc_fence_after();
-                    const uint8_t* st = smem + s * STAGE_BYTES;
-                    const uint64_t ad = sw128_desc(st);
-                    const uint64_t bd0 = sw128_desc(st + A_BYTES);
-                    const uint64_t bd1 = sw128_desc(st + A_BYTES + B_BYTES);
+                    const uint64_t ad = sw128_desc(ring_a + sa * A_BYTES);
+                    const uint64_t bd0 = sw128_desc(ring_b + sb * BSTAGE_BYTES);
+                    const uint64_t bd1 = sw128_desc(ring_b + sb * BSTAGE_BYTES + B_BYTES);
 #pragma unroll
                     for (int ks = 0; ks < TC_KC / 16; ++ks) {   // +32 bytes of K = +2 in the descriptor
                         const uint32_t acc = (kc > 0 || ks > 0) ? 1u : 0u;
                         umma_f16(tmem, ad + 2 * ks, bd0 + 2 * ks, acc);
                         if (MODE == 0) umma_f16(tmem + TC_N, ad + 2 * ks, bd1 + 2 * ks, acc);
                     }
-                    umma_commit(&empty_bar[s]);      // stage s is free once these MMAs have read it
+                    umma_commit(&empty_a[sa]);       // the stages are free once these MMAs have read them
+                    umma_commit(&empty_b[sb]);
+                    TC_STAMP(item_no, kc, 1);
                 }
                 if (ok) umma_commit(&acc_full);      // accumulators complete
             }
@@ -332,18 +418,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
             }
             for (int kc = 0; kc < KC; ++kc) {
                 const uint32_t st_it = it0 + kc;
-                const int s = st_it % STAGES;
-                const uint32_t round = st_it / STAGES;
-                if (round > 0 && !bar_wait(&empty_bar[s], (round - 1) & 1, &s_abort)) break;
+                const int s = st_it % AST;
+                const uint32_t round = st_it / AST;
+                if (round > 0 && !bar_wait(&empty_a[s], (round - 1) & 1, &s_abort)) break;
                 if (s_abort) break;
-                uint8_t* tile = smem + s * STAGE_BYTES;
+                if (t == 0) TC_STAMP(item_no, kc, 5);
+                uint8_t* tile = ring_a + s * A_BYTES;
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int r = rg + 16 * i;
                     const void* g = src[i] ? (const void*)(src[i] + kc * TC_KC + c * 8) : (const void*)a.A;
                     cp_async16(tile + r * 128 + ((c ^ (r & 7)) << 4), g, src[i] ? 16u : 0u);
                 }
-                cp_async_arrive_noinc(&full_bar[s]);
+                cp_async_arrive_noinc(&full_a[s]);
+                if (t == 0) TC_STAMP(item_no, kc, 6);
             }
         } else {
             // ---------------- B dequant (256 threads), then the epilogue ----------------
@@ -353,34 +441,62 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
             const uint8_t* base = sh ? a.lw.shared : a.lw.pool + (int64_t)slot * a.lw.slot_stride;
             const uint8_t* m0 = MODE == 0 ? base : base + (sh ? a.lw.sh_off_down : a.lw.off_down);
             const uint8_t* m1 = base + (sh ? a.lw.sh_off_up : a.lw.off_up);
-            Seg<TYPE> nx0, nx1;
-            nx0.load(m0, nblk_total, n * nbK, 0);
-            if (MODE == 0) nx1.load(m1, nblk_total, n * nbK, 0);
+            const int64_t row_blk = n * nbK;
+            auto issue = [&](int kc) {                           // raw bytes of stage kc, one commit group
+                if (kc < KC) {
+                    uint8_t* slot_p = ring + (kc % RAWD) * RAW_BYTES;
+                    Seg<TYPE>::issue(slot_p, r, m0, nblk_total, row_blk + (kc >> 2), kc & 3);
+                    if (MODE == 0) Seg<TYPE>::issue(slot_p + RAW_MAT, r, m1, nblk_total, row_blk + (kc >> 2), kc & 3);
+                }
+                asm volatile("cp.async.commit_group;" ::: "memory");
+            };
+#pragma unroll
+            for (int j = 0; j < RAWD; ++j) issue(j);
+            typename Seg<TYPE>::Hdr h0c = Seg<TYPE>::load_hdr(m0, nblk_total, row_blk), h0n = h0c;
+            typename Seg<TYPE>::Hdr h1c = h0c, h1n = h0c;
+            if (MODE == 0) h1c = h1n = Seg<TYPE>::load_hdr(m1, nblk_total, row_blk);
+            if (nbK > 1) {
+                h0n = Seg<TYPE>::load_hdr(m0, nblk_total, row_blk + 1);
+                if (MODE == 0) h1n = Seg<TYPE>::load_hdr(m1, nblk_total, row_blk + 1);
+            }
             for (int kc = 0; kc < KC; ++kc) {
                 const uint32_t st_it = it0 + kc;
-                const int s = st_it % STAGES;
-                const uint32_t round = st_it / STAGES;
-                const Seg<TYPE> cur0 = nx0, cur1 = nx1;
-                if (kc + 1 < KC) {                               // prefetch the next segment's bytes
-                    const int64_t blk = n * nbK + ((kc + 1) >> 2);
-                    nx0.load(m0, nblk_total, blk, (kc + 1) & 3);
-                    if (MODE == 0) nx1.load(m1, nblk_total, blk, (kc + 1) & 3);
+                const int s = st_it % BST;
+                const uint32_t round = st_it / BST;
+                if (kc > 0 && (kc & 3) == 0) {                   // next block: rotate the scale words
+                    h0c = h0n;
+                    h1c = h1n;
+                    const int nb_next = (kc >> 2) + 1;
+                    if (nb_next < nbK) {
+                        h0n = Seg<TYPE>::load_hdr(m0, nblk_total, row_blk + nb_next);
+                        if (MODE == 0) h1n = Seg<TYPE>::load_hdr(m1, nblk_total, row_blk + nb_next);
+                    }
                 }
+                asm volatile("cp.async.wait_group %0;" ::"n"(RAWD - 1) : "memory");
+                if (r == 0) TC_STAMP(item_no, kc, 2);
+                const uint8_t* slot_p = ring + (kc % RAWD) * RAW_BYTES;
+                Seg<TYPE> sg;
+                sg.read(slot_p, r);
                 uint4 v[8];
-                cur0.dequant(kc & 3, v);
-                if (round > 0 && !bar_wait(&empty_bar[s], (round - 1) & 1, &s_abort)) break;
+                sg.dequant(kc & 3, h0c, v);
+                if (round > 0 && !bar_wait(&empty_b[s], (round - 1) & 1, &s_abort)) break;
                 if (s_abort) break;
-                uint8_t* tile = smem + s * STAGE_BYTES + A_BYTES;
+                if (r == 0) TC_STAMP(item_no, kc, 3);
+                uint8_t* tile = ring_b + s * BSTAGE_BYTES;
                 store_row_sw128(tile, r, v);
                 if (MODE == 0) {
-                    cur1.dequant(kc & 3, v);
+                    sg.read(slot_p + RAW_MAT, r);
+                    sg.dequant(kc & 3, h1c, v);
                     store_row_sw128(tile + B_BYTES, r, v);
                 }
                 fence_async_smem();
-                bar_arrive(&full_bar[s]);
+                bar_arrive(&full_b[s]);
+                if (r == 0) TC_STAMP(item_no, kc, 4);
+                issue(kc + RAWD);                                // refill this ring slot (its bytes are consumed)
             }
             // ---- epilogue: warp % 4 selects the TMEM lane quarter, (warp - 5) / 4 the column half ----
             const bool ok = __all_sync(0xFFFFFFFFu, bar_wait(&acc_full, item_no & 1, &s_abort));
+            if (r == 0) TC_STAMP(item_no, 0, 7);
             const int q = warp & 3, half = (warp - 5) >> 2;
             const int m = 32 * q + lane;                          // accumulator row = tile row
             const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
@@ -446,14 +562,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
             }
             tc_fence_before();
             bar_arrive(&acc_empty);
+            if (r == 0) TC_STAMP(item_no, 1, 7);
         }
     }
+#undef TC_STAMP
     // ---- teardown: drain this CTA's tensor-core ops and copies, then free the tensor memory ----
     if (warp == 0 && lane == 0) {
         umma_commit(&done_bar);
         bar_drain(&done_bar, 0);
     }
-    if (warp >= 1 && warp < 5) asm volatile("cp.async.wait_all;" ::: "memory");
+    if (warp >= 1) asm volatile("cp.async.wait_all;" ::: "memory");
     tc_fence_before();
     __syncthreads();
     if (s_abort && tid == 0) atomicOr(a.err, 2u);
@@ -463,39 +581,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
     }
 }
 
-// Work list: one (slot, M tile) item per 128 sorted entries of each slot.
-__global__ void k_tc_items(const int* __restrict__ offsets, int NS, int2* __restrict__ items, int* __restrict__ n_items,
-                           int max_items) {
-    if (threadIdx.x != 0 || blockIdx.x != 0) return;
-    int n = 0;
-    for (int s = 0; s < NS; ++s) {
-        const int cnt = offsets[s + 1] - offsets[s];
-        for (int mt = 0; mt * TC_M < cnt && n < max_items; ++mt) items[n++] = make_int2(s, mt);
-    }
-    *n_items = n;
-}
-
 // ggml's Q8_K of rows [R][K] (256-value blocks, iscale = 127 / max|x|, round to nearest even, clamp
-// 127), written back as f16(q * d): the activation operand of the tensor-core GEMMs.
-__global__ void __launch_bounds__(256) k_q8_to_f16(const float* __restrict__ x, int K, __half* __restrict__ out) {
-    __shared__ float red[8];
-    const int nseg = K / QK;
-    const int64_t r = blockIdx.x / nseg;
-    const int seg = (int)(blockIdx.x - r * nseg);
-    const float v = x[r * K + seg * QK + threadIdx.x];
-    float am = warp_max(fabsf(v));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = am;
-    __syncthreads();
-    am = red[0];
+// 127), written back as f16(q * d): the activation operand of the tensor-core GEMMs. One warp per
+// 256-value block (8 values per lane), eight blocks per CTA.
+__global__ void __launch_bounds__(256) k_q8_to_f16(const float* __restrict__ x, int64_t nblocks, __half* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t b = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (b >= nblocks) return;
+    const float4* src = reinterpret_cast<const float4*>(x + b * QK) + 2 * lane;
+    const float4 v0 = src[0], v1 = src[1];
+    const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    float am = 0.f;
 #pragma unroll
-    for (int i = 1; i < 8; ++i) am = fmaxf(am, red[i]);
-    float o = 0.f;
-    if (am != 0.f) {
-        const float iscale = 127.f / am;
-        const int q = min(127, __float2int_rn(iscale * v));
-        o = (float)q * (1.f / iscale);
+    for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
+    am = warp_max(am);
+    const float iscale = am != 0.f ? 127.f / am : 0.f;
+    const float d = am != 0.f ? 1.f / iscale : 0.f;
+    uint32_t pk[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int q0 = min(127, __float2int_rn(iscale * v[2 * i])), q1 = min(127, __float2int_rn(iscale * v[2 * i + 1]));
+        pk[i] = bits_h2(__floats2half2_rn((float)q0 * d, (float)q1 * d));
     }
-    out[r * K + seg * QK + threadIdx.x] = __float2half_rn(o);
+    reinterpret_cast<uint4*>(out + b * QK)[lane] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
 }
 
 namespace {
@@ -510,12 +618,6 @@ int tc_grid() {
     return sms;
 }
 
-constexpr size_t tc_smem(int mode) {
-    return (mode == 0 ? 2 * ((size_t)TC_M * 128 + 2 * (size_t)TC_N * 128)
-                      : 3 * ((size_t)TC_M * 128 + (size_t)TC_N * 128)) +
-           1024;   // + slack to align the tiles to the 1024-byte swizzle atoms
-}
-
 template <int MODE, int TYPE>
 cudaError_t launch_tc(const TcArgs& a, cudaStream_t s) {
     static unsigned long long attr_set = 0;   // devices on which the shared-memory limit was raised
@@ -523,11 +625,11 @@ cudaError_t launch_tc(const TcArgs& a, cudaStream_t s) {
     cudaGetDevice(&dev);
     if (dev >= 64 || !(attr_set >> dev & 1ull)) {
         cudaError_t e = cudaFuncSetAttribute(k_tc_experts<MODE, TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)tc_smem(MODE));
+                                             (int)tc_smem(MODE, TYPE));
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_set |= 1ull << dev;
     }
-    k_tc_experts<MODE, TYPE><<<tc_grid(), TC_THREADS, tc_smem(MODE), s>>>(a);
+    k_tc_experts<MODE, TYPE><<<tc_grid(), TC_THREADS, tc_smem(MODE, TYPE), s>>>(a);
     return cudaGetLastError();
 }
 
@@ -545,26 +647,26 @@ bool tc_supported(const Dims& d, const LayerWeights& lw) {
 
 int64_t tc_max_items(int T, int KK, int n_slots) { return ((int64_t)T * KK + TC_M - 1) / TC_M + n_slots + 1; }
 
+int64_t tc_trace_elems() { return (int64_t)2 * TC_TRACE_CTAS * TC_TRACE_ITEMS * TC_TRACE_STAGES * TC_TRACE_SLOTS; }
+
 cudaError_t launch_experts_tc(const Dims& d, const LayerWeights& lw, const Scratch& sc, const float* fx,
                               const int32_t* slot_of_sel, const float* w, void* x_inout, int T, cudaStream_t s,
-                              int* launches) {
+                              int* launches, unsigned long long* trace) {
     const bool shared = lw.shared != nullptr;
     const int KK = d.k + (shared ? 1 : 0);
     const int NS = lw.n_slots + (shared ? 1 : 0);
     int nl = 0;
     cudaError_t e;
     // 1. ggml's Q8_K of fx, as f16 (q * d) rows
-    k_q8_to_f16<<<(unsigned)((d.H / QK) * T), 256, 0, s>>>(fx, d.H, reinterpret_cast<__half*>(sc.xq16));
+    const int64_t nq = (int64_t)T * (d.H / QK);
+    k_q8_to_f16<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(fx, nq, reinterpret_cast<__half*>(sc.xq16));
     ++nl;
     if (shared) {
         if ((e = launch_shared_gate(fx, lw.sh_gate_inp, d.H, T, sc.sh_gate, s)) != cudaSuccess) return e;
         ++nl;
     }
     // 2. counting sort of the entries by slot, and the (slot, M tile) work list
-    if ((e = launch_dispatch(slot_of_sel, T, d.k, KK, lw.n_slots, sc, s)) != cudaSuccess) return e;
-    ++nl;
-    k_tc_items<<<1, 32, 0, s>>>(sc.offsets, NS, sc.items, sc.n_items, (int)tc_max_items(T, KK, lw.n_slots));
-    ++nl;
+    if ((e = launch_dispatch(slot_of_sel, T, d.k, KK, lw.n_slots, sc, TC_M, s, &nl)) != cudaSuccess) return e;
     // 3. gate/up + SwiGLU + Q8_K(h); 4. down
     TcArgs a{};
     a.lw = lw;
@@ -576,6 +678,7 @@ cudaError_t launch_experts_tc(const Dims& d, const LayerWeights& lw, const Scrat
     a.items = sc.items;
     a.n_items = sc.n_items;
     a.err = sc.sync;
+    a.trace = trace;
     a.A = reinterpret_cast<const __half*>(sc.xq16);
     a.hq = reinterpret_cast<__half*>(sc.hq16);
     e = lw.gate_type == T_Q4K ? launch_tc<0, T_Q4K>(a, s) : launch_tc<0, T_Q6K>(a, s);
@@ -583,6 +686,7 @@ cudaError_t launch_experts_tc(const Dims& d, const LayerWeights& lw, const Scrat
     ++nl;
     a.A = reinterpret_cast<const __half*>(sc.hq16);
     a.y = sc.y;
+    if (trace) a.trace = trace + tc_trace_elems() / 2;
     e = lw.down_type == T_Q4K ? launch_tc<1, T_Q4K>(a, s) : launch_tc<1, T_Q6K>(a, s);
     if (e != cudaSuccess) return e;
     ++nl;

@@ -230,11 +230,15 @@ int hoard_moe_create(const hoard_moe_desc* d, hoard_moe_ctx** out) {
     if (rc == HOARD_OK) rc = dalloc(c, &s.hq16, T * KK * I * 2);
     if (rc == HOARD_OK) rc = dalloc(c, &s.items, tc_max_items((int)T, (int)KK, d->n_slots) * (int64_t)sizeof(int2));
     if (rc == HOARD_OK) rc = dalloc(c, &s.n_items, 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.rpart, router_partial_elems((int)T, E) * 8);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.dcount, (int64_t)(d->n_slots + 2) * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.dcursor, (int64_t)(d->n_slots + 2) * 4);
     if (rc == HOARD_OK) rc = dalloc(c, &c->staging, max_raw);
     c->staging_bytes = max_raw;
     if (rc == HOARD_OK) {
         e = cudaMemset(s.sync, 0, 1024 * 4);
         if (e == cudaSuccess) e = cudaMemset(s.amax, 0, amax_rows * (I / 256) * 4);
+        if (e == cudaSuccess) e = cudaMemset(s.dcount, 0, (size_t)(d->n_slots + 2) * 4);
         if (e == cudaSuccess) e = cudaMemset(s.partials, 0, (size_t)4096 * 1024 * 4);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->staging_free, cudaEventDisableTiming);
         if (e != cudaSuccess) rc = cuda_fail(c, e, "context init");
@@ -350,8 +354,9 @@ int hoard_moe_route(hoard_moe_ctx* c, int layer, const void* x, int T, int32_t* 
     if (!x || !sel || !w) return fail(c, HOARD_EINVAL, "null pointer");
     if ((rc = check_ready(c, layer))) return rc;
     const LayerWeights lw = layer_weights(c, layer);
-    HCHECK(c, launch_route(c->dims, lw, x, T, c->sc.fx, sel, w, nullptr, (cudaStream_t)stream));
-    ++c->launches;
+    int nl = 0;
+    HCHECK(c, launch_route(c->dims, lw, x, T, c->sc.fx, sel, w, c->sc.rpart, (cudaStream_t)stream, &nl));
+    c->launches += nl;
     c->routed_layer = layer;
     c->routed_T = T;
     return HOARD_OK;
@@ -374,7 +379,8 @@ int hoard_moe_experts(hoard_moe_ctx* c, int layer, const float* fx, const int32_
     int nl = 0;
     const int32_t* slots = slot_of_sel ? slot_of_sel : sel;
     if (c->gemm_min_tokens > 0 && T >= c->gemm_min_tokens && tc_supported(c->dims, lw))
-        HCHECK(c, launch_experts_tc(c->dims, lw, c->sc, fx, slots, w, x_inout, T, (cudaStream_t)stream, &nl));
+        HCHECK(c, launch_experts_tc(c->dims, lw, c->sc, fx, slots, w, x_inout, T, (cudaStream_t)stream, &nl,
+                                    c->trace && c->trace_cap >= tc_trace_elems() ? c->trace : nullptr));
     else
         HCHECK(c, launch_experts_grouped(c->dims, lw, c->sc, fx, slots, w, x_inout, T, true, (cudaStream_t)stream,
                                          &nl));

@@ -148,7 +148,12 @@ int hoard_moe_sync_status(hoard_moe_ctx* ctx, hoard_stream stream);
  * launch whose stamps fit writes %globaltimer values (ns) into dev_buf laid out
  * [cta][layer][phase]; capacity 0 turns tracing off. Phases: 0 layer start, 1 routed,
  * 2 copies issued, 3 fx quantised, 4 gate/up bytes landed, 5 h written, 6 past barrier,
- * 7 h quantised, 8 down bytes landed, 9 down done, 10 combined + router sums, 11 past barrier. */
+ * 7 h quantised, 8 down bytes landed, 9 down done, 10 combined + router sums, 11 past barrier.
+ * The tensor-core expert path (T >= the GEMM threshold) writes, when capacity >= 4096, stamps
+ * [gemm: gate/up, down][cta < 4][item < 2][stage < 32][8]: 0 stage full at the MMA thread,
+ * 1 committed, 2 B-row 0 dequant start, 3 B-row 0 saw the stage empty, 4 B-row 0 arrived,
+ * 5 A-thread 0 saw the stage empty, 6 A-thread 0 issued; slot 7 of stages 0/1 = epilogue
+ * start/end. */
 int hoard_moe_set_trace(hoard_moe_ctx* ctx, uint64_t* dev_buf, int64_t capacity);
 
 /* CTAs per persistent launch and stamps per (CTA, layer) of the trace layout. */

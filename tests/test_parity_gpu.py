@@ -87,6 +87,21 @@ def test_small_layer_parity(small, T):
     check_against_oracle(spec, L, x, out, sel, w)
 
 
+def test_large_batch_multi_cta_dispatch():
+    """More than 4096 (token, expert) entries: the multi-CTA histogram / scan / scatter dispatch."""
+    spec = LayerSpec(H=512, E=16, k=4, I=256)
+    L = make_layer(spec, seed=102)
+    T = 1100
+    ctx = make_ctx(spec, max_tokens=T)
+    load_context(ctx, 0, L)
+    x = make_x(T, spec.H, seed=1100)
+    out, sel, w = run_layer(ctx, x)
+    check_against_oracle(spec, L, x, out, sel, w)
+    again, _, _ = run_layer(ctx, x)
+    assert np.array_equal(again.view(np.uint32), out.view(np.uint32))
+    ctx.close()
+
+
 def test_deterministic_and_split_equals_fused(small):
     spec, L, ctx = small
     x_np = make_x(7, spec.H, seed=77)
