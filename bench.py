@@ -76,6 +76,9 @@ class ClockSampler:
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0:   # nvidia-smi's first sample
+                time.sleep(0.01)
         except Exception:
             self.proc = None
         return self
@@ -250,6 +253,69 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+PREFILL_T = 4096          # tokens per call of the prefill measurement (the C2 sweep's largest T)
+C2_TS = (16, 512, 4096)   # isolated-layer sweep (C2: T in {1, 16, 512, 4096}; T = 1 is the decode line)
+
+
+def layer_flops(T: int) -> float:
+    """Algorithmic FLOPs of the expert FFN of one layer for T tokens: k experts x 3 matmuls x 2HI."""
+    return 2.0 * T * K_USED * 3 * H * I
+
+
+def measure_prefill(ctx, device, stream, dist):
+    """Batched tokens through the tensor-core expert path: the 48-layer stack at T = PREFILL_T tokens per
+    call (prefill tok/s) and the isolated layer 0 (Q6_K down) at the C2 token counts. Inputs are seeded
+    RMS-normalised rows resident in HBM; every call streams all experts' weights of a layer (391 MB >
+    126 MB L2), so no flush is needed between calls."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED + 4096)
+    x0 = torch.randn(PREFILL_T, H, generator=g, device=device)
+    x0 = x0 / torch.sqrt((x0 * x0).mean(-1, keepdim=True) + 1e-6)
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        tpeak, tsrc = float(peaks["bf16_tflops_sustained"]), "measured (sustained)"
+    except Exception:
+        tpeak, tsrc = 1400.0, "fallback (sustained)"
+
+    def timed(fn, reps, warm):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize(device)
+        if dist:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        ms = a.elapsed_time(b) / reps
+        if dist:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    x = x0.clone()
+    ms = timed(lambda: ctx.layers(0, N_LAYER, x), reps=5, warm=2)
+    ctx.sync_status()
+    sweep = []
+    for T in C2_TS:
+        xt = x0[:T].clone()
+        ms_l = timed(lambda: ctx.layer(0, xt), reps=20, warm=3)
+        sweep.append({"T": T, "us_per_layer": round(ms_l * 1e3, 1), "tok_s": round(T / ms_l * 1e3, 1),
+                      "expert_tflops": round(layer_flops(T) / (ms_l * 1e-3) / 1e12, 1)})
+    ctx.sync_status()
+    achieved = layer_flops(PREFILL_T) * N_LAYER / (ms * 1e-3) / 1e12
+    return {"metric": f"prefill tok/s ({N_LAYER} MoE layers, {PREFILL_T} tokens per call)",
+            "value": PREFILL_T / ms * 1e3, "unit": "tok/s", "ms_per_step": round(ms, 3),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": tpeak, "unit": "TFLOP/s",
+                         "frac": round(achieved / tpeak, 4), "peak_source": tsrc,
+                         "flops": "expert FFN only: 2*T*k*3*H*I per layer (router, dispatch, combine excluded)"},
+            "c2_layer": sweep}
+
+
 def run_gpu(args, rank, world, local_rank):
     import torch
     from hoard_b200 import moe
@@ -264,8 +330,8 @@ def run_gpu(args, rank, world, local_rank):
 
     ctx = moe.MoEContext(n_embd=H, n_expert=E, n_expert_used=K_USED, n_ff=I, n_layer=N_LAYER, norm_topk=True,
                          eps=1e-6, resid_dtype=torch.float32, gate_types=[Q4_K] * N_LAYER, up_types=[Q4_K] * N_LAYER,
-                         down_types=[down_type(layer) for layer in range(N_LAYER)], max_tokens=16,
-                         device=local_rank)
+                         down_types=[down_type(layer) for layer in range(N_LAYER)],
+                         max_tokens=PREFILL_T if not args.no_prefill else 16, device=local_rank)
     if args.decode_impl is not None:
         ctx.set_decode_impl(args.decode_impl)
     build_model(ctx, device, N_LAYER)
@@ -282,9 +348,19 @@ def run_gpu(args, rank, world, local_rank):
     if dist:
         dist.barrier()
     torch.cuda.synchronize(device)
-    launches0 = ctx.launch_count
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
+        # the timed region is tens of ms, shorter than nvidia-smi's sampling period: keep the GPU in the
+        # same decode loop for ~0.5 s first, so the clock samples see the load the timed steps run under
+        t_pre = time.time()
+        while time.time() - t_pre < 0.5:
+            for i in range(warm):
+                ctx.layers(0, N_LAYER, xs[steps + i], sel[steps + i], wts[steps + i])
+            torch.cuda.synchronize(device)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        launches0 = ctx.launch_count
         ev0.record(stream)
         for i in range(steps):
             ctx.layers(0, N_LAYER, xs[i], sel[i], wts[i])
@@ -332,6 +408,10 @@ def run_gpu(args, rank, world, local_rank):
     if args.trace:
         phases = trace_breakdown(ctx, xs[0], device)
 
+    prefill = None
+    if not args.no_prefill:
+        prefill = measure_prefill(ctx, device, stream, dist)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle as orc
@@ -372,8 +452,11 @@ def run_gpu(args, rank, world, local_rank):
             "e2e": {"value": round(world * 1000.0 * steps / ms_e2e, 3), "unit": "tok/s",
                     "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": H * 4},
             "gpu_launches": int(launches),
-            "clocks": clk.summary(),
+            "clocks": dict(clk.summary(), window="0.5 s of the same decode steps, then the timed steps"),
         }
+        if prefill:
+            prefill["value"] = round(prefill["value"] * world, 1)   # replicas: whole-job tokens/s
+            line["prefill"] = prefill
         if cpu:
             line["cpu_baseline"] = cpu
         if phases:
@@ -396,6 +479,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--trace", action="store_true", help="add the persistent kernel's per-phase breakdown")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the batched-token (prefill) measurements")
     ap.add_argument("--layers", type=int, default=N_LAYER, help="MoE layers per step (48 = the full stack; "
                     "fewer only for small profiling captures)")
     args = ap.parse_args()

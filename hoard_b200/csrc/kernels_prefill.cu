@@ -29,7 +29,10 @@ namespace hoard {
 
 namespace {
 
-constexpr int TC_THREADS = 416;           // 13 warps
+// warps: 0 MMA issuer, 1-4 A gather, 5-12 B dequant (+ the gate/up epilogue), 13-16 down epilogue
+constexpr int tc_threads(int mode) { return mode == 0 ? 416 : 544; }
+constexpr int EPI_THREADS = 128;          // down epilogue warps 13-16
+constexpr int EPI_TID0 = 416;
 constexpr int TC_M = 128;                 // rows of an M tile (UMMA M)
 constexpr int TC_N = 256;                 // columns of an N block (UMMA N)
 constexpr int TC_KC = 64;                 // K per pipeline stage: one 128-byte f16 row segment
@@ -258,10 +261,12 @@ constexpr int TC_A_BYTES = TC_M * 128;
 constexpr int tc_b_bytes(int mode) { return (mode == 0 ? 2 : 1) * TC_N * 128; }
 constexpr int tc_raw_bytes(int mode, int type) { return (mode == 0 ? 2 : 1) * (type == T_Q4K ? 2 : 6) * 4096; }
 constexpr int TC_SMEM_BUDGET = 225 * 1024 - 1024;          // dynamic shared memory per CTA, less alignment slack
+constexpr int EPI_ROW = 36;                                 // floats per row of a warp's 32 x 32 transpose tile
+constexpr int tc_epi_bytes(int mode) { return mode == 1 ? 4 * 32 * EPI_ROW * 4 : 0; }
 constexpr int tc_raw_fit(int mode, int type, int a, int b) {
-    return (TC_SMEM_BUDGET - a * TC_A_BYTES - b * tc_b_bytes(mode)) / tc_raw_bytes(mode, type) > 4
+    return (TC_SMEM_BUDGET - tc_epi_bytes(mode) - a * TC_A_BYTES - b * tc_b_bytes(mode)) / tc_raw_bytes(mode, type) > 4
                ? 4
-               : (TC_SMEM_BUDGET - a * TC_A_BYTES - b * tc_b_bytes(mode)) / tc_raw_bytes(mode, type);
+               : (TC_SMEM_BUDGET - tc_epi_bytes(mode) - a * TC_A_BYTES - b * tc_b_bytes(mode)) / tc_raw_bytes(mode, type);
 }
 // deepest A ring first, then three B stages if the raw ring still gets three, else two
 constexpr TcCfg tc_cfg(int mode, int type) {
@@ -273,7 +278,7 @@ constexpr TcCfg tc_cfg(int mode, int type) {
 }
 constexpr size_t tc_smem(int mode, int type) {
     return (size_t)tc_cfg(mode, type).a * TC_A_BYTES + (size_t)tc_cfg(mode, type).b * tc_b_bytes(mode) +
-           (size_t)tc_cfg(mode, type).raw * tc_raw_bytes(mode, type) + 1024;   // + alignment slack
+           (size_t)tc_cfg(mode, type).raw * tc_raw_bytes(mode, type) + tc_epi_bytes(mode) + 1024;   // + alignment slack
 }
 static_assert(tc_cfg(0, T_Q4K).a >= 2 && tc_cfg(0, T_Q6K).a >= 2 && tc_cfg(1, T_Q4K).a >= 2 &&
                   tc_cfg(1, T_Q6K).a >= 2, "shared-memory plan");
@@ -302,7 +307,7 @@ struct TcArgs {
 };
 
 template <int MODE, int TYPE>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
+__global__ void __launch_bounds__(tc_threads(MODE), 1) k_tc_experts(TcArgs a) {
     constexpr int NMAT = MODE == 0 ? 2 : 1;
     constexpr TcCfg CFG = tc_cfg(MODE, TYPE);
     constexpr int AST = CFG.a, BST = CFG.b;
@@ -313,7 +318,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
     constexpr int RAW_BYTES = NMAT * RAW_MAT;
     constexpr int RAWD = CFG.raw;                          // stages of raw bytes in flight
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t full_a[AST], empty_a[AST], full_b[BST], empty_b[BST], acc_full, acc_empty, done_bar;
+    // accumulators: gate/up uses all 512 TMEM columns (one buffer); down double-buffers 2 x 256 columns
+    constexpr int NACC = MODE == 0 ? 1 : 2;
+    __shared__ uint64_t full_a[AST], empty_a[AST], full_b[BST], empty_b[BST], acc_full[NACC], acc_empty[NACC], done_bar;
     __shared__ uint32_t s_tmem;
     __shared__ volatile int s_abort;
     __shared__ float s_amax[2][TC_M];
@@ -322,6 +329,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
     uint8_t* ring_a = smem;                                // [AST][A_BYTES]
     uint8_t* ring_b = smem + AST * A_BYTES;                // [BST][NMAT][B_BYTES]
     uint8_t* ring = ring_b + BST * BSTAGE_BYTES;           // [RAWD][RAW_BYTES]
+    float* epi_tile = reinterpret_cast<float*>(ring + RAWD * RAW_BYTES);   // down epilogue: [4 warps][32][EPI_ROW]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = MODE == 0 ? a.H : a.I;                   // reduction length
     const int NOUT = MODE == 0 ? a.I : a.H;                // output rows of the weight matrix
@@ -339,8 +347,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
             bar_init(&full_b[s], B_THREADS);
             bar_init(&empty_b[s], 1);
         }
-        bar_init(&acc_full, 1);
-        bar_init(&acc_empty, B_THREADS);
+        for (int i = 0; i < NACC; ++i) {
+            bar_init(&acc_full[i], 1);
+            bar_init(&acc_empty[i], MODE == 0 ? B_THREADS : EPI_THREADS);
+        }
         bar_init(&done_bar, 1);
         s_abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -376,7 +386,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
         if (warp == 0) {
             // ---------------- MMA issuer ----------------
             if (lane == 0) {
-                bool ok = item_no == 0 || bar_wait(&acc_empty, (item_no - 1) & 1, &s_abort);
+                // this item's accumulator buffer must have been drained by the epilogue of its last user
+                const int buf = item_no % NACC, use = item_no / NACC;
+                const uint32_t dacc = tmem + (uint32_t)(buf * TC_N);
+                bool ok = use == 0 || bar_wait(&acc_empty[buf], (use - 1) & 1, &s_abort);
                 tc_fence_after();
                 for (int kc = 0; kc < KC && ok; ++kc) {
                     const uint32_t st_it = it0 + kc;
@@ -392,14 +405,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
 #pragma unroll
                     for (int ks = 0; ks < TC_KC / 16; ++ks) {   // +32 bytes of K = +2 in the descriptor
                         const uint32_t acc = (kc > 0 || ks > 0) ? 1u : 0u;
-                        umma_f16(tmem, ad + 2 * ks, bd0 + 2 * ks, acc);
+                        umma_f16(dacc, ad + 2 * ks, bd0 + 2 * ks, acc);
                         if (MODE == 0) umma_f16(tmem + TC_N, ad + 2 * ks, bd1 + 2 * ks, acc);
                     }
                     umma_commit(&empty_a[sa]);       // the stages are free once these MMAs have read them
                     umma_commit(&empty_b[sb]);
                     TC_STAMP(item_no, kc, 1);
                 }
-                if (ok) umma_commit(&acc_full);      // accumulators complete
+                if (ok) umma_commit(&acc_full[buf]); // accumulators complete
             }
             __syncwarp();
         } else if (warp < 5) {
@@ -433,8 +446,48 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
                 cp_async_arrive_noinc(&full_a[s]);
                 if (t == 0) TC_STAMP(item_no, kc, 6);
             }
+        } else if (MODE == 1 && warp >= EPI_TID0 / 32) {
+            // ---------------- down epilogue (128 threads): TMEM -> y rows, one accumulator row each -----
+            const int buf = item_no % NACC, use = item_no / NACC;
+            const bool ok = __all_sync(0xFFFFFFFFu, bar_wait(&acc_full[buf], use & 1, &s_abort));
+            if (tid == EPI_TID0) TC_STAMP(item_no, 0, 7);
+            const int q = warp & 3;
+            const int m = 32 * q + lane;                          // accumulator row = tile row
+            const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * TC_N);
+            const bool valid = m < nrows;
+            if (ok) {
+                tc_fence_after();
+                // each 32 x 32 chunk (lane = row) goes through a padded shared tile so that a store
+                // instruction writes four whole 128-byte row segments instead of 32 scattered 16 bytes
+                const int entry = valid ? a.perm[row0 + m] : -1;
+                float* tile = epi_tile + (warp & 3) * 32 * EPI_ROW;
+                const int rsub = lane >> 3, c4 = lane & 7;          // read phase: row 4i + rsub, float4 c4
+                float v[32];
+#pragma unroll 1
+                for (int cc = 0; cc < TC_N / 32; ++cc) {
+                    tmem_ld32(lane_base + 32 * cc, v);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        *reinterpret_cast<float4*>(tile + lane * EPI_ROW + 4 * i) =
+                            make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int rr = 4 * i + rsub;
+                        const int ent = __shfl_sync(0xFFFFFFFFu, entry, rr);
+                        const float4 val = *reinterpret_cast<const float4*>(tile + rr * EPI_ROW + 4 * c4);
+                        if (ent >= 0)
+                            *reinterpret_cast<float4*>(a.y + (int64_t)ent * a.H + (int64_t)nb_out * TC_N + 32 * cc +
+                                                       4 * c4) = val;
+                    }
+                    __syncwarp();
+                }
+            }
+            tc_fence_before();
+            bar_arrive(&acc_empty[buf]);
+            if (tid == EPI_TID0) TC_STAMP(item_no, 1, 7);
         } else {
-            // ---------------- B dequant (256 threads), then the epilogue ----------------
+            // ---------------- B dequant (256 threads), then the gate/up epilogue ----------------
             const int r = tid - B_TID0;                          // B row within the N block
             const int64_t n = (int64_t)nb_out * TC_N + r;        // weight row
             const bool sh = slot >= a.lw.n_slots;
@@ -494,15 +547,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
                 if (r == 0) TC_STAMP(item_no, kc, 4);
                 issue(kc + RAWD);                                // refill this ring slot (its bytes are consumed)
             }
-            // ---- epilogue: warp % 4 selects the TMEM lane quarter, (warp - 5) / 4 the column half ----
-            const bool ok = __all_sync(0xFFFFFFFFu, bar_wait(&acc_full, item_no & 1, &s_abort));
+            if (MODE == 1) continue;
+            // ---- gate/up epilogue: warp % 4 selects the TMEM lane quarter, (warp - 5) / 4 the column half ----
+            const bool ok = __all_sync(0xFFFFFFFFu, bar_wait(&acc_full[0], item_no & 1, &s_abort));
             if (r == 0) TC_STAMP(item_no, 0, 7);
             const int q = warp & 3, half = (warp - 5) >> 2;
             const int m = 32 * q + lane;                          // accumulator row = tile row
             const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
             const bool valid = m < nrows;
             if (ok) tc_fence_after();
-            if (MODE == 0) {
+            {
                 float amax = 0.f;
                 float g[32], u[32];
                 if (ok) {
@@ -546,22 +600,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(TcArgs a) {
                     }
                 }
                 asm volatile("bar.sync 1, 256;" ::: "memory");   // s_amax is reused by the next item
-            } else if (ok) {
-                const int entry = valid ? a.perm[row0 + m] : 0;
-                float v[32];
-#pragma unroll 1
-                for (int cc = 0; cc < 4; ++cc) {
-                    const int col = 128 * half + 32 * cc;
-                    tmem_ld32(lane_base + col, v);
-                    if (valid) {
-                        float4* dst = reinterpret_cast<float4*>(a.y + (int64_t)entry * a.H + (int64_t)nb_out * TC_N + col);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                    }
-                }
             }
             tc_fence_before();
-            bar_arrive(&acc_empty);
+            bar_arrive(&acc_empty[0]);
             if (r == 0) TC_STAMP(item_no, 1, 7);
         }
     }
@@ -629,7 +670,7 @@ cudaError_t launch_tc(const TcArgs& a, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_set |= 1ull << dev;
     }
-    k_tc_experts<MODE, TYPE><<<tc_grid(), TC_THREADS, tc_smem(MODE, TYPE), s>>>(a);
+    k_tc_experts<MODE, TYPE><<<tc_grid(), tc_threads(MODE), tc_smem(MODE, TYPE), s>>>(a);
     return cudaGetLastError();
 }
 
