@@ -94,6 +94,18 @@ cudaError_t launch_experts_tc(const Dims& d, const LayerWeights& lw, const Scrat
                               const int32_t* slot_of_sel, const float* w, void* x_inout, int T, cudaStream_t s,
                               int* launches, unsigned long long* trace);
 
+// Expert parallelism: the experts of R already-quantised rows, each bound to a slot, into y_out [R][H];
+// the combine of rows that came back in send order (pos[t*k + j] = row of entry (t, j)); the f16
+// Q8_K rows of fx; the pack of (token, j) entries by destination rank.
+cudaError_t launch_experts_tc_rows(const Dims& d, const LayerWeights& lw, const Scratch& sc, const uint16_t* rows,
+                                   const int32_t* slot_of_row, int R, float* y_out, cudaStream_t s, int* launches);
+cudaError_t launch_combine_rows(const Dims& d, const float* y, const int* pos, const float* w, void* x_inout, int T,
+                                cudaStream_t s);
+cudaError_t launch_q8_rows(const float* fx, int T, int H, uint16_t* out, cudaStream_t s);
+cudaError_t launch_ep_pack(const int32_t* sel, int T, int k, int n_ranks, int experts_per_rank, const uint16_t* xq,
+                           int H, int* counts, int* cursor, int* pos_of_entry, int32_t* send_expert,
+                           uint16_t* send_rows, unsigned* err, cudaStream_t s, int* launches);
+
 // Persistent fused decode kernel over n_layers layers (T <= decode_max_tokens()).
 int decode_max_tokens();
 int decode_grid();           // CTAs of a persistent launch (one per SM)

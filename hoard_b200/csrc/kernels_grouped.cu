@@ -512,12 +512,13 @@ __global__ void __launch_bounds__(256) k_shared_gate(const float* __restrict__ f
     if (threadIdx.x == 0) out[t] = sigmoid_f((float)acc);
 }
 
-// x[t] += sum_j w[t][j] * y[t*KK + j] (+ sh_gate[t] * y[t*KK + k]), j ascending; four columns per
-// thread, the k rows' loads issued together
+// x[t] += sum_j w[t][j] * y[row(t, j)] (+ sh_gate[t] * y[t*KK + k]), j ascending; row(t, j) =
+// t*KK + j, or pos[t*k + j] for rows that came back from an expert-parallel exchange. Four columns
+// per thread, the k rows' loads issued together.
 template <typename R>
 __global__ void __launch_bounds__(256) k_combine(const float* __restrict__ y, const float* __restrict__ w,
                                                  const float* __restrict__ sh_gate, int k, int KK, int H, int T,
-                                                 R* x) {
+                                                 R* x, const int* __restrict__ pos) {
     const int64_t nq = (int64_t)T * H / 4;
     for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < nq; q += (int64_t)gridDim.x * blockDim.x) {
         const int64_t t = (q * 4) / H;
@@ -526,7 +527,14 @@ __global__ void __launch_bounds__(256) k_combine(const float* __restrict__ y, co
         float4 yv[MAX_K];
 #pragma unroll
         for (int j = 0; j < MAX_K; ++j)
-            if (j < k) yv[j] = *reinterpret_cast<const float4*>(yb + (int64_t)j * H);
+            if (j < k) {
+                const int row = pos ? pos[t * k + j] : -1;
+                yv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (!pos)
+                    yv[j] = *reinterpret_cast<const float4*>(yb + (int64_t)j * H);
+                else if (row >= 0)                         // < 0: the entry was rejected at pack time
+                    yv[j] = *reinterpret_cast<const float4*>(y + (int64_t)row * H + dcol);
+            }
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int j = 0; j < MAX_K; ++j) {
@@ -538,7 +546,7 @@ __global__ void __launch_bounds__(256) k_combine(const float* __restrict__ y, co
                 acc.w += wj * yv[j].w;
             }
         }
-        if (KK > k) {
+        if (KK > k && !pos) {
             const float4 ys = *reinterpret_cast<const float4*>(yb + (int64_t)k * H);
             const float g = sh_gate[t];
             acc.x = acc.x + ys.x * g;
@@ -663,9 +671,21 @@ cudaError_t launch_combine(const Dims& d, const Scratch& sc, const float* w, voi
     const int64_t n = (int64_t)T * d.H / 4;
     const int cb = (int)((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
     if (d.resid_bf16)
-        k_combine<__nv_bfloat16><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, (__nv_bfloat16*)x_inout);
+        k_combine<__nv_bfloat16><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, (__nv_bfloat16*)x_inout,
+                                                    nullptr);
     else
-        k_combine<float><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, (float*)x_inout);
+        k_combine<float><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, (float*)x_inout, nullptr);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_combine_rows(const Dims& d, const float* y, const int* pos, const float* w, void* x_inout, int T,
+                                cudaStream_t s) {
+    const int64_t n = (int64_t)T * d.H / 4;
+    const int cb = (int)((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
+    if (d.resid_bf16)
+        k_combine<__nv_bfloat16><<<cb, 256, 0, s>>>(y, w, nullptr, d.k, d.k, d.H, T, (__nv_bfloat16*)x_inout, pos);
+    else
+        k_combine<float><<<cb, 256, 0, s>>>(y, w, nullptr, d.k, d.k, d.H, T, (float*)x_inout, pos);
     return cudaGetLastError();
 }
 

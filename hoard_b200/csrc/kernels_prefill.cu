@@ -688,6 +688,43 @@ bool tc_supported(const Dims& d, const LayerWeights& lw) {
 
 int64_t tc_max_items(int T, int KK, int n_slots) { return ((int64_t)T * KK + TC_M - 1) / TC_M + n_slots + 1; }
 
+// Expert FFN of R rows that arrive already quantised (Q8_K q*d as f16, [R][H]), each bound to one
+// pool slot: the expert-parallel receive side. y_out[r] (f32 [R][H]) is row r's expert output.
+cudaError_t launch_experts_tc_rows(const Dims& d, const LayerWeights& lw, const Scratch& sc, const uint16_t* rows,
+                                   const int32_t* slot_of_row, int R, float* y_out, cudaStream_t s, int* launches) {
+    int nl = 0;
+    cudaError_t e;
+    if ((e = launch_dispatch(slot_of_row, R, 1, 1, lw.n_slots, sc, TC_M, s, &nl)) != cudaSuccess) return e;
+    TcArgs a{};
+    a.lw = lw;
+    a.lw.shared = nullptr;           // rows name their slot; a shared expert is not dispatched
+    a.H = d.H;
+    a.I = d.I;
+    a.KK = 1;
+    a.offsets = sc.offsets;
+    a.perm = sc.perm;
+    a.items = sc.items;
+    a.n_items = sc.n_items;
+    a.err = sc.sync;
+    a.A = reinterpret_cast<const __half*>(rows);
+    a.hq = reinterpret_cast<__half*>(sc.hq16);
+    e = lw.gate_type == T_Q4K ? launch_tc<0, T_Q4K>(a, s) : launch_tc<0, T_Q6K>(a, s);
+    if (e != cudaSuccess) return e;
+    a.A = reinterpret_cast<const __half*>(sc.hq16);
+    a.y = y_out;
+    e = lw.down_type == T_Q4K ? launch_tc<1, T_Q4K>(a, s) : launch_tc<1, T_Q6K>(a, s);
+    if (e != cudaSuccess) return e;
+    if (launches) *launches += nl + 2;
+    return cudaSuccess;
+}
+
+// Q8_K-dequantised f16 rows of fx ([T][H]); used by the expert-parallel send side.
+cudaError_t launch_q8_rows(const float* fx, int T, int H, uint16_t* out, cudaStream_t s) {
+    const int64_t nq = (int64_t)T * (H / QK);
+    k_q8_to_f16<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(fx, nq, reinterpret_cast<__half*>(out));
+    return cudaGetLastError();
+}
+
 int64_t tc_trace_elems() { return (int64_t)2 * TC_TRACE_CTAS * TC_TRACE_ITEMS * TC_TRACE_STAGES * TC_TRACE_SLOTS; }
 
 cudaError_t launch_experts_tc(const Dims& d, const LayerWeights& lw, const Scratch& sc, const float* fx,

@@ -54,6 +54,10 @@ struct hoard_moe_ctx {
     bool decode_ok = false;            // the persistent decode kernel supports these shapes / types
     unsigned long long* trace = nullptr;
     int64_t trace_cap = 0;
+    // expert-parallel receive side (hoard_moe_ep_reserve): dispatch + h scratch for up to ep_rows rows
+    int64_t ep_rows = 0;
+    Scratch ep{};
+    int* ep_cursor = nullptr;          // [64] pack cursors
     std::string err;
 };
 
@@ -453,6 +457,77 @@ int hoard_moe_decode_noalloc(hoard_moe_ctx* c, int layer0, int n_layers, void* x
 int hoard_moe_set_decode_impl(hoard_moe_ctx* c, int impl) {
     if (!c || impl < 0 || impl > 1) return HOARD_EINVAL;
     c->decode_impl = impl;
+    return HOARD_OK;
+}
+
+int hoard_moe_ep_reserve(hoard_moe_ctx* c, int64_t max_rows) {
+    if (!c || max_rows <= 0 || max_rows > (int64_t)1 << 30) return c ? fail(c, HOARD_EINVAL, "max_rows out of range") : HOARD_EINVAL;
+    if (max_rows <= c->ep_rows) return HOARD_OK;
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    Scratch& e = c->ep;
+    const int64_t NS2 = (int64_t)c->desc.n_slots + 2;
+    int rc = dalloc(c, &e.counts, NS2 * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &e.offsets, NS2 * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &e.perm, max_rows * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &e.hq16, max_rows * c->dims.I * 2);
+    if (rc == HOARD_OK) rc = dalloc(c, &e.items, tc_max_items((int)max_rows, 1, c->desc.n_slots) * (int64_t)sizeof(int2));
+    if (rc == HOARD_OK) rc = dalloc(c, &e.n_items, 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &e.dcount, NS2 * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &e.dcursor, NS2 * 4);
+    if (rc == HOARD_OK && !c->ep_cursor) rc = dalloc(c, &c->ep_cursor, 64 * 4);
+    if (rc != HOARD_OK) return rc;
+    HCHECK(c, cudaMemset(e.dcount, 0, (size_t)NS2 * 4));
+    e.sync = c->sc.sync;
+    c->ep_rows = max_rows;
+    return HOARD_OK;
+}
+
+int hoard_moe_ep_pack(hoard_moe_ctx* c, int layer, const int32_t* sel, int T, int n_ranks, int experts_per_rank,
+                      int32_t* send_counts, int32_t* pos_of_entry, int32_t* send_expert, uint16_t* send_rows,
+                      hoard_stream stream) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (T <= 0 || T > c->desc.max_tokens) return fail(c, HOARD_EINVAL, "T out of range (1..max_tokens)");
+    if (n_ranks < 1 || n_ranks > 64 || experts_per_rank < 1 || (int64_t)n_ranks * experts_per_rank < c->dims.E)
+        return fail(c, HOARD_EINVAL, "n_ranks * experts_per_rank must cover n_expert (n_ranks <= 64)");
+    if (!sel || !send_counts || !pos_of_entry || !send_expert || !send_rows) return fail(c, HOARD_EINVAL, "null pointer");
+    if (c->routed_layer != layer || c->routed_T < T)
+        return fail(c, HOARD_ESTATE, "hoard_moe_route(layer, ..., T) must run first on this stream");
+    if (!c->ep_cursor && (rc = dalloc(c, &c->ep_cursor, 64 * 4))) return rc;
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    int nl = 0;
+    HCHECK(c, launch_q8_rows(c->sc.fx, T, c->dims.H, c->sc.xq16, (cudaStream_t)stream));
+    ++nl;
+    HCHECK(c, launch_ep_pack(sel, T, c->dims.k, n_ranks, experts_per_rank, c->sc.xq16, c->dims.H, send_counts,
+                             c->ep_cursor, pos_of_entry, send_expert, send_rows, c->sc.sync, (cudaStream_t)stream, &nl));
+    c->launches += nl;
+    return HOARD_OK;
+}
+
+int hoard_moe_ep_experts(hoard_moe_ctx* c, int layer, const uint16_t* rows, const int32_t* slot_of_row, int R,
+                         float* y_out, hoard_stream stream) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (R < 0 || R > c->ep_rows) return fail(c, HOARD_EINVAL, "R out of range (0..hoard_moe_ep_reserve's max_rows)");
+    if (R == 0) return HOARD_OK;
+    if (!rows || !slot_of_row || !y_out) return fail(c, HOARD_EINVAL, "null pointer");
+    const LayerWeights lw = layer_weights(c, layer);
+    if (!tc_supported(c->dims, lw)) return fail(c, HOARD_EINVAL, "expert types unsupported by the tensor-core path");
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    int nl = 0;
+    HCHECK(c, launch_experts_tc_rows(c->dims, lw, c->ep, rows, slot_of_row, R, y_out, (cudaStream_t)stream, &nl));
+    c->launches += nl;
+    return HOARD_OK;
+}
+
+int hoard_moe_ep_combine(hoard_moe_ctx* c, const float* w, const int32_t* pos_of_entry, const float* y_back,
+                         void* x_inout, int T, hoard_stream stream) {
+    if (!c) return HOARD_EINVAL;
+    if (T <= 0 || T > c->desc.max_tokens) return fail(c, HOARD_EINVAL, "T out of range (1..max_tokens)");
+    if (!w || !pos_of_entry || !y_back || !x_inout) return fail(c, HOARD_EINVAL, "null pointer");
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    HCHECK(c, launch_combine_rows(c->dims, y_back, pos_of_entry, w, x_inout, T, (cudaStream_t)stream));
+    ++c->launches;
     return HOARD_OK;
 }
 

@@ -34,7 +34,8 @@ EXPORTED = [
     "hoard_moe_set_shared", "hoard_moe_route", "hoard_moe_experts", "hoard_moe_layer", "hoard_moe_layers",
     "hoard_moe_sync_status", "hoard_moe_expert_bytes", "hoard_moe_launch_count", "hoard_moe_set_decode_impl",
     "hoard_moe_set_trace", "hoard_moe_trace_layout", "hoard_moe_decode_noalloc",
-    "hoard_moe_set_gemm_min_tokens", "hoard_moe_last_error", "hoard_strerror",
+    "hoard_moe_set_gemm_min_tokens", "hoard_moe_ep_reserve", "hoard_moe_ep_pack", "hoard_moe_ep_experts",
+    "hoard_moe_ep_combine", "hoard_moe_last_error", "hoard_strerror",
 ]
 
 
@@ -83,6 +84,10 @@ def lib() -> ctypes.CDLL:
         L.hoard_moe_launch_count.restype = i64
         L.hoard_moe_set_decode_impl.argtypes = [vp, i32]
         L.hoard_moe_set_gemm_min_tokens.argtypes = [vp, i32]
+        L.hoard_moe_ep_reserve.argtypes = [vp, i64]
+        L.hoard_moe_ep_pack.argtypes = [vp, i32, vp, i32, i32, i32, vp, vp, vp, vp, vp]
+        L.hoard_moe_ep_experts.argtypes = [vp, i32, vp, vp, i32, vp, vp]
+        L.hoard_moe_ep_combine.argtypes = [vp, vp, vp, vp, vp, i32, vp]
         L.hoard_moe_set_trace.argtypes = [vp, vp, i64]
         L.hoard_moe_decode_noalloc.argtypes = [vp, i32, i32, vp, vp, vp, vp]
         L.hoard_moe_trace_layout.argtypes = [vp, ctypes.POINTER(i32), ctypes.POINTER(i32)]
@@ -163,6 +168,42 @@ class MoEContext:
 
     def set_decode_impl(self, impl: int):
         self._check(lib().hoard_moe_set_decode_impl(self._h, impl), "set_decode_impl")
+
+    # ---- expert parallelism (the exchange between these calls is the caller's; see hoard_b200.ep) ----
+    def ep_reserve(self, max_rows: int):
+        """Receive-side scratch for up to max_rows rows per ep_experts call."""
+        self._check(lib().hoard_moe_ep_reserve(self._h, max_rows), "ep_reserve")
+
+    def ep_pack(self, layer: int, sel: torch.Tensor, n_ranks: int, experts_per_rank: int, stream=None):
+        """After route(layer, x): entries sorted by destination rank. Returns (send_counts [n_ranks],
+        pos_of_entry [T*k], send_expert [T*k], send_rows [T*k][H] f16) on the device."""
+        T = sel.shape[0]
+        dev = sel.device
+        n = T * self.k
+        counts = torch.empty(n_ranks, dtype=torch.int32, device=dev)
+        pos = torch.empty(n, dtype=torch.int32, device=dev)
+        expert = torch.empty(n, dtype=torch.int32, device=dev)
+        rows = torch.empty(n, self.H, dtype=torch.float16, device=dev)
+        self._check(lib().hoard_moe_ep_pack(self._h, layer, _ptr(sel), T, n_ranks, experts_per_rank, _ptr(counts),
+                                            _ptr(pos), _ptr(expert), _ptr(rows), _stream(stream)), "ep_pack")
+        return counts, pos, expert, rows
+
+    def ep_experts(self, layer: int, rows: torch.Tensor, slot_of_row: torch.Tensor, y_out: torch.Tensor | None = None,
+                   stream=None):
+        """Expert FFN of received f16 rows [R][H] bound to slots [R] -> y [R][H] f32."""
+        R = rows.shape[0]
+        if y_out is None:
+            y_out = torch.empty(R, self.H, dtype=torch.float32, device=rows.device)
+        self._check(lib().hoard_moe_ep_experts(self._h, layer, _ptr(rows), _ptr(slot_of_row), R, _ptr(y_out),
+                                               _stream(stream)), "ep_experts")
+        return y_out
+
+    def ep_combine(self, w: torch.Tensor, pos_of_entry: torch.Tensor, y_back: torch.Tensor, x_inout: torch.Tensor,
+                   stream=None):
+        T = x_inout.shape[0]
+        self._check(lib().hoard_moe_ep_combine(self._h, _ptr(w), _ptr(pos_of_entry), _ptr(y_back), _ptr(x_inout), T,
+                                               _stream(stream)), "ep_combine")
+        return x_inout
 
     def set_gemm_min_tokens(self, min_tokens: int):
         """T at or above which the expert FFN runs as the tensor-core grouped GEMM (0 = never)."""

@@ -176,6 +176,39 @@ int hoard_moe_set_decode_impl(hoard_moe_ctx* ctx, int impl);
  * its graph picks the backend's matmul kernel by batch size. */
 int hoard_moe_set_gemm_min_tokens(hoard_moe_ctx* ctx, int min_tokens);
 
+/* ---- Expert parallelism (batched tokens over G ranks, experts [g*E/G, (g+1)*E/G) on rank g) ----
+ * The sharded counterpart of the single-process mul_mat_id of src/run_specloop.cpp:125-140, which
+ * hoard runs on one GPU only. One context per rank; its pool holds at least the rank's own experts.
+ * Per layer: hoard_moe_route -> hoard_moe_ep_pack -> all-to-all of send_counts, then of send_rows and
+ * send_expert (rows for rank r are the r-th run of send_counts) -> hoard_moe_ep_experts on the
+ * received rows -> all-to-all of y back (the reverse splits) -> hoard_moe_ep_combine. The exchange is
+ * the caller's (NCCL / torch.distributed); every row is computed independently and y returns in f32,
+ * so G ranks reproduce the single-rank result bit for bit. */
+
+/* Reserves the receive-side scratch for up to max_rows rows per hoard_moe_ep_experts call. */
+int hoard_moe_ep_reserve(hoard_moe_ctx* ctx, int64_t max_rows);
+
+/* Send side, after hoard_moe_route(ctx, layer, x, T, sel, w) on the same stream: counting-sorts the
+ * T*k (token, j) entries by destination rank sel / experts_per_rank and gathers their Q8_K-quantised
+ * activation rows (q*d as f16). Device outputs: send_counts [n_ranks] rows per destination, in rank
+ * order; pos_of_entry [T*k] the send row of entry t*k+j (-1 if its expert id was out of range:
+ * reported by hoard_moe_sync_status); send_expert [T*k] the global expert id of each send row;
+ * send_rows [T*k][n_embd] f16 bits. Within one destination the row order is unspecified. */
+int hoard_moe_ep_pack(hoard_moe_ctx* ctx, int layer, const int32_t* sel, int T, int n_ranks,
+                      int experts_per_rank, int32_t* send_counts, int32_t* pos_of_entry, int32_t* send_expert,
+                      uint16_t* send_rows, hoard_stream stream);
+
+/* Receive side: expert FFN (gate/up, SwiGLU, Q8_K of h, down) of R received rows (f16 [R][n_embd])
+ * bound to this context's pool slots slot_of_row [R], into y_out [R][n_embd] f32 (device pointers).
+ * R <= the reserved max_rows. */
+int hoard_moe_ep_experts(hoard_moe_ctx* ctx, int layer, const uint16_t* rows, const int32_t* slot_of_row, int R,
+                         float* y_out, hoard_stream stream);
+
+/* Send side: x[t] += sum_j w[t][j] * y_back[pos_of_entry[t*k+j]] (j ascending, the combine of
+ * src/run_moe_stream.cpp:447), y_back [T*k][n_embd] f32 in send order. */
+int hoard_moe_ep_combine(hoard_moe_ctx* ctx, const float* w, const int32_t* pos_of_entry, const float* y_back,
+                         void* x_inout, int T, hoard_stream stream);
+
 /* Last error message of this context (CUDA error string or argument check). */
 const char* hoard_moe_last_error(const hoard_moe_ctx* ctx);
 
