@@ -11,7 +11,7 @@ own T tokens). One MoE layer on one rank:
 
 The arithmetic of every row is independent of which rows share its tile and the outputs travel in
 f32, so G ranks reproduce the single-rank result bit for bit. The exchange uses torch.distributed
-(NCCL on GPUs, gloo in the CPU tests): plain all-to-all collectives, no peer loads or multicast.
+(NCCL on GPUs, gloo in the CPU tests): plain all-to-all collectives; no kernel reads peer memory.
 
 hoard has no multi-GPU path; this is the sharded form of its batched mul_mat_id
 (src/run_specloop.cpp:125-140).
