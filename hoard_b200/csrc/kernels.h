@@ -83,8 +83,9 @@ cudaError_t launch_shared_gate(const float* fx, const float* gate_inp, int H, in
 // Counting sort of the entries by slot; with tile_m > 0 also the (slot, M tile) work list.
 cudaError_t launch_dispatch(const int32_t* slot_of_sel, int T, int k, int KK, int n_slots, const Scratch& sc,
                             int tile_m, cudaStream_t s, int* launches);
+// y_half: sc.y holds f16 rows (tensor-core path) instead of f32 rows (grouped path)
 cudaError_t launch_combine(const Dims& d, const Scratch& sc, const float* w, void* x_inout, int T, int KK,
-                           cudaStream_t s);
+                           cudaStream_t s, bool y_half);
 
 // The tensor-core grouped GEMM expert path (prefill / batched tokens), adding into x_inout.
 bool tc_supported(const Dims& d, const LayerWeights& lw);
@@ -98,8 +99,8 @@ cudaError_t launch_experts_tc(const Dims& d, const LayerWeights& lw, const Scrat
 // the combine of rows that came back in send order (pos[t*k + j] = row of entry (t, j)); the f16
 // Q8_K rows of fx; the pack of (token, j) entries by destination rank.
 cudaError_t launch_experts_tc_rows(const Dims& d, const LayerWeights& lw, const Scratch& sc, const uint16_t* rows,
-                                   const int32_t* slot_of_row, int R, float* y_out, cudaStream_t s, int* launches);
-cudaError_t launch_combine_rows(const Dims& d, const float* y, const int* pos, const float* w, void* x_inout, int T,
+                                   const int32_t* slot_of_row, int R, uint16_t* y_out, cudaStream_t s, int* launches);
+cudaError_t launch_combine_rows(const Dims& d, const uint16_t* y, const int* pos, const float* w, void* x_inout, int T,
                                 cudaStream_t s);
 cudaError_t launch_q8_rows(const float* fx, int T, int H, uint16_t* out, cudaStream_t s);
 cudaError_t launch_ep_pack(const int32_t* sel, int T, int k, int n_ranks, int experts_per_rank, const uint16_t* xq,

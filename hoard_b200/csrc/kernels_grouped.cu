@@ -515,15 +515,24 @@ __global__ void __launch_bounds__(256) k_shared_gate(const float* __restrict__ f
 // x[t] += sum_j w[t][j] * y[row(t, j)] (+ sh_gate[t] * y[t*KK + k]), j ascending; row(t, j) =
 // t*KK + j, or pos[t*k + j] for rows that came back from an expert-parallel exchange. Four columns
 // per thread, the k rows' loads issued together.
-template <typename R>
-__global__ void __launch_bounds__(256) k_combine(const float* __restrict__ y, const float* __restrict__ w,
+__device__ __forceinline__ float4 ld_y4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ld_y4(const __half* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// YT: float (grouped path) or __half (tensor-core path) expert outputs
+template <typename R, typename YT>
+__global__ void __launch_bounds__(256) k_combine(const YT* __restrict__ y, const float* __restrict__ w,
                                                  const float* __restrict__ sh_gate, int k, int KK, int H, int T,
                                                  R* x, const int* __restrict__ pos) {
     const int64_t nq = (int64_t)T * H / 4;
     for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < nq; q += (int64_t)gridDim.x * blockDim.x) {
         const int64_t t = (q * 4) / H;
         const int64_t dcol = q * 4 - t * H;
-        const float* yb = y + t * KK * H + dcol;
+        const YT* yb = y + t * KK * H + dcol;
         float4 yv[MAX_K];
 #pragma unroll
         for (int j = 0; j < MAX_K; ++j)
@@ -531,9 +540,9 @@ __global__ void __launch_bounds__(256) k_combine(const float* __restrict__ y, co
                 const int row = pos ? pos[t * k + j] : -1;
                 yv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (!pos)
-                    yv[j] = *reinterpret_cast<const float4*>(yb + (int64_t)j * H);
+                    yv[j] = ld_y4(yb + (int64_t)j * H);
                 else if (row >= 0)                         // < 0: the entry was rejected at pack time
-                    yv[j] = *reinterpret_cast<const float4*>(y + (int64_t)row * H + dcol);
+                    yv[j] = ld_y4(y + (int64_t)row * H + dcol);
             }
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
@@ -547,7 +556,7 @@ __global__ void __launch_bounds__(256) k_combine(const float* __restrict__ y, co
             }
         }
         if (KK > k && !pos) {
-            const float4 ys = *reinterpret_cast<const float4*>(yb + (int64_t)k * H);
+            const float4 ys = ld_y4(yb + (int64_t)k * H);
             const float g = sh_gate[t];
             acc.x = acc.x + ys.x * g;
             acc.y = acc.y + ys.y * g;
@@ -559,6 +568,62 @@ __global__ void __launch_bounds__(256) k_combine(const float* __restrict__ y, co
         xp[1] = from_f32<R>(acc.y + to_f32<R>(xp[1]));
         xp[2] = from_f32<R>(acc.z + to_f32<R>(xp[2]));
         xp[3] = from_f32<R>(acc.w + to_f32<R>(xp[3]));
+    }
+}
+
+// The same combine over f16 expert outputs (tensor-core path and expert-parallel returns): eight
+// columns per thread (one 16-byte load per row), the k rows in batches of eight loads in flight.
+template <typename R>
+__global__ void __launch_bounds__(256) k_combine_h(const __half* __restrict__ y, const float* __restrict__ w,
+                                                   const float* __restrict__ sh_gate, int k, int KK, int H, int T,
+                                                   R* x, const int* __restrict__ pos) {
+    const int64_t n8 = (int64_t)T * H / 8;
+    for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < n8; q += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = (q * 8) / H;
+        const int64_t dcol = q * 8 - t * H;
+        float acc[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+        for (int j0 = 0; j0 < k; j0 += 8) {
+            uint4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                v[u] = make_uint4(0, 0, 0, 0);
+                const int j = j0 + u;
+                if (j < k) {
+                    const int64_t row = pos ? (int64_t)pos[t * k + j] : t * KK + j;
+                    if (row >= 0) v[u] = *reinterpret_cast<const uint4*>(y + row * H + dcol);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int j = j0 + u;
+                if (j < k) {
+                    const float wj = w[t * k + j];
+                    const uint32_t pw[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pw[c]));
+                        acc[2 * c] += wj * f.x;
+                        acc[2 * c + 1] += wj * f.y;
+                    }
+                }
+            }
+        }
+        if (KK > k && !pos) {
+            const uint4 vs = *reinterpret_cast<const uint4*>(y + (t * KK + k) * H + dcol);
+            const float g = sh_gate[t];
+            const uint32_t pw[4] = {vs.x, vs.y, vs.z, vs.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pw[c]));
+                acc[2 * c] = acc[2 * c] + f.x * g;
+                acc[2 * c + 1] = acc[2 * c + 1] + f.y * g;
+            }
+        }
+        R* xp = x + q * 8;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) xp[c] = from_f32<R>(acc[c] + to_f32<R>(xp[c]));
     }
 }
 
@@ -667,25 +732,33 @@ cudaError_t launch_dispatch(const int32_t* slot_of_sel, int T, int k, int KK, in
 }
 
 cudaError_t launch_combine(const Dims& d, const Scratch& sc, const float* w, void* x_inout, int T, int KK,
-                           cudaStream_t s) {
+                           cudaStream_t s, bool y_half) {
     const int64_t n = (int64_t)T * d.H / 4;
     const int cb = (int)((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
-    if (d.resid_bf16)
-        k_combine<__nv_bfloat16><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, (__nv_bfloat16*)x_inout,
-                                                    nullptr);
-    else
-        k_combine<float><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, (float*)x_inout, nullptr);
+    const __half* yh = reinterpret_cast<const __half*>(sc.y);
+    const int64_t n8 = (int64_t)T * d.H / 8;
+    const int cbh = (int)((n8 + 255) / 256 < 148 * 16 ? (n8 + 255) / 256 : 148 * 16);
+    if (d.resid_bf16) {
+        auto* x = (__nv_bfloat16*)x_inout;
+        if (y_half) k_combine_h<__nv_bfloat16><<<cbh, 256, 0, s>>>(yh, w, sc.sh_gate, d.k, KK, d.H, T, x, nullptr);
+        else k_combine<__nv_bfloat16, float><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, x, nullptr);
+    } else {
+        auto* x = (float*)x_inout;
+        if (y_half) k_combine_h<float><<<cbh, 256, 0, s>>>(yh, w, sc.sh_gate, d.k, KK, d.H, T, x, nullptr);
+        else k_combine<float, float><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, x, nullptr);
+    }
     return cudaGetLastError();
 }
 
-cudaError_t launch_combine_rows(const Dims& d, const float* y, const int* pos, const float* w, void* x_inout, int T,
+cudaError_t launch_combine_rows(const Dims& d, const uint16_t* y, const int* pos, const float* w, void* x_inout, int T,
                                 cudaStream_t s) {
-    const int64_t n = (int64_t)T * d.H / 4;
-    const int cb = (int)((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
+    const int64_t n8 = (int64_t)T * d.H / 8;
+    const int cb = (int)((n8 + 255) / 256 < 148 * 16 ? (n8 + 255) / 256 : 148 * 16);
+    const __half* yh = reinterpret_cast<const __half*>(y);
     if (d.resid_bf16)
-        k_combine<__nv_bfloat16><<<cb, 256, 0, s>>>(y, w, nullptr, d.k, d.k, d.H, T, (__nv_bfloat16*)x_inout, pos);
+        k_combine_h<__nv_bfloat16><<<cb, 256, 0, s>>>(yh, w, nullptr, d.k, d.k, d.H, T, (__nv_bfloat16*)x_inout, pos);
     else
-        k_combine<float><<<cb, 256, 0, s>>>(y, w, nullptr, d.k, d.k, d.H, T, (float*)x_inout, pos);
+        k_combine_h<float><<<cb, 256, 0, s>>>(yh, w, nullptr, d.k, d.k, d.H, T, (float*)x_inout, pos);
     return cudaGetLastError();
 }
 
@@ -718,7 +791,7 @@ cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const 
                                                                     sc.h_bs, sc.y);
     ++nl;
     // 6. weighted combine into the residual
-    if ((e = launch_combine(d, sc, w, x_inout, T, KK, s)) != cudaSuccess) return e;
+    if ((e = launch_combine(d, sc, w, x_inout, T, KK, s, false)) != cudaSuccess) return e;
     ++nl;
     if (launches) *launches += nl;
     return cudaGetLastError();

@@ -301,7 +301,7 @@ struct TcArgs {
     const int* n_items;     // device count of M tiles (N blocks are expanded in the kernel)
     const __half* A;        // MODE 0: Q8_K-dequantised activations [T][H]; MODE 1: h [P][I] (sorted)
     __half* hq;             // MODE 0 output [P][I] (sorted order)
-    float* y;               // MODE 1 output [entries][H] by entry id
+    __half* y;              // MODE 1 output [entries][H] by entry id, f16 (clamped to the f16 range)
     unsigned* err;
     unsigned long long* trace;   // optional stamps [cta < TC_TRACE_CTAS][item < 2][stage < 32][TC_TRACE_SLOTS]
 };
@@ -476,9 +476,13 @@ __global__ void __launch_bounds__(tc_threads(MODE), 1) k_tc_experts(TcArgs a) {
                         const int rr = 4 * i + rsub;
                         const int ent = __shfl_sync(0xFFFFFFFFu, entry, rr);
                         const float4 val = *reinterpret_cast<const float4*>(tile + rr * EPI_ROW + 4 * c4);
+                        const float lim = 65504.f;
+                        const uint2 hv = make_uint2(
+                            bits_h2(__floats2half2_rn(fminf(fmaxf(val.x, -lim), lim), fminf(fmaxf(val.y, -lim), lim))),
+                            bits_h2(__floats2half2_rn(fminf(fmaxf(val.z, -lim), lim), fminf(fmaxf(val.w, -lim), lim))));
                         if (ent >= 0)
-                            *reinterpret_cast<float4*>(a.y + (int64_t)ent * a.H + (int64_t)nb_out * TC_N + 32 * cc +
-                                                       4 * c4) = val;
+                            *reinterpret_cast<uint2*>(a.y + (int64_t)ent * a.H + (int64_t)nb_out * TC_N + 32 * cc +
+                                                      4 * c4) = hv;
                     }
                     __syncwarp();
                 }
@@ -689,9 +693,9 @@ bool tc_supported(const Dims& d, const LayerWeights& lw) {
 int64_t tc_max_items(int T, int KK, int n_slots) { return ((int64_t)T * KK + TC_M - 1) / TC_M + n_slots + 1; }
 
 // Expert FFN of R rows that arrive already quantised (Q8_K q*d as f16, [R][H]), each bound to one
-// pool slot: the expert-parallel receive side. y_out[r] (f32 [R][H]) is row r's expert output.
+// pool slot: the expert-parallel receive side. y_out[r] (f16 [R][H]) is row r's expert output.
 cudaError_t launch_experts_tc_rows(const Dims& d, const LayerWeights& lw, const Scratch& sc, const uint16_t* rows,
-                                   const int32_t* slot_of_row, int R, float* y_out, cudaStream_t s, int* launches) {
+                                   const int32_t* slot_of_row, int R, uint16_t* y_out, cudaStream_t s, int* launches) {
     int nl = 0;
     cudaError_t e;
     if ((e = launch_dispatch(slot_of_row, R, 1, 1, lw.n_slots, sc, TC_M, s, &nl)) != cudaSuccess) return e;
@@ -711,7 +715,7 @@ cudaError_t launch_experts_tc_rows(const Dims& d, const LayerWeights& lw, const 
     e = lw.gate_type == T_Q4K ? launch_tc<0, T_Q4K>(a, s) : launch_tc<0, T_Q6K>(a, s);
     if (e != cudaSuccess) return e;
     a.A = reinterpret_cast<const __half*>(sc.hq16);
-    a.y = y_out;
+    a.y = reinterpret_cast<__half*>(y_out);
     e = lw.down_type == T_Q4K ? launch_tc<1, T_Q4K>(a, s) : launch_tc<1, T_Q6K>(a, s);
     if (e != cudaSuccess) return e;
     if (launches) *launches += nl + 2;
@@ -763,13 +767,13 @@ cudaError_t launch_experts_tc(const Dims& d, const LayerWeights& lw, const Scrat
     if (e != cudaSuccess) return e;
     ++nl;
     a.A = reinterpret_cast<const __half*>(sc.hq16);
-    a.y = sc.y;
+    a.y = reinterpret_cast<__half*>(sc.y);      // f16 rows in the f32 scratch
     if (trace) a.trace = trace + tc_trace_elems() / 2;
     e = lw.down_type == T_Q4K ? launch_tc<1, T_Q4K>(a, s) : launch_tc<1, T_Q6K>(a, s);
     if (e != cudaSuccess) return e;
     ++nl;
     // 5. weighted combine into the residual, j ascending (shared with the grouped path)
-    if ((e = launch_combine(d, sc, w, x_inout, T, KK, s)) != cudaSuccess) return e;
+    if ((e = launch_combine(d, sc, w, x_inout, T, KK, s, true)) != cudaSuccess) return e;
     ++nl;
     if (launches) *launches += nl;
     return cudaSuccess;

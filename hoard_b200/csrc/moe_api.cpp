@@ -505,7 +505,7 @@ int hoard_moe_ep_pack(hoard_moe_ctx* c, int layer, const int32_t* sel, int T, in
 }
 
 int hoard_moe_ep_experts(hoard_moe_ctx* c, int layer, const uint16_t* rows, const int32_t* slot_of_row, int R,
-                         float* y_out, hoard_stream stream) {
+                         uint16_t* y_out, hoard_stream stream) {
     int rc = check_layer(c, layer);
     if (rc) return rc;
     if (R < 0 || R > c->ep_rows) return fail(c, HOARD_EINVAL, "R out of range (0..hoard_moe_ep_reserve's max_rows)");
@@ -520,7 +520,7 @@ int hoard_moe_ep_experts(hoard_moe_ctx* c, int layer, const uint16_t* rows, cons
     return HOARD_OK;
 }
 
-int hoard_moe_ep_combine(hoard_moe_ctx* c, const float* w, const int32_t* pos_of_entry, const float* y_back,
+int hoard_moe_ep_combine(hoard_moe_ctx* c, const float* w, const int32_t* pos_of_entry, const uint16_t* y_back,
                          void* x_inout, int T, hoard_stream stream) {
     if (!c) return HOARD_EINVAL;
     if (T <= 0 || T > c->desc.max_tokens) return fail(c, HOARD_EINVAL, "T out of range (1..max_tokens)");

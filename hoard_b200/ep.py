@@ -6,11 +6,11 @@ own T tokens). One MoE layer on one rank:
     route (local)  ->  ep_pack: (token, j) entries counting-sorted by destination rank, their
     Q8_K-quantised f16 rows gathered  ->  all-to-all of the per-destination counts, then of the rows
     and their expert ids  ->  ep_experts on the received rows (the tensor-core grouped GEMM)  ->
-    all-to-all of the f32 outputs back (reverse splits)  ->  ep_combine: x[t] += sum_j w_j y_(t,j),
+    all-to-all of the f16 outputs back (reverse splits)  ->  ep_combine: x[t] += sum_j w_j y_(t,j),
     j ascending.
 
-The arithmetic of every row is independent of which rows share its tile and the outputs travel in
-f32, so G ranks reproduce the single-rank result bit for bit. The exchange uses torch.distributed
+The arithmetic of every row is independent of which rows share its tile and the outputs travel in the
+f16 form the single-rank tensor-core path stores too, so G ranks reproduce it bit for bit. The exchange uses torch.distributed
 (NCCL on GPUs, gloo in the CPU tests): plain all-to-all collectives; no kernel reads peer memory.
 
 hoard has no multi-GPU path; this is the sharded form of its batched mul_mat_id
@@ -66,7 +66,7 @@ class ExpertParallel:
         self._exchange(recv_expert, expert[:n_send], recv_splits, send_splits)
         slot = (recv_expert - self.rank * self.epr + self.slot_base).to(torch.int32)
         y = ctx.ep_experts(layer, recv_rows, slot)
-        y_back = torch.empty(T * k, H, dtype=torch.float32, device=rows.device)
+        y_back = torch.empty(T * k, H, dtype=y.dtype, device=rows.device)
         self._exchange(y_back[:n_send], y, send_splits, recv_splits)
         ctx.ep_combine(w, pos, y_back, x)
         return x, sel, w

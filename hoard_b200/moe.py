@@ -190,10 +190,10 @@ class MoEContext:
 
     def ep_experts(self, layer: int, rows: torch.Tensor, slot_of_row: torch.Tensor, y_out: torch.Tensor | None = None,
                    stream=None):
-        """Expert FFN of received f16 rows [R][H] bound to slots [R] -> y [R][H] f32."""
+        """Expert FFN of received f16 rows [R][H] bound to slots [R] -> y [R][H] f16."""
         R = rows.shape[0]
         if y_out is None:
-            y_out = torch.empty(R, self.H, dtype=torch.float32, device=rows.device)
+            y_out = torch.empty(R, self.H, dtype=torch.float16, device=rows.device)
         self._check(lib().hoard_moe_ep_experts(self._h, layer, _ptr(rows), _ptr(slot_of_row), R, _ptr(y_out),
                                                _stream(stream)), "ep_experts")
         return y_out

@@ -182,8 +182,8 @@ int hoard_moe_set_gemm_min_tokens(hoard_moe_ctx* ctx, int min_tokens);
  * Per layer: hoard_moe_route -> hoard_moe_ep_pack -> all-to-all of send_counts, then of send_rows and
  * send_expert (rows for rank r are the r-th run of send_counts) -> hoard_moe_ep_experts on the
  * received rows -> all-to-all of y back (the reverse splits) -> hoard_moe_ep_combine. The exchange is
- * the caller's (NCCL / torch.distributed); every row is computed independently and y returns in f32,
- * so G ranks reproduce the single-rank result bit for bit. */
+ * the caller's (NCCL / torch.distributed); every row is computed independently and y travels in the
+ * same f16 form the single-rank tensor-core path stores, so G ranks reproduce it bit for bit. */
 
 /* Reserves the receive-side scratch for up to max_rows rows per hoard_moe_ep_experts call. */
 int hoard_moe_ep_reserve(hoard_moe_ctx* ctx, int64_t max_rows);
@@ -199,14 +199,14 @@ int hoard_moe_ep_pack(hoard_moe_ctx* ctx, int layer, const int32_t* sel, int T, 
                       uint16_t* send_rows, hoard_stream stream);
 
 /* Receive side: expert FFN (gate/up, SwiGLU, Q8_K of h, down) of R received rows (f16 [R][n_embd])
- * bound to this context's pool slots slot_of_row [R], into y_out [R][n_embd] f32 (device pointers).
- * R <= the reserved max_rows. */
+ * bound to this context's pool slots slot_of_row [R], into y_out [R][n_embd] f16 bits (device
+ * pointers; values clamped to the f16 range). R <= the reserved max_rows. */
 int hoard_moe_ep_experts(hoard_moe_ctx* ctx, int layer, const uint16_t* rows, const int32_t* slot_of_row, int R,
-                         float* y_out, hoard_stream stream);
+                         uint16_t* y_out, hoard_stream stream);
 
 /* Send side: x[t] += sum_j w[t][j] * y_back[pos_of_entry[t*k+j]] (j ascending, the combine of
- * src/run_moe_stream.cpp:447), y_back [T*k][n_embd] f32 in send order. */
-int hoard_moe_ep_combine(hoard_moe_ctx* ctx, const float* w, const int32_t* pos_of_entry, const float* y_back,
+ * src/run_moe_stream.cpp:447), y_back [T*k][n_embd] f16 bits in send order. */
+int hoard_moe_ep_combine(hoard_moe_ctx* ctx, const float* w, const int32_t* pos_of_entry, const uint16_t* y_back,
                          void* x_inout, int T, hoard_stream stream);
 
 /* Last error message of this context (CUDA error string or argument check). */

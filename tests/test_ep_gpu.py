@@ -1,7 +1,8 @@
 """Expert parallelism on the GPU through the C ABI (hoard_moe_ep_pack / _experts / _combine).
 
-Every row's arithmetic is independent of the rows it shares a tile with and the outputs travel in f32,
-so the expert-parallel layer must equal the single-rank tensor-core layer bit for bit:
+Every row's arithmetic is independent of the rows it shares a tile with and the outputs travel in the
+same f16 form the single-rank path stores, so the expert-parallel layer must equal the single-rank
+tensor-core layer bit for bit:
   * one rank over a real NCCL process group (all-to-all of one rank);
   * four destination ranks emulated in one process (each destination's rows through ep_experts
     separately), which exercises the pack's partition on one GPU;
@@ -84,7 +85,7 @@ def test_emulated_ranks_equal_local_layer(layer_ctx, G):
     sel, w = ctx.route(0, x)
     counts, pos, expert, rows = ctx.ep_pack(0, sel, G, SPEC.E // G)
     c = counts.cpu().tolist()
-    y_back = torch.empty(T * SPEC.k, SPEC.H, device=x.device)
+    y_back = torch.empty(T * SPEC.k, SPEC.H, dtype=torch.float16, device=x.device)
     off = 0
     for r in range(G):             # destination r's rows through its own ep_experts call
         if c[r]:
