@@ -262,14 +262,15 @@ def layer_flops(T: int) -> float:
     return 2.0 * T * K_USED * 3 * H * I
 
 
-def measure_prefill(ctx, device, stream, dist):
+def measure_prefill(ctx, device, stream, dist, rank=0, world=1):
     """Batched tokens through the tensor-core expert path: the 48-layer stack at T = PREFILL_T tokens per
-    call (prefill tok/s) and the isolated layer 0 (Q6_K down) at the C2 token counts. Inputs are seeded
-    RMS-normalised rows resident in HBM; every call streams all experts' weights of a layer (391 MB >
-    126 MB L2), so no flush is needed between calls."""
+    call and rank (prefill tok/s; with world > 1 expert-parallel: experts [g*E/G, (g+1)*E/G) computed on
+    rank g, tokens exchanged by NCCL all-to-all, weak scaling) and the isolated layer 0 (Q6_K down) at
+    the C2 token counts. Inputs are seeded RMS-normalised rows resident in HBM, distinct per rank; every
+    call streams all experts' weights of a layer (391 MB > 126 MB L2), so no flush is needed."""
     import torch
     g = torch.Generator(device=device)
-    g.manual_seed(SEED + 4096)
+    g.manual_seed(SEED + 4096 + 7 * rank)
     x0 = torch.randn(PREFILL_T, H, generator=g, device=device)
     x0 = x0 / torch.sqrt((x0 * x0).mean(-1, keepdim=True) + 1e-6)
     try:
@@ -298,7 +299,14 @@ def measure_prefill(ctx, device, stream, dist):
         return ms
 
     x = x0.clone()
-    ms = timed(lambda: ctx.layers(0, N_LAYER, x), reps=5, warm=2)
+    ep = None
+    if world > 1:
+        from hoard_b200.ep import ExpertParallel
+        ep = ExpertParallel(ctx, experts_per_rank=E // world, slot_base=rank * (E // world),
+                            max_rows=PREFILL_T * K_USED * world)
+        ms = timed(lambda: ep.layers(0, N_LAYER, x), reps=5, warm=2)
+    else:
+        ms = timed(lambda: ctx.layers(0, N_LAYER, x), reps=5, warm=2)
     ctx.sync_status()
     sweep = []
     for T in C2_TS:
@@ -307,12 +315,21 @@ def measure_prefill(ctx, device, stream, dist):
         sweep.append({"T": T, "us_per_layer": round(ms_l * 1e3, 1), "tok_s": round(T / ms_l * 1e3, 1),
                       "expert_tflops": round(layer_flops(T) / (ms_l * 1e-3) / 1e12, 1)})
     ctx.sync_status()
-    achieved = layer_flops(PREFILL_T) * N_LAYER / (ms * 1e-3) / 1e12
-    return {"metric": f"prefill tok/s ({N_LAYER} MoE layers, {PREFILL_T} tokens per call)",
+    achieved = layer_flops(PREFILL_T) * N_LAYER / (ms * 1e-3) / 1e12    # per GPU
+    traffic = None
+    try:
+        traffic = json.load(open(os.path.join(ROOT, "profiles", "traffic.json"))).get("prefill_gateup_T4096_bytes")
+    except Exception:
+        pass
+    return {"metric": f"prefill tok/s ({N_LAYER} MoE layers, {PREFILL_T} tokens per call and GPU)",
             "value": PREFILL_T / ms * 1e3, "unit": "tok/s", "ms_per_step": round(ms, 3),
+            "parallelism": f"ep{world} (NCCL all-to-all dispatch/combine)" if world > 1 else "single GPU",
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": tpeak, "unit": "TFLOP/s",
                          "frac": round(achieved / tpeak, 4), "peak_source": tsrc,
-                         "flops": "expert FFN only: 2*T*k*3*H*I per layer (router, dispatch, combine excluded)"},
+                         "flops": "expert FFN only: 2*T*k*3*H*I per layer (router, dispatch, combine excluded)",
+                         "timing": "whole prefill step (all kernels of 48 layers), not the GEMM alone",
+                         "traffic": traffic,
+                         "traffic_kernel": "k_tc_experts<0> (gate/up GEMM), DRAM bytes per launch at T=4096"},
             "c2_layer": sweep}
 
 
@@ -410,7 +427,7 @@ def run_gpu(args, rank, world, local_rank):
 
     prefill = None
     if not args.no_prefill:
-        prefill = measure_prefill(ctx, device, stream, dist)
+        prefill = measure_prefill(ctx, device, stream, dist, rank, world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -455,7 +472,7 @@ def run_gpu(args, rank, world, local_rank):
             "clocks": dict(clk.summary(), window="0.5 s of the same decode steps, then the timed steps"),
         }
         if prefill:
-            prefill["value"] = round(prefill["value"] * world, 1)   # replicas: whole-job tokens/s
+            prefill["value"] = round(prefill["value"] * world, 1)   # whole job: every rank's tokens
             line["prefill"] = prefill
         if cpu:
             line["cpu_baseline"] = cpu
