@@ -6,6 +6,7 @@
 
 #include <cuda_runtime.h>
 #include <algorithm>
+#include <array>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -54,6 +55,21 @@ struct hoard_moe_ctx {
     bool decode_ok = false;            // the persistent decode kernel supports these shapes / types
     unsigned long long* trace = nullptr;
     int64_t trace_cap = 0;
+    // residency: per-layer LRU slot pool over a host RAM tier (hoard_moe_ram_tier / hoard_moe_ensure)
+    struct Residency {
+        bool init = false;
+        std::vector<std::array<const void*, 3>> host;   // [layer*E + expert] gate, up, down host bytes
+        std::vector<int> slot_of_expert;                // [layer*E + expert] -> slot or -1
+        std::vector<int> expert_of_slot;                // [layer*S + slot] -> expert or -1
+        std::vector<uint64_t> last_use;                 // [layer*S + slot] LRU clock
+        std::vector<cudaEvent_t> ready;                 // [layer*S + slot] upload of the slot's expert done
+        std::vector<char> pending;                      // [layer*S + slot] ready not yet seen complete
+        std::vector<cudaEvent_t> used;                  // [layer] last hoard_moe_experts of the layer done
+        std::vector<char> used_valid;
+        cudaStream_t upload = nullptr;
+        uint64_t clock = 0;
+        int64_t hits = 0, misses = 0, bytes = 0;
+    } res;
     // expert-parallel receive side (hoard_moe_ep_reserve): dispatch + h scratch for up to ep_rows rows
     int64_t ep_rows = 0;
     Scratch ep{};
@@ -272,6 +288,9 @@ int hoard_moe_destroy(hoard_moe_ctx* c) {
     cudaDeviceSynchronize();
     for (void* p : c->allocations) cudaFree(p);
     if (c->staging_free) cudaEventDestroy(c->staging_free);
+    for (cudaEvent_t ev : c->res.ready) if (ev) cudaEventDestroy(ev);
+    for (cudaEvent_t ev : c->res.used) if (ev) cudaEventDestroy(ev);
+    if (c->res.upload) cudaStreamDestroy(c->res.upload);
     delete c;
     return HOARD_OK;
 }
@@ -389,6 +408,124 @@ int hoard_moe_experts(hoard_moe_ctx* c, int layer, const float* fx, const int32_
         HCHECK(c, launch_experts_grouped(c->dims, lw, c->sc, fx, slots, w, x_inout, T, true, (cudaStream_t)stream,
                                          &nl));
     c->launches += nl;
+    if (c->res.init) {            // the residency layer must not overwrite these slots before this call ran
+        HCHECK(c, cudaEventRecord(c->res.used[layer], (cudaStream_t)stream));
+        c->res.used_valid[layer] = 1;
+    }
+    return HOARD_OK;
+}
+
+static int res_init(hoard_moe_ctx* c) {
+    auto& r = c->res;
+    if (r.init) return HOARD_OK;
+    const int L = c->desc.n_layer, E = c->dims.E, S = c->desc.n_slots;
+    r.host.assign((size_t)L * E, {nullptr, nullptr, nullptr});
+    r.slot_of_expert.assign((size_t)L * E, -1);
+    r.expert_of_slot.assign((size_t)L * S, -1);
+    r.last_use.assign((size_t)L * S, 0);
+    r.pending.assign((size_t)L * S, 0);
+    r.ready.assign((size_t)L * S, nullptr);
+    r.used.assign((size_t)L, nullptr);
+    r.used_valid.assign((size_t)L, 0);
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    for (auto& ev : r.ready) HCHECK(c, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    for (auto& ev : r.used) HCHECK(c, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    HCHECK(c, cudaStreamCreateWithFlags(&r.upload, cudaStreamNonBlocking));
+    r.init = true;
+    return HOARD_OK;
+}
+
+int hoard_moe_ram_tier(hoard_moe_ctx* c, int layer, int expert, const void* gate, const void* up, const void* down) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (expert < 0 || expert >= c->dims.E) return fail(c, HOARD_EINVAL, "expert out of range");
+    if (!gate || !up || !down) return fail(c, HOARD_EINVAL, "null expert pointer");
+    if ((rc = res_init(c))) return rc;
+    c->res.host[(size_t)layer * c->dims.E + expert] = {gate, up, down};
+    return HOARD_OK;
+}
+
+int hoard_moe_ensure(hoard_moe_ctx* c, int layer, const int32_t* sel, int n, int32_t* slot_of_sel,
+                     hoard_stream stream) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (!sel || !slot_of_sel || n <= 0) return fail(c, HOARD_EINVAL, "null pointer or n <= 0");
+    if ((rc = res_init(c))) return rc;
+    auto& r = c->res;
+    const int E = c->dims.E, S = c->desc.n_slots;
+    LayerStore& Ls = c->layers[layer];
+    int* slot_of = &r.slot_of_expert[(size_t)layer * E];
+    int* expert_of = &r.expert_of_slot[(size_t)layer * S];
+    uint64_t* last = &r.last_use[(size_t)layer * S];
+    for (int i = 0; i < n; ++i)
+        if (sel[i] < 0 || sel[i] >= E) return fail(c, HOARD_EINVAL, "expert id out of range");
+    // this call's slots are protected from eviction: stamp every hit first
+    const uint64_t stamp = ++r.clock;
+    for (int i = 0; i < n; ++i) {
+        const int s = slot_of[sel[i]];
+        if (s >= 0) last[s] = stamp;
+    }
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    for (int i = 0; i < n; ++i) {
+        const int e = sel[i];
+        int s = slot_of[e];
+        if (s >= 0) {
+            ++r.hits;
+        } else {
+            // miss: the least recently used slot that this call does not use (empty slots first)
+            int victim = -1;
+            for (int t = 0; t < S; ++t) {
+                if (last[t] == stamp) continue;
+                if (victim < 0 || (expert_of[t] < 0 && expert_of[victim] >= 0) ||
+                    ((expert_of[t] < 0) == (expert_of[victim] < 0) && last[t] < last[victim]))
+                    victim = t;
+            }
+            if (victim < 0) return fail(c, HOARD_EINVAL, "one call selects more experts than n_slots");
+            const auto& h = r.host[(size_t)layer * E + e];
+            if (!h[0]) return fail(c, HOARD_ESTATE, "selected expert is not in the RAM tier");
+            if (expert_of[victim] >= 0) slot_of[expert_of[victim]] = -1;
+            // the previous compute call of this layer may still read the victim slot
+            if (r.used_valid[layer]) HCHECK(c, cudaStreamWaitEvent(r.upload, r.used[layer], 0));
+            const int types[3] = {Ls.gt, Ls.ut, Ls.dt};
+            const int64_t offs[3] = {0, Ls.off_up, Ls.off_down};
+            const int64_t bytes[3] = {Ls.gate_bytes, Ls.up_bytes, Ls.down_bytes};
+            const int64_t rows[3] = {c->dims.I, c->dims.I, c->dims.H};
+            const void* const src[3] = {h[0], h[1], h[2]};
+            if ((rc = upload3(c, Ls.pool + (int64_t)victim * Ls.slot_stride, types, offs, bytes, rows, src, r.upload)))
+                return rc;
+            const size_t ri = (size_t)layer * S + victim;
+            HCHECK(c, cudaEventRecord(r.ready[ri], r.upload));
+            r.pending[ri] = 1;
+            expert_of[victim] = e;
+            slot_of[e] = victim;
+            s = victim;
+            ++r.misses;
+            r.bytes += Ls.gate_bytes + Ls.up_bytes + Ls.down_bytes;
+        }
+        last[s] = stamp;
+        slot_of_sel[i] = s;
+    }
+    // the compute stream waits only for uploads of the slots this call uses that may still be running
+    for (int i = 0; i < n; ++i) {
+        const size_t ri = (size_t)layer * S + slot_of_sel[i];
+        if (!r.pending[ri]) continue;
+        const cudaError_t q = cudaEventQuery(r.ready[ri]);
+        if (q == cudaSuccess) {
+            r.pending[ri] = 0;
+        } else if (q == cudaErrorNotReady) {
+            HCHECK(c, cudaStreamWaitEvent((cudaStream_t)stream, r.ready[ri], 0));
+        } else {
+            return cuda_fail(c, q, "upload event");
+        }
+    }
+    return HOARD_OK;
+}
+
+int hoard_moe_residency_stats(const hoard_moe_ctx* c, int64_t* hits, int64_t* misses, int64_t* bytes_uploaded) {
+    if (!c || !hits || !misses || !bytes_uploaded) return HOARD_EINVAL;
+    *hits = c->res.hits;
+    *misses = c->res.misses;
+    *bytes_uploaded = c->res.bytes;
     return HOARD_OK;
 }
 

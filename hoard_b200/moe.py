@@ -35,7 +35,8 @@ EXPORTED = [
     "hoard_moe_sync_status", "hoard_moe_expert_bytes", "hoard_moe_launch_count", "hoard_moe_set_decode_impl",
     "hoard_moe_set_trace", "hoard_moe_trace_layout", "hoard_moe_decode_noalloc",
     "hoard_moe_set_gemm_min_tokens", "hoard_moe_ep_reserve", "hoard_moe_ep_pack", "hoard_moe_ep_experts",
-    "hoard_moe_ep_combine", "hoard_moe_last_error", "hoard_strerror",
+    "hoard_moe_ep_combine", "hoard_moe_ram_tier", "hoard_moe_ensure", "hoard_moe_residency_stats",
+    "hoard_moe_last_error", "hoard_strerror",
 ]
 
 
@@ -84,6 +85,9 @@ def lib() -> ctypes.CDLL:
         L.hoard_moe_launch_count.restype = i64
         L.hoard_moe_set_decode_impl.argtypes = [vp, i32]
         L.hoard_moe_set_gemm_min_tokens.argtypes = [vp, i32]
+        L.hoard_moe_ram_tier.argtypes = [vp, i32, i32, vp, vp, vp]
+        L.hoard_moe_ensure.argtypes = [vp, i32, vp, i32, vp, vp]
+        L.hoard_moe_residency_stats.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64), ctypes.POINTER(i64)]
         L.hoard_moe_ep_reserve.argtypes = [vp, i64]
         L.hoard_moe_ep_pack.argtypes = [vp, i32, vp, i32, i32, i32, vp, vp, vp, vp, vp]
         L.hoard_moe_ep_experts.argtypes = [vp, i32, vp, vp, i32, vp, vp]
@@ -168,6 +172,26 @@ class MoEContext:
 
     def set_decode_impl(self, impl: int):
         self._check(lib().hoard_moe_set_decode_impl(self._h, impl), "set_decode_impl")
+
+    # ---- residency: LRU slot pool over a host RAM tier ----
+    def ram_tier(self, layer: int, expert: int, gate, up, down):
+        """Registers host copies (raw GGUF bytes: CPU tensors, ideally pinned; kept alive by the caller)."""
+        self._check(lib().hoard_moe_ram_tier(self._h, layer, expert, _ptr(gate), _ptr(up), _ptr(down)), "ram_tier")
+
+    def ensure(self, layer: int, sel, stream=None):
+        """Slots for the expert ids in sel (host int32 array); misses are uploaded from the RAM tier."""
+        import numpy as np
+        sel_h = np.ascontiguousarray(np.asarray(sel, dtype=np.int32).reshape(-1))
+        out = np.empty_like(sel_h)
+        self._check(lib().hoard_moe_ensure(self._h, layer, sel_h.ctypes.data, sel_h.size, out.ctypes.data,
+                                           _stream(stream)), "ensure")
+        return out
+
+    def residency_stats(self):
+        h, m, b = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+        self._check(lib().hoard_moe_residency_stats(self._h, ctypes.byref(h), ctypes.byref(m), ctypes.byref(b)),
+                    "residency_stats")
+        return {"hits": h.value, "misses": m.value, "bytes_uploaded": b.value}
 
     # ---- expert parallelism (the exchange between these calls is the caller's; see hoard_b200.ep) ----
     def ep_reserve(self, max_rows: int):

@@ -176,6 +176,30 @@ int hoard_moe_set_decode_impl(hoard_moe_ctx* ctx, int impl);
  * its graph picks the backend's matmul kernel by batch size. */
 int hoard_moe_set_gemm_min_tokens(hoard_moe_ctx* ctx, int min_tokens);
 
+/* ---- Residency: per-layer LRU slot pool over a host RAM tier --------------------------------------
+ * Replaces hoard's to_vram / fetch and its per-layer LRU (src/run_moe_stream.cpp:279-284, :380-421;
+ * the `ensure` of src/run_specloop.cpp:123) when n_slots < n_expert. Uploads run on the context's own
+ * upload stream (raw GGUF bytes H2D, re-laid into the slot); the compute stream waits only for the
+ * uploads of the slots a call uses, and a slot is overwritten only after the last hoard_moe_experts
+ * call of its layer that may read it. */
+
+/* Registers the host copy (raw GGUF bytes, as hoard_moe_upload_expert takes them) of one expert. The
+ * caller keeps the memory alive; page-locked memory makes the uploads asynchronous. */
+int hoard_moe_ram_tier(hoard_moe_ctx* ctx, int layer, int expert, const void* gate, const void* up,
+                       const void* down);
+
+/* For n selected expert ids (host array, e.g. the routed sel of one token), returns their pool slots in
+ * slot_of_sel (host array), uploading misses from the RAM tier into least-recently-used slots that this
+ * call does not use, and makes `stream` wait for those uploads. Pass the slots (copied to the device)
+ * to hoard_moe_experts on the same stream. HOARD_EINVAL if one call needs more slots than n_slots,
+ * HOARD_ESTATE if a selected expert was never registered with hoard_moe_ram_tier. */
+int hoard_moe_ensure(hoard_moe_ctx* ctx, int layer, const int32_t* sel, int n, int32_t* slot_of_sel,
+                     hoard_stream stream);
+
+/* Lookups that hit / missed and raw bytes uploaded by hoard_moe_ensure since creation (hoard's
+ * 3-tier metrics, src/run_moe_stream.cpp:539-543). */
+int hoard_moe_residency_stats(const hoard_moe_ctx* ctx, int64_t* hits, int64_t* misses, int64_t* bytes_uploaded);
+
 /* ---- Expert parallelism (batched tokens over G ranks, experts [g*E/G, (g+1)*E/G) on rank g) ----
  * The sharded counterpart of the single-process mul_mat_id of src/run_specloop.cpp:125-140, which
  * hoard runs on one GPU only. One context per rank; its pool holds at least the rank's own experts.
