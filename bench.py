@@ -333,6 +333,74 @@ def measure_prefill(ctx, device, stream, dist, rank=0, world=1):
             "c2_layer": sweep}
 
 
+LRU_SLOTS = 32       # C3 run (ii): K = 32 slots per layer
+LRU_TOKENS = 8
+
+
+def measure_lru(device, stream, n_layer: int):
+    """C3 run (ii): batch-1 decode through a K = 32 per-layer LRU slot pool backed by a pinned-host RAM
+    tier, hoard's own schedule: per layer route (T = 1) -> host readback of the 8 expert ids ->
+    hoard_moe_ensure (misses uploaded on the library's upload stream) -> experts on the slots. The RAM
+    tier holds layer 0's 128 experts (392 MB pinned) and serves every layer (same bytes, same traffic
+    as distinct layers); routers are the benchmark model's. Timed with CUDA events around whole
+    tokens (host round trips included)."""
+    import numpy as np
+    import torch
+    from hoard_b200 import moe, quant
+    ctx = moe.MoEContext(n_embd=H, n_expert=E, n_expert_used=K_USED, n_ff=I, n_layer=n_layer, n_slots=LRU_SLOTS,
+                         norm_topk=True, eps=1e-6, resid_dtype=torch.float32, gate_types=[Q4_K] * n_layer,
+                         up_types=[Q4_K] * n_layer, down_types=[down_type(layer) for layer in range(n_layer)],
+                         max_tokens=1, device=device.index)
+    ctx.set_decode_impl(0)
+    ctx.set_gemm_min_tokens(0)
+    g = torch.Generator(device=device)
+    host = {}
+    for dt in sorted(set(down_type(layer) for layer in range(n_layer))):
+        g.manual_seed(SEED + 31 * dt)
+        gate = quant.quantize_q4k(torch.randn(E, I, H, generator=g, device=device) * 0.02).cpu().pin_memory()
+        up = quant.quantize_q4k(torch.randn(E, I, H, generator=g, device=device) * 0.02).cpu().pin_memory()
+        down = quant.quantize(torch.randn(E, H, I, generator=g, device=device) * 0.02, dt).cpu().pin_memory()
+        host[dt] = (gate, up, down)
+    for layer in range(n_layer):
+        g.manual_seed(SEED + 7919 * layer)
+        ctx.set_router(layer, torch.randn(E, H, generator=g, device=device) * 0.02,
+                       1.0 + 0.1 * torch.randn(H, generator=g, device=device))
+        gate, up, down = host[down_type(layer)]
+        for e in range(E):
+            ctx.ram_tier(layer, e, gate[e], up[e], down[e])
+    xs = token_rows(LRU_TOKENS + 2, device)
+    slot_dev = torch.empty(K_USED, dtype=torch.int32, device=device)
+
+    def token(x):
+        for layer in range(n_layer):
+            sel, w = ctx.route(layer, x)
+            slots = ctx.ensure(layer, sel.cpu().numpy())
+            slot_dev.copy_(torch.from_numpy(slots), non_blocking=False)
+            ctx.experts(layer, sel, w, x, slot_of_sel=slot_dev)
+
+    for i in range(2):                                   # warm-up: fills the pool
+        token(xs[LRU_TOKENS + i].clone())
+    torch.cuda.synchronize(device)
+    st0 = ctx.residency_stats()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(LRU_TOKENS):
+        token(xs[i].clone())
+    b.record(stream)
+    torch.cuda.synchronize(device)
+    ms = a.elapsed_time(b)
+    ctx.sync_status()
+    st = ctx.residency_stats()
+    hits, misses = st["hits"] - st0["hits"], st["misses"] - st0["misses"]
+    up_bytes = st["bytes_uploaded"] - st0["bytes_uploaded"]
+    ctx.close()
+    return {"metric": f"decode tok/s b=1, {LRU_SLOTS}-slot LRU per layer + pinned-host RAM tier ({n_layer} layers)",
+            "value": round(LRU_TOKENS / (ms * 1e-3), 3), "unit": "tok/s", "tokens": LRU_TOKENS,
+            "hit_rate": round(hits / max(1, hits + misses), 4), "misses_per_token": round(misses / LRU_TOKENS, 1),
+            "h2d_gbs": round(up_bytes / (ms * 1e-3) / 1e9, 2),
+            "note": "uniform random routing on random weights: the hit rate is the pool's share of experts"}
+
+
 def run_gpu(args, rank, world, local_rank):
     import torch
     from hoard_b200 import moe
@@ -429,6 +497,10 @@ def run_gpu(args, rank, world, local_rank):
     if not args.no_prefill:
         prefill = measure_prefill(ctx, device, stream, dist, rank, world)
 
+    lru = None
+    if not args.no_lru and rank == 0 and world == 1:
+        lru = measure_lru(device, stream, N_LAYER)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle as orc
@@ -473,6 +545,8 @@ def run_gpu(args, rank, world, local_rank):
         }
         if prefill:
             prefill["value"] = round(prefill["value"] * world, 1)   # whole job: every rank's tokens
+        if lru:
+            line["lru_decode"] = lru
             line["prefill"] = prefill
         if cpu:
             line["cpu_baseline"] = cpu
@@ -497,6 +571,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--trace", action="store_true", help="add the persistent kernel's per-phase breakdown")
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-token (prefill) measurements")
+    ap.add_argument("--no-lru", action="store_true", help="skip the LRU slot pool + RAM tier decode measurement")
     ap.add_argument("--layers", type=int, default=N_LAYER, help="MoE layers per step (48 = the full stack; "
                     "fewer only for small profiling captures)")
     args = ap.parse_args()
