@@ -262,7 +262,7 @@ def layer_flops(T: int) -> float:
     return 2.0 * T * K_USED * 3 * H * I
 
 
-def measure_prefill(ctx, device, stream, dist, rank=0, world=1):
+def measure_prefill(ctx, device, stream, dist, rank=0, world=1, ep_chunks=1, ep_gemm_ctas=0, ep_transport="p2p"):
     """Batched tokens through the tensor-core expert path: the 48-layer stack at T = PREFILL_T tokens per
     call and rank (prefill tok/s; with world > 1 expert-parallel: experts [g*E/G, (g+1)*E/G) computed on
     rank g, tokens exchanged by NCCL all-to-all, weak scaling) and the isolated layer 0 (Q6_K down) at
@@ -303,8 +303,11 @@ def measure_prefill(ctx, device, stream, dist, rank=0, world=1):
     if world > 1:
         from hoard_b200.ep import ExpertParallel
         ep = ExpertParallel(ctx, experts_per_rank=E // world, slot_base=rank * (E // world),
-                            max_rows=PREFILL_T * K_USED * world)
+                            max_rows=PREFILL_T * K_USED * world, chunks=ep_chunks, transport=ep_transport)
+        ctx.set_gemm_ctas(ep_gemm_ctas if ep_chunks > 1 and ep_transport == "nccl" else 0)
         ms = timed(lambda: ep.layers(0, N_LAYER, x), reps=5, warm=2)
+        ctx.set_gemm_ctas(0)
+        ep.close()
     else:
         ms = timed(lambda: ctx.layers(0, N_LAYER, x), reps=5, warm=2)
     ctx.sync_status()
@@ -323,7 +326,11 @@ def measure_prefill(ctx, device, stream, dist, rank=0, world=1):
         pass
     return {"metric": f"prefill tok/s ({N_LAYER} MoE layers, {PREFILL_T} tokens per call and GPU)",
             "value": PREFILL_T / ms * 1e3, "unit": "tok/s", "ms_per_step": round(ms, 3),
-            "parallelism": f"ep{world} (NCCL all-to-all dispatch/combine)" if world > 1 else "single GPU",
+            "parallelism": (("ep{} (dispatch/combine by the library's kernels over NVLink peer memory)".format(world)
+                             if ep_transport == "p2p" else
+                             f"ep{world} (NCCL all-to-all dispatch/combine, {ep_chunks} micro-batches"
+                             f"{f', GEMMs on {ep_gemm_ctas} CTAs' if ep_chunks > 1 and ep_gemm_ctas else ''})")
+                            if world > 1 else "single GPU"),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": tpeak, "unit": "TFLOP/s",
                          "frac": round(achieved / tpeak, 4), "peak_source": tsrc,
                          "flops": "expert FFN only: 2*T*k*3*H*I per layer (router, dispatch, combine excluded)",
@@ -495,7 +502,8 @@ def run_gpu(args, rank, world, local_rank):
 
     prefill = None
     if not args.no_prefill:
-        prefill = measure_prefill(ctx, device, stream, dist, rank, world)
+        prefill = measure_prefill(ctx, device, stream, dist, rank, world, args.ep_chunks, args.ep_gemm_ctas,
+                                  args.ep_transport)
 
     lru = None
     if not args.no_lru and rank == 0 and world == 1:
@@ -572,6 +580,12 @@ def main():
     ap.add_argument("--trace", action="store_true", help="add the persistent kernel's per-phase breakdown")
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-token (prefill) measurements")
     ap.add_argument("--no-lru", action="store_true", help="skip the LRU slot pool + RAM tier decode measurement")
+    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
+                    help="expert-parallel prefill exchange: the library's peer-memory kernels or NCCL all-to-all")
+    ap.add_argument("--ep-chunks", type=int, default=2, help="expert-parallel prefill: micro-batches per layer "
+                    "whose all-to-alls overlap the other micro-batches' GEMMs")
+    ap.add_argument("--ep-gemm-ctas", type=int, default=132, help="expert-parallel prefill with micro-batches: "
+                    "CTAs of the tensor-core GEMMs (the remaining SMs run NCCL's kernels)")
     ap.add_argument("--layers", type=int, default=N_LAYER, help="MoE layers per step (48 = the full stack; "
                     "fewer only for small profiling captures)")
     args = ap.parse_args()

@@ -31,6 +31,7 @@ struct Dims {
     int renorm;
     float eps;
     int resid_bf16;
+    int gemm_ctas;    // CTAs of the tensor-core GEMMs (0 = one per SM); fewer leave SMs to concurrent kernels
 };
 
 // Scratch owned by a context (device pointers), sized for max_tokens.
@@ -80,9 +81,11 @@ cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const 
 
 // Pieces shared by the grouped and tensor-core expert paths.
 cudaError_t launch_shared_gate(const float* fx, const float* gate_inp, int H, int T, float* out, cudaStream_t s);
-// Counting sort of the entries by slot; with tile_m > 0 also the (slot, M tile) work list.
+// Counting sort of the entries by slot; with tile_m > 0 also the (slot, M tile) work list. Slots out
+// of range set error bit 1 and are skipped; with skip_neg, negative slots are skipped silently (the
+// unused rows of the expert-parallel receive regions).
 cudaError_t launch_dispatch(const int32_t* slot_of_sel, int T, int k, int KK, int n_slots, const Scratch& sc,
-                            int tile_m, cudaStream_t s, int* launches);
+                            int tile_m, cudaStream_t s, int* launches, bool skip_neg = false);
 // y_half: sc.y holds f16 rows (tensor-core path) instead of f32 rows (grouped path)
 cudaError_t launch_combine(const Dims& d, const Scratch& sc, const float* w, void* x_inout, int T, int KK,
                            cudaStream_t s, bool y_half);
@@ -106,6 +109,43 @@ cudaError_t launch_q8_rows(const float* fx, int T, int H, uint16_t* out, cudaStr
 cudaError_t launch_ep_pack(const int32_t* sel, int T, int k, int n_ranks, int experts_per_rank, const uint16_t* xq,
                            int H, int* counts, int* cursor, int* pos_of_entry, int32_t* send_expert,
                            uint16_t* send_rows, unsigned* err, cudaStream_t s, int* launches);
+
+// ---- expert parallelism over NVLink peer memory ----
+// Every rank allocates one block with this layout (identical on all ranks, so a peer's field is its
+// base + the same offset); peers map it (CUDA IPC) and write into it directly.
+//   flags[64]   u32  barrier epochs, flags[s] written by rank s
+//   count[64]   i32  count[s]: rows rank s sent here this layer
+//   start[64]   i32  start[s]: where those rows begin in rank s's send order
+//   expert      i32  [G][cap] expert id of each received row, region s written by rank s
+//   rows        f16  [G][cap][H] received Q8_K-dequantised activation rows, region s written by rank s
+//   yback       f16  [cap][H] expert outputs of this rank's own entries, in its send order, written by
+//                    the ranks that computed them
+struct P2PLayout {
+    int64_t flags, count, start, expert, rows, yback, bytes;
+};
+P2PLayout p2p_layout(int G, int cap, int H);
+
+struct P2PSend {
+    uint8_t* const* peer;    // device [G] block base of every rank (own included)
+    P2PLayout L;
+    int G, rank, cap, H, epr;
+};
+// Send side of one layer: entries counted by destination rank, their starts and counts written into
+// every destination's count/start[rank], pos_of_entry[e] = the entry's send position, and each
+// entry's expert id and f16 row written straight into the destination's region `rank`.
+cudaError_t launch_p2p_send(const P2PSend& p, const int32_t* sel, int T, int k, const uint16_t* xq, int* counts,
+                            int* cursor, int* start, int* pos_of_entry, unsigned* err, cudaStream_t s, int* launches);
+// Barrier halves: signal writes `epoch` into every rank's flags[rank] (system-scope release after a
+// system fence); wait spins (bounded by timeout_ns, then error bit 2) until every flags[s] >= epoch.
+// A wait returns at once when bit 2 is already set.
+cudaError_t launch_p2p_signal(const P2PSend& p, uint32_t epoch, cudaStream_t s);
+cudaError_t launch_p2p_wait(const uint8_t* block, const P2PLayout& L, int G, uint32_t epoch,
+                            unsigned long long timeout_ns, unsigned* err, cudaStream_t s);
+// Receive side: slot of every region row (-1 for the unused tail of a region, and for every row when
+// error bit 2 is set), then the tensor-core FFN whose down epilogue stores y of region row (s, i)
+// into rank s's yback[start[s] + i].
+cudaError_t launch_p2p_experts(const Dims& d, const LayerWeights& lw, const Scratch& sc, const P2PSend& p,
+                               const uint8_t* block, int slot_base, int* slots, cudaStream_t s, int* launches);
 
 // Persistent fused decode kernel over n_layers layers (T <= decode_max_tokens()).
 int decode_max_tokens();

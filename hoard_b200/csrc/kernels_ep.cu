@@ -81,7 +81,145 @@ __global__ void __launch_bounds__(256) k_ep_gather(const uint16_t* __restrict__ 
     for (int i = lane; i < H / 8; i += 32) dst[i] = src[i];
 }
 
+// ---- over NVLink peer memory ----
+
+// Exclusive prefix of the per-destination counts (this rank's send order), and both written into
+// every destination's count[rank] / start[rank].
+__global__ void k_p2p_meta(P2PSend p, const int* __restrict__ counts, int* __restrict__ cursor,
+                           int* __restrict__ start) {
+    if (threadIdx.x != 0) return;
+    int acc = 0;
+    for (int g = 0; g < p.G; ++g) {
+        const int c = counts[g];
+        cursor[g] = acc;
+        start[g] = acc;
+        reinterpret_cast<int*>(p.peer[g] + p.L.count)[p.rank] = c;
+        reinterpret_cast<int*>(p.peer[g] + p.L.start)[p.rank] = acc;
+        acc += c;
+    }
+}
+
+// Send positions (warp-aggregated cursors, as k_ep_scatter) and each entry's expert id into its
+// destination's region `rank`.
+__global__ void __launch_bounds__(256) k_p2p_scatter(P2PSend p, const int32_t* __restrict__ sel, int n,
+                                                     int* __restrict__ cursor, const int* __restrict__ start,
+                                                     int* __restrict__ pos_of_entry) {
+    const int lane = threadIdx.x & 31;
+    const int e0 = blockIdx.x * EP_CHUNK, e1 = min(n, e0 + EP_CHUNK);
+    for (int base = e0; base < e1; base += blockDim.x) {
+        const int e = base + threadIdx.x;
+        int dest = -1, ex = -1;
+        if (e < e1) {
+            ex = sel[e];
+            dest = (ex < 0 || ex >= p.G * p.epr) ? -1 : ex / p.epr;
+        }
+        const unsigned peers = __match_any_sync(0xFFFFFFFFu, dest);
+        const int leader = __ffs(peers) - 1;
+        int q = 0;
+        if (lane == leader && dest >= 0) q = atomicAdd(&cursor[dest], __popc(peers));
+        q = __shfl_sync(0xFFFFFFFFu, q, leader);
+        if (e < e1) {
+            if (dest >= 0) {
+                const int pos = q + __popc(peers & ((1u << lane) - 1u));
+                pos_of_entry[e] = pos;
+                const int64_t row = (int64_t)p.rank * p.cap + (pos - start[dest]);
+                reinterpret_cast<int32_t*>(p.peer[dest] + p.L.expert)[row] = ex;
+            } else {
+                pos_of_entry[e] = -1;
+            }
+        }
+    }
+}
+
+// One warp per entry: its token's f16 row into region `rank` of the destination, 16-byte stores
+// (512 contiguous bytes per warp instruction over NVLink).
+__global__ void __launch_bounds__(256) k_p2p_gather(P2PSend p, const int32_t* __restrict__ sel,
+                                                    const uint16_t* __restrict__ xq, int n, int k,
+                                                    const int* __restrict__ pos_of_entry,
+                                                    const int* __restrict__ start) {
+    const int lane = threadIdx.x & 31;
+    const int e = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (e >= n) return;
+    const int pos = pos_of_entry[e];
+    if (pos < 0) return;
+    const int dest = sel[e] / p.epr;
+    const int64_t row = (int64_t)p.rank * p.cap + (pos - start[dest]);
+    const uint4* src = reinterpret_cast<const uint4*>(xq + (int64_t)(e / k) * p.H);
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.peer[dest] + p.L.rows) + row * p.H);
+    for (int i = lane; i < p.H / 8; i += 32) dst[i] = src[i];
+}
+
+__global__ void k_p2p_signal(P2PSend p, uint32_t epoch) {
+    const int g = threadIdx.x;
+    if (g >= p.G) return;
+    __threadfence_system();
+    uint32_t* f = reinterpret_cast<uint32_t*>(p.peer[g] + p.L.flags) + p.rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
+}
+
+__global__ void k_p2p_wait(const uint8_t* block, int64_t flags_off, int G, uint32_t epoch,
+                           unsigned long long timeout_ns, unsigned* err) {
+    const int s = threadIdx.x;
+    if (s >= G) return;
+    if (*(volatile unsigned*)err & 2u) return;            // an earlier wait already gave up
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(block + flags_off) + s;
+    unsigned long long t0 = 0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (;;) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        if ((int32_t)(v - epoch) >= 0) break;
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 > timeout_ns) {
+            atomicOr(err, 2u);
+            break;
+        }
+        __nanosleep(200);
+    }
+    __threadfence_system();
+}
+
 }  // namespace
+
+P2PLayout p2p_layout(int G, int cap, int H) {
+    auto al = [](int64_t v) { return (v + 255) / 256 * 256; };
+    P2PLayout L{};
+    L.flags = 0;
+    L.count = 256;
+    L.start = 512;
+    L.expert = 1024;
+    L.rows = al(L.expert + (int64_t)G * cap * 4);
+    L.yback = al(L.rows + (int64_t)G * cap * H * 2);
+    L.bytes = al(L.yback + (int64_t)cap * H * 2);
+    return L;
+}
+
+cudaError_t launch_p2p_send(const P2PSend& p, const int32_t* sel, int T, int k, const uint16_t* xq, int* counts,
+                            int* cursor, int* start, int* pos_of_entry, unsigned* err, cudaStream_t s, int* launches) {
+    if (p.G < 1 || p.G > EP_MAX_RANKS) return cudaErrorInvalidValue;
+    const int n = T * k;
+    cudaError_t e = cudaMemsetAsync(counts, 0, (size_t)p.G * sizeof(int), s);
+    if (e != cudaSuccess) return e;
+    const int grid = (n + EP_CHUNK - 1) / EP_CHUNK;
+    k_ep_count<<<grid, 256, 0, s>>>(sel, n, p.G, p.epr, counts, err);
+    k_p2p_meta<<<1, 32, 0, s>>>(p, counts, cursor, start);
+    k_p2p_scatter<<<grid, 256, 0, s>>>(p, sel, n, cursor, start, pos_of_entry);
+    k_p2p_gather<<<(n + 7) / 8, 256, 0, s>>>(p, sel, xq, n, k, pos_of_entry, start);
+    if (launches) *launches += 4;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_p2p_signal(const P2PSend& p, uint32_t epoch, cudaStream_t s) {
+    k_p2p_signal<<<1, 64, 0, s>>>(p, epoch);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_p2p_wait(const uint8_t* block, const P2PLayout& L, int G, uint32_t epoch,
+                            unsigned long long timeout_ns, unsigned* err, cudaStream_t s) {
+    k_p2p_wait<<<1, 64, 0, s>>>(block, L.flags, G, epoch, timeout_ns, err);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_ep_pack(const int32_t* sel, int T, int k, int n_ranks, int experts_per_rank, const uint16_t* xq,
                            int H, int* counts, int* cursor, int* pos_of_entry, int32_t* send_expert,

@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(DISP_THREADS) k_dispatch(const int32_t* __rest
                                                            int n_slots, int* __restrict__ counts,
                                                            int* __restrict__ offsets, int* __restrict__ perm,
                                                            unsigned* err, int tile_m, int2* __restrict__ items,
-                                                           int* __restrict__ n_items) {
+                                                           int* __restrict__ n_items, bool skip_neg) {
     extern __shared__ int sm[];
     __shared__ int2 wtot[32];
     const int NS = n_slots + (KK > k ? 1 : 0);
@@ -376,7 +376,10 @@ __global__ void __launch_bounds__(DISP_THREADS) k_dispatch(const int32_t* __rest
         for (int u = 0; u < DISP_UNROLL; ++u) {
             const int e = e0 + u * DISP_THREADS;
             if (e >= n) continue;
-            if (!valid(e, sv[u])) { atomicOr(err, 1u); continue; }
+            if (!valid(e, sv[u])) {
+                if (!(skip_neg && sv[u] < 0)) atomicOr(err, 1u);
+                continue;
+            }
             atomicAdd(&cnt[sv[u]], 1);
         }
     }
@@ -638,7 +641,8 @@ constexpr int DISP_SMALL = 4096;     // entries handled by the single-CTA kernel
 constexpr int DISP_CHUNK = 4096;     // entries per CTA in the multi-CTA kernels
 
 __global__ void __launch_bounds__(512) k_disp_count(const int32_t* __restrict__ slot_of, int T, int k, int KK,
-                                                    int n_slots, int* __restrict__ gcount, unsigned* err) {
+                                                    int n_slots, int* __restrict__ gcount, unsigned* err,
+                                                    bool skip_neg) {
     extern __shared__ int hist[];
     const int NS = n_slots + (KK > k ? 1 : 0);
     for (int i = threadIdx.x; i < NS; i += blockDim.x) hist[i] = 0;
@@ -648,7 +652,10 @@ __global__ void __launch_bounds__(512) k_disp_count(const int32_t* __restrict__ 
     for (int e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
         const int t = e / KK, j = e - t * KK;
         const int sl = (j < k) ? (int)slot_of[(size_t)t * k + j] : n_slots;
-        if (sl < 0 || sl >= NS || (j < k && sl >= n_slots)) { atomicOr(err, 1u); continue; }
+        if (sl < 0 || sl >= NS || (j < k && sl >= n_slots)) {
+            if (!(skip_neg && sl < 0)) atomicOr(err, 1u);
+            continue;
+        }
         atomicAdd(&hist[sl], 1);
     }
     __syncthreads();
@@ -712,18 +719,19 @@ __global__ void __launch_bounds__(512) k_disp_scatter(const int32_t* __restrict_
 }
 
 cudaError_t launch_dispatch(const int32_t* slot_of_sel, int T, int k, int KK, int n_slots, const Scratch& sc,
-                            int tile_m, cudaStream_t s, int* launches) {
+                            int tile_m, cudaStream_t s, int* launches, bool skip_neg) {
     const int NS = n_slots + (KK > k ? 1 : 0);
     const int n = T * KK;
     if (n <= DISP_SMALL) {
         const size_t dsm = (size_t)2 * (NS + 1) * sizeof(int);
         k_dispatch<<<1, DISP_THREADS, dsm, s>>>(slot_of_sel, T, k, KK, n_slots, sc.counts, sc.offsets, sc.perm,
-                                                sc.sync, tile_m, sc.items, sc.n_items);
+                                                sc.sync, tile_m, sc.items, sc.n_items, skip_neg);
         if (launches) *launches += 1;
         return cudaGetLastError();
     }
     const int grid = (n + DISP_CHUNK - 1) / DISP_CHUNK;
-    k_disp_count<<<grid, 512, (size_t)NS * sizeof(int), s>>>(slot_of_sel, T, k, KK, n_slots, sc.dcount, sc.sync);
+    k_disp_count<<<grid, 512, (size_t)NS * sizeof(int), s>>>(slot_of_sel, T, k, KK, n_slots, sc.dcount, sc.sync,
+                                                                    skip_neg);
     k_disp_scan<<<1, DISP_THREADS, 0, s>>>(NS, sc.dcount, sc.counts, sc.offsets, sc.dcursor, tile_m, sc.items,
                                            sc.n_items);
     k_disp_scatter<<<grid, 512, 0, s>>>(slot_of_sel, T, k, KK, n_slots, sc.dcursor, sc.perm);

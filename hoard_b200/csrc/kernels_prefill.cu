@@ -301,6 +301,7 @@ __device__ __forceinline__ void store_row_sw128(uint8_t* tile, int r, const uint
 }  // namespace
 
 struct TcArgs {
+    int grid;               // CTAs of the launch
     LayerWeights lw;
     int H, I, KK;
     const int* offsets;     // [NS+1] sorted-entry offset of each slot
@@ -310,6 +311,12 @@ struct TcArgs {
     const __half* A;        // MODE 0: Q8_K-dequantised activations [T][H]; MODE 1: h [P][I] (sorted)
     __half* hq;             // MODE 0 output [P][I] (sorted order)
     __half* y;              // MODE 1 output [entries][H] by entry id, f16 (clamped to the f16 range)
+    // MODE 1 over peer memory (y_peer != null): entry r is row i = r % y_cap of source s = r / y_cap's
+    // region, and its output goes to rank s's yback row y_start[s] + i (block base y_peer[s] + y_off)
+    uint8_t* const* y_peer;
+    int64_t y_off;
+    const int* y_start;
+    int y_cap;
     unsigned* err;
     unsigned long long* trace;   // optional stamps [cta < TC_TRACE_CTAS][item < 2][stage < 32][TC_TRACE_SLOTS]
 };
@@ -474,6 +481,19 @@ __global__ void __launch_bounds__(tc_threads(MODE), 1) k_tc_experts(TcArgs a) {
                 // each 32 x 32 chunk (lane = row) goes through a padded shared tile so that a store
                 // instruction writes four whole 128-byte row segments instead of 32 scattered 16 bytes
                 const int entry = valid ? a.perm[row0 + m] : -1;
+                __half* yrow = nullptr;                             // this lane's output row
+                if (entry >= 0) {
+                    if (a.y_peer) {
+                        const int src = entry / a.y_cap, i = entry - src * a.y_cap;
+                        const int at = a.y_start[src] + i;
+                        if (at >= 0 && at < a.y_cap)
+                            yrow = reinterpret_cast<__half*>(a.y_peer[src] + a.y_off) + (int64_t)at * a.H;
+                        else
+                            atomicOr(a.err, 1u);
+                    } else {
+                        yrow = a.y + (int64_t)entry * a.H;
+                    }
+                }
                 float* tile = epi_tile + (warp & 3) * 32 * EPI_ROW;
                 const int rsub = lane >> 3, c4 = lane & 7;          // read phase: row 4i + rsub, float4 c4
                 float v[32];
@@ -488,15 +508,14 @@ __global__ void __launch_bounds__(tc_threads(MODE), 1) k_tc_experts(TcArgs a) {
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const int rr = 4 * i + rsub;
-                        const int ent = __shfl_sync(0xFFFFFFFFu, entry, rr);
+                        __half* dst = reinterpret_cast<__half*>(
+                            __shfl_sync(0xFFFFFFFFu, reinterpret_cast<unsigned long long>(yrow), rr));
                         const float4 val = *reinterpret_cast<const float4*>(tile + rr * EPI_ROW + 4 * c4);
                         const float lim = 65504.f;
                         const uint2 hv = make_uint2(
                             bits_h2(__floats2half2_rn(fminf(fmaxf(val.x, -lim), lim), fminf(fmaxf(val.y, -lim), lim))),
                             bits_h2(__floats2half2_rn(fminf(fmaxf(val.z, -lim), lim), fminf(fmaxf(val.w, -lim), lim))));
-                        if (ent >= 0)
-                            *reinterpret_cast<uint2*>(a.y + (int64_t)ent * a.H + (int64_t)nb_out * TC_N + 32 * cc +
-                                                      4 * c4) = hv;
+                        if (dst) *reinterpret_cast<uint2*>(dst + (int64_t)nb_out * TC_N + 32 * cc + 4 * c4) = hv;
                     }
                     __syncwarp();
                 }
@@ -688,7 +707,7 @@ cudaError_t launch_tc(const TcArgs& a, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_set |= 1ull << dev;
     }
-    k_tc_experts<MODE, TYPE><<<tc_grid(), tc_threads(MODE), tc_smem(MODE, TYPE), s>>>(a);
+    k_tc_experts<MODE, TYPE><<<a.grid, tc_threads(MODE), tc_smem(MODE, TYPE), s>>>(a);
     return cudaGetLastError();
 }
 
@@ -714,6 +733,7 @@ cudaError_t launch_experts_tc_rows(const Dims& d, const LayerWeights& lw, const 
     cudaError_t e;
     if ((e = launch_dispatch(slot_of_row, R, 1, 1, lw.n_slots, sc, TC_M, s, &nl)) != cudaSuccess) return e;
     TcArgs a{};
+    a.grid = d.gemm_ctas > 0 && d.gemm_ctas < tc_grid() ? d.gemm_ctas : tc_grid();
     a.lw = lw;
     a.lw.shared = nullptr;           // rows name their slot; a shared expert is not dispatched
     a.H = d.H;
@@ -730,6 +750,62 @@ cudaError_t launch_experts_tc_rows(const Dims& d, const LayerWeights& lw, const 
     if (e != cudaSuccess) return e;
     a.A = reinterpret_cast<const __half*>(sc.hq16);
     a.y = reinterpret_cast<__half*>(y_out);
+    e = lw.down_type == T_Q4K ? launch_tc<1, T_Q4K>(a, s) : launch_tc<1, T_Q6K>(a, s);
+    if (e != cudaSuccess) return e;
+    if (launches) *launches += nl + 2;
+    return cudaSuccess;
+}
+
+// Expert-parallel receive side over peer memory: the G regions of this rank's block hold the rows
+// that every source sent (count[s] of them in region s), each tagged with its expert id.
+__global__ void __launch_bounds__(256) k_p2p_rx_slots(const uint8_t* __restrict__ block, P2PLayout L, int G, int cap,
+                                                      int e_lo, int epr, int slot_base, int n_slots,
+                                                      unsigned* err, int* __restrict__ slots) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= (int64_t)G * cap) return;
+    const int src = (int)(r / cap), i = (int)(r - (int64_t)src * cap);
+    const int* count = reinterpret_cast<const int*>(block + L.count);
+    const int32_t* expert = reinterpret_cast<const int32_t*>(block + L.expert);
+    int sl = -1;
+    if (!(*(volatile unsigned*)err & 2u) && i < count[src]) {
+        const int ex = expert[r];
+        if (ex >= e_lo && ex < e_lo + epr && ex - e_lo + slot_base < n_slots)
+            sl = ex - e_lo + slot_base;
+        else
+            atomicOr(err, 1u);
+    }
+    slots[r] = sl;
+}
+
+cudaError_t launch_p2p_experts(const Dims& d, const LayerWeights& lw, const Scratch& sc, const P2PSend& p,
+                               const uint8_t* block, int slot_base, int* slots, cudaStream_t s, int* launches) {
+    const int64_t n = (int64_t)p.G * p.cap;
+    k_p2p_rx_slots<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(block, p.L, p.G, p.cap, p.rank * p.epr, p.epr,
+                                                                slot_base, lw.n_slots, sc.sync, slots);
+    int nl = 1;
+    cudaError_t e;
+    if ((e = launch_dispatch(slots, (int)n, 1, 1, lw.n_slots, sc, TC_M, s, &nl, true)) != cudaSuccess) return e;
+    TcArgs a{};
+    a.grid = d.gemm_ctas > 0 && d.gemm_ctas < tc_grid() ? d.gemm_ctas : tc_grid();
+    a.lw = lw;
+    a.lw.shared = nullptr;
+    a.H = d.H;
+    a.I = d.I;
+    a.KK = 1;
+    a.offsets = sc.offsets;
+    a.perm = sc.perm;
+    a.items = sc.items;
+    a.n_items = sc.n_items;
+    a.err = sc.sync;
+    a.A = reinterpret_cast<const __half*>(block + p.L.rows);
+    a.hq = reinterpret_cast<__half*>(sc.hq16);
+    e = lw.gate_type == T_Q4K ? launch_tc<0, T_Q4K>(a, s) : launch_tc<0, T_Q6K>(a, s);
+    if (e != cudaSuccess) return e;
+    a.A = reinterpret_cast<const __half*>(sc.hq16);
+    a.y_peer = p.peer;
+    a.y_off = p.L.yback;
+    a.y_start = reinterpret_cast<const int*>(block + p.L.start);
+    a.y_cap = p.cap;
     e = lw.down_type == T_Q4K ? launch_tc<1, T_Q4K>(a, s) : launch_tc<1, T_Q6K>(a, s);
     if (e != cudaSuccess) return e;
     if (launches) *launches += nl + 2;
@@ -765,6 +841,7 @@ cudaError_t launch_experts_tc(const Dims& d, const LayerWeights& lw, const Scrat
     if ((e = launch_dispatch(slot_of_sel, T, d.k, KK, lw.n_slots, sc, TC_M, s, &nl)) != cudaSuccess) return e;
     // 3. gate/up + SwiGLU + Q8_K(h); 4. down
     TcArgs a{};
+    a.grid = d.gemm_ctas > 0 && d.gemm_ctas < tc_grid() ? d.gemm_ctas : tc_grid();
     a.lw = lw;
     a.H = d.H;
     a.I = d.I;

@@ -74,6 +74,27 @@ struct hoard_moe_ctx {
     int64_t ep_rows = 0;
     Scratch ep{};
     int* ep_cursor = nullptr;          // [64] pack cursors
+    // expert parallelism over peer memory (hoard_moe_p2p_*)
+    struct P2P {
+        bool init = false, connected = false;
+        int G = 0, rank = 0, epr = 0, slot_base = 0, cap = 0;
+        P2PLayout L{};
+        uint8_t* block = nullptr;              // this rank's symmetric block
+        std::vector<uint8_t*> bases;           // every rank's block base in this process
+        std::vector<void*> opened;             // IPC mappings to close
+        uint8_t** peer_dev = nullptr;          // device copy of bases
+        uint32_t epoch = 0;                    // barrier epochs signalled so far
+        int* slots = nullptr;                  // [G*cap] slot of each received row
+        int* pos = nullptr;                    // [cap] send position of each (token, j) entry
+        int* counts = nullptr;                 // [64] send counts per destination
+        int* cursor = nullptr;                 // [64]
+        int* start = nullptr;                  // [64] send offsets per destination
+        Scratch rx{};                          // receive-side dispatch + h scratch for G*cap rows
+        int phase = 0;                         // 0 idle, 1 sent, 2 computed
+        int layer = -1, T = 0;
+        const float* w = nullptr;
+        unsigned long long timeout_ns = 5000000000ull;
+    } p2p;
     std::string err;
 };
 
@@ -188,7 +209,7 @@ int hoard_moe_create(const hoard_moe_desc* d, hoard_moe_ctx** out) {
     auto* c = new hoard_moe_ctx();
     c->desc = *d;
     c->desc.gate_types = c->desc.up_types = c->desc.down_types = nullptr;  // caller's arrays are not retained
-    c->dims = Dims{H, E, k, I, d->norm_topk ? 1 : 0, d->eps, d->resid_type == HOARD_TYPE_BF16 ? 1 : 0};
+    c->dims = Dims{H, E, k, I, d->norm_topk ? 1 : 0, d->eps, d->resid_type == HOARD_TYPE_BF16 ? 1 : 0, 0};
     int rc = HOARD_OK;
     cudaError_t e = cudaSetDevice(d->device);
     if (e != cudaSuccess) {
@@ -286,6 +307,7 @@ int hoard_moe_destroy(hoard_moe_ctx* c) {
     if (!c) return HOARD_EINVAL;
     cudaSetDevice(c->desc.device);
     cudaDeviceSynchronize();
+    for (void* p : c->p2p.opened) cudaIpcCloseMemHandle(p);
     for (void* p : c->allocations) cudaFree(p);
     if (c->staging_free) cudaEventDestroy(c->staging_free);
     for (cudaEvent_t ev : c->res.ready) if (ev) cudaEventDestroy(ev);
@@ -668,6 +690,12 @@ int hoard_moe_ep_combine(hoard_moe_ctx* c, const float* w, const int32_t* pos_of
     return HOARD_OK;
 }
 
+int hoard_moe_set_gemm_ctas(hoard_moe_ctx* c, int ctas) {
+    if (!c || ctas < 0) return HOARD_EINVAL;
+    c->dims.gemm_ctas = ctas;
+    return HOARD_OK;
+}
+
 int hoard_moe_set_gemm_min_tokens(hoard_moe_ctx* c, int min_tokens) {
     if (!c || min_tokens < 0) return HOARD_EINVAL;
     c->gemm_min_tokens = min_tokens;
@@ -699,6 +727,250 @@ int hoard_moe_sync_status(hoard_moe_ctx* c, hoard_stream stream) {
         HCHECK(c, cudaMemcpy(c->sc.sync, &zero, 4, cudaMemcpyHostToDevice));
         if (flags & 2u) return fail(c, HOARD_ETIMEOUT, "a device-side wait gave up");
         return fail(c, HOARD_EINVAL, "an expert or slot id was out of range (entries skipped)");
+    }
+    return HOARD_OK;
+}
+
+// ---- expert parallelism over peer memory ----
+
+namespace {
+
+struct P2PHandle {
+    uint32_t magic, version;
+    int32_t G, rank, cap, H;
+    int64_t bytes;
+    cudaIpcMemHandle_t ipc;
+};
+static_assert(sizeof(P2PHandle) <= HOARD_P2P_HANDLE_BYTES, "handle blob too small");
+constexpr uint32_t kP2PMagic = 0x50324850u;   // "PH2P"
+
+P2PSend p2p_args(const hoard_moe_ctx* c) {
+    P2PSend p{};
+    p.peer = c->p2p.peer_dev;
+    p.L = c->p2p.L;
+    p.G = c->p2p.G;
+    p.rank = c->p2p.rank;
+    p.cap = c->p2p.cap;
+    p.H = c->dims.H;
+    p.epr = c->p2p.epr;
+    return p;
+}
+
+int p2p_connect(hoard_moe_ctx* c) {
+    HCHECK(c, cudaMemcpy(c->p2p.peer_dev, c->p2p.bases.data(), c->p2p.G * sizeof(uint8_t*), cudaMemcpyHostToDevice));
+    c->p2p.connected = true;
+    c->p2p.phase = 0;
+    return HOARD_OK;
+}
+
+}  // namespace
+
+int hoard_moe_p2p_init(hoard_moe_ctx* c, int n_ranks, int rank, int experts_per_rank, int slot_base) {
+    if (!c) return HOARD_EINVAL;
+    auto& P = c->p2p;
+    if (P.init) return fail(c, HOARD_ESTATE, "peer-memory expert parallelism already initialised");
+    if (n_ranks < 1 || n_ranks > 64 || rank < 0 || rank >= n_ranks || experts_per_rank < 1 ||
+        (int64_t)n_ranks * experts_per_rank < c->dims.E || slot_base < 0)
+        return fail(c, HOARD_EINVAL, "need 1 <= n_ranks <= 64, 0 <= rank < n_ranks, n_ranks * experts_per_rank >= n_expert");
+    const int own = std::max(0, std::min(experts_per_rank, c->dims.E - rank * experts_per_rank));
+    if (slot_base + own > c->desc.n_slots) return fail(c, HOARD_EINVAL, "this rank's experts do not fit the pool");
+    if (c->desc.n_ff_shexp > 0) return fail(c, HOARD_EINVAL, "layers with a shared expert are not supported");
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    const int64_t cap = (int64_t)c->desc.max_tokens * c->dims.k;
+    if (cap * n_ranks > ((int64_t)1 << 30)) return fail(c, HOARD_EINVAL, "max_tokens * k * n_ranks too large");
+    P.G = n_ranks;
+    P.rank = rank;
+    P.epr = experts_per_rank;
+    P.slot_base = slot_base;
+    P.cap = (int)cap;
+    P.L = p2p_layout(n_ranks, P.cap, c->dims.H);
+    const int64_t R = cap * n_ranks;
+    Scratch& x = P.rx;
+    const int64_t NS2 = (int64_t)c->desc.n_slots + 2;
+    int rc = dalloc(c, &P.block, P.L.bytes);
+    if (rc == HOARD_OK) rc = dalloc(c, &P.peer_dev, 64 * sizeof(uint8_t*));
+    if (rc == HOARD_OK) rc = dalloc(c, &P.slots, R * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &P.pos, cap * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &P.counts, 64 * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &P.cursor, 64 * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &P.start, 64 * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &x.counts, NS2 * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &x.offsets, NS2 * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &x.perm, R * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &x.hq16, R * c->dims.I * 2);
+    if (rc == HOARD_OK) rc = dalloc(c, &x.items, tc_max_items((int)R, 1, c->desc.n_slots) * (int64_t)sizeof(int2));
+    if (rc == HOARD_OK) rc = dalloc(c, &x.n_items, 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &x.dcount, NS2 * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &x.dcursor, NS2 * 4);
+    if (rc != HOARD_OK) return rc;
+    HCHECK(c, cudaMemset(P.block, 0, (size_t)P.L.bytes));
+    HCHECK(c, cudaMemset(x.dcount, 0, (size_t)NS2 * 4));
+    HCHECK(c, cudaDeviceSynchronize());
+    x.sync = c->sc.sync;
+    P.bases.assign(n_ranks, nullptr);
+    P.bases[rank] = P.block;
+    P.init = true;
+    return HOARD_OK;
+}
+
+int hoard_moe_p2p_handle(hoard_moe_ctx* c, void* out) {
+    if (!c || !out) return HOARD_EINVAL;
+    if (!c->p2p.init) return fail(c, HOARD_ESTATE, "hoard_moe_p2p_init must run first");
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    P2PHandle h{};
+    h.magic = kP2PMagic;
+    h.version = 1;
+    h.G = c->p2p.G;
+    h.rank = c->p2p.rank;
+    h.cap = c->p2p.cap;
+    h.H = c->dims.H;
+    h.bytes = c->p2p.L.bytes;
+    HCHECK(c, cudaIpcGetMemHandle(&h.ipc, c->p2p.block));
+    std::memset(out, 0, HOARD_P2P_HANDLE_BYTES);
+    std::memcpy(out, &h, sizeof(h));
+    return HOARD_OK;
+}
+
+int hoard_moe_p2p_open(hoard_moe_ctx* c, const void* handles) {
+    if (!c || !handles) return HOARD_EINVAL;
+    auto& P = c->p2p;
+    if (!P.init) return fail(c, HOARD_ESTATE, "hoard_moe_p2p_init must run first");
+    if (P.connected) return fail(c, HOARD_ESTATE, "already connected (hoard_moe_p2p_close first)");
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    for (int s = 0; s < P.G; ++s) {
+        P2PHandle h;
+        std::memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)s * HOARD_P2P_HANDLE_BYTES, sizeof(h));
+        if (h.magic != kP2PMagic || h.version != 1 || h.G != P.G || h.rank != s || h.cap != P.cap ||
+            h.H != c->dims.H || h.bytes != P.L.bytes)
+            return fail(c, HOARD_EINVAL, "peer handle " + std::to_string(s) + " does not match this group");
+    }
+    for (int s = 0; s < P.G; ++s) {
+        if (s == P.rank) continue;
+        P2PHandle h;
+        std::memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)s * HOARD_P2P_HANDLE_BYTES, sizeof(h));
+        void* ptr = nullptr;
+        HCHECK(c, cudaIpcOpenMemHandle(&ptr, h.ipc, cudaIpcMemLazyEnablePeerAccess));
+        P.opened.push_back(ptr);
+        P.bases[s] = static_cast<uint8_t*>(ptr);
+    }
+    return p2p_connect(c);
+}
+
+int hoard_moe_p2p_attach(hoard_moe_ctx* c, hoard_moe_ctx* const* peers) {
+    if (!c || !peers) return HOARD_EINVAL;
+    auto& P = c->p2p;
+    if (!P.init) return fail(c, HOARD_ESTATE, "hoard_moe_p2p_init must run first");
+    if (P.connected) return fail(c, HOARD_ESTATE, "already connected (hoard_moe_p2p_close first)");
+    if (peers[P.rank] != c) return fail(c, HOARD_EINVAL, "peers[rank] must be this context");
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    for (int s = 0; s < P.G; ++s) {
+        const hoard_moe_ctx* q = peers[s];
+        if (!q || !q->p2p.init || q->p2p.G != P.G || q->p2p.rank != s || q->p2p.cap != P.cap ||
+            q->dims.H != c->dims.H)
+            return fail(c, HOARD_EINVAL, "peer " + std::to_string(s) + " does not match this group");
+        if (q->desc.device != c->desc.device) {
+            cudaError_t e = cudaDeviceEnablePeerAccess(q->desc.device, 0);
+            if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+            else if (e != cudaSuccess) return cuda_fail(c, e, "cudaDeviceEnablePeerAccess");
+        }
+        P.bases[s] = q->p2p.block;
+    }
+    return p2p_connect(c);
+}
+
+int hoard_moe_p2p_close(hoard_moe_ctx* c) {
+    if (!c) return HOARD_EINVAL;
+    auto& P = c->p2p;
+    if (!P.init) return HOARD_OK;
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    HCHECK(c, cudaDeviceSynchronize());
+    for (void* p : P.opened) cudaIpcCloseMemHandle(p);
+    P.opened.clear();
+    for (int s = 0; s < P.G; ++s)
+        if (s != P.rank) P.bases[s] = nullptr;
+    HCHECK(c, cudaMemset(P.block + P.L.flags, 0, 256));
+    HCHECK(c, cudaDeviceSynchronize());
+    P.epoch = 0;
+    P.connected = false;
+    P.phase = 0;
+    return HOARD_OK;
+}
+
+int hoard_moe_p2p_set_timeout(hoard_moe_ctx* c, double seconds) {
+    if (!c || !(seconds > 0) || seconds > 3600) return c ? fail(c, HOARD_EINVAL, "timeout out of range") : HOARD_EINVAL;
+    c->p2p.timeout_ns = (unsigned long long)(seconds * 1e9);
+    return HOARD_OK;
+}
+
+int hoard_moe_p2p_send(hoard_moe_ctx* c, int layer, const void* x, int T, int32_t* sel_out, float* w_out,
+                       hoard_stream stream) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    auto& P = c->p2p;
+    if (!P.connected) return fail(c, HOARD_ESTATE, "peer group not connected (hoard_moe_p2p_open / attach)");
+    if (P.phase != 0) return fail(c, HOARD_ESTATE, "hoard_moe_p2p_finish of the previous layer has not run");
+    if (!tc_supported(c->dims, layer_weights(c, layer)))
+        return fail(c, HOARD_EINVAL, "expert types unsupported by the tensor-core path");
+    int32_t* sel = sel_out ? sel_out : c->sc.sel;
+    float* w = w_out ? w_out : c->sc.w;
+    if ((rc = hoard_moe_route(c, layer, x, T, sel, w, stream))) return rc;
+    const cudaStream_t s = (cudaStream_t)stream;
+    HCHECK(c, launch_q8_rows(c->sc.fx, T, c->dims.H, c->sc.xq16, s));
+    int nl = 1;
+    const P2PSend a = p2p_args(c);
+    HCHECK(c, launch_p2p_send(a, sel, T, c->dims.k, c->sc.xq16, P.counts, P.cursor, P.start, P.pos, c->sc.sync, s, &nl));
+    HCHECK(c, launch_p2p_signal(a, ++P.epoch, s));
+    c->launches += nl + 1;
+    P.phase = 1;
+    P.layer = layer;
+    P.T = T;
+    P.w = w;
+    return HOARD_OK;
+}
+
+int hoard_moe_p2p_compute(hoard_moe_ctx* c, hoard_stream stream) {
+    if (!c) return HOARD_EINVAL;
+    auto& P = c->p2p;
+    if (P.phase != 1) return fail(c, HOARD_ESTATE, "hoard_moe_p2p_send must run first");
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    const cudaStream_t s = (cudaStream_t)stream;
+    const P2PSend a = p2p_args(c);
+    HCHECK(c, launch_p2p_wait(P.block, P.L, P.G, P.epoch, P.timeout_ns, c->sc.sync, s));
+    int nl = 1;
+    HCHECK(c, launch_p2p_experts(c->dims, layer_weights(c, P.layer), P.rx, a, P.block, P.slot_base, P.slots, s, &nl));
+    HCHECK(c, launch_p2p_signal(a, ++P.epoch, s));
+    c->launches += nl + 1;
+    P.phase = 2;
+    return HOARD_OK;
+}
+
+int hoard_moe_p2p_finish(hoard_moe_ctx* c, void* x_inout, hoard_stream stream) {
+    if (!c) return HOARD_EINVAL;
+    auto& P = c->p2p;
+    if (P.phase != 2) return fail(c, HOARD_ESTATE, "hoard_moe_p2p_compute must run first");
+    if (!x_inout) return fail(c, HOARD_EINVAL, "null x");
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    const cudaStream_t s = (cudaStream_t)stream;
+    HCHECK(c, launch_p2p_wait(P.block, P.L, P.G, P.epoch, P.timeout_ns, c->sc.sync, s));
+    HCHECK(c, launch_combine_rows(c->dims, reinterpret_cast<const uint16_t*>(P.block + P.L.yback), P.pos, P.w,
+                                  x_inout, P.T, s));
+    c->launches += 2;
+    P.phase = 0;
+    return HOARD_OK;
+}
+
+int hoard_moe_p2p_layers(hoard_moe_ctx* c, int layer0, int n_layers, void* x_inout, int T, int32_t* sel_out,
+                         float* w_out, hoard_stream stream) {
+    if (!c) return HOARD_EINVAL;
+    if (n_layers <= 0 || layer0 < 0 || layer0 + n_layers > c->desc.n_layer)
+        return fail(c, HOARD_EINVAL, "layer range out of bounds");
+    for (int l = layer0; l < layer0 + n_layers; ++l) {
+        const int64_t o = (int64_t)(l - layer0) * T * c->dims.k;
+        int rc = hoard_moe_p2p_send(c, l, x_inout, T, sel_out ? sel_out + o : nullptr, w_out ? w_out + o : nullptr,
+                                    stream);
+        if (!rc) rc = hoard_moe_p2p_compute(c, stream);
+        if (!rc) rc = hoard_moe_p2p_finish(c, x_inout, stream);
+        if (rc) return rc;
     }
     return HOARD_OK;
 }

@@ -34,10 +34,14 @@ EXPORTED = [
     "hoard_moe_set_shared", "hoard_moe_route", "hoard_moe_experts", "hoard_moe_layer", "hoard_moe_layers",
     "hoard_moe_sync_status", "hoard_moe_expert_bytes", "hoard_moe_launch_count", "hoard_moe_set_decode_impl",
     "hoard_moe_set_trace", "hoard_moe_trace_layout", "hoard_moe_decode_noalloc",
-    "hoard_moe_set_gemm_min_tokens", "hoard_moe_ep_reserve", "hoard_moe_ep_pack", "hoard_moe_ep_experts",
+    "hoard_moe_set_gemm_min_tokens", "hoard_moe_set_gemm_ctas", "hoard_moe_ep_reserve", "hoard_moe_ep_pack", "hoard_moe_ep_experts",
     "hoard_moe_ep_combine", "hoard_moe_ram_tier", "hoard_moe_ensure", "hoard_moe_residency_stats",
-    "hoard_moe_last_error", "hoard_strerror",
+    "hoard_moe_p2p_init", "hoard_moe_p2p_handle", "hoard_moe_p2p_open", "hoard_moe_p2p_attach", "hoard_moe_p2p_close",
+    "hoard_moe_p2p_set_timeout", "hoard_moe_p2p_send", "hoard_moe_p2p_compute", "hoard_moe_p2p_finish",
+    "hoard_moe_p2p_layers", "hoard_moe_last_error", "hoard_strerror",
 ]
+
+P2P_HANDLE_BYTES = 128
 
 
 class Desc(ctypes.Structure):
@@ -85,6 +89,7 @@ def lib() -> ctypes.CDLL:
         L.hoard_moe_launch_count.restype = i64
         L.hoard_moe_set_decode_impl.argtypes = [vp, i32]
         L.hoard_moe_set_gemm_min_tokens.argtypes = [vp, i32]
+        L.hoard_moe_set_gemm_ctas.argtypes = [vp, i32]
         L.hoard_moe_ram_tier.argtypes = [vp, i32, i32, vp, vp, vp]
         L.hoard_moe_ensure.argtypes = [vp, i32, vp, i32, vp, vp]
         L.hoard_moe_residency_stats.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64), ctypes.POINTER(i64)]
@@ -92,6 +97,16 @@ def lib() -> ctypes.CDLL:
         L.hoard_moe_ep_pack.argtypes = [vp, i32, vp, i32, i32, i32, vp, vp, vp, vp, vp]
         L.hoard_moe_ep_experts.argtypes = [vp, i32, vp, vp, i32, vp, vp]
         L.hoard_moe_ep_combine.argtypes = [vp, vp, vp, vp, vp, i32, vp]
+        L.hoard_moe_p2p_init.argtypes = [vp, i32, i32, i32, i32]
+        L.hoard_moe_p2p_handle.argtypes = [vp, vp]
+        L.hoard_moe_p2p_open.argtypes = [vp, vp]
+        L.hoard_moe_p2p_attach.argtypes = [vp, vp]
+        L.hoard_moe_p2p_close.argtypes = [vp]
+        L.hoard_moe_p2p_set_timeout.argtypes = [vp, ctypes.c_double]
+        L.hoard_moe_p2p_send.argtypes = [vp, i32, vp, i32, vp, vp, vp]
+        L.hoard_moe_p2p_compute.argtypes = [vp, vp]
+        L.hoard_moe_p2p_finish.argtypes = [vp, vp, vp]
+        L.hoard_moe_p2p_layers.argtypes = [vp, i32, i32, vp, i32, vp, vp, vp]
         L.hoard_moe_set_trace.argtypes = [vp, vp, i64]
         L.hoard_moe_decode_noalloc.argtypes = [vp, i32, i32, vp, vp, vp, vp]
         L.hoard_moe_trace_layout.argtypes = [vp, ctypes.POINTER(i32), ctypes.POINTER(i32)]
@@ -229,9 +244,57 @@ class MoEContext:
                                                _stream(stream)), "ep_combine")
         return x_inout
 
+    # ---- expert parallelism over NVLink peer memory ----
+    def p2p_init(self, n_ranks: int, rank: int, experts_per_rank: int, slot_base: int):
+        self._check(lib().hoard_moe_p2p_init(self._h, n_ranks, rank, experts_per_rank, slot_base), "p2p_init")
+
+    def p2p_handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(P2P_HANDLE_BYTES)
+        self._check(lib().hoard_moe_p2p_handle(self._h, buf), "p2p_handle")
+        return buf.raw
+
+    def p2p_open(self, handles):
+        """handles: every rank's p2p_handle() bytes in rank order."""
+        blob = b"".join(handles)
+        if len(blob) != P2P_HANDLE_BYTES * len(handles):
+            raise ValueError("each handle must be P2P_HANDLE_BYTES long")
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        self._check(lib().hoard_moe_p2p_open(self._h, buf), "p2p_open")
+
+    def p2p_attach(self, peers):
+        """peers: the group's contexts of this process in rank order (this one included)."""
+        arr = (ctypes.c_void_p * len(peers))(*[p._h for p in peers])
+        self._check(lib().hoard_moe_p2p_attach(self._h, arr), "p2p_attach")
+
+    def p2p_close(self):
+        self._check(lib().hoard_moe_p2p_close(self._h), "p2p_close")
+
+    def p2p_set_timeout(self, seconds: float):
+        self._check(lib().hoard_moe_p2p_set_timeout(self._h, float(seconds)), "p2p_set_timeout")
+
+    def p2p_send(self, layer: int, x: torch.Tensor, sel_out=None, w_out=None, stream=None):
+        self._check(lib().hoard_moe_p2p_send(self._h, layer, _ptr(x), x.shape[0], _ptr(sel_out), _ptr(w_out),
+                                             _stream(stream)), "p2p_send")
+
+    def p2p_compute(self, stream=None):
+        self._check(lib().hoard_moe_p2p_compute(self._h, _stream(stream)), "p2p_compute")
+
+    def p2p_finish(self, x_inout: torch.Tensor, stream=None):
+        self._check(lib().hoard_moe_p2p_finish(self._h, _ptr(x_inout), _stream(stream)), "p2p_finish")
+        return x_inout
+
+    def p2p_layers(self, layer0: int, n_layers: int, x_inout: torch.Tensor, sel_out=None, w_out=None, stream=None):
+        self._check(lib().hoard_moe_p2p_layers(self._h, layer0, n_layers, _ptr(x_inout), x_inout.shape[0],
+                                               _ptr(sel_out), _ptr(w_out), _stream(stream)), "p2p_layers")
+        return x_inout
+
     def set_gemm_min_tokens(self, min_tokens: int):
         """T at or above which the expert FFN runs as the tensor-core grouped GEMM (0 = never)."""
         self._check(lib().hoard_moe_set_gemm_min_tokens(self._h, min_tokens), "set_gemm_min_tokens")
+
+    def set_gemm_ctas(self, ctas: int):
+        """CTAs of the tensor-core GEMMs (0 = one per SM)."""
+        self._check(lib().hoard_moe_set_gemm_ctas(self._h, ctas), "set_gemm_ctas")
 
     def set_trace(self, buf: torch.Tensor | None):
         """Enables phase stamps of the persistent decode kernel into an int64 CUDA tensor."""

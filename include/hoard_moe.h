@@ -176,6 +176,11 @@ int hoard_moe_set_decode_impl(hoard_moe_ctx* ctx, int impl);
  * its graph picks the backend's matmul kernel by batch size. */
 int hoard_moe_set_gemm_min_tokens(hoard_moe_ctx* ctx, int min_tokens);
 
+/* CTAs of the tensor-core GEMM launches (0 = one per SM, the default). Fewer leave SMs free for
+ * kernels that should run alongside, e.g. NCCL's all-to-all of the next micro-batch during expert
+ * parallelism (hoard_b200/ep.py). No counterpart in hoard. */
+int hoard_moe_set_gemm_ctas(hoard_moe_ctx* ctx, int ctas);
+
 /* ---- Residency: per-layer LRU slot pool over a host RAM tier --------------------------------------
  * Replaces hoard's to_vram / fetch and its per-layer LRU (src/run_moe_stream.cpp:279-284, :380-421;
  * the `ensure` of src/run_specloop.cpp:123) when n_slots < n_expert. Uploads run on the context's own
@@ -232,6 +237,56 @@ int hoard_moe_ep_experts(hoard_moe_ctx* ctx, int layer, const uint16_t* rows, co
  * src/run_moe_stream.cpp:447), y_back [T*k][n_embd] f16 bits in send order. */
 int hoard_moe_ep_combine(hoard_moe_ctx* ctx, const float* w, const int32_t* pos_of_entry, const uint16_t* y_back,
                          void* x_inout, int T, hoard_stream stream);
+
+/* ---- Expert parallelism over NVLink peer memory (no host round trip, no collective library) ----
+ * The same sharding as above, with the exchange done by this library's own kernels: every rank owns
+ * one symmetric block (receive regions [n_ranks][cap][n_embd] f16 with cap = max_tokens * k, the
+ * per-source counts, and y_back [cap][n_embd]) that all ranks map. Per layer, on each rank's stream:
+ *   hoard_moe_p2p_send    route; entries counted by destination; rows and expert ids stored straight
+ *                         into each destination's region `rank`; signal
+ *   hoard_moe_p2p_compute wait for every rank's send; expert FFN (tensor cores) of the received rows,
+ *                         the down epilogue storing each output row straight into its source rank's
+ *                         y_back; signal
+ *   hoard_moe_p2p_finish  wait for every rank's compute; x[t] += sum_j w_j y_back[pos(t, j)]
+ * Waits are bounded (hoard_moe_p2p_set_timeout, default 5 s): on expiry they set the error that
+ * hoard_moe_sync_status reports as HOARD_ETIMEOUT, later waits return at once and the received rows
+ * are skipped, so the context stays usable; the peer group must then be closed and re-opened on every
+ * rank. Results equal hoard_moe_layer's on one GPU bit for bit. Layers with a shared expert are not
+ * supported (HOARD_EINVAL). */
+#define HOARD_P2P_HANDLE_BYTES 128
+
+/* Allocates this rank's block (zeroed) and the receive-side scratch. The rank computes experts
+ * [rank*experts_per_rank, (rank+1)*experts_per_rank) held in pool slots slot_base... */
+int hoard_moe_p2p_init(hoard_moe_ctx* ctx, int n_ranks, int rank, int experts_per_rank, int slot_base);
+
+/* HOARD_P2P_HANDLE_BYTES describing this rank's block (a CUDA IPC handle plus the layout), to be
+ * all-gathered by the caller. */
+int hoard_moe_p2p_handle(hoard_moe_ctx* ctx, void* handle_out);
+
+/* Maps every other rank's block from the all-gathered handles ([n_ranks][HOARD_P2P_HANDLE_BYTES],
+ * rank order; processes of one node). */
+int hoard_moe_p2p_open(hoard_moe_ctx* ctx, const void* handles);
+
+/* The same for ranks that are contexts of this process (peers[n_ranks], peers[rank] == ctx; on the same
+ * or on other GPUs of the node). */
+int hoard_moe_p2p_attach(hoard_moe_ctx* ctx, hoard_moe_ctx* const* peers);
+
+/* Unmaps the peers' blocks and resets this rank's barrier state; every rank closes before any re-opens. */
+int hoard_moe_p2p_close(hoard_moe_ctx* ctx);
+
+int hoard_moe_p2p_set_timeout(hoard_moe_ctx* ctx, double seconds);
+
+/* The three steps of one layer (above); x [T][n_embd] on this rank, T <= max_tokens (ranks may differ).
+ * sel_out / w_out may be null (internal buffers); w must stay valid until hoard_moe_p2p_finish. */
+int hoard_moe_p2p_send(hoard_moe_ctx* ctx, int layer, const void* x, int T, int32_t* sel_out, float* w_out,
+                       hoard_stream stream);
+int hoard_moe_p2p_compute(hoard_moe_ctx* ctx, hoard_stream stream);
+int hoard_moe_p2p_finish(hoard_moe_ctx* ctx, void* x_inout, hoard_stream stream);
+
+/* send + compute + finish over layers [layer0, layer0 + n_layers); sel_out / w_out as in
+ * hoard_moe_layers ([n_layers][T][k] or null). */
+int hoard_moe_p2p_layers(hoard_moe_ctx* ctx, int layer0, int n_layers, void* x_inout, int T, int32_t* sel_out,
+                         float* w_out, hoard_stream stream);
 
 /* Last error message of this context (CUDA error string or argument check). */
 const char* hoard_moe_last_error(const hoard_moe_ctx* ctx);

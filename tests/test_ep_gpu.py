@@ -96,7 +96,8 @@ def test_emulated_ranks_equal_local_layer(layer_ctx, G):
     assert np.array_equal(x.cpu().numpy().view(np.uint32), ref.view(np.uint32))
 
 
-def test_single_rank_process_group_equals_local_layer(layer_ctx):
+@pytest.mark.parametrize("chunks", [1, 3])
+def test_single_rank_process_group_equals_local_layer(layer_ctx, chunks):
     import torch.distributed as dist
     from hoard_b200.ep import ExpertParallel
     L, ctx = layer_ctx
@@ -107,11 +108,27 @@ def test_single_rank_process_group_equals_local_layer(layer_ctx):
         x_np = make_x(T, SPEC.H, seed=31)
         ref = local_layer(ctx, x_np)
         x = torch.from_numpy(x_np).cuda(DEV)
-        ExpertParallel(ctx, experts_per_rank=SPEC.E, slot_base=0).layer(0, x)
+        ep = ExpertParallel(ctx, experts_per_rank=SPEC.E, slot_base=0, chunks=chunks)
+        ep.layers(0, 1, x)
         ctx.sync_status()
         assert np.array_equal(x.cpu().numpy().view(np.uint32), ref.view(np.uint32))
     finally:
         dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("ctas", [1, 37, 132])
+def test_reduced_gemm_grid_is_bit_exact(layer_ctx, ctas):
+    """The tensor-core GEMMs on fewer CTAs than SMs (room for a concurrent all-to-all) compute the same
+    rows: the work list is strided over whatever grid runs it."""
+    L, ctx = layer_ctx
+    x_np = make_x(700, SPEC.H, seed=32)
+    ref = local_layer(ctx, x_np)
+    ctx.set_gemm_ctas(ctas)
+    try:
+        got = local_layer(ctx, x_np)
+    finally:
+        ctx.set_gemm_ctas(0)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
 
 
 def test_ep_reserve_bounds_received_rows(layer_ctx):
@@ -123,7 +140,7 @@ def test_ep_reserve_bounds_received_rows(layer_ctx):
     assert ei.value.status == moe.HOARD_EINVAL
 
 
-def _two_gpu_rank(rank, world, port, out_dir):
+def _two_gpu_rank(rank, world, port, out_dir, chunks=1):
     import torch.distributed as dist
     from hoard_b200.ep import ExpertParallel
     torch.cuda.set_device(rank)
@@ -139,8 +156,10 @@ def _two_gpu_rank(rank, world, port, out_dir):
         ctx.sync_status()
         x = torch.from_numpy(x_np).cuda(rank)
         ep = ExpertParallel(ctx, experts_per_rank=SPEC.E // world, slot_base=rank * (SPEC.E // world),
-                            max_rows=512 * SPEC.k * world)
-        ep.layer(0, x)
+                            max_rows=512 * SPEC.k * world, chunks=chunks)
+        if chunks > 1:
+            ctx.set_gemm_ctas(132)
+        ep.layers(0, 1, x)
         ctx.sync_status()
         np.savez(os.path.join(out_dir, f"r{rank}.npz"), ref=ref.cpu().numpy(), ep=x.cpu().numpy(),
                  recv=ep.last_recv_rows)
@@ -150,9 +169,10 @@ def _two_gpu_rank(rank, world, port, out_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_gpus_equal_local_layer(tmp_path):
+@pytest.mark.parametrize("chunks", [1, 2])
+def test_two_gpus_equal_local_layer(tmp_path, chunks):
     import torch.multiprocessing as mp
-    mp.spawn(_two_gpu_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_two_gpu_rank, args=(2, _free_port(), str(tmp_path), chunks), nprocs=2, join=True)
     recv = 0
     for r in range(2):
         d = np.load(tmp_path / f"r{r}.npz")
