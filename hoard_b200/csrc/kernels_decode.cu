@@ -37,6 +37,8 @@ constexpr int DEC_TRACE_PHASES = 20;
 constexpr int NCH = 4;                                   // gate/up arrival chunks
 constexpr int RACC_COPIES = 8;                           // router accumulators spread over copies
 constexpr unsigned long long WAIT_NS = 2000000000ull;   // 2 s bound on any wait
+constexpr int HREADY_OFF = 64;         // h block readiness counters: sync word HREADY_OFF + HREADY_STRIDE * b
+constexpr int HREADY_STRIDE = 32;      // one 128-byte line per counter (pollers of different blocks do not share)
 
 __device__ __forceinline__ unsigned long long gtimer() {
     unsigned long long t;
@@ -120,6 +122,24 @@ __device__ bool grid_barrier(unsigned* sync, unsigned n, int* s_ok, unsigned lon
     }
     __syncthreads();
     return *s_ok != 0;
+}
+
+// Bounded wait until the counter reaches `target` (relaxed polls, then an acquire fence); false if
+// the bound expired or another CTA has given up.
+__device__ bool wait_count(const unsigned* cnt, unsigned target, unsigned* sync) {
+    if ((int)(ld_relaxed(cnt) - target) < 0) {
+        const unsigned long long t0 = gtimer();
+        for (unsigned it = 1;; ++it) {
+            __nanosleep(64);
+            if ((int)(ld_relaxed(cnt) - target) >= 0) break;
+            if ((it & 15) == 0) {
+                if (ld_relaxed(&sync[0]) & 2u) return false;
+                if (gtimer() - t0 > WAIT_NS) { atomicOr(&sync[0], 2u); return false; }
+            }
+        }
+    }
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    return true;
 }
 
 inline __host__ __device__ int64_t a16(int64_t v) { return (v + 15) & ~(int64_t)15; }
@@ -343,6 +363,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
     __shared__ int s_sel[16];
     __shared__ float s_w[16];
     __shared__ int s_ok;
+    __shared__ int s_pos_ok[16];           // per expert position: its h blocks were seen ready
     __shared__ int4 s_cd_gu[32];           // gate/up copy descriptors: [NCH chunks][2 segments][4 planes]
     __shared__ int4 s_cd_dn[2][64];        // down copy descriptors per type (Q4_K, Q6_K): [k][planes]
     __shared__ unsigned s_gu_bytes[NCH];
@@ -360,6 +381,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
     const int nr = d1 - d0;
     const int racc_stride = RACC_COPIES * (E + 1);
     R* x = reinterpret_cast<R*>(a.x);
+    unsigned* hready = a.sync + HREADY_OFF;   // readiness counter of block b of h at hready[HREADY_STRIDE * b]
     bool alive = true;
     unsigned nbar = 0;
 #define DEC_TR(layer, ph)                                                                                  \
@@ -548,6 +570,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
                         bulk_g2s(smem + d.z, base + src, meta & 0xFFFFFu, bar_gu + ch);
                     }
                 }
+                // the down rows are needed only after the gate/up phase: issue them once the first
+                // gate/up chunk has landed, so that gate/up bytes are not queued behind them
+                if (!mbar_wait(bar_gu + 1, ph_gu)) { atomicOr(&a.sync[0], 2u); alive = false; }
                 const int tsel = L_dt == T_Q4K ? 0 : 1;
                 const int n_dn = k * (L_dt == T_Q4K ? 2 : 4);
                 for (int ci = lane; ci < n_dn; ci += 32) {
@@ -667,146 +692,188 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
                 if (issued && !mbar_wait(bar_gu + cw, ph_gu)) { atomicOr(&a.sync[0], 2u); alive = false; }
         }
         ph_gu ^= 1;
-        // publish this CTA's block maxima of h (a few atomics per CTA instead of one per row)
+        // publish this CTA's block maxima of h (a few atomics per CTA instead of one per row), then
+        // count this CTA in the readiness counter of every 256-value block of h it produced to
         __syncthreads();
         if (tid < k * nbI) {
             const unsigned v = s_amax[tid];
             if (v) atomicMax(&amax[tid], v);
             s_amax[tid] = 0u;
         }
+        __syncthreads();
+        if (tid == 0 && alive) {
+            asm volatile("fence.acq_rel.gpu;" ::: "memory");
+            for (int b = q0 / QK; b <= (q1 - 1) / QK; ++b)
+                asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(hready + HREADY_STRIDE * b) : "memory");
+        }
         DEC_TR(l, 7);
-        if (!grid_barrier(a.sync, nbar++, &s_ok, DEC_TRP(l, 14))) alive = false;
-        DEC_TR(l, 8);
-        // ---- D. Q8_K of h, down rows of every selected expert, combine, next router sums ---------
+        // ---- D. expert positions are spread over the warps (wpe warps each). A position's warps
+        //      wait until every CTA that produced part of its h has counted itself in, Q8_K that h
+        //      into shared memory and run this CTA's down rows of the expert: no grid barrier, the
+        //      quantisation and down rows of early experts overlap the production of later ones ----
+        int8_t* hq = reinterpret_cast<int8_t*>(smem + P.off_hq);
+        float* hd = reinterpret_cast<float*>(smem + P.off_hd);
+        int* hbs = reinterpret_cast<int*>(smem + P.off_hbs);
+        {
+            float* y = reinterpret_cast<float*>(smem + P.off_y);
+            const int wpe = nw / k;
+            const int j = warp / wpe, wi = warp - j * wpe;
+            if (j < k) {
+                bool ok = alive;
+                if (wi == 0 && lane < nbI && ok) {
+                    // the CTAs owning pairs p0 and p0 + 255 of block (j, lane), and all between
+                    const int64_t p0 = (int64_t)j * I + lane * QK;
+                    const int need = (int)(((p0 + QK) * G - 1) / P_pairs - ((p0 + 1) * G - 1) / P_pairs + 1);
+                    ok = wait_count(hready + HREADY_STRIDE * (j * nbI + lane), (unsigned)(l + 1) * (unsigned)need, a.sync);
+                }
+                if (wpe > 1) {                         // one warp of the position polls; the others follow
+                    if (wi == 0) {
+                        const bool all = __all_sync(0xffffffffu, ok);
+                        if (lane == 0) s_pos_ok[j] = all ? 1 : 0;
+                    }
+                    named_sync(3 + j, 32 * wpe);
+                    ok = ok && s_pos_ok[j] != 0;
+                }
+                ok = __all_sync(0xffffffffu, ok);
+                if (tid == 0) DEC_TR(l, 8);
+                for (int g0 = wi * 32; g0 < I / 16; g0 += wpe * 32) {
+                    const int gg = g0 + lane;
+                    const bool okg = ok && gg < I / 16;
+                    const int eb = 16 * (okg ? gg : 0), blk = eb >> 8, gl = (eb & 255) >> 4;
+                    int bsum = 0;
+                    if (okg) {
+                        const float am = __uint_as_float(__ldcg(amax + j * nbI + blk));
+                        const float iscale = am != 0.f ? 127.f / am : 0.f;
+                        float hv16[16];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float4 t4 = __ldcg(reinterpret_cast<const float4*>(a.h + (int64_t)j * I + eb + 4 * i));
+                            hv16[4 * i] = t4.x; hv16[4 * i + 1] = t4.y; hv16[4 * i + 2] = t4.z; hv16[4 * i + 3] = t4.w;
+                        }
+                        uint32_t packed[4] = {0, 0, 0, 0};
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const int q = am != 0.f ? min(127, __float2int_rn(iscale * hv16[i])) : 0;
+                            bsum += q;
+                            packed[i >> 2] |= ((uint32_t)(q & 0xFF)) << (8 * (i & 3));
+                        }
+                        *reinterpret_cast<uint4*>(hq + j * hq_stride(nbI) + blk * ACT_BLK + (eb & 255)) =
+                            make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                        if (gl == 0) hd[j * nbI + blk] = am != 0.f ? 1.f / iscale : 0.f;
+                    }
+                    const int pair = bsum + __shfl_xor_sync(0xffffffffu, bsum, 1);
+                    if (okg) {
+                        if (L_dt == T_Q6K) {
+                            // 16-sums in unit order [unit v = 2*h2 + r][a]: group gl = 8*h2 + 2*a + r
+                            const int h2 = gl >> 3, aa = (gl >> 1) & 3, rr = gl & 1;
+                            hbs[(j * nbI + blk) * 16 + 4 * (2 * h2 + rr) + aa] = bsum;
+                        } else if ((gl & 1) == 0) {
+                            hbs[(j * nbI + blk) * 8 + (gl >> 1)] = pair;     // 32-sums per sub-block
+                        }
+                    }
+                }
+                if (wpe > 1) named_sync(3 + j, 32 * wpe);
+                else __syncwarp();
+                if (tid == 0) DEC_TR(l, 9);
+                if (issued && ok && !mbar_wait(bar_dn, ph_dn)) { atomicOr(&a.sync[0], 2u); ok = false; }
+                if (tid == 0) DEC_TR(l, 10);
+                // nbI consecutive lanes per row, one per 256-weight block; the lanes of a warp read the
+                // same activation blocks (shared-memory broadcasts) and rotate their chunk order by
+                // lane so that one load instruction spreads over the banks. Block sums of a row are
+                // added as (b0 + b1) + (b2 + b3).
+                const int dsub = L_dt == T_Q6K ? (int)(((int64_t)d0 * nbI * 2) & 15) : 0;
+                const int ipw = 32 / nbI, ui = lane / nbI, bl = lane - ui * nbI;
+                const int rot = lane & 7;
+                for (int gi = wi; gi * ipw < nr; gi += wpe) {
+                    const int r = gi * ipw + ui;
+                    const bool valid = ok && ui < ipw && r < nr;
+                    float acc = 0.f;
+                    if (valid) {
+                        const uint8_t* reg = smem + P.off_dn + (int64_t)j * P.dn_stride;
+                        const int64_t blk = (int64_t)r * nbI + bl;
+                        const int8_t* act = hq + j * hq_stride(nbI) + ACT_BLK * bl;
+                        const float d8 = hd[j * nbI + bl];
+                        if (L_dt == T_Q6K) {
+                            const uint4 S = lds128(reg + P.dn_p2 + blk * 16);
+                            const float d6 = __half2float(__ushort_as_half(
+                                *reinterpret_cast<const unsigned short*>(reg + P.dn_p3 + dsub + blk * 2)));
+                            const int* bsu = hbs + (j * nbI + bl) * 16;
+                            const int sw = rot >> 2;       // half the lanes load the two ql chunks swapped
+                            int isum = 0;
+#pragma unroll
+                            for (int vv = 0; vv < 4; ++vv) {
+                                const int v = (vv + rot) & 3, h2 = v >> 1, rr = v & 1;
+                                const uint8_t* ql = reg + P.dn_p0 + blk * 128 + 64 * h2 + 16 * rr;
+                                const uint4 P0 = lds128(ql + 32 * sw);
+                                const uint4 P1 = lds128(ql + 32 * (sw ^ 1));
+                                const uint4 A = sw ? P1 : P0, B = sw ? P0 : P1;
+                                const uint4 C = lds128(reg + P.dn_p1 + blk * 64 + 32 * h2 + 16 * rr);
+                                const int8_t* a0 = act + 128 * h2 + 16 * rr;
+                                const int4 x0 = lds128i(a0), x1 = lds128i(a0 + 32), x2 = lds128i(a0 + 64),
+                                           x3 = lds128i(a0 + 96);
+                                const int4 bs4 = lds128i(bsu + 4 * v);
+                                const uint32_t Aw[4] = {A.x, A.y, A.z, A.w}, Bw[4] = {B.x, B.y, B.z, B.w};
+                                const uint32_t Cw[4] = {C.x, C.y, C.z, C.w};
+                                const int xa0[4] = {x0.x, x0.y, x0.z, x0.w}, xa1[4] = {x1.x, x1.y, x1.z, x1.w};
+                                const int xa2[4] = {x2.x, x2.y, x2.z, x2.w}, xa3[4] = {x3.x, x3.y, x3.z, x3.w};
+                                int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+#pragma unroll
+                                for (int i = 0; i < 4; ++i) {
+                                    const uint32_t cw = Cw[i];
+                                    s0 = __dp4a((int)((Aw[i] & 0x0F0F0F0Fu) | ((cw << 4) & 0x30303030u)), xa0[i], s0);
+                                    s1 = __dp4a((int)((Bw[i] & 0x0F0F0F0Fu) | ((cw << 2) & 0x30303030u)), xa1[i], s1);
+                                    s2 = __dp4a((int)(((Aw[i] >> 4) & 0x0F0F0F0Fu) | (cw & 0x30303030u)), xa2[i], s2);
+                                    s3 = __dp4a((int)(((Bw[i] >> 4) & 0x0F0F0F0Fu) | ((cw >> 2) & 0x30303030u)), xa3[i], s3);
+                                }
+                                // int8 scales sc[8h2 + rr + 2a]: bytes of word 2h2 (a = 0, 1) and 2h2+1 (a = 2, 3)
+                                const uint32_t wa = h2 ? S.z : S.x, wb = h2 ? S.w : S.y;
+                                const int sh = 8 * rr;
+                                isum += sext8(wa >> sh) * (s0 - 32 * bs4.x) + sext8(wa >> (sh + 16)) * (s1 - 32 * bs4.y) +
+                                        sext8(wb >> sh) * (s2 - 32 * bs4.z) + sext8(wb >> (sh + 16)) * (s3 - 32 * bs4.w);
+                            }
+                            acc = d8 * d6 * (float)isum;
+                        } else {
+                            const uint8_t* wq = reg + P.dn_p0 + blk * 128;
+                            const uint4 hh4 = lds128(reg + P.dn_p1 + blk * 16);
+                            const Q4Scales s4 = q4_scales(hh4);
+                            int isc = 0;
+#pragma unroll
+                            for (int cc = 0; cc < 8; ++cc) {
+                                const int cr = (cc + rot) & 7, g = cr >> 1, hh = cr & 1;
+                                const uint4 w = lds128(wq + 16 * cr);
+                                const int4 alo = lds128i(act + 64 * g + 16 * hh);
+                                const int4 ahi = lds128i(act + 64 * g + 32 + 16 * hh);
+                                isc += q4_chunk(w, alo, ahi, byte_of(s4.sc_lo, s4.sc_hi, 2 * g),
+                                                byte_of(s4.sc_lo, s4.sc_hi, 2 * g + 1));
+                            }
+                            const int mn = q4_min_dot(s4, hbs + (j * nbI + bl) * 8);
+                            const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hh4.x));
+                            acc = d8 * (dm.x * (float)isc - dm.y * (float)mn);
+                        }
+                    }
+                    const float t1 = __shfl_down_sync(0xffffffffu, acc, 1);
+                    const float t2 = __shfl_down_sync(0xffffffffu, acc, 2);
+                    const float t3 = __shfl_down_sync(0xffffffffu, acc, 3);
+                    float sum = acc;
+                    if (nbI == 2) sum = acc + t1;
+                    else if (nbI == 3) sum = (acc + t1) + t2;
+                    else if (nbI == 4) sum = (acc + t1) + (t2 + t3);
+                    if (valid && bl == 0) y[r * k + j] = sum;
+                }
+                if (!ok) alive = false;
+            }
+        }
+        ph_dn ^= 1;
+        __syncthreads();
+        DEC_TR(l, 11);
+        // every CTA has published its h, so every CTA has read this layer's router sums: clear them
+        // for layer l + 2, and the block maxima that layer l + 1 will use
         if (c == 0 && alive) {
             double* rz = a.racc + (int64_t)buf * racc_stride;
             for (int e = tid; e < racc_stride; e += blockDim.x) rz[e] = 0.0;
             unsigned* az = a.amax + (int64_t)(buf ^ 1) * k * nbI;
             for (int e = tid; e < k * nbI; e += blockDim.x) az[e] = 0u;
         }
-        int8_t* hq = reinterpret_cast<int8_t*>(smem + P.off_hq);
-        float* hd = reinterpret_cast<float*>(smem + P.off_hd);
-        int* hbs = reinterpret_cast<int*>(smem + P.off_hbs);
-        for (int g0 = 0; g0 < k * I / 16; g0 += blockDim.x) {
-            const int g = g0 + tid;
-            const bool ok = g < k * I / 16;
-            const int e0 = 16 * (ok ? g : 0);
-            const int j = e0 / I, eb = e0 - j * I, blk = eb >> 8, gl = (eb & 255) >> 4;
-            int bsum = 0;
-            if (ok) {
-                const float am = __uint_as_float(__ldcg(amax + j * nbI + blk));
-                const float iscale = am != 0.f ? 127.f / am : 0.f;
-                float hv16[16];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float4 t4 = __ldcg(reinterpret_cast<const float4*>(a.h + e0 + 4 * i));
-                    hv16[4 * i] = t4.x; hv16[4 * i + 1] = t4.y; hv16[4 * i + 2] = t4.z; hv16[4 * i + 3] = t4.w;
-                }
-                uint32_t packed[4] = {0, 0, 0, 0};
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int q = am != 0.f ? min(127, __float2int_rn(iscale * hv16[i])) : 0;
-                    bsum += q;
-                    packed[i >> 2] |= ((uint32_t)(q & 0xFF)) << (8 * (i & 3));
-                }
-                *reinterpret_cast<uint4*>(hq + j * hq_stride(nbI) + blk * ACT_BLK + (eb & 255)) =
-                    make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                if (gl == 0) hd[j * nbI + blk] = am != 0.f ? 1.f / iscale : 0.f;
-            }
-            const int pair = bsum + __shfl_xor_sync(0xffffffffu, bsum, 1);
-            if (ok) {
-                if (L_dt == T_Q6K) {
-                    // 16-sums in unit order [unit v = 2*h2 + r][a]: group gl = 8*h2 + 2*a + r
-                    const int h2 = gl >> 3, aa = (gl >> 1) & 3, rr = gl & 1;
-                    hbs[(j * nbI + blk) * 16 + 4 * (2 * h2 + rr) + aa] = bsum;
-                } else if ((gl & 1) == 0) {
-                    hbs[(j * nbI + blk) * 8 + (gl >> 1)] = pair;     // 32-sums per sub-block
-                }
-            }
-        }
-        __syncthreads();
-        DEC_TR(l, 9);
-        {
-            // four lanes per (row, expert) item, one per 256-weight block of the row (nbI <= 4)
-            float* y = reinterpret_cast<float*>(smem + P.off_y);
-            const int dsub = L_dt == T_Q6K ? (int)(((int64_t)d0 * nbI * 2) & 15) : 0;
-            const int bl = lane & 3;
-            const int items = nr * k, ngi = (items + 7) / 8;
-            if (issued && !mbar_wait(bar_dn, ph_dn)) { atomicOr(&a.sync[0], 2u); alive = false; }
-            DEC_TR(l, 10);
-            for (int gi = warp; gi < ngi; gi += nw) {
-                const int it = gi * 8 + (lane >> 2);
-                const bool valid = alive && it < items && bl < nbI;
-                const int r = valid ? it / k : 0, j = valid ? it - r * k : 0;
-                float acc = 0.f;
-                if (valid) {
-                    const uint8_t* reg = smem + P.off_dn + (int64_t)j * P.dn_stride;
-                    const int64_t blk = (int64_t)r * nbI + bl;
-                    const int8_t* act = hq + j * hq_stride(nbI) + ACT_BLK * bl;
-                    const float d8 = hd[j * nbI + bl];
-                    const int rot = (it + bl) & 7;
-                    if (L_dt == T_Q6K) {
-                        const uint4 S = lds128(reg + P.dn_p2 + blk * 16);
-                        const float d6 = __half2float(__ushort_as_half(
-                            *reinterpret_cast<const unsigned short*>(reg + P.dn_p3 + dsub + blk * 2)));
-                        const int* bsu = hbs + (j * nbI + bl) * 16;
-                        int isum = 0;
-#pragma unroll
-                        for (int vv = 0; vv < 4; ++vv) {
-                            const int v = (vv + rot) & 3, h2 = v >> 1, rr = v & 1;
-                            const uint4 A = lds128(reg + P.dn_p0 + blk * 128 + 64 * h2 + 16 * rr);
-                            const uint4 B = lds128(reg + P.dn_p0 + blk * 128 + 64 * h2 + 32 + 16 * rr);
-                            const uint4 C = lds128(reg + P.dn_p1 + blk * 64 + 32 * h2 + 16 * rr);
-                            const int8_t* a0 = act + 128 * h2 + 16 * rr;
-                            const int4 x0 = lds128i(a0), x1 = lds128i(a0 + 32), x2 = lds128i(a0 + 64), x3 = lds128i(a0 + 96);
-                            const int4 bs4 = lds128i(bsu + 4 * v);
-                            const uint32_t Aw[4] = {A.x, A.y, A.z, A.w}, Bw[4] = {B.x, B.y, B.z, B.w};
-                            const uint32_t Cw[4] = {C.x, C.y, C.z, C.w};
-                            const int xa0[4] = {x0.x, x0.y, x0.z, x0.w}, xa1[4] = {x1.x, x1.y, x1.z, x1.w};
-                            const int xa2[4] = {x2.x, x2.y, x2.z, x2.w}, xa3[4] = {x3.x, x3.y, x3.z, x3.w};
-                            int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
-#pragma unroll
-                            for (int i = 0; i < 4; ++i) {
-                                const uint32_t cw = Cw[i];
-                                s0 = __dp4a((int)((Aw[i] & 0x0F0F0F0Fu) | ((cw << 4) & 0x30303030u)), xa0[i], s0);
-                                s1 = __dp4a((int)((Bw[i] & 0x0F0F0F0Fu) | ((cw << 2) & 0x30303030u)), xa1[i], s1);
-                                s2 = __dp4a((int)(((Aw[i] >> 4) & 0x0F0F0F0Fu) | (cw & 0x30303030u)), xa2[i], s2);
-                                s3 = __dp4a((int)(((Bw[i] >> 4) & 0x0F0F0F0Fu) | ((cw >> 2) & 0x30303030u)), xa3[i], s3);
-                            }
-                            // int8 scales sc[8h2 + rr + 2a]: bytes of word 2h2 (a = 0, 1) and 2h2+1 (a = 2, 3)
-                            const uint32_t wa = h2 ? S.z : S.x, wb = h2 ? S.w : S.y;
-                            const int sh = 8 * rr;
-                            isum += sext8(wa >> sh) * (s0 - 32 * bs4.x) + sext8(wa >> (sh + 16)) * (s1 - 32 * bs4.y) +
-                                    sext8(wb >> sh) * (s2 - 32 * bs4.z) + sext8(wb >> (sh + 16)) * (s3 - 32 * bs4.w);
-                        }
-                        acc = d8 * d6 * (float)isum;
-                    } else {
-                        const uint8_t* wq = reg + P.dn_p0 + blk * 128;
-                        const uint4 hh4 = lds128(reg + P.dn_p1 + blk * 16);
-                        const Q4Scales s4 = q4_scales(hh4);
-                        int isc = 0;
-#pragma unroll
-                        for (int cc = 0; cc < 8; ++cc) {
-                            const int cr = (cc + rot) & 7, g = cr >> 1, hh = cr & 1;
-                            const uint4 w = lds128(wq + 16 * cr);
-                            const int4 alo = lds128i(act + 64 * g + 16 * hh);
-                            const int4 ahi = lds128i(act + 64 * g + 32 + 16 * hh);
-                            isc += q4_chunk(w, alo, ahi, byte_of(s4.sc_lo, s4.sc_hi, 2 * g),
-                                            byte_of(s4.sc_lo, s4.sc_hi, 2 * g + 1));
-                        }
-                        const int mn = q4_min_dot(s4, hbs + (j * nbI + bl) * 8);
-                        const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hh4.x));
-                        acc = d8 * (dm.x * (float)isc - dm.y * (float)mn);
-                    }
-                }
-                acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-                acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-                if (valid && bl == 0) y[r * k + j] = acc;
-            }
-        }
-        ph_dn ^= 1;
-        __syncthreads();
-        DEC_TR(l, 11);
         {
             const float* y = reinterpret_cast<const float*>(smem + P.off_y);
             for (int r = tid; r < nr; r += blockDim.x) {
@@ -848,6 +915,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
             __threadfence();
             unsigned* az = a.amax + (int64_t)((a.n_layers - 1) & 1) * k * nbI;
             for (int e = 0; e < k * nbI; ++e) az[e] = 0u;
+            for (int e = 0; e < k * nbI; ++e) hready[HREADY_STRIDE * e] = 0u;
             a.sync[1] = 0u;
             a.sync[2] = 0u;
             __threadfence();
@@ -939,7 +1007,7 @@ constexpr int NOALLOC_MAX_E = 512;      // experts per layer
 constexpr size_t NOALLOC_H_BYTES = (size_t)NOALLOC_MAX_K * NOALLOC_MAX_I * 4;                  // 64 KiB
 constexpr size_t NOALLOC_AMAX_BYTES = 2 * NOALLOC_MAX_K * (NOALLOC_MAX_I / QK) * 4;           // 512 B
 constexpr size_t NOALLOC_RACC_BYTES = (size_t)2 * RACC_COPIES * (NOALLOC_MAX_E + 1) * 8;       // 65,664 B
-constexpr size_t NOALLOC_SYNC_BYTES = 256;
+constexpr size_t NOALLOC_SYNC_BYTES = 8704;          // error word, barrier words, h block counters (one line each)
 constexpr size_t NOALLOC_ZERO_BYTES = NOALLOC_AMAX_BYTES + NOALLOC_RACC_BYTES + NOALLOC_SYNC_BYTES;
 constexpr size_t NOALLOC_BYTES = NOALLOC_H_BYTES + NOALLOC_ZERO_BYTES;                         // ~130 KiB
 static __device__ __align__(256) unsigned char g_decode_scratch[NOALLOC_BYTES];

@@ -266,7 +266,7 @@ int hoard_moe_create(const hoard_moe_desc* d, hoard_moe_ctx** out) {
     const int64_t amax_rows = std::max<int64_t>(T, 2) * KK;   // >= 2 layer buffers of k rows
     if (rc == HOARD_OK) rc = dalloc(c, &s.amax, amax_rows * (I / 256) * 4);
     if (rc == HOARD_OK) rc = dalloc(c, &s.partials, (int64_t)4096 * 1024 * 4);
-    if (rc == HOARD_OK) rc = dalloc(c, &s.sync, 1024 * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &s.sync, 4096 * 4);
     if (rc == HOARD_OK) rc = dalloc(c, &s.xq16, T * H * 2);
     if (rc == HOARD_OK) rc = dalloc(c, &s.hq16, T * KK * I * 2);
     if (rc == HOARD_OK) rc = dalloc(c, &s.items, tc_max_items((int)T, (int)KK, d->n_slots) * (int64_t)sizeof(int2));
@@ -277,7 +277,7 @@ int hoard_moe_create(const hoard_moe_desc* d, hoard_moe_ctx** out) {
     if (rc == HOARD_OK) rc = dalloc(c, &c->staging, max_raw);
     c->staging_bytes = max_raw;
     if (rc == HOARD_OK) {
-        e = cudaMemset(s.sync, 0, 1024 * 4);
+        e = cudaMemset(s.sync, 0, 4096 * 4);
         if (e == cudaSuccess) e = cudaMemset(s.amax, 0, amax_rows * (I / 256) * 4);
         if (e == cudaSuccess) e = cudaMemset(s.dcount, 0, (size_t)(d->n_slots + 2) * 4);
         if (e == cudaSuccess) e = cudaMemset(s.partials, 0, (size_t)4096 * 1024 * 4);
