@@ -25,7 +25,7 @@
 namespace hoard {
 
 constexpr int QK = 256;
-enum : int { T_F32 = 0, T_Q4K = 12, T_Q6K = 14, T_BF16 = 30 };
+enum : int { T_F32 = 0, T_F16 = 1, T_Q4K = 12, T_Q6K = 14, T_BF16 = 30 };
 
 __host__ __device__ inline int block_bytes(int type) { return type == T_Q4K ? 144 : (type == T_Q6K ? 210 : 0); }
 __host__ __device__ inline int64_t mat_bytes(int type, int64_t n, int64_t k) { return n * (k / QK) * block_bytes(type); }

@@ -1,0 +1,91 @@
+// harness_api.cpp -- the C ABI of include/hoard_harness.h: argument checks and launches of the
+// per-token decode-step operations (kernels_harness.cu). Stateless; status codes as hoard_moe.h.
+#include "../../include/hoard_harness.h"
+#include "kernels.h"
+
+#include <cuda_runtime.h>
+
+using namespace hoard;
+
+namespace {
+
+inline int64_t al256(int64_t v) { return (v + 255) / 256 * 256; }
+inline bool quant_type(int t) { return t == HOARD_TYPE_Q4_K || t == HOARD_TYPE_Q6_K; }
+inline int st(cudaError_t e) {
+    if (e == cudaSuccess) return HOARD_OK;
+    cudaGetLastError();
+    return e == cudaErrorInvalidValue ? HOARD_EINVAL : HOARD_ECUDA;
+}
+
+}  // namespace
+
+extern "C" {
+
+int hoard_hx_repack(int type, const void* src, void* dst, int64_t n_blocks, hoard_stream stream) {
+    if (!quant_type(type) || !src || !dst || n_blocks <= 0) return HOARD_EINVAL;
+    return st(launch_repack(type, static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), n_blocks,
+                            (cudaStream_t)stream));
+}
+
+int hoard_hx_embed(int type, const void* table, int n_embd, int64_t n_vocab, const int32_t* token, float* x_out,
+                   hoard_stream stream) {
+    if (!table || !token || !x_out || n_embd <= 0 || n_vocab <= 0) return HOARD_EINVAL;
+    if (!(type == HOARD_TYPE_F32 || type == 1 || quant_type(type))) return HOARD_EINVAL;
+    if (quant_type(type) && n_embd % 256) return HOARD_EINVAL;
+    return st(launch_embed(type, static_cast<const uint8_t*>(table), n_embd, n_vocab, token, x_out,
+                           (cudaStream_t)stream));
+}
+
+int hoard_hx_rmsnorm(const float* x, int rows, int cols, float eps, const float* w, float* out, hoard_stream stream) {
+    if (!x || !w || !out || rows <= 0 || cols <= 0 || cols > 8192) return HOARD_EINVAL;
+    return st(launch_rmsnorm_f32(x, rows, cols, eps, w, out, (cudaStream_t)stream));
+}
+
+int64_t hoard_hx_q8_bytes(int K) {
+    if (K <= 0 || K % 256) return -1;
+    return al256(K) + al256((int64_t)K / 256 * 4) + al256((int64_t)K / 16 * 4);
+}
+
+int hoard_hx_quant_q8(const float* x, int K, void* q8, hoard_stream stream) {
+    if (!x || !q8 || K <= 0 || K % 256) return HOARD_EINVAL;
+    uint8_t* b = static_cast<uint8_t*>(q8);
+    return st(launch_quant_q8(x, 1, K, reinterpret_cast<int8_t*>(b), reinterpret_cast<float*>(b + al256(K)),
+                              reinterpret_cast<int*>(b + al256(K) + al256((int64_t)K / 256 * 4)),
+                              (cudaStream_t)stream));
+}
+
+int hoard_hx_gemv(int type, const void* w_plane, int N, int K, const void* q8, const float* resid, float* y,
+                  hoard_stream stream) {
+    if (!quant_type(type) || !w_plane || !q8 || !y || N <= 0 || K <= 0 || K % 256) return HOARD_EINVAL;
+    const uint8_t* b = static_cast<const uint8_t*>(q8);
+    return st(launch_qgemv(type, static_cast<const uint8_t*>(w_plane), N, K, reinterpret_cast<const int8_t*>(b),
+                           reinterpret_cast<const float*>(b + al256(K)),
+                           reinterpret_cast<const int*>(b + al256(K) + al256((int64_t)K / 256 * 4)), resid, y,
+                           (cudaStream_t)stream));
+}
+
+int hoard_hx_rope_store(float* q, float* k, const float* v, int n_head, int n_head_kv, int head_dim, int pos,
+                        float freq_base, void* k_cache, void* v_cache, hoard_stream stream) {
+    if (!q || !k || !v || !k_cache || !v_cache || n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv ||
+        head_dim <= 0 || head_dim % 2 || pos < 0 || !(freq_base > 0))
+        return HOARD_EINVAL;
+    return st(launch_rope_store(q, k, v, n_head, n_head_kv, head_dim, pos, freq_base, static_cast<__half*>(k_cache),
+                                static_cast<__half*>(v_cache), (cudaStream_t)stream));
+}
+
+int hoard_hx_attention(const float* q, const void* k_cache, const void* v_cache, int n_head, int n_head_kv,
+                       int head_dim, int n_pos, float scale, float* out, hoard_stream stream) {
+    if (!q || !k_cache || !v_cache || !out || n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv ||
+        head_dim <= 0 || head_dim > 256 || 256 % head_dim || n_pos <= 0)
+        return HOARD_EINVAL;
+    if (attention_smem(head_dim, n_pos) > 200 * 1024) return HOARD_EINVAL;
+    return st(launch_attention(q, static_cast<const __half*>(k_cache), static_cast<const __half*>(v_cache), n_head,
+                               n_head_kv, head_dim, n_pos, scale, out, (cudaStream_t)stream));
+}
+
+int hoard_hx_argmax(const float* v, int n, int32_t* out, hoard_stream stream) {
+    if (!v || !out || n <= 0) return HOARD_EINVAL;
+    return st(launch_argmax(v, n, out, (cudaStream_t)stream));
+}
+
+}  // extern "C"

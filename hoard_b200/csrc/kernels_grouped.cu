@@ -718,6 +718,19 @@ __global__ void __launch_bounds__(512) k_disp_scatter(const int32_t* __restrict_
     }
 }
 
+cudaError_t launch_rmsnorm_f32(const float* x, int rows, int cols, float eps, const float* w, float* out,
+                               cudaStream_t s) {
+    if (rows <= 0 || cols <= 0 || cols > 256 * RMS_MAXV) return cudaErrorInvalidValue;
+    k_rmsnorm<float><<<rows, 256, 0, s>>>(x, cols, eps, w, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quant_q8(const float* x, int rows, int K, int8_t* q, float* d, int* bs, cudaStream_t s) {
+    if (rows <= 0 || K <= 0 || K % QK) return cudaErrorInvalidValue;
+    k_quant_q8<<<(unsigned)((int64_t)(K / QK) * rows), 256, 0, s>>>(x, K, q, d, bs);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_dispatch(const int32_t* slot_of_sel, int T, int k, int KK, int n_slots, const Scratch& sc,
                             int tile_m, cudaStream_t s, int* launches, bool skip_neg) {
     const int NS = n_slots + (KK > k ? 1 : 0);

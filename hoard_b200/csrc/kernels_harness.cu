@@ -1,0 +1,245 @@
+// kernels_harness.cu -- the per-token operations around the MoE layers of a decode step, i.e. hoard's
+// graph E / graph A attention / head (src/run_moe_stream.cpp:302-351, :452-472): embedding row,
+// RMSNorm over rows, Q8_K of an activation vector, quantised projection GEMV (the same exact
+// Q4_K / Q6_K . Q8_K integer dots as the expert path, on plane-layout weights), NEOX RoPE with the
+// KV-cache store, single-query attention over an f16 KV cache, argmax.
+#include "common.cuh"
+#include "kernels.h"
+#include "block_ops.cuh"
+
+#include <cuda_fp16.h>
+
+namespace hoard {
+
+namespace {
+
+// ---- embedding: one row of a raw GGUF table (Q4_K / Q6_K blocks, f32 or f16) to f32 ----
+__global__ void __launch_bounds__(256) k_embed(int type, const uint8_t* __restrict__ table, int H, int64_t n_vocab,
+                                               const int32_t* __restrict__ tok, float* __restrict__ out) {
+    const int nb = H / QK;
+    const int64_t token = *tok;
+    const bool ok = token >= 0 && token < n_vocab;     // an id out of range gives a zero row
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x) {
+        float v;
+        if (!ok) {
+            v = 0.f;
+        } else if (type == T_F32) {
+            v = reinterpret_cast<const float*>(table)[token * H + i];
+        } else if (type == T_F16) {
+            v = __half2float(reinterpret_cast<const __half*>(table)[token * H + i]);
+        } else if (type == T_Q4K) {
+            // block: fp16 d | fp16 dmin | 12 bytes of 6-bit scales/mins | 128 bytes of 4-bit values;
+            // value j of a block: 64-value group j/64, low nibble for j%64 < 32, sub-block j/32
+            const uint8_t* b = table + (token * nb + i / QK) * 144;
+            const int j = i % QK, g = j / 64, l = j % 32, is = j / 32;
+            const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(b)));
+            const float dmin = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(b + 2)));
+            const uint8_t* s = b + 4;
+            int sc, m;
+            if (is < 4) {
+                sc = s[is] & 63;
+                m = s[is + 4] & 63;
+            } else {
+                sc = (s[is + 4] & 0xF) | ((s[is - 4] >> 6) << 4);
+                m = (s[is + 4] >> 4) | ((s[is] >> 6) << 4);
+            }
+            const uint8_t qb = b[16 + 32 * g + l];
+            const int q = (j % 64) < 32 ? (qb & 0xF) : (qb >> 4);
+            v = (d * (float)sc) * (float)q - dmin * (float)m;
+        } else {
+            // block: 128 bytes low 4 bits | 64 bytes high 2 bits | 16 int8 scales | fp16 d; value j:
+            // half n = j/128, within it l = j%32 and quarter a = (j%128)/32
+            const uint8_t* b = table + (token * nb + i / QK) * 210;
+            const int j = i % QK, n = j / 128, a = (j % 128) / 32, l = j % 32;
+            const uint8_t* ql = b + 64 * n;
+            const uint8_t* qh = b + 128 + 32 * n;
+            const int8_t* sc = reinterpret_cast<const int8_t*>(b + 192) + 8 * n;
+            const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(b + 208)));
+            const int lo = (a & 1) ? ql[l + 32] : ql[l];
+            const int low4 = (a < 2) ? (lo & 0xF) : (lo >> 4);
+            const int hi2 = (qh[l] >> (2 * a)) & 3;
+            const int q = (low4 | (hi2 << 4)) - 32;
+            v = (d * (float)sc[l / 16 + 2 * a]) * (float)q;
+        }
+        out[i] = v;
+    }
+}
+
+// ---- y[n] = W[n] . Q8_K(x) (+ resid[n]): one warp per output row ----
+template <int TYPE>
+__global__ void __launch_bounds__(256) k_qgemv(const uint8_t* __restrict__ w, int N, int K,
+                                               const int8_t* __restrict__ xq, const float* __restrict__ xd,
+                                               const int* __restrict__ xbs, const float* __restrict__ resid,
+                                               float* __restrict__ y) {
+    const int lane = threadIdx.x & 31;
+    const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (n >= N) return;
+    const int nb = K / QK;
+    const ActRow a{xq, xd, xbs};
+    float v = warp_sum(row_dot_lane<TYPE>(w, (int64_t)N * nb, n, nb, a, lane));
+    if (lane == 0) y[n] = resid ? v + resid[n] : v;
+}
+
+// ---- NEOX RoPE of q [n_head][hd] and k [n_kv][hd] in place at position pos, then k and v stored
+//      as f16 into the caches at [pos][kv head][hd]. theta_i = pos * base^(-2i/hd) formed by
+//      repeated multiplication, as ggml's rope cache does ----
+__global__ void __launch_bounds__(256) k_rope_store(float* __restrict__ q, float* __restrict__ k,
+                                                    const float* __restrict__ v, int n_head, int n_kv, int hd,
+                                                    int pos, float theta_scale, __half* __restrict__ kc,
+                                                    __half* __restrict__ vc) {
+    const int half = hd / 2;
+    const int n_pairs = (n_head + n_kv) * half;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n_pairs; t += gridDim.x * blockDim.x) {
+        const int head = t / half, i = t - head * half;
+        float theta = (float)pos;
+        for (int s = 0; s < i; ++s) theta *= theta_scale;
+        const float c = cosf(theta), sn = sinf(theta);
+        float* x = head < n_head ? q + (int64_t)head * hd : k + (int64_t)(head - n_head) * hd;
+        const float x0 = x[i], x1 = x[i + half];
+        const float r0 = x0 * c - x1 * sn, r1 = x0 * sn + x1 * c;
+        x[i] = r0;
+        x[i + half] = r1;
+        if (head >= n_head) {
+            const int64_t o = ((int64_t)pos * n_kv + (head - n_head)) * hd;
+            kc[o + i] = __float2half_rn(r0);
+            kc[o + i + half] = __float2half_rn(r1);
+        }
+    }
+    const int nv = n_kv * hd;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < nv; t += gridDim.x * blockDim.x)
+        vc[(int64_t)pos * nv + t] = __float2half_rn(v[t]);
+}
+
+// ---- single-query attention: one CTA per head; scores over the n_pos cached keys of its KV head
+//      (f16, products and sums in f32), softmax with the max subtracted and a double sum, then the
+//      probability-weighted sum of the cached values ----
+constexpr int ATT_THREADS = 256;
+__global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restrict__ q, const __half* __restrict__ kc,
+                                                          const __half* __restrict__ vc, int n_head, int n_kv, int hd,
+                                                          int n_pos, float scale, float* __restrict__ out) {
+    extern __shared__ float sm[];
+    float* sq = sm;                  // [hd]
+    float* sp = sm + hd;             // [n_pos] scores, then probabilities
+    float* part = sp + n_pos;        // [ATT_THREADS / hd][hd] partial output sums
+    __shared__ float redf[32];
+    __shared__ double redd[32];
+    const int h = blockIdx.x, kvh = h / (n_head / n_kv);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) sq[i] = q[(int64_t)h * hd + i];
+    __syncthreads();
+    for (int j = warp; j < n_pos; j += nw) {
+        const __half* kr = kc + ((int64_t)j * n_kv + kvh) * hd;
+        float s = 0.f;
+        for (int i = lane; i < hd; i += 32) s += sq[i] * __half2float(kr[i]);
+        s = warp_sum(s);
+        if (lane == 0) sp[j] = s * scale;
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int j = threadIdx.x; j < n_pos; j += blockDim.x) mx = fmaxf(mx, sp[j]);
+    mx = block_max_f(mx, redf);
+    double sum = 0.0;
+    for (int j = threadIdx.x; j < n_pos; j += blockDim.x) {
+        const float e = expf(sp[j] - mx);
+        sp[j] = e;
+        sum += (double)e;
+    }
+    sum = block_sum_d(sum, redd);
+    const float inv = (float)(1.0 / sum);
+    __syncthreads();
+    // thread = (position group g, dimension i); groups take positions j = g, g + G, ...
+    const int G = blockDim.x / hd;
+    if (threadIdx.x < G * hd) {
+        const int g = threadIdx.x / hd, i = threadIdx.x - g * hd;
+        float acc = 0.f;
+        for (int j = g; j < n_pos; j += G) acc += (sp[j] * inv) * __half2float(vc[((int64_t)j * n_kv + kvh) * hd + i]);
+        part[g * hd + i] = acc;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+        float acc = 0.f;
+        for (int g = 0; g < G; ++g) acc += part[g * hd + i];
+        out[(int64_t)h * hd + i] = acc;
+    }
+}
+
+// ---- argmax (first index of the maximum) of n floats: one CTA of 1024 threads ----
+__global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ v, int n, int32_t* __restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float x = v[i];
+        if (x > best || (x == best && i < bi)) { best = x; bi = i; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+    __syncthreads();
+    if (warp == 0) {
+        best = lane < (int)(blockDim.x >> 5) ? sv[lane] : -INFINITY;
+        bi = lane < (int)(blockDim.x >> 5) ? si[lane] : 0x7fffffff;
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+        }
+        if (lane == 0) *out = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_embed(int type, const uint8_t* table, int H, int64_t n_vocab, const int32_t* token, float* out,
+                         cudaStream_t s) {
+    k_embed<<<(H + 255) / 256, 256, 0, s>>>(type, table, H, n_vocab, token, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm_rows(const float* x, int rows, int cols, float eps, const float* w, float* out,
+                                cudaStream_t s) {
+    return launch_rmsnorm_f32(x, rows, cols, eps, w, out, s);
+}
+
+cudaError_t launch_qgemv(int type, const uint8_t* w, int N, int K, const int8_t* xq, const float* xd, const int* xbs,
+                         const float* resid, float* y, cudaStream_t s) {
+    const unsigned grid = (unsigned)((N + 7) / 8);
+    if (type == T_Q4K) k_qgemv<T_Q4K><<<grid, 256, 0, s>>>(w, N, K, xq, xd, xbs, resid, y);
+    else k_qgemv<T_Q6K><<<grid, 256, 0, s>>>(w, N, K, xq, xd, xbs, resid, y);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rope_store(float* q, float* k, const float* v, int n_head, int n_kv, int hd, int pos,
+                              float freq_base, __half* kc, __half* vc, cudaStream_t s) {
+    const float theta_scale = powf(freq_base, -2.0f / (float)hd);
+    const int n = (n_head + n_kv) * (hd / 2);
+    k_rope_store<<<(n + 255) / 256, 256, 0, s>>>(q, k, v, n_head, n_kv, hd, pos, theta_scale, kc, vc);
+    return cudaGetLastError();
+}
+
+size_t attention_smem(int hd, int n_pos) {
+    return (size_t)(hd + n_pos + (ATT_THREADS / hd) * hd) * sizeof(float);
+}
+
+cudaError_t launch_attention(const float* q, const __half* kc, const __half* vc, int n_head, int n_kv, int hd,
+                             int n_pos, float scale, float* out, cudaStream_t s) {
+    const size_t smem = attention_smem(hd, n_pos);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    k_attention<<<n_head, ATT_THREADS, smem, s>>>(q, kc, vc, n_head, n_kv, hd, n_pos, scale, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const float* v, int n, int32_t* out, cudaStream_t s) {
+    k_argmax<<<1, 1024, 0, s>>>(v, n, out);
+    return cudaGetLastError();
+}
+
+}  // namespace hoard

@@ -1,0 +1,300 @@
+"""A minimal decode driver around the MoE path: hoard's per-token schedule (src/run_moe_stream.cpp:
+295-472) with every step on the device.
+
+    graph E   x = token_embd[token]                                            (hoard_hx_embed)
+    per layer (graph A, attention part; then the MoE layer):
+              cur = RMSNorm(x) * attn_norm
+              q, k, v = Wq cur, Wk cur, Wv cur          (Q4_K / Q6_K . Q8_K(cur), hoard_hx_gemv)
+              QK RMSNorm: over the whole projection (OLMoE) or per head (Qwen3)
+              NEOX RoPE of q, k at position p; k, v into the f16 KV cache      (hoard_hx_rope_store)
+              att = softmax(q k^T / sqrt(head_dim)) v over positions 0..p     (hoard_hx_attention)
+              ffn_inp = Wo att + x
+              x = ffn_inp + sum_j w_j FFN_j(RMSNorm(ffn_inp) * ffn_norm)       (hoard_moe_layers)
+    head      logits = W_out (RMSNorm(x) * output_norm); next = argmax         (hoard_hx_argmax)
+
+Prompt tokens run through the same step one at a time, as in hoard; generation starts from the
+logits of the last prompt token. Models come from a GGUF file (`DecodeModel.from_gguf`) or from
+seeded tensors generated on the device (`seeded_tensors`, the benchmark configurations' weights:
+N(0, 0.02), Q4_K_M types). The MoE layers use all experts HBM-resident (T = 1: the persistent
+decode kernel)."""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from hoard_b200 import moe, quant
+from hoard_b200.moe import HoardError, _ptr, _stream, lib
+
+Q4_K, Q6_K, F32 = quant.Q4_K, quant.Q6_K, 0
+
+_bound = False
+
+
+def _hx():
+    global _bound
+    L = lib()
+    if not _bound:
+        vp, i32, i64, f32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+        L.hoard_hx_repack.argtypes = [i32, vp, vp, i64, vp]
+        L.hoard_hx_embed.argtypes = [i32, vp, i32, i64, vp, vp, vp]
+        L.hoard_hx_rmsnorm.argtypes = [vp, i32, i32, f32, vp, vp, vp]
+        L.hoard_hx_q8_bytes.argtypes = [i32]
+        L.hoard_hx_q8_bytes.restype = i64
+        L.hoard_hx_quant_q8.argtypes = [vp, i32, vp, vp]
+        L.hoard_hx_gemv.argtypes = [i32, vp, i32, i32, vp, vp, vp, vp]
+        L.hoard_hx_rope_store.argtypes = [vp, vp, vp, i32, i32, i32, i32, f32, vp, vp, vp]
+        L.hoard_hx_attention.argtypes = [vp, vp, vp, i32, i32, i32, i32, f32, vp, vp]
+        L.hoard_hx_argmax.argtypes = [vp, i32, vp, vp]
+        _bound = True
+    return L
+
+
+def _ok(rc: int, what: str):
+    if rc != 0:
+        raise HoardError(rc, f"{what} failed ({lib().hoard_strerror(rc).decode()})")
+
+
+@dataclass
+class ModelConfig:
+    """Hyper-parameters and GGUF tensor types of a seeded model (Q4_K_M: attn q/k/o and the
+    embedding Q4_K, attn v and the lm-head Q6_K, expert gate/up Q4_K, expert down Q6_K on even and
+    Q4_K on odd layers)."""
+    arch: str
+    n_layer: int
+    n_embd: int
+    n_head: int
+    n_head_kv: int
+    head_dim: int
+    n_expert: int
+    n_expert_used: int
+    n_ff: int
+    n_vocab: int
+    freq_base: float
+    eps: float
+    qk_norm: str            # "full" (OLMoE: over the whole projection), "head" (Qwen3) or ""
+    norm_topk: bool
+
+    def down_type(self, il: int) -> int:
+        return Q6_K if il % 2 == 0 else Q4_K
+
+
+C1_OLMOE = ModelConfig("olmoe", 16, 2048, 16, 16, 128, 64, 8, 1024, 50304, 1e4, 1e-5, "full", False)
+C3_QWEN3 = ModelConfig("qwen3moe", 48, 2048, 32, 4, 128, 128, 8, 768, 151936, 1e6, 1e-6, "head", True)
+
+
+def seeded_tensors(cfg: ModelConfig, seed: int, device) -> dict:
+    """Every tensor of a seeded model, named as in hoard's GGUFs, on `device`:
+    name -> (ggml type, ne (GGUF order), tensor: uint8 raw blocks or f32)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    H, hd, E, I = cfg.n_embd, cfg.head_dim, cfg.n_expert, cfg.n_ff
+    nq, nkv = cfg.n_head * hd, cfg.n_head_kv * hd
+
+    def w(n_out, k_in, qt):
+        return quant.quantize(torch.randn(n_out, k_in, generator=g, device=device) * 0.02, qt)
+
+    def norm(n):
+        return (1.0 + 0.1 * torch.randn(n, generator=g, device=device)).float()
+
+    t = {"token_embd.weight": (Q4_K, (H, cfg.n_vocab), w(cfg.n_vocab, H, Q4_K)),
+         "output_norm.weight": (F32, (H,), norm(H)),
+         "output.weight": (Q6_K, (H, cfg.n_vocab), w(cfg.n_vocab, H, Q6_K))}
+    for il in range(cfg.n_layer):
+        b = f"blk.{il}."
+        t[b + "attn_norm.weight"] = (F32, (H,), norm(H))
+        t[b + "attn_q.weight"] = (Q4_K, (H, nq), w(nq, H, Q4_K))
+        t[b + "attn_k.weight"] = (Q4_K, (H, nkv), w(nkv, H, Q4_K))
+        t[b + "attn_v.weight"] = (Q6_K, (H, nkv), w(nkv, H, Q6_K))
+        t[b + "attn_output.weight"] = (Q4_K, (nq, H), w(H, nq, Q4_K))
+        if cfg.qk_norm == "full":
+            t[b + "attn_q_norm.weight"] = (F32, (nq,), norm(nq))
+            t[b + "attn_k_norm.weight"] = (F32, (nkv,), norm(nkv))
+        elif cfg.qk_norm == "head":
+            t[b + "attn_q_norm.weight"] = (F32, (hd,), norm(hd))
+            t[b + "attn_k_norm.weight"] = (F32, (hd,), norm(hd))
+        t[b + "ffn_norm.weight"] = (F32, (H,), norm(H))
+        t[b + "ffn_gate_inp.weight"] = (F32, (H, E), (torch.randn(E, H, generator=g, device=device) * 0.02).float())
+        dt = cfg.down_type(il)
+        t[b + "ffn_gate_exps.weight"] = (Q4_K, (H, I, E), quant.synth_experts(E, I, H, Q4_K, seed * 1000 + 3 * il, device))
+        t[b + "ffn_up_exps.weight"] = (Q4_K, (H, I, E), quant.synth_experts(E, I, H, Q4_K, seed * 1000 + 3 * il + 1, device))
+        t[b + "ffn_down_exps.weight"] = (dt, (I, H, E), quant.synth_experts(E, H, I, dt, seed * 1000 + 3 * il + 2, device))
+    return t
+
+
+def write_gguf(path: str, cfg: ModelConfig, tensors: dict):
+    from hoard_b200 import gguf_io as gi
+    w = gi.GGUFWriter(cfg.arch)
+    a = cfg.arch
+    w.add(f"{a}.block_count", cfg.n_layer)
+    w.add(f"{a}.embedding_length", cfg.n_embd)
+    w.add(f"{a}.attention.head_count", cfg.n_head)
+    w.add(f"{a}.attention.head_count_kv", cfg.n_head_kv)
+    w.add(f"{a}.attention.key_length", cfg.head_dim)
+    w.add(f"{a}.expert_feed_forward_length", cfg.n_ff)
+    w.add(f"{a}.expert_count", cfg.n_expert)
+    w.add(f"{a}.expert_used_count", cfg.n_expert_used)
+    w.add(f"{a}.rope.freq_base", float(cfg.freq_base))
+    w.add(f"{a}.attention.layer_norm_rms_epsilon", float(cfg.eps))
+    for name, (ty, ne, data) in tensors.items():
+        w.add_tensor(name, ne, ty, data.detach().cpu().numpy())
+    w.write(path)
+
+
+def config_from_hparams(hp) -> ModelConfig:
+    return ModelConfig(hp.arch, hp.n_layer, hp.n_embd, hp.n_head, hp.n_head_kv, hp.head_dim, hp.n_expert,
+                       hp.n_expert_used, hp.n_ff, hp.n_vocab, hp.freq_base, hp.eps,
+                       "" if not hp.has_qk_norm else ("head" if hp.qk_perhead else "full"), hp.norm_topk)
+
+
+class DecodeModel:
+    def __init__(self, cfg: ModelConfig, tensors: dict, device: int = 0, max_ctx: int = 512, eos_id: int = -1):
+        """tensors: name -> (ggml type, ne, array or tensor of raw bytes / f32 values), host or device."""
+        self.cfg, self.device, self.max_ctx, self.eos_id = cfg, device, max_ctx, eos_id
+        dev = self.dev = torch.device("cuda", device)
+        _hx()
+        H, hd = cfg.n_embd, cfg.head_dim
+        self.nq, self.nkv = cfg.n_head * hd, cfg.n_head_kv * hd
+
+        def raw(name):
+            ty, ne, data = tensors[name]
+            t = torch.as_tensor(np.asarray(data)) if not isinstance(data, torch.Tensor) else data
+            return ty, t.contiguous().to(dev)
+
+        def plane(name):
+            ty, t = raw(name)
+            out = torch.empty_like(t, dtype=torch.uint8)
+            nblk = t.numel() // quant.row_bytes(ty, 256)
+            _ok(_hx().hoard_hx_repack(ty, _ptr(t), _ptr(out), nblk, _stream(None)), "repack")
+            return ty, out
+
+        def f32(name):
+            ty, t = raw(name)
+            assert ty == F32
+            return t.view(torch.float32) if t.dtype == torch.uint8 else t.float()
+
+        self.embd_type, self.embd = raw("token_embd.weight")
+        self.out_norm = f32("output_norm.weight")
+        self.out_type, self.out_w = plane("output.weight")
+        self.layers = []
+        for il in range(cfg.n_layer):
+            b = f"blk.{il}."
+            L = {"attn_norm": f32(b + "attn_norm.weight"), "q": plane(b + "attn_q.weight"),
+                 "k": plane(b + "attn_k.weight"), "v": plane(b + "attn_v.weight"),
+                 "o": plane(b + "attn_output.weight")}
+            if cfg.qk_norm:
+                L["q_norm"], L["k_norm"] = f32(b + "attn_q_norm.weight"), f32(b + "attn_k_norm.weight")
+            self.layers.append(L)
+        # the MoE layers: all experts resident, T = 1
+        types = [tuple(tensors[f"blk.{il}.ffn_{m}_exps.weight"][0] for m in ("gate", "up", "down"))
+                 for il in range(cfg.n_layer)]
+        self.moe = moe.MoEContext(n_embd=H, n_expert=cfg.n_expert, n_expert_used=cfg.n_expert_used, n_ff=cfg.n_ff,
+                                  n_layer=cfg.n_layer, norm_topk=cfg.norm_topk, eps=cfg.eps,
+                                  gate_types=[t[0] for t in types], up_types=[t[1] for t in types],
+                                  down_types=[t[2] for t in types], max_tokens=1, device=device)
+        for il in range(cfg.n_layer):
+            b = f"blk.{il}."
+            self.moe.set_router(il, f32(b + "ffn_gate_inp.weight").view(cfg.n_expert, H), f32(b + "ffn_norm.weight"))
+            mats = [raw(b + f"ffn_{m}_exps.weight")[1].view(cfg.n_expert, -1) for m in ("gate", "up", "down")]
+            for e in range(cfg.n_expert):
+                self.moe.upload_expert(il, e, mats[0][e], mats[1][e], mats[2][e])
+        # activations, Q8_K workspaces, KV caches, token sequence
+        z = lambda n: torch.zeros(n, dtype=torch.float32, device=dev)
+        self.x, self.x2, self.cur = z(H), z(H), z(H)
+        self.q, self.k, self.v, self.att = z(self.nq), z(self.nkv), z(self.nkv), z(self.nq)
+        self.logits = z(cfg.n_vocab)
+        kq = max(H, self.nq)
+        self.q8 = torch.zeros(int(_hx().hoard_hx_q8_bytes(kq)), dtype=torch.uint8, device=dev)
+        self.kc = torch.zeros(cfg.n_layer, max_ctx, self.nkv, dtype=torch.float16, device=dev)
+        self.vc = torch.zeros_like(self.kc)
+        self.seq = torch.zeros(max_ctx + 1, dtype=torch.int32, device=dev)
+        self.scratch_tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+
+    @classmethod
+    def from_gguf(cls, path: str, device: int = 0, max_ctx: int = 512):
+        from hoard_b200 import gguf_io as gi
+        g = gi.GGUFFile(path)
+        hp = gi.read_hparams(g)
+        tensors = {}
+        for name, t in g.tensors.items():
+            data = g.array(name) if t.type == F32 else g.data(name)
+            tensors[name] = (t.type, t.ne, np.array(data))
+        g.close()
+        return cls(config_from_hparams(hp), tensors, device=device, max_ctx=max_ctx, eos_id=hp.eos_id)
+
+    def close(self):
+        self.moe.close()
+
+    # ---- one token: logits of position pos for token seq[pos]; argmax into `next_tok` ----
+    def step(self, pos: int, next_tok: torch.Tensor, stream=None):
+        c, hx, s = self.cfg, _hx(), _stream(stream)
+        H, hd = c.n_embd, c.head_dim
+        x, x2 = self.x, self.x2
+        _ok(hx.hoard_hx_embed(self.embd_type, _ptr(self.embd), H, c.n_vocab, _ptr(self.seq[pos:pos + 1]), _ptr(x), s),
+            "embed")
+        scale = 1.0 / math.sqrt(hd)
+        for il, L in enumerate(self.layers):
+            _ok(hx.hoard_hx_rmsnorm(_ptr(x), 1, H, c.eps, _ptr(L["attn_norm"]), _ptr(self.cur), s), "rmsnorm")
+            _ok(hx.hoard_hx_quant_q8(_ptr(self.cur), H, _ptr(self.q8), s), "quant")
+            for key, out, n in (("q", self.q, self.nq), ("k", self.k, self.nkv), ("v", self.v, self.nkv)):
+                ty, wt = L[key]
+                _ok(hx.hoard_hx_gemv(ty, _ptr(wt), n, H, _ptr(self.q8), None, _ptr(out), s), "gemv")
+            if c.qk_norm == "full":
+                _ok(hx.hoard_hx_rmsnorm(_ptr(self.q), 1, self.nq, c.eps, _ptr(L["q_norm"]), _ptr(self.q), s), "qnorm")
+                _ok(hx.hoard_hx_rmsnorm(_ptr(self.k), 1, self.nkv, c.eps, _ptr(L["k_norm"]), _ptr(self.k), s), "knorm")
+            elif c.qk_norm == "head":
+                _ok(hx.hoard_hx_rmsnorm(_ptr(self.q), c.n_head, hd, c.eps, _ptr(L["q_norm"]), _ptr(self.q), s), "qnorm")
+                _ok(hx.hoard_hx_rmsnorm(_ptr(self.k), c.n_head_kv, hd, c.eps, _ptr(L["k_norm"]), _ptr(self.k), s),
+                    "knorm")
+            _ok(hx.hoard_hx_rope_store(_ptr(self.q), _ptr(self.k), _ptr(self.v), c.n_head, c.n_head_kv, hd, pos,
+                                       c.freq_base, _ptr(self.kc[il]), _ptr(self.vc[il]), s), "rope")
+            _ok(hx.hoard_hx_attention(_ptr(self.q), _ptr(self.kc[il]), _ptr(self.vc[il]), c.n_head, c.n_head_kv, hd,
+                                      pos + 1, scale, _ptr(self.att), s), "attention")
+            _ok(hx.hoard_hx_quant_q8(_ptr(self.att), self.nq, _ptr(self.q8), s), "quant")
+            ty, wo = L["o"]
+            _ok(hx.hoard_hx_gemv(ty, _ptr(wo), H, self.nq, _ptr(self.q8), _ptr(x), _ptr(x2), s), "gemv")
+            self.moe.layers(il, 1, x2.view(1, H), stream=stream)
+            x, x2 = x2, x
+        self.x, self.x2 = x, x2
+        _ok(hx.hoard_hx_rmsnorm(_ptr(x), 1, H, c.eps, _ptr(self.out_norm), _ptr(self.cur), s), "rmsnorm")
+        _ok(hx.hoard_hx_quant_q8(_ptr(self.cur), H, _ptr(self.q8), s), "quant")
+        _ok(hx.hoard_hx_gemv(self.out_type, _ptr(self.out_w), c.n_vocab, H, _ptr(self.q8), None, _ptr(self.logits), s),
+            "gemv")
+        _ok(hx.hoard_hx_argmax(_ptr(self.logits), c.n_vocab, _ptr(next_tok), s), "argmax")
+
+    def score(self, tokens, first: int, stream=None) -> torch.Tensor:
+        """Teacher-forced logits: runs tokens[0 .. n-2] through the decode step and returns the logits
+        that predict tokens[first .. n-1] ([n - first][vocab])."""
+        n = len(tokens)
+        if not 1 <= first < n or n > self.max_ctx:
+            raise ValueError("need 1 <= first < len(tokens) <= max_ctx")
+        self.seq[:n].copy_(torch.tensor(tokens, dtype=torch.int32))
+        out = torch.empty(n - first, self.cfg.n_vocab, dtype=torch.float32, device=self.dev)
+        for p in range(n - 1):
+            self.step(p, self.scratch_tok, stream)
+            if p >= first - 1:
+                out[p - (first - 1)].copy_(self.logits)
+        self.moe.sync_status(stream)
+        return out
+
+    def generate(self, prompt, n_gen: int, stop_at_eos: bool = False, logits_out: torch.Tensor | None = None,
+                 stream=None):
+        """Greedy decode of n_gen tokens after `prompt` (a list of ids). logits_out [n_gen][vocab], if given,
+        receives the logits each generated token was chosen from. Returns the generated ids."""
+        T = len(prompt)
+        if T < 1 or T + n_gen > self.max_ctx:
+            raise ValueError("prompt + n_gen must fit max_ctx")
+        self.seq[:T].copy_(torch.tensor(prompt, dtype=torch.int32))
+        for p in range(T + n_gen - 1):
+            out = self.seq[p + 1:p + 2] if p >= T - 1 else self.scratch_tok
+            self.step(p, out, stream)
+            if p >= T - 1 and logits_out is not None:
+                logits_out[p - (T - 1)].copy_(self.logits)
+            if stop_at_eos and p >= T - 1 and int(self.seq[p + 1].item()) == self.eos_id:
+                return self.seq[T:p + 2].tolist()
+        self.moe.sync_status(stream)
+        return self.seq[T:T + n_gen].tolist()

@@ -1,0 +1,61 @@
+/* hoard_harness.h -- the per-token operations of a decode step around the MoE layers.
+ *
+ * hoard runs these as ggml graphs on its single backend thread: graph E (embedding row,
+ * src/run_moe_stream.cpp:302-312), graph A's attention part (:320-351: attn RMSNorm, q/k/v
+ * projections, QK RMSNorm over the full projection (OLMoE) or per head (Qwen3), NEOX RoPE, KV-cache
+ * store, single-query attention with softmax scale 1/sqrt(head_dim), output projection plus the
+ * residual) and the head (:452-472: output RMSNorm, lm-head, argmax). These entry points are the
+ * same steps as stateless device operations, so a decode driver keeps hoard's schedule
+ * (graph E -> per layer: attention, then hoard_moe_layer -> head) with every buffer on the device.
+ *
+ * Quantised weights (Q4_K = 12, Q6_K = 14) are used in the plane layout that hoard_hx_repack
+ * produces from raw GGUF blocks; projections quantise the activation to Q8_K first
+ * (hoard_hx_quant_q8) and form exact integer block dots, the semantics of ggml's CPU mul_mat. The KV
+ * cache is f16 [max_ctx][n_head_kv][head_dim] per layer. All pointers are device pointers; every
+ * call is asynchronous on `stream`. Status codes are those of hoard_moe.h. */
+#ifndef HOARD_HARNESS_H
+#define HOARD_HARNESS_H
+
+#include <stdint.h>
+#include "hoard_moe.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Raw GGUF Q4_K / Q6_K blocks (n_blocks of them, rows back to back) -> plane layout (same size). */
+int hoard_hx_repack(int type, const void* src, void* dst, int64_t n_blocks, hoard_stream stream);
+
+/* x_out[n_embd] = row *token of an embedding table (raw GGUF Q4_K / Q6_K blocks, or f32 = 0 / f16 = 1);
+ * token is a device int32 (ggml_get_rows). */
+int hoard_hx_embed(int type, const void* table, int n_embd, int64_t n_vocab, const int32_t* token, float* x_out,
+                   hoard_stream stream);
+
+/* out[r] = x[r] / sqrt(mean(x[r]^2) + eps) * w, rows of `cols` values (cols <= 8192). */
+int hoard_hx_rmsnorm(const float* x, int rows, int cols, float eps, const float* w, float* out, hoard_stream stream);
+
+/* Bytes of the Q8_K workspace of a K-vector: int8 [K] | f32 scales [K/256] | int32 16-sums [K/16]. */
+int64_t hoard_hx_q8_bytes(int K);
+int hoard_hx_quant_q8(const float* x, int K, void* q8, hoard_stream stream);
+
+/* y[N] = W . x (+ resid, elementwise, when non-null): W plane layout, N rows of K, x as Q8_K. */
+int hoard_hx_gemv(int type, const void* w_plane, int N, int K, const void* q8, const float* resid, float* y,
+                  hoard_stream stream);
+
+/* NEOX RoPE of q [n_head][head_dim] and k [n_head_kv][head_dim] (in place) at position pos with
+ * theta_i = pos * freq_base^(-2i/head_dim); then k and v stored as f16 at cache row pos. */
+int hoard_hx_rope_store(float* q, float* k, const float* v, int n_head, int n_head_kv, int head_dim, int pos,
+                        float freq_base, void* k_cache, void* v_cache, hoard_stream stream);
+
+/* out[h] = softmax(scale * q[h] . K[0..n_pos)) . V[0..n_pos) of KV head h / (n_head / n_head_kv). */
+int hoard_hx_attention(const float* q, const void* k_cache, const void* v_cache, int n_head, int n_head_kv,
+                       int head_dim, int n_pos, float scale, float* out, hoard_stream stream);
+
+/* *out = the first index of the maximum of v[0..n). */
+int hoard_hx_argmax(const float* v, int n, int32_t* out, hoard_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,132 @@
+"""CPU restatement of hoard's per-token decode schedule -- TEST INFRASTRUCTURE ONLY (the checker of
+hoard_b200.harness; never imported by the library).
+
+Follows src/run_moe_stream.cpp:295-472 step by step:
+  graph E   embedding row (ggml_get_rows of a Q4_K / Q6_K table: dequantised)          :302-312
+  graph A   RMSNorm(x) * attn_norm                                                   :322
+            q, k, v = ggml_mul_mat(W, cur): Q8_K activation, integer block dots      :323-325
+            QK RMSNorm over the whole projection (OLMoE) or per head (Qwen3)         :326-331
+            NEOX RoPE, theta_i = p * base^(-2i/head_dim) by repeated multiplication :332-333
+            KV cache store, single-query attention, scale 1/sqrt(head_dim),
+            softmax with the max subtracted and a double sum                         :334-347
+            ffn_inp = Wo att + x                                                     :348-349
+  MoE       x = ffn_inp + sum_j w_j FFN_j(RMSNorm(ffn_inp) * ffn_norm) (oracle.moe_layer)
+  head      RMSNorm(x) * output_norm, lm-head, argmax (first maximum)                :452-472
+Two choices follow the configuration rather than the reference (which keeps an f32 cache): the
+KV cache holds f16 (config C1 asks for an fp16 KV cache), and every position, the current one
+included, is read back from it.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from oracle import oracle as orc
+
+
+def rms_norm(x: np.ndarray, w: np.ndarray, rows: int, cols: int, eps: float) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32).reshape(rows, cols)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty_like(x)
+    wb = np.broadcast_to(w, (cols,)).copy() if w.size == cols else w
+    orc.lib().orc_rms_norm(orc._p(x), orc._p(wb), ctypes.c_int(rows), ctypes.c_int(cols), ctypes.c_float(eps),
+                           orc._p(out))
+    return out.reshape(-1)
+
+
+def rope_neox(x: np.ndarray, n_heads: int, hd: int, pos: int, freq_base: float) -> np.ndarray:
+    x = x.reshape(n_heads, hd).astype(np.float32).copy()
+    theta_scale = np.float32(np.float32(freq_base) ** np.float32(-2.0 / hd))
+    half = hd // 2
+    theta = np.empty(half, np.float32)
+    t = np.float32(pos)
+    for i in range(half):
+        theta[i] = t
+        t = np.float32(t * theta_scale)
+    c, s = np.cos(theta).astype(np.float32), np.sin(theta).astype(np.float32)
+    x0, x1 = x[:, :half].copy(), x[:, half:].copy()
+    x[:, :half] = x0 * c - x1 * s
+    x[:, half:] = x0 * s + x1 * c
+    return x.reshape(-1)
+
+
+class OracleDecoder:
+    def __init__(self, cfg, tensors: dict, max_ctx: int):
+        """tensors: name -> (ggml type, ne, numpy raw bytes / f32 values), as the harness takes them."""
+        self.cfg = cfg
+        self.t = {k: (ty, ne, np.asarray(v)) for k, (ty, ne, v) in tensors.items()}
+        hd = cfg.head_dim
+        self.nq, self.nkv = cfg.n_head * hd, cfg.n_head_kv * hd
+        self.kc = np.zeros((cfg.n_layer, max_ctx, self.nkv), np.float16)
+        self.vc = np.zeros_like(self.kc)
+
+    def _mv(self, name, n_out, k_in, x):
+        ty, _, w = self.t[name]
+        return orc.matvec(ty, w.reshape(-1), n_out, k_in, x, orc.MODE_GGML)
+
+    def _f(self, name):
+        return self.t[name][2].reshape(-1).view(np.float32) if self.t[name][2].dtype == np.uint8 else \
+            self.t[name][2].astype(np.float32).reshape(-1)
+
+    def step(self, token: int, pos: int) -> np.ndarray:
+        c = self.cfg
+        H, hd = c.n_embd, c.head_dim
+        ty, _, table = self.t["token_embd.weight"]
+        rb = table.reshape(-1).size // c.n_vocab
+        x = orc.dequant(ty, table.reshape(-1)[token * rb:(token + 1) * rb]) if ty in (12, 14) else \
+            table.reshape(c.n_vocab, H)[token].astype(np.float32)
+        for il in range(c.n_layer):
+            b = f"blk.{il}."
+            cur = rms_norm(x, self._f(b + "attn_norm.weight"), 1, H, c.eps)
+            q = self._mv(b + "attn_q.weight", self.nq, H, cur)
+            k = self._mv(b + "attn_k.weight", self.nkv, H, cur)
+            v = self._mv(b + "attn_v.weight", self.nkv, H, cur)
+            if c.qk_norm == "full":
+                q = rms_norm(q, self._f(b + "attn_q_norm.weight"), 1, self.nq, c.eps)
+                k = rms_norm(k, self._f(b + "attn_k_norm.weight"), 1, self.nkv, c.eps)
+            elif c.qk_norm == "head":
+                q = rms_norm(q, self._f(b + "attn_q_norm.weight"), c.n_head, hd, c.eps)
+                k = rms_norm(k, self._f(b + "attn_k_norm.weight"), c.n_head_kv, hd, c.eps)
+            q = rope_neox(q, c.n_head, hd, pos, c.freq_base)
+            k = rope_neox(k, c.n_head_kv, hd, pos, c.freq_base)
+            self.kc[il, pos] = k.astype(np.float16)
+            self.vc[il, pos] = v.astype(np.float16)
+            K = self.kc[il, :pos + 1].astype(np.float32).reshape(pos + 1, c.n_head_kv, hd)
+            V = self.vc[il, :pos + 1].astype(np.float32).reshape(pos + 1, c.n_head_kv, hd)
+            att = np.empty((c.n_head, hd), np.float32)
+            qh = q.reshape(c.n_head, hd)
+            scale = np.float32(1.0 / np.sqrt(hd))
+            grp = c.n_head // c.n_head_kv
+            for h in range(c.n_head):
+                s = (K[:, h // grp, :] @ qh[h]).astype(np.float32) * scale
+                e = np.exp(s - s.max()).astype(np.float32)
+                inv = np.float32(1.0 / e.astype(np.float64).sum())
+                att[h] = ((e * inv)[:, None] * V[:, h // grp, :]).sum(0, dtype=np.float32)
+            ffn_inp = (self._mv(b + "attn_output.weight", H, self.nq, att.reshape(-1)) + x).astype(np.float32)
+            gty = self.t[b + "ffn_gate_exps.weight"][0]
+            uty = self.t[b + "ffn_up_exps.weight"][0]
+            dty = self.t[b + "ffn_down_exps.weight"][0]
+            out, _, _, _, _ = orc.moe_layer(ffn_inp.reshape(1, H), self._f(b + "ffn_norm.weight"),
+                                            self._f(b + "ffn_gate_inp.weight").reshape(c.n_expert, H),
+                                            self.t[b + "ffn_gate_exps.weight"][2].reshape(c.n_expert, -1),
+                                            self.t[b + "ffn_up_exps.weight"][2].reshape(c.n_expert, -1),
+                                            self.t[b + "ffn_down_exps.weight"][2].reshape(c.n_expert, -1),
+                                            H=H, E=c.n_expert, k=c.n_expert_used, I=c.n_ff, types=(gty, uty, dty),
+                                            renorm=c.norm_topk, eps=c.eps)
+            x = out.reshape(-1)
+        r = rms_norm(x, self._f("output_norm.weight"), 1, H, c.eps)
+        return self._mv("output.weight", c.n_vocab, H, r)
+
+    def generate(self, prompt, n_gen: int):
+        """Greedy ids and the logits each was chosen from."""
+        toks, logits = [], []
+        seq = list(prompt)
+        for p in range(len(prompt) + n_gen - 1):
+            lg = self.step(seq[p], p)
+            if p >= len(prompt) - 1:
+                nxt = int(np.argmax(lg))
+                toks.append(nxt)
+                logits.append(lg)
+                seq.append(nxt)
+        return toks, np.stack(logits)

@@ -79,3 +79,30 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(moe, "LIB_PATH", str(tmp_path / "absent.so"))
     with pytest.raises(RuntimeError):
         moe.lib()
+
+
+HARNESS_HEADER = os.path.join(ROOT, "include", "hoard_harness.h")
+
+
+def test_harness_header_symbols_exported():
+    src = re.sub(r"/\*.*?\*/", "", open(HARNESS_HEADER).read(), flags=re.S)
+    names = sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(hoard_\w+)\s*\(", src, flags=re.M)))
+    assert "hoard_hx_gemv" in names and "hoard_hx_attention" in names
+    L = moe.lib()
+    assert not [n for n in names if not hasattr(L, n)]
+
+
+def test_harness_rejects_bad_arguments():
+    from hoard_b200 import harness as hx
+    L = hx._hx()
+    assert L.hoard_hx_q8_bytes(300) == -1 and L.hoard_hx_q8_bytes(0) == -1
+    assert L.hoard_hx_q8_bytes(2048) == 2048 + 256 + 512
+    one = ctypes.c_void_p(16)                      # never dereferenced: the checks come first
+    assert L.hoard_hx_gemv(3, one, 8, 512, one, None, one, None) == moe.HOARD_EINVAL          # type
+    assert L.hoard_hx_gemv(12, one, 8, 500, one, None, one, None) == moe.HOARD_EINVAL         # K % 256
+    assert L.hoard_hx_rope_store(one, one, one, 4, 4, 127, 0, 1e4, one, one, None) == moe.HOARD_EINVAL
+    assert L.hoard_hx_attention(one, one, one, 6, 4, 128, 5, 0.1, one, None) == moe.HOARD_EINVAL
+    assert L.hoard_hx_attention(one, one, one, 4, 4, 128, 0, 0.1, one, None) == moe.HOARD_EINVAL
+    assert L.hoard_hx_rmsnorm(one, 1, 9000, 1e-6, one, one, None) == moe.HOARD_EINVAL
+    assert L.hoard_hx_embed(13, one, 512, 10, one, one, None) == moe.HOARD_EINVAL
+    assert L.hoard_hx_argmax(None, 10, one, None) == moe.HOARD_EINVAL
