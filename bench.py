@@ -340,6 +340,44 @@ def measure_prefill(ctx, device, stream, dist, rank=0, world=1, ep_chunks=1, ep_
             "c2_layer": sweep}
 
 
+C1_PROMPT, C1_GEN = 16, 64
+
+
+def measure_c1_decode(device):
+    """C1: the OLMoE-shape model (16 layers, MHA 16 x 128 with QK norm over the whole projection, 64
+    experts top-8 without renorm, I 1024, vocab 50304, Q4_K_M, f16 KV cache), seeded weights, greedy
+    decode of 64 tokens after a 16-token prompt through the device driver (hoard_b200.harness): one
+    captured CUDA graph per token (embedding, 16 x (attention + MoE layer), lm-head, argmax), timed
+    with CUDA events around the 64 replays."""
+    import torch
+    from hoard_b200 import harness as hx
+    cfg = hx.C1_OLMOE
+    model = hx.DecodeModel(cfg, hx.seeded_tensors(cfg, seed=SEED + 101, device=device), device=device.index,
+                           max_ctx=C1_PROMPT + C1_GEN + 8)
+    try:
+        g = torch.Generator().manual_seed(SEED + 102)
+        prompt = torch.randint(0, cfg.n_vocab, (C1_PROMPT,), generator=g).tolist()
+        model.generate_graphed(prompt, 8)                      # warm-up (capture + replays)
+        graph = model.capture()
+        model.prefill(prompt)
+        torch.cuda.synchronize(device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(C1_GEN):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize(device)
+        model.moe.sync_status()
+        ms = a.elapsed_time(b)
+        toks = model.seq[C1_PROMPT:C1_PROMPT + C1_GEN].tolist()
+        return {"metric": "C1 decode tok/s (OLMoE shape, whole model: 16 layers attention + MoE, lm-head)",
+                "value": round(C1_GEN / ms * 1e3, 1), "unit": "tok/s", "ms_per_token": round(ms / C1_GEN, 4),
+                "prompt": C1_PROMPT, "generated": C1_GEN, "distinct_tokens": len(set(toks)),
+                "kv_cache": "f16", "timing": "CUDA events around 64 replays of the captured per-token graph"}
+    finally:
+        model.close()
+
+
 LRU_SLOTS = 32       # C3 run (ii): K = 32 slots per layer
 LRU_TOKENS = 8
 
@@ -509,6 +547,10 @@ def run_gpu(args, rank, world, local_rank):
     if not args.no_lru and rank == 0 and world == 1:
         lru = measure_lru(device, stream, N_LAYER)
 
+    c1 = None
+    if not args.no_c1 and rank == 0 and world == 1:
+        c1 = measure_c1_decode(device)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle as orc
@@ -555,7 +597,10 @@ def run_gpu(args, rank, world, local_rank):
             prefill["value"] = round(prefill["value"] * world, 1)   # whole job: every rank's tokens
         if lru:
             line["lru_decode"] = lru
+        if prefill:
             line["prefill"] = prefill
+        if c1:
+            line["c1_decode"] = c1
         if cpu:
             line["cpu_baseline"] = cpu
         if phases:
@@ -580,6 +625,7 @@ def main():
     ap.add_argument("--trace", action="store_true", help="add the persistent kernel's per-phase breakdown")
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-token (prefill) measurements")
     ap.add_argument("--no-lru", action="store_true", help="skip the LRU slot pool + RAM tier decode measurement")
+    ap.add_argument("--no-c1", action="store_true", help="skip the C1 whole-model decode (device driver) measurement")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="expert-parallel prefill exchange: the library's peer-memory kernels or NCCL all-to-all")
     ap.add_argument("--ep-chunks", type=int, default=2, help="expert-parallel prefill: micro-batches per layer "

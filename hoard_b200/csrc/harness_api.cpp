@@ -32,7 +32,16 @@ int hoard_hx_embed(int type, const void* table, int n_embd, int64_t n_vocab, con
     if (!table || !token || !x_out || n_embd <= 0 || n_vocab <= 0) return HOARD_EINVAL;
     if (!(type == HOARD_TYPE_F32 || type == 1 || quant_type(type))) return HOARD_EINVAL;
     if (quant_type(type) && n_embd % 256) return HOARD_EINVAL;
-    return st(launch_embed(type, static_cast<const uint8_t*>(table), n_embd, n_vocab, token, x_out,
+    return st(launch_embed(type, static_cast<const uint8_t*>(table), n_embd, n_vocab, token, nullptr, x_out,
+                           (cudaStream_t)stream));
+}
+
+int hoard_hx_embed_at(int type, const void* table, int n_embd, int64_t n_vocab, const int32_t* seq,
+                      const int32_t* pos, float* x_out, hoard_stream stream) {
+    if (!table || !seq || !pos || !x_out || n_embd <= 0 || n_vocab <= 0) return HOARD_EINVAL;
+    if (!(type == HOARD_TYPE_F32 || type == 1 || quant_type(type))) return HOARD_EINVAL;
+    if (quant_type(type) && n_embd % 256) return HOARD_EINVAL;
+    return st(launch_embed(type, static_cast<const uint8_t*>(table), n_embd, n_vocab, seq, pos, x_out,
                            (cudaStream_t)stream));
 }
 
@@ -69,8 +78,18 @@ int hoard_hx_rope_store(float* q, float* k, const float* v, int n_head, int n_he
     if (!q || !k || !v || !k_cache || !v_cache || n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv ||
         head_dim <= 0 || head_dim % 2 || pos < 0 || !(freq_base > 0))
         return HOARD_EINVAL;
-    return st(launch_rope_store(q, k, v, n_head, n_head_kv, head_dim, pos, freq_base, static_cast<__half*>(k_cache),
-                                static_cast<__half*>(v_cache), (cudaStream_t)stream));
+    return st(launch_rope_store(q, k, v, n_head, n_head_kv, head_dim, pos, nullptr, pos + 1, freq_base,
+                                static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), (cudaStream_t)stream));
+}
+
+int hoard_hx_rope_store_at(float* q, float* k, const float* v, int n_head, int n_head_kv, int head_dim,
+                           const int32_t* pos, int max_ctx, float freq_base, void* k_cache, void* v_cache,
+                           hoard_stream stream) {
+    if (!q || !k || !v || !pos || !k_cache || !v_cache || n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv ||
+        head_dim <= 0 || head_dim % 2 || max_ctx <= 0 || !(freq_base > 0))
+        return HOARD_EINVAL;
+    return st(launch_rope_store(q, k, v, n_head, n_head_kv, head_dim, 0, pos, max_ctx, freq_base,
+                                static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), (cudaStream_t)stream));
 }
 
 int hoard_hx_attention(const float* q, const void* k_cache, const void* v_cache, int n_head, int n_head_kv,
@@ -80,12 +99,27 @@ int hoard_hx_attention(const float* q, const void* k_cache, const void* v_cache,
         return HOARD_EINVAL;
     if (attention_smem(head_dim, n_pos) > 200 * 1024) return HOARD_EINVAL;
     return st(launch_attention(q, static_cast<const __half*>(k_cache), static_cast<const __half*>(v_cache), n_head,
-                               n_head_kv, head_dim, n_pos, scale, out, (cudaStream_t)stream));
+                               n_head_kv, head_dim, n_pos, nullptr, scale, out, (cudaStream_t)stream));
+}
+
+int hoard_hx_attention_at(const float* q, const void* k_cache, const void* v_cache, int n_head, int n_head_kv,
+                          int head_dim, const int32_t* pos, int max_ctx, float scale, float* out, hoard_stream stream) {
+    if (!q || !k_cache || !v_cache || !pos || !out || n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv ||
+        head_dim <= 0 || head_dim > 256 || 256 % head_dim || max_ctx <= 0)
+        return HOARD_EINVAL;
+    if (attention_smem(head_dim, max_ctx) > 200 * 1024) return HOARD_EINVAL;
+    return st(launch_attention(q, static_cast<const __half*>(k_cache), static_cast<const __half*>(v_cache), n_head,
+                               n_head_kv, head_dim, max_ctx, pos, scale, out, (cudaStream_t)stream));
 }
 
 int hoard_hx_argmax(const float* v, int n, int32_t* out, hoard_stream stream) {
     if (!v || !out || n <= 0) return HOARD_EINVAL;
-    return st(launch_argmax(v, n, out, (cudaStream_t)stream));
+    return st(launch_argmax(v, n, out, nullptr, 0, (cudaStream_t)stream));
+}
+
+int hoard_hx_argmax_at(const float* v, int n, int32_t* seq, int32_t* pos, int seq_len, hoard_stream stream) {
+    if (!v || !seq || !pos || n <= 0 || seq_len <= 0) return HOARD_EINVAL;
+    return st(launch_argmax(v, n, seq, pos, seq_len, (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -115,16 +115,17 @@ cudaError_t launch_ep_pack(const int32_t* sel, int T, int k, int n_ranks, int ex
 cudaError_t launch_rmsnorm_f32(const float* x, int rows, int cols, float eps, const float* w, float* out,
                                cudaStream_t s);
 cudaError_t launch_quant_q8(const float* x, int rows, int K, int8_t* q, float* d, int* bs, cudaStream_t s);
-cudaError_t launch_embed(int type, const uint8_t* table, int H, int64_t n_vocab, const int32_t* token, float* out,
-                         cudaStream_t s);
+cudaError_t launch_embed(int type, const uint8_t* table, int H, int64_t n_vocab, const int32_t* token,
+                         const int32_t* pos, float* out, cudaStream_t s);
 cudaError_t launch_qgemv(int type, const uint8_t* w, int N, int K, const int8_t* xq, const float* xd, const int* xbs,
                          const float* resid, float* y, cudaStream_t s);
 cudaError_t launch_rope_store(float* q, float* k, const float* v, int n_head, int n_kv, int hd, int pos,
-                              float freq_base, __half* kc, __half* vc, cudaStream_t s);
+                              const int32_t* pos_dev, int max_ctx, float freq_base, __half* kc, __half* vc,
+                              cudaStream_t s);
 size_t attention_smem(int hd, int n_pos);
 cudaError_t launch_attention(const float* q, const __half* kc, const __half* vc, int n_head, int n_kv, int hd,
-                             int n_pos, float scale, float* out, cudaStream_t s);
-cudaError_t launch_argmax(const float* v, int n, int32_t* out, cudaStream_t s);
+                             int n_pos, const int32_t* pos_dev, float scale, float* out, cudaStream_t s);
+cudaError_t launch_argmax(const float* v, int n, int32_t* out, int32_t* pos, int seq_len, cudaStream_t s);
 
 // ---- expert parallelism over NVLink peer memory ----
 // Every rank allocates one block with this layout (identical on all ranks, so a peer's field is its

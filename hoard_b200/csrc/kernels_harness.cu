@@ -15,9 +15,10 @@ namespace {
 
 // ---- embedding: one row of a raw GGUF table (Q4_K / Q6_K blocks, f32 or f16) to f32 ----
 __global__ void __launch_bounds__(256) k_embed(int type, const uint8_t* __restrict__ table, int H, int64_t n_vocab,
-                                               const int32_t* __restrict__ tok, float* __restrict__ out) {
+                                               const int32_t* __restrict__ tok, const int32_t* __restrict__ pos,
+                                               float* __restrict__ out) {
     const int nb = H / QK;
-    const int64_t token = *tok;
+    const int64_t token = tok[pos ? *pos : 0];
     const bool ok = token >= 0 && token < n_vocab;     // an id out of range gives a zero row
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x) {
         float v;
@@ -85,8 +86,11 @@ __global__ void __launch_bounds__(256) k_qgemv(const uint8_t* __restrict__ w, in
 //      repeated multiplication, as ggml's rope cache does ----
 __global__ void __launch_bounds__(256) k_rope_store(float* __restrict__ q, float* __restrict__ k,
                                                     const float* __restrict__ v, int n_head, int n_kv, int hd,
-                                                    int pos, float theta_scale, __half* __restrict__ kc,
+                                                    int pos, const int32_t* __restrict__ pos_dev, int max_ctx,
+                                                    float theta_scale, __half* __restrict__ kc,
                                                     __half* __restrict__ vc) {
+    if (pos_dev) pos = *pos_dev;
+    if (pos < 0 || pos >= max_ctx) return;              // outside the cache: nothing is written
     const int half = hd / 2;
     const int n_pairs = (n_head + n_kv) * half;
     for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n_pairs; t += gridDim.x * blockDim.x) {
@@ -116,11 +120,14 @@ __global__ void __launch_bounds__(256) k_rope_store(float* __restrict__ q, float
 constexpr int ATT_THREADS = 256;
 __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restrict__ q, const __half* __restrict__ kc,
                                                           const __half* __restrict__ vc, int n_head, int n_kv, int hd,
-                                                          int n_pos, float scale, float* __restrict__ out) {
+                                                          int n_pos, const int32_t* __restrict__ pos_dev,
+                                                          float scale, float* __restrict__ out) {
     extern __shared__ float sm[];
+    const int cap = n_pos;                           // positions the shared memory was sized for
+    if (pos_dev) n_pos = min(*pos_dev + 1, cap);
     float* sq = sm;                  // [hd]
     float* sp = sm + hd;             // [n_pos] scores, then probabilities
-    float* part = sp + n_pos;        // [ATT_THREADS / hd][hd] partial output sums
+    float* part = sp + cap;          // [ATT_THREADS / hd][hd] partial output sums
     __shared__ float redf[32];
     __shared__ double redd[32];
     const int h = blockIdx.x, kvh = h / (n_head / n_kv);
@@ -164,7 +171,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
 }
 
 // ---- argmax (first index of the maximum) of n floats: one CTA of 1024 threads ----
-__global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ v, int n, int32_t* __restrict__ out) {
+__global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ v, int n, int32_t* __restrict__ out,
+                                                 int32_t* __restrict__ pos, int seq_len) {
     __shared__ float sv[32];
     __shared__ int si[32];
     float best = -INFINITY;
@@ -189,15 +197,24 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ v, in
             const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
             if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
         }
-        if (lane == 0) *out = bi == 0x7fffffff ? 0 : bi;
+        if (lane == 0) {
+            const int r = bi == 0x7fffffff ? 0 : bi;
+            if (!pos) {
+                *out = r;
+            } else {                                 // out[*pos + 1] = r, then the position advances
+                const int p = *pos + 1;
+                if (p < seq_len) out[p] = r;
+                *pos = p;
+            }
+        }
     }
 }
 
 }  // namespace
 
-cudaError_t launch_embed(int type, const uint8_t* table, int H, int64_t n_vocab, const int32_t* token, float* out,
-                         cudaStream_t s) {
-    k_embed<<<(H + 255) / 256, 256, 0, s>>>(type, table, H, n_vocab, token, out);
+cudaError_t launch_embed(int type, const uint8_t* table, int H, int64_t n_vocab, const int32_t* token,
+                         const int32_t* pos, float* out, cudaStream_t s) {
+    k_embed<<<(H + 255) / 256, 256, 0, s>>>(type, table, H, n_vocab, token, pos, out);
     return cudaGetLastError();
 }
 
@@ -215,10 +232,12 @@ cudaError_t launch_qgemv(int type, const uint8_t* w, int N, int K, const int8_t*
 }
 
 cudaError_t launch_rope_store(float* q, float* k, const float* v, int n_head, int n_kv, int hd, int pos,
-                              float freq_base, __half* kc, __half* vc, cudaStream_t s) {
+                              const int32_t* pos_dev, int max_ctx, float freq_base, __half* kc, __half* vc,
+                              cudaStream_t s) {
     const float theta_scale = powf(freq_base, -2.0f / (float)hd);
     const int n = (n_head + n_kv) * (hd / 2);
-    k_rope_store<<<(n + 255) / 256, 256, 0, s>>>(q, k, v, n_head, n_kv, hd, pos, theta_scale, kc, vc);
+    k_rope_store<<<(n + 255) / 256, 256, 0, s>>>(q, k, v, n_head, n_kv, hd, pos, pos_dev, max_ctx, theta_scale, kc,
+                                                 vc);
     return cudaGetLastError();
 }
 
@@ -227,18 +246,18 @@ size_t attention_smem(int hd, int n_pos) {
 }
 
 cudaError_t launch_attention(const float* q, const __half* kc, const __half* vc, int n_head, int n_kv, int hd,
-                             int n_pos, float scale, float* out, cudaStream_t s) {
+                             int n_pos, const int32_t* pos_dev, float scale, float* out, cudaStream_t s) {
     const size_t smem = attention_smem(hd, n_pos);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    k_attention<<<n_head, ATT_THREADS, smem, s>>>(q, kc, vc, n_head, n_kv, hd, n_pos, scale, out);
+    k_attention<<<n_head, ATT_THREADS, smem, s>>>(q, kc, vc, n_head, n_kv, hd, n_pos, pos_dev, scale, out);
     return cudaGetLastError();
 }
 
-cudaError_t launch_argmax(const float* v, int n, int32_t* out, cudaStream_t s) {
-    k_argmax<<<1, 1024, 0, s>>>(v, n, out);
+cudaError_t launch_argmax(const float* v, int n, int32_t* out, int32_t* pos, int seq_len, cudaStream_t s) {
+    k_argmax<<<1, 1024, 0, s>>>(v, n, out, pos, seq_len);
     return cudaGetLastError();
 }
 

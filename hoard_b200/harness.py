@@ -49,6 +49,10 @@ def _hx():
         L.hoard_hx_rope_store.argtypes = [vp, vp, vp, i32, i32, i32, i32, f32, vp, vp, vp]
         L.hoard_hx_attention.argtypes = [vp, vp, vp, i32, i32, i32, i32, f32, vp, vp]
         L.hoard_hx_argmax.argtypes = [vp, i32, vp, vp]
+        L.hoard_hx_embed_at.argtypes = [i32, vp, i32, i64, vp, vp, vp, vp]
+        L.hoard_hx_rope_store_at.argtypes = [vp, vp, vp, i32, i32, i32, vp, i32, f32, vp, vp, vp]
+        L.hoard_hx_attention_at.argtypes = [vp, vp, vp, i32, i32, i32, vp, i32, f32, vp, vp]
+        L.hoard_hx_argmax_at.argtypes = [vp, i32, vp, vp, i32, vp]
         _bound = True
     return L
 
@@ -212,6 +216,8 @@ class DecodeModel:
         self.vc = torch.zeros_like(self.kc)
         self.seq = torch.zeros(max_ctx + 1, dtype=torch.int32, device=dev)
         self.scratch_tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.pos_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._graph = None
         torch.cuda.synchronize(dev)
 
     @classmethod
@@ -232,39 +238,100 @@ class DecodeModel:
     # ---- one token: logits of position pos for token seq[pos]; argmax into `next_tok` ----
     def step(self, pos: int, next_tok: torch.Tensor, stream=None):
         c, hx, s = self.cfg, _hx(), _stream(stream)
-        H, hd = c.n_embd, c.head_dim
+        H = c.n_embd
         x, x2 = self.x, self.x2
         _ok(hx.hoard_hx_embed(self.embd_type, _ptr(self.embd), H, c.n_vocab, _ptr(self.seq[pos:pos + 1]), _ptr(x), s),
             "embed")
-        scale = 1.0 / math.sqrt(hd)
         for il, L in enumerate(self.layers):
-            _ok(hx.hoard_hx_rmsnorm(_ptr(x), 1, H, c.eps, _ptr(L["attn_norm"]), _ptr(self.cur), s), "rmsnorm")
-            _ok(hx.hoard_hx_quant_q8(_ptr(self.cur), H, _ptr(self.q8), s), "quant")
-            for key, out, n in (("q", self.q, self.nq), ("k", self.k, self.nkv), ("v", self.v, self.nkv)):
-                ty, wt = L[key]
-                _ok(hx.hoard_hx_gemv(ty, _ptr(wt), n, H, _ptr(self.q8), None, _ptr(out), s), "gemv")
-            if c.qk_norm == "full":
-                _ok(hx.hoard_hx_rmsnorm(_ptr(self.q), 1, self.nq, c.eps, _ptr(L["q_norm"]), _ptr(self.q), s), "qnorm")
-                _ok(hx.hoard_hx_rmsnorm(_ptr(self.k), 1, self.nkv, c.eps, _ptr(L["k_norm"]), _ptr(self.k), s), "knorm")
-            elif c.qk_norm == "head":
-                _ok(hx.hoard_hx_rmsnorm(_ptr(self.q), c.n_head, hd, c.eps, _ptr(L["q_norm"]), _ptr(self.q), s), "qnorm")
-                _ok(hx.hoard_hx_rmsnorm(_ptr(self.k), c.n_head_kv, hd, c.eps, _ptr(L["k_norm"]), _ptr(self.k), s),
-                    "knorm")
-            _ok(hx.hoard_hx_rope_store(_ptr(self.q), _ptr(self.k), _ptr(self.v), c.n_head, c.n_head_kv, hd, pos,
-                                       c.freq_base, _ptr(self.kc[il]), _ptr(self.vc[il]), s), "rope")
-            _ok(hx.hoard_hx_attention(_ptr(self.q), _ptr(self.kc[il]), _ptr(self.vc[il]), c.n_head, c.n_head_kv, hd,
-                                      pos + 1, scale, _ptr(self.att), s), "attention")
-            _ok(hx.hoard_hx_quant_q8(_ptr(self.att), self.nq, _ptr(self.q8), s), "quant")
-            ty, wo = L["o"]
-            _ok(hx.hoard_hx_gemv(ty, _ptr(wo), H, self.nq, _ptr(self.q8), _ptr(x), _ptr(x2), s), "gemv")
+            self._layer_attention(il, L, x, x2, hx, s, pos)
             self.moe.layers(il, 1, x2.view(1, H), stream=stream)
             x, x2 = x2, x
-        self.x, self.x2 = x, x2
         _ok(hx.hoard_hx_rmsnorm(_ptr(x), 1, H, c.eps, _ptr(self.out_norm), _ptr(self.cur), s), "rmsnorm")
         _ok(hx.hoard_hx_quant_q8(_ptr(self.cur), H, _ptr(self.q8), s), "quant")
         _ok(hx.hoard_hx_gemv(self.out_type, _ptr(self.out_w), c.n_vocab, H, _ptr(self.q8), None, _ptr(self.logits), s),
             "gemv")
         _ok(hx.hoard_hx_argmax(_ptr(self.logits), c.n_vocab, _ptr(next_tok), s), "argmax")
+
+    def _layer_attention(self, il, L, x, x2, hx, s, pos=None):
+        """Graph A's attention part of layer il: x2 = Wo att + x. pos None: the device position."""
+        c = self.cfg
+        H, hd = c.n_embd, c.head_dim
+        _ok(hx.hoard_hx_rmsnorm(_ptr(x), 1, H, c.eps, _ptr(L["attn_norm"]), _ptr(self.cur), s), "rmsnorm")
+        _ok(hx.hoard_hx_quant_q8(_ptr(self.cur), H, _ptr(self.q8), s), "quant")
+        for key, out, n in (("q", self.q, self.nq), ("k", self.k, self.nkv), ("v", self.v, self.nkv)):
+            ty, wt = L[key]
+            _ok(hx.hoard_hx_gemv(ty, _ptr(wt), n, H, _ptr(self.q8), None, _ptr(out), s), "gemv")
+        if c.qk_norm == "full":
+            _ok(hx.hoard_hx_rmsnorm(_ptr(self.q), 1, self.nq, c.eps, _ptr(L["q_norm"]), _ptr(self.q), s), "qnorm")
+            _ok(hx.hoard_hx_rmsnorm(_ptr(self.k), 1, self.nkv, c.eps, _ptr(L["k_norm"]), _ptr(self.k), s), "knorm")
+        elif c.qk_norm == "head":
+            _ok(hx.hoard_hx_rmsnorm(_ptr(self.q), c.n_head, hd, c.eps, _ptr(L["q_norm"]), _ptr(self.q), s), "qnorm")
+            _ok(hx.hoard_hx_rmsnorm(_ptr(self.k), c.n_head_kv, hd, c.eps, _ptr(L["k_norm"]), _ptr(self.k), s), "knorm")
+        scale = 1.0 / math.sqrt(hd)
+        if pos is None:
+            _ok(hx.hoard_hx_rope_store_at(_ptr(self.q), _ptr(self.k), _ptr(self.v), c.n_head, c.n_head_kv, hd,
+                                          _ptr(self.pos_dev), self.max_ctx, c.freq_base, _ptr(self.kc[il]),
+                                          _ptr(self.vc[il]), s), "rope")
+            _ok(hx.hoard_hx_attention_at(_ptr(self.q), _ptr(self.kc[il]), _ptr(self.vc[il]), c.n_head, c.n_head_kv, hd,
+                                         _ptr(self.pos_dev), self.max_ctx, scale, _ptr(self.att), s), "attention")
+        else:
+            _ok(hx.hoard_hx_rope_store(_ptr(self.q), _ptr(self.k), _ptr(self.v), c.n_head, c.n_head_kv, hd, pos,
+                                       c.freq_base, _ptr(self.kc[il]), _ptr(self.vc[il]), s), "rope")
+            _ok(hx.hoard_hx_attention(_ptr(self.q), _ptr(self.kc[il]), _ptr(self.vc[il]), c.n_head, c.n_head_kv, hd,
+                                      pos + 1, scale, _ptr(self.att), s), "attention")
+        _ok(hx.hoard_hx_quant_q8(_ptr(self.att), self.nq, _ptr(self.q8), s), "quant")
+        ty, wo = L["o"]
+        _ok(hx.hoard_hx_gemv(ty, _ptr(wo), H, self.nq, _ptr(self.q8), _ptr(x), _ptr(x2), s), "gemv")
+
+    def _step_at(self, stream=None):
+        """One decode step at the device position: token seq[pos] -> seq[pos + 1], pos += 1."""
+        c, hx, s = self.cfg, _hx(), _stream(stream)
+        H = c.n_embd
+        x, x2 = self.x, self.x2
+        _ok(hx.hoard_hx_embed_at(self.embd_type, _ptr(self.embd), H, c.n_vocab, _ptr(self.seq), _ptr(self.pos_dev),
+                                 _ptr(x), s), "embed")
+        for il, L in enumerate(self.layers):
+            self._layer_attention(il, L, x, x2, hx, s)
+            self.moe.layers(il, 1, x2.view(1, H), stream=stream)
+            x, x2 = x2, x
+        _ok(hx.hoard_hx_rmsnorm(_ptr(x), 1, H, c.eps, _ptr(self.out_norm), _ptr(self.cur), s), "rmsnorm")
+        _ok(hx.hoard_hx_quant_q8(_ptr(self.cur), H, _ptr(self.q8), s), "quant")
+        _ok(hx.hoard_hx_gemv(self.out_type, _ptr(self.out_w), c.n_vocab, H, _ptr(self.q8), None, _ptr(self.logits), s),
+            "gemv")
+        _ok(hx.hoard_hx_argmax_at(_ptr(self.logits), c.n_vocab, _ptr(self.seq), _ptr(self.pos_dev), self.seq.numel(), s),
+            "argmax")
+
+    def prefill(self, prompt, stream=None):
+        """Runs the prompt tokens but the last through the step (their KV entries), then sets the
+        device position to the last prompt token."""
+        T = len(prompt)
+        self.seq[:T].copy_(torch.tensor(prompt, dtype=torch.int32))
+        for p in range(T - 1):
+            self.step(p, self.scratch_tok, stream)
+        self.pos_dev.fill_(T - 1)
+
+    def capture(self):
+        """Captures one decode step (position in device memory) as a CUDA graph."""
+        if self._graph is None:
+            torch.cuda.synchronize(self.dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._step_at()
+            self._graph = g
+        return self._graph
+
+    def generate_graphed(self, prompt, n_gen: int):
+        """Greedy decode like generate(), each generated token one replay of the captured step."""
+        T = len(prompt)
+        if T < 1 or T + n_gen > self.max_ctx:
+            raise ValueError("prompt + n_gen must fit max_ctx")
+        g = self.capture()
+        self.prefill(prompt)
+        for _ in range(n_gen):
+            g.replay()
+        torch.cuda.synchronize(self.dev)
+        self.moe.sync_status()
+        return self.seq[T:T + n_gen].tolist()
 
     def score(self, tokens, first: int, stream=None) -> torch.Tensor:
         """Teacher-forced logits: runs tokens[0 .. n-2] through the decode step and returns the logits

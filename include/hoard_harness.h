@@ -54,6 +54,20 @@ int hoard_hx_attention(const float* q, const void* k_cache, const void* v_cache,
 /* *out = the first index of the maximum of v[0..n). */
 int hoard_hx_argmax(const float* v, int n, int32_t* out, hoard_stream stream);
 
+/* ---- the same steps with the position in device memory, so that one captured CUDA graph of a
+ * whole decode step can be replayed for every token ----
+ * embed_at: token = seq[*pos]. rope_store_at: position *pos (nothing is written when
+ * *pos >= max_ctx). attention_at: n_pos = min(*pos + 1, max_ctx). argmax_at: seq[*pos + 1] = the
+ * argmax (when *pos + 1 < seq_len), then *pos += 1. */
+int hoard_hx_embed_at(int type, const void* table, int n_embd, int64_t n_vocab, const int32_t* seq,
+                      const int32_t* pos, float* x_out, hoard_stream stream);
+int hoard_hx_rope_store_at(float* q, float* k, const float* v, int n_head, int n_head_kv, int head_dim,
+                           const int32_t* pos, int max_ctx, float freq_base, void* k_cache, void* v_cache,
+                           hoard_stream stream);
+int hoard_hx_attention_at(const float* q, const void* k_cache, const void* v_cache, int n_head, int n_head_kv,
+                          int head_dim, const int32_t* pos, int max_ctx, float scale, float* out, hoard_stream stream);
+int hoard_hx_argmax_at(const float* v, int n, int32_t* seq, int32_t* pos, int seq_len, hoard_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -71,6 +71,8 @@ def test_greedy_decode_matches_oracle(tmp_path, cfg, via_gguf):
             if srt[-1] - srt[-2] >= GAP:
                 assert int(np.argmax(forced[i])) == want[i], (i, int(np.argmax(forced[i])), want[i])
         print(f"free-running match {n_free}/{N_GEN}; teacher-forced rel-L2 median {np.median(rel):.1e} max {rel.max():.1e}")
+        # one captured CUDA graph per step, position in device memory: the same tokens
+        assert model.generate_graphed(prompt, N_GEN) == got
     finally:
         model.close()
 
