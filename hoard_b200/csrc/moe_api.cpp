@@ -696,6 +696,17 @@ int hoard_moe_set_gemm_ctas(hoard_moe_ctx* c, int ctas) {
     return HOARD_OK;
 }
 
+int hoard_moe_set_top_k(hoard_moe_ctx* c, int k) {
+    if (!c) return HOARD_EINVAL;
+    if (k < 1 || k > c->desc.n_expert_used) return fail(c, HOARD_EINVAL, "k must be 1..n_expert_used");
+    c->dims.k = k;
+    std::vector<LayerWeights> tab(c->desc.n_layer);
+    for (int l = 0; l < c->desc.n_layer; ++l) tab[l] = layer_weights(c, l);
+    HCHECK(c, cudaSetDevice(c->desc.device));
+    c->decode_ok = decode_supported(c->dims, tab.data(), c->desc.n_layer);
+    return HOARD_OK;
+}
+
 int hoard_moe_set_gemm_min_tokens(hoard_moe_ctx* c, int min_tokens) {
     if (!c || min_tokens < 0) return HOARD_EINVAL;
     c->gemm_min_tokens = min_tokens;

@@ -30,6 +30,7 @@ from hoard_b200 import moe, quant
 from hoard_b200.moe import HoardError, _ptr, _stream, lib
 
 Q4_K, Q6_K, F32 = quant.Q4_K, quant.Q6_K, 0
+MAX_BATCH = 16          # tokens of one batched (verify) forward
 
 _bound = False
 
@@ -198,7 +199,7 @@ class DecodeModel:
         self.moe = moe.MoEContext(n_embd=H, n_expert=cfg.n_expert, n_expert_used=cfg.n_expert_used, n_ff=cfg.n_ff,
                                   n_layer=cfg.n_layer, norm_topk=cfg.norm_topk, eps=cfg.eps,
                                   gate_types=[t[0] for t in types], up_types=[t[1] for t in types],
-                                  down_types=[t[2] for t in types], max_tokens=1, device=device)
+                                  down_types=[t[2] for t in types], max_tokens=MAX_BATCH, device=device)
         for il in range(cfg.n_layer):
             b = f"blk.{il}."
             self.moe.set_router(il, f32(b + "ffn_gate_inp.weight").view(cfg.n_expert, H), f32(b + "ffn_norm.weight"))
@@ -332,6 +333,114 @@ class DecodeModel:
         torch.cuda.synchronize(self.dev)
         self.moe.sync_status()
         return self.seq[T:T + n_gen].tolist()
+
+    def forward_batch(self, tokens, base: int, stream=None) -> torch.Tensor:
+        """One forward over m <= MAX_BATCH consecutive tokens at positions base .. base+m-1 (causal:
+        token i attends to positions <= base+i; K/V stored for all m), the MoE layers batched (T = m).
+        Returns the logits [m][vocab]; row i predicts position base+i+1. hoard's verify pass,
+        src/run_specloop.cpp:76-150."""
+        c, hx, s = self.cfg, _hx(), _stream(stream)
+        m, H, hd = len(tokens), c.n_embd, c.head_dim
+        if not 1 <= m <= MAX_BATCH or base + m > self.max_ctx:
+            raise ValueError("batch must be 1..MAX_BATCH tokens inside max_ctx")
+        self.seq[base:base + m].copy_(torch.tensor(tokens, dtype=torch.int32))
+        if not hasattr(self, "_xb"):
+            z = lambda *sh: torch.zeros(*sh, dtype=torch.float32, device=self.dev)
+            self._xb, self._x2b, self._curb = z(MAX_BATCH, H), z(MAX_BATCH, H), z(MAX_BATCH, H)
+            self._qb, self._kb, self._vb = z(MAX_BATCH, self.nq), z(MAX_BATCH, self.nkv), z(MAX_BATCH, self.nkv)
+            self._attb, self._lgb = z(MAX_BATCH, self.nq), z(MAX_BATCH, c.n_vocab)
+        xb, x2b, cur = self._xb, self._x2b, self._curb
+        for i in range(m):
+            _ok(hx.hoard_hx_embed(self.embd_type, _ptr(self.embd), H, c.n_vocab, _ptr(self.seq[base + i:base + i + 1]),
+                                  _ptr(xb[i]), s), "embed")
+        scale = 1.0 / math.sqrt(hd)
+        for il, L in enumerate(self.layers):
+            _ok(hx.hoard_hx_rmsnorm(_ptr(xb), m, H, c.eps, _ptr(L["attn_norm"]), _ptr(cur), s), "rmsnorm")
+            for i in range(m):
+                _ok(hx.hoard_hx_quant_q8(_ptr(cur[i]), H, _ptr(self.q8), s), "quant")
+                for key, out, n in (("q", self._qb, self.nq), ("k", self._kb, self.nkv), ("v", self._vb, self.nkv)):
+                    ty, wt = L[key]
+                    _ok(hx.hoard_hx_gemv(ty, _ptr(wt), n, H, _ptr(self.q8), None, _ptr(out[i]), s), "gemv")
+            if c.qk_norm == "full":
+                _ok(hx.hoard_hx_rmsnorm(_ptr(self._qb), m, self.nq, c.eps, _ptr(L["q_norm"]), _ptr(self._qb), s), "qnorm")
+                _ok(hx.hoard_hx_rmsnorm(_ptr(self._kb), m, self.nkv, c.eps, _ptr(L["k_norm"]), _ptr(self._kb), s), "knorm")
+            elif c.qk_norm == "head":
+                _ok(hx.hoard_hx_rmsnorm(_ptr(self._qb), m * c.n_head, hd, c.eps, _ptr(L["q_norm"]), _ptr(self._qb), s),
+                    "qnorm")
+                _ok(hx.hoard_hx_rmsnorm(_ptr(self._kb), m * c.n_head_kv, hd, c.eps, _ptr(L["k_norm"]), _ptr(self._kb),
+                                        s), "knorm")
+            for i in range(m):
+                _ok(hx.hoard_hx_rope_store(_ptr(self._qb[i]), _ptr(self._kb[i]), _ptr(self._vb[i]), c.n_head,
+                                           c.n_head_kv, hd, base + i, c.freq_base, _ptr(self.kc[il]),
+                                           _ptr(self.vc[il]), s), "rope")
+            for i in range(m):
+                _ok(hx.hoard_hx_attention(_ptr(self._qb[i]), _ptr(self.kc[il]), _ptr(self.vc[il]), c.n_head,
+                                          c.n_head_kv, hd, base + i + 1, scale, _ptr(self._attb[i]), s), "attention")
+            ty, wo = L["o"]
+            for i in range(m):
+                _ok(hx.hoard_hx_quant_q8(_ptr(self._attb[i]), self.nq, _ptr(self.q8), s), "quant")
+                _ok(hx.hoard_hx_gemv(ty, _ptr(wo), H, self.nq, _ptr(self.q8), _ptr(xb[i]), _ptr(x2b[i]), s), "gemv")
+            self.moe.layers(il, 1, x2b[:m], stream=stream)
+            xb, x2b = x2b, xb
+        _ok(hx.hoard_hx_rmsnorm(_ptr(xb), m, H, c.eps, _ptr(self.out_norm), _ptr(cur), s), "rmsnorm")
+        for i in range(m):
+            _ok(hx.hoard_hx_quant_q8(_ptr(cur[i]), H, _ptr(self.q8), s), "quant")
+            _ok(hx.hoard_hx_gemv(self.out_type, _ptr(self.out_w), c.n_vocab, H, _ptr(self.q8), None,
+                                 _ptr(self._lgb[i]), s), "gemv")
+        return self._lgb[:m].clone()
+
+    def speculative_generate(self, prompt, n_gen: int, k_draft: int = 4):
+        """hoard's speculative loop (src/run_specloop.cpp:189-210): draft k tokens greedily with the same
+        model routed to its top-1 expert, verify them in one batched forward with the full top-k,
+        accept the matching prefix, then run the corrected token. Greedy and lossless: the result
+        equals generate()'s. Returns (tokens, {"rounds", "proposed", "accepted"})."""
+        T, k_full = len(prompt), self.cfg.n_expert_used
+        if T < 1 or T + n_gen + k_draft + 1 > self.max_ctx or not 1 <= k_draft <= MAX_BATCH:
+            raise ValueError("prompt + n_gen + k_draft must fit max_ctx, 1 <= k_draft <= MAX_BATCH")
+        self.seq[:T].copy_(torch.tensor(prompt, dtype=torch.int32))
+        for p in range(T):
+            self.step(p, self.scratch_tok)
+        pred = self.logits.clone()
+        cur, out, stats = T, [], {"rounds": 0, "proposed": 0, "accepted": 0}
+        while len(out) < n_gen:
+            draft, lg, dpos = [], pred, cur
+            self.moe.set_top_k(1)
+            try:
+                for _ in range(k_draft):
+                    d = int(torch.argmax(lg).item())
+                    draft.append(d)
+                    self.seq[dpos] = d
+                    self.step(dpos, self.scratch_tok)
+                    lg = self.logits.clone()
+                    dpos += 1
+            finally:
+                self.moe.set_top_k(k_full)
+            V = self.forward_batch(draft, cur)
+            n, last = 0, pred
+            for j in range(k_draft):
+                tgt_l = pred if j == 0 else V[j - 1]
+                if draft[j] == int(torch.argmax(tgt_l).item()):
+                    n += 1
+                    if j == k_draft - 1:
+                        last = V[k_draft - 1]
+                else:
+                    last = tgt_l
+                    break
+            stats["rounds"] += 1
+            stats["proposed"] += k_draft
+            stats["accepted"] += n
+            out += draft[:n]
+            cur += n
+            if len(out) >= n_gen:
+                break
+            corrected = int(torch.argmax(last).item())
+            out.append(corrected)
+            self.seq[cur] = corrected
+            self.step(cur, self.scratch_tok)
+            pred = self.logits.clone()
+            cur += 1
+        self.moe.sync_status()
+        return out[:n_gen], stats
 
     def score(self, tokens, first: int, stream=None) -> torch.Tensor:
         """Teacher-forced logits: runs tokens[0 .. n-2] through the decode step and returns the logits

@@ -34,7 +34,7 @@ EXPORTED = [
     "hoard_moe_set_shared", "hoard_moe_route", "hoard_moe_experts", "hoard_moe_layer", "hoard_moe_layers",
     "hoard_moe_sync_status", "hoard_moe_expert_bytes", "hoard_moe_launch_count", "hoard_moe_set_decode_impl",
     "hoard_moe_set_trace", "hoard_moe_trace_layout", "hoard_moe_decode_noalloc",
-    "hoard_moe_set_gemm_min_tokens", "hoard_moe_set_gemm_ctas", "hoard_moe_ep_reserve", "hoard_moe_ep_pack", "hoard_moe_ep_experts",
+    "hoard_moe_set_gemm_min_tokens", "hoard_moe_set_gemm_ctas", "hoard_moe_set_top_k", "hoard_moe_ep_reserve", "hoard_moe_ep_pack", "hoard_moe_ep_experts",
     "hoard_moe_ep_combine", "hoard_moe_ram_tier", "hoard_moe_ensure", "hoard_moe_residency_stats",
     "hoard_moe_p2p_init", "hoard_moe_p2p_handle", "hoard_moe_p2p_open", "hoard_moe_p2p_attach", "hoard_moe_p2p_close",
     "hoard_moe_p2p_set_timeout", "hoard_moe_p2p_send", "hoard_moe_p2p_compute", "hoard_moe_p2p_finish",
@@ -90,6 +90,7 @@ def lib() -> ctypes.CDLL:
         L.hoard_moe_set_decode_impl.argtypes = [vp, i32]
         L.hoard_moe_set_gemm_min_tokens.argtypes = [vp, i32]
         L.hoard_moe_set_gemm_ctas.argtypes = [vp, i32]
+        L.hoard_moe_set_top_k.argtypes = [vp, i32]
         L.hoard_moe_ram_tier.argtypes = [vp, i32, i32, vp, vp, vp]
         L.hoard_moe_ensure.argtypes = [vp, i32, vp, i32, vp, vp]
         L.hoard_moe_residency_stats.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64), ctypes.POINTER(i64)]
@@ -291,6 +292,11 @@ class MoEContext:
     def set_gemm_min_tokens(self, min_tokens: int):
         """T at or above which the expert FFN runs as the tensor-core grouped GEMM (0 = never)."""
         self._check(lib().hoard_moe_set_gemm_min_tokens(self._h, min_tokens), "set_gemm_min_tokens")
+
+    def set_top_k(self, k: int):
+        """Top-k override: 1 <= k <= n_expert_used (the value the context was created with)."""
+        self._check(lib().hoard_moe_set_top_k(self._h, k), "set_top_k")
+        self.k = k
 
     def set_gemm_ctas(self, ctas: int):
         """CTAs of the tensor-core GEMMs (0 = one per SM)."""

@@ -181,6 +181,11 @@ int hoard_moe_set_gemm_min_tokens(hoard_moe_ctx* ctx, int min_tokens);
  * parallelism (hoard_b200/ep.py). No counterpart in hoard. */
 int hoard_moe_set_gemm_ctas(hoard_moe_ctx* ctx, int ctas);
 
+/* Top-k override (hoard's TOPK, src/run_qwen35.cpp:169): route, experts and layer calls from now on
+ * select k experts per token, 1 <= k <= the n_expert_used the context was created with (its buffers
+ * are sized for that). Renormalisation follows norm_topk over the k selected. */
+int hoard_moe_set_top_k(hoard_moe_ctx* ctx, int k);
+
 /* ---- Residency: per-layer LRU slot pool over a host RAM tier --------------------------------------
  * Replaces hoard's to_vram / fetch and its per-layer LRU (src/run_moe_stream.cpp:279-284, :380-421;
  * the `ensure` of src/run_specloop.cpp:123) when n_slots < n_expert. Uploads run on the context's own

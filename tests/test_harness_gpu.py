@@ -150,3 +150,20 @@ def test_ops_match_oracle():
     idx = torch.empty(1, dtype=torch.int32, device=dev)
     assert L.hoard_hx_argmax(_ptr(vals), 5000, _ptr(idx), s) == 0
     assert int(idx.item()) == 123
+
+
+def test_speculative_loop_is_lossless():
+    """Draft with the top-1 expert, verify k tokens in one batched forward (MoE at T = k), accept the
+    matching prefix: the tokens equal plain greedy decoding's."""
+    cfg = QWEN_S
+    dev = torch.device("cuda", 0)
+    model = hx.DecodeModel(cfg, hx.seeded_tensors(cfg, seed=12, device=dev), device=0, max_ctx=128)
+    try:
+        prompt = np.random.default_rng(6).integers(0, cfg.n_vocab, N_PROMPT).tolist()
+        want = model.generate(prompt, 48)
+        got, st = model.speculative_generate(prompt, 48, k_draft=4)
+        assert got == want
+        assert st["rounds"] > 0 and 0 <= st["accepted"] <= st["proposed"]
+        assert model.generate(prompt, 48) == want          # the top-k override was restored
+    finally:
+        model.close()
