@@ -211,39 +211,24 @@ __device__ __forceinline__ int q4_min_dot(const Q4Scales& s, const int* bs32) {
            (int)((s.m_hi >> 16) & 0xFF) * b1.z + (int)(s.m_hi >> 24) * b1.w;
 }
 
-// Warp 0's router tail for E <= 32*NV: router sums (RACC_COPIES partial copies) -> logits ->
-// softmax over all E (double sum, as ggml's soft_max) -> top-k -> optional renormalisation with
-// clamp. Each lane sorts its NV probabilities once; every round takes the warp-wide maximum of the
-// lanes' heads (non-negative floats order as unsigned integers) and, among equal values, the
-// lowest expert id. Lanes < k leave expert id and weight of rank `lane` in s_sel / s_w.
+// Warp 0's router tail for E <= 32*NV, in two parts so that the expert copies can be issued between
+// them. route_select: logits -> top-k. The logits are selected in descending order (ties to the
+// lower expert id): softmax is monotonic, so this is the order of the probabilities except where
+// two different logits round to the same probability (a tie far below any parity tolerance). Each
+// lane sorts its NV logits once; every round takes the warp-wide maximum of the lanes' heads (keys
+// are order-preserving unsigned images of the floats) and, among equal keys, the lowest expert id.
+// Lanes < k leave expert id and logit of rank `lane` in s_sel and *my_logit.
 template <int NV>
-__device__ __forceinline__ void route_warp(const double* s_lgd, int E, int k, int renorm, float scale, int lane,
-                                           int* s_sel, float* s_w, int32_t* sel_out, float* w_out,
-                                           unsigned long long* st) {
-    float p[NV];
-#pragma unroll
-    for (int i = 0; i < NV; ++i) p[i] = lane + 32 * i < E ? (float)((double)scale * s_lgd[lane + 32 * i]) : -INFINITY;
-    float mx = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) mx = fmaxf(mx, p[i]);
-    mx = warp_max(mx);
-    double sum = 0.0;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-        if (lane + 32 * i < E) {
-            p[i] = expf(p[i] - mx);
-            sum += (double)p[i];
-        }
-    }
-    sum = warp_sum(sum);
-    const float inv = (float)(1.0 / sum);
-    if (st && lane == 0) st[0] = gtimer();
+__device__ __forceinline__ void route_select(const double* s_lgd, int E, int k, float scale, int lane, int* s_sel,
+                                             float* my_logit) {
     unsigned key[NV], idx[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-        const bool valid = lane + 32 * i < E;
-        key[i] = valid ? __float_as_uint(p[i] * inv) + 1u : 0u;
-        idx[i] = (unsigned)(lane + 32 * i);
+        const int e = lane + 32 * i;
+        const float p = e < E ? (float)((double)scale * s_lgd[e]) : 0.f;
+        const unsigned u = __float_as_uint(p);
+        key[i] = e < E ? ((u & 0x80000000u) ? ~u : (u | 0x80000000u)) : 0u;
+        idx[i] = (unsigned)e;
     }
 #pragma unroll
     for (int i = 1; i < NV; ++i) {
@@ -257,9 +242,8 @@ __device__ __forceinline__ void route_warp(const double* s_lgd, int E, int k, in
             idx[j] = sw ? i0 : idx[j];
         }
     }
-    if (st && lane == 0) st[1] = gtimer();
-    float my_w = 0.f, wsum = 0.f;
     int my_sel = 0;
+    unsigned my_key = 0;
     for (int r = 0; r < k; ++r) {
         const unsigned M = __reduce_max_sync(0xFFFFFFFFu, key[0]);
         const unsigned W = __reduce_min_sync(0xFFFFFFFFu, key[0] == M ? idx[0] : 0xFFFFFFFFu);
@@ -268,19 +252,43 @@ __device__ __forceinline__ void route_warp(const double* s_lgd, int E, int k, in
             for (int i = 0; i + 1 < NV; ++i) { key[i] = key[i + 1]; idx[i] = idx[i + 1]; }
             key[NV - 1] = 0u;
         }
-        const float wv = __uint_as_float(M - 1u);
-        wsum += wv;                               // sequential in rank order, as hoard's host loop
-        if (lane == r) { my_w = wv; my_sel = (int)W; }
+        if (lane == r) { my_sel = (int)W; my_key = M; }
     }
-    if (st && lane == 0) st[2] = gtimer();
+    if (lane < k) s_sel[lane] = my_sel;
+    const unsigned u = (my_key & 0x80000000u) ? (my_key & 0x7FFFFFFFu) : ~my_key;
+    *my_logit = __uint_as_float(u);
+}
+
+// route_weights: softmax over all E (max subtracted, double sum, as ggml's soft_max) evaluated at
+// the selected logits, then the optional renormalisation with clamp (sum in rank order, as hoard's
+// host loop). Lanes < k leave the weight of rank `lane` in s_w (and sel_out / w_out).
+template <int NV>
+__device__ __forceinline__ void route_weights(const double* s_lgd, int E, int k, int renorm, float scale, int lane,
+                                              float my_logit, const int* s_sel, float* s_w, int32_t* sel_out,
+                                              float* w_out) {
+    float p[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) p[i] = lane + 32 * i < E ? (float)((double)scale * s_lgd[lane + 32 * i]) : -INFINITY;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) mx = fmaxf(mx, p[i]);
+    mx = warp_max(mx);
+    double sum = 0.0;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+        if (lane + 32 * i < E) sum += (double)expf(p[i] - mx);
+    sum = warp_sum(sum);
+    const float inv = (float)(1.0 / sum);
+    float my_w = lane < k ? expf(my_logit - mx) * inv : 0.f;
+    float wsum = 0.f;
+    for (int r = 0; r < k; ++r) wsum += __shfl_sync(0xFFFFFFFFu, my_w, r);
     if (renorm) {
         if (wsum < 6.103515625e-5f) wsum = 6.103515625e-5f;
         my_w /= wsum;
     }
     if (lane < k) {
-        s_sel[lane] = my_sel;
         s_w[lane] = my_w;
-        if (sel_out) { sel_out[lane] = my_sel; w_out[lane] = my_w; }
+        if (sel_out) { sel_out[lane] = s_sel[lane]; w_out[lane] = my_w; }
     }
 }
 
@@ -528,6 +536,16 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
         int8_t* fxq = reinterpret_cast<int8_t*>(smem + P.off_fxq);
         float* fxd = reinterpret_cast<float*>(smem + P.off_fxd);
         int* fxbs32 = reinterpret_cast<int*>(smem + P.off_fxbs32);
+        // the byte counts of this layer's copies do not depend on the routing: post them first
+        if (warp == 0 && alive) {
+            if (lane < NCH) {
+                mbar_expect_tx(bar_gu + lane, s_gu_bytes[lane]);
+            } else if (lane == NCH) {
+                mbar_expect_tx(bar_dn, L_dt == T_Q4K ? dn_bytes_q4 : dn_bytes_q6);
+            } else if (lane == NCH + 1 && has_next) {
+                mbar_expect_tx(bar_wt, wt_bytes + (unsigned)(wn_hi - wn_lo));
+            }
+        }
         // router sums: every thread t <= E adds the RACC_COPIES partial copies of entry t (one L2 round trip)
         {
             const double* racc = a.racc + (int64_t)buf * racc_stride;
@@ -542,34 +560,36 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
         DEC_TR(l, 19);
         const float scale = 1.0f / sqrtf((float)(s_lgd[E] / H) + a.eps);
         if (warp == 0) {
-            int32_t* so = (c == 0 && a.sel_out) ? a.sel_out + (int64_t)l * k : nullptr;
-            float* wo = (c == 0 && a.sel_out) ? a.w_out + (int64_t)l * k : nullptr;
-            if (E <= 64) route_warp<2>(s_lgd, E, k, a.renorm, scale, lane, s_sel, s_w, so, wo, DEC_TRP(l, 1));
-            else if (E <= 128) route_warp<4>(s_lgd, E, k, a.renorm, scale, lane, s_sel, s_w, so, wo, DEC_TRP(l, 1));
-            else if (E <= 256) route_warp<8>(s_lgd, E, k, a.renorm, scale, lane, s_sel, s_w, so, wo, DEC_TRP(l, 1));
-            else route_warp<16>(s_lgd, E, k, a.renorm, scale, lane, s_sel, s_w, so, wo, DEC_TRP(l, 1));
+            // top-k on the logits, then the copies, then the weights (softmax) while the bytes fly
+            float my_logit;
+            if (E <= 64) route_select<2>(s_lgd, E, k, scale, lane, s_sel, &my_logit);
+            else if (E <= 128) route_select<4>(s_lgd, E, k, scale, lane, s_sel, &my_logit);
+            else if (E <= 256) route_select<8>(s_lgd, E, k, scale, lane, s_sel, &my_logit);
+            else route_select<16>(s_lgd, E, k, scale, lane, s_sel, &my_logit);
             __syncwarp();
+            DEC_TR(l, 1);
             // ---- B. this CTA's copies for the whole layer (descriptors precomputed at launch) ----
             if (alive) {
-                if (lane < NCH) {
-                    mbar_expect_tx(bar_gu + lane, s_gu_bytes[lane]);
-                } else if (lane == NCH) {
-                    mbar_expect_tx(bar_dn, L_dt == T_Q4K ? dn_bytes_q4 : dn_bytes_q6);
-                } else if (lane == NCH + 1 && has_next) {
-                    mbar_expect_tx(bar_wt, wt_bytes + (unsigned)(wn_hi - wn_lo));
+                const int4 d = s_cd_gu[lane];
+                const unsigned meta = (unsigned)d.w;
+                if (meta >> 29) {
+                    const int j = (meta >> 20) & 31, ch = (meta >> 25) & 7;
+                    const int64_t src = ((int64_t)(unsigned)d.y << 32) | (unsigned)d.x;
+                    const uint8_t* base = L_pool + (int64_t)s_sel[j] * L_stride + (((meta >> 28) & 1) ? L_off_up : 0);
+                    bulk_g2s(smem + d.z, base + src, meta & 0xFFFFFu, bar_gu + ch);
                 }
-                __syncwarp();
-                DEC_TR(l, 18);
-                {
-                    const int4 d = s_cd_gu[lane];
-                    const unsigned meta = (unsigned)d.w;
-                    if (meta >> 29) {
-                        const int j = (meta >> 20) & 31, ch = (meta >> 25) & 7;
-                        const int64_t src = ((int64_t)(unsigned)d.y << 32) | (unsigned)d.x;
-                        const uint8_t* base = L_pool + (int64_t)s_sel[j] * L_stride + (((meta >> 28) & 1) ? L_off_up : 0);
-                        bulk_g2s(smem + d.z, base + src, meta & 0xFFFFFu, bar_gu + ch);
-                    }
-                }
+            }
+            DEC_TR(l, 2);
+            {
+                int32_t* so = (c == 0 && a.sel_out) ? a.sel_out + (int64_t)l * k : nullptr;
+                float* wo = (c == 0 && a.sel_out) ? a.w_out + (int64_t)l * k : nullptr;
+                if (E <= 64) route_weights<2>(s_lgd, E, k, a.renorm, scale, lane, my_logit, s_sel, s_w, so, wo);
+                else if (E <= 128) route_weights<4>(s_lgd, E, k, a.renorm, scale, lane, my_logit, s_sel, s_w, so, wo);
+                else if (E <= 256) route_weights<8>(s_lgd, E, k, a.renorm, scale, lane, my_logit, s_sel, s_w, so, wo);
+                else route_weights<16>(s_lgd, E, k, a.renorm, scale, lane, my_logit, s_sel, s_w, so, wo);
+            }
+            DEC_TR(l, 3);
+            if (alive) {
                 // the down rows are needed only after the gate/up phase: issue them once the first
                 // gate/up chunk has landed, so that gate/up bytes are not queued behind them
                 if (!mbar_wait(bar_gu + 1, ph_gu)) { atomicOr(&a.sync[0], 2u); alive = false; }
