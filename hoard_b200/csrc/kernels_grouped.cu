@@ -84,29 +84,61 @@ constexpr int RL_TARGET_CTAS = 296;
 
 constexpr int RMS_MAXV = 32;   // H <= 8192: values per thread held in registers
 
-template <typename R>
+// VPT values per thread (a multiple of 4, loaded 4 at a time; H a multiple of 4)
+template <typename R> struct Vec4;
+template <> struct Vec4<float> {
+    static __device__ __forceinline__ void load(const float* p, float* v) {
+        const float4 a = *reinterpret_cast<const float4*>(p);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    }
+};
+template <> struct Vec4<__nv_bfloat16> {
+    static __device__ __forceinline__ void load(const __nv_bfloat16* p, float* v) {
+        const uint2 a = *reinterpret_cast<const uint2*>(p);
+        v[0] = __uint_as_float(a.x << 16); v[1] = __uint_as_float(a.x & 0xFFFF0000u);
+        v[2] = __uint_as_float(a.y << 16); v[3] = __uint_as_float(a.y & 0xFFFF0000u);
+    }
+};
+
+template <typename R, int VPT>
 __global__ void __launch_bounds__(256) k_rmsnorm(const R* __restrict__ x, int H, float eps,
                                                  const float* __restrict__ w_norm, float* __restrict__ fx) {
     __shared__ double redd[32];
     const int64_t t = blockIdx.x;
     const R* xr = x + t * H;
-    float v[RMS_MAXV];
+    float v[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT / 4; ++j) {
+        const int i = 4 * (threadIdx.x + 256 * j);
+        if (i < H) Vec4<R>::load(xr + i, v + 4 * j);
+        else v[4 * j] = v[4 * j + 1] = v[4 * j + 2] = v[4 * j + 3] = 0.f;
+    }
     double ss = 0.0;
 #pragma unroll
-    for (int j = 0; j < RMS_MAXV; ++j) {
-        const int i = threadIdx.x + 256 * j;
-        v[j] = i < H ? to_f32<R>(xr[i]) : 0.f;
-    }
-#pragma unroll
-    for (int j = 0; j < RMS_MAXV; ++j) ss += (double)(v[j] * v[j]);
+    for (int j = 0; j < VPT; ++j) ss += (double)(v[j] * v[j]);
     ss = block_sum_d(ss, redd);
     const float mean = (float)(ss / H);
     const float scale = 1.0f / sqrtf(mean + eps);
 #pragma unroll
-    for (int j = 0; j < RMS_MAXV; ++j) {
-        const int i = threadIdx.x + 256 * j;
-        if (i < H) fx[t * H + i] = (v[j] * scale) * w_norm[i];
+    for (int j = 0; j < VPT / 4; ++j) {
+        const int i = 4 * (threadIdx.x + 256 * j);
+        if (i < H) {
+            const float4 w = *reinterpret_cast<const float4*>(w_norm + i);
+            *reinterpret_cast<float4*>(fx + t * H + i) =
+                make_float4((v[4 * j] * scale) * w.x, (v[4 * j + 1] * scale) * w.y, (v[4 * j + 2] * scale) * w.z,
+                            (v[4 * j + 3] * scale) * w.w);
+        }
     }
+}
+
+template <typename R>
+cudaError_t launch_rmsnorm_rows(const R* x, int rows, int H, float eps, const float* w, float* out, cudaStream_t s) {
+    if (rows <= 0 || H <= 0 || H % 4 || H > 256 * RMS_MAXV) return cudaErrorInvalidValue;
+    if (H <= 1024) k_rmsnorm<R, 4><<<rows, 256, 0, s>>>(x, H, eps, w, out);
+    else if (H <= 2048) k_rmsnorm<R, 8><<<rows, 256, 0, s>>>(x, H, eps, w, out);
+    else if (H <= 4096) k_rmsnorm<R, 16><<<rows, 256, 0, s>>>(x, H, eps, w, out);
+    else k_rmsnorm<R, 32><<<rows, 256, 0, s>>>(x, H, eps, w, out);
+    return cudaGetLastError();
 }
 
 // grid (ceil(T/32), ceil(E/128), ksplit); CTA z covers K range [z*klen, (z+1)*klen)
@@ -182,11 +214,11 @@ __global__ void __launch_bounds__(256) k_router_logits(const float* __restrict__
 // 8 tokens per CTA: all 256 threads sum the K splits into shared memory (independent loads), then
 // one warp per token does softmax + top-k (E <= 1024)
 constexpr int TOPK_TT = 8;
-constexpr int TOPK_MAXE = 1024;
 
+template <int NV>
 __global__ void __launch_bounds__(256) k_route_topk(const double* __restrict__ part, int ksplit, int T, int E, int k,
                                                     int renorm, int32_t* __restrict__ sel, float* __restrict__ w) {
-    __shared__ float lg[TOPK_TT][TOPK_MAXE];
+    __shared__ float lg[TOPK_TT][32 * NV];
     const int t0 = blockIdx.x * TOPK_TT;
     const int nt = min(TOPK_TT, T - t0);
     for (int i = threadIdx.x; i < nt * E; i += blockDim.x) {
@@ -200,7 +232,6 @@ __global__ void __launch_bounds__(256) k_route_topk(const double* __restrict__ p
     const int lane = threadIdx.x & 31, tt = threadIdx.x >> 5;
     if (tt >= nt) return;
     const int t = t0 + tt;
-    constexpr int NV = TOPK_MAXE / 32;
     float p[NV];
     float m = -INFINITY;
 #pragma unroll
@@ -362,10 +393,10 @@ int64_t router_partial_elems(int max_tokens, int E) {
 
 cudaError_t launch_route(const Dims& d, const LayerWeights& lw, const void* x, int T, float* fx, int32_t* sel,
                          float* w, double* part, cudaStream_t s, int* launches) {
-    if (d.resid_bf16)
-        k_rmsnorm<__nv_bfloat16><<<T, 256, 0, s>>>((const __nv_bfloat16*)x, d.H, d.eps, lw.w_norm, fx);
-    else
-        k_rmsnorm<float><<<T, 256, 0, s>>>((const float*)x, d.H, d.eps, lw.w_norm, fx);
+    cudaError_t e0 = d.resid_bf16
+        ? launch_rmsnorm_rows((const __nv_bfloat16*)x, T, d.H, d.eps, lw.w_norm, fx, s)
+        : launch_rmsnorm_rows((const float*)x, T, d.H, d.eps, lw.w_norm, fx, s);
+    if (e0 != cudaSuccess) return e0;
     int ks;
     if (T >= RB_MIN_T && d.E % 4 == 0 && d.H % RB_KC == 0) {
         ks = router_ksplit_big(T, d.E, d.H);
@@ -376,7 +407,12 @@ cudaError_t launch_route(const Dims& d, const LayerWeights& lw, const void* x, i
         const dim3 grid((T + RL_TT - 1) / RL_TT, (d.E + RL_EB - 1) / RL_EB, ks);
         k_router_logits<<<grid, 256, 0, s>>>(fx, lw.w_router, T, d.H, d.E, d.H / ks, part);
     }
-    k_route_topk<<<(T + TOPK_TT - 1) / TOPK_TT, 256, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
+    const unsigned tgrid = (unsigned)((T + TOPK_TT - 1) / TOPK_TT);
+    if (d.E <= 64) k_route_topk<2><<<tgrid, 256, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
+    else if (d.E <= 128) k_route_topk<4><<<tgrid, 256, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
+    else if (d.E <= 256) k_route_topk<8><<<tgrid, 256, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
+    else if (d.E <= 512) k_route_topk<16><<<tgrid, 256, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
+    else k_route_topk<32><<<tgrid, 256, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
     if (launches) *launches += 3;
     return cudaGetLastError();
 }
@@ -817,9 +853,7 @@ __global__ void __launch_bounds__(512) k_disp_scatter(const int32_t* __restrict_
 
 cudaError_t launch_rmsnorm_f32(const float* x, int rows, int cols, float eps, const float* w, float* out,
                                cudaStream_t s) {
-    if (rows <= 0 || cols <= 0 || cols > 256 * RMS_MAXV) return cudaErrorInvalidValue;
-    k_rmsnorm<float><<<rows, 256, 0, s>>>(x, cols, eps, w, out);
-    return cudaGetLastError();
+    return launch_rmsnorm_rows(x, rows, cols, eps, w, out, s);
 }
 
 cudaError_t launch_quant_q8(const float* x, int rows, int K, int8_t* q, float* d, int* bs, cudaStream_t s) {
