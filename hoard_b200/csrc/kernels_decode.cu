@@ -306,7 +306,9 @@ struct DecodePlan {
     int64_t off_dn, off_wt, off_wn, off_fxq, off_fxd, off_fxbs32, off_hq, off_hd, off_hbs, off_y, off_xs,
         off_misc, total;
 
-    __host__ __device__ void init(int H_, int E_, int k_, int I_, int dt_, int G) {
+    // alias: the down rows go to the start of the gate/up region (issued once the CTA's gate/up rows
+    // are consumed) when both shares do not fit in shared memory together
+    __host__ __device__ void init(int H_, int E_, int k_, int I_, int dt_, int G, int alias = 0) {
         H = H_; E = E_; k = k_; I = I_; dt = dt_;
         nbH = H / QK; nbI = I / QK;
         np_max = (k * I + G - 1) / G;
@@ -332,7 +334,12 @@ struct DecodePlan {
         dn_p0 = 0;
         if (dt == T_Q4K) { dn_p1 = q4_p1; dn_p2 = q4_end; dn_p3 = q4_end; }
         else { dn_p1 = q6_p1; dn_p2 = q6_p2; dn_p3 = q6_p3; }
-        off_dn = o; o += (int64_t)k * dn_stride;
+        if (alias) {
+            off_dn = off_gate_qs;
+            o = o > off_dn + (int64_t)k * dn_stride ? o : off_dn + (int64_t)k * dn_stride;
+        } else {
+            off_dn = o; o += (int64_t)k * dn_stride;
+        }
         off_wt = o; o += a16((int64_t)nr_max * E * 4) + 16;
         off_wn = o; o += a16((int64_t)nr_max * 4) + 32;
         off_fxq = o; o += (int64_t)nbH * ACT_BLK + 16;
@@ -363,6 +370,7 @@ struct DecodeArgs {
     double* racc;               // [2][RACC_COPIES][E+1]
     unsigned* sync;             // [0] error bits, [1] barrier counter, [2] exit counter
     unsigned long long* trace;  // optional [G][n_layers][DEC_TRACE_PHASES] %globaltimer stamps
+    int alias_dn;               // DecodePlan alias mode (down rows over the consumed gate/up rows)
 };
 
 // NV = router logits per lane (E <= 32 * NV): one instantiation per width keeps only the routing code
@@ -409,7 +417,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
     const int ngroups = (np + RPW - 1) / RPW;
 
     DecodePlan P;
-    P.init(H, E, k, I, a.lw[0].down_type, G);
+    P.init(H, E, k, I, a.lw[0].down_type, G, a.alias_dn);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.off_misc);
     uint64_t* bar_gu = bars;                // [NCH]
     uint64_t* bar_dn = bars + NCH;
@@ -474,7 +482,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
         const int64_t nblk_dn = (int64_t)H * nbI;
         for (int tsel = 0; tsel < 2; ++tsel) {
             DecodePlan Pt;
-            Pt.init(H, E, k, I, tsel == 0 ? T_Q4K : T_Q6K, G);
+            Pt.init(H, E, k, I, tsel == 0 ? T_Q4K : T_Q6K, G, a.alias_dn);
             const int nplanes = tsel == 0 ? 2 : 4;
             for (int ci = lane; ci < k * nplanes; ci += 32) {
                 const int j = ci / nplanes, pl = ci - j * nplanes;
@@ -530,12 +538,24 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
         const bool has_next = l + 1 < a.n_layers;
         const float* Ln_wrt = has_next ? a.lw[l + 1].w_router_t : nullptr;
         const float* Ln_wnorm = has_next ? a.lw[l + 1].w_norm : nullptr;
-        P.init(H, E, k, I, L_dt, G);
+        P.init(H, E, k, I, L_dt, G, a.alias_dn);
         DEC_TR(l, 0);
         // ---- A/B. warp 0: router sums -> softmax -> top-k -> copies -> renorm, all in registers;
         //      warps 1..: fx = rms_norm(x) * ffn_norm -> Q8_K (named barriers, no CTA-wide sync) ------
         const bool issued = alive;
         const bool issued_wt = alive && has_next;
+        auto issue_down = [&]() {                       // warp 0: this CTA's down rows of every selected expert
+            const int tsel = L_dt == T_Q4K ? 0 : 1;
+            const int n_dn = k * (L_dt == T_Q4K ? 2 : 4);
+            for (int ci = lane; ci < n_dn; ci += 32) {
+                const int4 d = s_cd_dn[tsel][ci];
+                const unsigned meta = (unsigned)d.w;
+                const int j = (meta >> 20) & 31;
+                const int64_t src = ((int64_t)(unsigned)d.y << 32) | (unsigned)d.x;
+                bulk_g2s(smem + d.z, L_pool + (int64_t)s_sel[j] * L_stride + L_off_down + src, meta & 0xFFFFFu,
+                         bar_dn);
+            }
+        };
         int8_t* fxq = reinterpret_cast<int8_t*>(smem + P.off_fxq);
         float* fxd = reinterpret_cast<float*>(smem + P.off_fxd);
         int* fxbs32 = reinterpret_cast<int*>(smem + P.off_fxbs32);
@@ -588,17 +608,11 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
             DEC_TR(l, 3);
             if (alive) {
                 // the down rows are needed only after the gate/up phase: issue them once the first
-                // gate/up chunk has landed, so that gate/up bytes are not queued behind them
-                if (!mbar_wait(bar_gu + 1, ph_gu)) { atomicOr(&a.sync[0], 2u); alive = false; }
-                const int tsel = L_dt == T_Q4K ? 0 : 1;
-                const int n_dn = k * (L_dt == T_Q4K ? 2 : 4);
-                for (int ci = lane; ci < n_dn; ci += 32) {
-                    const int4 d = s_cd_dn[tsel][ci];
-                    const unsigned meta = (unsigned)d.w;
-                    const int j = (meta >> 20) & 31;
-                    const int64_t src = ((int64_t)(unsigned)d.y << 32) | (unsigned)d.x;
-                    bulk_g2s(smem + d.z, L_pool + (int64_t)s_sel[j] * L_stride + L_off_down + src, meta & 0xFFFFFu,
-                             bar_dn);
+                // gate/up chunk has landed, so that gate/up bytes are not queued behind them (in the
+                // alias mode, after this CTA's gate/up rows are consumed)
+                if (!a.alias_dn) {
+                    if (!mbar_wait(bar_gu + 1, ph_gu)) { atomicOr(&a.sync[0], 2u); alive = false; }
+                    issue_down();
                 }
                 if (has_next && lane == 0) bulk_g2s(wt, Ln_wrt + (int64_t)d0 * E, wt_bytes, bar_wt);
                 if (has_next && lane == 1)
@@ -718,6 +732,10 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
             s_amax[tid] = 0u;
         }
         __syncthreads();
+        if (a.alias_dn && warp == 0 && issued) {       // every warp is done with the gate/up rows
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue_down();
+        }
         if (tid == 0 && alive) {
             asm volatile("fence.acq_rel.gpu;" ::: "memory");
             for (int b = q0 / QK; b <= (q1 - 1) / QK; ++b)
@@ -949,15 +967,29 @@ int decode_grid() {
 }
 int decode_trace_phases() { return DEC_TRACE_PHASES; }
 
+// 0: both shares fit in shared memory, 1: only with the down rows over the gate/up rows, -1: neither
+static int decode_alias_mode(const Dims& d, int G) {
+    int dev = 0, max_smem = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    for (int alias = 0; alias < 2; ++alias) {
+        int64_t need = 0;
+        for (int dt : {(int)T_Q4K, (int)T_Q6K}) {
+            DecodePlan P;
+            P.init(d.H, d.E, d.k, d.I, dt, G, alias);
+            need = need > P.total ? need : P.total;
+        }
+        if (need + 1024 <= max_smem) return alias;       // + static shared memory
+    }
+    return -1;
+}
+
 bool decode_supported(const Dims& d, const LayerWeights* lws, int n_layers) {
     if (d.k > 16 || d.E % 4 != 0 || d.E > 512) return false;
     const int nbH = d.H / QK, nbI = d.I / QK;
     if (nbH > 32 || (nbH & (nbH - 1)) != 0) return false;    // lanes per gate/up row: a power of two <= 32
     if (nbI > 4) return false;                                // down rows: one lane per block, 4 lanes per item
     const int G = decode_grid();
-    int dev = 0, max_smem = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if ((int64_t)d.k * d.I < G || d.H < G) return false;     // every CTA must own rows
     if ((d.k * d.I + G - 1) / G > d.I) return false;          // a CTA's pairs span at most 2 experts
     for (int l = 0; l < n_layers; ++l) {
@@ -965,11 +997,8 @@ bool decode_supported(const Dims& d, const LayerWeights* lws, int n_layers) {
         if (L.gate_type != T_Q4K || L.up_type != T_Q4K) return false;
         if (L.down_type != T_Q4K && L.down_type != T_Q6K) return false;
         if (L.shared) return false;
-        DecodePlan P;
-        P.init(d.H, d.E, d.k, d.I, L.down_type, G);
-        if (P.total + 1024 > max_smem) return false;   // + static shared memory
     }
-    return true;
+    return decode_alias_mode(d, G) >= 0;
 }
 
 template <typename R, bool TRACE>
@@ -988,10 +1017,12 @@ cudaError_t launch_decode_persistent(const Dims& d, const LayerWeights* lws_dev,
                                      unsigned long long* trace) {
     if (T != 1) return cudaErrorInvalidValue;
     const int G = decode_grid();
+    const int alias = decode_alias_mode(d, G);
+    if (alias < 0) return cudaErrorInvalidValue;
     int64_t smem = 0;
     for (int dt : {(int)T_Q4K, (int)T_Q6K}) {
         DecodePlan P;
-        P.init(d.H, d.E, d.k, d.I, dt, G);
+        P.init(d.H, d.E, d.k, d.I, dt, G, alias);
         smem = smem > P.total ? smem : P.total;
     }
     DecodeArgs a;
@@ -1006,6 +1037,7 @@ cudaError_t launch_decode_persistent(const Dims& d, const LayerWeights* lws_dev,
     a.racc = reinterpret_cast<double*>(sc.partials);
     a.sync = sc.sync;
     a.trace = trace;
+    a.alias_dn = alias;
     void* args[] = {&a};
     const int nv = d.E <= 64 ? 2 : d.E <= 128 ? 4 : d.E <= 256 ? 8 : 16;
     const void* fn = decode_fn(d.resid_bf16 != 0, nv, trace != nullptr);

@@ -253,13 +253,14 @@ def test_layer_stack_equals_sequential_layers():
     ctx.close()
 
 
-@pytest.mark.parametrize("resid", [torch.float32, torch.bfloat16])
-def test_decode_persistent_matches_grouped_and_oracle(resid):
+@pytest.mark.parametrize("resid,I", [(torch.float32, 768), (torch.bfloat16, 768), (torch.float32, 1024)])
+def test_decode_persistent_matches_grouped_and_oracle(resid, I):
     """T = 1 through the persistent fused kernel (the default for decode) vs the grouped kernels
-    and vs the oracle, over a 4-layer stack with both down types (Q6_K even, Q4_K odd)."""
-    spec = LayerSpec(H=2048, E=64, k=8, I=768)
+    and vs the oracle, over a 4-layer stack with both down types (Q6_K even, Q4_K odd). I = 1024
+    (OLMoE's expert width) needs the shared-memory plan whose down rows reuse the gate/up rows."""
+    spec = LayerSpec(H=2048, E=64, k=8, I=I)
     types = [Q6_K, Q4_K, Q6_K, Q4_K]
-    Ls = [make_layer(LayerSpec(H=2048, E=64, k=8, I=768, types=(Q4_K, Q4_K, t)), seed=500 + i)
+    Ls = [make_layer(LayerSpec(H=2048, E=64, k=8, I=I, types=(Q4_K, Q4_K, t)), seed=500 + i)
           for i, t in enumerate(types)]
     ctx = make_ctx(spec, n_layer=4, down_types=types, resid=resid, max_tokens=2)
     for i, L in enumerate(Ls):
@@ -273,7 +274,10 @@ def test_decode_persistent_matches_grouped_and_oracle(resid):
         x = torch.from_numpy(x_np).cuda(DEV).to(resid)
         sel = torch.empty(4, 1, ctx.k, dtype=torch.int32, device=x.device)
         w = torch.empty(4, 1, ctx.k, device=x.device)
+        n0 = ctx.launch_count
         ctx.layers(0, 4, x, sel, w)
+        if impl == 1:
+            assert ctx.launch_count - n0 == 1          # the persistent kernel served the whole stack
         ctx.sync_status()
         outs[impl] = (x.float().cpu().numpy(), sel.cpu().numpy(), w.cpu().numpy())
     assert np.array_equal(outs[0][1], outs[1][1])
