@@ -122,4 +122,54 @@ int hoard_hx_argmax_at(const float* v, int n, int32_t* seq, int32_t* pos, int se
     return st(launch_argmax(v, n, seq, pos, seq_len, (cudaStream_t)stream));
 }
 
+int hoard_hx_rmsnorm_q8(const float* x, int H, float eps, const float* w, void* q8, hoard_stream stream) {
+    if (!x || !w || !q8 || H <= 0 || H % 256 || H > 8192 || ((H / 256) & (H / 256 - 1))) return HOARD_EINVAL;
+    uint8_t* b = static_cast<uint8_t*>(q8);
+    return st(launch_rmsnorm_q8(x, H, eps, w, reinterpret_cast<int8_t*>(b), reinterpret_cast<float*>(b + al256(H)),
+                                reinterpret_cast<int*>(b + al256(H) + al256((int64_t)H / 256 * 4)), (cudaStream_t)stream));
+}
+
+int hoard_hx_gemv_multi(int n, const int* types, const void* const* w_planes, const int* N, int K, const void* q8,
+                        const float* const* resid, float* const* y, hoard_stream stream) {
+    if (n < 1 || n > 3 || !types || !w_planes || !N || !q8 || !y || K <= 0 || K % 256) return HOARD_EINVAL;
+    for (int m = 0; m < n; ++m)
+        if (!quant_type(types[m]) || !w_planes[m] || !y[m] || N[m] <= 0) return HOARD_EINVAL;
+    const uint8_t* b = static_cast<const uint8_t*>(q8);
+    return st(launch_qgemv_set(n, types, reinterpret_cast<const uint8_t* const*>(w_planes), N, K, resid, y,
+                               reinterpret_cast<const int8_t*>(b), reinterpret_cast<const float*>(b + al256(K)),
+                               reinterpret_cast<const int*>(b + al256(K) + al256((int64_t)K / 256 * 4)),
+                               (cudaStream_t)stream));
+}
+
+static int qknorm_check(const float* q, const float* k, const float* v, const float* qn, const float* kn, int mode,
+                        int n_head, int n_head_kv, int head_dim, const float* q_out, const void* kc, const void* vc) {
+    if (!q || !k || !v || !q_out || !kc || !vc || n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv ||
+        head_dim <= 0 || head_dim % 2 || head_dim > 256 || mode < 0 || mode > 2 || q_out == q)
+        return HOARD_EINVAL;
+    if (mode != 0 && (!qn || !kn)) return HOARD_EINVAL;
+    return HOARD_OK;
+}
+
+int hoard_hx_qknorm_rope_store(const float* q, const float* k, const float* v, const float* q_norm,
+                               const float* k_norm, int mode, float eps, int n_head, int n_head_kv, int head_dim,
+                               int pos, float freq_base, float* q_out, void* k_cache, void* v_cache,
+                               hoard_stream stream) {
+    int rc = qknorm_check(q, k, v, q_norm, k_norm, mode, n_head, n_head_kv, head_dim, q_out, k_cache, v_cache);
+    if (rc || pos < 0 || !(freq_base > 0)) return rc ? rc : HOARD_EINVAL;
+    return st(launch_qknorm_rope_store(q, k, v, q_norm, k_norm, mode, eps, n_head, n_head_kv, head_dim, pos, nullptr,
+                                       pos + 1, freq_base, q_out, static_cast<__half*>(k_cache),
+                                       static_cast<__half*>(v_cache), (cudaStream_t)stream));
+}
+
+int hoard_hx_qknorm_rope_store_at(const float* q, const float* k, const float* v, const float* q_norm,
+                                  const float* k_norm, int mode, float eps, int n_head, int n_head_kv, int head_dim,
+                                  const int32_t* pos, int max_ctx, float freq_base, float* q_out, void* k_cache,
+                                  void* v_cache, hoard_stream stream) {
+    int rc = qknorm_check(q, k, v, q_norm, k_norm, mode, n_head, n_head_kv, head_dim, q_out, k_cache, v_cache);
+    if (rc || !pos || max_ctx <= 0 || !(freq_base > 0)) return rc ? rc : HOARD_EINVAL;
+    return st(launch_qknorm_rope_store(q, k, v, q_norm, k_norm, mode, eps, n_head, n_head_kv, head_dim, 0, pos,
+                                       max_ctx, freq_base, q_out, static_cast<__half*>(k_cache),
+                                       static_cast<__half*>(v_cache), (cudaStream_t)stream));
+}
+
 }  // extern "C"

@@ -126,6 +126,15 @@ size_t attention_smem(int hd, int n_pos);
 cudaError_t launch_attention(const float* q, const __half* kc, const __half* vc, int n_head, int n_kv, int hd,
                              int n_pos, const int32_t* pos_dev, float scale, float* out, cudaStream_t s);
 cudaError_t launch_argmax(const float* v, int n, int32_t* out, int32_t* pos, int seq_len, cudaStream_t s);
+cudaError_t launch_rmsnorm_q8(const float* x, int H, float eps, const float* w, int8_t* q, float* d, int* bs,
+                              cudaStream_t s);
+cudaError_t launch_qgemv_set(int n, const int* types, const uint8_t* const* w, const int* N, int K,
+                             const float* const* resid, float* const* y, const int8_t* xq, const float* xd,
+                             const int* xbs, cudaStream_t s);
+cudaError_t launch_qknorm_rope_store(const float* q, const float* k, const float* v, const float* qn, const float* kn,
+                                     int mode, float eps, int n_head, int n_kv, int hd, int pos,
+                                     const int32_t* pos_dev, int max_ctx, float freq_base, float* q_out, __half* kc,
+                                     __half* vc, cudaStream_t s);
 
 // ---- expert parallelism over NVLink peer memory ----
 // Every rank allocates one block with this layout (identical on all ranks, so a peer's field is its

@@ -170,6 +170,138 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
     }
 }
 
+// ---- fused: out = RMSNorm(x) * w, quantised to Q8_K (one CTA; thread t holds value 256j + t of
+//      every 256-value block j, so a block's maximum is one CTA-wide reduction per j) ----
+template <int NB>
+__global__ void __launch_bounds__(256) k_rmsnorm_q8(const float* __restrict__ x, int H, float eps,
+                                                    const float* __restrict__ w, int8_t* __restrict__ q,
+                                                    float* __restrict__ d, int* __restrict__ bs) {
+    __shared__ double redd[32];
+    __shared__ float samax[8][NB];
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    float v[NB];
+    double ss = 0.0;
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+        v[j] = x[256 * j + t];
+        ss += (double)(v[j] * v[j]);
+    }
+    ss = block_sum_d(ss, redd);
+    const float scale = 1.0f / sqrtf((float)(ss / H) + eps);
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+        v[j] = (v[j] * scale) * w[256 * j + t];
+        const float am = warp_max(fabsf(v[j]));
+        if (lane == 0) samax[warp][j] = am;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+        float am = samax[0][j];
+#pragma unroll
+        for (int u = 1; u < 8; ++u) am = fmaxf(am, samax[u][j]);
+        int qi = 0;
+        float dd = 0.f;
+        if (am != 0.f) {
+            const float iscale = 127.f / am;
+            qi = min(127, __float2int_rn(iscale * v[j]));
+            dd = 1.f / iscale;
+        }
+        q[256 * j + t] = (int8_t)qi;
+        int sum = qi;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if ((t & 15) == 0) bs[16 * j + (t >> 4)] = sum;
+        if (t == 0) d[j] = dd;
+    }
+}
+
+// ---- several projections of one Q8_K activation in one launch: rows of the matrices back to back,
+//      one warp per row ----
+struct GemvSet {
+    const uint8_t* w[3];
+    float* y[3];
+    const float* resid[3];
+    int N[3];
+    int type[3];
+    int n;
+};
+__global__ void __launch_bounds__(256) k_qgemv_set(GemvSet g, int K, const int8_t* __restrict__ xq,
+                                                   const float* __restrict__ xd, const int* __restrict__ xbs) {
+    const int lane = threadIdx.x & 31;
+    int n = blockIdx.x * 8 + (threadIdx.x >> 5);
+    int m = 0;
+    while (m < g.n && n >= g.N[m]) n -= g.N[m++];
+    if (m >= g.n) return;
+    const int nb = K / QK;
+    const ActRow a{xq, xd, xbs};
+    const float v = warp_sum(g.type[m] == T_Q4K ? row_dot_lane<T_Q4K>(g.w[m], (int64_t)g.N[m] * nb, n, nb, a, lane)
+                                                : row_dot_lane<T_Q6K>(g.w[m], (int64_t)g.N[m] * nb, n, nb, a, lane));
+    if (lane == 0) g.y[m][n] = g.resid[m] ? v + g.resid[m][n] : v;
+}
+
+// ---- fused QK RMSNorm (mode 1: over the whole projection, weights [n*hd]; mode 2: per head, weights
+//      [hd]; 0: none) + NEOX RoPE + KV store: one CTA per q or k head, one thread per rotated pair.
+//      Rotated q goes to q_out (mode 1 reads the whole input vector in every CTA); rotated k and v
+//      go to the caches ----
+__global__ void __launch_bounds__(128) k_qknorm_rope_store(const float* __restrict__ q, const float* __restrict__ k,
+                                                           const float* __restrict__ v, const float* __restrict__ qn,
+                                                           const float* __restrict__ kn, int mode, float eps,
+                                                           int n_head, int n_kv, int hd, int pos,
+                                                           const int32_t* __restrict__ pos_dev, int max_ctx,
+                                                           float theta_scale, float* __restrict__ q_out,
+                                                           __half* __restrict__ kc, __half* __restrict__ vc) {
+    __shared__ double redd[32];
+    if (pos_dev) pos = *pos_dev;
+    if (pos < 0 || pos >= max_ctx) return;
+    const int head = blockIdx.x;
+    const bool isq = head < n_head;
+    const int hh = isq ? head : head - n_head;
+    const float* vec = isq ? q : k;
+    const int nvec = (isq ? n_head : n_kv) * hd;
+    const float* wn = isq ? qn : kn;
+    const int half = hd / 2, i = threadIdx.x;
+    float scale = 1.f;
+    if (mode != 0) {
+        double ss = 0.0;
+        if (mode == 1) {
+            for (int u = threadIdx.x; u < nvec; u += blockDim.x) ss += (double)(vec[u] * vec[u]);
+        } else {
+            for (int u = threadIdx.x; u < hd; u += blockDim.x) {
+                const float x = vec[hh * hd + u];
+                ss += (double)(x * x);
+            }
+        }
+        ss = block_sum_d(ss, redd);
+        scale = 1.0f / sqrtf((float)(ss / (mode == 1 ? nvec : hd)) + eps);
+    }
+    if (i < half) {
+        const float* xh = vec + (int64_t)hh * hd;
+        float x0 = xh[i], x1 = xh[i + half];
+        if (mode == 1) {
+            x0 = (x0 * scale) * wn[hh * hd + i];
+            x1 = (x1 * scale) * wn[hh * hd + i + half];
+        } else if (mode == 2) {
+            x0 = (x0 * scale) * wn[i];
+            x1 = (x1 * scale) * wn[i + half];
+        }
+        float theta = (float)pos;
+        for (int u = 0; u < i; ++u) theta *= theta_scale;
+        const float c = cosf(theta), sn = sinf(theta);
+        const float r0 = x0 * c - x1 * sn, r1 = x0 * sn + x1 * c;
+        if (isq) {
+            q_out[(int64_t)hh * hd + i] = r0;
+            q_out[(int64_t)hh * hd + i + half] = r1;
+        } else {
+            const int64_t o = ((int64_t)pos * n_kv + hh) * hd;
+            kc[o + i] = __float2half_rn(r0);
+            kc[o + i + half] = __float2half_rn(r1);
+            vc[o + i] = __float2half_rn(v[(int64_t)hh * hd + i]);
+            vc[o + i + half] = __float2half_rn(v[(int64_t)hh * hd + i + half]);
+        }
+    }
+}
+
 // ---- argmax (first index of the maximum) of n floats: one CTA of 1024 threads ----
 __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ v, int n, int32_t* __restrict__ out,
                                                  int32_t* __restrict__ pos, int seq_len) {
@@ -177,10 +309,26 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ v, in
     __shared__ int si[32];
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float x = v[i];
+    auto take = [&](float x, int i) {
         if (x > best || (x == best && i < bi)) { best = x; bi = i; }
+    };
+    // 16-byte loads, four in flight per thread (v is 16-byte aligned), then the scalar tail
+    const int n4 = (reinterpret_cast<uintptr_t>(v) & 15) ? 0 : n / 4;
+    const float4* v4 = reinterpret_cast<const float4*>(v);
+    for (int q0 = threadIdx.x; q0 < n4; q0 += 4 * blockDim.x) {
+        float4 c[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int q = q0 + u * blockDim.x;
+            c[u] = q < n4 ? v4[q] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int q = q0 + u * blockDim.x;
+            if (q < n4) { take(c[u].x, 4 * q); take(c[u].y, 4 * q + 1); take(c[u].z, 4 * q + 2); take(c[u].w, 4 * q + 3); }
+        }
     }
+    for (int i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) take(v[i], i);
     for (int o = 16; o > 0; o >>= 1) {
         const float ob = __shfl_xor_sync(0xffffffffu, best, o);
         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
@@ -211,6 +359,50 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ v, in
 }
 
 }  // namespace
+
+cudaError_t launch_rmsnorm_q8(const float* x, int H, float eps, const float* w, int8_t* q, float* d, int* bs,
+                              cudaStream_t s) {
+    switch (H / QK) {
+        case 1: k_rmsnorm_q8<1><<<1, 256, 0, s>>>(x, H, eps, w, q, d, bs); break;
+        case 2: k_rmsnorm_q8<2><<<1, 256, 0, s>>>(x, H, eps, w, q, d, bs); break;
+        case 4: k_rmsnorm_q8<4><<<1, 256, 0, s>>>(x, H, eps, w, q, d, bs); break;
+        case 8: k_rmsnorm_q8<8><<<1, 256, 0, s>>>(x, H, eps, w, q, d, bs); break;
+        case 16: k_rmsnorm_q8<16><<<1, 256, 0, s>>>(x, H, eps, w, q, d, bs); break;
+        case 32: k_rmsnorm_q8<32><<<1, 256, 0, s>>>(x, H, eps, w, q, d, bs); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_qgemv_set(int n, const int* types, const uint8_t* const* w, const int* N, int K,
+                             const float* const* resid, float* const* y, const int8_t* xq, const float* xd,
+                             const int* xbs, cudaStream_t s) {
+    if (n < 1 || n > 3) return cudaErrorInvalidValue;
+    GemvSet g{};
+    int64_t rows = 0;
+    for (int m = 0; m < n; ++m) {
+        g.w[m] = w[m];
+        g.y[m] = y[m];
+        g.resid[m] = resid ? resid[m] : nullptr;
+        g.N[m] = N[m];
+        g.type[m] = types[m];
+        rows += N[m];
+    }
+    g.n = n;
+    k_qgemv_set<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(g, K, xq, xd, xbs);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_qknorm_rope_store(const float* q, const float* k, const float* v, const float* qn, const float* kn,
+                                     int mode, float eps, int n_head, int n_kv, int hd, int pos,
+                                     const int32_t* pos_dev, int max_ctx, float freq_base, float* q_out, __half* kc,
+                                     __half* vc, cudaStream_t s) {
+    if (hd / 2 > 128) return cudaErrorInvalidValue;
+    const float theta_scale = powf(freq_base, -2.0f / (float)hd);
+    k_qknorm_rope_store<<<n_head + n_kv, 128, 0, s>>>(q, k, v, qn, kn, mode, eps, n_head, n_kv, hd, pos, pos_dev,
+                                                      max_ctx, theta_scale, q_out, kc, vc);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_embed(int type, const uint8_t* table, int H, int64_t n_vocab, const int32_t* token,
                          const int32_t* pos, float* out, cudaStream_t s) {

@@ -31,6 +31,15 @@ from hoard_b200.moe import HoardError, _ptr, _stream, lib
 
 Q4_K, Q6_K, F32 = quant.Q4_K, quant.Q6_K, 0
 MAX_BATCH = 16          # tokens of one batched (verify) forward
+QK_MODE = {"": 0, "full": 1, "head": 2}
+
+
+def _iarr(vals):
+    return (ctypes.c_int * len(vals))(*vals)
+
+
+def _parr(ptrs):
+    return (ctypes.c_void_p * len(ptrs))(*ptrs)
 
 _bound = False
 
@@ -54,6 +63,11 @@ def _hx():
         L.hoard_hx_rope_store_at.argtypes = [vp, vp, vp, i32, i32, i32, vp, i32, f32, vp, vp, vp]
         L.hoard_hx_attention_at.argtypes = [vp, vp, vp, i32, i32, i32, vp, i32, f32, vp, vp]
         L.hoard_hx_argmax_at.argtypes = [vp, i32, vp, vp, i32, vp]
+        L.hoard_hx_rmsnorm_q8.argtypes = [vp, i32, f32, vp, vp, vp]
+        L.hoard_hx_gemv_multi.argtypes = [i32, vp, vp, vp, i32, vp, vp, vp, vp]
+        L.hoard_hx_qknorm_rope_store.argtypes = [vp, vp, vp, vp, vp, i32, f32, i32, i32, i32, i32, f32, vp, vp, vp, vp]
+        L.hoard_hx_qknorm_rope_store_at.argtypes = [vp, vp, vp, vp, vp, i32, f32, i32, i32, i32, vp, i32, f32, vp, vp,
+                                                   vp, vp]
         _bound = True
     return L
 
@@ -192,6 +206,8 @@ class DecodeModel:
                  "o": plane(b + "attn_output.weight")}
             if cfg.qk_norm:
                 L["q_norm"], L["k_norm"] = f32(b + "attn_q_norm.weight"), f32(b + "attn_k_norm.weight")
+            L["qkv_types"] = _iarr([L[m][0] for m in ("q", "k", "v")])
+            L["qkv_w"] = _parr([L[m][1].data_ptr() for m in ("q", "k", "v")])
             self.layers.append(L)
         # the MoE layers: all experts resident, T = 1
         types = [tuple(tensors[f"blk.{il}.ffn_{m}_exps.weight"][0] for m in ("gate", "up", "down"))
@@ -211,6 +227,9 @@ class DecodeModel:
         self.x, self.x2, self.cur = z(H), z(H), z(H)
         self.q, self.k, self.v, self.att = z(self.nq), z(self.nkv), z(self.nkv), z(self.nq)
         self.logits = z(cfg.n_vocab)
+        self.q_rot = z(self.nq)
+        self.qkv_N = _iarr([self.nq, self.nkv, self.nkv])
+        self.qkv_y = _parr([self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr()])
         kq = max(H, self.nq)
         self.q8 = torch.zeros(int(_hx().hoard_hx_q8_bytes(kq)), dtype=torch.uint8, device=dev)
         self.kc = torch.zeros(cfg.n_layer, max_ctx, self.nkv, dtype=torch.float16, device=dev)
@@ -247,40 +266,36 @@ class DecodeModel:
             self._layer_attention(il, L, x, x2, hx, s, pos)
             self.moe.layers(il, 1, x2.view(1, H), stream=stream)
             x, x2 = x2, x
-        _ok(hx.hoard_hx_rmsnorm(_ptr(x), 1, H, c.eps, _ptr(self.out_norm), _ptr(self.cur), s), "rmsnorm")
-        _ok(hx.hoard_hx_quant_q8(_ptr(self.cur), H, _ptr(self.q8), s), "quant")
+        _ok(hx.hoard_hx_rmsnorm_q8(_ptr(x), H, c.eps, _ptr(self.out_norm), _ptr(self.q8), s), "rmsnorm_q8")
         _ok(hx.hoard_hx_gemv(self.out_type, _ptr(self.out_w), c.n_vocab, H, _ptr(self.q8), None, _ptr(self.logits), s),
             "gemv")
         _ok(hx.hoard_hx_argmax(_ptr(self.logits), c.n_vocab, _ptr(next_tok), s), "argmax")
 
-    def _layer_attention(self, il, L, x, x2, hx, s, pos=None):
-        """Graph A's attention part of layer il: x2 = Wo att + x. pos None: the device position."""
+    def _layer_attention(self, il, L, x, x2, hx, s, pos=None, bufs=None):
+        """Graph A's attention part of layer il: x2 = Wo att + x. pos None: the device position.
+        bufs: (q, k, v, q_rot, att, qkv_y) of one token of a batch (default: the step's own)."""
         c = self.cfg
         H, hd = c.n_embd, c.head_dim
-        _ok(hx.hoard_hx_rmsnorm(_ptr(x), 1, H, c.eps, _ptr(L["attn_norm"]), _ptr(self.cur), s), "rmsnorm")
-        _ok(hx.hoard_hx_quant_q8(_ptr(self.cur), H, _ptr(self.q8), s), "quant")
-        for key, out, n in (("q", self.q, self.nq), ("k", self.k, self.nkv), ("v", self.v, self.nkv)):
-            ty, wt = L[key]
-            _ok(hx.hoard_hx_gemv(ty, _ptr(wt), n, H, _ptr(self.q8), None, _ptr(out), s), "gemv")
-        if c.qk_norm == "full":
-            _ok(hx.hoard_hx_rmsnorm(_ptr(self.q), 1, self.nq, c.eps, _ptr(L["q_norm"]), _ptr(self.q), s), "qnorm")
-            _ok(hx.hoard_hx_rmsnorm(_ptr(self.k), 1, self.nkv, c.eps, _ptr(L["k_norm"]), _ptr(self.k), s), "knorm")
-        elif c.qk_norm == "head":
-            _ok(hx.hoard_hx_rmsnorm(_ptr(self.q), c.n_head, hd, c.eps, _ptr(L["q_norm"]), _ptr(self.q), s), "qnorm")
-            _ok(hx.hoard_hx_rmsnorm(_ptr(self.k), c.n_head_kv, hd, c.eps, _ptr(L["k_norm"]), _ptr(self.k), s), "knorm")
+        q, k, v, q_rot, att, qkv_y = bufs or (self.q, self.k, self.v, self.q_rot, self.att, self.qkv_y)
+        _ok(hx.hoard_hx_rmsnorm_q8(_ptr(x), H, c.eps, _ptr(L["attn_norm"]), _ptr(self.q8), s), "rmsnorm_q8")
+        _ok(hx.hoard_hx_gemv_multi(3, L["qkv_types"], L["qkv_w"], self.qkv_N, H, _ptr(self.q8), None, qkv_y, s),
+            "gemv qkv")
+        mode = QK_MODE[c.qk_norm]
+        qn, kn = (L["q_norm"], L["k_norm"]) if mode else (None, None)
         scale = 1.0 / math.sqrt(hd)
         if pos is None:
-            _ok(hx.hoard_hx_rope_store_at(_ptr(self.q), _ptr(self.k), _ptr(self.v), c.n_head, c.n_head_kv, hd,
-                                          _ptr(self.pos_dev), self.max_ctx, c.freq_base, _ptr(self.kc[il]),
-                                          _ptr(self.vc[il]), s), "rope")
-            _ok(hx.hoard_hx_attention_at(_ptr(self.q), _ptr(self.kc[il]), _ptr(self.vc[il]), c.n_head, c.n_head_kv, hd,
-                                         _ptr(self.pos_dev), self.max_ctx, scale, _ptr(self.att), s), "attention")
+            _ok(hx.hoard_hx_qknorm_rope_store_at(_ptr(q), _ptr(k), _ptr(v), _ptr(qn), _ptr(kn), mode, c.eps, c.n_head,
+                                                 c.n_head_kv, hd, _ptr(self.pos_dev), self.max_ctx, c.freq_base,
+                                                 _ptr(q_rot), _ptr(self.kc[il]), _ptr(self.vc[il]), s), "qk rope")
+            _ok(hx.hoard_hx_attention_at(_ptr(q_rot), _ptr(self.kc[il]), _ptr(self.vc[il]), c.n_head, c.n_head_kv, hd,
+                                         _ptr(self.pos_dev), self.max_ctx, scale, _ptr(att), s), "attention")
         else:
-            _ok(hx.hoard_hx_rope_store(_ptr(self.q), _ptr(self.k), _ptr(self.v), c.n_head, c.n_head_kv, hd, pos,
-                                       c.freq_base, _ptr(self.kc[il]), _ptr(self.vc[il]), s), "rope")
-            _ok(hx.hoard_hx_attention(_ptr(self.q), _ptr(self.kc[il]), _ptr(self.vc[il]), c.n_head, c.n_head_kv, hd,
-                                      pos + 1, scale, _ptr(self.att), s), "attention")
-        _ok(hx.hoard_hx_quant_q8(_ptr(self.att), self.nq, _ptr(self.q8), s), "quant")
+            _ok(hx.hoard_hx_qknorm_rope_store(_ptr(q), _ptr(k), _ptr(v), _ptr(qn), _ptr(kn), mode, c.eps, c.n_head,
+                                              c.n_head_kv, hd, pos, c.freq_base, _ptr(q_rot), _ptr(self.kc[il]),
+                                              _ptr(self.vc[il]), s), "qk rope")
+            _ok(hx.hoard_hx_attention(_ptr(q_rot), _ptr(self.kc[il]), _ptr(self.vc[il]), c.n_head, c.n_head_kv, hd,
+                                      pos + 1, scale, _ptr(att), s), "attention")
+        _ok(hx.hoard_hx_quant_q8(_ptr(att), self.nq, _ptr(self.q8), s), "quant")
         ty, wo = L["o"]
         _ok(hx.hoard_hx_gemv(ty, _ptr(wo), H, self.nq, _ptr(self.q8), _ptr(x), _ptr(x2), s), "gemv")
 
@@ -295,8 +310,7 @@ class DecodeModel:
             self._layer_attention(il, L, x, x2, hx, s)
             self.moe.layers(il, 1, x2.view(1, H), stream=stream)
             x, x2 = x2, x
-        _ok(hx.hoard_hx_rmsnorm(_ptr(x), 1, H, c.eps, _ptr(self.out_norm), _ptr(self.cur), s), "rmsnorm")
-        _ok(hx.hoard_hx_quant_q8(_ptr(self.cur), H, _ptr(self.q8), s), "quant")
+        _ok(hx.hoard_hx_rmsnorm_q8(_ptr(x), H, c.eps, _ptr(self.out_norm), _ptr(self.q8), s), "rmsnorm_q8")
         _ok(hx.hoard_hx_gemv(self.out_type, _ptr(self.out_w), c.n_vocab, H, _ptr(self.q8), None, _ptr(self.logits), s),
             "gemv")
         _ok(hx.hoard_hx_argmax_at(_ptr(self.logits), c.n_vocab, _ptr(self.seq), _ptr(self.pos_dev), self.seq.numel(), s),
@@ -353,38 +367,18 @@ class DecodeModel:
         for i in range(m):
             _ok(hx.hoard_hx_embed(self.embd_type, _ptr(self.embd), H, c.n_vocab, _ptr(self.seq[base + i:base + i + 1]),
                                   _ptr(xb[i]), s), "embed")
-        scale = 1.0 / math.sqrt(hd)
+        if not hasattr(self, "_qrb"):
+            self._qrb = torch.zeros(MAX_BATCH, self.nq, dtype=torch.float32, device=self.dev)
+            self._qkv_yb = [_parr([self._qb[i].data_ptr(), self._kb[i].data_ptr(), self._vb[i].data_ptr()])
+                            for i in range(MAX_BATCH)]
         for il, L in enumerate(self.layers):
-            _ok(hx.hoard_hx_rmsnorm(_ptr(xb), m, H, c.eps, _ptr(L["attn_norm"]), _ptr(cur), s), "rmsnorm")
             for i in range(m):
-                _ok(hx.hoard_hx_quant_q8(_ptr(cur[i]), H, _ptr(self.q8), s), "quant")
-                for key, out, n in (("q", self._qb, self.nq), ("k", self._kb, self.nkv), ("v", self._vb, self.nkv)):
-                    ty, wt = L[key]
-                    _ok(hx.hoard_hx_gemv(ty, _ptr(wt), n, H, _ptr(self.q8), None, _ptr(out[i]), s), "gemv")
-            if c.qk_norm == "full":
-                _ok(hx.hoard_hx_rmsnorm(_ptr(self._qb), m, self.nq, c.eps, _ptr(L["q_norm"]), _ptr(self._qb), s), "qnorm")
-                _ok(hx.hoard_hx_rmsnorm(_ptr(self._kb), m, self.nkv, c.eps, _ptr(L["k_norm"]), _ptr(self._kb), s), "knorm")
-            elif c.qk_norm == "head":
-                _ok(hx.hoard_hx_rmsnorm(_ptr(self._qb), m * c.n_head, hd, c.eps, _ptr(L["q_norm"]), _ptr(self._qb), s),
-                    "qnorm")
-                _ok(hx.hoard_hx_rmsnorm(_ptr(self._kb), m * c.n_head_kv, hd, c.eps, _ptr(L["k_norm"]), _ptr(self._kb),
-                                        s), "knorm")
-            for i in range(m):
-                _ok(hx.hoard_hx_rope_store(_ptr(self._qb[i]), _ptr(self._kb[i]), _ptr(self._vb[i]), c.n_head,
-                                           c.n_head_kv, hd, base + i, c.freq_base, _ptr(self.kc[il]),
-                                           _ptr(self.vc[il]), s), "rope")
-            for i in range(m):
-                _ok(hx.hoard_hx_attention(_ptr(self._qb[i]), _ptr(self.kc[il]), _ptr(self.vc[il]), c.n_head,
-                                          c.n_head_kv, hd, base + i + 1, scale, _ptr(self._attb[i]), s), "attention")
-            ty, wo = L["o"]
-            for i in range(m):
-                _ok(hx.hoard_hx_quant_q8(_ptr(self._attb[i]), self.nq, _ptr(self.q8), s), "quant")
-                _ok(hx.hoard_hx_gemv(ty, _ptr(wo), H, self.nq, _ptr(self.q8), _ptr(xb[i]), _ptr(x2b[i]), s), "gemv")
+                bufs = (self._qb[i], self._kb[i], self._vb[i], self._qrb[i], self._attb[i], self._qkv_yb[i])
+                self._layer_attention(il, L, xb[i], x2b[i], hx, s, base + i, bufs)
             self.moe.layers(il, 1, x2b[:m], stream=stream)
             xb, x2b = x2b, xb
-        _ok(hx.hoard_hx_rmsnorm(_ptr(xb), m, H, c.eps, _ptr(self.out_norm), _ptr(cur), s), "rmsnorm")
         for i in range(m):
-            _ok(hx.hoard_hx_quant_q8(_ptr(cur[i]), H, _ptr(self.q8), s), "quant")
+            _ok(hx.hoard_hx_rmsnorm_q8(_ptr(xb[i]), H, c.eps, _ptr(self.out_norm), _ptr(self.q8), s), "rmsnorm_q8")
             _ok(hx.hoard_hx_gemv(self.out_type, _ptr(self.out_w), c.n_vocab, H, _ptr(self.q8), None,
                                  _ptr(self._lgb[i]), s), "gemv")
         return self._lgb[:m].clone()

@@ -68,6 +68,25 @@ int hoard_hx_attention_at(const float* q, const void* k_cache, const void* v_cac
                           int head_dim, const int32_t* pos, int max_ctx, float scale, float* out, hoard_stream stream);
 int hoard_hx_argmax_at(const float* v, int n, int32_t* seq, int32_t* pos, int seq_len, hoard_stream stream);
 
+/* ---- fused forms of the steps above (fewer launches per layer) ----
+ * rmsnorm_q8: RMSNorm(x) * w of one vector (H a power-of-two multiple of 256, <= 8192) straight into
+ * a Q8_K workspace. gemv_multi: 1..3 projections of the same Q8_K activation (types, plane-layout
+ * weights, row counts, optional residuals and outputs are host arrays of n device pointers/values).
+ * qknorm_rope_store: QK RMSNorm (mode 0 none, 1 over the whole projection with weights
+ * [n_head*head_dim] / [n_head_kv*head_dim], 2 per head with weights [head_dim]) + NEOX RoPE + KV
+ * store; the rotated q is written to q_out (!= q). */
+int hoard_hx_rmsnorm_q8(const float* x, int H, float eps, const float* w, void* q8, hoard_stream stream);
+int hoard_hx_gemv_multi(int n, const int* types, const void* const* w_planes, const int* N, int K, const void* q8,
+                        const float* const* resid, float* const* y, hoard_stream stream);
+int hoard_hx_qknorm_rope_store(const float* q, const float* k, const float* v, const float* q_norm,
+                               const float* k_norm, int mode, float eps, int n_head, int n_head_kv, int head_dim,
+                               int pos, float freq_base, float* q_out, void* k_cache, void* v_cache,
+                               hoard_stream stream);
+int hoard_hx_qknorm_rope_store_at(const float* q, const float* k, const float* v, const float* q_norm,
+                                  const float* k_norm, int mode, float eps, int n_head, int n_head_kv, int head_dim,
+                                  const int32_t* pos, int max_ctx, float freq_base, float* q_out, void* k_cache,
+                                  void* v_cache, hoard_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -167,3 +167,61 @@ def test_speculative_loop_is_lossless():
         assert model.generate(prompt, 48) == want          # the top-k override was restored
     finally:
         model.close()
+
+
+def test_fused_ops_match_unfused():
+    """rmsnorm_q8 == rmsnorm then quant_q8 (up to the order of the squares' sum), gemv_multi == three
+    gemv calls exactly, qknorm_rope_store == rmsnorm + rope_store (both norm modes)."""
+    from hoard_b200 import quant
+    from hoard_b200.moe import _ptr, _stream
+    dev = torch.device("cuda", 0)
+    L, s = hx._hx(), _stream(None)
+    g = torch.Generator(device=dev).manual_seed(9)
+    H = 2048
+    x = torch.randn(H, generator=g, device=dev)
+    w = (1 + 0.1 * torch.randn(H, generator=g, device=dev)).float()
+    nq = int(L.hoard_hx_q8_bytes(H))
+    qa, qb = torch.zeros(nq, dtype=torch.uint8, device=dev), torch.zeros(nq, dtype=torch.uint8, device=dev)
+    cur = torch.empty(H, device=dev)
+    assert L.hoard_hx_rmsnorm_q8(_ptr(x), H, 1e-5, _ptr(w), _ptr(qa), s) == 0
+    assert L.hoard_hx_rmsnorm(_ptr(x), 1, H, 1e-5, _ptr(w), _ptr(cur), s) == 0
+    assert L.hoard_hx_quant_q8(_ptr(cur), H, _ptr(qb), s) == 0
+    a8, b8 = qa[:H].view(torch.int8).int(), qb[:H].view(torch.int8).int()
+    assert int((a8 - b8).abs().max()) <= 1 and float((a8 != b8).float().mean()) < 1e-2
+    # three projections in one launch
+    Ws, Wp, ys = [], [], []
+    for qt, n in ((hx.Q4_K, 512), (hx.Q4_K, 256), (hx.Q6_K, 256)):
+        W = quant.quantize(torch.randn(n, H, generator=g, device=dev) * 0.02, qt)
+        P = torch.empty_like(W)
+        assert L.hoard_hx_repack(qt, _ptr(W), _ptr(P), W.numel() // quant.row_bytes(qt, 256), s) == 0
+        Wp.append((qt, P, n))
+    outs = [torch.empty(n, device=dev) for _, _, n in Wp]
+    rc = L.hoard_hx_gemv_multi(3, hx._iarr([t for t, _, _ in Wp]), hx._parr([p.data_ptr() for _, p, _ in Wp]),
+                               hx._iarr([n for _, _, n in Wp]), H, _ptr(qb), None, hx._parr([o.data_ptr() for o in outs]), s)
+    assert rc == 0
+    for (qt, P, n), o in zip(Wp, outs):
+        y = torch.empty(n, device=dev)
+        assert L.hoard_hx_gemv(qt, _ptr(P), n, H, _ptr(qb), None, _ptr(y), s) == 0
+        assert torch.equal(o, y)
+    # fused QK norm + rope + store against rmsnorm + rope_store
+    nh, nkv, hd, pos = 8, 2, 128, 11
+    for mode in (1, 2):
+        q = torch.randn(nh * hd, generator=g, device=dev)
+        k = torch.randn(nkv * hd, generator=g, device=dev)
+        v = torch.randn(nkv * hd, generator=g, device=dev)
+        qn = (1 + 0.1 * torch.randn(nh * hd if mode == 1 else hd, generator=g, device=dev)).float()
+        kn = (1 + 0.1 * torch.randn(nkv * hd if mode == 1 else hd, generator=g, device=dev)).float()
+        kc1, vc1 = torch.zeros(16, nkv * hd, dtype=torch.float16, device=dev), torch.zeros(16, nkv * hd, dtype=torch.float16, device=dev)
+        kc2, vc2 = kc1.clone(), vc1.clone()
+        qo = torch.empty_like(q)
+        assert L.hoard_hx_qknorm_rope_store(_ptr(q), _ptr(k), _ptr(v), _ptr(qn), _ptr(kn), mode, 1e-6, nh, nkv, hd, pos,
+                                            1e6, _ptr(qo), _ptr(kc1), _ptr(vc1), s) == 0
+        q2, k2 = q.clone(), k.clone()
+        rows_q, cols_q = (1, nh * hd) if mode == 1 else (nh, hd)
+        rows_k, cols_k = (1, nkv * hd) if mode == 1 else (nkv, hd)
+        assert L.hoard_hx_rmsnorm(_ptr(q2), rows_q, cols_q, 1e-6, _ptr(qn), _ptr(q2), s) == 0
+        assert L.hoard_hx_rmsnorm(_ptr(k2), rows_k, cols_k, 1e-6, _ptr(kn), _ptr(k2), s) == 0
+        assert L.hoard_hx_rope_store(_ptr(q2), _ptr(k2), _ptr(v), nh, nkv, hd, pos, 1e6, _ptr(kc2), _ptr(vc2), s) == 0
+        torch.testing.assert_close(qo, q2, rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(kc1.float(), kc2.float(), rtol=2e-3, atol=2e-3)
+        assert torch.equal(vc1, vc2)
