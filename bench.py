@@ -188,13 +188,17 @@ def cpu_sample(max_seconds: float, nthreads: int):
                    f"tok/s = 1/(48 x mean layer time)")
 
 
-PHASE_NAMES = ["router_sums_read", "softmax+fx_q8", "topk", "issue", "renorm", "gu_first_wait", "gate_up", "barrier_h",
-               "h_q8", "down_wait", "down", "combine+router_partials", "barrier_x_in_layer"]
+# the persistent kernel's phase stamps, in the order a layer passes them
+TRACE_STAMPS = [(19, "router_sums_read"), (1, "topk_selected"), (2, "gate_up_copies_issued"), (3, "weights"),
+                (5, "down_copies_issued"), (6, "first_gate_up_chunk"), (7, "h_published"),
+                (8, "first_expert_h_ready"), (9, "first_expert_h_quantised"), (10, "first_expert_down_landed"),
+                (11, "down_done"), (12, "router_partials"), (16, "barrier_arrive"), (17, "barrier_passed"),
+                (13, "layer_end")]
 
 
 def trace_breakdown(ctx, x_row, device):
-    """One extra (untimed) decode step with the persistent kernel's phase stamps on; returns the
-    mean over layers of the median and max over CTAs of each phase's duration (us)."""
+    """One extra (untimed) decode step with the persistent kernel's phase stamps on; returns, per stamp,
+    the time from the layer's start (us): the median and the max over CTAs, averaged over layers."""
     import torch
     ctas, nph = ctx.trace_layout()
     buf = torch.zeros(ctas * N_LAYER * nph, dtype=torch.int64, device=device)
@@ -206,27 +210,12 @@ def trace_breakdown(ctx, x_row, device):
     t = buf.view(ctas, N_LAYER, nph).cpu().numpy().astype(np.float64)
     if not t.any():
         return None
-    main = t[:, :, :14]
-    d = np.diff(main, axis=2) / 1e3                # [cta, layer, 13] us between consecutive stamps
     out = {}
-    for i, name in enumerate(PHASE_NAMES[:13]):
-        di = d[:, :-1, i] if i >= 10 else d[:, :, i]     # the last layer has no router partials
-        out[name] = {"median": round(float(np.median(di, axis=0).mean()), 3),
-                     "max": round(float(di.max(axis=0).mean()), 3)}
-    if nph >= 20:
-        def span(a_, b_, layers=slice(None)):
-            v = (t[:, layers, b_] - t[:, layers, a_]) / 1e3
-            return {"median": round(float(np.median(v, axis=0).mean()), 3), "max": round(float(v.max(axis=0).mean()), 3)}
-        out["barrier_h.fence"] = span(7, 14)
-        out["barrier_h.poll"] = span(14, 15)
-        out["barrier_x.fence"] = span(12, 16, slice(0, -1))
-        out["barrier_x.poll"] = span(16, 17, slice(0, -1))
-        out["route.sums_read"] = span(0, 19)
-        out["route.softmax"] = span(19, 1)
-        out["route.sort"] = span(1, 2)
-        out["route.topk"] = span(2, 3)
-        out["issue.expect_tx"] = span(3, 18)
-        out["issue.copies"] = span(18, 4)
+    for ph, name in TRACE_STAMPS:              # layers 0 .. N-2 (the last layer has no router partials)
+        v = (t[:, :-1, ph] - t[:, :-1, 0]) / 1e3
+        if (t[:, :-1, ph] == 0).any():
+            continue
+        out[name] = {"median": round(float(np.median(v, axis=0).mean()), 3), "max": round(float(v.max(axis=0).mean()), 3)}
     out["layer_total"] = round(float(np.median(t[:, 1:, 0] - t[:, :-1, 0]) / 1e3), 3)
     return out
 

@@ -66,6 +66,15 @@ struct Scratch {
 
 // Re-lays nrows x nb GGUF blocks of `type` from src (raw) into dst (plane layout).
 cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int64_t nblk_total, cudaStream_t s);
+// several matrices re-laid in one launch (every src 16-byte aligned: device or pinned host memory)
+constexpr int REPACK_MAX_JOBS = 48;
+struct RepackJob {
+    int type;
+    const uint8_t* src;
+    uint8_t* dst;
+    int64_t nblk;
+};
+cudaError_t launch_repack_batch(const RepackJob* jobs, int n, cudaStream_t s);
 
 // dst[c][r] = src[r][c] for an R x C f32 matrix.
 cudaError_t launch_transpose(const float* src, float* dst, int R, int C, cudaStream_t s);

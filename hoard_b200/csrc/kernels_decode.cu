@@ -386,8 +386,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
     __shared__ int4 s_cd_gu[32];           // gate/up copy descriptors: [NCH chunks][2 segments][4 planes]
     __shared__ int4 s_cd_dn[2][64];        // down copy descriptors per type (Q4_K, Q6_K): [k][planes]
     __shared__ unsigned s_gu_bytes[NCH];
-    __shared__ unsigned s_amax[16 * 4];
-    __shared__ double s_lgd[513];            // router sums of this layer: [E] logits/scale, [E] = sum x^2      // per (expert position, 256 block) max|h| of this CTA
+    __shared__ unsigned s_amax[16 * 4];    // per (expert position, 256 block) max|h| of this CTA
+    __shared__ double s_lgd[513];          // router sums of this layer: [E] logits/scale, [E] = sum x^2
 
     const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
@@ -968,10 +968,13 @@ int decode_grid() {
 int decode_trace_phases() { return DEC_TRACE_PHASES; }
 
 // 0: both shares fit in shared memory, 1: only with the down rows over the gate/up rows, -1: neither
+static const void* decode_fn(bool bf16, int nv, bool trace);
 static int decode_alias_mode(const Dims& d, int G) {
     int dev = 0, max_smem = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa{};                          // static shared memory (the same in every instantiation)
+    if (cudaFuncGetAttributes(&fa, decode_fn(false, 16, true)) != cudaSuccess) return -1;
     for (int alias = 0; alias < 2; ++alias) {
         int64_t need = 0;
         for (int dt : {(int)T_Q4K, (int)T_Q6K}) {
@@ -979,7 +982,7 @@ static int decode_alias_mode(const Dims& d, int G) {
             P.init(d.H, d.E, d.k, d.I, dt, G, alias);
             need = need > P.total ? need : P.total;
         }
-        if (need + 1024 <= max_smem) return alias;       // + static shared memory
+        if (need + (int64_t)fa.sharedSizeBytes <= max_smem) return alias;
     }
     return -1;
 }

@@ -38,8 +38,93 @@ __global__ void k_repack(int type, const uint8_t* __restrict__ src, uint8_t* __r
     }
 }
 
+// The same re-lay with wide source reads, for a batch of matrices in one launch: tiles of RP_TB
+// blocks (RP_TB * bytes per block is a multiple of 16) are read with 16-byte loads, all of a thread's
+// loads issued before any is used, into shared memory and scattered into the planes from there. Used
+// whenever every source is 16-byte aligned; it matters most when the source is pinned host memory
+// read over PCIe, where the bus is only kept busy by many wide reads in flight.
+constexpr int RP_TB = 64;
+constexpr int RP_THREADS = 256;
+
+__device__ __forceinline__ void repack_tile(int type, const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                            int64_t nblk, int64_t b0, uint8_t* sb) {
+    const int bb = block_bytes(type);
+    const int nb = (int)(nblk - b0 < RP_TB ? nblk - b0 : RP_TB);
+    const int bytes = nb * bb, n16 = bytes / 16;
+    const uint8_t* st = src + b0 * bb;
+    uint4 v[(RP_TB * 210 / 16 + RP_THREADS - 1) / RP_THREADS];
+#pragma unroll
+    for (int u = 0; u < (int)(sizeof(v) / sizeof(v[0])); ++u) {
+        const int i = threadIdx.x + u * RP_THREADS;
+        if (i < n16) v[u] = reinterpret_cast<const uint4*>(st)[i];
+    }
+#pragma unroll
+    for (int u = 0; u < (int)(sizeof(v) / sizeof(v[0])); ++u) {
+        const int i = threadIdx.x + u * RP_THREADS;
+        if (i < n16) reinterpret_cast<uint4*>(sb)[i] = v[u];
+    }
+    for (int i = n16 * 16 + threadIdx.x; i < bytes; i += RP_THREADS) sb[i] = st[i];
+    __syncthreads();
+    for (int i = threadIdx.x; i < bytes; i += RP_THREADS) {
+        const int bl = i / bb, o = i - bl * bb;
+        const int64_t b = b0 + bl;
+        int64_t off;
+        if (type == T_Q4K) {
+            off = (o < 16) ? nblk * 128 + b * 16 + o : b * 128 + (o - 16);
+        } else {
+            if (o < 128) off = b * 128 + o;
+            else if (o < 192) off = nblk * 128 + b * 64 + (o - 128);
+            else if (o < 208) off = nblk * 192 + b * 16 + (o - 192);
+            else off = nblk * 208 + b * 2 + (o - 208);
+        }
+        dst[off] = sb[i];
+    }
+    __syncthreads();
+}
+
+struct RepackBatch {
+    const uint8_t* src[REPACK_MAX_JOBS];
+    uint8_t* dst[REPACK_MAX_JOBS];
+    int64_t nblk[REPACK_MAX_JOBS];
+    int type[REPACK_MAX_JOBS];
+    int64_t tile0[REPACK_MAX_JOBS + 1];   // first tile of each job; tile0[n] = all tiles
+    int n;
+};
+
+__global__ void __launch_bounds__(RP_THREADS) k_repack_tiled(const RepackBatch bt) {
+    __shared__ __align__(16) uint8_t sb[RP_TB * 210];
+    int j = 0;
+    for (int64_t t = blockIdx.x; t < bt.tile0[bt.n]; t += gridDim.x) {
+        while (t >= bt.tile0[j + 1]) ++j;            // tiles are visited in increasing order
+        repack_tile(bt.type[j], bt.src[j], bt.dst[j], bt.nblk[j], (t - bt.tile0[j]) * RP_TB, sb);
+    }
+}
+
+cudaError_t launch_repack_batch(const RepackJob* jobs, int n, cudaStream_t s) {
+    if (n < 0 || n > REPACK_MAX_JOBS) return cudaErrorInvalidValue;
+    RepackBatch bt{};
+    bt.n = n;
+    for (int i = 0; i < n; ++i) {
+        if (jobs[i].type != T_Q4K && jobs[i].type != T_Q6K) return cudaErrorInvalidValue;
+        if ((reinterpret_cast<uintptr_t>(jobs[i].src) & 15) != 0 || jobs[i].nblk < 0) return cudaErrorInvalidValue;
+        bt.src[i] = jobs[i].src;
+        bt.dst[i] = jobs[i].dst;
+        bt.nblk[i] = jobs[i].nblk;
+        bt.type[i] = jobs[i].type;
+        bt.tile0[i + 1] = bt.tile0[i] + (jobs[i].nblk + RP_TB - 1) / RP_TB;
+    }
+    const int64_t tiles = bt.tile0[n];
+    if (tiles == 0) return cudaSuccess;
+    k_repack_tiled<<<(unsigned)(tiles < 148 * 6 ? tiles : 148 * 6), RP_THREADS, 0, s>>>(bt);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int64_t nblk, cudaStream_t s) {
     if (type != T_Q4K && type != T_Q6K) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        const RepackJob j{type, src, dst, nblk};
+        return launch_repack_batch(&j, 1, s);
+    }
     const int64_t total = nblk * block_bytes(type);
     const int threads = 256;
     const int64_t blocks = (total + threads - 1) / threads;

@@ -59,6 +59,8 @@ struct hoard_moe_ctx {
     struct Residency {
         bool init = false;
         std::vector<std::array<const void*, 3>> host;   // [layer*E + expert] gate, up, down host bytes
+        std::vector<std::array<const void*, 3>> direct; // the same bytes' device-accessible addresses
+                                                        // (pinned host or device memory), or null
         std::vector<int> slot_of_expert;                // [layer*E + expert] -> slot or -1
         std::vector<int> expert_of_slot;                // [layer*S + slot] -> expert or -1
         std::vector<uint64_t> last_use;                 // [layer*S + slot] LRU clock
@@ -442,6 +444,7 @@ static int res_init(hoard_moe_ctx* c) {
     if (r.init) return HOARD_OK;
     const int L = c->desc.n_layer, E = c->dims.E, S = c->desc.n_slots;
     r.host.assign((size_t)L * E, {nullptr, nullptr, nullptr});
+    r.direct.assign((size_t)L * E, {nullptr, nullptr, nullptr});
     r.slot_of_expert.assign((size_t)L * E, -1);
     r.expert_of_slot.assign((size_t)L * S, -1);
     r.last_use.assign((size_t)L * S, 0);
@@ -463,7 +466,26 @@ int hoard_moe_ram_tier(hoard_moe_ctx* c, int layer, int expert, const void* gate
     if (expert < 0 || expert >= c->dims.E) return fail(c, HOARD_EINVAL, "expert out of range");
     if (!gate || !up || !down) return fail(c, HOARD_EINVAL, "null expert pointer");
     if ((rc = res_init(c))) return rc;
-    c->res.host[(size_t)layer * c->dims.E + expert] = {gate, up, down};
+    const size_t i = (size_t)layer * c->dims.E + expert;
+    c->res.host[i] = {gate, up, down};
+    // pinned host (or device) bytes are read in place by the re-lay kernel: no staging copy
+    std::array<const void*, 3> dir{};
+    const void* src[3] = {gate, up, down};
+    bool ok = true;
+    for (int m = 0; m < 3 && ok; ++m) {
+        cudaPointerAttributes at{};
+        if (cudaPointerGetAttributes(&at, src[m]) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+        } else if ((at.type == cudaMemoryTypeHost || at.type == cudaMemoryTypeDevice) && at.devicePointer &&
+                   (at.type == cudaMemoryTypeHost || at.device == c->desc.device) &&
+                   (reinterpret_cast<uintptr_t>(at.devicePointer) & 15) == 0) {
+            dir[m] = at.devicePointer;
+        } else {
+            ok = false;
+        }
+    }
+    c->res.direct[i] = ok ? dir : std::array<const void*, 3>{};
     return HOARD_OK;
 }
 
@@ -488,6 +510,15 @@ int hoard_moe_ensure(hoard_moe_ctx* c, int layer, const int32_t* sel, int n, int
         if (s >= 0) last[s] = stamp;
     }
     HCHECK(c, cudaSetDevice(c->desc.device));
+    std::vector<RepackJob> jobs;          // direct re-lays, one launch for all of this call's misses
+    std::vector<size_t> filled;           // slots (layer * S + slot) filled by this call
+    auto flush_jobs = [&]() -> int {
+        if (jobs.empty()) return HOARD_OK;
+        HCHECK(c, launch_repack_batch(jobs.data(), (int)jobs.size(), r.upload));
+        ++c->launches;
+        jobs.clear();
+        return HOARD_OK;
+    };
     for (int i = 0; i < n; ++i) {
         const int e = sel[i];
         int s = slot_of[e];
@@ -512,12 +543,19 @@ int hoard_moe_ensure(hoard_moe_ctx* c, int layer, const int32_t* sel, int n, int
             const int64_t offs[3] = {0, Ls.off_up, Ls.off_down};
             const int64_t bytes[3] = {Ls.gate_bytes, Ls.up_bytes, Ls.down_bytes};
             const int64_t rows[3] = {c->dims.I, c->dims.I, c->dims.H};
-            const void* const src[3] = {h[0], h[1], h[2]};
-            if ((rc = upload3(c, Ls.pool + (int64_t)victim * Ls.slot_stride, types, offs, bytes, rows, src, r.upload)))
-                return rc;
-            const size_t ri = (size_t)layer * S + victim;
-            HCHECK(c, cudaEventRecord(r.ready[ri], r.upload));
-            r.pending[ri] = 1;
+            const auto& dv = r.direct[(size_t)layer * E + e];
+            uint8_t* slot_base = Ls.pool + (int64_t)victim * Ls.slot_stride;
+            if (dv[0]) {                      // re-laid straight from the RAM tier (over PCIe for host bytes)
+                for (int m = 0; m < 3; ++m) {
+                    jobs.push_back({types[m], static_cast<const uint8_t*>(dv[m]), slot_base + offs[m],
+                                    bytes[m] / fmt_block_bytes(types[m])});
+                    if ((int)jobs.size() == REPACK_MAX_JOBS && (rc = flush_jobs())) return rc;
+                }
+            } else {
+                const void* const src[3] = {h[0], h[1], h[2]};
+                if ((rc = upload3(c, slot_base, types, offs, bytes, rows, src, r.upload))) return rc;
+            }
+            filled.push_back((size_t)layer * S + victim);
             expert_of[victim] = e;
             slot_of[e] = victim;
             s = victim;
@@ -526,6 +564,11 @@ int hoard_moe_ensure(hoard_moe_ctx* c, int layer, const int32_t* sel, int n, int
         }
         last[s] = stamp;
         slot_of_sel[i] = s;
+    }
+    if ((rc = flush_jobs())) return rc;
+    for (size_t ri : filled) {
+        HCHECK(c, cudaEventRecord(r.ready[ri], r.upload));
+        r.pending[ri] = 1;
     }
     // the compute stream waits only for uploads of the slots this call uses that may still be running
     for (int i = 0; i < n; ++i) {

@@ -1,5 +1,5 @@
 """Residency layer on the GPU: a per-layer LRU slot pool smaller than the expert count, filled from a
-pinned-host RAM tier by hoard_moe_ensure on the library's upload stream (hoard's to_vram / fetch and
+RAM tier by hoard_moe_ensure on the library's upload stream (hoard's to_vram / fetch and
 LRU, src/run_moe_stream.cpp:279-284, :380-421).
 
 hoard's invariant "LRU cache == naive == all-resident, bit-identical" must hold: a decode sequence
@@ -29,8 +29,9 @@ def make_ctx(n_slots):
     return ctx
 
 
-@pytest.fixture(scope="module")
-def contexts():
+@pytest.fixture(scope="module", params=["pinned", "pageable"])
+def contexts(request):
+    """Pinned RAM-tier bytes are re-laid in place over PCIe; pageable ones go through the staging buffer."""
     dev = torch.device("cuda", DEV)
     layers = [make_layer(SPEC, seed=700 + i) for i in range(N_LAYER)]
     full = make_ctx(SPEC.E)
@@ -42,7 +43,9 @@ def contexts():
         for e in range(SPEC.E):
             full.upload_expert(il, e, torch.from_numpy(L.gate[e]).to(dev), torch.from_numpy(L.up[e]).to(dev),
                                torch.from_numpy(L.down[e]).to(dev))
-            g, u, d = (torch.from_numpy(np.ascontiguousarray(a[e])).pin_memory() for a in (L.gate, L.up, L.down))
+            g, u, d = (torch.from_numpy(np.ascontiguousarray(a[e])) for a in (L.gate, L.up, L.down))
+            if request.param == "pinned":
+                g, u, d = g.pin_memory(), u.pin_memory(), d.pin_memory()
             host.append((g, u, d))
             lru.ram_tier(il, e, g, u, d)
     torch.cuda.synchronize(dev)
