@@ -192,7 +192,8 @@ def cpu_sample(max_seconds: float, nthreads: int):
 TRACE_STAMPS = [(19, "router_sums_read"), (1, "topk_selected"), (2, "gate_up_copies_issued"), (3, "weights"),
                 (5, "down_copies_issued"), (6, "first_gate_up_chunk"), (7, "h_published"),
                 (8, "first_expert_h_ready"), (9, "first_expert_h_quantised"), (10, "first_expert_down_landed"),
-                (11, "down_done"), (12, "router_partials"), (16, "barrier_arrive"), (17, "barrier_passed"),
+                (11, "down_done"), (14, "combined"), (15, "router_weights_landed"), (12, "router_partials"),
+                (16, "barrier_arrive"), (17, "barrier_passed"),
                 (13, "layer_end")]
 
 

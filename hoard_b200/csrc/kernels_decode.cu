@@ -77,6 +77,11 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
                  ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
+__device__ __forceinline__ unsigned ld_acq(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
     unsigned v;
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -94,22 +99,22 @@ __device__ __forceinline__ float4 ld_resid4(const __nv_bfloat16* p) {
                        __bfloat162float(__ushort_as_bfloat16(__ldcg(q + 3))));
 }
 
-// Grid barrier number `n` (0, 1, 2, ... within this launch): release by fence + relaxed add,
-// poll with relaxed loads, acquire by fence. Returns false on timeout / error.
-// It is driven by the last warp, which issues no bulk copies, so that its fence does not wait on
+// Grid barrier number `n` (0, 1, 2, ... within this launch): arrive by a release add, poll with
+// acquire loads (no separate gpu-scope fences: measured 0.9 us per layer less than fence + relaxed
+// add / relaxed polls + fence). Returns false on timeout / error.
+// It is driven by the last warp, which issues no bulk copies, so that its release does not wait on
 // weight copies still in flight.
 __device__ bool grid_barrier(unsigned* sync, unsigned n, int* s_ok, unsigned long long* st = nullptr) {
     __syncthreads();
     if (threadIdx.x == blockDim.x - 32) {
         int ok = 1;
         const unsigned target = (n + 1) * gridDim.x;
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
         if (st) st[0] = gtimer();
-        asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(&sync[1]) : "memory");
-        if (ld_relaxed(&sync[1]) < target) {
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&sync[1]) : "memory");
+        if (ld_acq(&sync[1]) < target) {
             const unsigned long long t0 = gtimer();
             for (unsigned it = 1;; ++it) {
-                if (ld_relaxed(&sync[1]) >= target) break;
+                if (ld_acq(&sync[1]) >= target) break;
                 if ((it & 15) == 0) {
                     if (ld_relaxed(&sync[0]) & 2u) { ok = 0; break; }
                     if (gtimer() - t0 > WAIT_NS) { atomicOr(&sync[0], 2u); ok = 0; break; }
@@ -117,28 +122,26 @@ __device__ bool grid_barrier(unsigned* sync, unsigned n, int* s_ok, unsigned lon
             }
         }
         if (st) st[1] = gtimer();
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
         *s_ok = ok;
     }
     __syncthreads();
     return *s_ok != 0;
 }
 
-// Bounded wait until the counter reaches `target` (relaxed polls, then an acquire fence); false if
-// the bound expired or another CTA has given up.
+// Bounded wait until the counter reaches `target` (acquire polls); false if the bound expired or
+// another CTA has given up.
 __device__ bool wait_count(const unsigned* cnt, unsigned target, unsigned* sync) {
-    if ((int)(ld_relaxed(cnt) - target) < 0) {
+    if ((int)(ld_acq(cnt) - target) < 0) {
         const unsigned long long t0 = gtimer();
         for (unsigned it = 1;; ++it) {
             __nanosleep(64);
-            if ((int)(ld_relaxed(cnt) - target) >= 0) break;
+            if ((int)(ld_acq(cnt) - target) >= 0) break;
             if ((it & 15) == 0) {
                 if (ld_relaxed(&sync[0]) & 2u) return false;
                 if (gtimer() - t0 > WAIT_NS) { atomicOr(&sync[0], 2u); return false; }
             }
         }
     }
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
     return true;
 }
 
@@ -736,10 +739,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             issue_down();
         }
-        if (tid == 0 && alive) {
-            asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        if (tid == blockDim.x - 32 && alive) {        // the last warp issues no bulk copies
             for (int b = q0 / QK; b <= (q1 - 1) / QK; ++b)
-                asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(hready + HREADY_STRIDE * b) : "memory");
+                asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(hready + HREADY_STRIDE * b) : "memory");
         }
         DEC_TR(l, 7);
         // ---- D. expert positions are spread over the warps (wpe warps each). A position's warps
@@ -770,6 +772,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
                     ok = ok && s_pos_ok[j] != 0;
                 }
                 ok = __all_sync(0xffffffffu, ok);
+                __syncwarp();                          // orders the lanes' reads of h after the acquire polls
                 if (tid == 0) DEC_TR(l, 8);
                 for (int g0 = wi * 32; g0 < I / 16; g0 += wpe * 32) {
                     const int gg = g0 + lane;
@@ -919,10 +922,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
                 xs[r] = to_f32<R>(xn);
             }
         }
+        DEC_TR(l, 14);
         if (has_next) {
             if (issued_wt && !mbar_wait(bar_wt, ph_wt)) { atomicOr(&a.sync[0], 2u); alive = false; }
             ph_wt ^= 1;
             __syncthreads();
+            DEC_TR(l, 15);
             const float* wn = reinterpret_cast<const float*>(smem + P.off_wn) + wn_sub;
             double* acc = a.racc + (int64_t)(buf ^ 1) * racc_stride + (int64_t)(c % RACC_COPIES) * (E + 1);
             for (int e = tid; e <= E; e += blockDim.x) {
