@@ -577,7 +577,7 @@ def run_gpu(args, rank, world, local_rank):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "peak_source": peak_src, "bytes_per_step": int(bytes_step),
-                         "kernel": "whole decode step (48 layers)"},
+                         "kernel": f"k_decode: one launch = the whole decode step ({N_LAYER} layers)"},
             "e2e": {"value": round(world * 1000.0 * steps / ms_e2e, 3), "unit": "tok/s",
                     "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": H * 4},
             "gpu_launches": int(launches),
