@@ -41,8 +41,8 @@ __device__ __forceinline__ int4 ld16s(const void* p) { return *reinterpret_cast<
 // weights are streamed once per call: keep them out of L1
 __device__ __forceinline__ uint4 ld16_stream(const void* p) {
     uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
     return v;
 }
 
@@ -155,32 +155,63 @@ __device__ __forceinline__ int q6k_unit_isum(const uint4& A, const uint4& B, con
 
 // ---- one lane's share of a quantized row . Q8_K activation ---------------------------------------
 // Row `n` of a plane-layout matrix (N rows, nb blocks); this lane takes units u = lane, lane+32, ...
+// Units are taken two at a time with both units' weight loads issued before either is used (the
+// sum keeps the unit order).
+template <int TYPE> struct RowUnit;
+template <> struct RowUnit<T_Q4K> {
+    uint4 w, h;
+    int b, c8;
+    __device__ __forceinline__ void load(const uint8_t* base, int64_t nblk_total, int64_t row, int nb, int u) {
+        b = u >> 3;
+        c8 = u & 7;
+        const int64_t blk = row * nb + b;
+        const Q4KPlanes p(base, nblk_total);
+        w = ld16_stream(p.qs + blk * 128 + 16 * c8);
+        h = ld16(p.hdr + blk * 16);
+    }
+    __device__ __forceinline__ float dot(const ActRow& a) const {
+        return q4k_unit_dot(w, h, c8, a.q + QK * b, a.bs + 16 * b, a.d[b]);
+    }
+};
+template <> struct RowUnit<T_Q6K> {
+    uint4 A, B, C, S;
+    float d6;
+    int b, v;
+    __device__ __forceinline__ void load(const uint8_t* base, int64_t nblk_total, int64_t row, int nb, int u) {
+        b = u >> 2;
+        v = u & 3;
+        const int h2 = v >> 1, r = v & 1;
+        const int64_t blk = row * nb + b;
+        const Q6KPlanes p(base, nblk_total);
+        A = ld16_stream(p.ql + blk * 128 + 64 * h2 + 16 * r);
+        B = ld16_stream(p.ql + blk * 128 + 64 * h2 + 32 + 16 * r);
+        C = ld16_stream(p.qh + blk * 64 + 32 * h2 + 16 * r);
+        S = ld16(p.sc + blk * 16);
+        d6 = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(p.d + blk * 2)));
+    }
+    __device__ __forceinline__ float dot(const ActRow& a) const {
+        const int is = q6k_unit_isum(A, B, C, S, v, a.q + QK * b, a.bs + 16 * b);
+        return a.d[b] * d6 * (float)is;
+    }
+};
+
 template <int TYPE>
 __device__ __forceinline__ float row_dot_lane(const uint8_t* base, int64_t nblk_total, int64_t row, int nb,
                                               const ActRow& a, int lane) {
     float acc = 0.f;
     const int nunits = nb * (TYPE == T_Q4K ? 8 : 4);
-    for (int u = lane; u < nunits; u += 32) {
-        if (TYPE == T_Q4K) {
-            const int b = u >> 3, c8 = u & 7;
-            const int64_t blk = row * nb + b;
-            const Q4KPlanes p(base, nblk_total);
-            const uint4 w = ld16_stream(p.qs + blk * 128 + 16 * c8);
-            const uint4 h = ld16(p.hdr + blk * 16);
-            acc += q4k_unit_dot(w, h, c8, a.q + QK * b, a.bs + 16 * b, a.d[b]);
-        } else {
-            const int b = u >> 2, v = u & 3;
-            const int h2 = v >> 1, r = v & 1;
-            const int64_t blk = row * nb + b;
-            const Q6KPlanes p(base, nblk_total);
-            const uint4 A = ld16_stream(p.ql + blk * 128 + 64 * h2 + 16 * r);
-            const uint4 B = ld16_stream(p.ql + blk * 128 + 64 * h2 + 32 + 16 * r);
-            const uint4 C = ld16_stream(p.qh + blk * 64 + 32 * h2 + 16 * r);
-            const uint4 S = ld16(p.sc + blk * 16);
-            const float d6 = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(p.d + blk * 2)));
-            const int is = q6k_unit_isum(A, B, C, S, v, a.q + QK * b, a.bs + 16 * b);
-            acc += a.d[b] * d6 * (float)is;
-        }
+    int u = lane;
+    for (; u + 32 < nunits; u += 64) {
+        RowUnit<TYPE> x0, x1;
+        x0.load(base, nblk_total, row, nb, u);
+        x1.load(base, nblk_total, row, nb, u + 32);
+        acc += x0.dot(a);
+        acc += x1.dot(a);
+    }
+    if (u < nunits) {
+        RowUnit<TYPE> x0;
+        x0.load(base, nblk_total, row, nb, u);
+        acc += x0.dot(a);
     }
     return acc;
 }

@@ -114,6 +114,21 @@ __global__ void __launch_bounds__(256) k_rope_store(float* __restrict__ q, float
         vc[(int64_t)pos * nv + t] = __float2half_rn(v[t]);
 }
 
+// sum over u = t, t + 128, ... < n of (double)(v[u]^2), in that order, with eight loads issued
+// before their squares are added (a plain strided loop waits for each load in turn)
+__device__ __forceinline__ double sumsq_stride128(const float* __restrict__ v, int n, int t) {
+    double ss = 0.0;
+    for (int u0 = t; u0 < n; u0 += 8 * 128) {
+        float x[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] = u0 + k * 128 < n ? v[u0 + k * 128] : 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (u0 + k * 128 < n) ss += (double)(x[k] * x[k]);
+    }
+    return ss;
+}
+
 // ---- single-query attention: one CTA per head; scores over the n_pos cached keys of its KV head
 //      (f16, products and sums in f32), softmax with the max subtracted and a double sum, then the
 //      probability-weighted sum of the cached values ----
@@ -263,16 +278,8 @@ __global__ void __launch_bounds__(128) k_qknorm_rope_store(const float* __restri
     const int half = hd / 2, i = threadIdx.x;
     float scale = 1.f;
     if (mode != 0) {
-        double ss = 0.0;
-        if (mode == 1) {
-            for (int u = threadIdx.x; u < nvec; u += blockDim.x) ss += (double)(vec[u] * vec[u]);
-        } else {
-            for (int u = threadIdx.x; u < hd; u += blockDim.x) {
-                const float x = vec[hh * hd + u];
-                ss += (double)(x * x);
-            }
-        }
-        ss = block_sum_d(ss, redd);
+        const double ss = block_sum_d(mode == 1 ? sumsq_stride128(vec, nvec, threadIdx.x)
+                                                : sumsq_stride128(vec + (int64_t)hh * hd, hd, threadIdx.x), redd);
         scale = 1.0f / sqrtf((float)(ss / (mode == 1 ? nvec : hd)) + eps);
     }
     if (i < half) {
