@@ -321,3 +321,38 @@ def test_decode_persistent_repeatable_and_counters_reset(qwen_c2):
     assert all(np.array_equal(r.view(np.uint32), res[0].view(np.uint32)) for r in res)
     ref = oracle_layer(L, x_np, orc.MODE_GGML)[0]
     assert rel_l2(res[0] - x_np, ref - x_np) < 1e-3
+
+
+@pytest.mark.parametrize("path", ["decode", "grouped", "tensor_core"])
+def test_exact_logit_ties_go_to_the_lower_expert_id(path):
+    """Two experts with identical router rows have bit-identical logits and probabilities; hoard's
+    top-k (descending, ties to the lower id) then takes the lower id first: wherever exactly one of
+    the pair is selected it is the lower one, and where both are, the lower one ranks first. Checked
+    on the persistent decode kernel (T = 1), the grouped path (T = 64) and the tensor-core path
+    (T = 256). (The oracle's rule is pinned in tests/test_oracle.py.)"""
+    spec = LayerSpec(H=512, E=16, k=4, I=256)
+    L = make_layer(spec, seed=131)
+    L.w_router[6] = L.w_router[5]
+    L.w_router[11] = L.w_router[2]
+    ctx = make_ctx(spec, max_tokens=256)
+    if path == "tensor_core":
+        ctx.set_gemm_min_tokens(128)
+    load_context(ctx, 0, L)
+    try:
+        x_np = make_x(256 if path != "grouped" else 64, spec.H, seed=132)
+        if path == "decode":
+            sel = np.concatenate([run_layer(ctx, x_np[t:t + 1])[1] for t in range(x_np.shape[0])])
+        else:
+            sel = run_layer(ctx, x_np)[1]
+        straddles = 0
+        for lo, hi in ((5, 6), (2, 11)):
+            for t in range(x_np.shape[0]):
+                row = list(sel[t])
+                if hi in row:
+                    assert lo in row and row.index(lo) < row.index(hi), (t, row)
+                if (lo in row) != (hi in row):
+                    assert lo in row, (t, row)
+                    straddles += 1
+        assert straddles > 0                                 # the boundary case did occur
+    finally:
+        ctx.close()
