@@ -35,7 +35,7 @@ namespace {
 constexpr int DEC_THREADS = 512;
 constexpr int DEC_TRACE_PHASES = 20;
 constexpr int NCH = 4;                                   // gate/up arrival chunks
-constexpr int RACC_COPIES = 8;                           // router accumulators spread over copies
+constexpr int RACC_COPIES = 4;   // router accumulators spread over copies (4 measured best of 1, 2, 4, 8, 16)
 constexpr unsigned long long WAIT_NS = 2000000000ull;   // 2 s bound on any wait
 constexpr int HREADY_OFF = 64;         // h block readiness counters: sync word HREADY_OFF + HREADY_STRIDE * b
 constexpr int HREADY_STRIDE = 32;      // one 128-byte line per counter (pollers of different blocks do not share)
@@ -1067,10 +1067,10 @@ constexpr int NOALLOC_MAX_I = 1024;     // expert intermediate size
 constexpr int NOALLOC_MAX_E = 512;      // experts per layer
 constexpr size_t NOALLOC_H_BYTES = (size_t)NOALLOC_MAX_K * NOALLOC_MAX_I * 4;                  // 64 KiB
 constexpr size_t NOALLOC_AMAX_BYTES = 2 * NOALLOC_MAX_K * (NOALLOC_MAX_I / QK) * 4;           // 512 B
-constexpr size_t NOALLOC_RACC_BYTES = (size_t)2 * RACC_COPIES * (NOALLOC_MAX_E + 1) * 8;       // 65,664 B
+constexpr size_t NOALLOC_RACC_BYTES = (size_t)2 * RACC_COPIES * (NOALLOC_MAX_E + 1) * 8;       // 32,832 B
 constexpr size_t NOALLOC_SYNC_BYTES = 8704;          // error word, barrier words, h block counters (one line each)
 constexpr size_t NOALLOC_ZERO_BYTES = NOALLOC_AMAX_BYTES + NOALLOC_RACC_BYTES + NOALLOC_SYNC_BYTES;
-constexpr size_t NOALLOC_BYTES = NOALLOC_H_BYTES + NOALLOC_ZERO_BYTES;                         // ~130 KiB
+constexpr size_t NOALLOC_BYTES = NOALLOC_H_BYTES + NOALLOC_ZERO_BYTES;                         // ~105 KiB
 static __device__ __align__(256) unsigned char g_decode_scratch[NOALLOC_BYTES];
 
 static std::mutex g_scratch_mu;

@@ -121,7 +121,7 @@ int hoard_moe_layers(hoard_moe_ctx* ctx, int layer0, int n_layers, void* x_inout
                      int32_t* sel_out, float* w_out, hoard_stream stream);
 
 /* Decode (T = 1) through n_layers consecutive fused layers, like hoard_moe_layers, but without any
- * device allocation and without the context's scratch: the kernel's scratch (about 130 KiB) is a
+ * device allocation and without the context's scratch: the kernel's scratch (about 105 KiB) is a
  * fixed device array inside this library. It exists for callers that cannot allocate device memory
  * when they run a step -- code inside a CUDA stream capture that forbids cudaMalloc, or an engine
  * whose device memory is fully handed out by its own arena after start-up -- while the weights stay
