@@ -194,7 +194,9 @@ int hoard_moe_set_top_k(hoard_moe_ctx* ctx, int k);
  * call of its layer that may read it. */
 
 /* Registers the host copy (raw GGUF bytes, as hoard_moe_upload_expert takes them) of one expert. The
- * caller keeps the memory alive; page-locked memory makes the uploads asynchronous. */
+ * caller keeps the memory alive. Page-locked (or device) memory whose three matrices start on 16-byte
+ * boundaries is read in place by the re-lay kernel over PCIe (no staging copy; all misses of one
+ * hoard_moe_ensure call in one launch); pageable memory goes through a staging buffer. */
 int hoard_moe_ram_tier(hoard_moe_ctx* ctx, int layer, int expert, const void* gate, const void* up,
                        const void* down);
 
