@@ -370,6 +370,8 @@ def measure_c1_decode(device):
 
 LRU_SLOTS = 32       # C3 run (ii): K = 32 slots per layer
 LRU_TOKENS = 8
+LRU_SKEW_TOKENS = 16   # tokens of the skewed-routing variant
+ZIPF_S = 1.0           # expert popularity exponent of the skewed variant
 
 
 def measure_lru(device, stream, n_layer: int):
@@ -428,12 +430,56 @@ def measure_lru(device, stream, n_layer: int):
     st = ctx.residency_stats()
     hits, misses = st["hits"] - st0["hits"], st["misses"] - st0["misses"]
     up_bytes = st["bytes_uploaded"] - st0["bytes_uploaded"]
+    out = {"metric": f"decode tok/s b=1, {LRU_SLOTS}-slot LRU per layer + pinned-host RAM tier ({n_layer} layers)",
+           "value": round(LRU_TOKENS / (ms * 1e-3), 3), "unit": "tok/s", "tokens": LRU_TOKENS,
+           "hit_rate": round(hits / max(1, hits + misses), 4), "misses_per_token": round(misses / LRU_TOKENS, 1),
+           "h2d_gbs": round(up_bytes / (ms * 1e-3) / 1e9, 2),
+           "note": "uniform random routing on random weights: the hit rate is the pool's share of experts"}
+
+    # Skewed variant: the same schedule (the router still runs and its ids are read back), but the
+    # experts computed are drawn per layer from a Zipf(s = 1.0) law over a fixed random permutation of
+    # the experts -- the skew fitted to hoard's real routing traces -- with weights 1/k. Ids are drawn
+    # before the timed region.
+    rng = np.random.default_rng(SEED)
+    prob = 1.0 / np.arange(1, E + 1) ** ZIPF_S
+    prob /= prob.sum()
+    perms = [rng.permutation(E) for _ in range(n_layer)]
+    n_tok = LRU_SKEW_TOKENS + 4
+    draws = [[perms[layer][rng.choice(E, K_USED, replace=False, p=prob)].astype(np.int32) for layer in range(n_layer)]
+             for _ in range(n_tok)]
+    w_flat = torch.full((1, K_USED), 1.0 / K_USED, device=device)
+    sel_dev = torch.empty(1, K_USED, dtype=torch.int32, device=device)
+
+    def token_skewed(x, ids):
+        for layer in range(n_layer):
+            sel, _ = ctx.route(layer, x)
+            sel.cpu()
+            slots = ctx.ensure(layer, ids[layer])
+            sel_dev.copy_(torch.from_numpy(ids[layer]).view(1, K_USED))
+            slot_dev.copy_(torch.from_numpy(slots), non_blocking=False)
+            ctx.experts(layer, sel_dev, w_flat, x, slot_of_sel=slot_dev)
+
+    for i in range(4):                                   # warm-up: the pool takes the skewed working set
+        token_skewed(xs[i % LRU_TOKENS].clone(), draws[LRU_SKEW_TOKENS + i])
+    torch.cuda.synchronize(device)
+    st0 = ctx.residency_stats()
+    a.record(stream)
+    for i in range(LRU_SKEW_TOKENS):
+        token_skewed(xs[i % LRU_TOKENS].clone(), draws[i])
+    b.record(stream)
+    torch.cuda.synchronize(device)
+    ms = a.elapsed_time(b)
+    ctx.sync_status()
+    st = ctx.residency_stats()
+    hits, misses = st["hits"] - st0["hits"], st["misses"] - st0["misses"]
+    up_bytes = st["bytes_uploaded"] - st0["bytes_uploaded"]
+    out["skewed"] = {"value": round(LRU_SKEW_TOKENS / (ms * 1e-3), 3), "unit": "tok/s", "tokens": LRU_SKEW_TOKENS,
+                     "hit_rate": round(hits / max(1, hits + misses), 4),
+                     "misses_per_token": round(misses / LRU_SKEW_TOKENS, 1),
+                     "h2d_gbs": round(up_bytes / (ms * 1e-3) / 1e9, 2),
+                     "routing": f"expert ids per layer ~ Zipf(s = {ZIPF_S}) over a fixed permutation, weights 1/k"}
     ctx.close()
-    return {"metric": f"decode tok/s b=1, {LRU_SLOTS}-slot LRU per layer + pinned-host RAM tier ({n_layer} layers)",
-            "value": round(LRU_TOKENS / (ms * 1e-3), 3), "unit": "tok/s", "tokens": LRU_TOKENS,
-            "hit_rate": round(hits / max(1, hits + misses), 4), "misses_per_token": round(misses / LRU_TOKENS, 1),
-            "h2d_gbs": round(up_bytes / (ms * 1e-3) / 1e9, 2),
-            "note": "uniform random routing on random weights: the hit rate is the pool's share of experts"}
+    return out
 
 
 def run_gpu(args, rank, world, local_rank):
