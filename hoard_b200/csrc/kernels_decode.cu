@@ -1056,9 +1056,10 @@ cudaError_t launch_decode_persistent(const Dims& d, const LayerWeights* lws_dev,
 }
 
 // ---- decode without any device allocation ---------------------------------------------------------
-// Some callers cannot allocate device memory when they run a decode step: code inside a CUDA stream
-// capture that forbids cudaMalloc, or an engine whose device memory is entirely handed out by its own
-// arena after start-up (hoard itself sizes its expert slot pool to the VRAM budget). For them the
+// Some callers cannot allocate device memory when they run a decode step: an engine whose device
+// memory is entirely handed out by its own arena after start-up (hoard itself sizes its expert slot
+// pool to the VRAM budget), or a step loop that must not call cudaMalloc (it can synchronise the
+// device, and a failure in the middle of a step has no recovery). For them the
 // persistent decode kernel can take its scratch (h, the block maxima of h, the router accumulators and
 // the grid-barrier words) from this fixed file-scope device array instead of a context's scratch.
 // Every GPU that loads this library holds the array until the process exits.

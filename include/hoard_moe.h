@@ -123,9 +123,10 @@ int hoard_moe_layers(hoard_moe_ctx* ctx, int layer0, int n_layers, void* x_inout
 /* Decode (T = 1) through n_layers consecutive fused layers, like hoard_moe_layers, but without any
  * device allocation and without the context's scratch: the kernel's scratch (about 105 KiB) is a
  * fixed device array inside this library. It exists for callers that cannot allocate device memory
- * when they run a step -- code inside a CUDA stream capture that forbids cudaMalloc, or an engine
- * whose device memory is fully handed out by its own arena after start-up -- while the weights stay
- * in a context created at start-up. No counterpart in the hoard project.
+ * when they run a step: an engine whose device memory is entirely handed out by its own arena after
+ * start-up (hoard sizes its expert slot pool to the whole VRAM budget), or a step loop that must not
+ * call cudaMalloc at all (it can synchronise the device, and a failure mid-step has no recovery).
+ * The weights stay in a context created at start-up. No counterpart in the hoard project.
  *   - Limits: n_expert_used <= 16, n_ff <= 1024, n_expert <= 512; larger shapes return HOARD_EINVAL.
  *     Contexts the persistent decode kernel cannot serve return HOARD_ESTATE.
  *   - The first call on each device looks up the array's device address (cudaGetSymbolAddress);

@@ -1,6 +1,6 @@
 """hoard_moe_decode_noalloc: decode with the library's static device scratch, for callers that cannot
-allocate device memory when they run a step (inside a stream capture that forbids cudaMalloc, or
-with all device memory handed out by their own arena). Its output must match the regular fused
+allocate device memory when they run a step (all device memory handed out by their own arena, or a
+step loop that must not call cudaMalloc). Its output must match the regular fused
 decode entry point (hoard_moe_layers) on the same context, call after call.
 
 This file is collected last on purpose: it exercises a process-wide device array, and a failure here
