@@ -37,17 +37,20 @@ class LayerData:
     shared: dict | None = field(default=None)
 
 
-def make_layer(spec: LayerSpec, seed: int) -> LayerData:
-    g = torch.Generator().manual_seed(seed)
+def make_layer(spec: LayerSpec, seed: int, device: str = "cpu") -> LayerData:
+    """Seeded weights drawn and quantised on `device` (a GPU draws and quantises the 128-expert
+    layers of the benchmark shape in seconds); the bytes come back as numpy arrays either way."""
+    g = torch.Generator(device=device).manual_seed(seed)
     H, E, I = spec.H, spec.E, spec.I
-    w_router = (torch.randn(E, H, generator=g) * 0.02).numpy()
-    w_norm = (1.0 + 0.1 * torch.randn(H, generator=g)).numpy()
+    w_router = (torch.randn(E, H, generator=g, device=device) * 0.02).cpu().numpy()
+    w_norm = (1.0 + 0.1 * torch.randn(H, generator=g, device=device)).cpu().numpy()
 
     def q(n_out, k_in, qt, n_exp):
         out = np.empty((n_exp, n_out, quant.row_bytes(qt, k_in)), np.uint8)
         for e0 in range(0, n_exp, 16):
             e1 = min(n_exp, e0 + 16)
-            out[e0:e1] = quant.quantize(torch.randn(e1 - e0, n_out, k_in, generator=g) * 0.02, qt).numpy()
+            out[e0:e1] = quant.quantize(torch.randn(e1 - e0, n_out, k_in, generator=g, device=device) * 0.02,
+                                        qt).cpu().numpy()
         return out
 
     gate = q(I, H, spec.types[0], E)
@@ -58,7 +61,7 @@ def make_layer(spec: LayerSpec, seed: int) -> LayerData:
         shared = dict(I=I, gate_type=spec.sh_types[0], up_type=spec.sh_types[1], down_type=spec.sh_types[2],
                       gate=q(I, H, spec.sh_types[0], 1)[0], up=q(I, H, spec.sh_types[1], 1)[0],
                       down=q(H, I, spec.sh_types[2], 1)[0],
-                      gate_inp=(torch.randn(H, generator=g) * 0.02).numpy())
+                      gate_inp=(torch.randn(H, generator=g, device=device) * 0.02).cpu().numpy())
     return LayerData(spec, w_router, w_norm, gate, up, down, shared)
 
 
