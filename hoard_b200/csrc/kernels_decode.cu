@@ -13,7 +13,10 @@
 //      ---- grid barrier ----
 //   D  Q8_K of h in shared memory; this CTA's output rows for every selected expert; the combine
 //      x[d] = sum_j w_j*y_j[d] + x[d] (j ascending); then the next layer's router partial sums over
-//      these rows (sum x^2 and W_r^T[d,:] . (ffn_norm[d]*x[d])) added into double accumulators;
+//      these rows (sum x^2 and W_r^T[d,:] . (ffn_norm[d]*x[d])), each formed in double in row order,
+//      divided by the layer's norm and added as 2^-40 fixed point into int64 accumulators: integer
+//      adds commute, so the sums -- and the routing -- are bit-reproducible whatever order the
+//      CTAs arrive in;
 //      ---- grid barrier ----
 // Matmul mapping: one lane owns one 256-weight block of a row (its scales are decoded once), lanes
 // read the block's 16-byte chunks in a lane-rotated order so that a warp's shared-memory reads hit
@@ -35,6 +38,8 @@ namespace {
 constexpr int DEC_THREADS = 512;
 constexpr int DEC_TRACE_PHASES = 20;
 constexpr int NCH = 4;                                   // gate/up arrival chunks
+constexpr double RFIX = 1099511627776.0;      // 2^40: unit of a normalised router partial sum
+constexpr double RFIX_MAX = 4.0e18;           // |partial| * 2^40 beyond this sets error bit 4
 constexpr int RACC_COPIES = 4;   // router accumulators spread over copies (4 measured best of 1, 2, 4, 8, 16)
 constexpr unsigned long long WAIT_NS = 2000000000ull;   // 2 s bound on any wait
 constexpr int HREADY_OFF = 64;         // h block readiness counters: sync word HREADY_OFF + HREADY_STRIDE * b
@@ -214,6 +219,17 @@ __device__ __forceinline__ int q4_min_dot(const Q4Scales& s, const int* bs32) {
            (int)((s.m_hi >> 16) & 0xFF) * b1.z + (int)(s.m_hi >> 24) * b1.w;
 }
 
+// Adds one CTA's router partial sum s (formed in double) into a fixed-point accumulator: s * fix
+// rounded to an integer (fix = 2^40 / the layer's norm, or / its square for sum x^2). Out-of-range
+// values set error bit 4 instead.
+__device__ __forceinline__ void add_fixed(long long* acc, double s, double fix, unsigned* sync) {
+    const double v = s * fix;
+    if (fabs(v) < RFIX_MAX)
+        atomicAdd(reinterpret_cast<unsigned long long*>(acc), (unsigned long long)__double2ll_rn(v));
+    else
+        atomicOr(&sync[0], 4u);
+}
+
 // Warp 0's router tail for E <= 32*NV, in two parts so that the expert copies can be issued between
 // them. route_select: logits -> top-k. The logits are selected in descending order (ties to the
 // lower expert id): softmax is monotonic, so this is the order of the probabilities except where
@@ -370,7 +386,7 @@ struct DecodeArgs {
     float* w_out;
     float* h;                   // [k][I]
     unsigned* amax;             // [2][k][I/256]
-    double* racc;               // [2][RACC_COPIES][E+1]
+    long long* racc;            // [2][RACC_COPIES][E+1] fixed-point router sums (zero at rest)
     unsigned* sync;             // [0] error bits, [1] barrier counter, [2] exit counter
     unsigned long long* trace;  // optional [G][n_layers][DEC_TRACE_PHASES] %globaltimer stamps
     int alias_dn;               // DecodePlan alias mode (down rows over the consumed gate/up rows)
@@ -507,6 +523,23 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
 
     // ---- prologue: residual rows, router slice of layer 0, partial router sums ------------------
     for (int r = tid; r < nr; r += blockDim.x) xs[r] = to_f32<R>(x[d0 + r]);
+    // the norm that scales layer 0's fixed-point sums: every CTA sums the squares of the whole input in
+    // the same order, so all CTAs hold the same value
+    double Sprev;
+    {
+        __shared__ double s_red[DEC_THREADS / 32];
+        double sq = 0.0;
+        for (int i = tid; i < H; i += blockDim.x) {
+            const float v = to_f32<R>(x[i]);
+            sq += (double)(v * v);
+        }
+        sq = warp_sum(sq);
+        if (lane == 0) s_red[warp] = sq;
+        __syncthreads();
+        double t = 0.0;
+        for (int w = 0; w < nw; ++w) t += s_red[w];
+        Sprev = t > 0.0 ? sqrt(t) : 1.0;
+    }
     if (tid == 0) {
         mbar_expect_tx(bar_wt, wt_bytes + (unsigned)(wn_hi - wn_lo));
         bulk_g2s(wt, a.lw[0].w_router_t + (int64_t)d0 * E, wt_bytes, bar_wt);
@@ -518,7 +551,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
     __syncthreads();
     {
         const float* wn = reinterpret_cast<const float*>(smem + P.off_wn) + wn_sub;
-        double* acc = a.racc + (int64_t)(c % RACC_COPIES) * (E + 1);
+        long long* acc = a.racc + (int64_t)(c % RACC_COPIES) * (E + 1);
         for (int e = tid; e <= E; e += blockDim.x) {
             double s = 0.0;
             if (e < E) {
@@ -526,7 +559,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
             } else {
                 for (int r = 0; r < nr; ++r) s += (double)(xs[r] * xs[r]);
             }
-            if (alive) atomicAdd(&acc[e], s);
+            if (alive) add_fixed(&acc[e], s, e < E ? RFIX / Sprev : RFIX / (Sprev * Sprev), a.sync);
         }
     }
     if (!grid_barrier(a.sync, nbar++, &s_ok)) alive = false;
@@ -574,17 +607,19 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
         }
         // router sums: every thread t <= E adds the RACC_COPIES partial copies of entry t (one L2 round trip)
         {
-            const double* racc = a.racc + (int64_t)buf * racc_stride;
+            const long long* racc = a.racc + (int64_t)buf * racc_stride;
+            const double un1 = Sprev / RFIX, un2 = Sprev * Sprev / RFIX;
             for (int e = tid; e <= E; e += blockDim.x) {
-                double v = 0.0;
+                long long v = 0;
 #pragma unroll
                 for (int cp = 0; cp < RACC_COPIES; ++cp) v += __ldcg(racc + cp * (E + 1) + e);
-                s_lgd[e] = v;
+                s_lgd[e] = (double)v * (e < E ? un1 : un2);
             }
         }
         __syncthreads();
         DEC_TR(l, 19);
         const float scale = 1.0f / sqrtf((float)(s_lgd[E] / H) + a.eps);
+        const double Scur = s_lgd[E] > 0.0 ? sqrt(s_lgd[E]) : 1.0;   // scales the sums of layer l+1
         if (warp == 0) {
             // top-k on the logits, then the copies, then the weights (softmax) while the bytes fly
             float my_logit;
@@ -907,8 +942,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
         // every CTA has published its h, so every CTA has read this layer's router sums: clear them
         // for layer l + 2, and the block maxima that layer l + 1 will use
         if (c == 0 && alive) {
-            double* rz = a.racc + (int64_t)buf * racc_stride;
-            for (int e = tid; e < racc_stride; e += blockDim.x) rz[e] = 0.0;
+            long long* rz = a.racc + (int64_t)buf * racc_stride;
+            for (int e = tid; e < racc_stride; e += blockDim.x) rz[e] = 0;
             unsigned* az = a.amax + (int64_t)(buf ^ 1) * k * nbI;
             for (int e = tid; e < k * nbI; e += blockDim.x) az[e] = 0u;
         }
@@ -929,7 +964,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
             __syncthreads();
             DEC_TR(l, 15);
             const float* wn = reinterpret_cast<const float*>(smem + P.off_wn) + wn_sub;
-            double* acc = a.racc + (int64_t)(buf ^ 1) * racc_stride + (int64_t)(c % RACC_COPIES) * (E + 1);
+            long long* acc = a.racc + (int64_t)(buf ^ 1) * racc_stride + (int64_t)(c % RACC_COPIES) * (E + 1);
             for (int e = tid; e <= E; e += blockDim.x) {
                 double s = 0.0;
                 if (e < E) {
@@ -937,11 +972,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
                 } else {
                     for (int r = 0; r < nr; ++r) s += (double)(xs[r] * xs[r]);
                 }
-                if (alive) atomicAdd(&acc[e], s);
+                if (alive) add_fixed(&acc[e], s, e < E ? RFIX / Scur : RFIX / (Scur * Scur), a.sync);
             }
             DEC_TR(l, 12);
             if (!grid_barrier(a.sync, nbar++, &s_ok, DEC_TRP(l, 16))) alive = false;
         }
+        Sprev = Scur;
         DEC_TR(l, 13);
     }
 #undef DEC_TR
@@ -956,6 +992,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
             unsigned* az = a.amax + (int64_t)((a.n_layers - 1) & 1) * k * nbI;
             for (int e = 0; e < k * nbI; ++e) az[e] = 0u;
             for (int e = 0; e < k * nbI; ++e) hready[HREADY_STRIDE * e] = 0u;
+            if (ld_relaxed(&a.sync[0]) & 6u)      // an aborted launch may leave partial sums behind
+                for (int e = 0; e < 2 * racc_stride; ++e) a.racc[e] = 0;
             a.sync[1] = 0u;
             a.sync[2] = 0u;
             __threadfence();
@@ -1042,7 +1080,7 @@ cudaError_t launch_decode_persistent(const Dims& d, const LayerWeights* lws_dev,
     a.w_out = w_out;
     a.h = sc.h;
     a.amax = sc.amax;
-    a.racc = reinterpret_cast<double*>(sc.partials);
+    a.racc = reinterpret_cast<long long*>(sc.partials);
     a.sync = sc.sync;
     a.trace = trace;
     a.alias_dn = alias;

