@@ -13,6 +13,8 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "block_ops.cuh"
+#include <algorithm>
+#include <type_traits>
 
 namespace hoard {
 
@@ -164,7 +166,7 @@ constexpr int MAX_K = 16;
 constexpr int RL_TT = 32;      // tokens per tile: 8 warps x 4
 constexpr int RL_EB = 128;     // experts per tile: 32 lanes x 4
 constexpr int RL_KC = 32;      // K chunk staged in shared memory
-constexpr int RL_MIN_KLEN = 128;
+constexpr int RL_MIN_KLEN = 32;      // one K chunk per split at small T (the K splits are summed 8 loads at a time)
 constexpr int RL_TARGET_CTAS = 296;
 
 constexpr int RMS_MAXV = 32;   // H <= 8192: values per thread held in registers
@@ -309,8 +311,17 @@ __global__ void __launch_bounds__(256) k_route_topk(const double* __restrict__ p
     for (int i = threadIdx.x; i < nt * E; i += blockDim.x) {
         const int tt = i / E, e = i - tt * E;
         const double* src = part + (int64_t)(t0 + tt) * E + e;
+        const int64_t zs = (int64_t)T * E;
         double s = 0.0;
-        for (int z = 0; z < ksplit; ++z) s += src[(int64_t)z * T * E];
+        int z = 0;
+        for (; z + 8 <= ksplit; z += 8) {           // eight loads in flight, added in split order
+            double v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = src[(int64_t)(z + u) * zs];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) s += v[u];
+        }
+        for (; z < ksplit; ++z) s += src[(int64_t)z * zs];
         lg[tt][e] = (float)s;
     }
     __syncthreads();
@@ -674,6 +685,127 @@ __device__ __forceinline__ SlotMats slot_mats(const LayerWeights& lw, int s) {
 constexpr int GU_ROWS = 16;    // gate/up rows per CTA (8 warps x 2)
 constexpr int DN_ROWS = 16;    // down rows per CTA
 
+// A row's units held in registers: lane takes units lane, lane + 32, ... (UPL of them), loaded once
+// and dotted against every entry of the slot. The float sum runs over the units in the same order as
+// row_dot_lane's, so the result is bit-identical to re-reading the row for each entry.
+template <int TYPE, int UPL>
+struct RowRegs {
+    RowUnit<TYPE> u[UPL];
+    bool has[UPL];
+    __device__ __forceinline__ void load(const uint8_t* base, int64_t nblk, int64_t row, int nb, int unit0, int nunits) {
+#pragma unroll
+        for (int i = 0; i < UPL; ++i) {
+            const int un = unit0 + 32 * i;
+            has[i] = un < nunits;
+            if (has[i]) u[i].load(base, nblk, row, nb, un);
+        }
+    }
+    __device__ __forceinline__ float dot(const ActRow& a) const {
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < UPL; ++i)
+            if (has[i]) acc += u[i].dot(a);
+        return acc;
+    }
+};
+
+// Gate/up of Q4_K slots for small batches: a warp loads its two rows (gate and up) once and runs every
+// entry of the slot against them; other weight types take the per-entry row dots.
+template <int UPL>
+__global__ void __launch_bounds__(256) k_gateup_regs(LayerWeights lw, int H, int I, int KK,
+                                                     const int* __restrict__ offsets, const int* __restrict__ perm,
+                                                     const int8_t* __restrict__ xq, const float* __restrict__ xd,
+                                                     const int* __restrict__ xbs, float* __restrict__ h) {
+    const int s = blockIdx.x;
+    const int start = offsets[s], end = offsets[s + 1];
+    if (start == end) return;
+    const SlotMats m = slot_mats(lw, s);
+    const int nb = H / QK;
+    const int64_t nblk = (int64_t)I * nb;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int i0 = blockIdx.y * GU_ROWS + warp, i1 = i0 + 8;
+    const int r1 = min(I, (int)(blockIdx.y + 1) * GU_ROWS);
+    if (m.gt != T_Q4K || m.ut != T_Q4K) {
+        for (int i = i0; i < r1; i += 8) {
+            for (int p = start; p < end; ++p) {
+                const int ent = perm[p];
+                const int t = ent / KK;
+                const ActRow a{xq + (size_t)t * H, xd + (size_t)t * nb, xbs + (size_t)t * (H / 16)};
+                float g = row_dot_rt(m.gt, m.g, nblk, i, nb, a, lane);
+                float u = row_dot_rt(m.ut, m.u, nblk, i, nb, a, lane);
+                g = warp_sum(g);
+                u = warp_sum(u);
+                if (lane == 0) h[(size_t)ent * I + i] = silu_f(g) * u;
+            }
+        }
+        return;
+    }
+    const int nunits = nb * 8;
+    const bool v0 = i0 < r1, v1 = i1 < r1;
+    RowRegs<T_Q4K, UPL> g0, u0, g1, u1;
+    if (v0) { g0.load(m.g, nblk, i0, nb, lane, nunits); u0.load(m.u, nblk, i0, nb, lane, nunits); }
+    if (v1) { g1.load(m.g, nblk, i1, nb, lane, nunits); u1.load(m.u, nblk, i1, nb, lane, nunits); }
+    for (int p = start; p < end; ++p) {
+        const int ent = perm[p];
+        const int t = ent / KK;
+        const ActRow a{xq + (size_t)t * H, xd + (size_t)t * nb, xbs + (size_t)t * (H / 16)};
+        if (v0) {
+            const float g = warp_sum(g0.dot(a)), u = warp_sum(u0.dot(a));
+            if (lane == 0) h[(size_t)ent * I + i0] = silu_f(g) * u;
+        }
+        if (v1) {
+            const float g = warp_sum(g1.dot(a)), u = warp_sum(u1.dot(a));
+            if (lane == 0) h[(size_t)ent * I + i1] = silu_f(g) * u;
+        }
+    }
+}
+
+// Down rows for small batches: G lanes per row (G = the power of two covering the row's units, so a
+// warp holds 32/G rows), each lane's unit loaded once and run against every entry of the slot; two
+// row sets per warp in flight. The G-lane reduction equals a warp-wide one over a single row (the
+// lanes it leaves out hold zeros), so results match the per-entry kernel bit for bit.
+template <int G>
+__global__ void __launch_bounds__(256) k_down_regs(LayerWeights lw, int H, int I, const int* __restrict__ offsets,
+                                                   const int* __restrict__ perm, const int8_t* __restrict__ hq,
+                                                   const float* __restrict__ hd, const int* __restrict__ hbs,
+                                                   float* __restrict__ y) {
+    const int s = blockIdx.x;
+    const int start = offsets[s], end = offsets[s + 1];
+    if (start == end) return;
+    const SlotMats m = slot_mats(lw, s);
+    const int nb = I / QK;
+    const int64_t nblk = (int64_t)H * nb;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int RPW = 32 / G;                    // rows per warp and row set
+    const int sub = lane / G, gl = lane - sub * G;
+    const int rows_cta = 16 * RPW;                 // two row sets of 8 warps
+    const int base = blockIdx.y * rows_cta;
+    const int r1 = min(H, base + rows_cta);
+    const int ra = base + warp * RPW + sub, rb = ra + 8 * RPW;
+    auto run = [&](auto tag) {
+        constexpr int DT = decltype(tag)::value;
+        const int nunits = nb * (DT == T_Q4K ? 8 : 4);
+        const bool va = ra < r1 && gl < nunits, vb = rb < r1 && gl < nunits;
+        RowUnit<DT> xa, xb;
+        if (va) xa.load(m.d, nblk, ra, nb, gl);
+        if (vb) xb.load(m.d, nblk, rb, nb, gl);
+        for (int p = start; p < end; ++p) {
+            const int ent = perm[p];
+            const ActRow a{hq + (size_t)ent * I, hd + (size_t)ent * nb, hbs + (size_t)ent * (I / 16)};
+            float fa = va ? xa.dot(a) : 0.f, fb = vb ? xb.dot(a) : 0.f;
+#pragma unroll
+            for (int o = G / 2; o > 0; o >>= 1) {
+                fa += __shfl_xor_sync(0xffffffffu, fa, o);
+                fb += __shfl_xor_sync(0xffffffffu, fb, o);
+            }
+            if (gl == 0 && ra < r1) y[(size_t)ent * H + ra] = fa;
+            if (gl == 0 && rb < r1) y[(size_t)ent * H + rb] = fb;
+        }
+    };
+    if (m.dt == T_Q4K) run(std::integral_constant<int, T_Q4K>());
+    else run(std::integral_constant<int, T_Q6K>());
+}
+
 __global__ void __launch_bounds__(256) k_gateup(LayerWeights lw, int H, int I, int KK, const int* __restrict__ offsets,
                                                 const int* __restrict__ perm, const int8_t* __restrict__ xq,
                                                 const float* __restrict__ xd, const int* __restrict__ xbs,
@@ -1016,16 +1148,36 @@ cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const 
     }
     // 2. group entries by slot
     if ((e = launch_dispatch(slot_of_sel, T, d.k, KK, lw.n_slots, sc, 0, s, &nl)) != cudaSuccess) return e;
-    // 3. gate/up + SwiGLU
-    k_gateup<<<dim3(NS, (d.I + GU_ROWS - 1) / GU_ROWS), 256, 0, s>>>(lw, d.H, d.I, KK, sc.offsets, sc.perm, sc.fx_q,
-                                                                      sc.fx_d, sc.fx_bs, sc.h);
+    // 3. gate/up + SwiGLU (weights held in registers across a slot's entries where the row fits in
+    //    two units per lane)
+    const dim3 gu_grid(NS, (d.I + GU_ROWS - 1) / GU_ROWS);
+    const int gu_units = (d.H / QK) * 8;
+    if (gu_units <= 32)
+        k_gateup_regs<1><<<gu_grid, 256, 0, s>>>(lw, d.H, d.I, KK, sc.offsets, sc.perm, sc.fx_q, sc.fx_d, sc.fx_bs, sc.h);
+    else if (gu_units <= 64)
+        k_gateup_regs<2><<<gu_grid, 256, 0, s>>>(lw, d.H, d.I, KK, sc.offsets, sc.perm, sc.fx_q, sc.fx_d, sc.fx_bs, sc.h);
+    else
+        k_gateup<<<gu_grid, 256, 0, s>>>(lw, d.H, d.I, KK, sc.offsets, sc.perm, sc.fx_q, sc.fx_d, sc.fx_bs, sc.h);
     ++nl;
     // 4. quantise h
     k_quant_q8<<<(unsigned)((d.I / QK) * T * KK), 256, 0, s>>>(sc.h, d.I, sc.h_q, sc.h_d, sc.h_bs);
     ++nl;
-    // 5. down
-    k_down<<<dim3(NS, (d.H + DN_ROWS - 1) / DN_ROWS), 256, 0, s>>>(lw, d.H, d.I, sc.offsets, sc.perm, sc.h_q, sc.h_d,
-                                                                    sc.h_bs, sc.y);
+    // 5. down (the widest row type present sets the lanes per row)
+    const int nbI = d.I / QK;
+    int dn_units = nbI * (lw.down_type == T_Q4K ? 8 : 4);
+    if (shared) dn_units = std::max(dn_units, nbI * (lw.sh_down_type == T_Q4K ? 8 : 4));
+    if (dn_units <= 8)
+        k_down_regs<8><<<dim3(NS, (d.H + 63) / 64), 256, 0, s>>>(lw, d.H, d.I, sc.offsets, sc.perm, sc.h_q, sc.h_d,
+                                                                 sc.h_bs, sc.y);
+    else if (dn_units <= 16)
+        k_down_regs<16><<<dim3(NS, (d.H + 31) / 32), 256, 0, s>>>(lw, d.H, d.I, sc.offsets, sc.perm, sc.h_q, sc.h_d,
+                                                                  sc.h_bs, sc.y);
+    else if (dn_units <= 32)
+        k_down_regs<32><<<dim3(NS, (d.H + 15) / 16), 256, 0, s>>>(lw, d.H, d.I, sc.offsets, sc.perm, sc.h_q, sc.h_d,
+                                                                  sc.h_bs, sc.y);
+    else
+        k_down<<<dim3(NS, (d.H + DN_ROWS - 1) / DN_ROWS), 256, 0, s>>>(lw, d.H, d.I, sc.offsets, sc.perm, sc.h_q,
+                                                                        sc.h_d, sc.h_bs, sc.y);
     ++nl;
     // 6. weighted combine into the residual
     if ((e = launch_combine(d, sc, w, x_inout, T, KK, s, false)) != cudaSuccess) return e;
