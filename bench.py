@@ -368,6 +368,64 @@ def measure_c1_decode(device):
         model.close()
 
 
+C3_PROMPT, C3_GEN, C3_CTX = 512, 256, 4096
+
+
+def measure_c3_decode(device):
+    """C3: the Qwen3-30B-A3B-shape model (48 layers, GQA 32/4 x 128, per-head QK norm, theta 1e6,
+    vocab 151936, 128 experts top-8 + renorm, I 768, Q4_K_M, 4096-slot bf16 KV cache), seeded weights,
+    every expert resident; a 512-token prompt, then 256 greedy tokens, each one replay of the captured
+    per-token graph (embedding, 48 x (attention + MoE layer), lm-head, argmax), timed with CUDA events
+    around the 256 replays. The MoE share is 48 single-layer MoE launches (the graph's own MoE calls)
+    timed alone on the same context."""
+    import torch
+    from hoard_b200 import harness as hx
+    cfg = hx.C3_QWEN3
+    tensors = hx.seeded_tensors(cfg, seed=SEED + 303, device=device)
+    model = hx.DecodeModel(cfg, tensors, device=device.index, max_ctx=C3_CTX, kv_dtype=torch.bfloat16)
+    del tensors
+    torch.cuda.empty_cache()
+    try:
+        g = torch.Generator().manual_seed(SEED + 304)
+        prompt = torch.randint(0, cfg.n_vocab, (C3_PROMPT,), generator=g).tolist()
+        graph = model.capture()
+        model.prefill(prompt)
+        for _ in range(4):                                    # warm-up replays (positions 512..515)
+            graph.replay()
+        model.prefill(prompt)
+        torch.cuda.synchronize(device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(C3_GEN):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize(device)
+        model.moe.sync_status()
+        ms = a.elapsed_time(b)
+        toks = model.seq[C3_PROMPT:C3_PROMPT + C3_GEN].tolist()
+        xb = torch.zeros(1, cfg.n_embd, device=device)
+        xb.normal_()
+        for il in range(cfg.n_layer):
+            model.moe.layers(il, 1, xb)
+        torch.cuda.synchronize(device)
+        a.record()
+        for _ in range(10):
+            for il in range(cfg.n_layer):
+                model.moe.layers(il, 1, xb)
+        b.record()
+        torch.cuda.synchronize(device)
+        moe_ms = a.elapsed_time(b) / 10
+        return {"metric": "C3 decode tok/s (Qwen3-30B-A3B shape, whole model: 48 layers attention + MoE, lm-head)",
+                "value": round(C3_GEN / ms * 1e3, 1), "unit": "tok/s", "ms_per_token": round(ms / C3_GEN, 4),
+                "prompt": C3_PROMPT, "generated": C3_GEN, "distinct_tokens": len(set(toks)),
+                "kv_cache": f"bf16, {C3_CTX} slots", "moe_ms_per_token": round(moe_ms, 4),
+                "moe_share": round(moe_ms / (ms / C3_GEN), 3),
+                "timing": "CUDA events around 256 replays of the captured per-token graph; the MoE share from 48 "
+                          "single-layer MoE launches timed alone"}
+    finally:
+        model.close()
+
+
 LRU_SLOTS = 32       # C3 run (ii): K = 32 slots per layer
 LRU_TOKENS = 8
 LRU_SKEW_TOKENS = 16   # tokens of the skewed-routing variant
@@ -587,6 +645,10 @@ def run_gpu(args, rank, world, local_rank):
     if not args.no_c1 and rank == 0 and world == 1:
         c1 = measure_c1_decode(device)
 
+    c3 = None
+    if not args.no_c3 and rank == 0 and world == 1:
+        c3 = measure_c3_decode(device)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle as orc
@@ -637,6 +699,8 @@ def run_gpu(args, rank, world, local_rank):
             line["prefill"] = prefill
         if c1:
             line["c1_decode"] = c1
+        if c3:
+            line["c3_decode"] = c3
         if cpu:
             line["cpu_baseline"] = cpu
         if phases:
@@ -662,6 +726,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-token (prefill) measurements")
     ap.add_argument("--no-lru", action="store_true", help="skip the LRU slot pool + RAM tier decode measurement")
     ap.add_argument("--no-c1", action="store_true", help="skip the C1 whole-model decode (device driver) measurement")
+    ap.add_argument("--no-c3", action="store_true", help="skip the C3 whole-model decode (device driver) measurement")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="expert-parallel prefill exchange: the library's peer-memory kernels or NCCL all-to-all")
     ap.add_argument("--ep-chunks", type=int, default=2, help="expert-parallel prefill: micro-batches per layer "

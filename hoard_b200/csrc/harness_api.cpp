@@ -19,6 +19,9 @@ inline int st(cudaError_t e) {
 
 }  // namespace
 
+// KV cache element types: f16 (HOARD_TYPE_F16) or bf16 (HOARD_TYPE_BF16)
+static bool kv_ok(int t) { return t == HOARD_TYPE_F16 || t == HOARD_TYPE_BF16; }
+
 extern "C" {
 
 int hoard_hx_repack(int type, const void* src, void* dst, int64_t n_blocks, hoard_stream stream) {
@@ -74,42 +77,43 @@ int hoard_hx_gemv(int type, const void* w_plane, int N, int K, const void* q8, c
 }
 
 int hoard_hx_rope_store(float* q, float* k, const float* v, int n_head, int n_head_kv, int head_dim, int pos,
-                        float freq_base, void* k_cache, void* v_cache, hoard_stream stream) {
+                        float freq_base, void* k_cache, void* v_cache, int kv_type, hoard_stream stream) {
     if (!q || !k || !v || !k_cache || !v_cache || n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv ||
-        head_dim <= 0 || head_dim % 2 || pos < 0 || !(freq_base > 0))
+        head_dim <= 0 || head_dim % 2 || pos < 0 || !(freq_base > 0) || !kv_ok(kv_type))
         return HOARD_EINVAL;
-    return st(launch_rope_store(q, k, v, n_head, n_head_kv, head_dim, pos, nullptr, pos + 1, freq_base,
-                                static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), (cudaStream_t)stream));
+    return st(launch_rope_store(q, k, v, n_head, n_head_kv, head_dim, pos, nullptr, pos + 1, freq_base, k_cache, v_cache,
+                                kv_type == HOARD_TYPE_BF16, (cudaStream_t)stream));
 }
 
 int hoard_hx_rope_store_at(float* q, float* k, const float* v, int n_head, int n_head_kv, int head_dim,
                            const int32_t* pos, int max_ctx, float freq_base, void* k_cache, void* v_cache,
-                           hoard_stream stream) {
+                           int kv_type, hoard_stream stream) {
     if (!q || !k || !v || !pos || !k_cache || !v_cache || n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv ||
-        head_dim <= 0 || head_dim % 2 || max_ctx <= 0 || !(freq_base > 0))
+        head_dim <= 0 || head_dim % 2 || max_ctx <= 0 || !(freq_base > 0) || !kv_ok(kv_type))
         return HOARD_EINVAL;
-    return st(launch_rope_store(q, k, v, n_head, n_head_kv, head_dim, 0, pos, max_ctx, freq_base,
-                                static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), (cudaStream_t)stream));
+    return st(launch_rope_store(q, k, v, n_head, n_head_kv, head_dim, 0, pos, max_ctx, freq_base, k_cache, v_cache,
+                                kv_type == HOARD_TYPE_BF16, (cudaStream_t)stream));
 }
 
 int hoard_hx_attention(const float* q, const void* k_cache, const void* v_cache, int n_head, int n_head_kv,
-                       int head_dim, int n_pos, float scale, float* out, hoard_stream stream) {
+                       int head_dim, int n_pos, float scale, float* out, int kv_type, hoard_stream stream) {
     if (!q || !k_cache || !v_cache || !out || n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv ||
-        head_dim <= 0 || head_dim > 256 || 256 % head_dim || n_pos <= 0)
+        head_dim <= 0 || head_dim > 256 || 256 % head_dim || n_pos <= 0 || !kv_ok(kv_type))
         return HOARD_EINVAL;
     if (attention_smem(head_dim, n_pos) > 200 * 1024) return HOARD_EINVAL;
-    return st(launch_attention(q, static_cast<const __half*>(k_cache), static_cast<const __half*>(v_cache), n_head,
-                               n_head_kv, head_dim, n_pos, nullptr, scale, out, (cudaStream_t)stream));
+    return st(launch_attention(q, k_cache, v_cache, kv_type == HOARD_TYPE_BF16, n_head, n_head_kv, head_dim, n_pos,
+                               nullptr, scale, out, (cudaStream_t)stream));
 }
 
 int hoard_hx_attention_at(const float* q, const void* k_cache, const void* v_cache, int n_head, int n_head_kv,
-                          int head_dim, const int32_t* pos, int max_ctx, float scale, float* out, hoard_stream stream) {
+                          int head_dim, const int32_t* pos, int max_ctx, float scale, float* out, int kv_type,
+                          hoard_stream stream) {
     if (!q || !k_cache || !v_cache || !pos || !out || n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv ||
-        head_dim <= 0 || head_dim > 256 || 256 % head_dim || max_ctx <= 0)
+        head_dim <= 0 || head_dim > 256 || 256 % head_dim || max_ctx <= 0 || !kv_ok(kv_type))
         return HOARD_EINVAL;
     if (attention_smem(head_dim, max_ctx) > 200 * 1024) return HOARD_EINVAL;
-    return st(launch_attention(q, static_cast<const __half*>(k_cache), static_cast<const __half*>(v_cache), n_head,
-                               n_head_kv, head_dim, max_ctx, pos, scale, out, (cudaStream_t)stream));
+    return st(launch_attention(q, k_cache, v_cache, kv_type == HOARD_TYPE_BF16, n_head, n_head_kv, head_dim, max_ctx,
+                               pos, scale, out, (cudaStream_t)stream));
 }
 
 int hoard_hx_argmax(const float* v, int n, int32_t* out, hoard_stream stream) {
@@ -152,24 +156,24 @@ static int qknorm_check(const float* q, const float* k, const float* v, const fl
 
 int hoard_hx_qknorm_rope_store(const float* q, const float* k, const float* v, const float* q_norm,
                                const float* k_norm, int mode, float eps, int n_head, int n_head_kv, int head_dim,
-                               int pos, float freq_base, float* q_out, void* k_cache, void* v_cache,
+                               int pos, float freq_base, float* q_out, void* k_cache, void* v_cache, int kv_type,
                                hoard_stream stream) {
     int rc = qknorm_check(q, k, v, q_norm, k_norm, mode, n_head, n_head_kv, head_dim, q_out, k_cache, v_cache);
-    if (rc || pos < 0 || !(freq_base > 0)) return rc ? rc : HOARD_EINVAL;
+    if (rc || pos < 0 || !(freq_base > 0) || !kv_ok(kv_type)) return rc ? rc : HOARD_EINVAL;
     return st(launch_qknorm_rope_store(q, k, v, q_norm, k_norm, mode, eps, n_head, n_head_kv, head_dim, pos, nullptr,
-                                       pos + 1, freq_base, q_out, static_cast<__half*>(k_cache),
-                                       static_cast<__half*>(v_cache), (cudaStream_t)stream));
+                                       pos + 1, freq_base, q_out, k_cache, v_cache, kv_type == HOARD_TYPE_BF16,
+                                       (cudaStream_t)stream));
 }
 
 int hoard_hx_qknorm_rope_store_at(const float* q, const float* k, const float* v, const float* q_norm,
                                   const float* k_norm, int mode, float eps, int n_head, int n_head_kv, int head_dim,
                                   const int32_t* pos, int max_ctx, float freq_base, float* q_out, void* k_cache,
-                                  void* v_cache, hoard_stream stream) {
+                                  void* v_cache, int kv_type, hoard_stream stream) {
     int rc = qknorm_check(q, k, v, q_norm, k_norm, mode, n_head, n_head_kv, head_dim, q_out, k_cache, v_cache);
-    if (rc || !pos || max_ctx <= 0 || !(freq_base > 0)) return rc ? rc : HOARD_EINVAL;
+    if (rc || !pos || max_ctx <= 0 || !(freq_base > 0) || !kv_ok(kv_type)) return rc ? rc : HOARD_EINVAL;
     return st(launch_qknorm_rope_store(q, k, v, q_norm, k_norm, mode, eps, n_head, n_head_kv, head_dim, 0, pos,
-                                       max_ctx, freq_base, q_out, static_cast<__half*>(k_cache),
-                                       static_cast<__half*>(v_cache), (cudaStream_t)stream));
+                                       max_ctx, freq_base, q_out, k_cache, v_cache, kv_type == HOARD_TYPE_BF16,
+                                       (cudaStream_t)stream));
 }
 
 }  // extern "C"

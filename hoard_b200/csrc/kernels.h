@@ -128,12 +128,13 @@ cudaError_t launch_embed(int type, const uint8_t* table, int H, int64_t n_vocab,
                          const int32_t* pos, float* out, cudaStream_t s);
 cudaError_t launch_qgemv(int type, const uint8_t* w, int N, int K, const int8_t* xq, const float* xd, const int* xbs,
                          const float* resid, float* y, cudaStream_t s);
+// KV caches hold f16, or bf16 when kv_bf16
 cudaError_t launch_rope_store(float* q, float* k, const float* v, int n_head, int n_kv, int hd, int pos,
-                              const int32_t* pos_dev, int max_ctx, float freq_base, __half* kc, __half* vc,
+                              const int32_t* pos_dev, int max_ctx, float freq_base, void* kc, void* vc, bool kv_bf16,
                               cudaStream_t s);
 size_t attention_smem(int hd, int n_pos);
-cudaError_t launch_attention(const float* q, const __half* kc, const __half* vc, int n_head, int n_kv, int hd,
-                             int n_pos, const int32_t* pos_dev, float scale, float* out, cudaStream_t s);
+cudaError_t launch_attention(const float* q, const void* kc, const void* vc, bool kv_bf16, int n_head, int n_kv,
+                             int hd, int n_pos, const int32_t* pos_dev, float scale, float* out, cudaStream_t s);
 cudaError_t launch_argmax(const float* v, int n, int32_t* out, int32_t* pos, int seq_len, cudaStream_t s);
 cudaError_t launch_rmsnorm_q8(const float* x, int H, float eps, const float* w, int8_t* q, float* d, int* bs,
                               cudaStream_t s);
@@ -142,8 +143,8 @@ cudaError_t launch_qgemv_set(int n, const int* types, const uint8_t* const* w, c
                              const int* xbs, cudaStream_t s);
 cudaError_t launch_qknorm_rope_store(const float* q, const float* k, const float* v, const float* qn, const float* kn,
                                      int mode, float eps, int n_head, int n_kv, int hd, int pos,
-                                     const int32_t* pos_dev, int max_ctx, float freq_base, float* q_out, __half* kc,
-                                     __half* vc, cudaStream_t s);
+                                     const int32_t* pos_dev, int max_ctx, float freq_base, float* q_out, void* kc,
+                                     void* vc, bool kv_bf16, cudaStream_t s);
 
 // ---- expert parallelism over NVLink peer memory ----
 // Every rank allocates one block with this layout (identical on all ranks, so a peer's field is its

@@ -81,14 +81,20 @@ __global__ void __launch_bounds__(256) k_qgemv(const uint8_t* __restrict__ w, in
     if (lane == 0) y[n] = resid ? v + resid[n] : v;
 }
 
+// KV cache elements: f16 or bf16 (round to nearest even either way)
+__device__ __forceinline__ void kv_put(__half* p, float v) { *p = __float2half_rn(v); }
+__device__ __forceinline__ void kv_put(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+__device__ __forceinline__ float kv_get(const __half* p) { return __half2float(*p); }
+__device__ __forceinline__ float kv_get(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
 // ---- NEOX RoPE of q [n_head][hd] and k [n_kv][hd] in place at position pos, then k and v stored
-//      as f16 into the caches at [pos][kv head][hd]. theta_i = pos * base^(-2i/hd) formed by
+//      as f16 or bf16 into the caches at [pos][kv head][hd]. theta_i = pos * base^(-2i/hd) formed by
 //      repeated multiplication, as ggml's rope cache does ----
+template <typename KT>
 __global__ void __launch_bounds__(256) k_rope_store(float* __restrict__ q, float* __restrict__ k,
                                                     const float* __restrict__ v, int n_head, int n_kv, int hd,
                                                     int pos, const int32_t* __restrict__ pos_dev, int max_ctx,
-                                                    float theta_scale, __half* __restrict__ kc,
-                                                    __half* __restrict__ vc) {
+                                                    float theta_scale, KT* __restrict__ kc, KT* __restrict__ vc) {
     if (pos_dev) pos = *pos_dev;
     if (pos < 0 || pos >= max_ctx) return;              // outside the cache: nothing is written
     const int half = hd / 2;
@@ -105,13 +111,13 @@ __global__ void __launch_bounds__(256) k_rope_store(float* __restrict__ q, float
         x[i + half] = r1;
         if (head >= n_head) {
             const int64_t o = ((int64_t)pos * n_kv + (head - n_head)) * hd;
-            kc[o + i] = __float2half_rn(r0);
-            kc[o + i + half] = __float2half_rn(r1);
+            kv_put(kc + o + i, r0);
+            kv_put(kc + o + i + half, r1);
         }
     }
     const int nv = n_kv * hd;
     for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < nv; t += gridDim.x * blockDim.x)
-        vc[(int64_t)pos * nv + t] = __float2half_rn(v[t]);
+        kv_put(vc + (int64_t)pos * nv + t, v[t]);
 }
 
 // sum over u = t, t + 128, ... < n of (double)(v[u]^2), in that order, with eight loads issued
@@ -130,11 +136,12 @@ __device__ __forceinline__ double sumsq_stride128(const float* __restrict__ v, i
 }
 
 // ---- single-query attention: one CTA per head; scores over the n_pos cached keys of its KV head
-//      (f16, products and sums in f32), softmax with the max subtracted and a double sum, then the
-//      probability-weighted sum of the cached values ----
+//      (f16 or bf16, products and sums in f32), softmax with the max subtracted and a double sum, then
+//      the probability-weighted sum of the cached values ----
 constexpr int ATT_THREADS = 256;
-__global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restrict__ q, const __half* __restrict__ kc,
-                                                          const __half* __restrict__ vc, int n_head, int n_kv, int hd,
+template <typename KT>
+__global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restrict__ q, const KT* __restrict__ kc,
+                                                          const KT* __restrict__ vc, int n_head, int n_kv, int hd,
                                                           int n_pos, const int32_t* __restrict__ pos_dev,
                                                           float scale, float* __restrict__ out) {
     extern __shared__ float sm[];
@@ -150,9 +157,9 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
     for (int i = threadIdx.x; i < hd; i += blockDim.x) sq[i] = q[(int64_t)h * hd + i];
     __syncthreads();
     for (int j = warp; j < n_pos; j += nw) {
-        const __half* kr = kc + ((int64_t)j * n_kv + kvh) * hd;
+        const KT* kr = kc + ((int64_t)j * n_kv + kvh) * hd;
         float s = 0.f;
-        for (int i = lane; i < hd; i += 32) s += sq[i] * __half2float(kr[i]);
+        for (int i = lane; i < hd; i += 32) s += sq[i] * kv_get(kr + i);
         s = warp_sum(s);
         if (lane == 0) sp[j] = s * scale;
     }
@@ -174,7 +181,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
     if (threadIdx.x < G * hd) {
         const int g = threadIdx.x / hd, i = threadIdx.x - g * hd;
         float acc = 0.f;
-        for (int j = g; j < n_pos; j += G) acc += (sp[j] * inv) * __half2float(vc[((int64_t)j * n_kv + kvh) * hd + i]);
+        for (int j = g; j < n_pos; j += G) acc += (sp[j] * inv) * kv_get(vc + ((int64_t)j * n_kv + kvh) * hd + i);
         part[g * hd + i] = acc;
     }
     __syncthreads();
@@ -259,13 +266,14 @@ __global__ void __launch_bounds__(256) k_qgemv_set(GemvSet g, int K, const int8_
 //      [hd]; 0: none) + NEOX RoPE + KV store: one CTA per q or k head, one thread per rotated pair.
 //      Rotated q goes to q_out (mode 1 reads the whole input vector in every CTA); rotated k and v
 //      go to the caches ----
+template <typename KT>
 __global__ void __launch_bounds__(128) k_qknorm_rope_store(const float* __restrict__ q, const float* __restrict__ k,
                                                            const float* __restrict__ v, const float* __restrict__ qn,
                                                            const float* __restrict__ kn, int mode, float eps,
                                                            int n_head, int n_kv, int hd, int pos,
                                                            const int32_t* __restrict__ pos_dev, int max_ctx,
                                                            float theta_scale, float* __restrict__ q_out,
-                                                           __half* __restrict__ kc, __half* __restrict__ vc) {
+                                                           KT* __restrict__ kc, KT* __restrict__ vc) {
     __shared__ double redd[32];
     if (pos_dev) pos = *pos_dev;
     if (pos < 0 || pos >= max_ctx) return;
@@ -301,10 +309,10 @@ __global__ void __launch_bounds__(128) k_qknorm_rope_store(const float* __restri
             q_out[(int64_t)hh * hd + i + half] = r1;
         } else {
             const int64_t o = ((int64_t)pos * n_kv + hh) * hd;
-            kc[o + i] = __float2half_rn(r0);
-            kc[o + i + half] = __float2half_rn(r1);
-            vc[o + i] = __float2half_rn(v[(int64_t)hh * hd + i]);
-            vc[o + i + half] = __float2half_rn(v[(int64_t)hh * hd + i + half]);
+            kv_put(kc + o + i, r0);
+            kv_put(kc + o + i + half, r1);
+            kv_put(vc + o + i, v[(int64_t)hh * hd + i]);
+            kv_put(vc + o + i + half, v[(int64_t)hh * hd + i + half]);
         }
     }
 }
@@ -402,12 +410,17 @@ cudaError_t launch_qgemv_set(int n, const int* types, const uint8_t* const* w, c
 
 cudaError_t launch_qknorm_rope_store(const float* q, const float* k, const float* v, const float* qn, const float* kn,
                                      int mode, float eps, int n_head, int n_kv, int hd, int pos,
-                                     const int32_t* pos_dev, int max_ctx, float freq_base, float* q_out, __half* kc,
-                                     __half* vc, cudaStream_t s) {
+                                     const int32_t* pos_dev, int max_ctx, float freq_base, float* q_out, void* kc,
+                                     void* vc, bool kv_bf16, cudaStream_t s) {
     if (hd / 2 > 128) return cudaErrorInvalidValue;
     const float theta_scale = powf(freq_base, -2.0f / (float)hd);
-    k_qknorm_rope_store<<<n_head + n_kv, 128, 0, s>>>(q, k, v, qn, kn, mode, eps, n_head, n_kv, hd, pos, pos_dev,
-                                                      max_ctx, theta_scale, q_out, kc, vc);
+    if (kv_bf16)
+        k_qknorm_rope_store<<<n_head + n_kv, 128, 0, s>>>(q, k, v, qn, kn, mode, eps, n_head, n_kv, hd, pos, pos_dev,
+                                                          max_ctx, theta_scale, q_out, (__nv_bfloat16*)kc,
+                                                          (__nv_bfloat16*)vc);
+    else
+        k_qknorm_rope_store<<<n_head + n_kv, 128, 0, s>>>(q, k, v, qn, kn, mode, eps, n_head, n_kv, hd, pos, pos_dev,
+                                                          max_ctx, theta_scale, q_out, (__half*)kc, (__half*)vc);
     return cudaGetLastError();
 }
 
@@ -431,12 +444,16 @@ cudaError_t launch_qgemv(int type, const uint8_t* w, int N, int K, const int8_t*
 }
 
 cudaError_t launch_rope_store(float* q, float* k, const float* v, int n_head, int n_kv, int hd, int pos,
-                              const int32_t* pos_dev, int max_ctx, float freq_base, __half* kc, __half* vc,
+                              const int32_t* pos_dev, int max_ctx, float freq_base, void* kc, void* vc, bool kv_bf16,
                               cudaStream_t s) {
     const float theta_scale = powf(freq_base, -2.0f / (float)hd);
     const int n = (n_head + n_kv) * (hd / 2);
-    k_rope_store<<<(n + 255) / 256, 256, 0, s>>>(q, k, v, n_head, n_kv, hd, pos, pos_dev, max_ctx, theta_scale, kc,
-                                                 vc);
+    if (kv_bf16)
+        k_rope_store<<<(n + 255) / 256, 256, 0, s>>>(q, k, v, n_head, n_kv, hd, pos, pos_dev, max_ctx, theta_scale,
+                                                     (__nv_bfloat16*)kc, (__nv_bfloat16*)vc);
+    else
+        k_rope_store<<<(n + 255) / 256, 256, 0, s>>>(q, k, v, n_head, n_kv, hd, pos, pos_dev, max_ctx, theta_scale,
+                                                     (__half*)kc, (__half*)vc);
     return cudaGetLastError();
 }
 
@@ -444,14 +461,20 @@ size_t attention_smem(int hd, int n_pos) {
     return (size_t)(hd + n_pos + (ATT_THREADS / hd) * hd) * sizeof(float);
 }
 
-cudaError_t launch_attention(const float* q, const __half* kc, const __half* vc, int n_head, int n_kv, int hd,
-                             int n_pos, const int32_t* pos_dev, float scale, float* out, cudaStream_t s) {
+cudaError_t launch_attention(const float* q, const void* kc, const void* vc, bool kv_bf16, int n_head, int n_kv,
+                             int hd, int n_pos, const int32_t* pos_dev, float scale, float* out, cudaStream_t s) {
     const size_t smem = attention_smem(hd, n_pos);
+    const void* fn = kv_bf16 ? (const void*)k_attention<__nv_bfloat16> : (const void*)k_attention<__half>;
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    k_attention<<<n_head, ATT_THREADS, smem, s>>>(q, kc, vc, n_head, n_kv, hd, n_pos, pos_dev, scale, out);
+    if (kv_bf16)
+        k_attention<<<n_head, ATT_THREADS, smem, s>>>(q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, n_head,
+                                                      n_kv, hd, n_pos, pos_dev, scale, out);
+    else
+        k_attention<<<n_head, ATT_THREADS, smem, s>>>(q, (const __half*)kc, (const __half*)vc, n_head, n_kv, hd, n_pos,
+                                                      pos_dev, scale, out);
     return cudaGetLastError();
 }
 

@@ -6,7 +6,7 @@
               cur = RMSNorm(x) * attn_norm
               q, k, v = Wq cur, Wk cur, Wv cur          (Q4_K / Q6_K . Q8_K(cur), hoard_hx_gemv)
               QK RMSNorm: over the whole projection (OLMoE) or per head (Qwen3)
-              NEOX RoPE of q, k at position p; k, v into the f16 KV cache      (hoard_hx_rope_store)
+              NEOX RoPE of q, k at position p; k, v into the f16/bf16 KV cache (hoard_hx_rope_store)
               att = softmax(q k^T / sqrt(head_dim)) v over positions 0..p     (hoard_hx_attention)
               ffn_inp = Wo att + x
               x = ffn_inp + sum_j w_j FFN_j(RMSNorm(ffn_inp) * ffn_norm)       (hoard_moe_layers)
@@ -30,6 +30,7 @@ from hoard_b200 import moe, quant
 from hoard_b200.moe import HoardError, _ptr, _stream, lib
 
 Q4_K, Q6_K, F32 = quant.Q4_K, quant.Q6_K, 0
+KV_TYPES = {torch.float16: 1, torch.bfloat16: 30}     # KV cache element -> HOARD_TYPE_F16 / HOARD_TYPE_BF16
 MAX_BATCH = 16          # tokens of one batched (verify) forward
 QK_MODE = {"": 0, "full": 1, "head": 2}
 
@@ -56,18 +57,19 @@ def _hx():
         L.hoard_hx_q8_bytes.restype = i64
         L.hoard_hx_quant_q8.argtypes = [vp, i32, vp, vp]
         L.hoard_hx_gemv.argtypes = [i32, vp, i32, i32, vp, vp, vp, vp]
-        L.hoard_hx_rope_store.argtypes = [vp, vp, vp, i32, i32, i32, i32, f32, vp, vp, vp]
-        L.hoard_hx_attention.argtypes = [vp, vp, vp, i32, i32, i32, i32, f32, vp, vp]
+        L.hoard_hx_rope_store.argtypes = [vp, vp, vp, i32, i32, i32, i32, f32, vp, vp, i32, vp]
+        L.hoard_hx_attention.argtypes = [vp, vp, vp, i32, i32, i32, i32, f32, vp, i32, vp]
         L.hoard_hx_argmax.argtypes = [vp, i32, vp, vp]
         L.hoard_hx_embed_at.argtypes = [i32, vp, i32, i64, vp, vp, vp, vp]
-        L.hoard_hx_rope_store_at.argtypes = [vp, vp, vp, i32, i32, i32, vp, i32, f32, vp, vp, vp]
-        L.hoard_hx_attention_at.argtypes = [vp, vp, vp, i32, i32, i32, vp, i32, f32, vp, vp]
+        L.hoard_hx_rope_store_at.argtypes = [vp, vp, vp, i32, i32, i32, vp, i32, f32, vp, vp, i32, vp]
+        L.hoard_hx_attention_at.argtypes = [vp, vp, vp, i32, i32, i32, vp, i32, f32, vp, i32, vp]
         L.hoard_hx_argmax_at.argtypes = [vp, i32, vp, vp, i32, vp]
         L.hoard_hx_rmsnorm_q8.argtypes = [vp, i32, f32, vp, vp, vp]
         L.hoard_hx_gemv_multi.argtypes = [i32, vp, vp, vp, i32, vp, vp, vp, vp]
-        L.hoard_hx_qknorm_rope_store.argtypes = [vp, vp, vp, vp, vp, i32, f32, i32, i32, i32, i32, f32, vp, vp, vp, vp]
+        L.hoard_hx_qknorm_rope_store.argtypes = [vp, vp, vp, vp, vp, i32, f32, i32, i32, i32, i32, f32, vp, vp, vp, i32,
+                                                 vp]
         L.hoard_hx_qknorm_rope_store_at.argtypes = [vp, vp, vp, vp, vp, i32, f32, i32, i32, i32, vp, i32, f32, vp, vp,
-                                                   vp, vp]
+                                                   vp, i32, vp]
         _bound = True
     return L
 
@@ -170,9 +172,14 @@ def config_from_hparams(hp) -> ModelConfig:
 
 
 class DecodeModel:
-    def __init__(self, cfg: ModelConfig, tensors: dict, device: int = 0, max_ctx: int = 512, eos_id: int = -1):
-        """tensors: name -> (ggml type, ne, array or tensor of raw bytes / f32 values), host or device."""
+    def __init__(self, cfg: ModelConfig, tensors: dict, device: int = 0, max_ctx: int = 512, eos_id: int = -1,
+                 kv_dtype=torch.float16):
+        """tensors: name -> (ggml type, ne, array or tensor of raw bytes / f32 values), host or device.
+        kv_dtype: torch.float16 or torch.bfloat16 elements of the KV cache."""
+        if kv_dtype not in (torch.float16, torch.bfloat16):
+            raise ValueError("kv_dtype must be torch.float16 or torch.bfloat16")
         self.cfg, self.device, self.max_ctx, self.eos_id = cfg, device, max_ctx, eos_id
+        self.kv_type = KV_TYPES[kv_dtype]
         dev = self.dev = torch.device("cuda", device)
         _hx()
         H, hd = cfg.n_embd, cfg.head_dim
@@ -232,7 +239,7 @@ class DecodeModel:
         self.qkv_y = _parr([self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr()])
         kq = max(H, self.nq)
         self.q8 = torch.zeros(int(_hx().hoard_hx_q8_bytes(kq)), dtype=torch.uint8, device=dev)
-        self.kc = torch.zeros(cfg.n_layer, max_ctx, self.nkv, dtype=torch.float16, device=dev)
+        self.kc = torch.zeros(cfg.n_layer, max_ctx, self.nkv, dtype=kv_dtype, device=dev)
         self.vc = torch.zeros_like(self.kc)
         self.seq = torch.zeros(max_ctx + 1, dtype=torch.int32, device=dev)
         self.scratch_tok = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -241,7 +248,7 @@ class DecodeModel:
         torch.cuda.synchronize(dev)
 
     @classmethod
-    def from_gguf(cls, path: str, device: int = 0, max_ctx: int = 512):
+    def from_gguf(cls, path: str, device: int = 0, max_ctx: int = 512, kv_dtype=torch.float16):
         from hoard_b200 import gguf_io as gi
         g = gi.GGUFFile(path)
         hp = gi.read_hparams(g)
@@ -250,7 +257,8 @@ class DecodeModel:
             data = g.array(name) if t.type == F32 else g.data(name)
             tensors[name] = (t.type, t.ne, np.array(data))
         g.close()
-        return cls(config_from_hparams(hp), tensors, device=device, max_ctx=max_ctx, eos_id=hp.eos_id)
+        return cls(config_from_hparams(hp), tensors, device=device, max_ctx=max_ctx, eos_id=hp.eos_id,
+                   kv_dtype=kv_dtype)
 
     def close(self):
         self.moe.close()
@@ -286,15 +294,17 @@ class DecodeModel:
         if pos is None:
             _ok(hx.hoard_hx_qknorm_rope_store_at(_ptr(q), _ptr(k), _ptr(v), _ptr(qn), _ptr(kn), mode, c.eps, c.n_head,
                                                  c.n_head_kv, hd, _ptr(self.pos_dev), self.max_ctx, c.freq_base,
-                                                 _ptr(q_rot), _ptr(self.kc[il]), _ptr(self.vc[il]), s), "qk rope")
+                                                 _ptr(q_rot), _ptr(self.kc[il]), _ptr(self.vc[il]), self.kv_type, s),
+                "qk rope")
             _ok(hx.hoard_hx_attention_at(_ptr(q_rot), _ptr(self.kc[il]), _ptr(self.vc[il]), c.n_head, c.n_head_kv, hd,
-                                         _ptr(self.pos_dev), self.max_ctx, scale, _ptr(att), s), "attention")
+                                         _ptr(self.pos_dev), self.max_ctx, scale, _ptr(att), self.kv_type, s),
+                "attention")
         else:
             _ok(hx.hoard_hx_qknorm_rope_store(_ptr(q), _ptr(k), _ptr(v), _ptr(qn), _ptr(kn), mode, c.eps, c.n_head,
                                               c.n_head_kv, hd, pos, c.freq_base, _ptr(q_rot), _ptr(self.kc[il]),
-                                              _ptr(self.vc[il]), s), "qk rope")
+                                              _ptr(self.vc[il]), self.kv_type, s), "qk rope")
             _ok(hx.hoard_hx_attention(_ptr(q_rot), _ptr(self.kc[il]), _ptr(self.vc[il]), c.n_head, c.n_head_kv, hd,
-                                      pos + 1, scale, _ptr(att), s), "attention")
+                                      pos + 1, scale, _ptr(att), self.kv_type, s), "attention")
         _ok(hx.hoard_hx_quant_q8(_ptr(att), self.nq, _ptr(self.q8), s), "quant")
         ty, wo = L["o"]
         _ok(hx.hoard_hx_gemv(ty, _ptr(wo), H, self.nq, _ptr(self.q8), _ptr(x), _ptr(x2), s), "gemv")

@@ -11,7 +11,8 @@
  * Quantised weights (Q4_K = 12, Q6_K = 14) are used in the plane layout that hoard_hx_repack
  * produces from raw GGUF blocks; projections quantise the activation to Q8_K first
  * (hoard_hx_quant_q8) and form exact integer block dots, the semantics of ggml's CPU mul_mat. The KV
- * cache is f16 [max_ctx][n_head_kv][head_dim] per layer. All pointers are device pointers; every
+ * cache is [max_ctx][n_head_kv][head_dim] per layer of f16 or bf16 (kv_type HOARD_TYPE_F16 /
+ * HOARD_TYPE_BF16; hoard keeps an f32 cache, src/run_moe_stream.cpp:239). All pointers are device pointers; every
  * call is asynchronous on `stream`. Status codes are those of hoard_moe.h. */
 #ifndef HOARD_HARNESS_H
 #define HOARD_HARNESS_H
@@ -43,13 +44,14 @@ int hoard_hx_gemv(int type, const void* w_plane, int N, int K, const void* q8, c
                   hoard_stream stream);
 
 /* NEOX RoPE of q [n_head][head_dim] and k [n_head_kv][head_dim] (in place) at position pos with
- * theta_i = pos * freq_base^(-2i/head_dim); then k and v stored as f16 at cache row pos. */
+ * theta_i = pos * freq_base^(-2i/head_dim); then k and v stored (f16 or bf16, rounded to nearest) at
+ * cache row pos. */
 int hoard_hx_rope_store(float* q, float* k, const float* v, int n_head, int n_head_kv, int head_dim, int pos,
-                        float freq_base, void* k_cache, void* v_cache, hoard_stream stream);
+                        float freq_base, void* k_cache, void* v_cache, int kv_type, hoard_stream stream);
 
 /* out[h] = softmax(scale * q[h] . K[0..n_pos)) . V[0..n_pos) of KV head h / (n_head / n_head_kv). */
 int hoard_hx_attention(const float* q, const void* k_cache, const void* v_cache, int n_head, int n_head_kv,
-                       int head_dim, int n_pos, float scale, float* out, hoard_stream stream);
+                       int head_dim, int n_pos, float scale, float* out, int kv_type, hoard_stream stream);
 
 /* *out = the first index of the maximum of v[0..n). */
 int hoard_hx_argmax(const float* v, int n, int32_t* out, hoard_stream stream);
@@ -63,9 +65,10 @@ int hoard_hx_embed_at(int type, const void* table, int n_embd, int64_t n_vocab, 
                       const int32_t* pos, float* x_out, hoard_stream stream);
 int hoard_hx_rope_store_at(float* q, float* k, const float* v, int n_head, int n_head_kv, int head_dim,
                            const int32_t* pos, int max_ctx, float freq_base, void* k_cache, void* v_cache,
-                           hoard_stream stream);
+                           int kv_type, hoard_stream stream);
 int hoard_hx_attention_at(const float* q, const void* k_cache, const void* v_cache, int n_head, int n_head_kv,
-                          int head_dim, const int32_t* pos, int max_ctx, float scale, float* out, hoard_stream stream);
+                          int head_dim, const int32_t* pos, int max_ctx, float scale, float* out, int kv_type,
+                          hoard_stream stream);
 int hoard_hx_argmax_at(const float* v, int n, int32_t* seq, int32_t* pos, int seq_len, hoard_stream stream);
 
 /* ---- fused forms of the steps above (fewer launches per layer) ----
@@ -80,12 +83,12 @@ int hoard_hx_gemv_multi(int n, const int* types, const void* const* w_planes, co
                         const float* const* resid, float* const* y, hoard_stream stream);
 int hoard_hx_qknorm_rope_store(const float* q, const float* k, const float* v, const float* q_norm,
                                const float* k_norm, int mode, float eps, int n_head, int n_head_kv, int head_dim,
-                               int pos, float freq_base, float* q_out, void* k_cache, void* v_cache,
+                               int pos, float freq_base, float* q_out, void* k_cache, void* v_cache, int kv_type,
                                hoard_stream stream);
 int hoard_hx_qknorm_rope_store_at(const float* q, const float* k, const float* v, const float* q_norm,
                                   const float* k_norm, int mode, float eps, int n_head, int n_head_kv, int head_dim,
                                   const int32_t* pos, int max_ctx, float freq_base, float* q_out, void* k_cache,
-                                  void* v_cache, hoard_stream stream);
+                                  void* v_cache, int kv_type, hoard_stream stream);
 
 #ifdef __cplusplus
 }

@@ -31,6 +31,7 @@ extern "C" {
 
 /* weight / activation types: GGUF (ggml) type ids */
 #define HOARD_TYPE_F32 0
+#define HOARD_TYPE_F16 1
 #define HOARD_TYPE_Q4_K 12
 #define HOARD_TYPE_Q6_K 14
 #define HOARD_TYPE_BF16 30

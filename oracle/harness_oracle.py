@@ -13,8 +13,8 @@ Follows src/run_moe_stream.cpp:295-472 step by step:
   MoE       x = ffn_inp + sum_j w_j FFN_j(RMSNorm(ffn_inp) * ffn_norm) (oracle.moe_layer)
   head      RMSNorm(x) * output_norm, lm-head, argmax (first maximum)                :452-472
 Two choices follow the configuration rather than the reference (which keeps an f32 cache): the
-KV cache holds f16 (config C1 asks for an fp16 KV cache), and every position, the current one
-included, is read back from it.
+KV cache holds f16 (config C1 asks for an fp16 KV cache) or bf16 (config C3), and every position,
+the current one included, is read back from it.
 """
 from __future__ import annotations
 
@@ -51,14 +51,25 @@ def rope_neox(x: np.ndarray, n_heads: int, hd: int, pos: int, freq_base: float) 
     return x.reshape(-1)
 
 
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """f32 values rounded to the nearest bf16 (ties to even), returned as f32."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    return r.view(np.float32)
+
+
 class OracleDecoder:
-    def __init__(self, cfg, tensors: dict, max_ctx: int):
-        """tensors: name -> (ggml type, ne, numpy raw bytes / f32 values), as the harness takes them."""
+    def __init__(self, cfg, tensors: dict, max_ctx: int, kv: str = "f16"):
+        """tensors: name -> (ggml type, ne, numpy raw bytes / f32 values), as the harness takes them;
+        kv: "f16" or "bf16" elements of the KV cache."""
         self.cfg = cfg
         self.t = {k: (ty, ne, np.asarray(v)) for k, (ty, ne, v) in tensors.items()}
         hd = cfg.head_dim
         self.nq, self.nkv = cfg.n_head * hd, cfg.n_head_kv * hd
-        self.kc = np.zeros((cfg.n_layer, max_ctx, self.nkv), np.float16)
+        if kv not in ("f16", "bf16"):
+            raise ValueError("kv must be f16 or bf16")
+        self.kv = kv
+        self.kc = np.zeros((cfg.n_layer, max_ctx, self.nkv), np.float16 if kv == "f16" else np.float32)
         self.vc = np.zeros_like(self.kc)
 
     def _mv(self, name, n_out, k_in, x):
@@ -90,8 +101,12 @@ class OracleDecoder:
                 k = rms_norm(k, self._f(b + "attn_k_norm.weight"), c.n_head_kv, hd, c.eps)
             q = rope_neox(q, c.n_head, hd, pos, c.freq_base)
             k = rope_neox(k, c.n_head_kv, hd, pos, c.freq_base)
-            self.kc[il, pos] = k.astype(np.float16)
-            self.vc[il, pos] = v.astype(np.float16)
+            if self.kv == "f16":
+                self.kc[il, pos] = k.astype(np.float16)
+                self.vc[il, pos] = v.astype(np.float16)
+            else:
+                self.kc[il, pos] = bf16_round(k)
+                self.vc[il, pos] = bf16_round(v)
             K = self.kc[il, :pos + 1].astype(np.float32).reshape(pos + 1, c.n_head_kv, hd)
             V = self.vc[il, :pos + 1].astype(np.float32).reshape(pos + 1, c.n_head_kv, hd)
             att = np.empty((c.n_head, hd), np.float32)

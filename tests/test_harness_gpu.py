@@ -126,14 +126,14 @@ def test_ops_match_oracle():
     k = torch.randn(nkv * hd, generator=g, device=dev)
     v = torch.randn(nkv * hd, generator=g, device=dev)
     q0, k0 = q.cpu().numpy().copy(), k.cpu().numpy().copy()
-    assert L.hoard_hx_rope_store(_ptr(q), _ptr(k), _ptr(v), nh, nkv, hd, pos, 1e6, _ptr(kc), _ptr(vc), s) == 0
+    assert L.hoard_hx_rope_store(_ptr(q), _ptr(k), _ptr(v), nh, nkv, hd, pos, 1e6, _ptr(kc), _ptr(vc), 1, s) == 0
     np.testing.assert_allclose(q.cpu().numpy(), rope_neox(q0, nh, hd, pos, 1e6), rtol=1e-5, atol=2e-5)
     np.testing.assert_allclose(k.cpu().numpy(), rope_neox(k0, nkv, hd, pos, 1e6), rtol=1e-5, atol=2e-5)
     assert np.array_equal(kc[pos].cpu().numpy(), k.cpu().numpy().astype(np.float16))
     assert np.array_equal(vc[pos].cpu().numpy(), v.cpu().numpy().astype(np.float16))
     att = torch.empty(nh * hd, device=dev)
     sc = 1.0 / np.sqrt(hd)
-    assert L.hoard_hx_attention(_ptr(q), _ptr(kc), _ptr(vc), nh, nkv, hd, n_pos, sc, _ptr(att), s) == 0
+    assert L.hoard_hx_attention(_ptr(q), _ptr(kc), _ptr(vc), nh, nkv, hd, n_pos, sc, _ptr(att), 1, s) == 0
     K = kc[:n_pos].float().cpu().numpy().reshape(n_pos, nkv, hd)
     V = vc[:n_pos].float().cpu().numpy().reshape(n_pos, nkv, hd)
     qh = q.cpu().numpy().reshape(nh, hd)
@@ -215,13 +215,79 @@ def test_fused_ops_match_unfused():
         kc2, vc2 = kc1.clone(), vc1.clone()
         qo = torch.empty_like(q)
         assert L.hoard_hx_qknorm_rope_store(_ptr(q), _ptr(k), _ptr(v), _ptr(qn), _ptr(kn), mode, 1e-6, nh, nkv, hd, pos,
-                                            1e6, _ptr(qo), _ptr(kc1), _ptr(vc1), s) == 0
+                                            1e6, _ptr(qo), _ptr(kc1), _ptr(vc1), 1, s) == 0
         q2, k2 = q.clone(), k.clone()
         rows_q, cols_q = (1, nh * hd) if mode == 1 else (nh, hd)
         rows_k, cols_k = (1, nkv * hd) if mode == 1 else (nkv, hd)
         assert L.hoard_hx_rmsnorm(_ptr(q2), rows_q, cols_q, 1e-6, _ptr(qn), _ptr(q2), s) == 0
         assert L.hoard_hx_rmsnorm(_ptr(k2), rows_k, cols_k, 1e-6, _ptr(kn), _ptr(k2), s) == 0
-        assert L.hoard_hx_rope_store(_ptr(q2), _ptr(k2), _ptr(v), nh, nkv, hd, pos, 1e6, _ptr(kc2), _ptr(vc2), s) == 0
+        assert L.hoard_hx_rope_store(_ptr(q2), _ptr(k2), _ptr(v), nh, nkv, hd, pos, 1e6, _ptr(kc2), _ptr(vc2), 1, s) == 0
         torch.testing.assert_close(qo, q2, rtol=1e-5, atol=1e-6)
         torch.testing.assert_close(kc1.float(), kc2.float(), rtol=2e-3, atol=2e-3)
         assert torch.equal(vc1, vc2)
+
+
+def test_bf16_kv_ops_and_qwen3_attention_decode():
+    """The KV cache in bf16 (config C3): rope_store writes the rotated k and v rounded to bf16 and
+    attention reads them back (checked against numpy on the same rounded values); then greedy decode
+    at the Qwen3-30B-A3B attention shapes (GQA 32/4 x 128, per-head QK norm, theta 1e6, vocab 151936,
+    E 128 top-8 + renorm, I 768; 2 layers) against the oracle decoder with a bf16 cache, with the
+    criteria of test_greedy_decode_matches_oracle."""
+    from oracle.harness_oracle import OracleDecoder, bf16_round, rope_neox
+    from hoard_b200.moe import _ptr, _stream
+    dev = torch.device("cuda", 0)
+    L, s = hx._hx(), _stream(None)
+    g = torch.Generator(device=dev).manual_seed(21)
+    nh, nkv, hd, pos, n_pos = 32, 4, 128, 9, 10
+    q = torch.randn(nh * hd, generator=g, device=dev)
+    k = torch.randn(nkv * hd, generator=g, device=dev)
+    v = torch.randn(nkv * hd, generator=g, device=dev)
+    q0, k0, v0 = q.cpu().numpy().copy(), k.cpu().numpy().copy(), v.cpu().numpy().copy()
+    kc = torch.randn(16, nkv * hd, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(16, nkv * hd, generator=g, device=dev).to(torch.bfloat16)
+    assert L.hoard_hx_rope_store(_ptr(q), _ptr(k), _ptr(v), nh, nkv, hd, pos, 1e6, _ptr(kc), _ptr(vc), 30, s) == 0
+    np.testing.assert_allclose(k.cpu().numpy(), rope_neox(k0, nkv, hd, pos, 1e6), rtol=1e-5, atol=2e-5)
+    assert np.array_equal(kc[pos].float().cpu().numpy(), bf16_round(k.cpu().numpy()))
+    assert np.array_equal(vc[pos].float().cpu().numpy(), bf16_round(v0))
+    att = torch.empty(nh * hd, device=dev)
+    sc = 1.0 / np.sqrt(hd)
+    assert L.hoard_hx_attention(_ptr(q), _ptr(kc), _ptr(vc), nh, nkv, hd, n_pos, sc, _ptr(att), 30, s) == 0
+    K = kc[:n_pos].float().cpu().numpy().reshape(n_pos, nkv, hd)
+    V = vc[:n_pos].float().cpu().numpy().reshape(n_pos, nkv, hd)
+    qh = q.cpu().numpy().reshape(nh, hd)
+    for h in range(nh):
+        sco = K[:, h // (nh // nkv)] @ qh[h] * sc
+        p = np.exp(sco - sco.max())
+        p /= p.sum()
+        np.testing.assert_allclose(att[h * hd:(h + 1) * hd].cpu().numpy(), p @ V[:, h // (nh // nkv)],
+                                   rtol=1e-4, atol=1e-5)
+    # decode at the Qwen3 attention shapes, bf16 cache
+    cfg = hx.ModelConfig("qwen3moe", 2, 2048, 32, 4, 128, 128, 8, 768, 151936, 1e6, 1e-6, "head", True)
+    tensors = hx.seeded_tensors(cfg, seed=23, device=dev)
+    model = hx.DecodeModel(cfg, tensors, device=0, max_ctx=64, kv_dtype=torch.bfloat16)
+    try:
+        prompt = np.random.default_rng(8).integers(0, cfg.n_vocab, N_PROMPT).tolist()
+        n_gen = 16
+        logits = torch.empty(n_gen, cfg.n_vocab, device=dev)
+        got = model.generate(prompt, n_gen, logits_out=logits)
+        host = _host(tensors)
+        want, want_logits = OracleDecoder(cfg, host, max_ctx=64, kv="bf16").generate(prompt, n_gen)
+        n_free = 0
+        for i in range(n_gen):
+            if got[i] != want[i]:
+                top2 = np.sort(want_logits[i])[-2:]
+                assert top2[1] - top2[0] < GAP, (i, got[i], want[i], top2)
+                break
+            n_free += 1
+        forced = model.score(prompt + want, N_PROMPT).cpu().numpy()
+        rel = np.array([rel_l2(forced[i], want_logits[i]) for i in range(n_gen)])
+        assert rel[0] < 2e-2 and np.median(rel) < 2e-2 and rel.max() < 5e-2, rel
+        for i in range(n_gen):
+            srt = np.sort(want_logits[i])
+            if srt[-1] - srt[-2] >= GAP:
+                assert int(np.argmax(forced[i])) == want[i], (i, int(np.argmax(forced[i])), want[i])
+        print(f"Qwen3 attention shapes, bf16 KV: free-running match {n_free}/{n_gen}; teacher-forced rel-L2 "
+              f"median {np.median(rel):.1e} max {rel.max():.1e}")
+        assert model.generate_graphed(prompt, n_gen) == got
+    finally:
+        model.close()

@@ -100,9 +100,10 @@ def test_harness_rejects_bad_arguments():
     one = ctypes.c_void_p(16)                      # never dereferenced: the checks come first
     assert L.hoard_hx_gemv(3, one, 8, 512, one, None, one, None) == moe.HOARD_EINVAL          # type
     assert L.hoard_hx_gemv(12, one, 8, 500, one, None, one, None) == moe.HOARD_EINVAL         # K % 256
-    assert L.hoard_hx_rope_store(one, one, one, 4, 4, 127, 0, 1e4, one, one, None) == moe.HOARD_EINVAL
-    assert L.hoard_hx_attention(one, one, one, 6, 4, 128, 5, 0.1, one, None) == moe.HOARD_EINVAL
-    assert L.hoard_hx_attention(one, one, one, 4, 4, 128, 0, 0.1, one, None) == moe.HOARD_EINVAL
+    assert L.hoard_hx_rope_store(one, one, one, 4, 4, 127, 0, 1e4, one, one, 1, None) == moe.HOARD_EINVAL
+    assert L.hoard_hx_rope_store(one, one, one, 4, 4, 128, 0, 1e4, one, one, 0, None) == moe.HOARD_EINVAL  # f32 cache
+    assert L.hoard_hx_attention(one, one, one, 6, 4, 128, 5, 0.1, one, 1, None) == moe.HOARD_EINVAL
+    assert L.hoard_hx_attention(one, one, one, 4, 4, 128, 0, 0.1, one, 30, None) == moe.HOARD_EINVAL
     assert L.hoard_hx_rmsnorm(one, 1, 9000, 1e-6, one, one, None) == moe.HOARD_EINVAL
     assert L.hoard_hx_embed(13, one, 512, 10, one, one, None) == moe.HOARD_EINVAL
     assert L.hoard_hx_argmax(None, 10, one, None) == moe.HOARD_EINVAL
