@@ -188,13 +188,14 @@ int decode_max_tokens();
 int decode_grid();           // CTAs of a persistent launch (one per SM)
 int decode_trace_phases();   // stamps per CTA and layer written when tracing
 bool decode_supported(const Dims& d, const LayerWeights* lws, int n_layers);
-cudaError_t launch_decode_persistent(const Dims& d, const LayerWeights* lws_dev, int n_layers, const Scratch& sc,
-                                     void* x_inout, int T, int32_t* sel_out, float* w_out, cudaStream_t s,
-                                     unsigned long long* trace);
+// KK: expert positions (d.k, plus 1 when the layers have a shared expert); sh_dt: its down type
+cudaError_t launch_decode_persistent(const Dims& d, int KK, int sh_dt, const LayerWeights* lws_dev, int n_layers,
+                                     const Scratch& sc, void* x_inout, int T, int32_t* sel_out, float* w_out,
+                                     cudaStream_t s, unsigned long long* trace);
 
 // The same persistent decode kernel with its scratch in a static device array (no allocation).
-bool decode_static_fits(const Dims& d);
-cudaError_t launch_decode_static(const Dims& d, const LayerWeights* lws_dev, int n_layers, void* x_inout,
-                                 int32_t* sel_out, float* w_out, cudaStream_t s);
+bool decode_static_fits(const Dims& d, int KK);
+cudaError_t launch_decode_static(const Dims& d, int KK, int sh_dt, const LayerWeights* lws_dev, int n_layers,
+                                 void* x_inout, int32_t* sel_out, float* w_out, cudaStream_t s);
 
 }  // namespace hoard

@@ -314,7 +314,8 @@ __device__ __forceinline__ void route_weights(const double* s_lgd, int E, int k,
 }  // namespace
 
 // Shared-memory plan; identical on host (sizing) and device (offsets). Sized for the largest
-// share of any CTA: ceil(k*I/G) gate/up row pairs and ceil(H/G) output rows.
+// share of any CTA: ceil(k*I/G) gate/up row pairs and ceil(H/G) output rows. k counts the expert
+// positions of a token: the routed experts, plus the shared expert where the model has one.
 struct DecodePlan {
     int H, E, k, I, nbH, nbI, dt;
     int np_max, nr_max;
@@ -322,7 +323,7 @@ struct DecodePlan {
     int64_t off_gate_qs, off_gate_hdr, off_up_qs, off_up_hdr;
     int64_t dn_stride;                      // bytes of one expert's down rows (all planes)
     int64_t dn_p0, dn_p1, dn_p2, dn_p3;     // plane offsets inside an expert's down region
-    int64_t off_dn, off_wt, off_wn, off_fxq, off_fxd, off_fxbs32, off_hq, off_hd, off_hbs, off_y, off_xs,
+    int64_t off_dn, off_wt, off_wn, off_gs, off_fxq, off_fxd, off_fxbs32, off_hq, off_hd, off_hbs, off_y, off_xs,
         off_misc, total;
 
     // alias: the down rows go to the start of the gate/up region (issued once the CTA's gate/up rows
@@ -361,6 +362,7 @@ struct DecodePlan {
         }
         off_wt = o; o += a16((int64_t)nr_max * E * 4) + 16;
         off_wn = o; o += a16((int64_t)nr_max * 4) + 32;
+        off_gs = o; o += a16((int64_t)nr_max * 4) + 32;     // the shared expert's gate-input slice
         off_fxq = o; o += (int64_t)nbH * ACT_BLK + 16;
 
         off_fxd = o; o += a16((int64_t)nbH * 4);
@@ -375,10 +377,25 @@ struct DecodePlan {
     }
 };
 
+// plane offsets (qs/ql, hdr/qh, sc, d) inside a position's staged down region for type dt
+__host__ __device__ inline void dn_planes(int dt, int nr_max, int nbI, int64_t* p1, int64_t* p2, int64_t* p3) {
+    const int64_t rq = (int64_t)nbI * 128;
+    if (dt == T_Q4K) {
+        *p1 = a16(nr_max * rq) + 16;
+        *p2 = *p3 = 0;
+    } else {
+        *p1 = a16(nr_max * rq) + 16;
+        *p2 = *p1 + a16(nr_max * (int64_t)nbI * 64) + 16;
+        *p3 = *p2 + a16(nr_max * (int64_t)nbI * 16) + 16;
+    }
+}
+
 struct DecodeArgs {
     const LayerWeights* lw;     // [n_layers] (device)
     int n_layers;
     int H, E, k, I, renorm;
+    int KK;                     // expert positions: k routed, plus the shared expert when KK = k + 1
+    int sh_dt;                  // down type of the shared expert
     float eps;
     int resid_bf16;
     void* x;                    // [H] residual, f32 or bf16, updated in place
@@ -399,25 +416,26 @@ template <typename R, int NV, bool TRACE>
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_sel[16];
-    __shared__ float s_w[16];
+    __shared__ float s_w[16];              // routing weights; position k (the shared expert) its sigmoid gate
     __shared__ int s_ok;
     __shared__ int s_pos_ok[16];           // per expert position: its h blocks were seen ready
     __shared__ int4 s_cd_gu[32];           // gate/up copy descriptors: [NCH chunks][2 segments][4 planes]
-    __shared__ int4 s_cd_dn[2][64];        // down copy descriptors per type (Q4_K, Q6_K): [k][planes]
+    __shared__ int4 s_cd_dn[2][64];        // down copy descriptors per type (Q4_K, Q6_K): [position][planes]
     __shared__ unsigned s_gu_bytes[NCH];
     __shared__ unsigned s_amax[16 * 4];    // per (expert position, 256 block) max|h| of this CTA
-    __shared__ double s_lgd[513];          // router sums of this layer: [E] logits/scale, [E] = sum x^2
+    __shared__ double s_lgd[514];          // router sums: [E] logits/scale, [E] sum x^2, [E+1] shared gate
 
     const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    const int H = a.H, E = a.E, k = a.k, I = a.I;
+    const int H = a.H, E = a.E, k = a.k, I = a.I, KK = a.KK;
     const int nbH = H / QK, nbI = I / QK;
-    const int P_pairs = k * I;
+    const int P_pairs = KK * I;
     const int q0 = (int)((int64_t)c * P_pairs / G), q1 = (int)((int64_t)(c + 1) * P_pairs / G);
     const int np = q1 - q0;
     const int d0 = (int)((int64_t)c * H / G), d1 = (int)((int64_t)(c + 1) * H / G);
     const int nr = d1 - d0;
-    const int racc_stride = RACC_COPIES * (E + 1);
+    const int NA = E + 2;                   // accumulators per copy: logits, sum x^2, shared gate
+    const int racc_stride = RACC_COPIES * NA;
     R* x = reinterpret_cast<R*>(a.x);
     unsigned* hready = a.sync + HREADY_OFF;   // readiness counter of block b of h at hready[HREADY_STRIDE * b]
     bool alive = true;
@@ -436,7 +454,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
     const int ngroups = (np + RPW - 1) / RPW;
 
     DecodePlan P;
-    P.init(H, E, k, I, a.lw[0].down_type, G, a.alias_dn);
+    P.init(H, E, KK, I, a.lw[0].down_type, G, a.alias_dn);
+    int64_t sh_p1 = 0, sh_p2 = 0, sh_p3 = 0;     // the shared position's plane offsets (its own down type)
+    dn_planes(a.sh_dt, P.nr_max, nbI, &sh_p1, &sh_p2, &sh_p3);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.off_misc);
     uint64_t* bar_gu = bars;                // [NCH]
     uint64_t* bar_dn = bars + NCH;
@@ -452,7 +472,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
     const int wn_sub = (int)(((int64_t)d0 * 4) & 15) / 4;
     const int64_t wn_lo = ((int64_t)d0 * 4) & ~(int64_t)15, wn_hi = a16((int64_t)d1 * 4);
     const unsigned wt_bytes = (unsigned)((int64_t)nr * E * 4);
-    // bytes of one layer's down rows [d0, d1) of all k experts, per down type (16-byte supersets)
+    // bytes of one position's down rows [d0, d1), per down type (16-byte supersets)
     unsigned dn_bytes_q4 = 0, dn_bytes_q6 = 0;
     {
         const int64_t nblk_dn = (int64_t)H * nbI;
@@ -460,12 +480,13 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
         const int64_t q6_off[4] = {0, nblk_dn * 128, nblk_dn * 192, nblk_dn * 208};
         const int64_t q6_row[4] = {(int64_t)nbI * 128, (int64_t)nbI * 64, (int64_t)nbI * 16, (int64_t)nbI * 2};
         for (int pl = 0; pl < 2; ++pl)
-            dn_bytes_q4 += (unsigned)(k * (a16(q4_off[pl] + (int64_t)d1 * q4_row[pl]) -
-                                           ((q4_off[pl] + (int64_t)d0 * q4_row[pl]) & ~(int64_t)15)));
+            dn_bytes_q4 += (unsigned)(a16(q4_off[pl] + (int64_t)d1 * q4_row[pl]) -
+                                      ((q4_off[pl] + (int64_t)d0 * q4_row[pl]) & ~(int64_t)15));
         for (int pl = 0; pl < 4; ++pl)
-            dn_bytes_q6 += (unsigned)(k * (a16(q6_off[pl] + (int64_t)d1 * q6_row[pl]) -
-                                           ((q6_off[pl] + (int64_t)d0 * q6_row[pl]) & ~(int64_t)15)));
+            dn_bytes_q6 += (unsigned)(a16(q6_off[pl] + (int64_t)d1 * q6_row[pl]) -
+                                      ((q6_off[pl] + (int64_t)d0 * q6_row[pl]) & ~(int64_t)15));
     }
+    const unsigned dn_bytes_sh = KK > k ? (a.sh_dt == T_Q4K ? dn_bytes_q4 : dn_bytes_q6) : 0u;
 
     // Copy descriptors of this CTA's share, fixed for the whole launch: {src offset lo, hi, smem
     // offset, meta = bytes | j << 20 | chunk << 25 | up << 28 | valid << 29}; gate/up sources are
@@ -479,7 +500,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
             if (pa < pb) {
                 const int j = (q0 + pa) / I + sg;
                 const int qa = max(q0 + pa, j * I), qe = min(q0 + pb, (j + 1) * I);
-                if (qa < qe && j < k) {
+                if (qa < qe && j < KK) {
                     const int i = qa - j * I, n = qe - qa;
                     const int64_t pp = qa - q0;
                     const int64_t nblk_gu = (int64_t)I * nbH;
@@ -501,9 +522,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
         const int64_t nblk_dn = (int64_t)H * nbI;
         for (int tsel = 0; tsel < 2; ++tsel) {
             DecodePlan Pt;
-            Pt.init(H, E, k, I, tsel == 0 ? T_Q4K : T_Q6K, G, a.alias_dn);
+            Pt.init(H, E, KK, I, tsel == 0 ? T_Q4K : T_Q6K, G, a.alias_dn);
             const int nplanes = tsel == 0 ? 2 : 4;
-            for (int ci = lane; ci < k * nplanes; ci += 32) {
+            for (int ci = lane; ci < KK * nplanes; ci += 32) {
                 const int j = ci / nplanes, pl = ci - j * nplanes;
                 int64_t off, row, dst;
                 if (pl == 0) { off = 0; row = (int64_t)nbI * 128; dst = Pt.dn_p0; }
@@ -541,25 +562,31 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
         Sprev = t > 0.0 ? sqrt(t) : 1.0;
     }
     if (tid == 0) {
-        mbar_expect_tx(bar_wt, wt_bytes + (unsigned)(wn_hi - wn_lo));
+        mbar_expect_tx(bar_wt, wt_bytes + (unsigned)(wn_hi - wn_lo) * (KK > k ? 2u : 1u));
         bulk_g2s(wt, a.lw[0].w_router_t + (int64_t)d0 * E, wt_bytes, bar_wt);
         bulk_g2s(smem + P.off_wn, reinterpret_cast<const uint8_t*>(a.lw[0].w_norm) + wn_lo, (unsigned)(wn_hi - wn_lo),
                  bar_wt);
+        if (KK > k)
+            bulk_g2s(smem + P.off_gs, reinterpret_cast<const uint8_t*>(a.lw[0].sh_gate_inp) + wn_lo,
+                     (unsigned)(wn_hi - wn_lo), bar_wt);
     }
     if (!mbar_wait(bar_wt, ph_wt)) { atomicOr(&a.sync[0], 2u); alive = false; }
     ph_wt ^= 1;
     __syncthreads();
     {
         const float* wn = reinterpret_cast<const float*>(smem + P.off_wn) + wn_sub;
-        long long* acc = a.racc + (int64_t)(c % RACC_COPIES) * (E + 1);
-        for (int e = tid; e <= E; e += blockDim.x) {
+        const float* gs = reinterpret_cast<const float*>(smem + P.off_gs) + wn_sub;
+        long long* acc = a.racc + (int64_t)(c % RACC_COPIES) * NA;
+        for (int e = tid; e < NA; e += blockDim.x) {
             double s = 0.0;
             if (e < E) {
                 for (int r = 0; r < nr; ++r) s += (double)wt[r * E + e] * (double)(wn[r] * xs[r]);
-            } else {
+            } else if (e == E) {
                 for (int r = 0; r < nr; ++r) s += (double)(xs[r] * xs[r]);
+            } else if (KK > k) {
+                for (int r = 0; r < nr; ++r) s += (double)gs[r] * (double)(wn[r] * xs[r]);
             }
-            if (alive) add_fixed(&acc[e], s, e < E ? RFIX / Sprev : RFIX / (Sprev * Sprev), a.sync);
+            if (alive && (e <= E || KK > k)) add_fixed(&acc[e], s, e == E ? RFIX / (Sprev * Sprev) : RFIX / Sprev, a.sync);
         }
     }
     if (!grid_barrier(a.sync, nbar++, &s_ok)) alive = false;
@@ -571,25 +598,36 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
         const int64_t L_stride = a.lw[l].slot_stride, L_off_up = a.lw[l].off_up, L_off_down = a.lw[l].off_down;
         const int L_dt = a.lw[l].down_type;
         const float* L_wnorm = a.lw[l].w_norm;
+        const uint8_t* L_sh = a.lw[l].shared;
+        const int64_t L_sh_up = a.lw[l].sh_off_up, L_sh_down = a.lw[l].sh_off_down;
         const bool has_next = l + 1 < a.n_layers;
         const float* Ln_wrt = has_next ? a.lw[l + 1].w_router_t : nullptr;
         const float* Ln_wnorm = has_next ? a.lw[l + 1].w_norm : nullptr;
-        P.init(H, E, k, I, L_dt, G, a.alias_dn);
+        const float* Ln_gs = has_next && KK > k ? a.lw[l + 1].sh_gate_inp : nullptr;
+        P.init(H, E, KK, I, L_dt, G, a.alias_dn);
         DEC_TR(l, 0);
         // ---- A/B. warp 0: router sums -> softmax -> top-k -> copies -> renorm, all in registers;
         //      warps 1..: fx = rms_norm(x) * ffn_norm -> Q8_K (named barriers, no CTA-wide sync) ------
         const bool issued = alive;
         const bool issued_wt = alive && has_next;
-        auto issue_down = [&]() {                       // warp 0: this CTA's down rows of every selected expert
+        auto issue_down = [&]() {                       // warp 0: this CTA's down rows of every expert position
             const int tsel = L_dt == T_Q4K ? 0 : 1;
-            const int n_dn = k * (L_dt == T_Q4K ? 2 : 4);
-            for (int ci = lane; ci < n_dn; ci += 32) {
+            const int np_l = L_dt == T_Q4K ? 2 : 4;
+            for (int ci = lane; ci < k * np_l; ci += 32) {
                 const int4 d = s_cd_dn[tsel][ci];
                 const unsigned meta = (unsigned)d.w;
                 const int j = (meta >> 20) & 31;
                 const int64_t src = ((int64_t)(unsigned)d.y << 32) | (unsigned)d.x;
                 bulk_g2s(smem + d.z, L_pool + (int64_t)s_sel[j] * L_stride + L_off_down + src, meta & 0xFFFFFu,
                          bar_dn);
+            }
+            if (KK > k) {                                // the shared expert: position k, its own down type
+                const int ts = a.sh_dt == T_Q4K ? 0 : 1, np_s = a.sh_dt == T_Q4K ? 2 : 4;
+                if (lane < np_s) {
+                    const int4 d = s_cd_dn[ts][k * np_s + lane];
+                    const int64_t src = ((int64_t)(unsigned)d.y << 32) | (unsigned)d.x;
+                    bulk_g2s(smem + d.z, L_sh + L_sh_down + src, (unsigned)d.w & 0xFFFFFu, bar_dn);
+                }
             }
         };
         int8_t* fxq = reinterpret_cast<int8_t*>(smem + P.off_fxq);
@@ -600,20 +638,20 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
             if (lane < NCH) {
                 mbar_expect_tx(bar_gu + lane, s_gu_bytes[lane]);
             } else if (lane == NCH) {
-                mbar_expect_tx(bar_dn, L_dt == T_Q4K ? dn_bytes_q4 : dn_bytes_q6);
+                mbar_expect_tx(bar_dn, (unsigned)k * (L_dt == T_Q4K ? dn_bytes_q4 : dn_bytes_q6) + dn_bytes_sh);
             } else if (lane == NCH + 1 && has_next) {
-                mbar_expect_tx(bar_wt, wt_bytes + (unsigned)(wn_hi - wn_lo));
+                mbar_expect_tx(bar_wt, wt_bytes + (unsigned)(wn_hi - wn_lo) * (KK > k ? 2u : 1u));
             }
         }
         // router sums: every thread t <= E adds the RACC_COPIES partial copies of entry t (one L2 round trip)
         {
             const long long* racc = a.racc + (int64_t)buf * racc_stride;
             const double un1 = Sprev / RFIX, un2 = Sprev * Sprev / RFIX;
-            for (int e = tid; e <= E; e += blockDim.x) {
+            for (int e = tid; e < NA; e += blockDim.x) {
                 long long v = 0;
 #pragma unroll
-                for (int cp = 0; cp < RACC_COPIES; ++cp) v += __ldcg(racc + cp * (E + 1) + e);
-                s_lgd[e] = (double)v * (e < E ? un1 : un2);
+                for (int cp = 0; cp < RACC_COPIES; ++cp) v += __ldcg(racc + cp * NA + e);
+                s_lgd[e] = (double)v * (e == E ? un2 : un1);
             }
         }
         __syncthreads();
@@ -633,7 +671,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
                 if (meta >> 29) {
                     const int j = (meta >> 20) & 31, ch = (meta >> 25) & 7;
                     const int64_t src = ((int64_t)(unsigned)d.y << 32) | (unsigned)d.x;
-                    const uint8_t* base = L_pool + (int64_t)s_sel[j] * L_stride + (((meta >> 28) & 1) ? L_off_up : 0);
+                    const bool upm = (meta >> 28) & 1;
+                    const uint8_t* base = j < k ? L_pool + (int64_t)s_sel[j] * L_stride + (upm ? L_off_up : 0)
+                                                : L_sh + (upm ? L_sh_up : 0);
                     bulk_g2s(smem + d.z, base + src, meta & 0xFFFFFu, bar_gu + ch);
                 }
             }
@@ -642,6 +682,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
                 int32_t* so = (c == 0 && a.sel_out) ? a.sel_out + (int64_t)l * k : nullptr;
                 float* wo = (c == 0 && a.sel_out) ? a.w_out + (int64_t)l * k : nullptr;
                 route_weights<NV>(s_lgd, E, k, a.renorm, scale, lane, my_logit, s_sel, s_w, so, wo);
+                // the shared expert's weight: sigmoid of its gate logit (src/run_qwen35.cpp:659-666)
+                if (KK > k && lane == 0) s_w[k] = sigmoid_f((float)((double)scale * s_lgd[E + 1]));
             }
             DEC_TR(l, 3);
             if (alive) {
@@ -656,6 +698,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
                 if (has_next && lane == 1)
                     bulk_g2s(smem + P.off_wn, reinterpret_cast<const uint8_t*>(Ln_wnorm) + wn_lo,
                              (unsigned)(wn_hi - wn_lo), bar_wt);
+                if (Ln_gs && lane == 2)
+                    bulk_g2s(smem + P.off_gs, reinterpret_cast<const uint8_t*>(Ln_gs) + wn_lo, (unsigned)(wn_hi - wn_lo),
+                             bar_wt);
             }
             DEC_TR(l, 4);
             DEC_TR(l, 5);
@@ -703,7 +748,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
             named_sync(1, blockDim.x - 32);         // among warps 1..
         }
         // ---- C. gate/up + SwiGLU: lane = (row slot, 256-weight block) -----------------------------
-        unsigned* amax = a.amax + (int64_t)buf * k * nbI;
+        unsigned* amax = a.amax + (int64_t)buf * KK * nbI;
         {
             const int rs = lane / LPR, b = lane % LPR;
             const int8_t* act = fxq + ACT_BLK * b;
@@ -764,7 +809,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
         // publish this CTA's block maxima of h (a few atomics per CTA instead of one per row), then
         // count this CTA in the readiness counter of every 256-value block of h it produced to
         __syncthreads();
-        if (tid < k * nbI) {
+        if (tid < KK * nbI) {
             const unsigned v = s_amax[tid];
             if (v) atomicMax(&amax[tid], v);
             s_amax[tid] = 0u;
@@ -788,9 +833,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
         int* hbs = reinterpret_cast<int*>(smem + P.off_hbs);
         {
             float* y = reinterpret_cast<float*>(smem + P.off_y);
-            const int wpe = nw / k;
+            const int wpe = nw / KK;
             const int j = warp / wpe, wi = warp - j * wpe;
-            if (j < k) {
+            // the position's down type and plane offsets (the shared expert, position k, has its own)
+            const int dtj = j < k ? L_dt : a.sh_dt;
+            const int64_t pj1 = j < k ? P.dn_p1 : sh_p1, pj2 = j < k ? P.dn_p2 : sh_p2, pj3 = j < k ? P.dn_p3 : sh_p3;
+            if (j < KK) {
                 bool ok = alive;
                 if (wi == 0 && lane < nbI && ok) {
                     // the CTAs owning pairs p0 and p0 + 255 of block (j, lane), and all between
@@ -836,7 +884,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
                     }
                     const int pair = bsum + __shfl_xor_sync(0xffffffffu, bsum, 1);
                     if (okg) {
-                        if (L_dt == T_Q6K) {
+                        if (dtj == T_Q6K) {
                             // 16-sums in unit order [unit v = 2*h2 + r][a]: group gl = 8*h2 + 2*a + r
                             const int h2 = gl >> 3, aa = (gl >> 1) & 3, rr = gl & 1;
                             hbs[(j * nbI + blk) * 16 + 4 * (2 * h2 + rr) + aa] = bsum;
@@ -854,7 +902,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
                 // same activation blocks (shared-memory broadcasts) and rotate their chunk order by
                 // lane so that one load instruction spreads over the banks. Block sums of a row are
                 // added as (b0 + b1) + (b2 + b3).
-                const int dsub = L_dt == T_Q6K ? (int)(((int64_t)d0 * nbI * 2) & 15) : 0;
+                const int dsub = dtj == T_Q6K ? (int)(((int64_t)d0 * nbI * 2) & 15) : 0;
                 const int ipw = 32 / nbI, ui = lane / nbI, bl = lane - ui * nbI;
                 const int rot = lane & 7;
                 for (int gi = wi; gi * ipw < nr; gi += wpe) {
@@ -866,21 +914,21 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
                         const int64_t blk = (int64_t)r * nbI + bl;
                         const int8_t* act = hq + j * hq_stride(nbI) + ACT_BLK * bl;
                         const float d8 = hd[j * nbI + bl];
-                        if (L_dt == T_Q6K) {
-                            const uint4 S = lds128(reg + P.dn_p2 + blk * 16);
+                        if (dtj == T_Q6K) {
+                            const uint4 S = lds128(reg + pj2 + blk * 16);
                             const float d6 = __half2float(__ushort_as_half(
-                                *reinterpret_cast<const unsigned short*>(reg + P.dn_p3 + dsub + blk * 2)));
+                                *reinterpret_cast<const unsigned short*>(reg + pj3 + dsub + blk * 2)));
                             const int* bsu = hbs + (j * nbI + bl) * 16;
                             const int sw = rot >> 2;       // half the lanes load the two ql chunks swapped
                             int isum = 0;
 #pragma unroll
                             for (int vv = 0; vv < 4; ++vv) {
                                 const int v = (vv + rot) & 3, h2 = v >> 1, rr = v & 1;
-                                const uint8_t* ql = reg + P.dn_p0 + blk * 128 + 64 * h2 + 16 * rr;
+                                const uint8_t* ql = reg + blk * 128 + 64 * h2 + 16 * rr;
                                 const uint4 P0 = lds128(ql + 32 * sw);
                                 const uint4 P1 = lds128(ql + 32 * (sw ^ 1));
                                 const uint4 A = sw ? P1 : P0, B = sw ? P0 : P1;
-                                const uint4 C = lds128(reg + P.dn_p1 + blk * 64 + 32 * h2 + 16 * rr);
+                                const uint4 C = lds128(reg + pj1 + blk * 64 + 32 * h2 + 16 * rr);
                                 const int8_t* a0 = act + 128 * h2 + 16 * rr;
                                 const int4 x0 = lds128i(a0), x1 = lds128i(a0 + 32), x2 = lds128i(a0 + 64),
                                            x3 = lds128i(a0 + 96);
@@ -906,8 +954,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
                             }
                             acc = d8 * d6 * (float)isum;
                         } else {
-                            const uint8_t* wq = reg + P.dn_p0 + blk * 128;
-                            const uint4 hh4 = lds128(reg + P.dn_p1 + blk * 16);
+                            const uint8_t* wq = reg + blk * 128;
+                            const uint4 hh4 = lds128(reg + pj1 + blk * 16);
                             const Q4Scales s4 = q4_scales(hh4);
                             int isc = 0;
 #pragma unroll
@@ -931,7 +979,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
                     if (nbI == 2) sum = acc + t1;
                     else if (nbI == 3) sum = (acc + t1) + t2;
                     else if (nbI == 4) sum = (acc + t1) + (t2 + t3);
-                    if (valid && bl == 0) y[r * k + j] = sum;
+                    if (valid && bl == 0) y[r * KK + j] = sum;
                 }
                 if (!ok) alive = false;
             }
@@ -944,14 +992,15 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
         if (c == 0 && alive) {
             long long* rz = a.racc + (int64_t)buf * racc_stride;
             for (int e = tid; e < racc_stride; e += blockDim.x) rz[e] = 0;
-            unsigned* az = a.amax + (int64_t)(buf ^ 1) * k * nbI;
-            for (int e = tid; e < k * nbI; e += blockDim.x) az[e] = 0u;
+            unsigned* az = a.amax + (int64_t)(buf ^ 1) * KK * nbI;
+            for (int e = tid; e < KK * nbI; e += blockDim.x) az[e] = 0u;
         }
         {
             const float* y = reinterpret_cast<const float*>(smem + P.off_y);
             for (int r = tid; r < nr; r += blockDim.x) {
                 float acc = 0.f;
-                for (int j = 0; j < k; ++j) acc += s_w[j] * y[r * k + j];
+                for (int j = 0; j < k; ++j) acc += s_w[j] * y[r * KK + j];
+                if (KK > k) acc = acc + y[r * KK + k] * s_w[k];      // shared expert, added after its gate
                 const R xn = from_f32<R>(acc + xs[r]);
                 if (alive) x[d0 + r] = xn;
                 xs[r] = to_f32<R>(xn);
@@ -964,15 +1013,19 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
             __syncthreads();
             DEC_TR(l, 15);
             const float* wn = reinterpret_cast<const float*>(smem + P.off_wn) + wn_sub;
-            long long* acc = a.racc + (int64_t)(buf ^ 1) * racc_stride + (int64_t)(c % RACC_COPIES) * (E + 1);
-            for (int e = tid; e <= E; e += blockDim.x) {
+            const float* gs = reinterpret_cast<const float*>(smem + P.off_gs) + wn_sub;
+            long long* acc = a.racc + (int64_t)(buf ^ 1) * racc_stride + (int64_t)(c % RACC_COPIES) * NA;
+            for (int e = tid; e < NA; e += blockDim.x) {
                 double s = 0.0;
                 if (e < E) {
                     for (int r = 0; r < nr; ++r) s += (double)wt[r * E + e] * (double)(wn[r] * xs[r]);
-                } else {
+                } else if (e == E) {
                     for (int r = 0; r < nr; ++r) s += (double)(xs[r] * xs[r]);
+                } else if (KK > k) {
+                    for (int r = 0; r < nr; ++r) s += (double)gs[r] * (double)(wn[r] * xs[r]);
                 }
-                if (alive) add_fixed(&acc[e], s, e < E ? RFIX / Scur : RFIX / (Scur * Scur), a.sync);
+                if (alive && (e <= E || KK > k))
+                    add_fixed(&acc[e], s, e == E ? RFIX / (Scur * Scur) : RFIX / Scur, a.sync);
             }
             DEC_TR(l, 12);
             if (!grid_barrier(a.sync, nbar++, &s_ok, DEC_TRP(l, 16))) alive = false;
@@ -989,9 +1042,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeArgs a) {
         const unsigned old = atomicAdd(&a.sync[2], 1u);
         if (old == (unsigned)G - 1) {
             __threadfence();
-            unsigned* az = a.amax + (int64_t)((a.n_layers - 1) & 1) * k * nbI;
-            for (int e = 0; e < k * nbI; ++e) az[e] = 0u;
-            for (int e = 0; e < k * nbI; ++e) hready[HREADY_STRIDE * e] = 0u;
+            unsigned* az = a.amax + (int64_t)((a.n_layers - 1) & 1) * KK * nbI;
+            for (int e = 0; e < KK * nbI; ++e) az[e] = 0u;
+            for (int e = 0; e < KK * nbI; ++e) hready[HREADY_STRIDE * e] = 0u;
             if (ld_relaxed(&a.sync[0]) & 6u)      // an aborted launch may leave partial sums behind
                 for (int e = 0; e < 2 * racc_stride; ++e) a.racc[e] = 0;
             a.sync[1] = 0u;
@@ -1012,7 +1065,7 @@ int decode_trace_phases() { return DEC_TRACE_PHASES; }
 
 // 0: both shares fit in shared memory, 1: only with the down rows over the gate/up rows, -1: neither
 static const void* decode_fn(bool bf16, int nv, bool trace);
-static int decode_alias_mode(const Dims& d, int G) {
+static int decode_alias_mode(const Dims& d, int KK, int G) {
     int dev = 0, max_smem = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
@@ -1022,7 +1075,7 @@ static int decode_alias_mode(const Dims& d, int G) {
         int64_t need = 0;
         for (int dt : {(int)T_Q4K, (int)T_Q6K}) {
             DecodePlan P;
-            P.init(d.H, d.E, d.k, d.I, dt, G, alias);
+            P.init(d.H, d.E, KK, d.I, dt, G, alias);
             need = need > P.total ? need : P.total;
         }
         if (need + (int64_t)fa.sharedSizeBytes <= max_smem) return alias;
@@ -1031,20 +1084,25 @@ static int decode_alias_mode(const Dims& d, int G) {
 }
 
 bool decode_supported(const Dims& d, const LayerWeights* lws, int n_layers) {
-    if (d.k > 16 || d.E % 4 != 0 || d.E > 512) return false;
+    if (n_layers <= 0) return false;
+    const int KK = d.k + (lws[0].shared ? 1 : 0);            // expert positions: routed + shared
+    if (KK > 16 || d.E % 4 != 0 || d.E > 512) return false;
     const int nbH = d.H / QK, nbI = d.I / QK;
     if (nbH > 32 || (nbH & (nbH - 1)) != 0) return false;    // lanes per gate/up row: a power of two <= 32
     if (nbI > 4) return false;                                // down rows: one lane per block, 4 lanes per item
     const int G = decode_grid();
-    if ((int64_t)d.k * d.I < G || d.H < G) return false;     // every CTA must own rows
-    if ((d.k * d.I + G - 1) / G > d.I) return false;          // a CTA's pairs span at most 2 experts
+    if ((int64_t)KK * d.I < G || d.H < G) return false;      // every CTA must own rows
+    if ((KK * d.I + G - 1) / G > d.I) return false;           // a CTA's pairs span at most 2 experts
     for (int l = 0; l < n_layers; ++l) {
         const LayerWeights& L = lws[l];
         if (L.gate_type != T_Q4K || L.up_type != T_Q4K) return false;
         if (L.down_type != T_Q4K && L.down_type != T_Q6K) return false;
-        if (L.shared) return false;
+        if ((L.shared != nullptr) != (KK > d.k)) return false;
+        if (L.shared && (L.sh_gate_type != T_Q4K || L.sh_up_type != T_Q4K || L.sh_down_type != lws[0].sh_down_type ||
+                         (L.sh_down_type != T_Q4K && L.sh_down_type != T_Q6K) || !L.sh_gate_inp))
+            return false;
     }
-    return decode_alias_mode(d, G) >= 0;
+    return decode_alias_mode(d, KK, G) >= 0;
 }
 
 template <typename R, bool TRACE>
@@ -1058,20 +1116,22 @@ static const void* decode_fn(bool bf16, int nv, bool trace) {
     return trace ? decode_fn_nv<float, true>(nv) : decode_fn_nv<float, false>(nv);
 }
 
-cudaError_t launch_decode_persistent(const Dims& d, const LayerWeights* lws_dev, int n_layers, const Scratch& sc,
-                                     void* x_inout, int T, int32_t* sel_out, float* w_out, cudaStream_t s,
-                                     unsigned long long* trace) {
+cudaError_t launch_decode_persistent(const Dims& d, int KK, int sh_dt, const LayerWeights* lws_dev, int n_layers,
+                                     const Scratch& sc, void* x_inout, int T, int32_t* sel_out, float* w_out,
+                                     cudaStream_t s, unsigned long long* trace) {
     if (T != 1) return cudaErrorInvalidValue;
     const int G = decode_grid();
-    const int alias = decode_alias_mode(d, G);
+    const int alias = decode_alias_mode(d, KK, G);
     if (alias < 0) return cudaErrorInvalidValue;
     int64_t smem = 0;
     for (int dt : {(int)T_Q4K, (int)T_Q6K}) {
         DecodePlan P;
-        P.init(d.H, d.E, d.k, d.I, dt, G, alias);
+        P.init(d.H, d.E, KK, d.I, dt, G, alias);
         smem = smem > P.total ? smem : P.total;
     }
     DecodeArgs a;
+    a.KK = KK;
+    a.sh_dt = sh_dt;
     a.lw = lws_dev;
     a.n_layers = n_layers;
     a.H = d.H; a.E = d.E; a.k = d.k; a.I = d.I; a.renorm = d.renorm; a.eps = d.eps; a.resid_bf16 = d.resid_bf16;
@@ -1101,12 +1161,12 @@ cudaError_t launch_decode_persistent(const Dims& d, const LayerWeights* lws_dev,
 // persistent decode kernel can take its scratch (h, the block maxima of h, the router accumulators and
 // the grid-barrier words) from this fixed file-scope device array instead of a context's scratch.
 // Every GPU that loads this library holds the array until the process exits.
-constexpr int NOALLOC_MAX_K = 16;       // experts per token
+constexpr int NOALLOC_MAX_K = 16;       // expert positions per token (routed + shared)
 constexpr int NOALLOC_MAX_I = 1024;     // expert intermediate size
 constexpr int NOALLOC_MAX_E = 512;      // experts per layer
 constexpr size_t NOALLOC_H_BYTES = (size_t)NOALLOC_MAX_K * NOALLOC_MAX_I * 4;                  // 64 KiB
 constexpr size_t NOALLOC_AMAX_BYTES = 2 * NOALLOC_MAX_K * (NOALLOC_MAX_I / QK) * 4;           // 512 B
-constexpr size_t NOALLOC_RACC_BYTES = (size_t)2 * RACC_COPIES * (NOALLOC_MAX_E + 1) * 8;       // 32,832 B
+constexpr size_t NOALLOC_RACC_BYTES = (size_t)2 * RACC_COPIES * (NOALLOC_MAX_E + 2) * 8;       // 32,896 B
 constexpr size_t NOALLOC_SYNC_BYTES = 8704;          // error word, barrier words, h block counters (one line each)
 constexpr size_t NOALLOC_ZERO_BYTES = NOALLOC_AMAX_BYTES + NOALLOC_RACC_BYTES + NOALLOC_SYNC_BYTES;
 constexpr size_t NOALLOC_BYTES = NOALLOC_H_BYTES + NOALLOC_ZERO_BYTES;                         // ~105 KiB
@@ -1133,13 +1193,13 @@ static cudaError_t decode_scratch_address(void** out) {
     return cudaSuccess;
 }
 
-bool decode_static_fits(const Dims& d) {
-    return d.k <= NOALLOC_MAX_K && d.I <= NOALLOC_MAX_I && d.E <= NOALLOC_MAX_E;
+bool decode_static_fits(const Dims& d, int KK) {
+    return KK <= NOALLOC_MAX_K && d.I <= NOALLOC_MAX_I && d.E <= NOALLOC_MAX_E;
 }
 
-cudaError_t launch_decode_static(const Dims& d, const LayerWeights* lws_dev, int n_layers, void* x_inout,
-                                 int32_t* sel_out, float* w_out, cudaStream_t s) {
-    if (!decode_static_fits(d)) return cudaErrorInvalidValue;
+cudaError_t launch_decode_static(const Dims& d, int KK, int sh_dt, const LayerWeights* lws_dev, int n_layers,
+                                 void* x_inout, int32_t* sel_out, float* w_out, cudaStream_t s) {
+    if (!decode_static_fits(d, KK)) return cudaErrorInvalidValue;
     void* base = nullptr;
     cudaError_t e = decode_scratch_address(&base);
     if (e != cudaSuccess) return e;
@@ -1153,7 +1213,7 @@ cudaError_t launch_decode_static(const Dims& d, const LayerWeights* lws_dev, int
     // (block maxima, router accumulators, barrier counters, error word); h needs no clearing
     e = cudaMemsetAsync(b + NOALLOC_H_BYTES, 0, NOALLOC_ZERO_BYTES, s);
     if (e != cudaSuccess) return e;
-    return launch_decode_persistent(d, lws_dev, n_layers, sc, x_inout, 1, sel_out, w_out, s, nullptr);
+    return launch_decode_persistent(d, KK, sh_dt, lws_dev, n_layers, sc, x_inout, 1, sel_out, w_out, s, nullptr);
 }
 
 }  // namespace hoard

@@ -143,7 +143,7 @@ LayerWeights layer_weights(const hoard_moe_ctx* c, int layer) {
     lw.gate_type = L.gt;
     lw.up_type = L.ut;
     lw.down_type = L.dt;
-    if (c->desc.n_ff_shexp > 0 && L.shared_set) {
+    if (c->desc.n_ff_shexp > 0) {   // compute paths run only after check_ready saw it uploaded
         lw.shared = L.shared;
         lw.sh_off_up = L.sh_off_up;
         lw.sh_off_down = L.sh_off_down;
@@ -163,6 +163,9 @@ int check_layer(hoard_moe_ctx* c, int layer) {
     if (layer < 0 || layer >= c->desc.n_layer) return fail(c, HOARD_EINVAL, "layer out of range");
     return HOARD_OK;
 }
+
+// expert positions of a token in the persistent decode kernel: the routed experts, plus the shared one
+int decode_kk(const hoard_moe_ctx* c) { return c->dims.k + (c->desc.n_ff_shexp > 0 ? 1 : 0); }
 
 int check_ready(hoard_moe_ctx* c, int layer) {
     const LayerStore& L = c->layers[layer];
@@ -611,8 +614,8 @@ int hoard_moe_layers(hoard_moe_ctx* c, int layer0, int n_layers, void* x_inout, 
     if (T == 1 && c->decode_impl == 1 && c->decode_ok) {
         unsigned long long* tr = nullptr;
         if (c->trace && (int64_t)decode_grid() * n_layers * decode_trace_phases() <= c->trace_cap) tr = c->trace;
-        HCHECK(c, launch_decode_persistent(c->dims, c->lw_dev + layer0, n_layers, c->sc, x_inout, T, sel_out, w_out,
-                                           (cudaStream_t)stream, tr));
+        HCHECK(c, launch_decode_persistent(c->dims, decode_kk(c), c->desc.shexp_down_type, c->lw_dev + layer0, n_layers,
+                                           c->sc, x_inout, T, sel_out, w_out, (cudaStream_t)stream, tr));
         ++c->launches;
         return HOARD_OK;
     }
@@ -640,7 +643,7 @@ int hoard_moe_decode_noalloc(hoard_moe_ctx* c, int layer0, int n_layers, void* x
         return fail(c, HOARD_EINVAL, "layer range out of bounds");
     if (!x_inout) return fail(c, HOARD_EINVAL, "null x");
     if ((sel_out == nullptr) != (w_out == nullptr)) return fail(c, HOARD_EINVAL, "sel_out and w_out go together");
-    if (!decode_static_fits(c->dims))
+    if (!decode_static_fits(c->dims, decode_kk(c)))
         return fail(c, HOARD_EINVAL, "shape exceeds the static decode scratch (needs n_expert_used <= 16, "
                                      "n_ff <= 1024, n_expert <= 512)");
     if (!c->decode_ok || c->desc.n_slots < c->dims.E)
@@ -650,8 +653,8 @@ int hoard_moe_decode_noalloc(hoard_moe_ctx* c, int layer0, int n_layers, void* x
         if (rc) return rc;
     }
     HCHECK(c, cudaSetDevice(c->desc.device));
-    HCHECK(c, launch_decode_static(c->dims, c->lw_dev + layer0, n_layers, x_inout, sel_out, w_out,
-                                   (cudaStream_t)stream));
+    HCHECK(c, launch_decode_static(c->dims, decode_kk(c), c->desc.shexp_down_type, c->lw_dev + layer0, n_layers,
+                                   x_inout, sel_out, w_out, (cudaStream_t)stream));
     ++c->launches;
     return HOARD_OK;
 }

@@ -259,3 +259,79 @@ def test_c1_greedy_decode_64_tokens_vs_oracle():
         assert np.median(rel_r) < 2e-2 and rel_r.max() < 5e-2
     finally:
         model.close()
+
+
+def _shared_stack(spec, n_layer, max_tokens, seed):
+    Ls = [make_layer(LayerSpec(H=spec.H, E=spec.E, k=spec.k, I=spec.I, shared=True,
+                               types=(Q4_K, Q4_K, Q6_K if l % 2 == 0 else Q4_K)), seed=seed + l, device=f"cuda:{DEV}")
+          for l in range(n_layer)]
+    ctx = moe.MoEContext(n_embd=spec.H, n_expert=spec.E, n_expert_used=spec.k, n_ff=spec.I, n_layer=n_layer,
+                         norm_topk=True, eps=spec.eps, resid_dtype=torch.float32, gate_types=[Q4_K] * n_layer,
+                         up_types=[Q4_K] * n_layer, down_types=[L.spec.types[2] for L in Ls], n_ff_shexp=spec.I,
+                         shexp_types=spec.sh_types, max_tokens=max_tokens, device=DEV)
+    for l, L in enumerate(Ls):
+        load_context(ctx, l, L)
+    return Ls, ctx
+
+
+@pytest.mark.parametrize("E,k,I", [(64, 8, 768), (512, 10, 512)])
+def test_decode_with_shared_expert(E, k, I):
+    """T = 1 with a gated shared expert (src/run_qwen35.cpp:659-676) through the persistent decode kernel
+    (one launch for the stack) against the grouped kernels and a chain of oracle layers; (512, 10, 512)
+    is the Qwen3-Next-80B-A3B MoE shape (E 512, top-10, I 512, shared expert I 512)."""
+    spec = LayerSpec(H=H, E=E, k=k, I=I, shared=True)
+    Ls, ctx = _shared_stack(spec, 2, 4, seed=6100 + E)
+    try:
+        x0 = make_x(1, H, seed=61)
+        outs = {}
+        for impl in (1, 0):
+            ctx.set_decode_impl(impl)
+            x = torch.from_numpy(x0.copy()).cuda(DEV)
+            sel = torch.empty(2, 1, k, dtype=torch.int32, device=x.device)
+            w = torch.empty(2, 1, k, device=x.device)
+            n0 = ctx.launch_count
+            ctx.layers(0, 2, x, sel, w)
+            ctx.sync_status()
+            if impl == 1:
+                assert ctx.launch_count - n0 == 1                  # the persistent kernel ran the stack
+            outs[impl] = (x.cpu().numpy(), sel.cpu().numpy(), w.cpu().numpy())
+        assert np.array_equal(outs[0][1], outs[1][1])
+        assert np.allclose(outs[0][2], outs[1][2], rtol=1e-5, atol=1e-7)
+        assert rel_l2(outs[1][0] - x0, outs[0][0] - x0) < 1e-3
+        ref = x0
+        for l, L in enumerate(Ls):
+            ref_l, ref_sel, _, _, probs = oracle_layer(L, ref, orc.MODE_GGML)
+            if not near_tie_mask(probs, ref_sel, k)[0]:
+                assert np.array_equal(np.sort(ref_sel, 1), np.sort(outs[1][1][l], 1))
+            ref = ref_l
+        err = rel_l2(outs[1][0] - x0, ref - x0)
+        print(f"E={E} k={k} I={I} + shared expert, decode kernel vs oracle: rel-L2 {err:.1e}")
+        assert err < 1e-3
+    finally:
+        ctx.close()
+
+
+def test_tc_path_c5_shape():
+    """Batched tokens at the Qwen3-Next MoE shape (E 512, top-10, I 512, shared expert) on the tensor-core
+    path against the oracle, tensor-core tolerances."""
+    spec = LayerSpec(H=H, E=512, k=10, I=512, shared=True)
+    Ls, ctx = _shared_stack(spec, 1, 512, seed=6300)
+    try:
+        ctx.set_gemm_min_tokens(64)
+        T = 512
+        x = make_x(T, H, seed=63)
+        xd = torch.from_numpy(x).cuda(DEV)
+        ctx.layer(0, xd)
+        ctx.sync_status()
+        out = xd.cpu().numpy()
+        rows = np.sort(np.random.default_rng(5).choice(T, 128, replace=False))
+        xs = x[rows]
+        ref_out, ref_sel, _, _, probs = oracle_layer(Ls[0], xs, orc.MODE_GGML)
+        ok = ~near_tie_mask(probs, ref_sel, 10)
+        d, r = out[rows][ok] - xs[ok], ref_out[ok] - xs[ok]
+        err = rel_l2(d, r)
+        per_tok = max(rel_l2(d[i], r[i]) for i in range(d.shape[0]))
+        print(f"C5 shape, T={T}, tensor-core path: rel-L2 vs ggml mode {err:.1e} (max token {per_tok:.1e})")
+        assert err < 1e-2 and per_tok < 3e-2
+    finally:
+        ctx.close()
