@@ -244,6 +244,7 @@ def run_reference(args, rank, world):
 
 
 PREFILL_T = 4096          # tokens per call of the prefill measurement (the C2 sweep's largest T)
+C4_TOKENS = 64 * 2048     # C4: 64 sequences x 2048 tokens per prefill step, split over the ranks
 C2_TS = (16, 512, 4096)   # isolated-layer sweep (C2: T in {1, 16, 512, 4096}; T = 1 is the decode line)
 
 
@@ -289,17 +290,36 @@ def measure_prefill(ctx, device, stream, dist, rank=0, world=1, ep_chunks=1, ep_
         return ms
 
     x = x0.clone()
-    ep = None
+    # C4 as specified: 131,072 tokens per step through the 48 MoE layers, split evenly over the ranks
+    # (strong scaling), each rank running its share as calls of PREFILL_T tokens; with G > 1 the experts
+    # [g*E/G, (g+1)*E/G) are computed on rank g. `local_ms` times one call of PREFILL_T tokens with every
+    # expert on this rank (the single-GPU rate) in the same run, for the efficiency figure.
+    n_calls = max(1, C4_TOKENS // (world * PREFILL_T))
+    local_ms = timed(lambda: ctx.layers(0, N_LAYER, x), reps=3, warm=1)
+    x = x0.clone()
+    imbalance = None
     if world > 1:
         from hoard_b200.ep import ExpertParallel
+        sel, _ = ctx.route(0, x0)
+        per_rank = torch.bincount((sel.view(-1) // (E // world)).long(), minlength=world).float()
+        if dist:
+            dist.all_reduce(per_rank)
+        imbalance = float(per_rank.max() / per_rank.mean())
         ep = ExpertParallel(ctx, experts_per_rank=E // world, slot_base=rank * (E // world),
                             max_rows=PREFILL_T * K_USED * world, chunks=ep_chunks, transport=ep_transport)
         ctx.set_gemm_ctas(ep_gemm_ctas if ep_chunks > 1 and ep_transport == "nccl" else 0)
-        ms = timed(lambda: ep.layers(0, N_LAYER, x), reps=5, warm=2)
+
+        def step():
+            for _ in range(n_calls):
+                ep.layers(0, N_LAYER, x)
+        ms = timed(step, reps=2, warm=1)
         ctx.set_gemm_ctas(0)
         ep.close()
     else:
-        ms = timed(lambda: ctx.layers(0, N_LAYER, x), reps=5, warm=2)
+        def step():
+            for _ in range(n_calls):
+                ctx.layers(0, N_LAYER, x)
+        ms = timed(step, reps=2, warm=1)
     ctx.sync_status()
     sweep = []
     for T in C2_TS:
@@ -308,14 +328,23 @@ def measure_prefill(ctx, device, stream, dist, rank=0, world=1, ep_chunks=1, ep_
         sweep.append({"T": T, "us_per_layer": round(ms_l * 1e3, 1), "tok_s": round(T / ms_l * 1e3, 1),
                       "expert_tflops": round(layer_flops(T) / (ms_l * 1e-3) / 1e12, 1)})
     ctx.sync_status()
-    achieved = layer_flops(PREFILL_T) * N_LAYER / (ms * 1e-3) / 1e12    # per GPU
+    achieved = layer_flops(PREFILL_T) * N_LAYER * n_calls / (ms * 1e-3) / 1e12    # per GPU
     traffic = None
     try:
         traffic = json.load(open(os.path.join(ROOT, "profiles", "traffic.json"))).get("prefill_gateup_T4096_bytes")
     except Exception:
         pass
-    return {"metric": f"prefill tok/s ({N_LAYER} MoE layers, {PREFILL_T} tokens per call and GPU)",
-            "value": PREFILL_T / ms * 1e3, "unit": "tok/s", "ms_per_step": round(ms, 3),
+    tok_s = C4_TOKENS / ms * 1e3 if n_calls * world * PREFILL_T == C4_TOKENS else PREFILL_T * n_calls * world / ms * 1e3
+    local_tok_s = PREFILL_T / local_ms * 1e3
+    return {"metric": f"prefill tok/s (C4: {C4_TOKENS} tokens per step through {N_LAYER} MoE layers, split over the "
+                      f"GPUs; {PREFILL_T} tokens per call)",
+            "value": tok_s, "unit": "tok/s", "ms_per_step": round(ms, 3), "scaling": "strong",
+            "tokens_per_step": C4_TOKENS, "calls_per_rank": n_calls,
+            "single_gpu_tok_s": round(local_tok_s, 1),
+            "efficiency_vs_single_gpu": round(tok_s / (world * local_tok_s), 4),
+            "speedup_vs_single_gpu": round(tok_s / local_tok_s, 3),
+            "expert_load_imbalance": None if imbalance is None else round(imbalance, 4),
+            "imbalance_note": "entries received by the busiest rank / the mean over ranks (one call's routing)",
             "parallelism": (("ep{} (dispatch/combine by the library's kernels over NVLink peer memory)".format(world)
                              if ep_transport == "p2p" else
                              f"ep{world} (NCCL all-to-all dispatch/combine, {ep_chunks} micro-batches"
@@ -692,7 +721,7 @@ def run_gpu(args, rank, world, local_rank):
             "clocks": dict(clk.summary(), window="0.5 s of the same decode steps, then the timed steps"),
         }
         if prefill:
-            prefill["value"] = round(prefill["value"] * world, 1)   # whole job: every rank's tokens
+            prefill["value"] = round(prefill["value"], 1)           # whole job: C4's tokens over all ranks
         if lru:
             line["lru_decode"] = lru
         if prefill:
