@@ -194,8 +194,10 @@ cudaError_t launch_decode_persistent(const Dims& d, int KK, int sh_dt, const Lay
                                      cudaStream_t s, unsigned long long* trace);
 
 // The same persistent decode kernel with its scratch in a static device array (no allocation).
+// scratch: the array's device address on the current device, from decode_static_address
 bool decode_static_fits(const Dims& d, int KK);
+cudaError_t decode_static_address(void** out);
 cudaError_t launch_decode_static(const Dims& d, int KK, int sh_dt, const LayerWeights* lws_dev, int n_layers,
-                                 void* x_inout, int32_t* sel_out, float* w_out, cudaStream_t s);
+                                 void* scratch, void* x_inout, int32_t* sel_out, float* w_out, cudaStream_t s);
 
 }  // namespace hoard

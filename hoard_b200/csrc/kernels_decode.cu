@@ -27,7 +27,6 @@
 #include "kernels.h"
 #include "block_ops.cuh"
 
-#include <mutex>
 
 namespace hoard {
 
@@ -1172,24 +1171,14 @@ constexpr size_t NOALLOC_ZERO_BYTES = NOALLOC_AMAX_BYTES + NOALLOC_RACC_BYTES + 
 constexpr size_t NOALLOC_BYTES = NOALLOC_H_BYTES + NOALLOC_ZERO_BYTES;                         // ~105 KiB
 static __device__ __align__(256) unsigned char g_decode_scratch[NOALLOC_BYTES];
 
-static std::mutex g_scratch_mu;
-static void* g_scratch_addr[64];          // per device ordinal, resolved on the first call there
-
 // Device address of g_decode_scratch on the current device. In host code the array's name is only a
-// host-side stand-in, so the address is looked up once per device with that device current.
-static cudaError_t decode_scratch_address(void** out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+// host-side stand-in, so the address is looked up with that device current; the lookup also loads the
+// module that holds the array. A context resolves it once, when it is created.
+cudaError_t decode_static_address(void** out) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
-        void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_decode_scratch);
-        if (e != cudaSuccess) return e;
-        g_scratch_addr[dev] = p;
-    }
-    *out = g_scratch_addr[dev];
+    *out = p;
     return cudaSuccess;
 }
 
@@ -1198,12 +1187,10 @@ bool decode_static_fits(const Dims& d, int KK) {
 }
 
 cudaError_t launch_decode_static(const Dims& d, int KK, int sh_dt, const LayerWeights* lws_dev, int n_layers,
-                                 void* x_inout, int32_t* sel_out, float* w_out, cudaStream_t s) {
-    if (!decode_static_fits(d, KK)) return cudaErrorInvalidValue;
-    void* base = nullptr;
-    cudaError_t e = decode_scratch_address(&base);
-    if (e != cudaSuccess) return e;
-    uint8_t* b = static_cast<uint8_t*>(base);
+                                 void* scratch, void* x_inout, int32_t* sel_out, float* w_out, cudaStream_t s) {
+    if (!decode_static_fits(d, KK) || !scratch) return cudaErrorInvalidValue;
+    cudaError_t e;
+    uint8_t* b = static_cast<uint8_t*>(scratch);
     Scratch sc{};
     sc.h = reinterpret_cast<float*>(b);
     sc.amax = reinterpret_cast<unsigned*>(b + NOALLOC_H_BYTES);

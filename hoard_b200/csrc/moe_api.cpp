@@ -53,6 +53,7 @@ struct hoard_moe_ctx {
     int routed_T = 0;
     LayerWeights* lw_dev = nullptr;    // device copy of every layer's LayerWeights (persistent kernel)
     bool decode_ok = false;            // the persistent decode kernel supports these shapes / types
+    void* noalloc_scratch = nullptr;   // device address of the no-allocation decode's static array
     unsigned long long* trace = nullptr;
     int64_t trace_cap = 0;
     // residency: per-layer LRU slot pool over a host RAM tier (hoard_moe_ram_tier / hoard_moe_ensure)
@@ -297,8 +298,15 @@ int hoard_moe_create(const hoard_moe_desc* d, hoard_moe_ctx** out) {
             e = cudaMemcpy(c->lw_dev, tab.data(), tab.size() * sizeof(LayerWeights), cudaMemcpyHostToDevice);
             if (e != cudaSuccess) rc = cuda_fail(c, e, "layer table upload");
         }
-        if (rc == HOARD_OK)
+        if (rc == HOARD_OK) {
             c->decode_ok = decode_supported(c->dims, tab.data(), d->n_layer);
+            // resolved now, so that the module holding the array is loaded before the caller hands the
+            // rest of the device memory to its own arena
+            if (c->decode_ok && decode_static_address(&c->noalloc_scratch) != cudaSuccess) {
+                cudaGetLastError();
+                c->noalloc_scratch = nullptr;
+            }
+        }
     }
     if (rc != HOARD_OK) {
         hoard_moe_destroy(c);
@@ -653,8 +661,9 @@ int hoard_moe_decode_noalloc(hoard_moe_ctx* c, int layer0, int n_layers, void* x
         if (rc) return rc;
     }
     HCHECK(c, cudaSetDevice(c->desc.device));
+    if (!c->noalloc_scratch) return fail(c, HOARD_ESTATE, "the static decode scratch could not be resolved on this device");
     HCHECK(c, launch_decode_static(c->dims, decode_kk(c), c->desc.shexp_down_type, c->lw_dev + layer0, n_layers,
-                                   x_inout, sel_out, w_out, (cudaStream_t)stream));
+                                   c->noalloc_scratch, x_inout, sel_out, w_out, (cudaStream_t)stream));
     ++c->launches;
     return HOARD_OK;
 }
@@ -750,6 +759,10 @@ int hoard_moe_set_top_k(hoard_moe_ctx* c, int k) {
     for (int l = 0; l < c->desc.n_layer; ++l) tab[l] = layer_weights(c, l);
     HCHECK(c, cudaSetDevice(c->desc.device));
     c->decode_ok = decode_supported(c->dims, tab.data(), c->desc.n_layer);
+    if (c->decode_ok && !c->noalloc_scratch && decode_static_address(&c->noalloc_scratch) != cudaSuccess) {
+        cudaGetLastError();
+        c->noalloc_scratch = nullptr;
+    }
     return HOARD_OK;
 }
 

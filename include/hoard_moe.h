@@ -128,10 +128,13 @@ int hoard_moe_layers(hoard_moe_ctx* ctx, int layer0, int n_layers, void* x_inout
  * start-up (hoard sizes its expert slot pool to the whole VRAM budget), or a step loop that must not
  * call cudaMalloc at all (it can synchronise the device, and a failure mid-step has no recovery).
  * The weights stay in a context created at start-up. No counterpart in the hoard project.
- *   - Limits: n_expert_used <= 16, n_ff <= 1024, n_expert <= 512; larger shapes return HOARD_EINVAL.
- *     Contexts the persistent decode kernel cannot serve return HOARD_ESTATE.
- *   - The first call on each device looks up the array's device address (cudaGetSymbolAddress);
- *     make that first call before any stream capture.
+ *   - Limits: n_expert_used (plus 1 with a shared expert) <= 16, n_ff <= 1024, n_expert <= 512;
+ *     larger shapes return HOARD_EINVAL. Contexts the persistent decode kernel cannot serve return
+ *     HOARD_ESTATE.
+ *   - hoard_moe_create looks up the array's device address (cudaGetSymbolAddress) on the context's
+ *     device, which also loads the code module that holds the array: the array is reserved when the
+ *     context is created, before the caller's arena takes the rest of the device memory. A context
+ *     must not be used across a device reset (cudaDeviceReset), which invalidates that address.
  *   - Every call on a device shares the one array; each call clears the parts that must start at
  *     zero. Calls whose kernels overlap on the GPU (other streams, other threads) race: serialise them.
  *   - A device-side wait that gives up is not reported back; use hoard_moe_layers where that matters.

@@ -52,9 +52,26 @@ def test_noalloc_matches_layers_on_consecutive_calls(model):
         out, sel, w = run(ctx, ctx.decode_noalloc, x_np)
         assert np.array_equal(sel, ref_sel), call
         assert np.allclose(w, ref_w, rtol=1e-5, atol=1e-7), call
-        # same kernel and arithmetic; the router sums are double-precision atomics, so at most a
-        # last-bit difference can reach the output
+        # the same kernel and arithmetic with integer (fixed-point) router sums: the same bits
         assert rel_l2(out - x_np, ref - x_np) < 1e-5, call
+        assert np.array_equal(out.view(np.uint32), ref.view(np.uint32)), call
+    ctx.sync_status()
+
+
+def test_noalloc_calls_allocate_no_device_memory(model):
+    """The entry point's promise: after the first call, further calls change neither the device's free
+    memory nor torch's allocations."""
+    spec, ctx = model
+    x = torch.from_numpy(make_x(1, spec.H, seed=4100)).cuda(DEV)
+    ctx.decode_noalloc(0, N_LAYER, x)
+    torch.cuda.synchronize(DEV)
+    free0, _ = torch.cuda.mem_get_info(DEV)
+    alloc0 = torch.cuda.memory_allocated(DEV)
+    for _ in range(5):
+        ctx.decode_noalloc(0, N_LAYER, x)
+    torch.cuda.synchronize(DEV)
+    free1, _ = torch.cuda.mem_get_info(DEV)
+    assert free1 == free0 and torch.cuda.memory_allocated(DEV) == alloc0
     ctx.sync_status()
 
 
