@@ -89,6 +89,14 @@ cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const 
                                    const int32_t* slot_of_sel, const float* w, void* x_inout, int T,
                                    bool need_sh_gate, cudaStream_t s, int* launches);
 
+// Weight-streaming gate/up and down kernels of the grouped path (persistent, bulk-copy staged; the
+// dispatch's work list with one item per non-empty slot). Supported: gate/up Q4_K with H = 2048;
+// down Q4_K / Q6_K with I/256 <= 4 and H a multiple of 64.
+bool gateup_sw_supported(const Dims& d, const LayerWeights& lw);
+bool down_sw_supported(const Dims& d, const LayerWeights& lw);
+cudaError_t launch_gateup_sw(const Dims& d, const LayerWeights& lw, const Scratch& sc, int KK, cudaStream_t s);
+cudaError_t launch_down_sw(const Dims& d, const LayerWeights& lw, const Scratch& sc, cudaStream_t s);
+
 // Pieces shared by the grouped and tensor-core expert paths.
 cudaError_t launch_shared_gate(const float* fx, const float* gate_inp, int H, int T, float* out, cudaStream_t s);
 // Counting sort of the entries by slot; with tile_m > 0 also the (slot, M tile) work list. Slots out

@@ -26,6 +26,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "block_ops.cuh"
+#include "async_copy.cuh"
 
 
 namespace hoard {
@@ -40,46 +41,8 @@ constexpr int NCH = 4;                                   // gate/up arrival chun
 constexpr double RFIX = 1099511627776.0;      // 2^40: unit of a normalised router partial sum
 constexpr double RFIX_MAX = 4.0e18;           // |partial| * 2^40 beyond this sets error bit 4
 constexpr int RACC_COPIES = 4;   // router accumulators spread over copies (4 measured best of 1, 2, 4, 8, 16)
-constexpr unsigned long long WAIT_NS = 2000000000ull;   // 2 s bound on any wait
 constexpr int HREADY_OFF = 64;         // h block readiness counters: sync word HREADY_OFF + HREADY_STRIDE * b
 constexpr int HREADY_STRIDE = 32;      // one 128-byte line per counter (pollers of different blocks do not share)
-
-__device__ __forceinline__ unsigned long long gtimer() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ unsigned smem_u32(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-// try_wait with a suspend-time hint: a waiting warp sleeps in hardware until the phase completes
-// (or the hint elapses) instead of spinning, so it takes no issue slots from the working warps.
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
-    unsigned ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u) : "memory");
-    return ok != 0;
-}
-// Bounded wait for phase `parity` of an mbarrier; false if the bound expired.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = gtimer();
-    while (!mbar_try_wait(bar, parity)) {
-        if (gtimer() - t0 > WAIT_NS) return false;
-    }
-    return true;
-}
-// 1-D bulk copy global -> shared, completion counted on `bar` (16-byte aligned, size % 16 == 0).
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
-}
 
 __device__ __forceinline__ unsigned ld_acq(const unsigned* p) {
     unsigned v;
@@ -160,9 +123,6 @@ inline __host__ __device__ int hq_stride(int nbI) {
     return ((s / 16) & 1) ? s : s + 16;
 }
 
-__device__ __forceinline__ void named_sync(int id, int count) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
 __device__ __forceinline__ void named_arrive(int id, int count) {
     asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
 }

@@ -298,31 +298,56 @@ __global__ void __launch_bounds__(256) k_router_logits(const float* __restrict__
     }
 }
 
-// 8 tokens per CTA: all 256 threads sum the K splits into shared memory (independent loads), then
-// one warp per token does softmax + top-k (E <= 1024)
+// TT tokens per CTA (1 at small T, so that the split sums of a batch of a few tokens are spread over
+// many CTAs, with TOPK_SMALL_THREADS threads; 8 at large T, 256 threads): the CTA's threads sum the K
+// splits into shared memory, then one warp per token does softmax + top-k (E <= 1024). Where the
+// CTA's (token, expert) elements number at most half its threads, SUBS = threads / elements threads
+// share an element: each sums a contiguous range of the splits (eight independent loads in flight,
+// added in split order) and the range sums are added in range order, so the result depends only on
+// (ksplit, T, E).
 constexpr int TOPK_TT = 8;
+constexpr int TOPK_SMALL_T = 1024;   // at most this many tokens: one token per CTA
+constexpr int TOPK_SMALL_THREADS = 512;
 
 template <int NV>
-__global__ void __launch_bounds__(256) k_route_topk(const double* __restrict__ part, int ksplit, int T, int E, int k,
-                                                    int renorm, int32_t* __restrict__ sel, float* __restrict__ w) {
+__global__ void __launch_bounds__(TOPK_SMALL_THREADS) k_route_topk(const double* __restrict__ part, int ksplit, int T,
+                                                                   int E, int k, int renorm, int32_t* __restrict__ sel,
+                                                                   float* __restrict__ w) {
     __shared__ float lg[TOPK_TT][32 * NV];
-    const int t0 = blockIdx.x * TOPK_TT;
-    const int nt = min(TOPK_TT, T - t0);
-    for (int i = threadIdx.x; i < nt * E; i += blockDim.x) {
-        const int tt = i / E, e = i - tt * E;
+    __shared__ double rs[TOPK_SMALL_THREADS];
+    const int tpc = T <= TOPK_SMALL_T ? 1 : TOPK_TT;
+    const int t0 = blockIdx.x * tpc;
+    const int nt = min(tpc, T - t0);
+    const int nel = nt * E;
+    int subs = 1;
+    while (subs < 16 && subs * 2 * nel <= (int)blockDim.x && subs * 2 <= ksplit) subs *= 2;
+    const int64_t zs = (int64_t)T * E;
+    for (int i = threadIdx.x; i < subs * nel; i += blockDim.x) {
+        const int el = i % nel, sub = i / nel;
+        const int tt = el / E, e = el - tt * E;
+        const int z0 = (int)((int64_t)ksplit * sub / subs), z1 = (int)((int64_t)ksplit * (sub + 1) / subs);
         const double* src = part + (int64_t)(t0 + tt) * E + e;
-        const int64_t zs = (int64_t)T * E;
         double s = 0.0;
-        int z = 0;
-        for (; z + 8 <= ksplit; z += 8) {           // eight loads in flight, added in split order
+        int z = z0;
+        for (; z + 8 <= z1; z += 8) {
             double v[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) v[u] = src[(int64_t)(z + u) * zs];
 #pragma unroll
             for (int u = 0; u < 8; ++u) s += v[u];
         }
-        for (; z < ksplit; ++z) s += src[(int64_t)z * zs];
-        lg[tt][e] = (float)s;
+        for (; z < z1; ++z) s += src[(int64_t)z * zs];
+        if (subs == 1) lg[tt][e] = (float)s;
+        else rs[i] = s;
+    }
+    if (subs > 1) {
+        __syncthreads();
+        for (int el = threadIdx.x; el < nel; el += blockDim.x) {
+            double s = rs[el];
+            for (int sub = 1; sub < subs; ++sub) s += rs[sub * nel + el];
+            const int tt = el / E;
+            lg[tt][el - tt * E] = (float)s;
+        }
     }
     __syncthreads();
     const int lane = threadIdx.x & 31, tt = threadIdx.x >> 5;
@@ -503,12 +528,14 @@ cudaError_t launch_route(const Dims& d, const LayerWeights& lw, const void* x, i
         const dim3 grid((T + RL_TT - 1) / RL_TT, (d.E + RL_EB - 1) / RL_EB, ks);
         k_router_logits<<<grid, 256, 0, s>>>(fx, lw.w_router, T, d.H, d.E, d.H / ks, part);
     }
-    const unsigned tgrid = (unsigned)((T + TOPK_TT - 1) / TOPK_TT);
-    if (d.E <= 64) k_route_topk<2><<<tgrid, 256, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
-    else if (d.E <= 128) k_route_topk<4><<<tgrid, 256, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
-    else if (d.E <= 256) k_route_topk<8><<<tgrid, 256, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
-    else if (d.E <= 512) k_route_topk<16><<<tgrid, 256, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
-    else k_route_topk<32><<<tgrid, 256, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
+    const int tpc = T <= TOPK_SMALL_T ? 1 : TOPK_TT;
+    const unsigned tgrid = (unsigned)((T + tpc - 1) / tpc);
+    const int tth = tpc == 1 ? TOPK_SMALL_THREADS : 256;
+    if (d.E <= 64) k_route_topk<2><<<tgrid, tth, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
+    else if (d.E <= 128) k_route_topk<4><<<tgrid, tth, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
+    else if (d.E <= 256) k_route_topk<8><<<tgrid, tth, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
+    else if (d.E <= 512) k_route_topk<16><<<tgrid, tth, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
+    else k_route_topk<32><<<tgrid, tth, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
     if (launches) *launches += 3;
     return cudaGetLastError();
 }
@@ -854,246 +881,6 @@ __global__ void __launch_bounds__(256) k_down(LayerWeights lw, int H, int I, con
     }
 }
 
-// ---- streamed small-batch expert matmuls ----------------------------------------------------------
-// Persistent CTAs walk the (non-empty slot, row tile) work list of the dispatch. The rows of the next
-// tile are copied into the other half of a shared-memory double buffer (16-byte cp.async pieces,
-// consecutive threads taking consecutive pieces of each plane range) while the current tile is
-// computed, so the weight stream never waits on the dependent loads of the slot's entries. Each
-// lane's unit arithmetic and the lane reductions are those of the per-entry kernels: the results are
-// bit-identical.
-constexpr int ST_THREADS = 256;
-constexpr int ST_CTAS_PER_SM = 2;
-constexpr int GS_ROWS = 16;          // gate/up rows per tile (8 warps x 2)
-constexpr int DS_ROWS = 32;          // down rows per tile
-
-__device__ __forceinline__ void cp16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-// bytes [lo, lo + n*16) of src into dst, pieces spread over the CTA's threads
-__device__ __forceinline__ void cp_range(uint8_t* dst, const uint8_t* src, int n16) {
-    for (int i = threadIdx.x; i < n16; i += blockDim.x) cp16(dst + 16 * i, src + 16 * i);
-}
-
-// One Q4_K unit with its scales decoded once (they depend only on the weights), for dots against
-// many activation rows; the float operations are q4k_unit_dot's, so the result is bit-identical.
-struct Q4Pre {
-    uint4 w;
-    int sc0, sc1, m0, m1, g, hh;
-    float d, dmin;
-};
-__device__ __forceinline__ Q4Pre q4_pre(const uint4& w, const uint4& h, int c8) {
-    Q4Pre u;
-    u.w = w;
-    u.g = c8 >> 1;
-    u.hh = c8 & 1;
-    q4k_scale_min(h, 2 * u.g, u.sc0, u.m0);
-    q4k_scale_min(h, 2 * u.g + 1, u.sc1, u.m1);
-    u.d = h2f(h.x);
-    u.dmin = h2f(h.x >> 16);
-    return u;
-}
-__device__ __forceinline__ float q4_pre_dot(const Q4Pre& u, const int8_t* a_blk, const int* bs_blk, float d8) {
-    const int4 alo = ld16s(a_blk + 64 * u.g + 16 * u.hh);
-    const int4 ahi = ld16s(a_blk + 64 * u.g + 32 + 16 * u.hh);
-    int slo = __dp4a((int)(u.w.x & 0x0F0F0F0Fu), alo.x, 0);
-    slo = __dp4a((int)(u.w.y & 0x0F0F0F0Fu), alo.y, slo);
-    slo = __dp4a((int)(u.w.z & 0x0F0F0F0Fu), alo.z, slo);
-    slo = __dp4a((int)(u.w.w & 0x0F0F0F0Fu), alo.w, slo);
-    int shi = __dp4a((int)((u.w.x >> 4) & 0x0F0F0F0Fu), ahi.x, 0);
-    shi = __dp4a((int)((u.w.y >> 4) & 0x0F0F0F0Fu), ahi.y, shi);
-    shi = __dp4a((int)((u.w.z >> 4) & 0x0F0F0F0Fu), ahi.z, shi);
-    shi = __dp4a((int)((u.w.w >> 4) & 0x0F0F0F0Fu), ahi.w, shi);
-    const int bs0 = bs_blk[4 * u.g + u.hh], bs1 = bs_blk[4 * u.g + 2 + u.hh];
-    return d8 * (u.d * (float)(u.sc0 * slo + u.sc1 * shi) - u.dmin * (float)(u.m0 * bs0 + u.m1 * bs1));
-}
-
-// Gate/up of Q4_K slots (H/256 <= 16 blocks per row): tile = 16 rows of one slot's gate and up.
-// Shared layout of one buffer: gate qs [16][nb*128] | gate hdr [16][nb*16] | up qs | up hdr.
-__global__ void __launch_bounds__(ST_THREADS) k_gateup_stream(LayerWeights lw, int H, int I, int KK,
-                                                              const int* __restrict__ offsets,
-                                                              const int* __restrict__ perm,
-                                                              const int2* __restrict__ items,
-                                                              const int* __restrict__ n_items,
-                                                              const int8_t* __restrict__ xq, const float* __restrict__ xd,
-                                                              const int* __restrict__ xbs, float* __restrict__ h) {
-    extern __shared__ __align__(128) uint8_t sm_st[];
-    const int nb = H / QK;
-    const int64_t nblk = (int64_t)I * nb;
-    const int qrow = nb * 128, hrow = nb * 16;
-    const int buf_bytes = GS_ROWS * 2 * (qrow + hrow);
-    const int ntr = (I + GS_ROWS - 1) / GS_ROWS;
-    const int ntiles = *n_items * ntr;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    auto issue = [&](int tile, int b) {
-        const int slot = items[tile / ntr].x, r0 = (tile % ntr) * GS_ROWS, nr = min(GS_ROWS, I - r0);
-        const SlotMats m = slot_mats(lw, slot);
-        uint8_t* B = sm_st + b * buf_bytes;
-        cp_range(B, m.g + (int64_t)r0 * qrow, nr * qrow / 16);
-        cp_range(B + GS_ROWS * qrow, m.g + nblk * 128 + (int64_t)r0 * hrow, nr * hrow / 16);
-        cp_range(B + GS_ROWS * (qrow + hrow), m.u + (int64_t)r0 * qrow, nr * qrow / 16);
-        cp_range(B + GS_ROWS * (2 * qrow + hrow), m.u + nblk * 128 + (int64_t)r0 * hrow, nr * hrow / 16);
-    };
-    int tile = blockIdx.x, b = 0;
-    if (tile < ntiles) issue(tile, 0);
-    cp_commit();
-    for (; tile < ntiles; tile += gridDim.x, b ^= 1) {
-        const int next = tile + gridDim.x;
-        if (next < ntiles) issue(next, b ^ 1);
-        cp_commit();
-        cp_wait<1>();
-        __syncthreads();
-        const int slot = items[tile / ntr].x, r0 = (tile % ntr) * GS_ROWS;
-        const int start = offsets[slot], end = offsets[slot + 1];
-        const uint8_t* B = sm_st + b * buf_bytes;
-        const int nunits = nb * 8;
-        for (int rr = warp; rr < GS_ROWS; rr += 8) {
-            const int i = r0 + rr;
-            if (i >= I) break;
-            // this lane's units (lane, lane + 32, ...) of the gate and up rows, from shared memory
-            Q4Pre ug[2], uu[2];
-            bool has[2];
-#pragma unroll
-            for (int k2 = 0; k2 < 2; ++k2) {
-                const int u = lane + 32 * k2;
-                has[k2] = u < nunits;
-                if (has[k2]) {
-                    ug[k2] = q4_pre(*reinterpret_cast<const uint4*>(B + rr * qrow + 16 * u),
-                                    *reinterpret_cast<const uint4*>(B + GS_ROWS * qrow + rr * hrow + 16 * (u >> 3)), u & 7);
-                    uu[k2] = q4_pre(*reinterpret_cast<const uint4*>(B + GS_ROWS * (qrow + hrow) + rr * qrow + 16 * u),
-                                    *reinterpret_cast<const uint4*>(B + GS_ROWS * (2 * qrow + hrow) + rr * hrow + 16 * (u >> 3)),
-                                    u & 7);
-                }
-            }
-            for (int p = start; p < end; ++p) {
-                const int ent = perm[p];
-                const int t = ent / KK;
-                const int8_t* aq = xq + (size_t)t * H;
-                const float* ad = xd + (size_t)t * nb;
-                const int* abs_ = xbs + (size_t)t * (H / 16);
-                float g = 0.f, u = 0.f;
-#pragma unroll
-                for (int k2 = 0; k2 < 2; ++k2) {
-                    if (!has[k2]) continue;
-                    const int bb = (lane + 32 * k2) >> 3;
-                    const float d8 = ad[bb];
-                    g += q4_pre_dot(ug[k2], aq + QK * bb, abs_ + 16 * bb, d8);
-                    u += q4_pre_dot(uu[k2], aq + QK * bb, abs_ + 16 * bb, d8);
-                }
-                g = warp_sum(g);
-                u = warp_sum(u);
-                if (lane == 0) h[(size_t)ent * I + i] = silu_f(g) * u;
-            }
-        }
-        __syncthreads();             // the next iteration copies into this buffer
-    }
-    cp_wait<0>();
-}
-
-// Down rows (Q4_K or Q6_K, I/256 <= 4): tile = 32 rows of one slot's down matrix, G lanes per row.
-// Shared layout of one buffer (both types, sized for Q6_K): ql/qs [32][nbI*128] | qh or hdr
-// [32][nbI*64] | sc [32][nbI*16] | d superset [32*nbI*2 + 32].
-template <int G>
-__global__ void __launch_bounds__(ST_THREADS) k_down_stream(LayerWeights lw, int H, int I,
-                                                            const int* __restrict__ offsets,
-                                                            const int* __restrict__ perm,
-                                                            const int2* __restrict__ items,
-                                                            const int* __restrict__ n_items,
-                                                            const int8_t* __restrict__ hq, const float* __restrict__ hd,
-                                                            const int* __restrict__ hbs, float* __restrict__ y) {
-    extern __shared__ __align__(128) uint8_t sm_st[];
-    const int nb = I / QK;
-    const int64_t nblk = (int64_t)H * nb;
-    const int p1 = DS_ROWS * nb * 128, p2 = p1 + DS_ROWS * nb * 64, p3 = p2 + DS_ROWS * nb * 16;
-    const int buf_bytes = p3 + DS_ROWS * nb * 2 + 32;
-    const int ntr = (H + DS_ROWS - 1) / DS_ROWS;
-    const int ntiles = *n_items * ntr;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    constexpr int RPW = 32 / G;
-    const int sub = lane / G, gl = lane - sub * G;
-    auto issue = [&](int tile, int b) {
-        const int slot = items[tile / ntr].x, r0 = (tile % ntr) * DS_ROWS, nr = min(DS_ROWS, H - r0);
-        const SlotMats m = slot_mats(lw, slot);
-        uint8_t* B = sm_st + b * buf_bytes;
-        const int64_t blk0 = (int64_t)r0 * nb;
-        cp_range(B, m.d + blk0 * 128, nr * nb * 8);
-        if (m.dt == T_Q6K) {
-            cp_range(B + p1, m.d + nblk * 128 + blk0 * 64, nr * nb * 4);
-            cp_range(B + p2, m.d + nblk * 192 + blk0 * 16, nr * nb);
-            const int64_t lo = (nblk * 208 + blk0 * 2) & ~(int64_t)15;
-            const int64_t hi = (nblk * 208 + (blk0 + (int64_t)nr * nb) * 2 + 15) & ~(int64_t)15;
-            cp_range(B + p3, m.d + lo, (int)((hi - lo) / 16));
-        } else {
-            cp_range(B + p1, m.d + nblk * 128 + blk0 * 16, nr * nb);
-        }
-    };
-    int tile = blockIdx.x, b = 0;
-    if (tile < ntiles) issue(tile, 0);
-    cp_commit();
-    for (; tile < ntiles; tile += gridDim.x, b ^= 1) {
-        const int next = tile + gridDim.x;
-        if (next < ntiles) issue(next, b ^ 1);
-        cp_commit();
-        cp_wait<1>();
-        __syncthreads();
-        const int slot = items[tile / ntr].x, r0 = (tile % ntr) * DS_ROWS;
-        const int start = offsets[slot], end = offsets[slot + 1];
-        const SlotMats m = slot_mats(lw, slot);
-        const uint8_t* B = sm_st + b * buf_bytes;
-        const int dsub = (int)(((int64_t)r0 * nb * 2) & 15);
-        const int nunits = nb * (m.dt == T_Q4K ? 8 : 4);
-        for (int rr = warp * RPW + sub; rr - sub < DS_ROWS; rr += 8 * RPW) {
-            const int dr = r0 + rr;
-            const bool v = dr < H && gl < nunits;
-            // this lane's unit of the row, from shared memory (the per-entry kernels' RowUnit layout)
-            uint4 A = make_uint4(0, 0, 0, 0), Bv = A, C = A, S = A;
-            float d6 = 0.f;
-            int bb = 0, vv = 0;
-            Q4Pre q4u{};
-            if (v) {
-                if (m.dt == T_Q6K) {
-                    bb = gl >> 2; vv = gl & 3;
-                    const int h2 = vv >> 1, r = vv & 1, blk = rr * nb + bb;
-                    A = *reinterpret_cast<const uint4*>(B + blk * 128 + 64 * h2 + 16 * r);
-                    Bv = *reinterpret_cast<const uint4*>(B + blk * 128 + 64 * h2 + 32 + 16 * r);
-                    C = *reinterpret_cast<const uint4*>(B + p1 + blk * 64 + 32 * h2 + 16 * r);
-                    S = *reinterpret_cast<const uint4*>(B + p2 + blk * 16);
-                    d6 = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(B + p3 + dsub + blk * 2)));
-                } else {
-                    bb = gl >> 3; vv = gl & 7;
-                    const int blk = rr * nb + bb;
-                    q4u = q4_pre(*reinterpret_cast<const uint4*>(B + blk * 128 + 16 * vv),
-                                 *reinterpret_cast<const uint4*>(B + p1 + blk * 16), vv);
-                }
-            }
-            for (int p = start; p < end; ++p) {
-                const int ent = perm[p];
-                const int8_t* aq = hq + (size_t)ent * I;
-                const int* abs_ = hbs + (size_t)ent * (I / 16);
-                const float* ad = hd + (size_t)ent * nb;
-                float f = 0.f;
-                if (v) {
-                    if (m.dt == T_Q6K) {
-                        const int is = q6k_unit_isum(A, Bv, C, S, vv, aq + QK * bb, abs_ + 16 * bb);
-                        f = ad[bb] * d6 * (float)is;
-                    } else {
-                        f = q4_pre_dot(q4u, aq + QK * bb, abs_ + 16 * bb, ad[bb]);
-                    }
-                }
-                f = 0.f + f;
-#pragma unroll
-                for (int o = G / 2; o > 0; o >>= 1) f += __shfl_xor_sync(0xffffffffu, f, o);
-                if (gl == 0 && dr < H) y[(size_t)ent * H + dr] = f;
-            }
-        }
-        __syncthreads();
-    }
-    cp_wait<0>();
-}
-
 // sigmoid(gate_inp . fx[t]) per token (double accumulation, as the router GEMV)
 __global__ void __launch_bounds__(256) k_shared_gate(const float* __restrict__ fx, const float* __restrict__ g, int H,
                                                      float* __restrict__ out) {
@@ -1371,17 +1158,6 @@ cudaError_t launch_combine_rows(const Dims& d, const uint16_t* y, const int* pos
     return cudaGetLastError();
 }
 
-// persistent CTAs of the streamed small-batch kernels: ST_CTAS_PER_SM per SM
-static int st_grid() {
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    }
-    return sms * ST_CTAS_PER_SM;
-}
-
 cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const Scratch& sc, const float* fx,
                                    const int32_t* slot_of_sel, const float* w, void* x_inout, int T,
                                    bool /*need_sh_gate*/, cudaStream_t s, int* launches) {
@@ -1397,25 +1173,17 @@ cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const 
         if ((e = launch_shared_gate(fx, lw.sh_gate_inp, d.H, T, sc.sh_gate, s)) != cudaSuccess) return e;
         ++nl;
     }
-    // 2. group entries by slot (with a work list of the non-empty slots for the streamed kernels)
-    const int nbH = d.H / QK, nbI = d.I / QK;
-    const bool gu_stream = nbH <= 8 && lw.gate_type == T_Q4K && lw.up_type == T_Q4K &&
-                           (!shared || (lw.sh_gate_type == T_Q4K && lw.sh_up_type == T_Q4K));
-    const bool dn_stream = nbI <= 4;
-    const int st_ctas = st_grid();
-    if ((e = launch_dispatch(slot_of_sel, T, d.k, KK, lw.n_slots, sc, (gu_stream || dn_stream) ? (1 << 20) : 0, s, &nl))
+    // 2. group entries by slot (with a work list of the non-empty slots for the streaming kernels)
+    const bool gu_sw = gateup_sw_supported(d, lw), dn_sw = down_sw_supported(d, lw);
+    if ((e = launch_dispatch(slot_of_sel, T, d.k, KK, lw.n_slots, sc, (gu_sw || dn_sw) ? (1 << 20) : 0, s, &nl))
         != cudaSuccess)
         return e;
-    // 3. gate/up + SwiGLU (weights held in registers across a slot's entries where the row fits in
-    //    two units per lane)
+    // 3. gate/up + SwiGLU: each selected slot's rows streamed once; otherwise weight rows held in
+    //    registers across a slot's entries where the row fits in two units per lane
     const dim3 gu_grid(NS, (d.I + GU_ROWS - 1) / GU_ROWS);
     const int gu_units = (d.H / QK) * 8;
-    if (gu_stream) {
-        const int smem = 2 * GS_ROWS * 2 * nbH * (128 + 16);
-        if ((e = cudaFuncSetAttribute(k_gateup_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
-            return e;
-        k_gateup_stream<<<st_ctas, ST_THREADS, smem, s>>>(lw, d.H, d.I, KK, sc.offsets, sc.perm, sc.items, sc.n_items,
-                                                           sc.fx_q, sc.fx_d, sc.fx_bs, sc.h);
+    if (gu_sw) {
+        if ((e = launch_gateup_sw(d, lw, sc, KK, s)) != cudaSuccess) return e;
     } else if (gu_units <= 32)
         k_gateup_regs<1><<<gu_grid, 256, 0, s>>>(lw, d.H, d.I, KK, sc.offsets, sc.perm, sc.fx_q, sc.fx_d, sc.fx_bs, sc.h);
     else if (gu_units <= 64)
@@ -1427,22 +1195,11 @@ cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const 
     k_quant_q8<<<(unsigned)((d.I / QK) * T * KK), 256, 0, s>>>(sc.h, d.I, sc.h_q, sc.h_d, sc.h_bs);
     ++nl;
     // 5. down (the widest row type present sets the lanes per row)
+    const int nbI = d.I / QK;
     int dn_units = nbI * (lw.down_type == T_Q4K ? 8 : 4);
     if (shared) dn_units = std::max(dn_units, nbI * (lw.sh_down_type == T_Q4K ? 8 : 4));
-    if (dn_stream) {
-        const int smem = 2 * (DS_ROWS * nbI * 208 + DS_ROWS * nbI * 2 + 32);
-        const void* fn = dn_units <= 8 ? (const void*)k_down_stream<8> : dn_units <= 16 ? (const void*)k_down_stream<16>
-                                                                                    : (const void*)k_down_stream<32>;
-        if ((e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
-        if (dn_units <= 8)
-            k_down_stream<8><<<st_ctas, ST_THREADS, smem, s>>>(lw, d.H, d.I, sc.offsets, sc.perm, sc.items, sc.n_items,
-                                                               sc.h_q, sc.h_d, sc.h_bs, sc.y);
-        else if (dn_units <= 16)
-            k_down_stream<16><<<st_ctas, ST_THREADS, smem, s>>>(lw, d.H, d.I, sc.offsets, sc.perm, sc.items, sc.n_items,
-                                                                sc.h_q, sc.h_d, sc.h_bs, sc.y);
-        else
-            k_down_stream<32><<<st_ctas, ST_THREADS, smem, s>>>(lw, d.H, d.I, sc.offsets, sc.perm, sc.items, sc.n_items,
-                                                                sc.h_q, sc.h_d, sc.h_bs, sc.y);
+    if (dn_sw) {
+        if ((e = launch_down_sw(d, lw, sc, s)) != cudaSuccess) return e;
     } else if (dn_units <= 8)
         k_down_regs<8><<<dim3(NS, (d.H + 63) / 64), 256, 0, s>>>(lw, d.H, d.I, sc.offsets, sc.perm, sc.h_q, sc.h_d,
                                                                  sc.h_bs, sc.y);

@@ -192,6 +192,113 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
     }
 }
 
+// ---- the same attention for head dims that are a multiple of 8 (16-byte rows of 8 cache values):
+//      one CTA of AV_THREADS per head; a thread takes whole positions for the scores (its key row read
+//      with 16-byte loads, q from shared memory), and (position group, 8 dimensions) for the
+//      probability-weighted value sum; the groups' partial sums are added in group order ----
+constexpr int AV_THREADS = 512;
+__device__ __forceinline__ void kv_get8(const __half* p, float* f) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+    }
+}
+__device__ __forceinline__ void kv_get8(const __nv_bfloat16* p, float* f) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+}
+
+template <typename KT>
+__global__ void __launch_bounds__(AV_THREADS) k_attention_v8(const float* __restrict__ q, const KT* __restrict__ kc,
+                                                             const KT* __restrict__ vc, int n_head, int n_kv, int hd,
+                                                             int n_pos, const int32_t* __restrict__ pos_dev,
+                                                             float scale, float* __restrict__ out) {
+    extern __shared__ float sm[];
+    const int cap = n_pos;
+    if (pos_dev) n_pos = min(*pos_dev + 1, cap);
+    const int V8 = hd / 8, PG = AV_THREADS / V8;
+    float* sq = sm;                  // [hd]
+    float* sp = sm + hd;             // [cap] scores, then probabilities
+    float* part = sp + cap;          // [PG][hd]
+    __shared__ float redf[32];
+    __shared__ double redd[32];
+    const int h = blockIdx.x, kvh = h / (n_head / n_kv);
+    const int64_t rs = (int64_t)n_kv * hd;           // cache row stride (elements)
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) sq[i] = q[(int64_t)h * hd + i];
+    __syncthreads();
+    for (int j = threadIdx.x; j < n_pos; j += blockDim.x) {
+        const KT* kr = kc + j * rs + (int64_t)kvh * hd;
+        float s = 0.f;
+        for (int v = 0; v < V8; v += 2) {            // two 16-byte loads in flight (V8 is even or 1)
+            float f0[8], f1[8];
+            kv_get8(kr + 8 * v, f0);
+            if (v + 1 < V8) kv_get8(kr + 8 * v + 8, f1);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) s += sq[8 * v + i] * f0[i];
+            if (v + 1 < V8) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) s += sq[8 * v + 8 + i] * f1[i];
+            }
+        }
+        sp[j] = s * scale;
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int j = threadIdx.x; j < n_pos; j += blockDim.x) mx = fmaxf(mx, sp[j]);
+    mx = block_max_f(mx, redf);
+    double sum = 0.0;
+    for (int j = threadIdx.x; j < n_pos; j += blockDim.x) {
+        const float e = expf(sp[j] - mx);
+        sp[j] = e;
+        sum += (double)e;
+    }
+    sum = block_sum_d(sum, redd);
+    const float inv = (float)(1.0 / sum);
+    __syncthreads();
+    {
+        const int g = threadIdx.x / V8, v = threadIdx.x - g * V8;
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        const KT* vb = vc + (int64_t)kvh * hd + 8 * v;
+        int j = g;
+        for (; j + PG < n_pos; j += 2 * PG) {        // two rows in flight
+            float f0[8], f1[8];
+            kv_get8(vb + j * rs, f0);
+            kv_get8(vb + (j + PG) * rs, f1);
+            const float p0 = sp[j] * inv, p1 = sp[j + PG] * inv;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] += p0 * f0[i];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] += p1 * f1[i];
+        }
+        if (j < n_pos) {
+            float f0[8];
+            kv_get8(vb + j * rs, f0);
+            const float p0 = sp[j] * inv;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] += p0 * f0[i];
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) part[g * hd + 8 * v + i] = acc[i];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+        float acc = 0.f;
+        for (int g = 0; g < PG; ++g) acc += part[g * hd + i];
+        out[(int64_t)h * hd + i] = acc;
+    }
+}
+
 // ---- fused: out = RMSNorm(x) * w, quantised to Q8_K (one CTA; thread t holds value 256j + t of
 //      every 256-value block j, so a block's maximum is one CTA-wide reduction per j) ----
 template <int NB>
@@ -458,24 +565,33 @@ cudaError_t launch_rope_store(float* q, float* k, const float* v, int n_head, in
 }
 
 size_t attention_smem(int hd, int n_pos) {
+    if (hd % 8 == 0) return (size_t)(hd + n_pos + (AV_THREADS / (hd / 8)) * hd) * sizeof(float);
     return (size_t)(hd + n_pos + (ATT_THREADS / hd) * hd) * sizeof(float);
 }
 
-cudaError_t launch_attention(const float* q, const void* kc, const void* vc, bool kv_bf16, int n_head, int n_kv,
-                             int hd, int n_pos, const int32_t* pos_dev, float scale, float* out, cudaStream_t s) {
+template <typename KT>
+static cudaError_t attention_t(const float* q, const void* kc, const void* vc, int n_head, int n_kv, int hd, int n_pos,
+                               const int32_t* pos_dev, float scale, float* out, cudaStream_t s) {
     const size_t smem = attention_smem(hd, n_pos);
-    const void* fn = kv_bf16 ? (const void*)k_attention<__nv_bfloat16> : (const void*)k_attention<__half>;
+    const bool v8 = hd % 8 == 0;
+    const void* fn = v8 ? (const void*)k_attention_v8<KT> : (const void*)k_attention<KT>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    if (kv_bf16)
-        k_attention<<<n_head, ATT_THREADS, smem, s>>>(q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, n_head,
-                                                      n_kv, hd, n_pos, pos_dev, scale, out);
+    if (v8)
+        k_attention_v8<KT><<<n_head, AV_THREADS, smem, s>>>(q, (const KT*)kc, (const KT*)vc, n_head, n_kv, hd, n_pos,
+                                                            pos_dev, scale, out);
     else
-        k_attention<<<n_head, ATT_THREADS, smem, s>>>(q, (const __half*)kc, (const __half*)vc, n_head, n_kv, hd, n_pos,
-                                                      pos_dev, scale, out);
+        k_attention<KT><<<n_head, ATT_THREADS, smem, s>>>(q, (const KT*)kc, (const KT*)vc, n_head, n_kv, hd, n_pos,
+                                                          pos_dev, scale, out);
     return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const float* q, const void* kc, const void* vc, bool kv_bf16, int n_head, int n_kv,
+                             int hd, int n_pos, const int32_t* pos_dev, float scale, float* out, cudaStream_t s) {
+    return kv_bf16 ? attention_t<__nv_bfloat16>(q, kc, vc, n_head, n_kv, hd, n_pos, pos_dev, scale, out, s)
+                   : attention_t<__half>(q, kc, vc, n_head, n_kv, hd, n_pos, pos_dev, scale, out, s);
 }
 
 cudaError_t launch_argmax(const float* v, int n, int32_t* out, int32_t* pos, int seq_len, cudaStream_t s) {

@@ -126,7 +126,7 @@ def qwen_c2():
     ctx.close()
 
 
-@pytest.mark.parametrize("T", [1, 16])
+@pytest.mark.parametrize("T", [1, 16, 63])
 def test_c2_layer_parity(qwen_c2, T):
     spec, L, ctx = qwen_c2
     x = make_x(T, spec.H, seed=1000 + T)
@@ -171,6 +171,22 @@ def test_shared_expert_top10():
     load_context(ctx, 0, L)
     x = make_x(5, spec.H, seed=5)
     out, sel, w = run_layer(ctx, x)
+    check_against_oracle(spec, L, x, out, sel, w)
+    ctx.close()
+
+
+def test_shared_expert_many_entries_per_slot():
+    """More entries per slot than the streaming kernels stage in shared memory (the shared expert
+    takes every token; a few routed experts take many): the overflow entries read their activations
+    from global memory. Q6_K and Q4_K down in one layer (shared expert Q4_K)."""
+    spec = LayerSpec(H=2048, E=16, k=6, I=512, shared=True, sh_types=(Q4_K, Q4_K, Q4_K))
+    L = make_layer(spec, seed=55)
+    ctx = make_ctx(spec, max_tokens=48)
+    load_context(ctx, 0, L)
+    x = make_x(45, spec.H, seed=55)
+    out, sel, w = run_layer(ctx, x)
+    counts = np.bincount(sel.ravel(), minlength=spec.E)
+    assert counts.max() > 16, counts           # a routed slot beyond the down kernel's staged entries
     check_against_oracle(spec, L, x, out, sel, w)
     ctx.close()
 
