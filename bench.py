@@ -56,6 +56,12 @@ def algorithmic_bytes_per_token(sel_layers) -> int:
     return total
 
 
+def c2_layer_bytes(sel, T: int) -> int:
+    """Bytes one C2 layer call must move: the distinct selected experts' bytes (layer 0: Q6_K down),
+    the f32 router weight [E][H] and ffn_norm [H], and the T residual rows in and out (f32)."""
+    return (len(set(int(e) for e in sel.reshape(-1))) * expert_bytes(0) + E * H * 4 + H * 4 + 2 * T * H * 4)
+
+
 # --------------------------------------------------------------------------------------------
 class ClockSampler:
     """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
@@ -253,6 +259,64 @@ def layer_flops(T: int) -> float:
     return 2.0 * T * K_USED * 3 * H * I
 
 
+def measure_c2(ctx, x0, Ts, timed):
+    """Isolated layer 0 of the context (C2: Q6_K down) at each T in Ts on the rows x0[:T]: us per layer
+    call (events around 20 calls after 3), tok/s, expert-FFN TFLOP/s and the HBM roofline of the call's
+    algorithmic bytes (the distinct experts its routing selects)."""
+    try:
+        hbm_peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"])
+    except Exception:
+        hbm_peak = 6650.0                                                    # the pool's fallback figure
+    sweep = []
+    for T in Ts:
+        xt = x0[:T].clone()
+        sel_t, _ = ctx.route(0, xt)
+        nbytes = c2_layer_bytes(sel_t.cpu(), T)
+        ms_l = timed(lambda: ctx.layer(0, xt), reps=20, warm=3)
+        gbs = nbytes / (ms_l * 1e-3) / 1e9
+        sweep.append({"T": T, "us_per_layer": round(ms_l * 1e3, 1), "tok_s": round(T / ms_l * 1e3, 1),
+                      "expert_tflops": round(layer_flops(T) / (ms_l * 1e-3) / 1e12, 1),
+                      "roofline": {"bound": "hbm", "algorithmic_bytes": int(nbytes), "achieved": round(gbs, 1),
+                                   "peak": hbm_peak, "unit": "GB/s", "frac": round(gbs / hbm_peak, 4)}})
+    return sweep
+
+
+def run_c2_only(args, local_rank):
+    """`--c2-only T,T,...`: the isolated C2 layer alone (one MoE layer, Q6_K down) at the given token
+    counts, one JSON line; the command that the small-batch kernel profiles are taken with."""
+    import torch
+    from hoard_b200 import moe
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    Ts = [int(t) for t in args.c2_only.split(",")]
+    ctx = moe.MoEContext(n_embd=H, n_expert=E, n_expert_used=K_USED, n_ff=I, n_layer=1, norm_topk=True, eps=1e-6,
+                         resid_dtype=torch.float32, gate_types=[Q4_K], up_types=[Q4_K], down_types=[Q6_K],
+                         max_tokens=max(Ts), device=local_rank)
+    build_model(ctx, device, 1)
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED + 4096)
+    x0 = torch.randn(max(Ts), H, generator=g, device=device)
+    x0 = x0 / torch.sqrt((x0 * x0).mean(-1, keepdim=True) + 1e-6)
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn, reps, warm):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize(device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        return a.elapsed_time(b) / reps
+
+    sweep = measure_c2(ctx, x0, Ts, timed)
+    ctx.sync_status()
+    ctx.close()
+    print(json.dumps({"metric": "C2 isolated MoE layer (Qwen3-30B-A3B shape)", "c2_layer": sweep}))
+
+
 def measure_prefill(ctx, device, stream, dist, rank=0, world=1, ep_chunks=1, ep_gemm_ctas=0, ep_transport="p2p"):
     """Batched tokens through the tensor-core expert path: the 48-layer stack at T = PREFILL_T tokens per
     call and rank (prefill tok/s; with world > 1 expert-parallel: experts [g*E/G, (g+1)*E/G) computed on
@@ -321,12 +385,7 @@ def measure_prefill(ctx, device, stream, dist, rank=0, world=1, ep_chunks=1, ep_
                 ctx.layers(0, N_LAYER, x)
         ms = timed(step, reps=2, warm=1)
     ctx.sync_status()
-    sweep = []
-    for T in C2_TS:
-        xt = x0[:T].clone()
-        ms_l = timed(lambda: ctx.layer(0, xt), reps=20, warm=3)
-        sweep.append({"T": T, "us_per_layer": round(ms_l * 1e3, 1), "tok_s": round(T / ms_l * 1e3, 1),
-                      "expert_tflops": round(layer_flops(T) / (ms_l * 1e-3) / 1e12, 1)})
+    sweep = measure_c2(ctx, x0, C2_TS, timed)
     ctx.sync_status()
     achieved = layer_flops(PREFILL_T) * N_LAYER * n_calls / (ms * 1e-3) / 1e12    # per GPU
     traffic = None
@@ -756,6 +815,7 @@ def main():
     ap.add_argument("--no-lru", action="store_true", help="skip the LRU slot pool + RAM tier decode measurement")
     ap.add_argument("--no-c1", action="store_true", help="skip the C1 whole-model decode (device driver) measurement")
     ap.add_argument("--no-c3", action="store_true", help="skip the C3 whole-model decode (device driver) measurement")
+    ap.add_argument("--c2-only", default=None, help="comma-separated token counts: time only the isolated C2 layer")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="expert-parallel prefill exchange: the library's peer-memory kernels or NCCL all-to-all")
     ap.add_argument("--ep-chunks", type=int, default=2, help="expert-parallel prefill: micro-batches per layer "
@@ -772,6 +832,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)
+    elif args.c2_only:
+        run_c2_only(args, local_rank)
     else:
         run_gpu(args, rank, world, local_rank)
 
