@@ -102,7 +102,7 @@ int hoard_hx_attention(const float* q, const void* k_cache, const void* v_cache,
         return HOARD_EINVAL;
     if (attention_smem(head_dim, n_pos) > 200 * 1024) return HOARD_EINVAL;
     return st(launch_attention(q, k_cache, v_cache, kv_type == HOARD_TYPE_BF16, n_head, n_head_kv, head_dim, n_pos,
-                               nullptr, scale, out, (cudaStream_t)stream));
+                               nullptr, scale, nullptr, 0, out, (cudaStream_t)stream));
 }
 
 int hoard_hx_attention_at(const float* q, const void* k_cache, const void* v_cache, int n_head, int n_head_kv,
@@ -113,7 +113,7 @@ int hoard_hx_attention_at(const float* q, const void* k_cache, const void* v_cac
         return HOARD_EINVAL;
     if (attention_smem(head_dim, max_ctx) > 200 * 1024) return HOARD_EINVAL;
     return st(launch_attention(q, k_cache, v_cache, kv_type == HOARD_TYPE_BF16, n_head, n_head_kv, head_dim, max_ctx,
-                               pos, scale, out, (cudaStream_t)stream));
+                               pos, scale, nullptr, 0, out, (cudaStream_t)stream));
 }
 
 int hoard_hx_argmax(const float* v, int n, int32_t* out, hoard_stream stream) {
@@ -160,8 +160,8 @@ int hoard_hx_qknorm_rope_store(const float* q, const float* k, const float* v, c
                                hoard_stream stream) {
     int rc = qknorm_check(q, k, v, q_norm, k_norm, mode, n_head, n_head_kv, head_dim, q_out, k_cache, v_cache);
     if (rc || pos < 0 || !(freq_base > 0) || !kv_ok(kv_type)) return rc ? rc : HOARD_EINVAL;
-    return st(launch_qknorm_rope_store(q, k, v, q_norm, k_norm, mode, eps, n_head, n_head_kv, head_dim, pos, nullptr,
-                                       pos + 1, freq_base, q_out, k_cache, v_cache, kv_type == HOARD_TYPE_BF16,
+    return st(launch_qknorm_rope_store(q, k, v, q_norm, k_norm, mode, eps, n_head, n_head_kv, head_dim, head_dim,
+                                       head_dim, pos, nullptr, pos + 1, freq_base, q_out, k_cache, v_cache, kv_type == HOARD_TYPE_BF16,
                                        (cudaStream_t)stream));
 }
 
@@ -171,9 +171,49 @@ int hoard_hx_qknorm_rope_store_at(const float* q, const float* k, const float* v
                                   void* v_cache, int kv_type, hoard_stream stream) {
     int rc = qknorm_check(q, k, v, q_norm, k_norm, mode, n_head, n_head_kv, head_dim, q_out, k_cache, v_cache);
     if (rc || !pos || max_ctx <= 0 || !(freq_base > 0) || !kv_ok(kv_type)) return rc ? rc : HOARD_EINVAL;
-    return st(launch_qknorm_rope_store(q, k, v, q_norm, k_norm, mode, eps, n_head, n_head_kv, head_dim, 0, pos,
-                                       max_ctx, freq_base, q_out, k_cache, v_cache, kv_type == HOARD_TYPE_BF16,
+    return st(launch_qknorm_rope_store(q, k, v, q_norm, k_norm, mode, eps, n_head, n_head_kv, head_dim, head_dim,
+                                       head_dim, 0, pos, max_ctx, freq_base, q_out, k_cache, v_cache, kv_type == HOARD_TYPE_BF16,
                                        (cudaStream_t)stream));
+}
+
+int hoard_hx_qknorm_rope_store_ex(const float* q, const float* k, const float* v, const float* q_norm,
+                                  const float* k_norm, int mode, float eps, int n_head, int n_head_kv, int head_dim,
+                                  int q_stride, int rope_dim, int pos, const int32_t* pos_dev, int max_ctx,
+                                  float freq_base, float* q_out, void* k_cache, void* v_cache, int kv_type,
+                                  hoard_stream stream) {
+    int rc = qknorm_check(q, k, v, q_norm, k_norm, mode, n_head, n_head_kv, head_dim, q_out, k_cache, v_cache);
+    if (rc) return rc;
+    if (q_stride < head_dim || (mode == 1 && q_stride != head_dim) || rope_dim < 2 || rope_dim > head_dim ||
+        rope_dim % 2 || max_ctx <= 0 || (!pos_dev && (pos < 0 || pos >= max_ctx)) || !(freq_base > 0) ||
+        !kv_ok(kv_type))
+        return HOARD_EINVAL;
+    return st(launch_qknorm_rope_store(q, k, v, q_norm, k_norm, mode, eps, n_head, n_head_kv, head_dim, q_stride,
+                                       rope_dim, pos, pos_dev, max_ctx, freq_base, q_out, k_cache, v_cache,
+                                       kv_type == HOARD_TYPE_BF16, (cudaStream_t)stream));
+}
+
+int hoard_hx_attention_ex(const float* q, const void* k_cache, const void* v_cache, int n_head, int n_head_kv,
+                          int head_dim, int n_pos, const int32_t* pos_dev, float scale, const float* gate,
+                          int gate_stride, float* out, int kv_type, hoard_stream stream) {
+    if (!q || !k_cache || !v_cache || !out || n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv ||
+        head_dim <= 0 || head_dim > 256 || 256 % head_dim || n_pos <= 0 || !kv_ok(kv_type) ||
+        (gate && gate_stride < head_dim))
+        return HOARD_EINVAL;
+    if (attention_smem(head_dim, n_pos) > 200 * 1024) return HOARD_EINVAL;
+    return st(launch_attention(q, k_cache, v_cache, kv_type == HOARD_TYPE_BF16, n_head, n_head_kv, head_dim, n_pos,
+                               pos_dev, scale, gate, gate_stride, out, (cudaStream_t)stream));
+}
+
+int hoard_hx_gdn_step(const float* qkv, const float* z, const float* ba, const float* conv_w, float* conv_ring,
+                      const float* dt_bias, const float* ssm_a, const float* norm_w, float* state, int n_v_heads,
+                      int n_k_heads, int d_state, int d_conv, float eps, int pos, const int32_t* pos_dev, float* out,
+                      hoard_stream stream) {
+    if (!qkv || !z || !ba || !conv_w || !conv_ring || !dt_bias || !ssm_a || !norm_w || !state || !out ||
+        d_state != 128 || n_k_heads <= 0 || n_v_heads <= 0 || n_v_heads % n_k_heads || d_conv < 1 || d_conv > 8 ||
+        (!pos_dev && pos < 0))
+        return HOARD_EINVAL;
+    return st(launch_gdn_step(qkv, z, ba, conv_w, conv_ring, dt_bias, ssm_a, norm_w, state, n_v_heads, n_k_heads,
+                              d_state, d_conv, eps, pos, pos_dev, out, (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -142,7 +142,8 @@ cudaError_t launch_rope_store(float* q, float* k, const float* v, int n_head, in
                               cudaStream_t s);
 size_t attention_smem(int hd, int n_pos);
 cudaError_t launch_attention(const float* q, const void* kc, const void* vc, bool kv_bf16, int n_head, int n_kv,
-                             int hd, int n_pos, const int32_t* pos_dev, float scale, float* out, cudaStream_t s);
+                             int hd, int n_pos, const int32_t* pos_dev, float scale, const float* gate, int gstride,
+                             float* out, cudaStream_t s);
 cudaError_t launch_argmax(const float* v, int n, int32_t* out, int32_t* pos, int seq_len, cudaStream_t s);
 cudaError_t launch_rmsnorm_q8(const float* x, int H, float eps, const float* w, int8_t* q, float* d, int* bs,
                               cudaStream_t s);
@@ -150,9 +151,15 @@ cudaError_t launch_qgemv_set(int n, const int* types, const uint8_t* const* w, c
                              const float* const* resid, float* const* y, const int8_t* xq, const float* xd,
                              const int* xbs, cudaStream_t s);
 cudaError_t launch_qknorm_rope_store(const float* q, const float* k, const float* v, const float* qn, const float* kn,
-                                     int mode, float eps, int n_head, int n_kv, int hd, int pos,
-                                     const int32_t* pos_dev, int max_ctx, float freq_base, float* q_out, void* kc,
-                                     void* vc, bool kv_bf16, cudaStream_t s);
+                                     int mode, float eps, int n_head, int n_kv, int hd, int q_stride, int rope_dim,
+                                     int pos, const int32_t* pos_dev, int max_ctx, float freq_base, float* q_out,
+                                     void* kc, void* vc, bool kv_bf16, cudaStream_t s);
+// Gated delta-net decode step of one token (d_state 128): causal conv over a ring of the last d_conv
+// inputs, the delta-rule state update and the gated RMSNorm; see kernels_harness.cu
+cudaError_t launch_gdn_step(const float* qkv, const float* z, const float* ba, const float* conv_w, float* ring,
+                            const float* dt_bias, const float* ssm_a, const float* norm_w, float* state, int Hv, int Hk,
+                            int d_state, int d_conv, float eps, int pos, const int32_t* pos_dev, float* out,
+                            cudaStream_t s);
 
 // ---- expert parallelism over NVLink peer memory ----
 // Every rank allocates one block with this layout (identical on all ranks, so a peer's field is its
@@ -160,36 +167,42 @@ cudaError_t launch_qknorm_rope_store(const float* q, const float* k, const float
 //   flags[64]   u32  barrier epochs, flags[s] written by rank s
 //   count[64]   i32  count[s]: rows rank s sent here this layer
 //   start[64]   i32  start[s]: where those rows begin in rank s's send order
-//   expert      i32  [G][cap] expert id of each received row, region s written by rank s
-//   rows        f16  [G][cap][H] received Q8_K-dequantised activation rows, region s written by rank s
+//   expert      i32  [G][cap] expert id of each received entry, region s written by rank s
+//   row_of      i32  [G][cap] the entry's token row within region s of `rows`
+//   rows        f16  [G][cap_rows][H] received Q8_K-dequantised token rows, one per (token, this rank)
+//                    however many of the token's experts this rank computes; region s written by rank s
 //   yback       f16  [cap][H] expert outputs of this rank's own entries, in its send order, written by
 //                    the ranks that computed them
 struct P2PLayout {
-    int64_t flags, count, start, expert, rows, yback, bytes;
+    int64_t flags, count, start, expert, row_of, rows, yback, bytes;
 };
-P2PLayout p2p_layout(int G, int cap, int H);
+P2PLayout p2p_layout(int G, int cap, int cap_rows, int H);
 
 struct P2PSend {
     uint8_t* const* peer;    // device [G] block base of every rank (own included)
     P2PLayout L;
-    int G, rank, cap, H, epr;
+    int G, rank, cap, cap_rows, H, epr;
 };
 // Send side of one layer: entries counted by destination rank, their starts and counts written into
-// every destination's count/start[rank], pos_of_entry[e] = the entry's send position, and each
-// entry's expert id and f16 row written straight into the destination's region `rank`.
+// every destination's count/start[rank], pos_of_entry[e] = the entry's send position, each entry's
+// expert id and token row written into the destination's region `rank`, and each token's f16 row
+// written once per destination rank that computes any of its experts (rowinfo[e] >= 0 marks the entry
+// that sends it; rcursor counts rows per destination).
 cudaError_t launch_p2p_send(const P2PSend& p, const int32_t* sel, int T, int k, const uint16_t* xq, int* counts,
-                            int* cursor, int* start, int* pos_of_entry, unsigned* err, cudaStream_t s, int* launches);
+                            int* cursor, int* start, int* rcursor, int* pos_of_entry, int* rowinfo, unsigned* err,
+                            cudaStream_t s, int* launches);
 // Barrier halves: signal writes `epoch` into every rank's flags[rank] (system-scope release after a
 // system fence); wait spins (bounded by timeout_ns, then error bit 2) until every flags[s] >= epoch.
 // A wait returns at once when bit 2 is already set.
 cudaError_t launch_p2p_signal(const P2PSend& p, uint32_t epoch, cudaStream_t s);
 cudaError_t launch_p2p_wait(const uint8_t* block, const P2PLayout& L, int G, uint32_t epoch,
                             unsigned long long timeout_ns, unsigned* err, cudaStream_t s);
-// Receive side: slot of every region row (-1 for the unused tail of a region, and for every row when
-// error bit 2 is set), then the tensor-core FFN whose down epilogue stores y of region row (s, i)
-// into rank s's yback[start[s] + i].
+// Receive side: slot of every region entry (-1 for the unused tail of a region, and for every entry
+// when error bit 2 is set) and its activation row (arow), then the tensor-core FFN whose down
+// epilogue stores y of region entry (s, i) into rank s's yback[start[s] + i].
 cudaError_t launch_p2p_experts(const Dims& d, const LayerWeights& lw, const Scratch& sc, const P2PSend& p,
-                               const uint8_t* block, int slot_base, int* slots, cudaStream_t s, int* launches);
+                               const uint8_t* block, int slot_base, int* slots, int* arow, cudaStream_t s,
+                               int* launches);
 
 // Persistent fused decode kernel over n_layers layers (T <= decode_max_tokens()).
 int decode_max_tokens();

@@ -99,51 +99,60 @@ __global__ void k_p2p_meta(P2PSend p, const int* __restrict__ counts, int* __res
     }
 }
 
-// Send positions (warp-aggregated cursors, as k_ep_scatter) and each entry's expert id into its
-// destination's region `rank`.
-__global__ void __launch_bounds__(256) k_p2p_scatter(P2PSend p, const int32_t* __restrict__ sel, int n,
+// One warp per token (lanes j < k: its entries): send positions (warp-aggregated cursors per
+// destination), each entry's expert id and token row into its destination's region `rank`; the first
+// lane of each destination group takes one row of that destination's region for the token, so a token
+// row crosses NVLink once per destination rank, not once per expert. Row order within a region is
+// arbitrary: every entry's arithmetic is independent of its neighbours.
+__global__ void __launch_bounds__(256) k_p2p_scatter(P2PSend p, const int32_t* __restrict__ sel, int T, int k,
                                                      int* __restrict__ cursor, const int* __restrict__ start,
-                                                     int* __restrict__ pos_of_entry) {
+                                                     int* __restrict__ rcursor, int* __restrict__ pos_of_entry,
+                                                     int* __restrict__ rowinfo) {
     const int lane = threadIdx.x & 31;
-    const int e0 = blockIdx.x * EP_CHUNK, e1 = min(n, e0 + EP_CHUNK);
-    for (int base = e0; base < e1; base += blockDim.x) {
-        const int e = base + threadIdx.x;
-        int dest = -1, ex = -1;
-        if (e < e1) {
-            ex = sel[e];
-            dest = (ex < 0 || ex >= p.G * p.epr) ? -1 : ex / p.epr;
-        }
-        const unsigned peers = __match_any_sync(0xFFFFFFFFu, dest);
-        const int leader = __ffs(peers) - 1;
-        int q = 0;
-        if (lane == leader && dest >= 0) q = atomicAdd(&cursor[dest], __popc(peers));
-        q = __shfl_sync(0xFFFFFFFFu, q, leader);
-        if (e < e1) {
-            if (dest >= 0) {
-                const int pos = q + __popc(peers & ((1u << lane) - 1u));
-                pos_of_entry[e] = pos;
-                const int64_t row = (int64_t)p.rank * p.cap + (pos - start[dest]);
-                reinterpret_cast<int32_t*>(p.peer[dest] + p.L.expert)[row] = ex;
-            } else {
-                pos_of_entry[e] = -1;
-            }
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= T) return;                                   // whole warps
+    const int64_t e = (int64_t)t * k + lane;
+    int dest = -1 - lane, ex = -1;                        // absent / rejected entries: groups of one
+    if (lane < k) {
+        ex = sel[e];
+        if (ex >= 0 && ex < p.G * p.epr) dest = ex / p.epr;
+    }
+    const unsigned peers = __match_any_sync(0xFFFFFFFFu, dest);
+    const int leader = __ffs(peers) - 1;
+    int q = 0, rr = 0;
+    if (lane == leader && dest >= 0) {
+        q = atomicAdd(&cursor[dest], __popc(peers));
+        rr = atomicAdd(&rcursor[dest], 1);
+    }
+    q = __shfl_sync(0xFFFFFFFFu, q, leader);
+    rr = __shfl_sync(0xFFFFFFFFu, rr, leader);
+    if (lane < k) {
+        if (dest >= 0) {
+            const int pos = q + __popc(peers & ((1u << lane) - 1u));
+            pos_of_entry[e] = pos;
+            const int64_t i = (int64_t)p.rank * p.cap + (pos - start[dest]);
+            reinterpret_cast<int32_t*>(p.peer[dest] + p.L.expert)[i] = ex;
+            reinterpret_cast<int32_t*>(p.peer[dest] + p.L.row_of)[i] = rr;
+            rowinfo[e] = lane == leader ? rr : -1;
+        } else {
+            pos_of_entry[e] = -1;
+            rowinfo[e] = -1;
         }
     }
 }
 
-// One warp per entry: its token's f16 row into region `rank` of the destination, 16-byte stores
-// (512 contiguous bytes per warp instruction over NVLink).
+// One warp per entry that sends its token's row (rowinfo >= 0): the f16 row into row rowinfo of the
+// destination's region `rank`, 16-byte stores (512 contiguous bytes per warp instruction over NVLink).
 __global__ void __launch_bounds__(256) k_p2p_gather(P2PSend p, const int32_t* __restrict__ sel,
                                                     const uint16_t* __restrict__ xq, int n, int k,
-                                                    const int* __restrict__ pos_of_entry,
-                                                    const int* __restrict__ start) {
+                                                    const int* __restrict__ rowinfo) {
     const int lane = threadIdx.x & 31;
     const int e = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (e >= n) return;
-    const int pos = pos_of_entry[e];
-    if (pos < 0) return;
+    const int rr = rowinfo[e];
+    if (rr < 0) return;
     const int dest = sel[e] / p.epr;
-    const int64_t row = (int64_t)p.rank * p.cap + (pos - start[dest]);
+    const int64_t row = (int64_t)p.rank * p.cap_rows + rr;
     const uint4* src = reinterpret_cast<const uint4*>(xq + (int64_t)(e / k) * p.H);
     uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.peer[dest] + p.L.rows) + row * p.H);
     for (int i = lane; i < p.H / 8; i += 32) dst[i] = src[i];
@@ -182,30 +191,33 @@ __global__ void k_p2p_wait(const uint8_t* block, int64_t flags_off, int G, uint3
 
 }  // namespace
 
-P2PLayout p2p_layout(int G, int cap, int H) {
+P2PLayout p2p_layout(int G, int cap, int cap_rows, int H) {
     auto al = [](int64_t v) { return (v + 255) / 256 * 256; };
     P2PLayout L{};
     L.flags = 0;
     L.count = 256;
     L.start = 512;
     L.expert = 1024;
-    L.rows = al(L.expert + (int64_t)G * cap * 4);
-    L.yback = al(L.rows + (int64_t)G * cap * H * 2);
+    L.row_of = al(L.expert + (int64_t)G * cap * 4);
+    L.rows = al(L.row_of + (int64_t)G * cap * 4);
+    L.yback = al(L.rows + (int64_t)G * cap_rows * H * 2);
     L.bytes = al(L.yback + (int64_t)cap * H * 2);
     return L;
 }
 
 cudaError_t launch_p2p_send(const P2PSend& p, const int32_t* sel, int T, int k, const uint16_t* xq, int* counts,
-                            int* cursor, int* start, int* pos_of_entry, unsigned* err, cudaStream_t s, int* launches) {
-    if (p.G < 1 || p.G > EP_MAX_RANKS) return cudaErrorInvalidValue;
+                            int* cursor, int* start, int* rcursor, int* pos_of_entry, int* rowinfo, unsigned* err,
+                            cudaStream_t s, int* launches) {
+    if (p.G < 1 || p.G > EP_MAX_RANKS || k < 1 || k > 32 || T > p.cap_rows) return cudaErrorInvalidValue;
     const int n = T * k;
     cudaError_t e = cudaMemsetAsync(counts, 0, (size_t)p.G * sizeof(int), s);
     if (e != cudaSuccess) return e;
+    if ((e = cudaMemsetAsync(rcursor, 0, (size_t)p.G * sizeof(int), s)) != cudaSuccess) return e;
     const int grid = (n + EP_CHUNK - 1) / EP_CHUNK;
     k_ep_count<<<grid, 256, 0, s>>>(sel, n, p.G, p.epr, counts, err);
     k_p2p_meta<<<1, 32, 0, s>>>(p, counts, cursor, start);
-    k_p2p_scatter<<<grid, 256, 0, s>>>(p, sel, n, cursor, start, pos_of_entry);
-    k_p2p_gather<<<(n + 7) / 8, 256, 0, s>>>(p, sel, xq, n, k, pos_of_entry, start);
+    k_p2p_scatter<<<(T + 7) / 8, 256, 0, s>>>(p, sel, T, k, cursor, start, rcursor, pos_of_entry, rowinfo);
+    k_p2p_gather<<<(n + 7) / 8, 256, 0, s>>>(p, sel, xq, n, k, rowinfo);
     if (launches) *launches += 4;
     return cudaGetLastError();
 }

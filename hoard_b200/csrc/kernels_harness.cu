@@ -143,7 +143,8 @@ template <typename KT>
 __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restrict__ q, const KT* __restrict__ kc,
                                                           const KT* __restrict__ vc, int n_head, int n_kv, int hd,
                                                           int n_pos, const int32_t* __restrict__ pos_dev,
-                                                          float scale, float* __restrict__ out) {
+                                                          float scale, const float* __restrict__ gate, int gstride,
+                                                          float* __restrict__ out) {
     extern __shared__ float sm[];
     const int cap = n_pos;                           // positions the shared memory was sized for
     if (pos_dev) n_pos = min(*pos_dev + 1, cap);
@@ -188,6 +189,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
     for (int i = threadIdx.x; i < hd; i += blockDim.x) {
         float acc = 0.f;
         for (int g = 0; g < G; ++g) acc += part[g * hd + i];
+        if (gate) acc *= sigmoid_f(gate[(int64_t)h * gstride + i]);
         out[(int64_t)h * hd + i] = acc;
     }
 }
@@ -221,7 +223,8 @@ template <typename KT>
 __global__ void __launch_bounds__(AV_THREADS) k_attention_v8(const float* __restrict__ q, const KT* __restrict__ kc,
                                                              const KT* __restrict__ vc, int n_head, int n_kv, int hd,
                                                              int n_pos, const int32_t* __restrict__ pos_dev,
-                                                             float scale, float* __restrict__ out) {
+                                                             float scale, const float* __restrict__ gate, int gstride,
+                                                             float* __restrict__ out) {
     extern __shared__ float sm[];
     const int cap = n_pos;
     if (pos_dev) n_pos = min(*pos_dev + 1, cap);
@@ -295,6 +298,7 @@ __global__ void __launch_bounds__(AV_THREADS) k_attention_v8(const float* __rest
     for (int i = threadIdx.x; i < hd; i += blockDim.x) {
         float acc = 0.f;
         for (int g = 0; g < PG; ++g) acc += part[g * hd + i];
+        if (gate) acc *= sigmoid_f(gate[(int64_t)h * gstride + i]);
         out[(int64_t)h * hd + i] = acc;
     }
 }
@@ -377,8 +381,8 @@ template <typename KT>
 __global__ void __launch_bounds__(128) k_qknorm_rope_store(const float* __restrict__ q, const float* __restrict__ k,
                                                            const float* __restrict__ v, const float* __restrict__ qn,
                                                            const float* __restrict__ kn, int mode, float eps,
-                                                           int n_head, int n_kv, int hd, int pos,
-                                                           const int32_t* __restrict__ pos_dev, int max_ctx,
+                                                           int n_head, int n_kv, int hd, int q_stride, int rope_dim,
+                                                           int pos, const int32_t* __restrict__ pos_dev, int max_ctx,
                                                            float theta_scale, float* __restrict__ q_out,
                                                            KT* __restrict__ kc, KT* __restrict__ vc) {
     __shared__ double redd[32];
@@ -390,36 +394,44 @@ __global__ void __launch_bounds__(128) k_qknorm_rope_store(const float* __restri
     const float* vec = isq ? q : k;
     const int nvec = (isq ? n_head : n_kv) * hd;
     const float* wn = isq ? qn : kn;
-    const int half = hd / 2, i = threadIdx.x;
+    const float* xh = vec + (int64_t)hh * (isq ? q_stride : hd);
+    const int rh = rope_dim / 2;
     float scale = 1.f;
     if (mode != 0) {
         const double ss = block_sum_d(mode == 1 ? sumsq_stride128(vec, nvec, threadIdx.x)
-                                                : sumsq_stride128(vec + (int64_t)hh * hd, hd, threadIdx.x), redd);
+                                                : sumsq_stride128(xh, hd, threadIdx.x), redd);
         scale = 1.0f / sqrtf((float)(ss / (mode == 1 ? nvec : hd)) + eps);
     }
-    if (i < half) {
-        const float* xh = vec + (int64_t)hh * hd;
-        float x0 = xh[i], x1 = xh[i + half];
-        if (mode == 1) {
-            x0 = (x0 * scale) * wn[hh * hd + i];
-            x1 = (x1 * scale) * wn[hh * hd + i + half];
-        } else if (mode == 2) {
-            x0 = (x0 * scale) * wn[i];
-            x1 = (x1 * scale) * wn[i + half];
-        }
-        float theta = (float)pos;
-        for (int u = 0; u < i; ++u) theta *= theta_scale;
-        const float c = cosf(theta), sn = sinf(theta);
-        const float r0 = x0 * c - x1 * sn, r1 = x0 * sn + x1 * c;
+    auto normed = [&](int j) {
+        const float x = xh[j];
+        if (mode == 1) return (x * scale) * wn[hh * hd + j];
+        if (mode == 2) return (x * scale) * wn[j];
+        return x;
+    };
+    auto put = [&](int j, float r) {
         if (isq) {
-            q_out[(int64_t)hh * hd + i] = r0;
-            q_out[(int64_t)hh * hd + i + half] = r1;
+            q_out[(int64_t)hh * hd + j] = r;
         } else {
             const int64_t o = ((int64_t)pos * n_kv + hh) * hd;
-            kv_put(kc + o + i, r0);
-            kv_put(kc + o + i + half, r1);
-            kv_put(vc + o + i, v[(int64_t)hh * hd + i]);
-            kv_put(vc + o + i + half, v[(int64_t)hh * hd + i + half]);
+            kv_put(kc + o + j, r);
+        }
+    };
+    // NEOX rotation of the first rope_dim values (pairs j, j + rope_dim/2, theta_j = pos * base^(-2j/rope_dim));
+    // values past rope_dim pass through
+    for (int j = threadIdx.x; j < hd; j += blockDim.x) {
+        if (j < rh) {
+            const float x0 = normed(j), x1 = normed(j + rh);
+            float theta = (float)pos;
+            for (int u = 0; u < j; ++u) theta *= theta_scale;
+            const float c = cosf(theta), sn = sinf(theta);
+            put(j, x0 * c - x1 * sn);
+            put(j + rh, x0 * sn + x1 * c);
+        } else if (j >= rope_dim) {
+            put(j, normed(j));
+        }
+        if (!isq) {
+            const int64_t o = ((int64_t)pos * n_kv + hh) * hd;
+            kv_put(vc + o + j, v[(int64_t)hh * hd + j]);
         }
     }
 }
@@ -516,18 +528,20 @@ cudaError_t launch_qgemv_set(int n, const int* types, const uint8_t* const* w, c
 }
 
 cudaError_t launch_qknorm_rope_store(const float* q, const float* k, const float* v, const float* qn, const float* kn,
-                                     int mode, float eps, int n_head, int n_kv, int hd, int pos,
-                                     const int32_t* pos_dev, int max_ctx, float freq_base, float* q_out, void* kc,
-                                     void* vc, bool kv_bf16, cudaStream_t s) {
-    if (hd / 2 > 128) return cudaErrorInvalidValue;
-    const float theta_scale = powf(freq_base, -2.0f / (float)hd);
+                                     int mode, float eps, int n_head, int n_kv, int hd, int q_stride, int rope_dim,
+                                     int pos, const int32_t* pos_dev, int max_ctx, float freq_base, float* q_out,
+                                     void* kc, void* vc, bool kv_bf16, cudaStream_t s) {
+    if (rope_dim < 2 || rope_dim > hd || rope_dim % 2 || q_stride < hd || (mode == 1 && q_stride != hd))
+        return cudaErrorInvalidValue;
+    const float theta_scale = powf(freq_base, -2.0f / (float)rope_dim);
     if (kv_bf16)
-        k_qknorm_rope_store<<<n_head + n_kv, 128, 0, s>>>(q, k, v, qn, kn, mode, eps, n_head, n_kv, hd, pos, pos_dev,
-                                                          max_ctx, theta_scale, q_out, (__nv_bfloat16*)kc,
-                                                          (__nv_bfloat16*)vc);
+        k_qknorm_rope_store<<<n_head + n_kv, 128, 0, s>>>(q, k, v, qn, kn, mode, eps, n_head, n_kv, hd, q_stride,
+                                                          rope_dim, pos, pos_dev, max_ctx, theta_scale, q_out,
+                                                          (__nv_bfloat16*)kc, (__nv_bfloat16*)vc);
     else
-        k_qknorm_rope_store<<<n_head + n_kv, 128, 0, s>>>(q, k, v, qn, kn, mode, eps, n_head, n_kv, hd, pos, pos_dev,
-                                                          max_ctx, theta_scale, q_out, (__half*)kc, (__half*)vc);
+        k_qknorm_rope_store<<<n_head + n_kv, 128, 0, s>>>(q, k, v, qn, kn, mode, eps, n_head, n_kv, hd, q_stride,
+                                                          rope_dim, pos, pos_dev, max_ctx, theta_scale, q_out,
+                                                          (__half*)kc, (__half*)vc);
     return cudaGetLastError();
 }
 
@@ -571,7 +585,8 @@ size_t attention_smem(int hd, int n_pos) {
 
 template <typename KT>
 static cudaError_t attention_t(const float* q, const void* kc, const void* vc, int n_head, int n_kv, int hd, int n_pos,
-                               const int32_t* pos_dev, float scale, float* out, cudaStream_t s) {
+                               const int32_t* pos_dev, float scale, const float* gate, int gstride, float* out,
+                               cudaStream_t s) {
     const size_t smem = attention_smem(hd, n_pos);
     const bool v8 = hd % 8 == 0;
     const void* fn = v8 ? (const void*)k_attention_v8<KT> : (const void*)k_attention<KT>;
@@ -581,17 +596,113 @@ static cudaError_t attention_t(const float* q, const void* kc, const void* vc, i
     }
     if (v8)
         k_attention_v8<KT><<<n_head, AV_THREADS, smem, s>>>(q, (const KT*)kc, (const KT*)vc, n_head, n_kv, hd, n_pos,
-                                                            pos_dev, scale, out);
+                                                            pos_dev, scale, gate, gstride, out);
     else
         k_attention<KT><<<n_head, ATT_THREADS, smem, s>>>(q, (const KT*)kc, (const KT*)vc, n_head, n_kv, hd, n_pos,
-                                                          pos_dev, scale, out);
+                                                          pos_dev, scale, gate, gstride, out);
     return cudaGetLastError();
 }
 
 cudaError_t launch_attention(const float* q, const void* kc, const void* vc, bool kv_bf16, int n_head, int n_kv,
-                             int hd, int n_pos, const int32_t* pos_dev, float scale, float* out, cudaStream_t s) {
-    return kv_bf16 ? attention_t<__nv_bfloat16>(q, kc, vc, n_head, n_kv, hd, n_pos, pos_dev, scale, out, s)
-                   : attention_t<__half>(q, kc, vc, n_head, n_kv, hd, n_pos, pos_dev, scale, out, s);
+                             int hd, int n_pos, const int32_t* pos_dev, float scale, const float* gate, int gstride,
+                             float* out, cudaStream_t s) {
+    return kv_bf16 ? attention_t<__nv_bfloat16>(q, kc, vc, n_head, n_kv, hd, n_pos, pos_dev, scale, gate, gstride, out, s)
+                   : attention_t<__half>(q, kc, vc, n_head, n_kv, hd, n_pos, pos_dev, scale, gate, gstride, out, s);
+}
+
+// ---- gated delta-net decode step (one token), one CTA of GDN_THREADS per value head h ----------------
+// qkv [conv_dim] = [q: Hk*D | k: Hk*D | v: Hv*D] projection outputs before the causal conv; the conv
+// keeps the last d_conv inputs in a ring (slot = position % d_conv; positions < 0 read as zero), the
+// weights ne = [d_conv, conv_dim] (tap t of channel c at c*d_conv + t, tap d_conv-1 = this token).
+// Value head h uses key head h / (Hv/Hk). With x = silu(conv): q, k L2-normalised (1/max(|x|, eps)),
+// q scaled by 1/sqrt(D); beta = sigmoid(b_h), decay = exp(softplus(a_h + dt_bias_h) * ssm_a_h) with
+// (b_h, a_h) from ba's per-key-head groups [Hv/Hk betas | Hv/Hk alphas];
+//   S <- decay * S;  delta = beta * (v - S^T k);  S <- S + k delta^T;  o = S^T q
+// (S[h] = [D key][D value] f32), then out_h = RMSNorm(o) * norm_w * silu(z_h).
+constexpr int GDN_D = 128;
+constexpr int GDN_THREADS = 256;
+__global__ void __launch_bounds__(GDN_THREADS) k_gdn_step(const float* __restrict__ qkv, const float* __restrict__ z,
+                                                          const float* __restrict__ ba, const float* __restrict__ conv_w,
+                                                          float* __restrict__ ring, const float* __restrict__ dt_bias,
+                                                          const float* __restrict__ ssm_a, const float* __restrict__ norm_w,
+                                                          float* __restrict__ state, int Hv, int Hk, int d_conv,
+                                                          float eps, int pos, const int32_t* __restrict__ pos_dev,
+                                                          float* __restrict__ out) {
+    __shared__ float sq[GDN_D], sk[GDN_D], sv[GDN_D], s_red[2][GDN_D];
+    __shared__ double redd[32];
+    if (pos_dev) pos = *pos_dev;
+    const int h = blockIdx.x, vpg = Hv / Hk, g = h / vpg, r = h - g * vpg;
+    const int conv_dim = 2 * Hk * GDN_D + Hv * GDN_D;
+    const int t = threadIdx.x;
+    // causal conv + silu of this head's q, k (threads 0..127) and v (threads 128..255) channels
+    auto conv = [&](int c) {
+        const float xn = qkv[c];
+        float acc = xn * conv_w[(int64_t)c * d_conv + d_conv - 1];
+        for (int u = 0; u < d_conv - 1; ++u) {               // tap u: position pos - (d_conv - 1) + u
+            const int p = pos - (d_conv - 1) + u;
+            if (p >= 0) acc += ring[(int64_t)(p % d_conv) * conv_dim + c] * conv_w[(int64_t)c * d_conv + u];
+        }
+        ring[(int64_t)(pos % d_conv) * conv_dim + c] = xn;    // read by the next d_conv - 1 positions
+        return silu_f(acc);
+    };
+    if (t < GDN_D) {
+        sq[t] = conv(g * GDN_D + t);
+        sk[t] = conv(Hk * GDN_D + g * GDN_D + t);
+    } else {
+        sv[t - GDN_D] = conv(2 * Hk * GDN_D + h * GDN_D + (t - GDN_D));
+    }
+    __syncthreads();
+    // L2 norms of q and k (double sums), q also scaled by 1/sqrt(D)
+    const double qq = block_sum_d(t < GDN_D ? (double)(sq[t] * sq[t]) : 0.0, redd);
+    const double kk = block_sum_d(t < GDN_D ? (double)(sk[t] * sk[t]) : 0.0, redd);
+    const float qs = (1.0f / fmaxf(sqrtf((float)qq), eps)) * (1.0f / sqrtf((float)GDN_D));
+    const float ks = 1.0f / fmaxf(sqrtf((float)kk), eps);
+    const float beta = sigmoid_f(ba[g * 2 * vpg + r]);
+    const float araw = ba[g * 2 * vpg + vpg + r] + dt_bias[h];
+    const float sp = araw > 20.f ? araw : log1pf(expf(araw));
+    const float decay = expf(sp * ssm_a[h]);
+    // thread = (value column j, half of the key rows)
+    const int j = t & (GDN_D - 1), half = t >> 7;
+    float* S = state + (int64_t)h * GDN_D * GDN_D;
+    float sreg[GDN_D / 2];
+    float kv = 0.f;
+#pragma unroll
+    for (int u = 0; u < GDN_D / 2; ++u) {
+        const int i = half * (GDN_D / 2) + u;
+        sreg[u] = S[(int64_t)i * GDN_D + j] * decay;
+        kv += sreg[u] * (sk[i] * ks);
+    }
+    s_red[half][j] = kv;
+    __syncthreads();
+    const float delta = beta * (sv[j] - (s_red[0][j] + s_red[1][j]));
+    __syncthreads();
+    float o = 0.f;
+#pragma unroll
+    for (int u = 0; u < GDN_D / 2; ++u) {
+        const int i = half * (GDN_D / 2) + u;
+        sreg[u] += (sk[i] * ks) * delta;
+        S[(int64_t)i * GDN_D + j] = sreg[u];
+        o += sreg[u] * (sq[i] * qs);
+    }
+    s_red[half][j] = o;
+    __syncthreads();
+    o = s_red[0][j] + s_red[1][j];
+    // gated RMSNorm over the head's D outputs
+    const double oo = block_sum_d(half == 0 ? (double)(o * o) : 0.0, redd);
+    if (half == 0) {
+        const float rs = 1.0f / sqrtf((float)(oo / GDN_D) + eps);
+        out[(int64_t)h * GDN_D + j] = ((o * rs) * norm_w[j]) * silu_f(z[(int64_t)h * GDN_D + j]);
+    }
+}
+
+cudaError_t launch_gdn_step(const float* qkv, const float* z, const float* ba, const float* conv_w, float* ring,
+                            const float* dt_bias, const float* ssm_a, const float* norm_w, float* state, int Hv, int Hk,
+                            int d_state, int d_conv, float eps, int pos, const int32_t* pos_dev, float* out,
+                            cudaStream_t s) {
+    if (d_state != GDN_D || Hk <= 0 || Hv <= 0 || Hv % Hk || d_conv < 1 || d_conv > 8) return cudaErrorInvalidValue;
+    k_gdn_step<<<Hv, GDN_THREADS, 0, s>>>(qkv, z, ba, conv_w, ring, dt_bias, ssm_a, norm_w, state, Hv, Hk, d_conv, eps,
+                                          pos, pos_dev, out);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_argmax(const float* v, int n, int32_t* out, int32_t* pos, int seq_len, cudaStream_t s) {

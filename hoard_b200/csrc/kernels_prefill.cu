@@ -309,6 +309,7 @@ struct TcArgs {
     const int2* items;      // (slot, M tile) per M tile
     const int* n_items;     // device count of M tiles (N blocks are expanded in the kernel)
     const __half* A;        // MODE 0: Q8_K-dequantised activations [T][H]; MODE 1: h [P][I] (sorted)
+    const int* a_row;       // MODE 0, optional: A row of each entry id (else entry id / KK)
     __half* hq;             // MODE 0 output [P][I] (sorted order)
     __half* y;              // MODE 1 output [entries][H] by entry id, f16 (clamped to the f16 range)
     // MODE 1 over peer memory (y_peer != null): entry r is row i = r % y_cap of source s = r / y_cap's
@@ -447,7 +448,8 @@ __global__ void __launch_bounds__(tc_threads(MODE), 1) k_tc_experts(TcArgs a) {
                 src[i] = nullptr;
                 if (r < nrows) {
                     const int sp = row0 + r;
-                    src[i] = MODE == 0 ? a.A + (int64_t)(a.perm[sp] / a.KK) * a.H : a.A + (int64_t)sp * a.I;
+                    src[i] = MODE == 0 ? a.A + (int64_t)(a.a_row ? a.a_row[a.perm[sp]] : a.perm[sp] / a.KK) * a.H
+                                         : a.A + (int64_t)sp * a.I;
                 }
             }
             for (int kc = 0; kc < KC; ++kc) {
@@ -756,32 +758,38 @@ cudaError_t launch_experts_tc_rows(const Dims& d, const LayerWeights& lw, const 
     return cudaSuccess;
 }
 
-// Expert-parallel receive side over peer memory: the G regions of this rank's block hold the rows
-// that every source sent (count[s] of them in region s), each tagged with its expert id.
+// Expert-parallel receive side over peer memory: the G regions of this rank's block hold the entries
+// that every source sent (count[s] of them in region s), each tagged with its expert id and the row of
+// its token in region s of `rows`.
 __global__ void __launch_bounds__(256) k_p2p_rx_slots(const uint8_t* __restrict__ block, P2PLayout L, int G, int cap,
-                                                      int e_lo, int epr, int slot_base, int n_slots,
-                                                      unsigned* err, int* __restrict__ slots) {
+                                                      int cap_rows, int e_lo, int epr, int slot_base, int n_slots,
+                                                      unsigned* err, int* __restrict__ slots, int* __restrict__ arow) {
     const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= (int64_t)G * cap) return;
     const int src = (int)(r / cap), i = (int)(r - (int64_t)src * cap);
     const int* count = reinterpret_cast<const int*>(block + L.count);
     const int32_t* expert = reinterpret_cast<const int32_t*>(block + L.expert);
-    int sl = -1;
+    const int32_t* row_of = reinterpret_cast<const int32_t*>(block + L.row_of);
+    int sl = -1, ar = 0;
     if (!(*(volatile unsigned*)err & 2u) && i < count[src]) {
-        const int ex = expert[r];
-        if (ex >= e_lo && ex < e_lo + epr && ex - e_lo + slot_base < n_slots)
+        const int ex = expert[r], ro = row_of[r];
+        if (ex >= e_lo && ex < e_lo + epr && ex - e_lo + slot_base < n_slots && ro >= 0 && ro < cap_rows) {
             sl = ex - e_lo + slot_base;
-        else
+            ar = src * cap_rows + ro;
+        } else {
             atomicOr(err, 1u);
+        }
     }
     slots[r] = sl;
+    arow[r] = ar;
 }
 
 cudaError_t launch_p2p_experts(const Dims& d, const LayerWeights& lw, const Scratch& sc, const P2PSend& p,
-                               const uint8_t* block, int slot_base, int* slots, cudaStream_t s, int* launches) {
+                               const uint8_t* block, int slot_base, int* slots, int* arow, cudaStream_t s,
+                               int* launches) {
     const int64_t n = (int64_t)p.G * p.cap;
-    k_p2p_rx_slots<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(block, p.L, p.G, p.cap, p.rank * p.epr, p.epr,
-                                                                slot_base, lw.n_slots, sc.sync, slots);
+    k_p2p_rx_slots<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(block, p.L, p.G, p.cap, p.cap_rows, p.rank * p.epr,
+                                                                p.epr, slot_base, lw.n_slots, sc.sync, slots, arow);
     int nl = 1;
     cudaError_t e;
     if ((e = launch_dispatch(slots, (int)n, 1, 1, lw.n_slots, sc, TC_M, s, &nl, true)) != cudaSuccess) return e;
@@ -798,10 +806,12 @@ cudaError_t launch_p2p_experts(const Dims& d, const LayerWeights& lw, const Scra
     a.n_items = sc.n_items;
     a.err = sc.sync;
     a.A = reinterpret_cast<const __half*>(block + p.L.rows);
+    a.a_row = arow;
     a.hq = reinterpret_cast<__half*>(sc.hq16);
     e = lw.gate_type == T_Q4K ? launch_tc<0, T_Q4K>(a, s) : launch_tc<0, T_Q6K>(a, s);
     if (e != cudaSuccess) return e;
     a.A = reinterpret_cast<const __half*>(sc.hq16);
+    a.a_row = nullptr;
     a.y_peer = p.peer;
     a.y_off = p.L.yback;
     a.y_start = reinterpret_cast<const int*>(block + p.L.start);

@@ -87,8 +87,12 @@ struct hoard_moe_ctx {
         std::vector<void*> opened;             // IPC mappings to close
         uint8_t** peer_dev = nullptr;          // device copy of bases
         uint32_t epoch = 0;                    // barrier epochs signalled so far
-        int* slots = nullptr;                  // [G*cap] slot of each received row
+        int cap_rows = 0;                      // token rows per region (max_tokens)
+        int* slots = nullptr;                  // [G*cap] slot of each received entry
+        int* arow = nullptr;                   // [G*cap] activation row of each received entry
         int* pos = nullptr;                    // [cap] send position of each (token, j) entry
+        int* rowinfo = nullptr;                // [cap] row of the entry's token in its destination, or -1
+        int* rcursor = nullptr;                // [64] rows sent per destination
         int* counts = nullptr;                 // [64] send counts per destination
         int* cursor = nullptr;                 // [64]
         int* start = nullptr;                  // [64] send offsets per destination
@@ -822,6 +826,7 @@ P2PSend p2p_args(const hoard_moe_ctx* c) {
     p.G = c->p2p.G;
     p.rank = c->p2p.rank;
     p.cap = c->p2p.cap;
+    p.cap_rows = c->p2p.cap_rows;
     p.H = c->dims.H;
     p.epr = c->p2p.epr;
     return p;
@@ -854,14 +859,18 @@ int hoard_moe_p2p_init(hoard_moe_ctx* c, int n_ranks, int rank, int experts_per_
     P.epr = experts_per_rank;
     P.slot_base = slot_base;
     P.cap = (int)cap;
-    P.L = p2p_layout(n_ranks, P.cap, c->dims.H);
+    P.cap_rows = c->desc.max_tokens;
+    P.L = p2p_layout(n_ranks, P.cap, P.cap_rows, c->dims.H);
     const int64_t R = cap * n_ranks;
     Scratch& x = P.rx;
     const int64_t NS2 = (int64_t)c->desc.n_slots + 2;
     int rc = dalloc(c, &P.block, P.L.bytes);
     if (rc == HOARD_OK) rc = dalloc(c, &P.peer_dev, 64 * sizeof(uint8_t*));
     if (rc == HOARD_OK) rc = dalloc(c, &P.slots, R * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &P.arow, R * 4);
     if (rc == HOARD_OK) rc = dalloc(c, &P.pos, cap * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &P.rowinfo, cap * 4);
+    if (rc == HOARD_OK) rc = dalloc(c, &P.rcursor, 64 * 4);
     if (rc == HOARD_OK) rc = dalloc(c, &P.counts, 64 * 4);
     if (rc == HOARD_OK) rc = dalloc(c, &P.cursor, 64 * 4);
     if (rc == HOARD_OK) rc = dalloc(c, &P.start, 64 * 4);
@@ -890,7 +899,7 @@ int hoard_moe_p2p_handle(hoard_moe_ctx* c, void* out) {
     HCHECK(c, cudaSetDevice(c->desc.device));
     P2PHandle h{};
     h.magic = kP2PMagic;
-    h.version = 1;
+    h.version = 2;
     h.G = c->p2p.G;
     h.rank = c->p2p.rank;
     h.cap = c->p2p.cap;
@@ -911,7 +920,7 @@ int hoard_moe_p2p_open(hoard_moe_ctx* c, const void* handles) {
     for (int s = 0; s < P.G; ++s) {
         P2PHandle h;
         std::memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)s * HOARD_P2P_HANDLE_BYTES, sizeof(h));
-        if (h.magic != kP2PMagic || h.version != 1 || h.G != P.G || h.rank != s || h.cap != P.cap ||
+        if (h.magic != kP2PMagic || h.version != 2 || h.G != P.G || h.rank != s || h.cap != P.cap ||
             h.H != c->dims.H || h.bytes != P.L.bytes)
             return fail(c, HOARD_EINVAL, "peer handle " + std::to_string(s) + " does not match this group");
     }
@@ -989,7 +998,8 @@ int hoard_moe_p2p_send(hoard_moe_ctx* c, int layer, const void* x, int T, int32_
     HCHECK(c, launch_q8_rows(c->sc.fx, T, c->dims.H, c->sc.xq16, s));
     int nl = 1;
     const P2PSend a = p2p_args(c);
-    HCHECK(c, launch_p2p_send(a, sel, T, c->dims.k, c->sc.xq16, P.counts, P.cursor, P.start, P.pos, c->sc.sync, s, &nl));
+    HCHECK(c, launch_p2p_send(a, sel, T, c->dims.k, c->sc.xq16, P.counts, P.cursor, P.start, P.rcursor, P.pos,
+                              P.rowinfo, c->sc.sync, s, &nl));
     HCHECK(c, launch_p2p_signal(a, ++P.epoch, s));
     c->launches += nl + 1;
     P.phase = 1;
@@ -1008,7 +1018,8 @@ int hoard_moe_p2p_compute(hoard_moe_ctx* c, hoard_stream stream) {
     const P2PSend a = p2p_args(c);
     HCHECK(c, launch_p2p_wait(P.block, P.L, P.G, P.epoch, P.timeout_ns, c->sc.sync, s));
     int nl = 1;
-    HCHECK(c, launch_p2p_experts(c->dims, layer_weights(c, P.layer), P.rx, a, P.block, P.slot_base, P.slots, s, &nl));
+    HCHECK(c, launch_p2p_experts(c->dims, layer_weights(c, P.layer), P.rx, a, P.block, P.slot_base, P.slots, P.arow, s,
+                                 &nl));
     HCHECK(c, launch_p2p_signal(a, ++P.epoch, s));
     c->launches += nl + 1;
     P.phase = 2;

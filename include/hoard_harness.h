@@ -90,6 +90,33 @@ int hoard_hx_qknorm_rope_store_at(const float* q, const float* k, const float* v
                                   const int32_t* pos, int max_ctx, float freq_base, float* q_out, void* k_cache,
                                   void* v_cache, int kv_type, hoard_stream stream);
 
+/* ---- the hybrid (Qwen3-Next) layer kinds, graph A of src/run_qwen35.cpp:472-553 ----
+ * qknorm_rope_store_ex: qknorm_rope_store with q heads q_stride floats apart (2 * head_dim for the
+ * fused q + gate projection, whose head h is [q (head_dim) | gate (head_dim)]) and NEOX RoPE on the
+ * first rope_dim values of each head only (the rest pass through); pos_dev != NULL reads the
+ * position from device memory (bounded by max_ctx), else pos is used.
+ * attention_ex: attention with n_pos positions, or min(*pos_dev + 1, n_pos) when pos_dev != NULL,
+ * and with gate != NULL the output of head h multiplied by sigmoid(gate[h * gate_stride + i]).
+ * gdn_step: one token through a gated delta-net layer (d_state 128): qkv [conv_dim] = [q: Hk*128 |
+ * k: Hk*128 | v: Hv*128] projection outputs, z [Hv*128] the output-gate projection, ba [2*Hv] the
+ * beta/alpha projection in per-key-head groups [Hv/Hk betas | Hv/Hk alphas], conv_w ne = [d_conv,
+ * conv_dim] (f32), conv_ring [d_conv][conv_dim] the last inputs (slot = position % d_conv; any
+ * contents at position 0), dt_bias / ssm_a [Hv], norm_w [128], state [Hv][128 key][128 value] f32
+ * (zero at the start of a sequence). Writes out [Hv*128] = RMSNorm(S^T q) * norm_w * silu(z) per value
+ * head and updates state and the ring. */
+int hoard_hx_qknorm_rope_store_ex(const float* q, const float* k, const float* v, const float* q_norm,
+                                  const float* k_norm, int mode, float eps, int n_head, int n_head_kv, int head_dim,
+                                  int q_stride, int rope_dim, int pos, const int32_t* pos_dev, int max_ctx,
+                                  float freq_base, float* q_out, void* k_cache, void* v_cache, int kv_type,
+                                  hoard_stream stream);
+int hoard_hx_attention_ex(const float* q, const void* k_cache, const void* v_cache, int n_head, int n_head_kv,
+                          int head_dim, int n_pos, const int32_t* pos_dev, float scale, const float* gate,
+                          int gate_stride, float* out, int kv_type, hoard_stream stream);
+int hoard_hx_gdn_step(const float* qkv, const float* z, const float* ba, const float* conv_w, float* conv_ring,
+                      const float* dt_bias, const float* ssm_a, const float* norm_w, float* state, int n_v_heads,
+                      int n_k_heads, int d_state, int d_conv, float eps, int pos, const int32_t* pos_dev, float* out,
+                      hoard_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

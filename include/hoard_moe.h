@@ -252,10 +252,12 @@ int hoard_moe_ep_combine(hoard_moe_ctx* ctx, const float* w, const int32_t* pos_
 
 /* ---- Expert parallelism over NVLink peer memory (no host round trip, no collective library) ----
  * The same sharding as above, with the exchange done by this library's own kernels: every rank owns
- * one symmetric block (receive regions [n_ranks][cap][n_embd] f16 with cap = max_tokens * k, the
- * per-source counts, and y_back [cap][n_embd]) that all ranks map. Per layer, on each rank's stream:
- *   hoard_moe_p2p_send    route; entries counted by destination; rows and expert ids stored straight
- *                         into each destination's region `rank`; signal
+ * one symmetric block (per source rank: the received entries' expert ids and token rows [cap],
+ * cap = max_tokens * k, and the token rows [max_tokens][n_embd] f16; the per-source counts; and
+ * y_back [cap][n_embd]) that all ranks map. Per layer, on each rank's stream:
+ *   hoard_moe_p2p_send    route; entries counted by destination; expert ids stored straight into each
+ *                         destination's region `rank`, and each token row once per destination rank
+ *                         that computes any of its experts; signal
  *   hoard_moe_p2p_compute wait for every rank's send; expert FFN (tensor cores) of the received rows,
  *                         the down epilogue storing each output row straight into its source rank's
  *                         y_back; signal
