@@ -457,40 +457,59 @@ def measure_c1_decode(device):
 
 
 C3_PROMPT, C3_GEN, C3_CTX = 512, 256, 4096
+C5_PROMPT, C5_GEN, C5_CTX = 1024, 256, 2048
 
 
 def measure_c3_decode(device):
     """C3: the Qwen3-30B-A3B-shape model (48 layers, GQA 32/4 x 128, per-head QK norm, theta 1e6,
     vocab 151936, 128 experts top-8 + renorm, I 768, Q4_K_M, 4096-slot bf16 KV cache), seeded weights,
-    every expert resident; a 512-token prompt, then 256 greedy tokens, each one replay of the captured
-    per-token graph (embedding, 48 x (attention + MoE layer), lm-head, argmax), timed with CUDA events
-    around the 256 replays. The MoE share is 48 single-layer MoE launches (the graph's own MoE calls)
-    timed alone on the same context."""
+    every expert resident; a 512-token prompt, then 256 greedy tokens."""
+    from hoard_b200 import harness as hx
+    return measure_whole_decode(device, hx.C3_QWEN3, C3_PROMPT, C3_GEN, C3_CTX, SEED + 303,
+                                "C3 decode tok/s (Qwen3-30B-A3B shape, whole model: 48 layers attention + MoE, lm-head)")
+
+
+def measure_c5_decode(device):
+    """C5: the Qwen3-Next-80B-A3B-shape hybrid model (48 layers: 36 gated delta-net + 12 gated attention
+    with 16 q / 2 KV heads of 256, RoPE on 64 dims; 512 experts top-10 + renorm, I 512, a gated shared
+    expert of 512; vocab 151936; Q4_K_M), seeded weights, every expert resident, bf16 KV cache for the
+    attention layers; a 1024-token prompt, then 256 greedy tokens."""
+    from hoard_b200 import harness as hx
+    return measure_whole_decode(device, hx.C5_QWEN3NEXT, C5_PROMPT, C5_GEN, C5_CTX, SEED + 505,
+                                "C5 decode tok/s (Qwen3-Next-80B-A3B shape, whole model: 36 delta-net + 12 gated "
+                                "attention layers, MoE with a shared expert, lm-head)")
+
+
+def measure_whole_decode(device, cfg, n_prompt, n_gen, ctx, seed, metric):
+    """Whole-model greedy decode of a seeded model: the prompt through the per-token step, then n_gen
+    tokens, each one replay of the captured per-token graph (embedding, the layers' attention or
+    delta-net blocks + MoE layers, lm-head, argmax), timed with CUDA events around the replays. The MoE
+    share is n_layer single-layer MoE launches (the graph's own MoE calls) timed alone on the same
+    context."""
     import torch
     from hoard_b200 import harness as hx
-    cfg = hx.C3_QWEN3
-    tensors = hx.seeded_tensors(cfg, seed=SEED + 303, device=device)
-    model = hx.DecodeModel(cfg, tensors, device=device.index, max_ctx=C3_CTX, kv_dtype=torch.bfloat16)
+    tensors = hx.seeded_tensors(cfg, seed=seed, device=device)
+    model = hx.DecodeModel(cfg, tensors, device=device.index, max_ctx=ctx, kv_dtype=torch.bfloat16)
     del tensors
     torch.cuda.empty_cache()
     try:
-        g = torch.Generator().manual_seed(SEED + 304)
-        prompt = torch.randint(0, cfg.n_vocab, (C3_PROMPT,), generator=g).tolist()
+        g = torch.Generator().manual_seed(seed + 1)
+        prompt = torch.randint(0, cfg.n_vocab, (n_prompt,), generator=g).tolist()
         graph = model.capture()
         model.prefill(prompt)
-        for _ in range(4):                                    # warm-up replays (positions 512..515)
+        for _ in range(4):                                    # warm-up replays
             graph.replay()
         model.prefill(prompt)
         torch.cuda.synchronize(device)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        for _ in range(C3_GEN):
+        for _ in range(n_gen):
             graph.replay()
         b.record()
         torch.cuda.synchronize(device)
         model.moe.sync_status()
         ms = a.elapsed_time(b)
-        toks = model.seq[C3_PROMPT:C3_PROMPT + C3_GEN].tolist()
+        toks = model.seq[n_prompt:n_prompt + n_gen].tolist()
         xb = torch.zeros(1, cfg.n_embd, device=device)
         xb.normal_()
         for il in range(cfg.n_layer):
@@ -503,13 +522,12 @@ def measure_c3_decode(device):
         b.record()
         torch.cuda.synchronize(device)
         moe_ms = a.elapsed_time(b) / 10
-        return {"metric": "C3 decode tok/s (Qwen3-30B-A3B shape, whole model: 48 layers attention + MoE, lm-head)",
-                "value": round(C3_GEN / ms * 1e3, 1), "unit": "tok/s", "ms_per_token": round(ms / C3_GEN, 4),
-                "prompt": C3_PROMPT, "generated": C3_GEN, "distinct_tokens": len(set(toks)),
-                "kv_cache": f"bf16, {C3_CTX} slots", "moe_ms_per_token": round(moe_ms, 4),
-                "moe_share": round(moe_ms / (ms / C3_GEN), 3),
-                "timing": "CUDA events around 256 replays of the captured per-token graph; the MoE share from 48 "
-                          "single-layer MoE launches timed alone"}
+        return {"metric": metric, "value": round(n_gen / ms * 1e3, 1), "unit": "tok/s",
+                "ms_per_token": round(ms / n_gen, 4), "prompt": n_prompt, "generated": n_gen,
+                "distinct_tokens": len(set(toks)), "kv_cache": f"bf16, {ctx} slots", "moe_ms_per_token": round(moe_ms, 4),
+                "moe_share": round(moe_ms / (ms / n_gen), 3),
+                "timing": f"CUDA events around {n_gen} replays of the captured per-token graph; the MoE share from "
+                          f"{cfg.n_layer} single-layer MoE launches timed alone"}
     finally:
         model.close()
 
@@ -736,6 +754,12 @@ def run_gpu(args, rank, world, local_rank):
     c3 = None
     if not args.no_c3 and rank == 0 and world == 1:
         c3 = measure_c3_decode(device)
+        torch.cuda.empty_cache()
+
+    c5 = None
+    if not args.no_c5 and rank == 0 and world == 1:
+        c5 = measure_c5_decode(device)
+        torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -789,6 +813,8 @@ def run_gpu(args, rank, world, local_rank):
             line["c1_decode"] = c1
         if c3:
             line["c3_decode"] = c3
+        if c5:
+            line["c5_decode"] = c5
         if cpu:
             line["cpu_baseline"] = cpu
         if phases:
@@ -815,6 +841,7 @@ def main():
     ap.add_argument("--no-lru", action="store_true", help="skip the LRU slot pool + RAM tier decode measurement")
     ap.add_argument("--no-c1", action="store_true", help="skip the C1 whole-model decode (device driver) measurement")
     ap.add_argument("--no-c3", action="store_true", help="skip the C3 whole-model decode (device driver) measurement")
+    ap.add_argument("--no-c5", action="store_true", help="skip the C5 whole-model (hybrid) decode measurement")
     ap.add_argument("--c2-only", default=None, help="comma-separated token counts: time only the isolated C2 layer")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="expert-parallel prefill exchange: the library's peer-memory kernels or NCCL all-to-all")

@@ -70,6 +70,10 @@ def _hx():
                                                  vp]
         L.hoard_hx_qknorm_rope_store_at.argtypes = [vp, vp, vp, vp, vp, i32, f32, i32, i32, i32, vp, i32, f32, vp, vp,
                                                    vp, i32, vp]
+        L.hoard_hx_qknorm_rope_store_ex.argtypes = [vp, vp, vp, vp, vp, i32, f32, i32, i32, i32, i32, i32, i32, vp, i32,
+                                                   f32, vp, vp, vp, i32, vp]
+        L.hoard_hx_attention_ex.argtypes = [vp, vp, vp, i32, i32, i32, i32, vp, f32, vp, i32, vp, i32, vp]
+        L.hoard_hx_gdn_step.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, i32, vp, vp, vp]
         _bound = True
     return L
 
@@ -98,13 +102,41 @@ class ModelConfig:
     eps: float
     qk_norm: str            # "full" (OLMoE: over the whole projection), "head" (Qwen3) or ""
     norm_topk: bool
+    # hybrid models (Qwen3-Next, src/run_qwen35.cpp:472-553): every full_attn_interval-th layer is gated
+    # full attention (fused q + sigmoid output gate, NEOX RoPE on the first rope_dim values of a head),
+    # the others gated delta-net; a gated shared expert of n_ff_shexp
+    n_ff_shexp: int = 0
+    full_attn_interval: int = 0     # 0: every layer is full attention
+    attn_gate: bool = False
+    rope_dim: int = 0               # 0: head_dim
+    ssm_d_state: int = 0            # delta-net head dim (key = value)
+    ssm_n_group: int = 0            # key heads
+    ssm_dt_rank: int = 0            # value heads
+    ssm_d_conv: int = 0             # causal conv taps
 
     def down_type(self, il: int) -> int:
         return Q6_K if il % 2 == 0 else Q4_K
 
+    def is_recurrent(self, il: int) -> bool:
+        return self.full_attn_interval > 0 and (il + 1) % self.full_attn_interval != 0
+
+    def ffn_norm_name(self) -> str:
+        return "post_attention_norm.weight" if self.full_attn_interval > 0 else "ffn_norm.weight"
+
+    @property
+    def n_rot(self) -> int:
+        return self.rope_dim or self.head_dim
+
+    @property
+    def conv_dim(self) -> int:
+        return (2 * self.ssm_n_group + self.ssm_dt_rank) * self.ssm_d_state
+
 
 C1_OLMOE = ModelConfig("olmoe", 16, 2048, 16, 16, 128, 64, 8, 1024, 50304, 1e4, 1e-5, "full", False)
 C3_QWEN3 = ModelConfig("qwen3moe", 48, 2048, 32, 4, 128, 128, 8, 768, 151936, 1e6, 1e-6, "head", True)
+C5_QWEN3NEXT = ModelConfig("qwen3next", 48, 2048, 16, 2, 256, 512, 10, 512, 151936, 1e7, 1e-6, "head", True,
+                           n_ff_shexp=512, full_attn_interval=4, attn_gate=True, rope_dim=64, ssm_d_state=128,
+                           ssm_n_group=16, ssm_dt_rank=32, ssm_d_conv=4)
 
 
 def seeded_tensors(cfg: ModelConfig, seed: int, device) -> dict:
@@ -127,22 +159,43 @@ def seeded_tensors(cfg: ModelConfig, seed: int, device) -> dict:
     for il in range(cfg.n_layer):
         b = f"blk.{il}."
         t[b + "attn_norm.weight"] = (F32, (H,), norm(H))
-        t[b + "attn_q.weight"] = (Q4_K, (H, nq), w(nq, H, Q4_K))
-        t[b + "attn_k.weight"] = (Q4_K, (H, nkv), w(nkv, H, Q4_K))
-        t[b + "attn_v.weight"] = (Q6_K, (H, nkv), w(nkv, H, Q6_K))
-        t[b + "attn_output.weight"] = (Q4_K, (nq, H), w(H, nq, Q4_K))
-        if cfg.qk_norm == "full":
-            t[b + "attn_q_norm.weight"] = (F32, (nq,), norm(nq))
-            t[b + "attn_k_norm.weight"] = (F32, (nkv,), norm(nkv))
-        elif cfg.qk_norm == "head":
-            t[b + "attn_q_norm.weight"] = (F32, (hd,), norm(hd))
-            t[b + "attn_k_norm.weight"] = (F32, (hd,), norm(hd))
-        t[b + "ffn_norm.weight"] = (F32, (H,), norm(H))
+        if cfg.is_recurrent(il):
+            D, Hk, Hv = cfg.ssm_d_state, cfg.ssm_n_group, cfg.ssm_dt_rank
+            cd, vd = cfg.conv_dim, Hv * D
+            t[b + "attn_qkv.weight"] = (Q4_K, (H, cd), w(cd, H, Q4_K))
+            t[b + "attn_gate.weight"] = (Q4_K, (H, vd), w(vd, H, Q4_K))
+            t[b + "ssm_ba.weight"] = (Q4_K, (H, 2 * Hv), w(2 * Hv, H, Q4_K))
+            t[b + "ssm_conv1d.weight"] = (F32, (cfg.ssm_d_conv, cd),
+                                          (torch.randn(cd, cfg.ssm_d_conv, generator=g, device=device) * 0.3).float())
+            t[b + "ssm_dt.bias"] = (F32, (Hv,), (torch.randn(Hv, generator=g, device=device) * 0.5).float())
+            # ssm_a = -exp(A_log), A_log ~ U(0, log 16)
+            t[b + "ssm_a"] = (F32, (Hv,), (-torch.exp(torch.rand(Hv, generator=g, device=device) * math.log(16.0))).float())
+            t[b + "ssm_norm.weight"] = (F32, (D,), norm(D))
+            t[b + "ssm_out.weight"] = (Q4_K, (vd, H), w(H, vd, Q4_K))
+        else:
+            nqp = 2 * nq if cfg.attn_gate else nq
+            t[b + "attn_q.weight"] = (Q4_K, (H, nqp), w(nqp, H, Q4_K))
+            t[b + "attn_k.weight"] = (Q4_K, (H, nkv), w(nkv, H, Q4_K))
+            t[b + "attn_v.weight"] = (Q6_K, (H, nkv), w(nkv, H, Q6_K))
+            t[b + "attn_output.weight"] = (Q4_K, (nq, H), w(H, nq, Q4_K))
+            if cfg.qk_norm == "full":
+                t[b + "attn_q_norm.weight"] = (F32, (nq,), norm(nq))
+                t[b + "attn_k_norm.weight"] = (F32, (nkv,), norm(nkv))
+            elif cfg.qk_norm == "head":
+                t[b + "attn_q_norm.weight"] = (F32, (hd,), norm(hd))
+                t[b + "attn_k_norm.weight"] = (F32, (hd,), norm(hd))
+        t[b + cfg.ffn_norm_name()] = (F32, (H,), norm(H))
         t[b + "ffn_gate_inp.weight"] = (F32, (H, E), (torch.randn(E, H, generator=g, device=device) * 0.02).float())
         dt = cfg.down_type(il)
         t[b + "ffn_gate_exps.weight"] = (Q4_K, (H, I, E), quant.synth_experts(E, I, H, Q4_K, seed * 1000 + 3 * il, device))
         t[b + "ffn_up_exps.weight"] = (Q4_K, (H, I, E), quant.synth_experts(E, I, H, Q4_K, seed * 1000 + 3 * il + 1, device))
         t[b + "ffn_down_exps.weight"] = (dt, (I, H, E), quant.synth_experts(E, H, I, dt, seed * 1000 + 3 * il + 2, device))
+        if cfg.n_ff_shexp:
+            Is = cfg.n_ff_shexp
+            t[b + "ffn_gate_shexp.weight"] = (Q4_K, (H, Is), w(Is, H, Q4_K))
+            t[b + "ffn_up_shexp.weight"] = (Q4_K, (H, Is), w(Is, H, Q4_K))
+            t[b + "ffn_down_shexp.weight"] = (Q6_K, (Is, H), w(H, Is, Q6_K))
+            t[b + "ffn_gate_inp_shexp.weight"] = (F32, (H,), (torch.randn(H, generator=g, device=device) * 0.02).float())
     return t
 
 
@@ -205,42 +258,75 @@ class DecodeModel:
         self.embd_type, self.embd = raw("token_embd.weight")
         self.out_norm = f32("output_norm.weight")
         self.out_type, self.out_w = plane("output.weight")
+        self.nqp = 2 * self.nq if cfg.attn_gate else self.nq      # q projection rows (+ the output gate)
+        hybrid = cfg.full_attn_interval > 0
+        self.gdn_vd = cfg.ssm_dt_rank * cfg.ssm_d_state
         self.layers = []
         for il in range(cfg.n_layer):
             b = f"blk.{il}."
-            L = {"attn_norm": f32(b + "attn_norm.weight"), "q": plane(b + "attn_q.weight"),
-                 "k": plane(b + "attn_k.weight"), "v": plane(b + "attn_v.weight"),
-                 "o": plane(b + "attn_output.weight")}
-            if cfg.qk_norm:
-                L["q_norm"], L["k_norm"] = f32(b + "attn_q_norm.weight"), f32(b + "attn_k_norm.weight")
-            L["qkv_types"] = _iarr([L[m][0] for m in ("q", "k", "v")])
-            L["qkv_w"] = _parr([L[m][1].data_ptr() for m in ("q", "k", "v")])
+            L = {"attn_norm": f32(b + "attn_norm.weight"), "recurrent": cfg.is_recurrent(il)}
+            if L["recurrent"]:
+                L.update({"qkv": plane(b + "attn_qkv.weight"), "z": plane(b + "attn_gate.weight"),
+                          "ba": plane(b + "ssm_ba.weight"), "conv_w": f32(b + "ssm_conv1d.weight"),
+                          "dt_bias": f32(b + "ssm_dt.bias"), "ssm_a": f32(b + "ssm_a"),
+                          "ssm_norm": f32(b + "ssm_norm.weight"), "o": plane(b + "ssm_out.weight")})
+                L["qkv_types"] = _iarr([L[m][0] for m in ("qkv", "z", "ba")])
+                L["qkv_w"] = _parr([L[m][1].data_ptr() for m in ("qkv", "z", "ba")])
+            else:
+                L.update({"q": plane(b + "attn_q.weight"), "k": plane(b + "attn_k.weight"),
+                          "v": plane(b + "attn_v.weight"), "o": plane(b + "attn_output.weight")})
+                if cfg.qk_norm:
+                    L["q_norm"], L["k_norm"] = f32(b + "attn_q_norm.weight"), f32(b + "attn_k_norm.weight")
+                L["qkv_types"] = _iarr([L[m][0] for m in ("q", "k", "v")])
+                L["qkv_w"] = _parr([L[m][1].data_ptr() for m in ("q", "k", "v")])
             self.layers.append(L)
         # the MoE layers: all experts resident, T = 1
         types = [tuple(tensors[f"blk.{il}.ffn_{m}_exps.weight"][0] for m in ("gate", "up", "down"))
                  for il in range(cfg.n_layer)]
+        sh_types = (Q4_K, Q4_K, Q6_K)
+        if cfg.n_ff_shexp:
+            sh_types = tuple(tensors[f"blk.0.ffn_{m}_shexp.weight"][0] for m in ("gate", "up", "down"))
         self.moe = moe.MoEContext(n_embd=H, n_expert=cfg.n_expert, n_expert_used=cfg.n_expert_used, n_ff=cfg.n_ff,
                                   n_layer=cfg.n_layer, norm_topk=cfg.norm_topk, eps=cfg.eps,
                                   gate_types=[t[0] for t in types], up_types=[t[1] for t in types],
-                                  down_types=[t[2] for t in types], max_tokens=MAX_BATCH, device=device)
+                                  down_types=[t[2] for t in types], n_ff_shexp=cfg.n_ff_shexp, shexp_types=sh_types,
+                                  max_tokens=MAX_BATCH, device=device)
         for il in range(cfg.n_layer):
             b = f"blk.{il}."
-            self.moe.set_router(il, f32(b + "ffn_gate_inp.weight").view(cfg.n_expert, H), f32(b + "ffn_norm.weight"))
+            self.moe.set_router(il, f32(b + "ffn_gate_inp.weight").view(cfg.n_expert, H), f32(b + cfg.ffn_norm_name()))
             mats = [raw(b + f"ffn_{m}_exps.weight")[1].view(cfg.n_expert, -1) for m in ("gate", "up", "down")]
             for e in range(cfg.n_expert):
                 self.moe.upload_expert(il, e, mats[0][e], mats[1][e], mats[2][e])
-        # activations, Q8_K workspaces, KV caches, token sequence
+            if cfg.n_ff_shexp:
+                self.moe.set_shared(il, *(raw(b + f"ffn_{m}_shexp.weight")[1] for m in ("gate", "up", "down")),
+                                    f32(b + "ffn_gate_inp_shexp.weight"))
+        # activations, Q8_K workspaces, KV caches, delta-net states, token sequence
         z = lambda n: torch.zeros(n, dtype=torch.float32, device=dev)
         self.x, self.x2, self.cur = z(H), z(H), z(H)
-        self.q, self.k, self.v, self.att = z(self.nq), z(self.nkv), z(self.nkv), z(self.nq)
+        self.q, self.k, self.v, self.att = z(self.nqp), z(self.nkv), z(self.nkv), z(self.nq)
         self.logits = z(cfg.n_vocab)
         self.q_rot = z(self.nq)
-        self.qkv_N = _iarr([self.nq, self.nkv, self.nkv])
+        self.qkv_N = _iarr([self.nqp, self.nkv, self.nkv])
         self.qkv_y = _parr([self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr()])
-        kq = max(H, self.nq)
+        kq = max(H, self.nq, self.gdn_vd)
         self.q8 = torch.zeros(int(_hx().hoard_hx_q8_bytes(kq)), dtype=torch.uint8, device=dev)
-        self.kc = torch.zeros(cfg.n_layer, max_ctx, self.nkv, dtype=kv_dtype, device=dev)
+        n_full = sum(1 for L in self.layers if not L["recurrent"])
+        self.kv_index = {}
+        for il, L in enumerate(self.layers):
+            if not L["recurrent"]:
+                self.kv_index[il] = len(self.kv_index)
+        self.kc = torch.zeros(max(1, n_full), max_ctx, self.nkv, dtype=kv_dtype, device=dev)
         self.vc = torch.zeros_like(self.kc)
+        if hybrid:
+            n_rec = cfg.n_layer - n_full
+            self.gdn_qkv, self.gdn_z, self.gdn_ba = z(cfg.conv_dim), z(self.gdn_vd), z(2 * cfg.ssm_dt_rank)
+            self.gdn_out = z(self.gdn_vd)
+            self.gdn_N = _iarr([cfg.conv_dim, self.gdn_vd, 2 * cfg.ssm_dt_rank])
+            self.gdn_y = _parr([self.gdn_qkv.data_ptr(), self.gdn_z.data_ptr(), self.gdn_ba.data_ptr()])
+            self.gdn_ring = torch.zeros(n_rec, cfg.ssm_d_conv, cfg.conv_dim, dtype=torch.float32, device=dev)
+            self.gdn_state = torch.zeros(n_rec, cfg.ssm_dt_rank, cfg.ssm_d_state, cfg.ssm_d_state, dtype=torch.float32,
+                                         device=dev)
+            self.rec_index = {il: i for i, il in enumerate(j for j, L in enumerate(self.layers) if L["recurrent"])}
         self.seq = torch.zeros(max_ctx + 1, dtype=torch.int32, device=dev)
         self.scratch_tok = torch.zeros(1, dtype=torch.int32, device=dev)
         self.pos_dev = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -280,34 +366,71 @@ class DecodeModel:
         _ok(hx.hoard_hx_argmax(_ptr(self.logits), c.n_vocab, _ptr(next_tok), s), "argmax")
 
     def _layer_attention(self, il, L, x, x2, hx, s, pos=None, bufs=None):
-        """Graph A's attention part of layer il: x2 = Wo att + x. pos None: the device position.
-        bufs: (q, k, v, q_rot, att, qkv_y) of one token of a batch (default: the step's own)."""
+        """Graph A's attention part of layer il: x2 = Wo att + x (or the delta-net block's output
+        projection + x). pos None: the device position. bufs: (q, k, v, q_rot, att, qkv_y) of one token of
+        a batch (default: the step's own)."""
         c = self.cfg
         H, hd = c.n_embd, c.head_dim
+        if L["recurrent"]:
+            self._layer_gdn(il, L, x, x2, hx, s, pos)
+            return
         q, k, v, q_rot, att, qkv_y = bufs or (self.q, self.k, self.v, self.q_rot, self.att, self.qkv_y)
+        kc, vc = self.kc[self.kv_index[il]], self.vc[self.kv_index[il]]
         _ok(hx.hoard_hx_rmsnorm_q8(_ptr(x), H, c.eps, _ptr(L["attn_norm"]), _ptr(self.q8), s), "rmsnorm_q8")
         _ok(hx.hoard_hx_gemv_multi(3, L["qkv_types"], L["qkv_w"], self.qkv_N, H, _ptr(self.q8), None, qkv_y, s),
             "gemv qkv")
         mode = QK_MODE[c.qk_norm]
         qn, kn = (L["q_norm"], L["k_norm"]) if mode else (None, None)
         scale = 1.0 / math.sqrt(hd)
-        if pos is None:
+        if c.attn_gate or c.n_rot != hd:
+            # fused q + gate rows ([q | gate] per head), partial rotary dims
+            qs = 2 * hd if c.attn_gate else hd
+            pd = None if pos is not None else _ptr(self.pos_dev)
+            p0 = pos if pos is not None else 0
+            _ok(hx.hoard_hx_qknorm_rope_store_ex(_ptr(q), _ptr(k), _ptr(v), _ptr(qn), _ptr(kn), mode, c.eps, c.n_head,
+                                                 c.n_head_kv, hd, qs, c.n_rot, p0, pd, self.max_ctx, c.freq_base,
+                                                 _ptr(q_rot), _ptr(kc), _ptr(vc), self.kv_type, s), "qk rope")
+            n_pos = pos + 1 if pos is not None else self.max_ctx
+            gate = _ptr(q) + 4 * hd if c.attn_gate else None
+            _ok(hx.hoard_hx_attention_ex(_ptr(q_rot), _ptr(kc), _ptr(vc), c.n_head, c.n_head_kv, hd, n_pos, pd, scale,
+                                         gate, qs, _ptr(att), self.kv_type, s), "attention")
+        elif pos is None:
             _ok(hx.hoard_hx_qknorm_rope_store_at(_ptr(q), _ptr(k), _ptr(v), _ptr(qn), _ptr(kn), mode, c.eps, c.n_head,
                                                  c.n_head_kv, hd, _ptr(self.pos_dev), self.max_ctx, c.freq_base,
-                                                 _ptr(q_rot), _ptr(self.kc[il]), _ptr(self.vc[il]), self.kv_type, s),
-                "qk rope")
-            _ok(hx.hoard_hx_attention_at(_ptr(q_rot), _ptr(self.kc[il]), _ptr(self.vc[il]), c.n_head, c.n_head_kv, hd,
+                                                 _ptr(q_rot), _ptr(kc), _ptr(vc), self.kv_type, s), "qk rope")
+            _ok(hx.hoard_hx_attention_at(_ptr(q_rot), _ptr(kc), _ptr(vc), c.n_head, c.n_head_kv, hd,
                                          _ptr(self.pos_dev), self.max_ctx, scale, _ptr(att), self.kv_type, s),
                 "attention")
         else:
             _ok(hx.hoard_hx_qknorm_rope_store(_ptr(q), _ptr(k), _ptr(v), _ptr(qn), _ptr(kn), mode, c.eps, c.n_head,
-                                              c.n_head_kv, hd, pos, c.freq_base, _ptr(q_rot), _ptr(self.kc[il]),
-                                              _ptr(self.vc[il]), self.kv_type, s), "qk rope")
-            _ok(hx.hoard_hx_attention(_ptr(q_rot), _ptr(self.kc[il]), _ptr(self.vc[il]), c.n_head, c.n_head_kv, hd,
-                                      pos + 1, scale, _ptr(att), self.kv_type, s), "attention")
+                                              c.n_head_kv, hd, pos, c.freq_base, _ptr(q_rot), _ptr(kc), _ptr(vc),
+                                              self.kv_type, s), "qk rope")
+            _ok(hx.hoard_hx_attention(_ptr(q_rot), _ptr(kc), _ptr(vc), c.n_head, c.n_head_kv, hd, pos + 1, scale,
+                                      _ptr(att), self.kv_type, s), "attention")
         _ok(hx.hoard_hx_quant_q8(_ptr(att), self.nq, _ptr(self.q8), s), "quant")
         ty, wo = L["o"]
         _ok(hx.hoard_hx_gemv(ty, _ptr(wo), H, self.nq, _ptr(self.q8), _ptr(x), _ptr(x2), s), "gemv")
+
+    def _layer_gdn(self, il, L, x, x2, hx, s, pos=None):
+        """A gated delta-net block (src/run_qwen35.cpp:508-553): x2 = W_out gdn(RMSNorm(x) * attn_norm) + x."""
+        c = self.cfg
+        H, r = c.n_embd, self.rec_index[il]
+        _ok(hx.hoard_hx_rmsnorm_q8(_ptr(x), H, c.eps, _ptr(L["attn_norm"]), _ptr(self.q8), s), "rmsnorm_q8")
+        _ok(hx.hoard_hx_gemv_multi(3, L["qkv_types"], L["qkv_w"], self.gdn_N, H, _ptr(self.q8), None, self.gdn_y, s),
+            "gemv qkv z ba")
+        _ok(hx.hoard_hx_gdn_step(_ptr(self.gdn_qkv), _ptr(self.gdn_z), _ptr(self.gdn_ba), _ptr(L["conv_w"]),
+                                 _ptr(self.gdn_ring[r]), _ptr(L["dt_bias"]), _ptr(L["ssm_a"]), _ptr(L["ssm_norm"]),
+                                 _ptr(self.gdn_state[r]), c.ssm_dt_rank, c.ssm_n_group, c.ssm_d_state, c.ssm_d_conv,
+                                 c.eps, pos if pos is not None else 0, None if pos is not None else _ptr(self.pos_dev),
+                                 _ptr(self.gdn_out), s), "gdn step")
+        _ok(hx.hoard_hx_quant_q8(_ptr(self.gdn_out), self.gdn_vd, _ptr(self.q8), s), "quant")
+        ty, wo = L["o"]
+        _ok(hx.hoard_hx_gemv(ty, _ptr(wo), H, self.gdn_vd, _ptr(self.q8), _ptr(x), _ptr(x2), s), "gemv")
+
+    def reset_state(self):
+        """Zeroes the delta-net states (the start of a sequence; src/run_qwen35.cpp:366-373)."""
+        if hasattr(self, "gdn_state"):
+            self.gdn_state.zero_()
 
     def _step_at(self, stream=None):
         """One decode step at the device position: token seq[pos] -> seq[pos + 1], pos += 1."""
@@ -330,6 +453,7 @@ class DecodeModel:
         """Runs the prompt tokens but the last through the step (their KV entries), then sets the
         device position to the last prompt token."""
         T = len(prompt)
+        self.reset_state()
         self.seq[:T].copy_(torch.tensor(prompt, dtype=torch.int32))
         for p in range(T - 1):
             self.step(p, self.scratch_tok, stream)
@@ -365,6 +489,8 @@ class DecodeModel:
         src/run_specloop.cpp:76-150."""
         c, hx, s = self.cfg, _hx(), _stream(stream)
         m, H, hd = len(tokens), c.n_embd, c.head_dim
+        if c.full_attn_interval > 0:
+            raise ValueError("batched forward of a hybrid (delta-net) model is not supported: its state is sequential")
         if not 1 <= m <= MAX_BATCH or base + m > self.max_ctx:
             raise ValueError("batch must be 1..MAX_BATCH tokens inside max_ctx")
         self.seq[base:base + m].copy_(torch.tensor(tokens, dtype=torch.int32))
@@ -452,6 +578,7 @@ class DecodeModel:
         n = len(tokens)
         if not 1 <= first < n or n > self.max_ctx:
             raise ValueError("need 1 <= first < len(tokens) <= max_ctx")
+        self.reset_state()
         self.seq[:n].copy_(torch.tensor(tokens, dtype=torch.int32))
         out = torch.empty(n - first, self.cfg.n_vocab, dtype=torch.float32, device=self.dev)
         for p in range(n - 1):
@@ -468,6 +595,7 @@ class DecodeModel:
         T = len(prompt)
         if T < 1 or T + n_gen > self.max_ctx:
             raise ValueError("prompt + n_gen must fit max_ctx")
+        self.reset_state()
         self.seq[:T].copy_(torch.tensor(prompt, dtype=torch.int32))
         for p in range(T + n_gen - 1):
             out = self.seq[p + 1:p + 2] if p >= T - 1 else self.scratch_tok

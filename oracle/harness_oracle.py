@@ -15,6 +15,18 @@ Follows src/run_moe_stream.cpp:295-472 step by step:
 Two choices follow the configuration rather than the reference (which keeps an f32 cache): the
 KV cache holds f16 (config C1 asks for an fp16 KV cache) or bf16 (config C3), and every position,
 the current one included, is read back from it.
+
+Hybrid models (Qwen3-Next, src/run_qwen35.cpp:472-553) add two layer kinds:
+  gated full attention  q projection rows [q | gate] per head, per-head QK RMSNorm, NEOX RoPE on
+                        the first rope_dim values of a head, att * sigmoid(gate)           :472-507
+  gated delta-net       qkv / z / ba projections; causal conv1d (kernel d_conv) over the last
+                        inputs, silu; q, k L2-normalised, key heads repeated to the value
+                        heads; beta = sigmoid(b), decay = exp(softplus(a + dt_bias) * ssm_a);
+                        the delta rule S <- decay S; S <- S + k (beta (v - S^T k))^T; o = S^T q
+                        (q scaled by 1/sqrt(d), the published recurrent form of gated delta-net);
+                        RMSNorm(o) * ssm_norm * silu(z); ssm_out                            :508-553
+ggml's fused gated_delta_net / ssm_conv kernels are not vendored in the reference, so this
+restatement of their published algorithm is not pinned against ggml output.
 """
 from __future__ import annotations
 
@@ -35,20 +47,70 @@ def rms_norm(x: np.ndarray, w: np.ndarray, rows: int, cols: int, eps: float) -> 
     return out.reshape(-1)
 
 
-def rope_neox(x: np.ndarray, n_heads: int, hd: int, pos: int, freq_base: float) -> np.ndarray:
+def rope_neox(x: np.ndarray, n_heads: int, hd: int, pos: int, freq_base: float, n_rot: int = 0) -> np.ndarray:
+    """NEOX RoPE of the first n_rot (default: all hd) values of each head; the rest pass through."""
+    n_rot = n_rot or hd
     x = x.reshape(n_heads, hd).astype(np.float32).copy()
-    theta_scale = np.float32(np.float32(freq_base) ** np.float32(-2.0 / hd))
-    half = hd // 2
+    theta_scale = np.float32(np.float32(freq_base) ** np.float32(-2.0 / n_rot))
+    half = n_rot // 2
     theta = np.empty(half, np.float32)
     t = np.float32(pos)
     for i in range(half):
         theta[i] = t
         t = np.float32(t * theta_scale)
     c, s = np.cos(theta).astype(np.float32), np.sin(theta).astype(np.float32)
-    x0, x1 = x[:, :half].copy(), x[:, half:].copy()
+    x0, x1 = x[:, :half].copy(), x[:, half:n_rot].copy()
     x[:, :half] = x0 * c - x1 * s
-    x[:, half:] = x0 * s + x1 * c
+    x[:, half:n_rot] = x0 * s + x1 * c
     return x.reshape(-1)
+
+
+def silu(x):
+    x = np.asarray(x, np.float32)
+    return (x / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
+
+
+def sigmoid(x):
+    x = np.asarray(x, np.float32)
+    return (np.float32(1.0) / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
+
+
+def gdn_step(qkv, z, ba, conv_w, hist, dt_bias, ssm_a, norm_w, S, Hv: int, Hk: int, D: int, d_conv: int, eps: float):
+    """One token through a gated delta-net block (see the module docstring). hist: the previous inputs
+    (newest last, at most d_conv - 1 used); S [Hv][D key][D value] f32 is updated in place.
+    Returns out [Hv*D] (before the output projection)."""
+    cd = qkv.size
+    W = np.asarray(conv_w, np.float32).reshape(cd, d_conv)
+    acc = (qkv * W[:, d_conv - 1]).astype(np.float32)
+    prev = hist[-(d_conv - 1):] if d_conv > 1 else []
+    for u in range(d_conv - 1):                    # tap u: position pos - (d_conv - 1) + u
+        j = u - (d_conv - 1 - len(prev))
+        if j >= 0:
+            acc = (acc + prev[j] * W[:, u]).astype(np.float32)
+    x = silu(acc)
+    vpg = Hv // Hk
+    out = np.empty(Hv * D, np.float32)
+    for h in range(Hv):
+        g, r = h // vpg, h % vpg
+        q = x[g * D:(g + 1) * D]
+        k = x[Hk * D + g * D:Hk * D + (g + 1) * D]
+        v = x[2 * Hk * D + h * D:2 * Hk * D + (h + 1) * D]
+        qs = np.float32(1.0 / max(np.sqrt(np.float32((q.astype(np.float64) ** 2).sum())), eps)) * np.float32(1.0 / np.sqrt(D))
+        ks = np.float32(1.0 / max(np.sqrt(np.float32((k.astype(np.float64) ** 2).sum())), eps))
+        beta = sigmoid(ba[g * 2 * vpg + r])
+        a = np.float32(ba[g * 2 * vpg + vpg + r] + dt_bias[h])
+        sp = a if a > 20 else np.float32(np.log1p(np.exp(a)))
+        decay = np.float32(np.exp(np.float32(sp * ssm_a[h])))
+        kn, qn = (k * ks).astype(np.float32), (q * qs).astype(np.float32)
+        Sh = (S[h] * decay).astype(np.float32)
+        kv = (Sh * kn[:, None]).sum(0, dtype=np.float32)
+        delta = (beta * (v - kv)).astype(np.float32)
+        Sh = (Sh + kn[:, None] * delta[None, :]).astype(np.float32)
+        S[h] = Sh
+        o = (Sh * qn[:, None]).sum(0, dtype=np.float32)
+        rs = np.float32(1.0 / np.sqrt(np.float32((o.astype(np.float64) ** 2).sum() / D) + np.float32(eps)))
+        out[h * D:(h + 1) * D] = ((o * rs) * norm_w) * silu(z[h * D:(h + 1) * D])
+    return out
 
 
 def bf16_round(x: np.ndarray) -> np.ndarray:
@@ -71,6 +133,10 @@ class OracleDecoder:
         self.kv = kv
         self.kc = np.zeros((cfg.n_layer, max_ctx, self.nkv), np.float16 if kv == "f16" else np.float32)
         self.vc = np.zeros_like(self.kc)
+        hybrid = getattr(cfg, "full_attn_interval", 0) > 0
+        self.hist = {il: [] for il in range(cfg.n_layer)} if hybrid else {}
+        self.S = {il: np.zeros((cfg.ssm_dt_rank, cfg.ssm_d_state, cfg.ssm_d_state), np.float32)
+                  for il in range(cfg.n_layer) if hybrid and cfg.is_recurrent(il)}
 
     def _mv(self, name, n_out, k_in, x):
         ty, _, w = self.t[name]
@@ -87,48 +153,79 @@ class OracleDecoder:
         rb = table.reshape(-1).size // c.n_vocab
         x = orc.dequant(ty, table.reshape(-1)[token * rb:(token + 1) * rb]) if ty in (12, 14) else \
             table.reshape(c.n_vocab, H)[token].astype(np.float32)
+        hybrid = getattr(c, "full_attn_interval", 0) > 0
         for il in range(c.n_layer):
             b = f"blk.{il}."
             cur = rms_norm(x, self._f(b + "attn_norm.weight"), 1, H, c.eps)
-            q = self._mv(b + "attn_q.weight", self.nq, H, cur)
-            k = self._mv(b + "attn_k.weight", self.nkv, H, cur)
-            v = self._mv(b + "attn_v.weight", self.nkv, H, cur)
-            if c.qk_norm == "full":
-                q = rms_norm(q, self._f(b + "attn_q_norm.weight"), 1, self.nq, c.eps)
-                k = rms_norm(k, self._f(b + "attn_k_norm.weight"), 1, self.nkv, c.eps)
-            elif c.qk_norm == "head":
-                q = rms_norm(q, self._f(b + "attn_q_norm.weight"), c.n_head, hd, c.eps)
-                k = rms_norm(k, self._f(b + "attn_k_norm.weight"), c.n_head_kv, hd, c.eps)
-            q = rope_neox(q, c.n_head, hd, pos, c.freq_base)
-            k = rope_neox(k, c.n_head_kv, hd, pos, c.freq_base)
-            if self.kv == "f16":
-                self.kc[il, pos] = k.astype(np.float16)
-                self.vc[il, pos] = v.astype(np.float16)
+            if hybrid and c.is_recurrent(il):
+                D, Hk, Hv = c.ssm_d_state, c.ssm_n_group, c.ssm_dt_rank
+                qkv = self._mv(b + "attn_qkv.weight", c.conv_dim, H, cur)
+                zz = self._mv(b + "attn_gate.weight", Hv * D, H, cur)
+                bav = self._mv(b + "ssm_ba.weight", 2 * Hv, H, cur)
+                o = gdn_step(qkv, zz, bav, self._f(b + "ssm_conv1d.weight"), self.hist[il], self._f(b + "ssm_dt.bias"),
+                             self._f(b + "ssm_a"), self._f(b + "ssm_norm.weight"), self.S[il], Hv, Hk, D, c.ssm_d_conv,
+                             c.eps)
+                self.hist[il].append(qkv.astype(np.float32))
+                ffn_inp = (self._mv(b + "ssm_out.weight", H, Hv * D, o) + x).astype(np.float32)
             else:
-                self.kc[il, pos] = bf16_round(k)
-                self.vc[il, pos] = bf16_round(v)
-            K = self.kc[il, :pos + 1].astype(np.float32).reshape(pos + 1, c.n_head_kv, hd)
-            V = self.vc[il, :pos + 1].astype(np.float32).reshape(pos + 1, c.n_head_kv, hd)
-            att = np.empty((c.n_head, hd), np.float32)
-            qh = q.reshape(c.n_head, hd)
-            scale = np.float32(1.0 / np.sqrt(hd))
-            grp = c.n_head // c.n_head_kv
-            for h in range(c.n_head):
-                s = (K[:, h // grp, :] @ qh[h]).astype(np.float32) * scale
-                e = np.exp(s - s.max()).astype(np.float32)
-                inv = np.float32(1.0 / e.astype(np.float64).sum())
-                att[h] = ((e * inv)[:, None] * V[:, h // grp, :]).sum(0, dtype=np.float32)
-            ffn_inp = (self._mv(b + "attn_output.weight", H, self.nq, att.reshape(-1)) + x).astype(np.float32)
+                gated = getattr(c, "attn_gate", False)
+                qg = self._mv(b + "attn_q.weight", 2 * self.nq if gated else self.nq, H, cur)
+                if gated:
+                    qg2 = qg.reshape(c.n_head, 2, hd)
+                    q, gate = qg2[:, 0, :].reshape(-1).copy(), qg2[:, 1, :].reshape(-1).copy()
+                else:
+                    q, gate = qg, None
+                k = self._mv(b + "attn_k.weight", self.nkv, H, cur)
+                v = self._mv(b + "attn_v.weight", self.nkv, H, cur)
+                if c.qk_norm == "full":
+                    q = rms_norm(q, self._f(b + "attn_q_norm.weight"), 1, self.nq, c.eps)
+                    k = rms_norm(k, self._f(b + "attn_k_norm.weight"), 1, self.nkv, c.eps)
+                elif c.qk_norm == "head":
+                    q = rms_norm(q, self._f(b + "attn_q_norm.weight"), c.n_head, hd, c.eps)
+                    k = rms_norm(k, self._f(b + "attn_k_norm.weight"), c.n_head_kv, hd, c.eps)
+                n_rot = getattr(c, "rope_dim", 0) or hd
+                q = rope_neox(q, c.n_head, hd, pos, c.freq_base, n_rot)
+                k = rope_neox(k, c.n_head_kv, hd, pos, c.freq_base, n_rot)
+                if self.kv == "f16":
+                    self.kc[il, pos] = k.astype(np.float16)
+                    self.vc[il, pos] = v.astype(np.float16)
+                else:
+                    self.kc[il, pos] = bf16_round(k)
+                    self.vc[il, pos] = bf16_round(v)
+                K = self.kc[il, :pos + 1].astype(np.float32).reshape(pos + 1, c.n_head_kv, hd)
+                V = self.vc[il, :pos + 1].astype(np.float32).reshape(pos + 1, c.n_head_kv, hd)
+                att = np.empty((c.n_head, hd), np.float32)
+                qh = q.reshape(c.n_head, hd)
+                scale = np.float32(1.0 / np.sqrt(hd))
+                grp = c.n_head // c.n_head_kv
+                for h in range(c.n_head):
+                    s = (K[:, h // grp, :] @ qh[h]).astype(np.float32) * scale
+                    e = np.exp(s - s.max()).astype(np.float32)
+                    inv = np.float32(1.0 / e.astype(np.float64).sum())
+                    att[h] = ((e * inv)[:, None] * V[:, h // grp, :]).sum(0, dtype=np.float32)
+                    if gate is not None:
+                        att[h] = att[h] * sigmoid(gate[h * hd:(h + 1) * hd])
+                ffn_inp = (self._mv(b + "attn_output.weight", H, self.nq, att.reshape(-1)) + x).astype(np.float32)
             gty = self.t[b + "ffn_gate_exps.weight"][0]
             uty = self.t[b + "ffn_up_exps.weight"][0]
             dty = self.t[b + "ffn_down_exps.weight"][0]
-            out, _, _, _, _ = orc.moe_layer(ffn_inp.reshape(1, H), self._f(b + "ffn_norm.weight"),
+            shared = None
+            if getattr(c, "n_ff_shexp", 0):
+                shared = {"I": c.n_ff_shexp, "gate_type": self.t[b + "ffn_gate_shexp.weight"][0],
+                          "up_type": self.t[b + "ffn_up_shexp.weight"][0],
+                          "down_type": self.t[b + "ffn_down_shexp.weight"][0],
+                          "gate": self.t[b + "ffn_gate_shexp.weight"][2].reshape(-1),
+                          "up": self.t[b + "ffn_up_shexp.weight"][2].reshape(-1),
+                          "down": self.t[b + "ffn_down_shexp.weight"][2].reshape(-1),
+                          "gate_inp": self._f(b + "ffn_gate_inp_shexp.weight")}
+            norm_name = c.ffn_norm_name() if hasattr(c, "ffn_norm_name") else "ffn_norm.weight"
+            out, _, _, _, _ = orc.moe_layer(ffn_inp.reshape(1, H), self._f(b + norm_name),
                                             self._f(b + "ffn_gate_inp.weight").reshape(c.n_expert, H),
                                             self.t[b + "ffn_gate_exps.weight"][2].reshape(c.n_expert, -1),
                                             self.t[b + "ffn_up_exps.weight"][2].reshape(c.n_expert, -1),
                                             self.t[b + "ffn_down_exps.weight"][2].reshape(c.n_expert, -1),
                                             H=H, E=c.n_expert, k=c.n_expert_used, I=c.n_ff, types=(gty, uty, dty),
-                                            renorm=c.norm_topk, eps=c.eps)
+                                            renorm=c.norm_topk, eps=c.eps, shared=shared)
             x = out.reshape(-1)
         r = rms_norm(x, self._f("output_norm.weight"), 1, H, c.eps)
         return self._mv("output.weight", c.n_vocab, H, r)
