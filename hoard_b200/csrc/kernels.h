@@ -218,6 +218,8 @@ cudaError_t launch_decode_persistent(const Dims& d, int KK, int sh_dt, const Lay
 // scratch: the array's device address on the current device, from decode_static_address
 bool decode_static_fits(const Dims& d, int KK);
 cudaError_t decode_static_address(void** out);
+// byte offset of the static scratch's error word (the same bits as Scratch::sync[0])
+size_t decode_static_error_offset();
 cudaError_t launch_decode_static(const Dims& d, int KK, int sh_dt, const LayerWeights* lws_dev, int n_layers,
                                  void* scratch, void* x_inout, int32_t* sel_out, float* w_out, cudaStream_t s);
 

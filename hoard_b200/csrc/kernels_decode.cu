@@ -1146,6 +1146,8 @@ bool decode_static_fits(const Dims& d, int KK) {
     return KK <= NOALLOC_MAX_K && d.I <= NOALLOC_MAX_I && d.E <= NOALLOC_MAX_E;
 }
 
+size_t decode_static_error_offset() { return NOALLOC_H_BYTES + NOALLOC_AMAX_BYTES + NOALLOC_RACC_BYTES; }
+
 cudaError_t launch_decode_static(const Dims& d, int KK, int sh_dt, const LayerWeights* lws_dev, int n_layers,
                                  void* scratch, void* x_inout, int32_t* sel_out, float* w_out, cudaStream_t s) {
     if (!decode_static_fits(d, KK) || !scratch) return cudaErrorInvalidValue;

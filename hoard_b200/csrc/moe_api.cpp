@@ -790,20 +790,35 @@ int hoard_moe_trace_layout(const hoard_moe_ctx* c, int* ctas, int* phases) {
     return HOARD_OK;
 }
 
-int hoard_moe_sync_status(hoard_moe_ctx* c, hoard_stream stream) {
-    if (!c) return HOARD_EINVAL;
+namespace {
+// waits for `stream`, reads and clears the device error word at `word`, and maps its bits to a status
+int read_error_word(hoard_moe_ctx* c, unsigned* word, hoard_stream stream) {
     HCHECK(c, cudaSetDevice(c->desc.device));
     HCHECK(c, cudaStreamSynchronize((cudaStream_t)stream));
     unsigned flags = 0;
-    HCHECK(c, cudaMemcpy(&flags, c->sc.sync, 4, cudaMemcpyDeviceToHost));
+    HCHECK(c, cudaMemcpy(&flags, word, 4, cudaMemcpyDeviceToHost));
     if (flags) {
         const unsigned zero = 0;
-        HCHECK(c, cudaMemcpy(c->sc.sync, &zero, 4, cudaMemcpyHostToDevice));
+        HCHECK(c, cudaMemcpy(word, &zero, 4, cudaMemcpyHostToDevice));
         if (flags & 2u) return fail(c, HOARD_ETIMEOUT, "a device-side wait gave up");
         if (flags & 4u) return fail(c, HOARD_EINVAL, "decode router sums left the fixed-point range");
         return fail(c, HOARD_EINVAL, "an expert or slot id was out of range (entries skipped)");
     }
     return HOARD_OK;
+}
+}  // namespace
+
+int hoard_moe_sync_status(hoard_moe_ctx* c, hoard_stream stream) {
+    if (!c) return HOARD_EINVAL;
+    return read_error_word(c, c->sc.sync, stream);
+}
+
+int hoard_moe_decode_noalloc_status(hoard_moe_ctx* c, hoard_stream stream) {
+    if (!c) return HOARD_EINVAL;
+    if (!c->noalloc_scratch) return fail(c, HOARD_ESTATE, "the static decode scratch could not be resolved on this device");
+    return read_error_word(c, reinterpret_cast<unsigned*>(static_cast<uint8_t*>(c->noalloc_scratch) +
+                                                           decode_static_error_offset()),
+                           stream);
 }
 
 // ---- expert parallelism over peer memory ----

@@ -33,7 +33,7 @@ EXPORTED = [
     "hoard_moe_create", "hoard_moe_destroy", "hoard_moe_set_router", "hoard_moe_upload_expert",
     "hoard_moe_set_shared", "hoard_moe_route", "hoard_moe_experts", "hoard_moe_layer", "hoard_moe_layers",
     "hoard_moe_sync_status", "hoard_moe_expert_bytes", "hoard_moe_launch_count", "hoard_moe_set_decode_impl",
-    "hoard_moe_set_trace", "hoard_moe_trace_layout", "hoard_moe_decode_noalloc",
+    "hoard_moe_set_trace", "hoard_moe_trace_layout", "hoard_moe_decode_noalloc", "hoard_moe_decode_noalloc_status",
     "hoard_moe_set_gemm_min_tokens", "hoard_moe_set_gemm_ctas", "hoard_moe_set_top_k", "hoard_moe_ep_reserve", "hoard_moe_ep_pack", "hoard_moe_ep_experts",
     "hoard_moe_ep_combine", "hoard_moe_ram_tier", "hoard_moe_ensure", "hoard_moe_residency_stats",
     "hoard_moe_p2p_init", "hoard_moe_p2p_handle", "hoard_moe_p2p_open", "hoard_moe_p2p_attach", "hoard_moe_p2p_close",
@@ -110,6 +110,7 @@ def lib() -> ctypes.CDLL:
         L.hoard_moe_p2p_layers.argtypes = [vp, i32, i32, vp, i32, vp, vp, vp]
         L.hoard_moe_set_trace.argtypes = [vp, vp, i64]
         L.hoard_moe_decode_noalloc.argtypes = [vp, i32, i32, vp, vp, vp, vp]
+        L.hoard_moe_decode_noalloc_status.argtypes = [vp, vp]
         L.hoard_moe_trace_layout.argtypes = [vp, ctypes.POINTER(i32), ctypes.POINTER(i32)]
         L.hoard_moe_last_error.argtypes = [vp]
         L.hoard_moe_last_error.restype = ctypes.c_char_p
@@ -370,6 +371,10 @@ class MoEContext:
         self._check(lib().hoard_moe_decode_noalloc(self._h, layer0, n_layers, _ptr(x_inout), _ptr(sel_out),
                                                    _ptr(w_out), _stream(stream)), "decode_noalloc")
         return x_inout
+
+    def decode_noalloc_status(self, stream=None):
+        """Waits for the stream; raises HoardError for errors recorded in the static scratch's error word."""
+        self._check(lib().hoard_moe_decode_noalloc_status(self._h, _stream(stream)), "decode_noalloc_status")
 
     def layers(self, layer0: int, n_layers: int, x_inout: torch.Tensor, sel_out=None, w_out=None, stream=None):
         T = x_inout.shape[0]

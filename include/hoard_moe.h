@@ -137,10 +137,14 @@ int hoard_moe_layers(hoard_moe_ctx* ctx, int layer0, int n_layers, void* x_inout
  *     must not be used across a device reset (cudaDeviceReset), which invalidates that address.
  *   - Every call on a device shares the one array; each call clears the parts that must start at
  *     zero. Calls whose kernels overlap on the GPU (other streams, other threads) race: serialise them.
- *   - A device-side wait that gives up is not reported back; use hoard_moe_layers where that matters.
+ *   - Device-side errors (an id out of range, a wait that gave up) go to the static array's own error
+ *     word, which the next call clears: read it with hoard_moe_decode_noalloc_status after a call.
  * x_inout: device [H] of resid_type; sel_out / w_out: NULL or [n_layers][k]. */
 int hoard_moe_decode_noalloc(hoard_moe_ctx* ctx, int layer0, int n_layers, void* x_inout, int32_t* sel_out,
                              float* w_out, hoard_stream stream);
+/* Waits for `stream`, then reports and clears the error word of the static decode scratch (the
+ * statuses of hoard_moe_sync_status); allocates nothing. */
+int hoard_moe_decode_noalloc_status(hoard_moe_ctx* ctx, hoard_stream stream);
 
 /* Waits for `stream`, then reports and clears the errors kernels recorded on the device:
  * HOARD_EINVAL for expert or slot ids out of range (those entries were skipped), HOARD_ETIMEOUT

@@ -69,6 +69,7 @@ def test_noalloc_calls_allocate_no_device_memory(model):
     alloc0 = torch.cuda.memory_allocated(DEV)
     for _ in range(5):
         ctx.decode_noalloc(0, N_LAYER, x)
+    ctx.decode_noalloc_status()            # the static array's error word: clear, read without allocating
     torch.cuda.synchronize(DEV)
     free1, _ = torch.cuda.mem_get_info(DEV)
     assert free1 == free0 and torch.cuda.memory_allocated(DEV) == alloc0
