@@ -24,6 +24,31 @@
 
 namespace hoard {
 
+// ---- programmatic dependent launch (the decode harness's chains of small kernels) ----------------
+// A kernel launched by launch_pdl may be scheduled while the previous kernel of its stream still runs:
+// it first lets its own successor be scheduled (launch_dependents), then waits until its predecessor has
+// completed and its memory is visible (wait), before it reads or writes anything. With a predecessor
+// that was not launched this way, or with a plain launch, both instructions return at once.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 constexpr int QK = 256;
 enum : int { T_F32 = 0, T_F16 = 1, T_Q4K = 12, T_Q6K = 14, T_BF16 = 30 };
 

@@ -545,6 +545,7 @@ cudaError_t launch_route(const Dims& d, const LayerWeights& lw, const void* x, i
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_quant_q8(const float* __restrict__ x, int K, int8_t* __restrict__ q,
                                                   float* __restrict__ dout, int* __restrict__ bs) {
+    pdl_enter();
     __shared__ float redf[32];
     const int nseg = K / QK;
     const int64_t r = blockIdx.x / nseg;       // one CTA per (row, 256-segment), 1-D grid
@@ -1102,8 +1103,7 @@ cudaError_t launch_rmsnorm_f32(const float* x, int rows, int cols, float eps, co
 
 cudaError_t launch_quant_q8(const float* x, int rows, int K, int8_t* q, float* d, int* bs, cudaStream_t s) {
     if (rows <= 0 || K <= 0 || K % QK) return cudaErrorInvalidValue;
-    k_quant_q8<<<(unsigned)((int64_t)(K / QK) * rows), 256, 0, s>>>(x, K, q, d, bs);
-    return cudaGetLastError();
+    return launch_pdl(k_quant_q8, (unsigned)((int64_t)(K / QK) * rows), 256, 0, s, x, K, q, d, bs);
 }
 
 cudaError_t launch_dispatch(const int32_t* slot_of_sel, int T, int k, int KK, int n_slots, const Scratch& sc,

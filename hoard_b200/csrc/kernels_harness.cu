@@ -17,6 +17,7 @@ namespace {
 __global__ void __launch_bounds__(256) k_embed(int type, const uint8_t* __restrict__ table, int H, int64_t n_vocab,
                                                const int32_t* __restrict__ tok, const int32_t* __restrict__ pos,
                                                float* __restrict__ out) {
+    pdl_enter();
     const int nb = H / QK;
     const int64_t token = tok[pos ? *pos : 0];
     const bool ok = token >= 0 && token < n_vocab;     // an id out of range gives a zero row
@@ -72,6 +73,7 @@ __global__ void __launch_bounds__(256) k_qgemv(const uint8_t* __restrict__ w, in
                                                const int8_t* __restrict__ xq, const float* __restrict__ xd,
                                                const int* __restrict__ xbs, const float* __restrict__ resid,
                                                float* __restrict__ y) {
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (n >= N) return;
@@ -95,6 +97,7 @@ __global__ void __launch_bounds__(256) k_rope_store(float* __restrict__ q, float
                                                     const float* __restrict__ v, int n_head, int n_kv, int hd,
                                                     int pos, const int32_t* __restrict__ pos_dev, int max_ctx,
                                                     float theta_scale, KT* __restrict__ kc, KT* __restrict__ vc) {
+    pdl_enter();
     if (pos_dev) pos = *pos_dev;
     if (pos < 0 || pos >= max_ctx) return;              // outside the cache: nothing is written
     const int half = hd / 2;
@@ -145,6 +148,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
                                                           int n_pos, const int32_t* __restrict__ pos_dev,
                                                           float scale, const float* __restrict__ gate, int gstride,
                                                           float* __restrict__ out) {
+    pdl_enter();
     extern __shared__ float sm[];
     const int cap = n_pos;                           // positions the shared memory was sized for
     if (pos_dev) n_pos = min(*pos_dev + 1, cap);
@@ -225,6 +229,7 @@ __global__ void __launch_bounds__(AV_THREADS) k_attention_v8(const float* __rest
                                                              int n_pos, const int32_t* __restrict__ pos_dev,
                                                              float scale, const float* __restrict__ gate, int gstride,
                                                              float* __restrict__ out) {
+    pdl_enter();
     extern __shared__ float sm[];
     const int cap = n_pos;
     if (pos_dev) n_pos = min(*pos_dev + 1, cap);
@@ -309,6 +314,7 @@ template <int NB>
 __global__ void __launch_bounds__(256) k_rmsnorm_q8(const float* __restrict__ x, int H, float eps,
                                                     const float* __restrict__ w, int8_t* __restrict__ q,
                                                     float* __restrict__ d, int* __restrict__ bs) {
+    pdl_enter();
     __shared__ double redd[32];
     __shared__ float samax[8][NB];
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -361,6 +367,7 @@ struct GemvSet {
 };
 __global__ void __launch_bounds__(256) k_qgemv_set(GemvSet g, int K, const int8_t* __restrict__ xq,
                                                    const float* __restrict__ xd, const int* __restrict__ xbs) {
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     int n = blockIdx.x * 8 + (threadIdx.x >> 5);
     int m = 0;
@@ -385,6 +392,7 @@ __global__ void __launch_bounds__(128) k_qknorm_rope_store(const float* __restri
                                                            int pos, const int32_t* __restrict__ pos_dev, int max_ctx,
                                                            float theta_scale, float* __restrict__ q_out,
                                                            KT* __restrict__ kc, KT* __restrict__ vc) {
+    pdl_enter();
     __shared__ double redd[32];
     if (pos_dev) pos = *pos_dev;
     if (pos < 0 || pos >= max_ctx) return;
@@ -439,6 +447,7 @@ __global__ void __launch_bounds__(128) k_qknorm_rope_store(const float* __restri
 // ---- argmax (first index of the maximum) of n floats: one CTA of 1024 threads ----
 __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ v, int n, int32_t* __restrict__ out,
                                                  int32_t* __restrict__ pos, int seq_len) {
+    pdl_enter();
     __shared__ float sv[32];
     __shared__ int si[32];
     float best = -INFINITY;
@@ -497,12 +506,12 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ v, in
 cudaError_t launch_rmsnorm_q8(const float* x, int H, float eps, const float* w, int8_t* q, float* d, int* bs,
                               cudaStream_t s) {
     switch (H / QK) {
-        case 1: k_rmsnorm_q8<1><<<1, 256, 0, s>>>(x, H, eps, w, q, d, bs); break;
-        case 2: k_rmsnorm_q8<2><<<1, 256, 0, s>>>(x, H, eps, w, q, d, bs); break;
-        case 4: k_rmsnorm_q8<4><<<1, 256, 0, s>>>(x, H, eps, w, q, d, bs); break;
-        case 8: k_rmsnorm_q8<8><<<1, 256, 0, s>>>(x, H, eps, w, q, d, bs); break;
-        case 16: k_rmsnorm_q8<16><<<1, 256, 0, s>>>(x, H, eps, w, q, d, bs); break;
-        case 32: k_rmsnorm_q8<32><<<1, 256, 0, s>>>(x, H, eps, w, q, d, bs); break;
+        case 1: return launch_pdl(k_rmsnorm_q8<1>, 1, 256, 0, s, x, H, eps, w, q, d, bs);
+        case 2: return launch_pdl(k_rmsnorm_q8<2>, 1, 256, 0, s, x, H, eps, w, q, d, bs);
+        case 4: return launch_pdl(k_rmsnorm_q8<4>, 1, 256, 0, s, x, H, eps, w, q, d, bs);
+        case 8: return launch_pdl(k_rmsnorm_q8<8>, 1, 256, 0, s, x, H, eps, w, q, d, bs);
+        case 16: return launch_pdl(k_rmsnorm_q8<16>, 1, 256, 0, s, x, H, eps, w, q, d, bs);
+        case 32: return launch_pdl(k_rmsnorm_q8<32>, 1, 256, 0, s, x, H, eps, w, q, d, bs);
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
@@ -523,8 +532,7 @@ cudaError_t launch_qgemv_set(int n, const int* types, const uint8_t* const* w, c
         rows += N[m];
     }
     g.n = n;
-    k_qgemv_set<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(g, K, xq, xd, xbs);
-    return cudaGetLastError();
+    return launch_pdl(k_qgemv_set, (unsigned)((rows + 7) / 8), 256, 0, s, g, K, xq, xd, xbs);
 }
 
 cudaError_t launch_qknorm_rope_store(const float* q, const float* k, const float* v, const float* qn, const float* kn,
@@ -535,20 +543,16 @@ cudaError_t launch_qknorm_rope_store(const float* q, const float* k, const float
         return cudaErrorInvalidValue;
     const float theta_scale = powf(freq_base, -2.0f / (float)rope_dim);
     if (kv_bf16)
-        k_qknorm_rope_store<<<n_head + n_kv, 128, 0, s>>>(q, k, v, qn, kn, mode, eps, n_head, n_kv, hd, q_stride,
-                                                          rope_dim, pos, pos_dev, max_ctx, theta_scale, q_out,
-                                                          (__nv_bfloat16*)kc, (__nv_bfloat16*)vc);
-    else
-        k_qknorm_rope_store<<<n_head + n_kv, 128, 0, s>>>(q, k, v, qn, kn, mode, eps, n_head, n_kv, hd, q_stride,
-                                                          rope_dim, pos, pos_dev, max_ctx, theta_scale, q_out,
-                                                          (__half*)kc, (__half*)vc);
-    return cudaGetLastError();
+        return launch_pdl(k_qknorm_rope_store<__nv_bfloat16>, n_head + n_kv, 128, 0, s, q, k, v, qn, kn, mode, eps,
+                          n_head, n_kv, hd, q_stride, rope_dim, pos, pos_dev, max_ctx, theta_scale, q_out,
+                          (__nv_bfloat16*)kc, (__nv_bfloat16*)vc);
+    return launch_pdl(k_qknorm_rope_store<__half>, n_head + n_kv, 128, 0, s, q, k, v, qn, kn, mode, eps, n_head, n_kv,
+                      hd, q_stride, rope_dim, pos, pos_dev, max_ctx, theta_scale, q_out, (__half*)kc, (__half*)vc);
 }
 
 cudaError_t launch_embed(int type, const uint8_t* table, int H, int64_t n_vocab, const int32_t* token,
                          const int32_t* pos, float* out, cudaStream_t s) {
-    k_embed<<<(H + 255) / 256, 256, 0, s>>>(type, table, H, n_vocab, token, pos, out);
-    return cudaGetLastError();
+    return launch_pdl(k_embed, (H + 255) / 256, 256, 0, s, type, table, H, n_vocab, token, pos, out);
 }
 
 cudaError_t launch_rmsnorm_rows(const float* x, int rows, int cols, float eps, const float* w, float* out,
@@ -559,8 +563,8 @@ cudaError_t launch_rmsnorm_rows(const float* x, int rows, int cols, float eps, c
 cudaError_t launch_qgemv(int type, const uint8_t* w, int N, int K, const int8_t* xq, const float* xd, const int* xbs,
                          const float* resid, float* y, cudaStream_t s) {
     const unsigned grid = (unsigned)((N + 7) / 8);
-    if (type == T_Q4K) k_qgemv<T_Q4K><<<grid, 256, 0, s>>>(w, N, K, xq, xd, xbs, resid, y);
-    else k_qgemv<T_Q6K><<<grid, 256, 0, s>>>(w, N, K, xq, xd, xbs, resid, y);
+    if (type == T_Q4K) return launch_pdl(k_qgemv<T_Q4K>, grid, 256, 0, s, w, N, K, xq, xd, xbs, resid, y);
+    return launch_pdl(k_qgemv<T_Q6K>, grid, 256, 0, s, w, N, K, xq, xd, xbs, resid, y);
     return cudaGetLastError();
 }
 
@@ -595,12 +599,10 @@ static cudaError_t attention_t(const float* q, const void* kc, const void* vc, i
         if (e != cudaSuccess) return e;
     }
     if (v8)
-        k_attention_v8<KT><<<n_head, AV_THREADS, smem, s>>>(q, (const KT*)kc, (const KT*)vc, n_head, n_kv, hd, n_pos,
-                                                            pos_dev, scale, gate, gstride, out);
-    else
-        k_attention<KT><<<n_head, ATT_THREADS, smem, s>>>(q, (const KT*)kc, (const KT*)vc, n_head, n_kv, hd, n_pos,
-                                                          pos_dev, scale, gate, gstride, out);
-    return cudaGetLastError();
+        return launch_pdl(k_attention_v8<KT>, n_head, AV_THREADS, smem, s, q, (const KT*)kc, (const KT*)vc, n_head,
+                          n_kv, hd, n_pos, pos_dev, scale, gate, gstride, out);
+    return launch_pdl(k_attention<KT>, n_head, ATT_THREADS, smem, s, q, (const KT*)kc, (const KT*)vc, n_head, n_kv, hd,
+                      n_pos, pos_dev, scale, gate, gstride, out);
 }
 
 cudaError_t launch_attention(const float* q, const void* kc, const void* vc, bool kv_bf16, int n_head, int n_kv,
@@ -628,6 +630,7 @@ __global__ void __launch_bounds__(GDN_THREADS) k_gdn_step(const float* __restric
                                                           float* __restrict__ state, int Hv, int Hk, int d_conv,
                                                           float eps, int pos, const int32_t* __restrict__ pos_dev,
                                                           float* __restrict__ out) {
+    pdl_enter();
     __shared__ float sq[GDN_D], sk[GDN_D], sv[GDN_D], s_red[2][GDN_D];
     __shared__ double redd[32];
     if (pos_dev) pos = *pos_dev;
@@ -700,14 +703,12 @@ cudaError_t launch_gdn_step(const float* qkv, const float* z, const float* ba, c
                             int d_state, int d_conv, float eps, int pos, const int32_t* pos_dev, float* out,
                             cudaStream_t s) {
     if (d_state != GDN_D || Hk <= 0 || Hv <= 0 || Hv % Hk || d_conv < 1 || d_conv > 8) return cudaErrorInvalidValue;
-    k_gdn_step<<<Hv, GDN_THREADS, 0, s>>>(qkv, z, ba, conv_w, ring, dt_bias, ssm_a, norm_w, state, Hv, Hk, d_conv, eps,
-                                          pos, pos_dev, out);
-    return cudaGetLastError();
+    return launch_pdl(k_gdn_step, Hv, GDN_THREADS, 0, s, qkv, z, ba, conv_w, ring, dt_bias, ssm_a, norm_w, state, Hv,
+                      Hk, d_conv, eps, pos, pos_dev, out);
 }
 
 cudaError_t launch_argmax(const float* v, int n, int32_t* out, int32_t* pos, int seq_len, cudaStream_t s) {
-    k_argmax<<<1, 1024, 0, s>>>(v, n, out, pos, seq_len);
-    return cudaGetLastError();
+    return launch_pdl(k_argmax, 1, 1024, 0, s, v, n, out, pos, seq_len);
 }
 
 }  // namespace hoard
