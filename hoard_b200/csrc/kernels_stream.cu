@@ -35,20 +35,23 @@
 namespace hoard {
 namespace {
 
+constexpr int SW_CTAS_PER_SM = 2;                        // resident CTAs per SM (each with its own pipeline)
 constexpr int SW_CONSUMERS = 8;                          // consumer warps
 constexpr int SW_THREADS = 32 * (SW_CONSUMERS + 1);      // + the producer warp
-constexpr int SW_SMEM = 227 * 1024;                      // shared memory per CTA (1 CTA / SM)
+constexpr int sw_smem(int ctas_per_sm) { return (ctas_per_sm == 1 ? 227 : 112) * 1024; }   // per CTA
+constexpr int SW_SMEM = sw_smem(SW_CTAS_PER_SM);
 constexpr int RT = 64;                                   // tiles per metadata round
 constexpr int MAX_ACT = 16;
 constexpr int SW_STATIC = RT * 16 + RT * MAX_ACT * 4 + 64;   // static shared memory of either kernel
-constexpr int SW_DYN = SW_SMEM - SW_STATIC - 1024;        // dynamic shared memory budget
+constexpr int sw_dyn(int ctas_per_sm) { return sw_smem(ctas_per_sm) - SW_STATIC - 1024; }  // dynamic budget
+constexpr int SW_DYN = sw_dyn(SW_CTAS_PER_SM);
 constexpr int NAB = 3;                                   // activation buffers (staged two tiles ahead)
 constexpr int GT_R = 16;                                 // gate rows (and up rows) per tile
-constexpr int GT_STAGES = 4;
-constexpr int GT_ACT = 8;                                // entries staged per gate/up tile
+constexpr int GT_STAGES = SW_CTAS_PER_SM == 1 ? 4 : 2;
+constexpr int GT_ACT = SW_CTAS_PER_SM == 1 ? 8 : 4;      // entries staged per gate/up tile
 constexpr int DT_R = 64;                                 // down rows per tile (8 warps x 8 rows)
-constexpr int DT_ACT = 16;                               // entries staged per down tile
-constexpr int TG = 4;                                    // entries per register group
+constexpr int DT_ACT = SW_CTAS_PER_SM == 1 ? 16 : 8;     // entries staged per down tile
+constexpr int TG = SW_CTAS_PER_SM == 1 ? 4 : 2;          // entries per register group
 static_assert(GT_ACT <= MAX_ACT && DT_ACT <= MAX_ACT, "staged entries");
 static_assert(DT_ACT % TG == 0, "token groups lie wholly inside or outside the staged entries");
 
@@ -319,7 +322,7 @@ __device__ __forceinline__ void gu_group(const GuArgs& a, const GuLane& L, const
     }
 }
 
-__global__ void __launch_bounds__(SW_THREADS, 1) k_gateup_sw(GuArgs a) {
+__global__ void __launch_bounds__(SW_THREADS, SW_CTAS_PER_SM) k_gateup_sw(GuArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
     uint8_t* abuf = sm + GT_STAGES * GU_STAGE;
     uint64_t* full = reinterpret_cast<uint64_t*>(abuf + NAB * GU_ABUF);
@@ -591,7 +594,7 @@ __device__ __forceinline__ void dn_group(const DnArgs& a, const DnLane& L, const
     }
 }
 
-__global__ void __launch_bounds__(SW_THREADS, 1) k_down_sw(DnArgs a) {
+__global__ void __launch_bounds__(SW_THREADS, SW_CTAS_PER_SM) k_down_sw(DnArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int S = a.stages;
     uint8_t* abuf = sm + S * a.stage_bytes;
@@ -693,13 +696,13 @@ __global__ void __launch_bounds__(SW_THREADS, 1) k_down_sw(DnArgs a) {
     }
 }
 
-int sw_grid() {
+int sw_grid(int ctas_per_sm = SW_CTAS_PER_SM) {
     static int sms[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
     if (sms[dev] == 0) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    return sms[dev];
+    return sms[dev] * ctas_per_sm;
 }
 
 }  // namespace
@@ -734,13 +737,20 @@ cudaError_t launch_down_sw(const Dims& d, const LayerWeights& lw, const Scratch&
     a.stage_bytes = DT_R * nb * 210;                     // sized for Q6_K (Q4_K tiles use 144 per block)
     a.aent = d.I + d.I / 4 + 16;
     const int fixed = NAB * DT_ACT * a.aent;
-    a.stages = (SW_DYN - fixed - 2 * 4 * 8) / a.stage_bytes;
+    // SW_CTAS_PER_SM CTAs per SM where two pipeline stages fit their share of shared memory (I <= 768
+    // with two CTAs), else one CTA per SM with the whole of it
+    int per_sm = SW_CTAS_PER_SM;
+    a.stages = (sw_dyn(per_sm) - fixed - 2 * 4 * 8) / a.stage_bytes;
+    if (a.stages < 2 && per_sm > 1) {
+        per_sm = 1;
+        a.stages = (sw_dyn(1) - fixed - 2 * 4 * 8) / a.stage_bytes;
+    }
     if (a.stages > 4) a.stages = 4;
     if (a.stages < 2) return cudaErrorInvalidValue;
     const int smem = a.stages * a.stage_bytes + fixed + 2 * a.stages * 8;
     cudaError_t e = cudaFuncSetAttribute(k_down_sw, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    k_down_sw<<<sw_grid(), SW_THREADS, smem, s>>>(a);
+    k_down_sw<<<sw_grid(per_sm), SW_THREADS, smem, s>>>(a);
     return cudaGetLastError();
 }
 
