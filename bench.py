@@ -293,6 +293,8 @@ def run_c2_only(args, local_rank):
                          resid_dtype=torch.float32, gate_types=[Q4_K], up_types=[Q4_K], down_types=[Q6_K],
                          max_tokens=max(Ts), device=local_rank)
     build_model(ctx, device, 1)
+    if args.gemm_min_tokens is not None:
+        ctx.set_gemm_min_tokens(args.gemm_min_tokens)
     g = torch.Generator(device=device)
     g.manual_seed(SEED + 4096)
     x0 = torch.randn(max(Ts), H, generator=g, device=device)
@@ -850,6 +852,8 @@ def main():
     ap.add_argument("--no-c3", action="store_true", help="skip the C3 whole-model decode (device driver) measurement")
     ap.add_argument("--no-c5", action="store_true", help="skip the C5 whole-model (hybrid) decode measurement")
     ap.add_argument("--c2-only", default=None, help="comma-separated token counts: time only the isolated C2 layer")
+    ap.add_argument("--gemm-min-tokens", type=int, default=None,
+                    help="with --c2-only: T at or above which the tensor-core path runs (0: never)")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="expert-parallel prefill exchange: the library's peer-memory kernels or NCCL all-to-all")
     ap.add_argument("--ep-chunks", type=int, default=2, help="expert-parallel prefill: micro-batches per layer "

@@ -48,7 +48,7 @@ struct hoard_moe_ctx {
     cudaEvent_t staging_free = nullptr;
     int64_t launches = 0;
     int decode_impl = 1;
-    int gemm_min_tokens = 64;          // T at or above which the tensor-core expert path runs (0 = never)
+    int gemm_min_tokens = 96;          // T at or above which the tensor-core expert path runs (0 = never)
     int routed_layer = -1;
     int routed_T = 0;
     LayerWeights* lw_dev = nullptr;    // device copy of every layer's LayerWeights (persistent kernel)

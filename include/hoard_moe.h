@@ -180,7 +180,9 @@ int hoard_moe_set_decode_impl(hoard_moe_ctx* ctx, int impl);
 
 /* Token count at or above which hoard_moe_experts / hoard_moe_layer(s) run the expert FFN as the
  * token-sorted grouped GEMM on the tensor cores (weights dequantised to f16 in shared memory, f32
- * accumulation) instead of the exact-integer grouped kernels; 0 = never. Default 64. The batched
+ * accumulation) instead of the exact-integer grouped kernels; 0 = never. Default 96 (C2 shape, measured:
+ * the weight-streaming kernels take 259 / 348 / 439 us at T = 64 / 96 / 128, the tensor-core path a
+ * flat ~345-356 us from T = 64 to 256: they cross at T ~ 96). The batched
  * counterpart of hoard's mul_mat_id path (src/run_specloop.cpp:125-140); hoard has no such switch,
  * its graph picks the backend's matmul kernel by batch size. */
 int hoard_moe_set_gemm_min_tokens(hoard_moe_ctx* ctx, int min_tokens);
