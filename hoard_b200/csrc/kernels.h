@@ -87,15 +87,26 @@ cudaError_t launch_route(const Dims& d, const LayerWeights& lw, const void* x, i
 // The grouped expert path for any T (fx given), adding into x_inout.
 cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const Scratch& sc, const float* fx,
                                    const int32_t* slot_of_sel, const float* w, void* x_inout, int T,
-                                   bool need_sh_gate, cudaStream_t s, int* launches);
+                                   bool need_sh_gate, cudaStream_t s, int* launches, bool prepared = false,
+                                   unsigned long long* stamp = nullptr);
+// Small batches (T <= 64, H 1024 or 2048, E <= 512), every expert resident: RMSNorm, router logits,
+// softmax + top-k, Q8_K of fx and the dispatch with its work list (tile_m entries per item) in one
+// kernel; the routing is identical to launch_route's. launch_experts_grouped(..., prepared = true)
+// then skips its own quantisation and dispatch.
+bool route_fused_supported(const Dims& d, int T);
+cudaError_t launch_route_fused(const Dims& d, const LayerWeights& lw, const Scratch& sc, const void* x, int T, int KK,
+                               int32_t* sel, float* w, int tile_m, cudaStream_t s, unsigned long long* stamp = nullptr);
 
 // Weight-streaming gate/up and down kernels of the grouped path (persistent, bulk-copy staged; the
 // dispatch's work list with one item per non-empty slot). Supported: gate/up Q4_K with H = 2048;
 // down Q4_K / Q6_K with I/256 <= 4 and H a multiple of 64.
 bool gateup_sw_supported(const Dims& d, const LayerWeights& lw);
 bool down_sw_supported(const Dims& d, const LayerWeights& lw);
-cudaError_t launch_gateup_sw(const Dims& d, const LayerWeights& lw, const Scratch& sc, int KK, cudaStream_t s);
-cudaError_t launch_down_sw(const Dims& d, const LayerWeights& lw, const Scratch& sc, cudaStream_t s);
+// stamp: optional {first start, last end} (%globaltimer, atomicMin / atomicMax) of the launch
+cudaError_t launch_gateup_sw(const Dims& d, const LayerWeights& lw, const Scratch& sc, int KK, cudaStream_t s,
+                             unsigned long long* stamp = nullptr);
+cudaError_t launch_down_sw(const Dims& d, const LayerWeights& lw, const Scratch& sc, cudaStream_t s,
+                           unsigned long long* stamp = nullptr);
 
 // Pieces shared by the grouped and tensor-core expert paths.
 cudaError_t launch_shared_gate(const float* fx, const float* gate_inp, int H, int T, float* out, cudaStream_t s);

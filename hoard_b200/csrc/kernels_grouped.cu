@@ -13,6 +13,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "block_ops.cuh"
+#include "async_copy.cuh"
 #include <algorithm>
 #include <type_traits>
 
@@ -187,13 +188,10 @@ template <> struct Vec4<__nv_bfloat16> {
     }
 };
 
+// RMS scale of one row by a 256-thread CTA: thread t holds values 4*(t + 256*j) + 0..3, j < VPT/4, in v
+// (zeros past H); the squares are summed per thread in j order and over the CTA by block_sum_d.
 template <typename R, int VPT>
-__global__ void __launch_bounds__(256) k_rmsnorm(const R* __restrict__ x, int H, float eps,
-                                                 const float* __restrict__ w_norm, float* __restrict__ fx) {
-    __shared__ double redd[32];
-    const int64_t t = blockIdx.x;
-    const R* xr = x + t * H;
-    float v[VPT];
+__device__ __forceinline__ float rms_row_scale(const R* __restrict__ xr, int H, float eps, float* v, double* redd) {
 #pragma unroll
     for (int j = 0; j < VPT / 4; ++j) {
         const int i = 4 * (threadIdx.x + 256 * j);
@@ -205,7 +203,17 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const R* __restrict__ x, int H,
     for (int j = 0; j < VPT; ++j) ss += (double)(v[j] * v[j]);
     ss = block_sum_d(ss, redd);
     const float mean = (float)(ss / H);
-    const float scale = 1.0f / sqrtf(mean + eps);
+    return 1.0f / sqrtf(mean + eps);
+}
+
+template <typename R, int VPT>
+__global__ void __launch_bounds__(256) k_rmsnorm(const R* __restrict__ x, int H, float eps,
+                                                 const float* __restrict__ w_norm, float* __restrict__ fx) {
+    pdl_enter();
+    __shared__ double redd[32];
+    const int64_t t = blockIdx.x;
+    float v[VPT];
+    const float scale = rms_row_scale<R, VPT>(x + t * H, H, eps, v, redd);
 #pragma unroll
     for (int j = 0; j < VPT / 4; ++j) {
         const int i = 4 * (threadIdx.x + 256 * j);
@@ -221,16 +229,17 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const R* __restrict__ x, int H,
 template <typename R>
 cudaError_t launch_rmsnorm_rows(const R* x, int rows, int H, float eps, const float* w, float* out, cudaStream_t s) {
     if (rows <= 0 || H <= 0 || H % 4 || H > 256 * RMS_MAXV) return cudaErrorInvalidValue;
-    if (H <= 1024) k_rmsnorm<R, 4><<<rows, 256, 0, s>>>(x, H, eps, w, out);
-    else if (H <= 2048) k_rmsnorm<R, 8><<<rows, 256, 0, s>>>(x, H, eps, w, out);
-    else if (H <= 4096) k_rmsnorm<R, 16><<<rows, 256, 0, s>>>(x, H, eps, w, out);
-    else k_rmsnorm<R, 32><<<rows, 256, 0, s>>>(x, H, eps, w, out);
+    if (H <= 1024) launch_pdl(k_rmsnorm<R, 4>, rows, 256, 0, s, x, H, eps, w, out);
+    else if (H <= 2048) launch_pdl(k_rmsnorm<R, 8>, rows, 256, 0, s, x, H, eps, w, out);
+    else if (H <= 4096) launch_pdl(k_rmsnorm<R, 16>, rows, 256, 0, s, x, H, eps, w, out);
+    else launch_pdl(k_rmsnorm<R, 32>, rows, 256, 0, s, x, H, eps, w, out);
     return cudaGetLastError();
 }
 
 // grid (ceil(T/32), ceil(E/128), ksplit); CTA z covers K range [z*klen, (z+1)*klen)
 __global__ void __launch_bounds__(256) k_router_logits(const float* __restrict__ fx, const float* __restrict__ w_router,
                                                        int T, int H, int E, int klen, double* __restrict__ part) {
+    pdl_enter();
     __shared__ __align__(16) float sf[RL_KC][RL_TT];          // fx chunk, k-major
     __shared__ __align__(16) float sw[RL_KC][RL_EB + 4];      // router chunk, k-major (padded rows)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -298,6 +307,67 @@ __global__ void __launch_bounds__(256) k_router_logits(const float* __restrict__
     }
 }
 
+// Softmax over the E logits of one token (max subtracted, double sum), then k rounds of arg-max over
+// (probability desc, id asc) and the optional renormalisation (sequential f32 sum in rank order, clamped
+// at 6.103515625e-5); one warp, E <= 32 * NV. Lanes < k write rank `lane` to sel_t / w_t.
+template <int NV>
+__device__ __forceinline__ void route_topk_row(const float* lgrow, int E, int k, int renorm, int lane,
+                                               int32_t* __restrict__ sel_t, float* __restrict__ w_t) {
+    float p[NV];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int e = lane + 32 * i;
+        p[i] = e < E ? lgrow[e] : -INFINITY;
+        m = fmaxf(m, p[i]);
+    }
+    m = warp_max(m);
+    double ssum = 0.0;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        if (lane + 32 * i < E) {
+            p[i] = expf(p[i] - m);
+            ssum += (double)p[i];
+        }
+    }
+    ssum = warp_sum(ssum);
+    const float inv = (float)(1.0 / ssum);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) p[i] = lane + 32 * i < E ? p[i] * inv : -1.f;
+    // k rounds of arg-max over (p desc, id asc): each lane's best value (lowest id among equal p), then
+    // the warp's largest key (an order-preserving unsigned image of p) and, among lanes holding it, the
+    // lowest id (two redux instructions); the winner's entry is retired with p = -1
+    float my_w = 0.f, wsum = 0.f;
+    int my_e = 0;
+    for (int r = 0; r < k; ++r) {
+        float bp = -1.f;
+        int be = 0x7FFFFFFF;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int e = lane + 32 * i;
+            if (p[i] > bp || (p[i] == bp && e < be)) { bp = p[i]; be = e; }
+        }
+        const unsigned u = __float_as_uint(bp);
+        const unsigned key = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+        const unsigned M = __reduce_max_sync(0xFFFFFFFFu, key);
+        const int W = (int)__reduce_min_sync(0xFFFFFFFFu, key == M ? (unsigned)be : 0xFFFFFFFFu);
+        const float wp = __uint_as_float((M & 0x80000000u) ? (M & 0x7FFFFFFFu) : ~M);
+#pragma unroll
+        for (int i = 0; i < NV; ++i)
+            if (lane + 32 * i == W) p[i] = -1.f;
+        wsum += wp;                                   // sequential f32 sum in rank order
+        if (lane == r) { my_w = wp; my_e = W; }
+    }
+    if (renorm) {
+        if (wsum < 6.103515625e-5f) wsum = 6.103515625e-5f;
+        my_w /= wsum;
+    }
+    if (lane < k) {
+        sel_t[lane] = my_e;
+        w_t[lane] = my_w;
+    }
+}
+
 // TT tokens per CTA (1 at small T, so that the split sums of a batch of a few tokens are spread over
 // many CTAs, with TOPK_SMALL_THREADS threads; 8 at large T, 256 threads): the CTA's threads sum the K
 // splits into shared memory, then one warp per token does softmax + top-k (E <= 1024). Where the
@@ -313,6 +383,7 @@ template <int NV>
 __global__ void __launch_bounds__(TOPK_SMALL_THREADS) k_route_topk(const double* __restrict__ part, int ksplit, int T,
                                                                    int E, int k, int renorm, int32_t* __restrict__ sel,
                                                                    float* __restrict__ w) {
+    pdl_enter();
     __shared__ float lg[TOPK_TT][32 * NV];
     __shared__ double rs[TOPK_SMALL_THREADS];
     const int tpc = T <= TOPK_SMALL_T ? 1 : TOPK_TT;
@@ -350,61 +421,10 @@ __global__ void __launch_bounds__(TOPK_SMALL_THREADS) k_route_topk(const double*
         }
     }
     __syncthreads();
-    const int lane = threadIdx.x & 31, tt = threadIdx.x >> 5;
+    const int tt = threadIdx.x >> 5;
     if (tt >= nt) return;
     const int t = t0 + tt;
-    float p[NV];
-    float m = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-        const int e = lane + 32 * i;
-        p[i] = e < E ? lg[tt][e] : -INFINITY;
-        m = fmaxf(m, p[i]);
-    }
-    m = warp_max(m);
-    double ssum = 0.0;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-        if (lane + 32 * i < E) {
-            p[i] = expf(p[i] - m);
-            ssum += (double)p[i];
-        }
-    }
-    ssum = warp_sum(ssum);
-    const float inv = (float)(1.0 / ssum);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) p[i] = lane + 32 * i < E ? p[i] * inv : -1.f;
-    // k rounds of arg-max over (p desc, id asc); the winner's entry is retired with p = -1
-    float my_w = 0.f, wsum = 0.f;
-    int my_e = 0;
-    for (int r = 0; r < k; ++r) {
-        float bp = -1.f;
-        int be = 0x7FFFFFFF;
-#pragma unroll
-        for (int i = 0; i < NV; ++i) {
-            const int e = lane + 32 * i;
-            if (p[i] > bp || (p[i] == bp && e < be)) { bp = p[i]; be = e; }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float op = __shfl_xor_sync(0xFFFFFFFFu, bp, o);
-            const int oe = __shfl_xor_sync(0xFFFFFFFFu, be, o);
-            if (op > bp || (op == bp && oe < be)) { bp = op; be = oe; }
-        }
-#pragma unroll
-        for (int i = 0; i < NV; ++i)
-            if (lane + 32 * i == be) p[i] = -1.f;
-        wsum += bp;                                   // sequential f32 sum in rank order
-        if (lane == r) { my_w = bp; my_e = be; }
-    }
-    if (renorm) {
-        if (wsum < 6.103515625e-5f) wsum = 6.103515625e-5f;
-        my_w /= wsum;
-    }
-    if (lane < k) {
-        sel[(int64_t)t * k + lane] = my_e;
-        w[(int64_t)t * k + lane] = my_w;
-    }
+    route_topk_row<NV>(lg[tt], E, k, renorm, threadIdx.x & 31, sel + (int64_t)t * k, w + (int64_t)t * k);
 }
 
 // Large batches: 128 tokens x 128 experts per CTA, 8 x 8 accumulators per thread (f32 over the CTA's K
@@ -419,6 +439,7 @@ constexpr int RB_TARGET_CTAS = 148;    // one CTA per SM (64 accumulators + stag
 __global__ void __launch_bounds__(256, 1) k_router_logits_big(const float* __restrict__ fx,
                                                               const float* __restrict__ w_t, int T, int H, int E,
                                                               int klen, double* __restrict__ part) {
+    pdl_enter();
     __shared__ __align__(16) float sf[RB_KC][RB_TT + RB_PAD];
     __shared__ __align__(16) float sw[RB_KC][RB_EB];
     const int tid = threadIdx.x;
@@ -522,20 +543,20 @@ cudaError_t launch_route(const Dims& d, const LayerWeights& lw, const void* x, i
     if (T >= RB_MIN_T && d.E % 4 == 0 && d.H % RB_KC == 0) {
         ks = router_ksplit_big(T, d.E, d.H);
         const dim3 grid((T + RB_TT - 1) / RB_TT, (d.E + RB_EB - 1) / RB_EB, ks);
-        k_router_logits_big<<<grid, 256, 0, s>>>(fx, lw.w_router_t, T, d.H, d.E, d.H / ks, part);
+        launch_pdl(k_router_logits_big, grid, 256, 0, s, fx, lw.w_router_t, T, d.H, d.E, d.H / ks, part);
     } else {
         ks = router_ksplit(T, d.E, d.H);
         const dim3 grid((T + RL_TT - 1) / RL_TT, (d.E + RL_EB - 1) / RL_EB, ks);
-        k_router_logits<<<grid, 256, 0, s>>>(fx, lw.w_router, T, d.H, d.E, d.H / ks, part);
+        launch_pdl(k_router_logits, grid, 256, 0, s, fx, lw.w_router, T, d.H, d.E, d.H / ks, part);
     }
     const int tpc = T <= TOPK_SMALL_T ? 1 : TOPK_TT;
     const unsigned tgrid = (unsigned)((T + tpc - 1) / tpc);
     const int tth = tpc == 1 ? TOPK_SMALL_THREADS : 256;
-    if (d.E <= 64) k_route_topk<2><<<tgrid, tth, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
-    else if (d.E <= 128) k_route_topk<4><<<tgrid, tth, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
-    else if (d.E <= 256) k_route_topk<8><<<tgrid, tth, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
-    else if (d.E <= 512) k_route_topk<16><<<tgrid, tth, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
-    else k_route_topk<32><<<tgrid, tth, 0, s>>>(part, ks, T, d.E, d.k, d.renorm, sel, w);
+    if (d.E <= 64) launch_pdl(k_route_topk<2>, tgrid, tth, 0, s, part, ks, T, d.E, d.k, d.renorm, sel, w);
+    else if (d.E <= 128) launch_pdl(k_route_topk<4>, tgrid, tth, 0, s, part, ks, T, d.E, d.k, d.renorm, sel, w);
+    else if (d.E <= 256) launch_pdl(k_route_topk<8>, tgrid, tth, 0, s, part, ks, T, d.E, d.k, d.renorm, sel, w);
+    else if (d.E <= 512) launch_pdl(k_route_topk<16>, tgrid, tth, 0, s, part, ks, T, d.E, d.k, d.renorm, sel, w);
+    else launch_pdl(k_route_topk<32>, tgrid, tth, 0, s, part, ks, T, d.E, d.k, d.renorm, sel, w);
     if (launches) *launches += 3;
     return cudaGetLastError();
 }
@@ -543,14 +564,10 @@ cudaError_t launch_route(const Dims& d, const LayerWeights& lw, const void* x, i
 // ---------------------------------------------------------------------------------------------
 // Q8_K quantisation of rows [R][K]: one 256-segment per CTA
 // ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_quant_q8(const float* __restrict__ x, int K, int8_t* __restrict__ q,
-                                                  float* __restrict__ dout, int* __restrict__ bs) {
-    pdl_enter();
-    __shared__ float redf[32];
-    const int nseg = K / QK;
-    const int64_t r = blockIdx.x / nseg;       // one CTA per (row, 256-segment), 1-D grid
-    const int seg = (int)(blockIdx.x - r * nseg);
-    const float v = x[r * K + seg * QK + threadIdx.x];
+// Q8_K of one 256-value segment by a 256-thread CTA, thread i holding value i: scale = max|v| / 127,
+// q = min(127, round(v * 127 / max|v|)), 16-value sums of q; q, d and bs point at the segment's outputs.
+__device__ __forceinline__ void quant_seg256(float v, float* redf, int8_t* __restrict__ q, float* __restrict__ d,
+                                             int* __restrict__ bs) {
     const float amax = block_max_f(fabsf(v), redf);
     int qi = 0;
     float dd = 0.f;
@@ -559,12 +576,23 @@ __global__ void __launch_bounds__(256) k_quant_q8(const float* __restrict__ x, i
         qi = min(127, __float2int_rn(iscale * v));
         dd = 1.f / iscale;
     }
-    q[r * K + seg * QK + threadIdx.x] = (int8_t)qi;
+    q[threadIdx.x] = (int8_t)qi;
     int sum = qi;
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if ((threadIdx.x & 15) == 0) bs[r * (K / 16) + seg * 16 + (threadIdx.x >> 4)] = sum;
-    if (threadIdx.x == 0) dout[r * nseg + seg] = dd;
+    if ((threadIdx.x & 15) == 0) bs[threadIdx.x >> 4] = sum;
+    if (threadIdx.x == 0) *d = dd;
+}
+
+__global__ void __launch_bounds__(256) k_quant_q8(const float* __restrict__ x, int K, int8_t* __restrict__ q,
+                                                  float* __restrict__ dout, int* __restrict__ bs) {
+    pdl_enter();
+    __shared__ float redf[32];
+    const int nseg = K / QK;
+    const int64_t r = blockIdx.x / nseg;       // one CTA per (row, 256-segment), 1-D grid
+    const int seg = (int)(blockIdx.x - r * nseg);
+    quant_seg256(x[r * K + seg * QK + threadIdx.x], redf, q + r * K + seg * QK, dout + r * nseg + seg,
+                 bs + r * (K / 16) + seg * 16);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -576,7 +604,10 @@ __global__ void __launch_bounds__(256) k_quant_q8(const float* __restrict__ x, i
 constexpr int DISP_THREADS = 1024;
 constexpr int DISP_UNROLL = 8;
 
-__device__ __forceinline__ int2 scan_excl_1024(int2 v, int2* wtot, int2& total) {
+// exclusive scan of one int2 per thread over a CTA of NT threads (NT / 32 <= 32 warps)
+template <int NT>
+__device__ __forceinline__ int2 scan_excl_cta(int2 v, int2* wtot, int2& total) {
+    constexpr int NW = NT / 32;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int2 inc = v;
 #pragma unroll
@@ -587,51 +618,54 @@ __device__ __forceinline__ int2 scan_excl_1024(int2 v, int2* wtot, int2& total) 
     if (lane == 31) wtot[warp] = inc;
     __syncthreads();
     if (warp == 0) {
-        int2 t = wtot[lane];
+        int2 t = lane < NW ? wtot[lane] : make_int2(0, 0);
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const int a = __shfl_up_sync(0xFFFFFFFFu, t.x, o), b = __shfl_up_sync(0xFFFFFFFFu, t.y, o);
             if (lane >= o) { t.x += a; t.y += b; }
         }
-        wtot[lane] = t;
+        if (lane < NW) wtot[lane] = t;
     }
     __syncthreads();
     const int2 pre = warp > 0 ? wtot[warp - 1] : make_int2(0, 0);
-    total = wtot[31];
+    total = wtot[NW - 1];
     return make_int2(pre.x + inc.x - v.x, pre.y + inc.y - v.y);
 }
 
-__global__ void __launch_bounds__(DISP_THREADS) k_dispatch(const int32_t* __restrict__ slot_of, int T, int k, int KK,
-                                                           int n_slots, int* __restrict__ counts,
-                                                           int* __restrict__ offsets, int* __restrict__ perm,
-                                                           unsigned* err, int tile_m, int2* __restrict__ items,
-                                                           int* __restrict__ n_items, bool skip_neg) {
-    extern __shared__ int sm[];
-    __shared__ int2 wtot[32];
+// The counting sort of one CTA of NT threads: entries e = t*KK + j (slot slot_of[t*k + j] for j < k,
+// the shared slot n_slots for j = k) -> counts, offsets, perm and, with tile_m > 0, the work list
+// items (one (slot, M tile) per tile_m entries of a slot). sm holds 2 * (NS + 1) ints. slot_of is
+// read through L2 (it may have been written earlier in the same launch by another CTA).
+template <int NT>
+__device__ __forceinline__ void dispatch_cta(const int32_t* slot_of, int T, int k, int KK, int n_slots,
+                                             int* __restrict__ counts, int* __restrict__ offsets,
+                                             int* __restrict__ perm, unsigned* err, int tile_m,
+                                             int2* __restrict__ items, int* __restrict__ n_items, bool skip_neg,
+                                             int* sm, int2* wtot) {
     const int NS = n_slots + (KK > k ? 1 : 0);
     int* cnt = sm;
     int* cur = sm + NS + 1;
-    for (int i = threadIdx.x; i <= NS; i += blockDim.x) cnt[i] = 0;
+    for (int i = threadIdx.x; i <= NS; i += NT) cnt[i] = 0;
     __syncthreads();
     const int n = T * KK;
     auto slot_at = [&](int e) {
         const int t = e / KK, j = e - t * KK;
-        return (j < k) ? (int)slot_of[(size_t)t * k + j] : n_slots;
+        return (j < k) ? (int)__ldcg(slot_of + (size_t)t * k + j) : n_slots;
     };
     auto valid = [&](int e, int sl) {
         const int j = e % KK;
         return !(sl < 0 || sl >= NS || (j < k && sl >= n_slots));
     };
-    for (int e0 = threadIdx.x; e0 < n; e0 += DISP_THREADS * DISP_UNROLL) {
+    for (int e0 = threadIdx.x; e0 < n; e0 += NT * DISP_UNROLL) {
         int sv[DISP_UNROLL];
 #pragma unroll
         for (int u = 0; u < DISP_UNROLL; ++u) {
-            const int e = e0 + u * DISP_THREADS;
+            const int e = e0 + u * NT;
             sv[u] = e < n ? slot_at(e) : -1;
         }
 #pragma unroll
         for (int u = 0; u < DISP_UNROLL; ++u) {
-            const int e = e0 + u * DISP_THREADS;
+            const int e = e0 + u * NT;
             if (e >= n) continue;
             if (!valid(e, sv[u])) {
                 if (!(skip_neg && sv[u] < 0)) atomicOr(err, 1u);
@@ -642,7 +676,7 @@ __global__ void __launch_bounds__(DISP_THREADS) k_dispatch(const int32_t* __rest
     }
     __syncthreads();
     // exclusive scan of (entries, M tiles) over the slots; thread i owns slots [i*c, (i+1)*c)
-    const int c = (NS + DISP_THREADS - 1) / DISP_THREADS;
+    const int c = (NS + NT - 1) / NT;
     const int s0 = threadIdx.x * c, s1 = min(NS, s0 + c);
     int2 mine = make_int2(0, 0);
     for (int sl = s0; sl < s1; ++sl) {
@@ -650,7 +684,7 @@ __global__ void __launch_bounds__(DISP_THREADS) k_dispatch(const int32_t* __rest
         if (tile_m > 0) mine.y += (cnt[sl] + tile_m - 1) / tile_m;
     }
     int2 total;
-    int2 off = scan_excl_1024(mine, wtot, total);
+    int2 off = scan_excl_cta<NT>(mine, wtot, total);
     for (int sl = s0; sl < s1; ++sl) {
         const int cn = cnt[sl];
         offsets[sl] = off.x;
@@ -667,20 +701,381 @@ __global__ void __launch_bounds__(DISP_THREADS) k_dispatch(const int32_t* __rest
         if (tile_m > 0) *n_items = total.y;
     }
     __syncthreads();
-    for (int e0 = threadIdx.x; e0 < n; e0 += DISP_THREADS * DISP_UNROLL) {
+    for (int e0 = threadIdx.x; e0 < n; e0 += NT * DISP_UNROLL) {
         int sv[DISP_UNROLL];
 #pragma unroll
         for (int u = 0; u < DISP_UNROLL; ++u) {
-            const int e = e0 + u * DISP_THREADS;
+            const int e = e0 + u * NT;
             sv[u] = e < n ? slot_at(e) : -1;
         }
 #pragma unroll
         for (int u = 0; u < DISP_UNROLL; ++u) {
-            const int e = e0 + u * DISP_THREADS;
+            const int e = e0 + u * NT;
             if (e >= n || !valid(e, sv[u])) continue;
             perm[atomicAdd(&cur[sv[u]], 1)] = e;
         }
     }
+}
+
+// The counting sort of a small batch (n = T*KK entries) by one CTA of NT threads in one pass over
+// slot_of: each entry's slot and its rank within the slot (a shared-memory atomic) are kept in shared
+// memory, the scan gives the slots' offsets, and perm[offset + rank] = e. sm holds NS + 1 + 2n ints.
+template <int NT>
+__device__ __forceinline__ void dispatch_small(const int32_t* slot_of, int T, int k, int KK, int n_slots,
+                                               int* __restrict__ counts, int* __restrict__ offsets,
+                                               int* __restrict__ perm, unsigned* err, int tile_m,
+                                               int2* __restrict__ items, int* __restrict__ n_items, int* sm,
+                                               int2* wtot) {
+    const int NS = n_slots + (KK > k ? 1 : 0);
+    const int n = T * KK;
+    int* cnt = sm;
+    int* es = sm + NS + 1;
+    int* er = es + n;
+    for (int i = threadIdx.x; i <= NS; i += NT) cnt[i] = 0;
+#pragma unroll 4
+    for (int e = threadIdx.x; e < n; e += NT) {
+        const int t = e / KK, j = e - t * KK;
+        es[e] = (j < k) ? (int)__ldcg(slot_of + (size_t)t * k + j) : n_slots;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < n; e += NT) {
+        const int sl = es[e], j = e % KK;
+        if (sl < 0 || sl >= NS || (j < k && sl >= n_slots)) {
+            atomicOr(err, 1u);
+            es[e] = -1;
+        } else {
+            er[e] = atomicAdd(&cnt[sl], 1);
+        }
+    }
+    __syncthreads();
+    const int c = (NS + NT - 1) / NT;
+    const int s0 = threadIdx.x * c, s1 = min(NS, s0 + c);
+    int2 mine = make_int2(0, 0);
+    for (int sl = s0; sl < s1; ++sl) {
+        mine.x += cnt[sl];
+        if (tile_m > 0) mine.y += (cnt[sl] + tile_m - 1) / tile_m;
+    }
+    int2 total;
+    int2 off = scan_excl_cta<NT>(mine, wtot, total);
+    for (int sl = s0; sl < s1; ++sl) {
+        const int cn = cnt[sl];
+        offsets[sl] = off.x;
+        counts[sl] = cn;
+        cnt[sl] = off.x;
+        off.x += cn;
+        if (tile_m > 0) {
+            for (int mt = 0; mt * tile_m < cn; ++mt) items[off.y + mt] = make_int2(sl, mt);
+            off.y += (cn + tile_m - 1) / tile_m;
+        }
+    }
+    if (threadIdx.x == 0) {
+        offsets[NS] = total.x;
+        if (tile_m > 0) *n_items = total.y;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < n; e += NT)
+        if (es[e] >= 0) perm[cnt[es[e]] + er[e]] = e;
+}
+
+__global__ void __launch_bounds__(DISP_THREADS) k_dispatch(const int32_t* __restrict__ slot_of, int T, int k, int KK,
+                                                           int n_slots, int* __restrict__ counts,
+                                                           int* __restrict__ offsets, int* __restrict__ perm,
+                                                           unsigned* err, int tile_m, int2* __restrict__ items,
+                                                           int* __restrict__ n_items, bool skip_neg) {
+    pdl_enter();
+    extern __shared__ int sm[];
+    __shared__ int2 wtot[32];
+    dispatch_cta<DISP_THREADS>(slot_of, T, k, KK, n_slots, counts, offsets, perm, err, tile_m, items, n_items,
+                               skip_neg, sm, wtot);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Small batches through a whole layer: one kernel for graph A's RMSNorm, router GEMV, softmax + top-k,
+// the Q8_K of the FFN input and the dispatch, for T <= RF_MAX_T tokens with every expert resident.
+// CTA (ec, tg) takes tokens [RF_TPG*tg, +RF_TPG) and experts [RF_EC*ec, +RF_EC) (one per warp):
+//   1. the experts' router rows go into registers before the wait on the previous kernel (constant
+//      weights), the tokens' fx = rms_norm(x) * ffn_norm into shared memory (the arithmetic of
+//      k_rmsnorm, so fx is bit-identical; the ec = 0 CTA also stores it);
+//   2. logits: each lane forms the f32 sums of its 32-wide K chunks, then the chunk sums are added
+//      in double exactly as k_router_logits (per K split) and k_route_topk (splits in `subs`
+//      ranges) add them for the same (T, E, H), so the logits -- and the routing -- are identical
+//      to the three-kernel path;
+//   3. 256-value segments ec, ec + n_ec, ... of each token's fx are quantised to Q8_K (k_quant_q8's
+//      arithmetic);
+//   4. the CTA counts itself in its token group's counter (release: CTA barrier + fence + atomic);
+//      the group's last CTA runs the top-k of the group's tokens and counts the group in; the last
+//      group's CTA runs the dispatch (counting sort by slot + the work list). Last arrivers reset the
+//      counters, which are zero between launches. No CTA waits for another.
+// ---------------------------------------------------------------------------------------------
+constexpr int RF_THREADS = 256;
+constexpr int RF_TPG = 4;              // most tokens per CTA
+constexpr int RF_EC = RF_THREADS / 32; // experts per CTA
+constexpr int RF_MAX_T = 64;
+constexpr int RF_MAX_E = 512;
+constexpr int RF_MAX_CH = 64;          // 32-wide K chunks per row (H <= 2048)
+constexpr int RF_CPAD = 36;            // floats per staged K chunk (padding spreads the lanes' reads over the banks)
+constexpr int RF_CNT_OFF = 2560;       // the counters' place in the scratch sync words
+constexpr int RF_CNT_STRIDE = 32;      // one 128-byte line per counter
+
+struct RouteFusedArgs {
+    const void* x;
+    int T, H, E, k, KK, renorm, n_slots, tile_m;
+    float eps;
+    int ks, subs;                      // K splits and their summation ranges (k_route_topk's for this T)
+    int tpg;                           // tokens per CTA (<= RF_TPG)
+    const float* w_norm;
+    const float* w_router;             // [E][H]
+    float* fx;
+    int8_t* fx_q;
+    float* fx_d;
+    int* fx_bs;
+    float* logits;                     // [T][E] scratch
+    int32_t* sel;
+    float* w;
+    int* counts;
+    int* offsets;
+    int* perm;
+    int2* items;
+    int* n_items;
+    unsigned* err;
+    unsigned* cnt;                     // [n_tg + 1] counters at stride RF_CNT_STRIDE (zero at rest)
+    unsigned long long* stamp;         // optional {first start, last end} (%globaltimer) of this launch
+};
+
+template <typename R, int VPT, int NV>
+__global__ void __launch_bounds__(RF_THREADS) k_route_fused(const RouteFusedArgs a) {
+    extern __shared__ __align__(16) float rf_sm[];     // fx [tpg][chunks * RF_CPAD]; later logits + dispatch
+    __shared__ float cs[RF_EC][RF_MAX_CH];
+    __shared__ double ps[RF_EC][RF_MAX_CH];
+    __shared__ double redd[32];
+    __shared__ float redf[32];
+    __shared__ int2 wtot[32];
+    __shared__ int s_last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ec = blockIdx.x, tg = blockIdx.y, n_ec = gridDim.x, n_tg = gridDim.y;
+    const int tpg = a.tpg;
+    const int H = a.H, E = a.E;
+    const int nch = H / 32, cpl = nch / 32;            // chunks per row, per lane (1 or 2)
+    const int t0 = tg * tpg, nt = min(tpg, a.T - t0);
+    const int e = ec * RF_EC + warp;
+    const int rowf = nch * RF_CPAD;
+    pdl_launch_dependents();
+    // 1. router rows (constant) before the wait; chunk c = lane + 32 * i of the row
+    float4 wr[2][8];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            wr[i][q] = (e < E && i < cpl)
+                ? __ldg(reinterpret_cast<const float4*>(a.w_router + (int64_t)e * H + 32 * (lane + 32 * i) + 4 * q))
+                : make_float4(0.f, 0.f, 0.f, 0.f);
+    pdl_wait();
+    if (a.stamp && tid == 0) atomicMin(a.stamp, gtimer());
+    const R* x = reinterpret_cast<const R*>(a.x);
+    // f32 rows: all the CTA's rows are copied into the fx layout at once (cp.async), then normalised
+    // in place; bf16 rows are read per token
+    if (std::is_same<R, float>::value) {
+        for (int pc = tid; pc < nt * (H / 4); pc += RF_THREADS) {
+            const int tt = pc / (H / 4), i = 4 * (pc - tt * (H / 4));
+            cp_async16(rf_sm + tt * rowf + (i >> 5) * RF_CPAD + (i & 31), x + (int64_t)(t0 + tt) * H + i);
+        }
+        cp_async_commit();
+        cp_async_wait_all();
+        __syncthreads();
+    }
+#pragma unroll 1
+    for (int tt = 0; tt < nt; ++tt) {
+        // the arithmetic of rms_row_scale (thread order of the squares, warp butterfly, warps in order)
+        const int64_t t = t0 + tt;
+        float* fr = rf_sm + tt * rowf;
+        float v[VPT];
+#pragma unroll
+        for (int j = 0; j < VPT / 4; ++j) {
+            const int i = 4 * (tid + 256 * j);
+            if (i < H) {
+                if (std::is_same<R, float>::value) {
+                    const float4 f = *reinterpret_cast<const float4*>(fr + (i >> 5) * RF_CPAD + (i & 31));
+                    v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+                } else {
+                    Vec4<R>::load(x + t * H + i, v + 4 * j);
+                }
+            } else {
+                v[4 * j] = v[4 * j + 1] = v[4 * j + 2] = v[4 * j + 3] = 0.f;
+            }
+        }
+        double ss = 0.0;
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) ss += (double)(v[j] * v[j]);
+        ss = block_sum_d(ss, redd);
+        const float scale = 1.0f / sqrtf((float)(ss / H) + a.eps);
+#pragma unroll
+        for (int j = 0; j < VPT / 4; ++j) {
+            const int i = 4 * (tid + 256 * j);
+            if (i < H) {
+                const float4 wn = *reinterpret_cast<const float4*>(a.w_norm + i);
+                const float4 f = make_float4((v[4 * j] * scale) * wn.x, (v[4 * j + 1] * scale) * wn.y,
+                                             (v[4 * j + 2] * scale) * wn.z, (v[4 * j + 3] * scale) * wn.w);
+                *reinterpret_cast<float4*>(fr + (i >> 5) * RF_CPAD + (i & 31)) = f;
+                if (ec == 0) *reinterpret_cast<float4*>(a.fx + t * H + i) = f;
+            }
+        }
+    }
+    __syncthreads();
+    // 2. logits of expert e for the CTA's tokens
+#pragma unroll 1
+    for (int tt = 0; tt < nt; ++tt) {
+        if (e < E) {
+            const float* fr = rf_sm + tt * rowf;
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                if (i < cpl) {
+                    const int c = lane + 32 * i;
+                    float acc = 0.f;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const float4 f = *reinterpret_cast<const float4*>(fr + c * RF_CPAD + 4 * q);
+                        acc = fmaf(f.x, wr[i][q].x, acc);
+                        acc = fmaf(f.y, wr[i][q].y, acc);
+                        acc = fmaf(f.z, wr[i][q].z, acc);
+                        acc = fmaf(f.w, wr[i][q].w, acc);
+                    }
+                    cs[warp][c] = acc;
+                }
+            }
+            __syncwarp();
+            // split sums: split z covers chunks [z*cps, (z+1)*cps), added in double from 0
+            const int cps = nch / a.ks;
+            for (int z = lane; z < a.ks; z += 32) {
+                double sz = 0.0;
+                for (int c = z * cps; c < (z + 1) * cps; ++c) sz += (double)cs[warp][c];
+                ps[warp][z] = sz;
+            }
+            __syncwarp();
+            double rs = 0.0;
+            if (lane < a.subs) {
+                const int z0 = (int)((int64_t)a.ks * lane / a.subs), z1 = (int)((int64_t)a.ks * (lane + 1) / a.subs);
+                for (int z = z0; z < z1; ++z) rs += ps[warp][z];
+            }
+            double tot = __shfl_sync(0xFFFFFFFFu, rs, 0);
+            for (int sb = 1; sb < a.subs; ++sb) tot += __shfl_sync(0xFFFFFFFFu, rs, sb);
+            if (lane == 0) a.logits[(t0 + tt) * (int64_t)E + e] = (float)tot;
+            __syncwarp();
+        }
+    }
+    // 3. Q8_K of fx segments ec, ec + n_ec, ...
+    const int nseg = H / QK;
+    for (int sg = ec; sg < nseg; sg += n_ec) {
+#pragma unroll 1
+        for (int tt = 0; tt < nt; ++tt) {
+            const int i = sg * QK + tid;
+            const int64_t t = t0 + tt;
+            quant_seg256(rf_sm[tt * rowf + (i >> 5) * RF_CPAD + (i & 31)], redf, a.fx_q + t * H + sg * QK,
+                         a.fx_d + t * nseg + sg, a.fx_bs + t * (H / 16) + sg * 16);
+        }
+    }
+    // 4. arrival of the CTA in its token group (release: CTA barrier, fence, atomic; the last arriver
+    //    fences again before it reads what the others wrote, through L2)
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const bool last = atomicAdd(&a.cnt[RF_CNT_STRIDE * tg], 1u) == (unsigned)(n_ec - 1);
+        if (last) __threadfence();
+        s_last = last;
+    }
+    __syncthreads();
+    if (!s_last) {
+        if (a.stamp && tid == 0) atomicMax(a.stamp + 1, gtimer());
+        return;
+    }
+    float* lgs = rf_sm;                                  // [tpg][32 * NV]
+    for (int i = tid; i < nt * E; i += RF_THREADS) {
+        const int tt = i / E;
+        lgs[tt * 32 * NV + (i - tt * E)] = __ldcg(a.logits + (int64_t)t0 * E + i);
+    }
+    __syncthreads();
+    if (warp < nt)
+        route_topk_row<NV>(lgs + warp * 32 * NV, E, a.k, a.renorm, lane, a.sel + (int64_t)(t0 + warp) * a.k,
+                           a.w + (int64_t)(t0 + warp) * a.k);
+    __syncthreads();
+    if (tid == 0) {
+        a.cnt[RF_CNT_STRIDE * tg] = 0u;                  // every CTA of the group has arrived
+        __threadfence();
+        const bool last = atomicAdd(&a.cnt[RF_CNT_STRIDE * n_tg], 1u) == (unsigned)(n_tg - 1);
+        if (last) {
+            __threadfence();
+            a.cnt[RF_CNT_STRIDE * n_tg] = 0u;
+        }
+        s_last = last;
+    }
+    __syncthreads();
+    if (!s_last) {
+        if (a.stamp && tid == 0) atomicMax(a.stamp + 1, gtimer());
+        return;
+    }
+    dispatch_small<RF_THREADS>(a.sel, a.T, a.k, a.KK, a.n_slots, a.counts, a.offsets, a.perm, a.err, a.tile_m,
+                               a.items, a.n_items, reinterpret_cast<int*>(rf_sm), wtot);
+    if (a.stamp) {
+        __syncthreads();
+        if (tid == 0) atomicMax(a.stamp + 1, gtimer());
+    }
+}
+
+bool route_fused_supported(const Dims& d, int T) {
+    if (T < 1 || T > RF_MAX_T || T >= RB_MIN_T) return false;
+    if (d.H != 1024 && d.H != 2048) return false;            // one or two K chunks per lane
+    if (d.E < 1 || d.E > RF_MAX_E || d.k < 1 || d.k > MAX_K || d.k > d.E) return false;
+    const int ks = router_ksplit(T, d.E, d.H);
+    return ks >= 1 && (d.H / RL_KC) % ks == 0;
+}
+
+template <typename R, int VPT>
+static cudaError_t launch_route_fused_t(const RouteFusedArgs& a, dim3 grid, size_t dyn, cudaStream_t s) {
+    if (a.E <= 128) return launch_pdl(k_route_fused<R, VPT, 4>, grid, RF_THREADS, dyn, s, a);
+    return launch_pdl(k_route_fused<R, VPT, 16>, grid, RF_THREADS, dyn, s, a);
+}
+
+cudaError_t launch_route_fused(const Dims& d, const LayerWeights& lw, const Scratch& sc, const void* x, int T, int KK,
+                               int32_t* sel, float* w, int tile_m, cudaStream_t s, unsigned long long* stamp) {
+    if (!route_fused_supported(d, T)) return cudaErrorInvalidValue;
+    RouteFusedArgs a{};
+    a.x = x;
+    a.T = T; a.H = d.H; a.E = d.E; a.k = d.k; a.KK = KK; a.renorm = d.renorm; a.n_slots = lw.n_slots;
+    a.tile_m = tile_m;
+    a.eps = d.eps;
+    a.ks = router_ksplit(T, d.E, d.H);
+    // k_route_topk's summation ranges of the K splits with one token per CTA (T <= TOPK_SMALL_T)
+    int subs = 1;
+    while (subs < 16 && subs * 2 * d.E <= TOPK_SMALL_THREADS && subs * 2 <= a.ks) subs *= 2;
+    a.subs = subs;
+    a.w_norm = lw.w_norm; a.w_router = lw.w_router;
+    a.fx = sc.fx; a.fx_q = sc.fx_q; a.fx_d = sc.fx_d; a.fx_bs = sc.fx_bs;
+    a.logits = reinterpret_cast<float*>(sc.rpart);
+    a.sel = sel; a.w = w;
+    a.counts = sc.counts; a.offsets = sc.offsets; a.perm = sc.perm; a.items = sc.items; a.n_items = sc.n_items;
+    a.err = sc.sync;
+    a.cnt = sc.sync + RF_CNT_OFF;
+    a.stamp = stamp;
+    // tokens per CTA: the fewest (most parallel) that keep the grid within two CTAs per SM
+    static int sms[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (sms[dev] == 0) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    const int n_ec = (d.E + RF_EC - 1) / RF_EC;
+    a.tpg = RF_TPG;
+    for (int tp = 1; tp < RF_TPG; tp *= 2)
+        if ((int64_t)n_ec * ((T + tp - 1) / tp) <= 2 * (int64_t)sms[dev]) { a.tpg = tp; break; }
+    const dim3 grid(n_ec, (T + a.tpg - 1) / a.tpg);
+    const int NS = lw.n_slots + (KK > d.k ? 1 : 0);
+    size_t dyn = (size_t)RF_TPG * (d.H / RL_KC) * RF_CPAD * 4;
+    dyn = std::max(dyn, (size_t)RF_TPG * 32 * (d.E <= 128 ? 4 : 16) * 4);
+    dyn = std::max(dyn, (size_t)(NS + 1 + 2 * T * KK) * 4);
+    if (dyn > 48 * 1024) return cudaErrorInvalidValue;
+    if (d.H <= 1024)
+        return d.resid_bf16 ? launch_route_fused_t<__nv_bfloat16, 4>(a, grid, dyn, s)
+                            : launch_route_fused_t<float, 4>(a, grid, dyn, s);
+    return d.resid_bf16 ? launch_route_fused_t<__nv_bfloat16, 8>(a, grid, dyn, s)
+                        : launch_route_fused_t<float, 8>(a, grid, dyn, s);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -744,6 +1139,7 @@ __global__ void __launch_bounds__(256) k_gateup_regs(LayerWeights lw, int H, int
                                                      const int* __restrict__ offsets, const int* __restrict__ perm,
                                                      const int8_t* __restrict__ xq, const float* __restrict__ xd,
                                                      const int* __restrict__ xbs, float* __restrict__ h) {
+    pdl_enter();
     const int s = blockIdx.x;
     const int start = offsets[s], end = offsets[s + 1];
     if (start == end) return;
@@ -797,6 +1193,7 @@ __global__ void __launch_bounds__(256) k_down_regs(LayerWeights lw, int H, int I
                                                    const int* __restrict__ perm, const int8_t* __restrict__ hq,
                                                    const float* __restrict__ hd, const int* __restrict__ hbs,
                                                    float* __restrict__ y) {
+    pdl_enter();
     const int s = blockIdx.x;
     const int start = offsets[s], end = offsets[s + 1];
     if (start == end) return;
@@ -838,6 +1235,7 @@ __global__ void __launch_bounds__(256) k_gateup(LayerWeights lw, int H, int I, i
                                                 const int* __restrict__ perm, const int8_t* __restrict__ xq,
                                                 const float* __restrict__ xd, const int* __restrict__ xbs,
                                                 float* __restrict__ h) {
+    pdl_enter();
     const int s = blockIdx.x;
     const int start = offsets[s], end = offsets[s + 1];
     if (start == end) return;
@@ -864,6 +1262,7 @@ __global__ void __launch_bounds__(256) k_down(LayerWeights lw, int H, int I, con
                                               const int* __restrict__ perm, const int8_t* __restrict__ hq,
                                               const float* __restrict__ hd, const int* __restrict__ hbs,
                                               float* __restrict__ y) {
+    pdl_enter();
     const int s = blockIdx.x;
     const int start = offsets[s], end = offsets[s + 1];
     if (start == end) return;
@@ -885,6 +1284,7 @@ __global__ void __launch_bounds__(256) k_down(LayerWeights lw, int H, int I, con
 // sigmoid(gate_inp . fx[t]) per token (double accumulation, as the router GEMV)
 __global__ void __launch_bounds__(256) k_shared_gate(const float* __restrict__ fx, const float* __restrict__ g, int H,
                                                      float* __restrict__ out) {
+    pdl_enter();
     __shared__ double redd[32];
     const int t = blockIdx.x;
     double acc = 0.0;
@@ -909,6 +1309,7 @@ template <typename R, typename YT>
 __global__ void __launch_bounds__(256) k_combine(const YT* __restrict__ y, const float* __restrict__ w,
                                                  const float* __restrict__ sh_gate, int k, int KK, int H, int T,
                                                  R* x, const int* __restrict__ pos) {
+    pdl_enter();
     const int64_t nq = (int64_t)T * H / 4;
     for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < nq; q += (int64_t)gridDim.x * blockDim.x) {
         const int64_t t = (q * 4) / H;
@@ -930,19 +1331,19 @@ __global__ void __launch_bounds__(256) k_combine(const YT* __restrict__ y, const
         for (int j = 0; j < MAX_K; ++j) {
             if (j < k) {
                 const float wj = w[t * k + j];
-                acc.x += wj * yv[j].x;
-                acc.y += wj * yv[j].y;
-                acc.z += wj * yv[j].z;
-                acc.w += wj * yv[j].w;
+                acc.x = fmaf(wj, yv[j].x, acc.x);
+                acc.y = fmaf(wj, yv[j].y, acc.y);
+                acc.z = fmaf(wj, yv[j].z, acc.z);
+                acc.w = fmaf(wj, yv[j].w, acc.w);
             }
         }
         if (KK > k && !pos) {
             const float4 ys = ld_y4(yb + (int64_t)k * H);
             const float g = sh_gate[t];
-            acc.x = acc.x + ys.x * g;
-            acc.y = acc.y + ys.y * g;
-            acc.z = acc.z + ys.z * g;
-            acc.w = acc.w + ys.w * g;
+            acc.x = fmaf(ys.x, g, acc.x);
+            acc.y = fmaf(ys.y, g, acc.y);
+            acc.z = fmaf(ys.z, g, acc.z);
+            acc.w = fmaf(ys.w, g, acc.w);
         }
         R* xp = x + q * 4;
         xp[0] = from_f32<R>(acc.x + to_f32<R>(xp[0]));
@@ -958,6 +1359,7 @@ template <typename R>
 __global__ void __launch_bounds__(256) k_combine_h(const __half* __restrict__ y, const float* __restrict__ w,
                                                    const float* __restrict__ sh_gate, int k, int KK, int H, int T,
                                                    R* x, const int* __restrict__ pos) {
+    pdl_enter();
     const int64_t n8 = (int64_t)T * H / 8;
     for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < n8; q += (int64_t)gridDim.x * blockDim.x) {
         const int64_t t = (q * 8) / H;
@@ -1009,7 +1411,7 @@ __global__ void __launch_bounds__(256) k_combine_h(const __half* __restrict__ y,
 }
 
 cudaError_t launch_shared_gate(const float* fx, const float* gate_inp, int H, int T, float* out, cudaStream_t s) {
-    k_shared_gate<<<T, 256, 0, s>>>(fx, gate_inp, H, out);
+    launch_pdl(k_shared_gate, T, 256, 0, s, fx, gate_inp, H, out);
     return cudaGetLastError();
 }
 
@@ -1021,6 +1423,7 @@ constexpr int DISP_CHUNK = 4096;     // entries per CTA in the multi-CTA kernels
 __global__ void __launch_bounds__(512) k_disp_count(const int32_t* __restrict__ slot_of, int T, int k, int KK,
                                                     int n_slots, int* __restrict__ gcount, unsigned* err,
                                                     bool skip_neg) {
+    pdl_enter();
     extern __shared__ int hist[];
     const int NS = n_slots + (KK > k ? 1 : 0);
     for (int i = threadIdx.x; i < NS; i += blockDim.x) hist[i] = 0;
@@ -1045,6 +1448,7 @@ __global__ void __launch_bounds__(DISP_THREADS) k_disp_scan(int NS, int* __restr
                                                             int* __restrict__ offsets, int* __restrict__ cursor,
                                                             int tile_m, int2* __restrict__ items,
                                                             int* __restrict__ n_items) {
+    pdl_enter();
     __shared__ int2 wtot[32];
     const int c = (NS + DISP_THREADS - 1) / DISP_THREADS;
     const int s0 = threadIdx.x * c, s1 = min(NS, s0 + c);
@@ -1054,7 +1458,7 @@ __global__ void __launch_bounds__(DISP_THREADS) k_disp_scan(int NS, int* __restr
         if (tile_m > 0) mine.y += (gcount[sl] + tile_m - 1) / tile_m;
     }
     int2 total;
-    int2 off = scan_excl_1024(mine, wtot, total);
+    int2 off = scan_excl_cta<DISP_THREADS>(mine, wtot, total);
     for (int sl = s0; sl < s1; ++sl) {
         const int cn = gcount[sl];
         offsets[sl] = off.x;
@@ -1075,6 +1479,7 @@ __global__ void __launch_bounds__(DISP_THREADS) k_disp_scan(int NS, int* __restr
 
 __global__ void __launch_bounds__(512) k_disp_scatter(const int32_t* __restrict__ slot_of, int T, int k, int KK,
                                                       int n_slots, int* __restrict__ cursor, int* __restrict__ perm) {
+    pdl_enter();
     const int NS = n_slots + (KK > k ? 1 : 0);
     const int n = T * KK;
     const int lane = threadIdx.x & 31;
@@ -1112,17 +1517,17 @@ cudaError_t launch_dispatch(const int32_t* slot_of_sel, int T, int k, int KK, in
     const int n = T * KK;
     if (n <= DISP_SMALL) {
         const size_t dsm = (size_t)2 * (NS + 1) * sizeof(int);
-        k_dispatch<<<1, DISP_THREADS, dsm, s>>>(slot_of_sel, T, k, KK, n_slots, sc.counts, sc.offsets, sc.perm,
+        launch_pdl(k_dispatch, 1, DISP_THREADS, dsm, s, slot_of_sel, T, k, KK, n_slots, sc.counts, sc.offsets, sc.perm,
                                                 sc.sync, tile_m, sc.items, sc.n_items, skip_neg);
         if (launches) *launches += 1;
         return cudaGetLastError();
     }
     const int grid = (n + DISP_CHUNK - 1) / DISP_CHUNK;
-    k_disp_count<<<grid, 512, (size_t)NS * sizeof(int), s>>>(slot_of_sel, T, k, KK, n_slots, sc.dcount, sc.sync,
+    launch_pdl(k_disp_count, grid, 512, (size_t)NS * sizeof(int), s, slot_of_sel, T, k, KK, n_slots, sc.dcount, sc.sync,
                                                                     skip_neg);
-    k_disp_scan<<<1, DISP_THREADS, 0, s>>>(NS, sc.dcount, sc.counts, sc.offsets, sc.dcursor, tile_m, sc.items,
+    launch_pdl(k_disp_scan, 1, DISP_THREADS, 0, s, NS, sc.dcount, sc.counts, sc.offsets, sc.dcursor, tile_m, sc.items,
                                            sc.n_items);
-    k_disp_scatter<<<grid, 512, 0, s>>>(slot_of_sel, T, k, KK, n_slots, sc.dcursor, sc.perm);
+    launch_pdl(k_disp_scatter, grid, 512, 0, s, slot_of_sel, T, k, KK, n_slots, sc.dcursor, sc.perm);
     if (launches) *launches += 3;
     return cudaGetLastError();
 }
@@ -1136,12 +1541,12 @@ cudaError_t launch_combine(const Dims& d, const Scratch& sc, const float* w, voi
     const int cbh = (int)((n8 + 255) / 256 < 148 * 16 ? (n8 + 255) / 256 : 148 * 16);
     if (d.resid_bf16) {
         auto* x = (__nv_bfloat16*)x_inout;
-        if (y_half) k_combine_h<__nv_bfloat16><<<cbh, 256, 0, s>>>(yh, w, sc.sh_gate, d.k, KK, d.H, T, x, nullptr);
-        else k_combine<__nv_bfloat16, float><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, x, nullptr);
+        if (y_half) launch_pdl(k_combine_h<__nv_bfloat16>, cbh, 256, 0, s, yh, w, sc.sh_gate, d.k, KK, d.H, T, x, nullptr);
+        else launch_pdl(k_combine<__nv_bfloat16, float>, cb, 256, 0, s, sc.y, w, sc.sh_gate, d.k, KK, d.H, T, x, nullptr);
     } else {
         auto* x = (float*)x_inout;
-        if (y_half) k_combine_h<float><<<cbh, 256, 0, s>>>(yh, w, sc.sh_gate, d.k, KK, d.H, T, x, nullptr);
-        else k_combine<float, float><<<cb, 256, 0, s>>>(sc.y, w, sc.sh_gate, d.k, KK, d.H, T, x, nullptr);
+        if (y_half) launch_pdl(k_combine_h<float>, cbh, 256, 0, s, yh, w, sc.sh_gate, d.k, KK, d.H, T, x, nullptr);
+        else launch_pdl(k_combine<float, float>, cb, 256, 0, s, sc.y, w, sc.sh_gate, d.k, KK, d.H, T, x, nullptr);
     }
     return cudaGetLastError();
 }
@@ -1152,65 +1557,70 @@ cudaError_t launch_combine_rows(const Dims& d, const uint16_t* y, const int* pos
     const int cb = (int)((n8 + 255) / 256 < 148 * 16 ? (n8 + 255) / 256 : 148 * 16);
     const __half* yh = reinterpret_cast<const __half*>(y);
     if (d.resid_bf16)
-        k_combine_h<__nv_bfloat16><<<cb, 256, 0, s>>>(yh, w, nullptr, d.k, d.k, d.H, T, (__nv_bfloat16*)x_inout, pos);
+        launch_pdl(k_combine_h<__nv_bfloat16>, cb, 256, 0, s, yh, w, nullptr, d.k, d.k, d.H, T, (__nv_bfloat16*)x_inout, pos);
     else
-        k_combine_h<float><<<cb, 256, 0, s>>>(yh, w, nullptr, d.k, d.k, d.H, T, (float*)x_inout, pos);
+        launch_pdl(k_combine_h<float>, cb, 256, 0, s, yh, w, nullptr, d.k, d.k, d.H, T, (float*)x_inout, pos);
     return cudaGetLastError();
 }
 
 cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const Scratch& sc, const float* fx,
                                    const int32_t* slot_of_sel, const float* w, void* x_inout, int T,
-                                   bool /*need_sh_gate*/, cudaStream_t s, int* launches) {
+                                   bool /*need_sh_gate*/, cudaStream_t s, int* launches, bool prepared,
+                                   unsigned long long* stamp) {
     const bool shared = lw.shared != nullptr;
     const int KK = d.k + (shared ? 1 : 0);
     const int NS = lw.n_slots + (shared ? 1 : 0);
     int nl = 0;
     cudaError_t e;
-    // 1. quantise fx
-    k_quant_q8<<<(unsigned)((d.H / QK) * T), 256, 0, s>>>(fx, d.H, sc.fx_q, sc.fx_d, sc.fx_bs);
-    ++nl;
+    // 1. quantise fx (done by the fused route kernel when `prepared`, with the dispatch)
+    if (!prepared) {
+        launch_pdl(k_quant_q8, (unsigned)((d.H / QK) * T), 256, 0, s, fx, d.H, sc.fx_q, sc.fx_d, sc.fx_bs);
+        ++nl;
+    }
     if (shared) {
         if ((e = launch_shared_gate(fx, lw.sh_gate_inp, d.H, T, sc.sh_gate, s)) != cudaSuccess) return e;
         ++nl;
     }
     // 2. group entries by slot (with a work list of the non-empty slots for the streaming kernels)
     const bool gu_sw = gateup_sw_supported(d, lw), dn_sw = down_sw_supported(d, lw);
-    if ((e = launch_dispatch(slot_of_sel, T, d.k, KK, lw.n_slots, sc, (gu_sw || dn_sw) ? (1 << 20) : 0, s, &nl))
-        != cudaSuccess)
+    if (prepared && !(gu_sw || dn_sw)) return cudaErrorInvalidValue;      // the work list must exist
+    if (!prepared &&
+        (e = launch_dispatch(slot_of_sel, T, d.k, KK, lw.n_slots, sc, (gu_sw || dn_sw) ? (1 << 20) : 0, s, &nl)) !=
+            cudaSuccess)
         return e;
     // 3. gate/up + SwiGLU: each selected slot's rows streamed once; otherwise weight rows held in
     //    registers across a slot's entries where the row fits in two units per lane
     const dim3 gu_grid(NS, (d.I + GU_ROWS - 1) / GU_ROWS);
     const int gu_units = (d.H / QK) * 8;
     if (gu_sw) {
-        if ((e = launch_gateup_sw(d, lw, sc, KK, s)) != cudaSuccess) return e;
+        if ((e = launch_gateup_sw(d, lw, sc, KK, s, stamp)) != cudaSuccess) return e;
     } else if (gu_units <= 32)
-        k_gateup_regs<1><<<gu_grid, 256, 0, s>>>(lw, d.H, d.I, KK, sc.offsets, sc.perm, sc.fx_q, sc.fx_d, sc.fx_bs, sc.h);
+        launch_pdl(k_gateup_regs<1>, gu_grid, 256, 0, s, lw, d.H, d.I, KK, sc.offsets, sc.perm, sc.fx_q, sc.fx_d, sc.fx_bs, sc.h);
     else if (gu_units <= 64)
-        k_gateup_regs<2><<<gu_grid, 256, 0, s>>>(lw, d.H, d.I, KK, sc.offsets, sc.perm, sc.fx_q, sc.fx_d, sc.fx_bs, sc.h);
+        launch_pdl(k_gateup_regs<2>, gu_grid, 256, 0, s, lw, d.H, d.I, KK, sc.offsets, sc.perm, sc.fx_q, sc.fx_d, sc.fx_bs, sc.h);
     else
-        k_gateup<<<gu_grid, 256, 0, s>>>(lw, d.H, d.I, KK, sc.offsets, sc.perm, sc.fx_q, sc.fx_d, sc.fx_bs, sc.h);
+        launch_pdl(k_gateup, gu_grid, 256, 0, s, lw, d.H, d.I, KK, sc.offsets, sc.perm, sc.fx_q, sc.fx_d, sc.fx_bs, sc.h);
     ++nl;
     // 4. quantise h
-    k_quant_q8<<<(unsigned)((d.I / QK) * T * KK), 256, 0, s>>>(sc.h, d.I, sc.h_q, sc.h_d, sc.h_bs);
+    launch_pdl(k_quant_q8, (unsigned)((d.I / QK) * T * KK), 256, 0, s, sc.h, d.I, sc.h_q, sc.h_d, sc.h_bs);
     ++nl;
     // 5. down (the widest row type present sets the lanes per row)
     const int nbI = d.I / QK;
     int dn_units = nbI * (lw.down_type == T_Q4K ? 8 : 4);
     if (shared) dn_units = std::max(dn_units, nbI * (lw.sh_down_type == T_Q4K ? 8 : 4));
     if (dn_sw) {
-        if ((e = launch_down_sw(d, lw, sc, s)) != cudaSuccess) return e;
+        if ((e = launch_down_sw(d, lw, sc, s, stamp ? stamp + 2 : nullptr)) != cudaSuccess) return e;
     } else if (dn_units <= 8)
-        k_down_regs<8><<<dim3(NS, (d.H + 63) / 64), 256, 0, s>>>(lw, d.H, d.I, sc.offsets, sc.perm, sc.h_q, sc.h_d,
+        launch_pdl(k_down_regs<8>, dim3(NS, (d.H + 63) / 64), 256, 0, s, lw, d.H, d.I, sc.offsets, sc.perm, sc.h_q, sc.h_d,
                                                                  sc.h_bs, sc.y);
     else if (dn_units <= 16)
-        k_down_regs<16><<<dim3(NS, (d.H + 31) / 32), 256, 0, s>>>(lw, d.H, d.I, sc.offsets, sc.perm, sc.h_q, sc.h_d,
+        launch_pdl(k_down_regs<16>, dim3(NS, (d.H + 31) / 32), 256, 0, s, lw, d.H, d.I, sc.offsets, sc.perm, sc.h_q, sc.h_d,
                                                                   sc.h_bs, sc.y);
     else if (dn_units <= 32)
-        k_down_regs<32><<<dim3(NS, (d.H + 15) / 16), 256, 0, s>>>(lw, d.H, d.I, sc.offsets, sc.perm, sc.h_q, sc.h_d,
+        launch_pdl(k_down_regs<32>, dim3(NS, (d.H + 15) / 16), 256, 0, s, lw, d.H, d.I, sc.offsets, sc.perm, sc.h_q, sc.h_d,
                                                                   sc.h_bs, sc.y);
     else
-        k_down<<<dim3(NS, (d.H + DN_ROWS - 1) / DN_ROWS), 256, 0, s>>>(lw, d.H, d.I, sc.offsets, sc.perm, sc.h_q,
+        launch_pdl(k_down, dim3(NS, (d.H + DN_ROWS - 1) / DN_ROWS), 256, 0, s, lw, d.H, d.I, sc.offsets, sc.perm, sc.h_q,
                                                                         sc.h_d, sc.h_bs, sc.y);
     ++nl;
     // 6. weighted combine into the residual

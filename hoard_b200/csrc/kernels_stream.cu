@@ -210,6 +210,7 @@ struct GuArgs {
     const int* xbs;
     float* h;
     unsigned* err;
+    unsigned long long* stamp;                           // optional {first start, last end}
 };
 
 // Consumers copy the activations of the round's tile i (its first GT_ACT entries) into `buf` and
@@ -332,7 +333,7 @@ __global__ void __launch_bounds__(SW_THREADS, SW_CTAS_PER_SM) k_gateup_sw(GuArgs
     __shared__ volatile int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntr = a.I / GT_R;
-    const int ntiles = *a.n_items * ntr;
+    pdl_launch_dependents();                             // the successor may be scheduled now
     if (threadIdx.x == 0) {
         for (int s = 0; s < GT_STAGES; ++s) {
             mbar_init(full + s, 1);
@@ -342,6 +343,9 @@ __global__ void __launch_bounds__(SW_THREADS, SW_CTAS_PER_SM) k_gateup_sw(GuArgs
         abort_flag = 0;
     }
     __syncthreads();
+    pdl_wait();                                          // the work list and activations are complete
+    if (a.stamp && threadIdx.x == 0) atomicMin(a.stamp, gtimer());
+    const int ntiles = *a.n_items * ntr;
     const int64_t nblk = (int64_t)a.I * GU_NB;
     constexpr int H = QK * GU_NB;
     const bool producer = warp == SW_CONSUMERS;
@@ -415,6 +419,7 @@ __global__ void __launch_bounds__(SW_THREADS, SW_CTAS_PER_SM) k_gateup_sw(GuArgs
         for (int q = n_issued - GT_STAGES > 0 ? n_issued - GT_STAGES : 0; q < n_issued; ++q)
             if (!mbar_wait(full + q % GT_STAGES, (q / GT_STAGES) & 1)) { atomicOr(a.err, 2u); break; }
     }
+    if (a.stamp && threadIdx.x == 0) atomicMax(a.stamp + 1, gtimer());
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -436,6 +441,7 @@ struct DnArgs {
     float* y;
     unsigned* err;
     int stages, stage_bytes, aent;
+    unsigned long long* stamp;                           // optional {first start, last end}
 };
 
 // piece p (16 bytes, 0..15) of a 256-block -> its position in the unit-interleaved shared layout
@@ -607,7 +613,7 @@ __global__ void __launch_bounds__(SW_THREADS, SW_CTAS_PER_SM) k_down_sw(DnArgs a
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = a.I / QK;
     const int ntr = a.H / DT_R;
-    const int ntiles = *a.n_items * ntr;
+    pdl_launch_dependents();                             // the successor may be scheduled now
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(full + s, 1);
@@ -617,6 +623,9 @@ __global__ void __launch_bounds__(SW_THREADS, SW_CTAS_PER_SM) k_down_sw(DnArgs a
         abort_flag = 0;
     }
     __syncthreads();
+    pdl_wait();                                          // the work list and activations are complete
+    if (a.stamp && threadIdx.x == 0) atomicMin(a.stamp, gtimer());
+    const int ntiles = *a.n_items * ntr;
     const int64_t nblk = (int64_t)a.H * nb;
     const bool producer = warp == SW_CONSUMERS;
     const DnLane DL(lane, warp);
@@ -694,6 +703,7 @@ __global__ void __launch_bounds__(SW_THREADS, SW_CTAS_PER_SM) k_down_sw(DnArgs a
         for (int qq = n_issued - S > 0 ? n_issued - S : 0; qq < n_issued; ++qq)
             if (!mbar_wait(full + qq % S, (qq / S) & 1)) { atomicOr(a.err, 2u); break; }
     }
+    if (a.stamp && threadIdx.x == 0) atomicMax(a.stamp + 1, gtimer());
 }
 
 int sw_grid(int ctas_per_sm = SW_CTAS_PER_SM) {
@@ -722,18 +732,19 @@ bool down_sw_supported(const Dims& d, const LayerWeights& lw) {
     return true;
 }
 
-cudaError_t launch_gateup_sw(const Dims& d, const LayerWeights& lw, const Scratch& sc, int KK, cudaStream_t s) {
+cudaError_t launch_gateup_sw(const Dims& d, const LayerWeights& lw, const Scratch& sc, int KK, cudaStream_t s,
+                             unsigned long long* stamp) {
     static_assert(GU_SMEM % 8 == 0, "mbarrier alignment");
     cudaError_t e = cudaFuncSetAttribute(k_gateup_sw, cudaFuncAttributeMaxDynamicSharedMemorySize, GU_SMEM);
     if (e != cudaSuccess) return e;
-    GuArgs a{lw, d.I, KK, sc.offsets, sc.perm, sc.items, sc.n_items, sc.fx_q, sc.fx_d, sc.fx_bs, sc.h, sc.sync};
-    k_gateup_sw<<<sw_grid(), SW_THREADS, GU_SMEM, s>>>(a);
-    return cudaGetLastError();
+    GuArgs a{lw, d.I, KK, sc.offsets, sc.perm, sc.items, sc.n_items, sc.fx_q, sc.fx_d, sc.fx_bs, sc.h, sc.sync, stamp};
+    return launch_pdl(k_gateup_sw, sw_grid(), SW_THREADS, GU_SMEM, s, a);
 }
 
-cudaError_t launch_down_sw(const Dims& d, const LayerWeights& lw, const Scratch& sc, cudaStream_t s) {
+cudaError_t launch_down_sw(const Dims& d, const LayerWeights& lw, const Scratch& sc, cudaStream_t s,
+                           unsigned long long* stamp) {
     const int nb = d.I / QK;
-    DnArgs a{lw, d.H, d.I, sc.offsets, sc.perm, sc.items, sc.n_items, sc.h_q, sc.h_d, sc.h_bs, sc.y, sc.sync, 0, 0, 0};
+    DnArgs a{lw, d.H, d.I, sc.offsets, sc.perm, sc.items, sc.n_items, sc.h_q, sc.h_d, sc.h_bs, sc.y, sc.sync, 0, 0, 0, stamp};
     a.stage_bytes = DT_R * nb * 210;                     // sized for Q6_K (Q4_K tiles use 144 per block)
     a.aent = d.I + d.I / 4 + 16;
     const int fixed = NAB * DT_ACT * a.aent;
@@ -750,8 +761,7 @@ cudaError_t launch_down_sw(const Dims& d, const LayerWeights& lw, const Scratch&
     const int smem = a.stages * a.stage_bytes + fixed + 2 * a.stages * 8;
     cudaError_t e = cudaFuncSetAttribute(k_down_sw, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    k_down_sw<<<sw_grid(per_sm), SW_THREADS, smem, s>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(k_down_sw, sw_grid(per_sm), SW_THREADS, smem, s, a);
 }
 
 }  // namespace hoard

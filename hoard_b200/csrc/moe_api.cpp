@@ -635,6 +635,27 @@ int hoard_moe_layers(hoard_moe_ctx* c, int layer0, int n_layers, void* x_inout, 
         const int64_t o = (int64_t)(l - layer0) * T * k;
         int32_t* sel = sel_out ? sel_out + o : c->sc.sel;
         float* w = w_out ? w_out + o : c->sc.w;
+        const LayerWeights lw = layer_weights(c, l);
+        const bool gemm = c->gemm_min_tokens > 0 && T >= c->gemm_min_tokens && tc_supported(c->dims, lw);
+        if (!gemm && route_fused_supported(c->dims, T) && gateup_sw_supported(c->dims, lw) &&
+            down_sw_supported(c->dims, lw)) {
+            // small batches: graph A's tail, the Q8_K of fx and the dispatch in one kernel, then the
+            // streaming expert kernels
+            const int KK = k + (lw.shared ? 1 : 0);
+            unsigned long long* st = c->trace && c->trace_cap >= 6 ? c->trace : nullptr;
+            HCHECK(c, launch_route_fused(c->dims, lw, c->sc, x_inout, T, KK, sel, w, 1 << 20, (cudaStream_t)stream, st));
+            int nl = 1;
+            HCHECK(c, launch_experts_grouped(c->dims, lw, c->sc, c->sc.fx, sel, w, x_inout, T, true,
+                                             (cudaStream_t)stream, &nl, true, st ? st + 2 : nullptr));
+            c->launches += nl;
+            c->routed_layer = l;
+            c->routed_T = T;
+            if (c->res.init) {
+                HCHECK(c, cudaEventRecord(c->res.used[l], (cudaStream_t)stream));
+                c->res.used_valid[l] = 1;
+            }
+            continue;
+        }
         int rc = hoard_moe_route(c, l, x_inout, T, sel, w, stream);
         if (rc) return rc;
         rc = hoard_moe_experts(c, l, nullptr, sel, nullptr, w, x_inout, T, stream);

@@ -162,7 +162,9 @@ int hoard_moe_sync_status(hoard_moe_ctx* ctx, hoard_stream stream);
  * [gemm: gate/up, down][cta < 4][item < 2][stage < 32][8]: 0 stage full at the MMA thread,
  * 1 committed, 2 B-row 0 dequant start, 3 B-row 0 saw the stage empty, 4 B-row 0 arrived,
  * 5 A-thread 0 saw the stage empty, 6 A-thread 0 issued; slot 7 of stages 0/1 = epilogue
- * start/end. */
+ * start/end. The small-batch layer path (2 <= T <= 64, every expert resident) writes, when
+ * capacity >= 6, {first start, last end} pairs of its fused route, gate/up and down kernels into
+ * words 0-5 by atomicMin / atomicMax: the caller sets the starts to UINT64_MAX and the ends to 0. */
 int hoard_moe_set_trace(hoard_moe_ctx* ctx, uint64_t* dev_buf, int64_t capacity);
 
 /* CTAs per persistent launch and stamps per (CTA, layer) of the trace layout. */

@@ -134,6 +134,23 @@ def test_c2_layer_parity(qwen_c2, T):
     check_against_oracle(spec, L, x, out, sel, w)
 
 
+@pytest.mark.parametrize("T", [2, 16, 63])
+def test_c2_fused_route_equals_split(qwen_c2, T):
+    """T <= 64 with every expert resident: the layer call runs RMSNorm, router, top-k, the Q8_K of fx and
+    the dispatch as one kernel; its routing and output equal those of the separate route + experts
+    calls bit for bit (same summation order of the logits, same quantisation)."""
+    spec, L, ctx = qwen_c2
+    x_np = make_x(T, spec.H, seed=3000 + T)
+    a, sa, wa = run_layer(ctx, x_np)
+    x = torch.from_numpy(x_np).cuda(DEV)
+    sel, w = ctx.route(0, x)
+    ctx.experts(0, sel, w, x)
+    ctx.sync_status()
+    assert np.array_equal(sel.cpu().numpy(), sa)
+    assert np.array_equal(w.cpu().numpy().view(np.uint32), wa.view(np.uint32))
+    assert np.array_equal(x.cpu().numpy().view(np.uint32), a.view(np.uint32))
+
+
 def test_c2_bf16_residual(qwen_c2):
     spec, L, _ = qwen_c2
     ctx = make_ctx(spec, resid=torch.bfloat16, max_tokens=4)
@@ -227,6 +244,25 @@ def test_out_of_range_slot_is_reported(small):
     ctx.sync_status()            # cleared, context still usable
     out, _, _ = run_layer(ctx, make_x(1, spec.H, seed=1))
     assert np.isfinite(out).all()
+
+
+def test_skipped_entry_leaves_later_calls_exact(small):
+    """A skipped entry (slot out of range) still counts towards its token's fused combine, so a later
+    call on the same context -- before the error is read -- is exact."""
+    spec, L, ctx = small
+    x = torch.from_numpy(make_x(3, spec.H, seed=9)).cuda(DEV)
+    sel, w = ctx.route(0, x)
+    bad = sel.clone()
+    bad[2, 1] = -7
+    ctx.experts(0, sel, w, x, slot_of_sel=bad)
+    x2_np = make_x(5, spec.H, seed=10)
+    x2 = torch.from_numpy(x2_np).cuda(DEV)
+    sel2 = torch.empty(5, ctx.k, dtype=torch.int32, device=x2.device)
+    w2 = torch.empty(5, ctx.k, dtype=torch.float32, device=x2.device)
+    ctx.layer(0, x2, sel2, w2)
+    with pytest.raises(moe.HoardError):
+        ctx.sync_status()
+    check_against_oracle(spec, L, x2_np, x2.cpu().numpy(), sel2.cpu().numpy(), w2.cpu().numpy())
 
 
 def test_argument_errors(small):
