@@ -528,22 +528,42 @@ __global__ void __launch_bounds__(tc_threads(MODE), 1) k_tc_experts(TcArgs a) {
         } else {
             // ---------------- B dequant (256 threads), then the gate/up epilogue ----------------
             const int r = tid - B_TID0;                          // B row within the N block
-            const int64_t n = (int64_t)nb_out * TC_N + r;        // weight row
-            const bool sh = slot >= a.lw.n_slots;
-            const uint8_t* base = sh ? a.lw.shared : a.lw.pool + (int64_t)slot * a.lw.slot_stride;
-            const uint8_t* m0 = MODE == 0 ? base : base + (sh ? a.lw.sh_off_down : a.lw.off_down);
-            const uint8_t* m1 = base + (sh ? a.lw.sh_off_up : a.lw.off_up);
-            const int64_t row_blk = n * nbK;
-            auto issue = [&](int kc) {                           // raw bytes of stage kc, one commit group
+            // this row's weight matrices (m0 gate or down, m1 up) and first block for item `itm`
+            auto row_of = [&](int itm, const uint8_t*& m0_, const uint8_t*& m1_, int64_t& rb_) {
+                const int2 itx = a.items[itm / NBLK];
+                const int sl = itx.x;
+                const int64_t nrow = (int64_t)(itm - (itm / NBLK) * NBLK) * TC_N + r;
+                const bool shx = sl >= a.lw.n_slots;
+                const uint8_t* bs = shx ? a.lw.shared : a.lw.pool + (int64_t)sl * a.lw.slot_stride;
+                m0_ = MODE == 0 ? bs : bs + (shx ? a.lw.sh_off_down : a.lw.off_down);
+                m1_ = bs + (shx ? a.lw.sh_off_up : a.lw.off_up);
+                rb_ = nrow * nbK;
+            };
+            const uint8_t *m0, *m1;
+            int64_t row_blk;
+            row_of(item, m0, m1, row_blk);
+            const int next = item + gridDim.x;                   // this CTA's next item, if any
+            const uint8_t *m0n = m0, *m1n = m1;
+            int64_t row_blk_n = row_blk;
+            if (next < n_items) row_of(next, m0n, m1n, row_blk_n);
+            // raw bytes of stage kc (one commit group, ring slot by the CTA's stage counter); stages past
+            // this item's last are the next item's first ones, so a new item starts on bytes in flight
+            auto issue = [&](int kc) {
+                uint8_t* slot_p = ring + ((it0 + kc) % RAWD) * RAW_BYTES;
                 if (kc < KC) {
-                    uint8_t* slot_p = ring + (kc % RAWD) * RAW_BYTES;
                     Seg<TYPE>::issue(slot_p, r, m0, nblk_total, row_blk + (kc >> 2), kc & 3);
                     if (MODE == 0) Seg<TYPE>::issue(slot_p + RAW_MAT, r, m1, nblk_total, row_blk + (kc >> 2), kc & 3);
+                } else if (next < n_items) {
+                    const int kn = kc - KC;
+                    Seg<TYPE>::issue(slot_p, r, m0n, nblk_total, row_blk_n + (kn >> 2), kn & 3);
+                    if (MODE == 0) Seg<TYPE>::issue(slot_p + RAW_MAT, r, m1n, nblk_total, row_blk_n + (kn >> 2), kn & 3);
                 }
                 asm volatile("cp.async.commit_group;" ::: "memory");
             };
+            if (item_no == 0) {                                  // later items' first stages were issued by the previous one
 #pragma unroll
-            for (int j = 0; j < RAWD; ++j) issue(j);
+                for (int j = 0; j < RAWD; ++j) issue(j);
+            }
             typename Seg<TYPE>::Hdr h0c = Seg<TYPE>::load_hdr(m0, nblk_total, row_blk), h0n = h0c;
             typename Seg<TYPE>::Hdr h1c = h0c, h1n = h0c;
             if (MODE == 0) h1c = h1n = Seg<TYPE>::load_hdr(m1, nblk_total, row_blk);
@@ -566,7 +586,7 @@ __global__ void __launch_bounds__(tc_threads(MODE), 1) k_tc_experts(TcArgs a) {
                 }
                 asm volatile("cp.async.wait_group %0;" ::"n"(RAWD - 1) : "memory");
                 if (r == 0) TC_STAMP(item_no, kc, 2);
-                const uint8_t* slot_p = ring + (kc % RAWD) * RAW_BYTES;
+                const uint8_t* slot_p = ring + ((it0 + kc) % RAWD) * RAW_BYTES;
                 Seg<TYPE> sg;
                 sg.read(slot_p, r);
                 uint4 v[8];
