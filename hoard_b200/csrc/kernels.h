@@ -82,7 +82,7 @@ cudaError_t launch_transpose(const float* src, float* dst, int R, int C, cudaStr
 // Router: fx, sel, w for T tokens (three launches). `part` holds router_partial_elems() doubles.
 int64_t router_partial_elems(int max_tokens, int E);
 cudaError_t launch_route(const Dims& d, const LayerWeights& lw, const void* x, int T, float* fx, int32_t* sel,
-                         float* w, double* part, cudaStream_t s, int* launches);
+                         float* w, double* part, cudaStream_t s, int* launches, unsigned* err);
 
 // The grouped expert path for any T (fx given), adding into x_inout.
 cudaError_t launch_experts_grouped(const Dims& d, const LayerWeights& lw, const Scratch& sc, const float* fx,
@@ -121,6 +121,10 @@ cudaError_t launch_combine(const Dims& d, const Scratch& sc, const float* w, voi
 
 // The tensor-core grouped GEMM expert path (prefill / batched tokens), adding into x_inout.
 bool tc_supported(const Dims& d, const LayerWeights& lw);
+// Router logits of large batches on the tensor cores (tf32 with a hi/lo split, f32-accurate): partial
+// sums of `ksplit` K ranges into part[ksplit][T][E] (double), the layout k_route_topk sums.
+cudaError_t launch_router_tc(const float* fx, const float* w_router, int T, int H, int E, int ksplit, double* part,
+                             unsigned* err, cudaStream_t s);
 int64_t tc_max_items(int T, int KK, int n_slots);
 int64_t tc_trace_elems();   // stamps written by one call when tracing: [gate/up, down][cta][item][stage][slot]
 cudaError_t launch_experts_tc(const Dims& d, const LayerWeights& lw, const Scratch& sc, const float* fx,

@@ -427,89 +427,14 @@ __global__ void __launch_bounds__(TOPK_SMALL_THREADS) k_route_topk(const double*
     route_topk_row<NV>(lg[tt], E, k, renorm, threadIdx.x & 31, sel + (int64_t)t * k, w + (int64_t)t * k);
 }
 
-// Large batches: 128 tokens x 128 experts per CTA, 8 x 8 accumulators per thread (f32 over the CTA's K
-// range; the K splits are summed in double by k_route_topk). K chunks of 32 are staged through
-// registers into shared memory: fx transposed to [k][token], the router from its [H][E] transpose
-// (rows already k-major). Thread (tg, eg) = (tid / 16, tid % 16) owns tokens 8tg.. and experts 8eg..:
-// per k step two 16-byte loads of each operand for 64 FMAs, token loads broadcast within a warp.
-constexpr int RB_TT = 128, RB_EB = 128, RB_KC = 32, RB_PAD = 4;
-constexpr int RB_MIN_T = 1024;         // T at or above which the large-tile kernel runs
-constexpr int RB_TARGET_CTAS = 148;    // one CTA per SM (64 accumulators + staging need > 128 registers)
-
-__global__ void __launch_bounds__(256, 1) k_router_logits_big(const float* __restrict__ fx,
-                                                              const float* __restrict__ w_t, int T, int H, int E,
-                                                              int klen, double* __restrict__ part) {
-    pdl_enter();
-    __shared__ __align__(16) float sf[RB_KC][RB_TT + RB_PAD];
-    __shared__ __align__(16) float sw[RB_KC][RB_EB];
-    const int tid = threadIdx.x;
-    const int tg = tid >> 4, eg = tid & 15;
-    const int t0 = blockIdx.x * RB_TT, e0 = blockIdx.y * RB_EB;
-    const int k0 = blockIdx.z * klen;
-    float acc[8][8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
-    // staging: fx rows (128 tokens x 32 k = 1024 float4, four per thread: token ft, k quad fq) and
-    // router rows (32 k x 128 experts = 1024 float4, four per thread: k wk, expert quad wq)
-    float4 pf[4], pw[4];
-    auto fetch = [&](int kb) {
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int idx = tid + 256 * r;
-            const int ft = idx >> 3, fq = idx & 7;
-            pf[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (t0 + ft < T) pf[r] = __ldg(reinterpret_cast<const float4*>(fx + (int64_t)(t0 + ft) * H + kb + 4 * fq));
-            const int wk = idx >> 5, wq = idx & 31;
-            pw[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (e0 + 4 * wq < E)
-                pw[r] = __ldg(reinterpret_cast<const float4*>(w_t + (int64_t)(kb + wk) * E + e0 + 4 * wq));
-        }
-    };
-    fetch(k0);
-    for (int kb = k0; kb < k0 + klen; kb += RB_KC) {
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int idx = tid + 256 * r;
-            const int ft = idx >> 3, fq = idx & 7;
-            sf[4 * fq][ft] = pf[r].x;
-            sf[4 * fq + 1][ft] = pf[r].y;
-            sf[4 * fq + 2][ft] = pf[r].z;
-            sf[4 * fq + 3][ft] = pf[r].w;
-            const int wk = idx >> 5, wq = idx & 31;
-            *reinterpret_cast<float4*>(&sw[wk][4 * wq]) = pw[r];
-        }
-        __syncthreads();
-        if (kb + RB_KC < k0 + klen) fetch(kb + RB_KC);     // the next chunk in flight during this one
-#pragma unroll 4
-        for (int kk = 0; kk < RB_KC; ++kk) {
-            const float4 f0 = *reinterpret_cast<const float4*>(&sf[kk][8 * tg]);
-            const float4 f1 = *reinterpret_cast<const float4*>(&sf[kk][8 * tg + 4]);
-            const float4 w0 = *reinterpret_cast<const float4*>(&sw[kk][8 * eg]);
-            const float4 w1 = *reinterpret_cast<const float4*>(&sw[kk][8 * eg + 4]);
-            const float fv[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
-            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(fv[i], wv[j], acc[i][j]);
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int t = t0 + 8 * tg + i;
-        if (t >= T) continue;
-        double* dst = part + ((int64_t)blockIdx.z * T + t) * E + e0 + 8 * eg;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            if (e0 + 8 * eg + j < E) dst[j] = (double)acc[i][j];
-    }
-}
+// Large batches (T >= RB_MIN_T): the logits come from the tensor-core router GEMM (launch_router_tc,
+// kernels_prefill.cu) in RB_KC-aligned K splits, one 128-token x 128-expert tile per CTA.
+constexpr int RB_TT = 128, RB_KC = 32;
+constexpr int RB_MIN_T = 1024;         // T at or above which the tensor-core router runs
+constexpr int RB_TARGET_CTAS = 148;    // K splits sized for about one CTA per SM
 
 int router_ksplit_big(int T, int E, int H) {
-    const int tiles = ((T + RB_TT - 1) / RB_TT) * ((E + RB_EB - 1) / RB_EB);
+    const int tiles = ((T + RB_TT - 1) / RB_TT) * ((E + 127) / 128);
     int ks = RB_TARGET_CTAS / tiles;
     const int max_ks = H / (4 * RB_KC);                  // at least 4 chunks per split
     if (ks > max_ks) ks = max_ks;
@@ -534,16 +459,16 @@ int64_t router_partial_elems(int max_tokens, int E) {
 }
 
 cudaError_t launch_route(const Dims& d, const LayerWeights& lw, const void* x, int T, float* fx, int32_t* sel,
-                         float* w, double* part, cudaStream_t s, int* launches) {
+                         float* w, double* part, cudaStream_t s, int* launches, unsigned* err) {
     cudaError_t e0 = d.resid_bf16
         ? launch_rmsnorm_rows((const __nv_bfloat16*)x, T, d.H, d.eps, lw.w_norm, fx, s)
         : launch_rmsnorm_rows((const float*)x, T, d.H, d.eps, lw.w_norm, fx, s);
     if (e0 != cudaSuccess) return e0;
     int ks;
-    if (T >= RB_MIN_T && d.E % 4 == 0 && d.H % RB_KC == 0) {
+    if (T >= RB_MIN_T && d.H % RB_KC == 0) {
         ks = router_ksplit_big(T, d.E, d.H);
-        const dim3 grid((T + RB_TT - 1) / RB_TT, (d.E + RB_EB - 1) / RB_EB, ks);
-        launch_pdl(k_router_logits_big, grid, 256, 0, s, fx, lw.w_router_t, T, d.H, d.E, d.H / ks, part);
+        cudaError_t e = launch_router_tc(fx, lw.w_router, T, d.H, d.E, ks, part, err, s);
+        if (e != cudaSuccess) return e;
     } else {
         ks = router_ksplit(T, d.E, d.H);
         const dim3 grid((T + RL_TT - 1) / RL_TT, (d.E + RL_EB - 1) / RL_EB, ks);

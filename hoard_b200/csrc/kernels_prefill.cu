@@ -706,6 +706,176 @@ __global__ void __launch_bounds__(256) k_q8_to_f16(const float* __restrict__ x, 
     reinterpret_cast<uint4*>(out + b * QK)[lane] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
 }
 
+// ---------------------------------------------------------------------------------------------
+// Router logits of large batches on the tensor cores (tcgen05 kind::tf32), f32-accurate by a
+// three-term split: x = x_hi + x_lo and w = w_hi + w_lo with x_hi = x rounded to tf32 and x_lo =
+// x - x_hi (exact in f32) rounded to tf32; x . w is taken as x_hi.w_hi + x_hi.w_lo + x_lo.w_hi with
+// f32 accumulation in tensor memory (the dropped x_lo.w_lo and the rounding of the low parts are
+// ~2^-22 of |x||w| per product). CTA (128-token tile, N-expert tile, K split z): warp 0's lane 0 issues
+// the MMAs (M = 128, N, K = 8; three per K step); warps 1-8 each load one row's 32-value K segment per
+// stage (threads 0-127 of them the token rows of fx, 128-255 the expert rows of the router), split it
+// and store the hi and lo parts 128B-swizzled; warps 1-4 then read the accumulator rows and write the
+// split's partial logits (double) in the layout k_route_topk sums: part[z][t][e].
+// ---------------------------------------------------------------------------------------------
+namespace {
+
+constexpr int RT_M = 128;                  // tokens per tile (UMMA M)
+constexpr int RT_NMAX = 128;               // experts per tile (UMMA N: a multiple of 16)
+constexpr int RT_STAGES = 3;
+constexpr int RT_THREADS = 288;
+constexpr int RT_A_BYTES = RT_M * 128;     // one 128-row x 32-value f32 tile (hi or lo)
+constexpr int RT_B_BYTES = RT_NMAX * 128;
+constexpr int RT_STAGE = 2 * RT_A_BYTES + 2 * RT_B_BYTES;
+constexpr size_t RT_SMEM = (size_t)RT_STAGES * RT_STAGE + 1024;
+
+__device__ __forceinline__ float tf32_round(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+}  // namespace
+
+struct RouterTcArgs {
+    const float* fx;       // [T][H]
+    const float* w;        // [E][H]
+    int T, H, E, N, klen;  // N experts per tile (multiple of 16, <= RT_NMAX); klen K per split (multiple of 32)
+    double* part;          // [splits][T][E]
+    unsigned* err;
+};
+
+__global__ void __launch_bounds__(RT_THREADS, 1) k_router_tc(const RouterTcArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t full[RT_STAGES], empty[RT_STAGES], done_bar;
+    __shared__ uint32_t s_tmem;
+    __shared__ volatile int s_abort;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int t0 = blockIdx.x * RT_M, e0 = blockIdx.y * a.N, k0 = blockIdx.z * a.klen;
+    const int KS = a.klen / 32;
+    if (tid == 0) {
+        for (int s = 0; s < RT_STAGES; ++s) {
+            bar_init(&full[s], RT_THREADS - 32);
+            bar_init(&empty[s], 1);
+        }
+        bar_init(&done_bar, 1);
+        s_abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&s_tmem)),
+                     "r"(RT_NMAX) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    // D f32 (bits 4-5 = 1), A and B tf32 (bits 7-9, 10-12 = 2), both K-major, N >> 3, M >> 4
+    const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(a.N >> 3) << 17) | ((uint32_t)(RT_M >> 4) << 24);
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int kc = 0; kc < KS; ++kc) {
+                const int s = kc % RT_STAGES;
+                if (!bar_wait(&full[s], (kc / RT_STAGES) & 1, &s_abort)) break;
+                fence_async_smem();
+                tc_fence_after();
+                const uint8_t* st = smem + s * RT_STAGE;
+                const uint64_t ahi = sw128_desc(st), alo = sw128_desc(st + RT_A_BYTES);
+                const uint64_t bhi = sw128_desc(st + 2 * RT_A_BYTES), blo = sw128_desc(st + 2 * RT_A_BYTES + RT_B_BYTES);
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {           // K = 8 per MMA: +32 bytes = +2 in the descriptor
+                    umma_tf32(tmem, ahi + 2 * ks, bhi + 2 * ks, idesc, (kc > 0 || ks > 0) ? 1u : 0u);
+                    umma_tf32(tmem, ahi + 2 * ks, blo + 2 * ks, idesc, 1u);
+                    umma_tf32(tmem, alo + 2 * ks, bhi + 2 * ks, idesc, 1u);
+                }
+                umma_commit(&empty[s]);                  // the stage is free once these MMAs have read it
+            }
+            umma_commit(&done_bar);                      // the accumulators are complete
+        }
+        __syncwarp();
+    } else {
+        // one row per thread: threads 0-127 token rows, 128-255 expert rows (those < N)
+        const int p = tid - 32;
+        const bool is_a = p < RT_M;
+        const int r = is_a ? p : p - RT_M;
+        const bool active = is_a || r < a.N;
+        const bool valid = is_a ? t0 + r < a.T : (r < a.N && e0 + r < a.E);
+        const float* src = is_a ? a.fx + (int64_t)(t0 + r) * a.H + k0 : a.w + (int64_t)(e0 + r) * a.H + k0;
+        float4 nxt[8];
+        auto load = [&](int kc) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                nxt[i] = valid ? __ldg(reinterpret_cast<const float4*>(src + 32 * kc) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        };
+        load(0);
+        for (int kc = 0; kc < KS; ++kc) {
+            const int s = kc % RT_STAGES;
+            float4 v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = nxt[i];
+            if (kc + 1 < KS) load(kc + 1);               // the next segment in flight during this one
+            if (kc >= RT_STAGES && !bar_wait(&empty[s], ((kc / RT_STAGES) - 1) & 1, &s_abort)) break;
+            if (s_abort) break;
+            if (active) {
+                uint8_t* st = smem + s * RT_STAGE + (is_a ? 0 : 2 * RT_A_BYTES);
+                const int part_bytes = is_a ? RT_A_BYTES : RT_B_BYTES;
+                uint4 hi[8], lo[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float h0 = tf32_round(v[i].x), h1 = tf32_round(v[i].y), h2 = tf32_round(v[i].z),
+                                h3 = tf32_round(v[i].w);
+                    hi[i] = make_uint4(__float_as_uint(h0), __float_as_uint(h1), __float_as_uint(h2), __float_as_uint(h3));
+                    lo[i] = make_uint4(__float_as_uint(tf32_round(v[i].x - h0)), __float_as_uint(tf32_round(v[i].y - h1)),
+                                       __float_as_uint(tf32_round(v[i].z - h2)), __float_as_uint(tf32_round(v[i].w - h3)));
+                }
+                store_row_sw128(st, r, hi);
+                store_row_sw128(st + part_bytes, r, lo);
+            }
+            fence_async_smem();
+            bar_arrive(&full[s]);
+        }
+    }
+    // epilogue: warps 1-4 read the accumulator rows (warp w reaches TMEM lanes 32 * (w % 4) ..)
+    if (warp >= 1 && warp <= 4) {
+        const bool ok = __all_sync(0xFFFFFFFFu, bar_wait(&done_bar, 0, &s_abort));
+        if (ok) {
+            tc_fence_after();
+            const int q = warp & 3, m = 32 * q + lane, t = t0 + m;
+            const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+            double* dst = a.part + ((int64_t)blockIdx.z * a.T + t) * a.E + e0;
+            float v[32];
+            for (int cc = 0; cc * 32 < a.N; ++cc) {
+                tmem_ld32(lane_base + 32 * cc, v);
+                if (t < a.T) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int col = 32 * cc + i;
+                        if (col < a.N && e0 + col < a.E) dst[col] = (double)v[i];
+                    }
+                }
+            }
+        }
+    }
+    // teardown: the MMAs have completed (or the CTA gave up and drains them), then free the tensor memory
+    if (warp == 0 && lane == 0) bar_drain(&done_bar, 0);
+    tc_fence_before();
+    __syncthreads();
+    if (s_abort && tid == 0) atomicOr(a.err, 2u);
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(RT_NMAX) : "memory");
+    }
+}
+
 namespace {
 
 int tc_grid() {
@@ -746,6 +916,24 @@ bool tc_supported(const Dims& d, const LayerWeights& lw) {
 }
 
 int64_t tc_max_items(int T, int KK, int n_slots) { return ((int64_t)T * KK + TC_M - 1) / TC_M + n_slots + 1; }
+
+cudaError_t launch_router_tc(const float* fx, const float* w_router, int T, int H, int E, int ksplit, double* part,
+                             unsigned* err, cudaStream_t s) {
+    if (T <= 0 || E <= 0 || H % (32 * ksplit) != 0) return cudaErrorInvalidValue;
+    static unsigned long long attr_set = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || !(attr_set >> dev & 1ull)) {
+        cudaError_t e = cudaFuncSetAttribute(k_router_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RT_SMEM);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) attr_set |= 1ull << dev;
+    }
+    RouterTcArgs a{fx, w_router, T, H, E, 0, H / ksplit, part, err};
+    a.N = E >= RT_NMAX ? RT_NMAX : ((E + 15) / 16) * 16;
+    const dim3 grid((T + RT_M - 1) / RT_M, (E + a.N - 1) / a.N, ksplit);
+    k_router_tc<<<grid, RT_THREADS, RT_SMEM, s>>>(a);
+    return cudaGetLastError();
+}
 
 // Expert FFN of R rows that arrive already quantised (Q8_K q*d as f16, [R][H]), each bound to one
 // pool slot: the expert-parallel receive side. y_out[r] (f16 [R][H]) is row r's expert output.

@@ -417,7 +417,7 @@ int hoard_moe_route(hoard_moe_ctx* c, int layer, const void* x, int T, int32_t* 
     if ((rc = check_ready(c, layer))) return rc;
     const LayerWeights lw = layer_weights(c, layer);
     int nl = 0;
-    HCHECK(c, launch_route(c->dims, lw, x, T, c->sc.fx, sel, w, c->sc.rpart, (cudaStream_t)stream, &nl));
+    HCHECK(c, launch_route(c->dims, lw, x, T, c->sc.fx, sel, w, c->sc.rpart, (cudaStream_t)stream, &nl, c->sc.sync));
     c->launches += nl;
     c->routed_layer = layer;
     c->routed_T = T;
