@@ -1343,7 +1343,7 @@ cudaError_t launch_shared_gate(const float* fx, const float* gate_inp, int H, in
 // Large batches: per-CTA shared-memory histograms added into global counts, a one-CTA scan, and a
 // scatter through global cursors (warp-aggregated atomics).
 constexpr int DISP_SMALL = 4096;     // entries handled by the single-CTA kernel
-constexpr int DISP_CHUNK = 4096;     // entries per CTA in the multi-CTA kernels
+constexpr int DISP_CHUNK = 512;      // entries per CTA in the multi-CTA kernels (one per thread)
 
 __global__ void __launch_bounds__(512) k_disp_count(const int32_t* __restrict__ slot_of, int T, int k, int KK,
                                                     int n_slots, int* __restrict__ gcount, unsigned* err,
