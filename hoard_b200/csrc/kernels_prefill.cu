@@ -708,14 +708,16 @@ __global__ void __launch_bounds__(256) k_q8_to_f16(const float* __restrict__ x, 
 
 // ---------------------------------------------------------------------------------------------
 // Router logits of large batches on the tensor cores (tcgen05 kind::tf32), f32-accurate by a
-// three-term split: x = x_hi + x_lo and w = w_hi + w_lo with x_hi = x rounded to tf32 and x_lo =
-// x - x_hi (exact in f32) rounded to tf32; x . w is taken as x_hi.w_hi + x_hi.w_lo + x_lo.w_hi with
-// f32 accumulation in tensor memory (the dropped x_lo.w_lo and the rounding of the low parts are
-// ~2^-22 of |x||w| per product). CTA (128-token tile, N-expert tile, K split z): warp 0's lane 0 issues
-// the MMAs (M = 128, N, K = 8; three per K step); warps 1-8 each load one row's 32-value K segment per
-// stage (threads 0-127 of them the token rows of fx, 128-255 the expert rows of the router), split it
-// and store the hi and lo parts 128B-swizzled; warps 1-4 then read the accumulator rows and write the
-// split's partial logits (double) in the layout k_route_topk sums: part[z][t][e].
+// three-term split: x = x_hi + x_lo and w = w_hi + w_lo with x_hi = x truncated to tf32 and x_lo =
+// x - x_hi (exact in f32, read by the tensor core truncated to tf32); x . w is taken as
+// x_hi.w_hi + x_hi.w_lo + x_lo.w_hi with f32 accumulation in tensor memory (the dropped x_lo.w_lo
+// and the truncation of the low parts are ~2^-21 of |x||w| per product). CTA (128-token tile,
+// N-expert tile, K split z): warp 0's lane 0 issues the MMAs (M = 128, N, K = 8; three per K step);
+// warps 1-8 load the stage's 32-value K segments of the 128 token rows of fx and the N expert rows of
+// the router as 16-byte pieces (eight lanes per row, so a warp's loads cover whole 128-byte lines: a
+// row per thread saturated the L1 tag stage, 87 % of L1TEX throughput for 13 % tensor-pipe activity),
+// split them and store the hi and lo parts 128B-swizzled; warps 1-4 then read the accumulator rows and
+// write the split's partial logits (double) in the layout k_route_topk sums: part[z][t][e].
 // ---------------------------------------------------------------------------------------------
 namespace {
 
@@ -728,11 +730,8 @@ constexpr int RT_B_BYTES = RT_NMAX * 128;
 constexpr int RT_STAGE = 2 * RT_A_BYTES + 2 * RT_B_BYTES;
 constexpr size_t RT_SMEM = (size_t)RT_STAGES * RT_STAGE + 1024;
 
-__device__ __forceinline__ float tf32_round(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
-}
+// the tf32 value the tensor core reads from an f32 word: the low 13 mantissa bits dropped
+__device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                           uint32_t accumulate) {
     asm volatile(
@@ -803,42 +802,54 @@ __global__ void __launch_bounds__(RT_THREADS, 1) k_router_tc(const RouterTcArgs 
         }
         __syncwarp();
     } else {
-        // one row per thread: threads 0-127 token rows, 128-255 expert rows (those < N)
+        // 16-byte pieces: piece idx = p + 256 j (j < 8) is chunk idx % 8 of row idx / 8 (rows 0-127 the
+        // token rows of fx, 128-255 the expert rows of the router), so that a warp's loads cover four
+        // whole 128-byte row segments
         const int p = tid - 32;
-        const bool is_a = p < RT_M;
-        const int r = is_a ? p : p - RT_M;
-        const bool active = is_a || r < a.N;
-        const bool valid = is_a ? t0 + r < a.T : (r < a.N && e0 + r < a.E);
-        const float* src = is_a ? a.fx + (int64_t)(t0 + r) * a.H + k0 : a.w + (int64_t)(e0 + r) * a.H + k0;
+        const float* src[8];
+        bool valid[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int idx = p + 256 * j, row = idx >> 3, c = idx & 7;
+            const bool is_a = row < RT_M;
+            const int rr = is_a ? row : row - RT_M;
+            valid[j] = is_a ? t0 + rr < a.T : (rr < a.N && e0 + rr < a.E);
+            src[j] = (is_a ? a.fx + (int64_t)(t0 + rr) * a.H : a.w + (int64_t)(e0 + rr) * a.H) + k0 + 4 * c;
+        }
         float4 nxt[8];
         auto load = [&](int kc) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                nxt[i] = valid ? __ldg(reinterpret_cast<const float4*>(src + 32 * kc) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int j = 0; j < 8; ++j)
+                nxt[j] = valid[j] ? __ldg(reinterpret_cast<const float4*>(src[j] + 32 * kc)) : make_float4(0.f, 0.f, 0.f, 0.f);
         };
         load(0);
         for (int kc = 0; kc < KS; ++kc) {
             const int s = kc % RT_STAGES;
             float4 v[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = nxt[i];
+            for (int j = 0; j < 8; ++j) v[j] = nxt[j];
             if (kc + 1 < KS) load(kc + 1);               // the next segment in flight during this one
             if (kc >= RT_STAGES && !bar_wait(&empty[s], ((kc / RT_STAGES) - 1) & 1, &s_abort)) break;
             if (s_abort) break;
-            if (active) {
-                uint8_t* st = smem + s * RT_STAGE + (is_a ? 0 : 2 * RT_A_BYTES);
-                const int part_bytes = is_a ? RT_A_BYTES : RT_B_BYTES;
-                uint4 hi[8], lo[8];
+            uint8_t* st = smem + s * RT_STAGE;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float h0 = tf32_round(v[i].x), h1 = tf32_round(v[i].y), h2 = tf32_round(v[i].z),
-                                h3 = tf32_round(v[i].w);
-                    hi[i] = make_uint4(__float_as_uint(h0), __float_as_uint(h1), __float_as_uint(h2), __float_as_uint(h3));
-                    lo[i] = make_uint4(__float_as_uint(tf32_round(v[i].x - h0)), __float_as_uint(tf32_round(v[i].y - h1)),
-                                       __float_as_uint(tf32_round(v[i].z - h2)), __float_as_uint(tf32_round(v[i].w - h3)));
-                }
-                store_row_sw128(st, r, hi);
-                store_row_sw128(st + part_bytes, r, lo);
+            for (int j = 0; j < 8; ++j) {
+                const int idx = p + 256 * j, row = idx >> 3, c = idx & 7;
+                const bool is_a = row < RT_M;
+                const int rr = is_a ? row : row - RT_M;
+                if (!is_a && rr >= a.N) continue;            // expert rows past the tile are not read
+                // hi = x with the mantissa bits below tf32 cleared; lo = x - hi (exact in f32), of which
+                // the tensor core reads the leading 11 bits
+                const float h0 = tf32_trunc(v[j].x), h1 = tf32_trunc(v[j].y), h2 = tf32_trunc(v[j].z),
+                            h3 = tf32_trunc(v[j].w);
+                const uint4 hi = make_uint4(__float_as_uint(h0), __float_as_uint(h1), __float_as_uint(h2), __float_as_uint(h3));
+                const uint4 lo = make_uint4(__float_as_uint(v[j].x - h0), __float_as_uint(v[j].y - h1),
+                                            __float_as_uint(v[j].z - h2), __float_as_uint(v[j].w - h3));
+                uint8_t* th = st + (is_a ? 0 : 2 * RT_A_BYTES);
+                const int part_bytes = is_a ? RT_A_BYTES : RT_B_BYTES;
+                const int off = rr * 128 + ((c ^ (rr & 7)) << 4);    // 128B swizzle
+                *reinterpret_cast<uint4*>(th + off) = hi;
+                *reinterpret_cast<uint4*>(th + part_bytes + off) = lo;
             }
             fence_async_smem();
             bar_arrive(&full[s]);
