@@ -739,6 +739,7 @@ constexpr int RF_MAX_T = 64;
 constexpr int RF_MAX_E = 512;
 constexpr int RF_MAX_CH = 64;          // 32-wide K chunks per row (H <= 2048)
 constexpr int RF_CPAD = 36;            // floats per staged K chunk (padding spreads the lanes' reads over the banks)
+constexpr int RF_SMEM_MAX = 96 * 1024;  // dynamic shared memory limit of the kernel (two CTAs per SM)
 constexpr int RF_CNT_OFF = 2560;       // the counters' place in the scratch sync words
 constexpr int RF_CNT_STRIDE = 32;      // one 128-byte line per counter
 
@@ -769,8 +770,10 @@ struct RouteFusedArgs {
 
 template <typename R, int VPT, int NV>
 __global__ void __launch_bounds__(RF_THREADS) k_route_fused(const RouteFusedArgs a) {
-    extern __shared__ __align__(16) float rf_sm[];     // fx [tpg][chunks * RF_CPAD]; later logits + dispatch
-    __shared__ float cs[RF_EC][RF_MAX_CH];
+    // dynamic: fx [RF_TPG][chunks * RF_CPAD] | router rows, one K half [RF_EC][32 chunks][RF_CPAD];
+    // later the logits and the dispatch
+    extern __shared__ __align__(16) float rf_sm[];
+    __shared__ float cs[RF_EC][RF_TPG][RF_MAX_CH];
     __shared__ double ps[RF_EC][RF_MAX_CH];
     __shared__ double redd[32];
     __shared__ float redf[32];
@@ -785,15 +788,25 @@ __global__ void __launch_bounds__(RF_THREADS) k_route_fused(const RouteFusedArgs
     const int e = ec * RF_EC + warp;
     const int rowf = nch * RF_CPAD;
     pdl_launch_dependents();
-    // 1. router rows (constant) before the wait; chunk c = lane + 32 * i of the row
-    float4 wr[2][8];
+    // 1. the CTA's router rows, one K half (32 chunks of 32 values) at a time, copied into shared memory
+    //    as 16-byte pieces with consecutive threads on consecutive pieces of a row (coalesced; a lane
+    //    loading its own chunks touched 32 lines per load instruction); the first half before the wait
+    //    (constant weights), the second half into L2 meanwhile
+    float* ws = rf_sm + RF_TPG * rowf;
+    auto load_w_half = [&](int half) {
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-            wr[i][q] = (e < E && i < cpl)
-                ? __ldg(reinterpret_cast<const float4*>(a.w_router + (int64_t)e * H + 32 * (lane + 32 * i) + 4 * q))
-                : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < 8; ++j) {
+            const int idx = tid + RF_THREADS * j;                // expert idx / 256, chunk (idx / 8) % 32, piece idx % 8
+            const int we = idx >> 8, c = (idx >> 3) & 31, pc = idx & 7;
+            const int eg = ec * RF_EC + we;
+            if (eg < E)
+                cp_async16(ws + (we * 32 + c) * RF_CPAD + 4 * pc, a.w_router + (int64_t)eg * H + 32 * (32 * half + c) + 4 * pc);
+        }
+        cp_async_commit();
+    };
+    load_w_half(0);
+    if (cpl > 1 && ec * RF_EC + (tid >> 5) < E)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a.w_router + (int64_t)(ec * RF_EC + (tid >> 5)) * H + 32 * (32 + lane)));
     pdl_wait();
     if (a.stamp && tid == 0) atomicMin(a.stamp, gtimer());
     const R* x = reinterpret_cast<const R*>(a.x);
@@ -805,9 +818,9 @@ __global__ void __launch_bounds__(RF_THREADS) k_route_fused(const RouteFusedArgs
             cp_async16(rf_sm + tt * rowf + (i >> 5) * RF_CPAD + (i & 31), x + (int64_t)(t0 + tt) * H + i);
         }
         cp_async_commit();
-        cp_async_wait_all();
-        __syncthreads();
     }
+    cp_async_wait_all();
+    __syncthreads();
 #pragma unroll 1
     for (int tt = 0; tt < nt; ++tt) {
         // the arithmetic of rms_row_scale (thread order of the squares, warp butterfly, warps in order)
@@ -846,33 +859,46 @@ __global__ void __launch_bounds__(RF_THREADS) k_route_fused(const RouteFusedArgs
         }
     }
     __syncthreads();
-    // 2. logits of expert e for the CTA's tokens
-#pragma unroll 1
-    for (int tt = 0; tt < nt; ++tt) {
+    // 2. logits of expert e for the CTA's tokens: lane = chunk within the K half; the f32 sum of a chunk
+    //    runs over its 32 values in order (the chunk sums of k_router_logits)
+    for (int half = 0; half < cpl; ++half) {
+        if (half > 0) {
+            __syncthreads();                                 // every warp is done with the first half
+            load_w_half(half);
+            cp_async_wait_all();
+            __syncthreads();
+        }
         if (e < E) {
-            const float* fr = rf_sm + tt * rowf;
+            const float* wrow = ws + (warp * 32 + lane) * RF_CPAD;
+            float4 wv[8];
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                if (i < cpl) {
-                    const int c = lane + 32 * i;
-                    float acc = 0.f;
+            for (int q = 0; q < 8; ++q) wv[q] = *reinterpret_cast<const float4*>(wrow + 4 * q);
+            const int c = 32 * half + lane;
+#pragma unroll 1
+            for (int tt = 0; tt < nt; ++tt) {
+                const float* fr = rf_sm + tt * rowf + c * RF_CPAD;
+                float acc = 0.f;
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const float4 f = *reinterpret_cast<const float4*>(fr + c * RF_CPAD + 4 * q);
-                        acc = fmaf(f.x, wr[i][q].x, acc);
-                        acc = fmaf(f.y, wr[i][q].y, acc);
-                        acc = fmaf(f.z, wr[i][q].z, acc);
-                        acc = fmaf(f.w, wr[i][q].w, acc);
-                    }
-                    cs[warp][c] = acc;
+                for (int q = 0; q < 8; ++q) {
+                    const float4 f = *reinterpret_cast<const float4*>(fr + 4 * q);
+                    acc = fmaf(f.x, wv[q].x, acc);
+                    acc = fmaf(f.y, wv[q].y, acc);
+                    acc = fmaf(f.z, wv[q].z, acc);
+                    acc = fmaf(f.w, wv[q].w, acc);
                 }
+                cs[warp][tt][c] = acc;
             }
-            __syncwarp();
+        }
+    }
+    __syncwarp();
+    if (e < E) {
+        const int cps = nch / a.ks;
+#pragma unroll 1
+        for (int tt = 0; tt < nt; ++tt) {
             // split sums: split z covers chunks [z*cps, (z+1)*cps), added in double from 0
-            const int cps = nch / a.ks;
             for (int z = lane; z < a.ks; z += 32) {
                 double sz = 0.0;
-                for (int c = z * cps; c < (z + 1) * cps; ++c) sz += (double)cs[warp][c];
+                for (int c = z * cps; c < (z + 1) * cps; ++c) sz += (double)cs[warp][tt][c];
                 ps[warp][z] = sz;
             }
             __syncwarp();
@@ -953,10 +979,23 @@ bool route_fused_supported(const Dims& d, int T) {
     return ks >= 1 && (d.H / RL_KC) % ks == 0;
 }
 
+template <typename R, int VPT, int NV>
+static cudaError_t launch_route_fused_nv(const RouteFusedArgs& a, dim3 grid, size_t dyn, cudaStream_t s) {
+    static unsigned long long attr_set = 0;             // devices on which the shared-memory limit was raised
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || !(attr_set >> dev & 1ull)) {
+        cudaError_t e = cudaFuncSetAttribute(k_route_fused<R, VPT, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             RF_SMEM_MAX);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) attr_set |= 1ull << dev;
+    }
+    return launch_pdl(k_route_fused<R, VPT, NV>, grid, RF_THREADS, dyn, s, a);
+}
 template <typename R, int VPT>
 static cudaError_t launch_route_fused_t(const RouteFusedArgs& a, dim3 grid, size_t dyn, cudaStream_t s) {
-    if (a.E <= 128) return launch_pdl(k_route_fused<R, VPT, 4>, grid, RF_THREADS, dyn, s, a);
-    return launch_pdl(k_route_fused<R, VPT, 16>, grid, RF_THREADS, dyn, s, a);
+    if (a.E <= 128) return launch_route_fused_nv<R, VPT, 4>(a, grid, dyn, s);
+    return launch_route_fused_nv<R, VPT, 16>(a, grid, dyn, s);
 }
 
 cudaError_t launch_route_fused(const Dims& d, const LayerWeights& lw, const Scratch& sc, const void* x, int T, int KK,
@@ -992,10 +1031,10 @@ cudaError_t launch_route_fused(const Dims& d, const LayerWeights& lw, const Scra
         if ((int64_t)n_ec * ((T + tp - 1) / tp) <= 2 * (int64_t)sms[dev]) { a.tpg = tp; break; }
     const dim3 grid(n_ec, (T + a.tpg - 1) / a.tpg);
     const int NS = lw.n_slots + (KK > d.k ? 1 : 0);
-    size_t dyn = (size_t)RF_TPG * (d.H / RL_KC) * RF_CPAD * 4;
+    size_t dyn = (size_t)RF_TPG * (d.H / RL_KC) * RF_CPAD * 4 + (size_t)RF_EC * 32 * RF_CPAD * 4;   // fx + a W half
     dyn = std::max(dyn, (size_t)RF_TPG * 32 * (d.E <= 128 ? 4 : 16) * 4);
     dyn = std::max(dyn, (size_t)(NS + 1 + 2 * T * KK) * 4);
-    if (dyn > 48 * 1024) return cudaErrorInvalidValue;
+    if (dyn > (size_t)RF_SMEM_MAX) return cudaErrorInvalidValue;
     if (d.H <= 1024)
         return d.resid_bf16 ? launch_route_fused_t<__nv_bfloat16, 4>(a, grid, dyn, s)
                             : launch_route_fused_t<float, 4>(a, grid, dyn, s);
