@@ -1,15 +1,20 @@
 // kernels_grouped.cu -- the router and the token-grouped expert path, valid for any T.
 //
 // One MoE layer for T tokens runs as:
-//   k_route         RMSNorm -> f32 router GEMV -> softmax over all E -> top-k (+renorm), per token
+//   k_rmsnorm, k_router_logits (k_router_tc for T >= 1024), k_route_topk
+//                   RMSNorm -> f32 router GEMV -> softmax over all E -> top-k (+renorm), per token
 //   k_quant_q8      Q8_K quantisation of the normed activations fx
-//   k_dispatch      group the (token, j) pairs by pool slot (counting sort, one CTA)
-//   k_gateup        per slot and row tile: h = silu(gate . fx) * (up . fx) for the slot's tokens
+//   k_dispatch      group the (token, j) pairs by pool slot (counting sort, one CTA; k_disp_* above
+//                   4096 entries)
+//   k_gateup_sw     per slot and row tile: h = silu(gate . fx) * (up . fx) for the slot's tokens
 //   k_quant_q8      Q8_K quantisation of h
-//   k_down          per slot and row tile: y = down . h for the slot's tokens
+//   k_down_sw       per slot and row tile: y = down . h for the slot's tokens
 //   k_combine       x = (sum_j w_j * y_j + sigmoid(g_sh . fx) * y_sh) + x, j ascending
-// which restates graph A's router tail and graph B of hoard (src/run_moe_stream.cpp:352-373,
-// :425-447) and the batched mul_mat_id form (src/run_specloop.cpp:115-140).
+// (for T <= 64 with every expert resident, k_route_fused replaces the first five kernels; the
+// per-entry kernels k_gateup / k_down serve the shapes the streaming kernels do not), which restates
+// graph A's router tail and graph B of hoard (src/run_moe_stream.cpp:352-373, :425-447) and the
+// batched mul_mat_id form (src/run_specloop.cpp:115-140). Every kernel here is a programmatic
+// dependent launch.
 #include "common.cuh"
 #include "kernels.h"
 #include "block_ops.cuh"
@@ -717,10 +722,11 @@ __global__ void __launch_bounds__(DISP_THREADS) k_dispatch(const int32_t* __rest
 // ---------------------------------------------------------------------------------------------
 // Small batches through a whole layer: one kernel for graph A's RMSNorm, router GEMV, softmax + top-k,
 // the Q8_K of the FFN input and the dispatch, for T <= RF_MAX_T tokens with every expert resident.
-// CTA (ec, tg) takes tokens [RF_TPG*tg, +RF_TPG) and experts [RF_EC*ec, +RF_EC) (one per warp):
-//   1. the experts' router rows go into registers before the wait on the previous kernel (constant
-//      weights), the tokens' fx = rms_norm(x) * ffn_norm into shared memory (the arithmetic of
-//      k_rmsnorm, so fx is bit-identical; the ec = 0 CTA also stores it);
+// CTA (ec, tg) takes tpg (<= RF_TPG) tokens from tpg*tg and experts [RF_EC*ec, +RF_EC) (one per warp):
+//   1. the experts' router rows are copied into shared memory one K half at a time (the first before
+//      the wait on the previous kernel: constant weights), the tokens' fx = rms_norm(x) * ffn_norm
+//      into shared memory (the arithmetic of k_rmsnorm, so fx is bit-identical; the ec = 0 CTA also
+//      stores it);
 //   2. logits: each lane forms the f32 sums of its 32-wide K chunks, then the chunk sums are added
 //      in double exactly as k_router_logits (per K split) and k_route_topk (splits in `subs`
 //      ranges) add them for the same (T, E, H), so the logits -- and the routing -- are identical
