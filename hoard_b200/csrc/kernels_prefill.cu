@@ -20,6 +20,7 @@
 // of the two operands (f16 rather than bf16: same tensor-core rate, three more mantissa bits).
 // Every wait is bounded by %globaltimer; on expiry the CTA records an error bit, skips all further
 // work, waits (bounded) for its own tensor-core and copy operations and frees its tensor memory.
+// The file also holds the router GEMM of large batches on the same tensor cores (k_router_tc).
 #include "common.cuh"
 #include "kernels.h"
 
