@@ -1056,7 +1056,6 @@ cudaError_t launch_experts_tc(const Dims& d, const LayerWeights& lw, const Scrat
                               int* launches, unsigned long long* trace) {
     const bool shared = lw.shared != nullptr;
     const int KK = d.k + (shared ? 1 : 0);
-    const int NS = lw.n_slots + (shared ? 1 : 0);
     int nl = 0;
     cudaError_t e;
     // 1. ggml's Q8_K of fx, as f16 (q * d) rows

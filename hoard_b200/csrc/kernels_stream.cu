@@ -39,7 +39,6 @@ constexpr int SW_CTAS_PER_SM = 2;                        // resident CTAs per SM
 constexpr int SW_CONSUMERS = 8;                          // consumer warps
 constexpr int SW_THREADS = 32 * (SW_CONSUMERS + 1);      // + the producer warp
 constexpr int sw_smem(int ctas_per_sm) { return (ctas_per_sm == 1 ? 227 : 112) * 1024; }   // per CTA
-constexpr int SW_SMEM = sw_smem(SW_CTAS_PER_SM);
 constexpr int RT = 64;                                   // tiles per metadata round
 constexpr int MAX_ACT = 16;
 constexpr int SW_STATIC = RT * 16 + RT * MAX_ACT * 4 + 64;   // static shared memory of either kernel
@@ -347,7 +346,6 @@ __global__ void __launch_bounds__(SW_THREADS, SW_CTAS_PER_SM) k_gateup_sw(GuArgs
     if (a.stamp && threadIdx.x == 0) atomicMin(a.stamp, gtimer());
     const int ntiles = *a.n_items * ntr;
     const int64_t nblk = (int64_t)a.I * GU_NB;
-    constexpr int H = QK * GU_NB;
     const bool producer = warp == SW_CONSUMERS;
     const GuLane GL(lane, warp);                         // consumer lane constants
     int j = 0;                                           // the CTA's tile counter (stage and phase)
