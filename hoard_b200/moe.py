@@ -304,7 +304,10 @@ class MoEContext:
         self._check(lib().hoard_moe_set_gemm_ctas(self._h, ctas), "set_gemm_ctas")
 
     def set_trace(self, buf: torch.Tensor | None):
-        """Enables phase stamps of the persistent decode kernel into an int64 CUDA tensor."""
+        """Enables %globaltimer stamps into an int64 CUDA tensor (None turns them off): the persistent
+        decode kernel's phases ([cta][layer][phase], see trace_layout), the tensor-core GEMMs' stages
+        (capacity >= 4096), and for the small-batch layer path words 0-5 = {first start, last end} of
+        the fused route, gate/up and down kernels (set the starts to -1 and the ends to 0 first)."""
         if buf is None:
             self._check(lib().hoard_moe_set_trace(self._h, None, 0), "set_trace")
         else:
