@@ -111,8 +111,10 @@ int hoard_moe_experts(hoard_moe_ctx* ctx, int layer, const float* fx, const int3
                       hoard_stream stream);
 
 /* Fused layer with every expert resident (slot == expert id): route + experts + combine, with
- * no host round trip. sel_out / w_out may be NULL. Replaces src/run_moe_stream.cpp:352-447 for
- * the all-resident case (K = n_expert) and the fused chain of src/run_m1.cpp:92-108. */
+ * no host round trip. sel_out / w_out may be NULL. For 2 <= T <= 64 below the GEMM threshold the
+ * RMSNorm, router, top-k, Q8_K of fx and dispatch run as one kernel whose routing is bit-for-bit
+ * that of hoard_moe_route. Replaces src/run_moe_stream.cpp:352-447 for the all-resident case
+ * (K = n_expert) and the fused chain of src/run_m1.cpp:92-108. */
 int hoard_moe_layer(hoard_moe_ctx* ctx, int layer, void* x_inout, int T, int32_t* sel_out,
                     float* w_out, hoard_stream stream);
 
